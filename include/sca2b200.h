@@ -1,0 +1,171 @@
+/*
+ * sca2b200 -- C ABI of the B200 (sm_100a) decayed-state / delta-rule scan.
+ *
+ * One recurrence covers every C-head / long-head variant of the reference
+ * (per batch b, head h; fp32 state S in R^{K x V}):
+ *
+ *     S~_t = diag(gamma_t) S_{t-1}          gamma_t[m] = exp(g_t) * exp(-lam[m])
+ *     e_t  = v_t - beta_t * (k_t^T S~_t) / kappa
+ *     S_t  = S~_t + k_t e_t^T
+ *     o_t  = Q_t^T S_t / kappa              (R read columns)
+ *
+ * Two input flavours:
+ *   SCA2_FLAVOR_PHASE  phase-coded heads.  Inputs are the write phase phi and the
+ *                      read phase psi (fp32, Mh modes); k = [cos phi ; sin phi]
+ *                      (K = 2 Mh), kappa = Mh, R = 2 with the read columns
+ *                      c1 = wr cos psi + wi sin psi, c2 = wr sin psi - wi cos psi:
+ *                      o_re = c1.sr + c2.si, o_im = c1.si - c2.sr.
+ *                      Replaces the chunk loop of LongHead._batched / _chunk
+ *                      (lapa/layer.py:241-366), CHeadDeltaDamp._prefill_batched
+ *                      (sca2/arch_damp.py:141-198), CHeadDelta._prefill_chunk
+ *                      (sca2/arch_cdelta.py:137-172) and CHeadGated._chunk
+ *                      (sca2/arch_gatedc.py:121-169).
+ *   SCA2_FLAVOR_KEY    explicit keys (GDN form).  k, q given (K channels), R = 1,
+ *                      kappa = 1, Q = q_scale * q; with v_times_beta = 1 the value
+ *                      is pre-scaled by beta (write-gated GDN, e = beta (v - k^T S~)).
+ *                      Replaces fla's naive_chunk_gated_delta_rule as called at
+ *                      lapa/benchmarks/baselines.py:111-120.
+ *
+ * Conventions
+ *   - All pointers are device pointers on the current device; all launches go
+ *     on the given stream; no call synchronises the host or allocates memory.
+ *   - Per-token tensors are passed as {ptr, stride_b, stride_t, stride_h} in
+ *     ELEMENTS; the innermost (channel) dimension is contiguous.
+ *   - Outputs o and dO carry a fourth stride, over the read column r.
+ *   - State tensors are dense (B, H, K, V) fp32; for the phase flavour rows
+ *     [0, Mh) hold the real part sr and rows [Mh, 2Mh) the imaginary part si.
+ *   - Optional inputs (beta, g, lam, S0, dS_final) may be NULL; NULL beta is
+ *     the additive write, NULL g / lam mean no decay of that kind.
+ *   - lam * chunk must stay below ~80 (the closed form forms exp(+lam i) in
+ *     fp32; the reference's guard is lam * chunk < 60, lapa/layer.py:39-43).
+ *   - Return value: SCA2_OK, or an error code; sca2_last_error() gives the
+ *     message (thread-local).  Invalid arguments are rejected on the host
+ *     before any launch.
+ */
+#ifndef SCA2B200_H
+#define SCA2B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SCA2_API __attribute__((visibility("default")))
+#else
+#define SCA2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum sca2_status {
+  SCA2_OK = 0,
+  SCA2_ERR_ARG = 1,       /* invalid argument (shape, stride, null, dtype) */
+  SCA2_ERR_UNSUPPORTED = 2,
+  SCA2_ERR_CUDA = 3,      /* a CUDA runtime call or launch failed */
+};
+
+enum sca2_dtype { SCA2_F32 = 0, SCA2_BF16 = 1 };
+enum sca2_flavor { SCA2_FLAVOR_PHASE = 0, SCA2_FLAVOR_KEY = 1 };
+
+/* One per-token tensor: element (b, t, h, c) at ptr[b*sb + t*st + h*sh + c]. */
+typedef struct sca2_tok {
+  const void* ptr;
+  int64_t sb, st, sh;
+} sca2_tok;
+
+/* Output per-token tensor with a read-column stride: (b,t,h,r,c). */
+typedef struct sca2_out {
+  void* ptr;
+  int64_t sb, st, sh, sr;
+} sca2_out;
+
+typedef struct sca2_scan_args {
+  int32_t flavor;       /* sca2_flavor */
+  int32_t B, T, H;
+  int32_t K;            /* key width: 2*Mh (phase) or K (key flavour) */
+  int32_t V;            /* value width */
+  int32_t io_dtype;     /* dtype of v, q, k (key flavour), o, dO, dv */
+  int32_t v_times_beta; /* key flavour: value pre-scaled by beta (GDN) */
+  float q_scale;        /* key flavour: Q = q_scale * q */
+  /* inputs */
+  sca2_tok phw;         /* phase: write phase phi (fp32, Mh)   | key: k (io dtype, K) */
+  sca2_tok phq;         /* phase: read phase psi (fp32, Mh)    | key: q (io dtype, K) */
+  sca2_tok v;           /* value (io dtype, V) */
+  sca2_tok beta;        /* erase gate, fp32, one channel; ptr NULL = additive */
+  sca2_tok g;           /* scalar log-decay <= 0, fp32; ptr NULL = none */
+  const float* lam;     /* (H, Mh) phase / (H, K) key, >= 0; NULL = none */
+  const float* wr;      /* (H, Mh) phase only */
+  const float* wi;      /* (H, Mh) phase only */
+  const float* S0;      /* (B,H,K,V) incoming state; NULL = zeros */
+} sca2_scan_args;
+
+/* Forward scan.
+ *   o             (b,t,h,r,V) raw read, io dtype (R = 2 phase, 1 key)
+ *   S_final       (B,H,K,V) fp32 or NULL
+ *   chunk_states  NULL, or (B,H,NC,K,V) fp32 with NC = sca2_num_chunks(T): the
+ *                 state entering every chunk, kept for the backward.
+ * Replaces the forward of the reference's prefill paths listed above. */
+SCA2_API int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final,
+                  float* chunk_states, void* stream);
+
+/* Number of internal chunks the scan uses for T tokens. */
+SCA2_API int32_t sca2_num_chunks(int32_t T);
+
+/* Gradients written by sca2_scan_bwd.  All per-token gradient buffers except dv
+ * are fp32 and ACCUMULATED INTO (the caller zero-fills them); dv is written in the
+ * io dtype.  Per-head gradients (dlam, dwr, dwi) are fp32 and accumulated into.
+ *   dphw / dphq : phase: d phi, d psi (Mh)     | key: dk, dq (K)
+ *   dv          : (io dtype, V)
+ *   dbeta, dg   : one channel, fp32 (ignored where the input was NULL)
+ *   dlam        : (H, Mh) phase / (H, K) key, or NULL
+ *   dwr, dwi    : (H, Mh) phase, or NULL
+ *   dS0         : (B,H,K,V) fp32 gradient of the incoming state (written), or NULL
+ */
+typedef struct sca2_scan_grads {
+  sca2_tok dphw, dphq, dv, dbeta, dg;
+  float* dlam;
+  float* dwr;
+  float* dwi;
+  float* dS0;
+} sca2_scan_grads;
+
+/* Backward scan: reverse chunk sweep of the adjoint state, all per-token
+ * gradients of a chunk from (state entering the chunk, adjoint leaving it).
+ *   dO            (b,t,h,r,V) io dtype, upstream gradient of o
+ *   dS_final      (B,H,K,V) fp32 upstream gradient of S_final, or NULL
+ *   chunk_states  as written by sca2_scan_fwd for the same inputs.
+ * Replaces torch autograd through the reference's prefill (sca2/arch_damp.py:141-198,
+ * lapa/layer.py:298-366). */
+SCA2_API int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
+                  const float* chunk_states, const sca2_scan_grads* gr, void* stream);
+
+/* Single-token decode step for every (b, h): read S (B,H,K,V) fp32, write the new
+ * state to S_out (may equal S_in) and the read o (b,h,r,V).  Per-token inputs use
+ * sca2_tok with T = 1 (st ignored).  Replaces LongHead.step (lapa/layer.py:387-412),
+ * CHeadDeltaDamp.step (sca2/arch_damp.py:225-245), CHeadDelta.step
+ * (sca2/arch_cdelta.py:186-206), CHeadGated.step (sca2/arch_gatedc.py:171-193) and
+ * fla's naive_recurrent_gated_delta_rule with T = 1 (lapa/benchmarks/baselines.py:142). */
+SCA2_API int sca2_scan_step(const sca2_scan_args* a, const float* S_in, float* S_out,
+                   sca2_out o, void* stream);
+
+/* Per-row RMS read-out u = x * rsqrt(mean(x^2) + eps) over the last dim D, with
+ * x (N, D) io dtype contiguous rows and u in the same dtype (sca2/ref.py:29-30,
+ * lapa/layer.py:117-118). */
+SCA2_API int sca2_rms_fwd(const void* x, void* u, int64_t N, int32_t D, float eps,
+                 int32_t io_dtype, void* stream);
+/* dx = (du - u * mean(du * u)) * rsqrt(mean(x^2) + eps); dx may alias du. */
+SCA2_API int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D,
+                 float eps, int32_t io_dtype, void* stream);
+
+/* Thread-local message of the last failing call on this thread. */
+SCA2_API const char* sca2_last_error(void);
+
+/* Library version string. */
+SCA2_API const char* sca2_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCA2B200_H */

@@ -1,0 +1,180 @@
+// extern "C" entry points of libsca2b200.so: argument validation on the host, then
+// dispatch to the kernels.  No entry point allocates memory or synchronises the host.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+namespace sca2 {
+// scan_f32.cu
+int f32_smem_bytes(int K, int R, bool bwd);
+int f32_num_chunks(int T);
+cudaError_t f32_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final,
+                         float* cstates, cudaStream_t st);
+cudaError_t f32_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final,
+                         const float* cstates, const sca2_scan_grads& gr, cudaStream_t st);
+// step.cu
+int step_rows_per_thread(int K, int V, int vec);
+int step_max_rows();
+size_t step_smem_bytes(int K, int V, int R, int vec);
+cudaError_t launch_step(const sca2_scan_args& p, const float* S_in, float* S_out,
+                        const sca2_out& o, int vec, cudaStream_t st);
+cudaError_t launch_rms_fwd(const void* x, void* u, int64_t N, int D, float eps, int dt,
+                           cudaStream_t st);
+cudaError_t launch_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int D, float eps,
+                           int dt, cudaStream_t st);
+}  // namespace sca2
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(SCA2_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+int max_optin_smem() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return 0;
+  return v;
+}
+
+// Checks shared by the forward, backward and step entry points.
+int check_common(const sca2_scan_args* a, bool step) {
+  if (!a) return fail(SCA2_ERR_ARG, "null argument struct");
+  if (a->flavor != SCA2_FLAVOR_PHASE && a->flavor != SCA2_FLAVOR_KEY)
+    return fail(SCA2_ERR_ARG, "flavor must be SCA2_FLAVOR_PHASE or SCA2_FLAVOR_KEY");
+  if (a->io_dtype != SCA2_F32 && a->io_dtype != SCA2_BF16)
+    return fail(SCA2_ERR_ARG, "io_dtype must be SCA2_F32 or SCA2_BF16");
+  if (a->B < 1 || a->H < 1 || a->K < 1 || a->V < 1 || a->T < 0 || (step && a->T != 1))
+    return fail(SCA2_ERR_ARG, "sizes must satisfy B, H, K, V >= 1, T >= 0 (T == 1 for a step)");
+  if ((int64_t)a->B * a->H > 2147483647LL)
+    return fail(SCA2_ERR_ARG, "B * H too large");
+  if (a->flavor == SCA2_FLAVOR_PHASE) {
+    if (a->K % 2) return fail(SCA2_ERR_ARG, "phase flavour needs an even K (= 2 * Mh)");
+    if (!a->wr || !a->wi) return fail(SCA2_ERR_ARG, "phase flavour needs wr and wi");
+    if (a->v_times_beta) return fail(SCA2_ERR_ARG, "v_times_beta is a key-flavour option");
+  }
+  if (!a->phw.ptr || !a->phq.ptr || !a->v.ptr)
+    return fail(SCA2_ERR_ARG, "phw/k, phq/q and v must be non-null");
+  if (a->v_times_beta && !a->beta.ptr) return fail(SCA2_ERR_ARG, "v_times_beta needs beta");
+  return SCA2_OK;
+}
+
+int check_scan(const sca2_scan_args* a, bool bwd) {
+  int rc = check_common(a, false);
+  if (rc) return rc;
+  if (a->K > 128)
+    return fail(SCA2_ERR_UNSUPPORTED, "key width K > 128 is not supported by this build");
+  const int R = a->flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
+  const int need = sca2::f32_smem_bytes(a->K, R, bwd);
+  const int have = max_optin_smem();
+  if (need > have)
+    return fail(SCA2_ERR_UNSUPPORTED, "shape needs " + std::to_string(need) +
+                                          " bytes of shared memory per CTA, device allows " +
+                                          std::to_string(have));
+  return SCA2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sca2_last_error(void) { return g_err.c_str(); }
+
+const char* sca2_version(void) { return "sca2b200 0.1.0 (sm_100a)"; }
+
+int32_t sca2_num_chunks(int32_t T) { return sca2::f32_num_chunks(T); }
+
+int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* chunk_states,
+                  void* stream) {
+  int rc = check_scan(a, false);
+  if (rc) return rc;
+  if (!o.ptr && a->T > 0) return fail(SCA2_ERR_ARG, "output o must be non-null");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t sbytes = (size_t)a->B * a->H * a->K * a->V * sizeof(float);
+  if (a->T == 0) {  // empty input: the state passes through unchanged
+    if (S_final) {
+      cudaError_t e = a->S0 ? cudaMemcpyAsync(S_final, a->S0, sbytes, cudaMemcpyDeviceToDevice, st)
+                            : cudaMemsetAsync(S_final, 0, sbytes, st);
+      if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd(T=0)");
+    }
+    return SCA2_OK;
+  }
+  cudaError_t e = sca2::f32_scan_fwd(*a, o, S_final, chunk_states, st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd");
+  return SCA2_OK;
+}
+
+int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
+                  const float* chunk_states, const sca2_scan_grads* gr, void* stream) {
+  int rc = check_scan(a, true);
+  if (rc) return rc;
+  if (!gr) return fail(SCA2_ERR_ARG, "null gradient struct");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t sbytes = (size_t)a->B * a->H * a->K * a->V * sizeof(float);
+  if (a->T == 0) {
+    if (gr->dS0) {
+      cudaError_t e = dS_final
+                          ? cudaMemcpyAsync(gr->dS0, dS_final, sbytes, cudaMemcpyDeviceToDevice, st)
+                          : cudaMemsetAsync(gr->dS0, 0, sbytes, st);
+      if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd(T=0)");
+    }
+    return SCA2_OK;
+  }
+  if (!dO.ptr || !chunk_states) return fail(SCA2_ERR_ARG, "dO and chunk_states must be non-null");
+  if (!gr->dphw.ptr || !gr->dphq.ptr || !gr->dv.ptr)
+    return fail(SCA2_ERR_ARG, "dphw/dk, dphq/dq and dv must be non-null");
+  if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
+  if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
+  cudaError_t e = sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
+  return SCA2_OK;
+}
+
+int sca2_scan_step(const sca2_scan_args* a, const float* S_in, float* S_out, sca2_out o,
+                   void* stream) {
+  int rc = check_common(a, true);
+  if (rc) return rc;
+  if (!S_in || !S_out || !o.ptr) return fail(SCA2_ERR_ARG, "S_in, S_out and o must be non-null");
+  const int vec = (a->V % 4 == 0 && ((uintptr_t)S_in % 16 == 0) && ((uintptr_t)S_out % 16 == 0)) ? 4 : 1;
+  const int rows = sca2::step_rows_per_thread(a->K, a->V, vec);
+  if (rows > sca2::step_max_rows())
+    return fail(SCA2_ERR_UNSUPPORTED, "state too large for the decode kernel (K*V)");
+  const int R = a->flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
+  if ((int)sca2::step_smem_bytes(a->K, a->V, R, vec) > max_optin_smem())
+    return fail(SCA2_ERR_UNSUPPORTED, "decode step needs too much shared memory");
+  cudaError_t e = sca2::launch_step(*a, S_in, S_out, o, vec, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_step");
+  return SCA2_OK;
+}
+
+int sca2_rms_fwd(const void* x, void* u, int64_t N, int32_t D, float eps, int32_t io_dtype,
+                 void* stream) {
+  if (!x || !u || N < 0 || D < 1) return fail(SCA2_ERR_ARG, "rms: bad arguments");
+  if (io_dtype != SCA2_F32 && io_dtype != SCA2_BF16) return fail(SCA2_ERR_ARG, "rms: bad dtype");
+  if (N == 0) return SCA2_OK;
+  cudaError_t e = sca2::launch_rms_fwd(x, u, N, D, eps, io_dtype, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_rms_fwd");
+  return SCA2_OK;
+}
+
+int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D, float eps,
+                 int32_t io_dtype, void* stream) {
+  if (!x || !du || !dx || N < 0 || D < 1) return fail(SCA2_ERR_ARG, "rms: bad arguments");
+  if (io_dtype != SCA2_F32 && io_dtype != SCA2_BF16) return fail(SCA2_ERR_ARG, "rms: bad dtype");
+  if (N == 0) return SCA2_OK;
+  cudaError_t e = sca2::launch_rms_bwd(x, du, dx, N, D, eps, io_dtype, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_rms_bwd");
+  return SCA2_OK;
+}
+
+}  // extern "C"

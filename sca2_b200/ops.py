@@ -1,0 +1,380 @@
+"""Differentiable scan ops over the C ABI (torch tensors in, torch tensors out).
+
+    phase_scan(phw, phq, v, beta, g, lam, wr, wi, S0)     -> o (B,T,H,2,V), S (B,H,2Mh,V)
+    key_scan(q, k, v, g, beta, scale, S0, v_times_beta)   -> o (B,T,H,V),   S (B,H,K,V)
+    phase_step(...) / key_step(...)                       one decode token, state in place
+    rms(x, eps)                                           per-row RMS read-out
+
+Every op runs the CUDA kernels of libsca2b200.so on the current stream.  There is no
+CPU path: a CPU tensor or a missing library raises.  Device memory (outputs, saved
+chunk states, gradients) comes from the PyTorch caching allocator; the library itself
+allocates nothing.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import Out, ScanArgs, ScanGrads, Tok
+
+_DT = {torch.float32: _lib.SCA2_F32, torch.bfloat16: _lib.SCA2_BF16}
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise _lib.Sca2Error("sca2_b200 ops run on CUDA tensors only (no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise _lib.Sca2Error("all tensors must be on the same CUDA device")
+    return dev
+
+
+def _inner(t: torch.Tensor) -> torch.Tensor:
+    """Make the innermost dimension contiguous (strides of the others are passed through)."""
+    return t if t.stride(-1) == 1 or t.size(-1) == 1 else t.contiguous()
+
+
+def _tok(t: Optional[torch.Tensor], step: bool = False) -> Tok:
+    """(B,T,H,C) or (B,T,H) tensor -> Tok; for a step, (B,H,C) or (B,H) (T stride 0)."""
+    if t is None:
+        return Tok(None, 0, 0, 0)
+    if step:
+        return Tok(t.data_ptr(), t.stride(0), 0, t.stride(1))
+    return Tok(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def _out(t: torch.Tensor) -> Out:
+    """(B,T,H,R,V) -> Out."""
+    return Out(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2), t.stride(3))
+
+
+def _f32(t):
+    return None if t is None else t.float()
+
+
+# ======================================================================================
+#  phase-coded scan
+# ======================================================================================
+def _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0):
+    B, T, H, Mh = phw.shape
+    a = ScanArgs()
+    a.flavor = _lib.FLAVOR_PHASE
+    a.B, a.T, a.H, a.K, a.V = B, T, H, 2 * Mh, v.shape[-1]
+    a.io_dtype = _DT[v.dtype]
+    a.v_times_beta = 0
+    a.q_scale = 1.0
+    a.phw, a.phq, a.v = _tok(phw), _tok(phq), _tok(v)
+    a.beta, a.g = _tok(beta), _tok(g)
+    a.lam, a.wr, a.wi, a.S0 = _ptr(lam), _ptr(wr), _ptr(wi), _ptr(S0)
+    return a
+
+
+def _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0):
+    if phw.dim() != 4 or phq.shape != phw.shape:
+        raise _lib.Sca2Error(f"phases must be (B,T,H,Mh) and equal-shaped, got {tuple(phw.shape)}"
+                             f" and {tuple(phq.shape)}")
+    B, T, H, Mh = phw.shape
+    if v.dim() != 4 or tuple(v.shape[:3]) != (B, T, H):
+        raise _lib.Sca2Error(f"v must be (B,T,H,V) with (B,T,H)={B, T, H}, got {tuple(v.shape)}")
+    if v.dtype not in _DT:
+        raise _lib.Sca2Error(f"v dtype {v.dtype} unsupported (float32 or bfloat16)")
+    for n, t in (("beta", beta), ("g", g)):
+        if t is not None and tuple(t.shape) != (B, T, H):
+            raise _lib.Sca2Error(f"{n} must be (B,T,H), got {tuple(t.shape)}")
+    for n, t in (("lam", lam), ("wr", wr), ("wi", wi)):
+        if t is not None and tuple(t.shape) != (H, Mh):
+            raise _lib.Sca2Error(f"{n} must be (H,Mh)={(H, Mh)}, got {tuple(t.shape)}")
+    if S0 is not None and tuple(S0.shape) != (B, H, 2 * Mh, v.shape[-1]):
+        raise _lib.Sca2Error(f"S0 must be (B,H,2Mh,V), got {tuple(S0.shape)}")
+
+
+class _PhaseScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, phw, phq, v, beta, g, lam, wr, wi, S0):
+        _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0)
+        phw, phq = _inner(phw.float()), _inner(phq.float())
+        v = _inner(v)
+        beta, g = _f32(beta), _f32(g)
+        lam = None if lam is None else lam.float().contiguous()
+        wr, wi = wr.float().contiguous(), wi.float().contiguous()
+        S0 = None if S0 is None else S0.float().contiguous()
+        a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
+        B, T, H, Mh = phw.shape
+        V = v.shape[-1]
+        o = torch.empty(B, T, H, 2, V, device=v.device, dtype=v.dtype)
+        S = torch.empty(B, H, 2 * Mh, V, device=v.device, dtype=torch.float32)
+        lib = _lib.load()
+        need = any(ctx.needs_input_grad)
+        cs = None
+        if need:
+            NC = lib.sca2_num_chunks(T)
+            cs = torch.empty(B, H, NC, 2 * Mh, V, device=v.device, dtype=torch.float32)
+        _lib.check(lib.sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs), _stream()), "scan_fwd")
+        if need:
+            ctx.save_for_backward(phw, phq, v, beta, g, lam, wr, wi, S0, cs)
+        return o, S
+
+    @staticmethod
+    def backward(ctx, do, dS):
+        phw, phq, v, beta, g, lam, wr, wi, S0, cs = ctx.saved_tensors
+        B, T, H, Mh = phw.shape
+        V = v.shape[-1]
+        dev = v.device
+        if do is None:
+            do = torch.zeros(B, T, H, 2, V, device=dev, dtype=v.dtype)
+        do = do.to(v.dtype)
+        if do.stride(-1) != 1:
+            do = do.contiguous()
+        dS = None if dS is None else dS.float().contiguous()
+        a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
+        z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
+        dphw, dphq = z(B, T, H, Mh), z(B, T, H, Mh)
+        dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
+        dbeta = z(B, T, H) if beta is not None else None
+        dg = z(B, T, H) if g is not None else None
+        dlam = z(H, Mh) if lam is not None else None
+        dwr, dwi = z(H, Mh), z(H, Mh)
+        dS0 = torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32)
+        gr = ScanGrads()
+        gr.dphw, gr.dphq, gr.dv = _tok(dphw), _tok(dphq), _tok(dv)
+        gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
+        gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), _ptr(dwr), _ptr(dwi), _ptr(dS0)
+        lib = _lib.load()
+        _lib.check(lib.sca2_scan_bwd(C_ref(a), _out(do), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
+                   "scan_bwd")
+        ni = ctx.needs_input_grad
+        return (dphw if ni[0] else None, dphq if ni[1] else None, dv if ni[2] else None,
+                dbeta if ni[3] else None, dg if ni[4] else None, dlam if ni[5] else None,
+                dwr if ni[6] else None, dwi if ni[7] else None,
+                dS0 if (ni[8] and S0 is not None) else None)
+
+
+def C_ref(x):
+    import ctypes
+    return ctypes.byref(x)
+
+
+def phase_scan(phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None, S0=None
+               ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Phase-coded decayed-state scan (the C head / long head of the reference).
+
+    phw, phq (B,T,H,Mh) write / read phases (fp32); v (B,T,H,V) fp32 or bf16;
+    beta, g (B,T,H) erase gate and scalar log-decay (None: additive / no decay);
+    lam (H,Mh) per-mode decay; wr, wi (H,Mh) spectral read weights; S0 (B,H,2Mh,V)
+    incoming state [sr ; si].  Returns the raw read o (B,T,H,2,V) in v's dtype
+    ([re, im] along dim 3) and the final fp32 state.  Differentiable in every input.
+    """
+    _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0)
+    if wr is None or wi is None:
+        raise _lib.Sca2Error("wr and wi are required")
+    return _PhaseScan.apply(phw, phq, v, beta, g, lam, wr, wi, S0)
+
+
+# ======================================================================================
+#  explicit-key (GDN) scan
+# ======================================================================================
+def _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta):
+    B, T, H, K = k.shape
+    a = ScanArgs()
+    a.flavor = _lib.FLAVOR_KEY
+    a.B, a.T, a.H, a.K, a.V = B, T, H, K, v.shape[-1]
+    a.io_dtype = _DT[v.dtype]
+    a.v_times_beta = 1 if v_times_beta else 0
+    a.q_scale = float(scale)
+    a.phw, a.phq, a.v = _tok(k), _tok(q), _tok(v)
+    a.beta, a.g = _tok(beta), _tok(g)
+    a.lam, a.wr, a.wi, a.S0 = _ptr(lam), None, None, _ptr(S0)
+    return a
+
+
+class _KeyScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, lam, S0, scale, v_times_beta):
+        _need_cuda(q, k, v, g, beta, lam, S0)
+        dt = v.dtype
+        q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
+        g, beta = _f32(g), _f32(beta)
+        lam = None if lam is None else lam.float().contiguous()
+        S0 = None if S0 is None else S0.float().contiguous()
+        a = _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta)
+        B, T, H, K = k.shape
+        V = v.shape[-1]
+        o = torch.empty(B, T, H, 1, V, device=v.device, dtype=dt)
+        S = torch.empty(B, H, K, V, device=v.device, dtype=torch.float32)
+        lib = _lib.load()
+        need = any(ctx.needs_input_grad)
+        cs = None
+        if need:
+            cs = torch.empty(B, H, lib.sca2_num_chunks(T), K, V, device=v.device, dtype=torch.float32)
+        _lib.check(lib.sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs), _stream()), "scan_fwd")
+        if need:
+            ctx.save_for_backward(q, k, v, g, beta, lam, S0, cs)
+            ctx.scale, ctx.vtb = scale, v_times_beta
+        return o[:, :, :, 0], S
+
+    @staticmethod
+    def backward(ctx, do, dS):
+        q, k, v, g, beta, lam, S0, cs = ctx.saved_tensors
+        B, T, H, K = k.shape
+        V = v.shape[-1]
+        dev = v.device
+        if do is None:
+            do = torch.zeros(B, T, H, V, device=dev, dtype=v.dtype)
+        do = do.to(v.dtype)
+        if do.stride(-1) != 1:
+            do = do.contiguous()
+        do5 = do.unsqueeze(3)
+        dS = None if dS is None else dS.float().contiguous()
+        a = _key_args(q, k, v, g, beta, lam, S0, ctx.scale, ctx.vtb)
+        z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
+        dk, dq = z(B, T, H, K), z(B, T, H, K)
+        dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
+        dbeta = z(B, T, H) if beta is not None else None
+        dg = z(B, T, H) if g is not None else None
+        dlam = z(H, K) if lam is not None else None
+        dS0 = torch.empty(B, H, K, V, device=dev, dtype=torch.float32)
+        gr = ScanGrads()
+        gr.dphw, gr.dphq, gr.dv = _tok(dk), _tok(dq), _tok(dv)
+        gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
+        gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), None, None, _ptr(dS0)
+        lib = _lib.load()
+        _lib.check(lib.sca2_scan_bwd(C_ref(a), _out(do5), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
+                   "scan_bwd")
+        ni = ctx.needs_input_grad
+        return (dq if ni[0] else None, dk if ni[1] else None, dv if ni[2] else None,
+                dg if ni[3] else None, dbeta if ni[4] else None, dlam if ni[5] else None,
+                dS0 if (ni[6] and S0 is not None) else None, None, None)
+
+
+def key_scan(q, k, v, g=None, beta=None, scale=None, S0=None, lam=None, v_times_beta=True):
+    """Explicit-key delta scan in fla's gated-delta-rule convention:
+    S~ = exp(g) S;  e = beta (v - k^T S~)  (v_times_beta) or v - beta k^T S~;  S = S~ + k e^T;
+    o = scale q^T S.  q, k (B,T,H,K), v (B,T,H,V) same dtype (fp32/bf16); g, beta (B,T,H);
+    S0 (B,H,K,V).  scale defaults to K^-1/2.  Returns o (B,T,H,V), S (B,H,K,V) fp32."""
+    if k.dim() != 4 or q.shape != k.shape or tuple(v.shape[:3]) != tuple(k.shape[:3]):
+        raise _lib.Sca2Error("q, k must be (B,T,H,K) and v (B,T,H,V)")
+    if v.dtype not in _DT:
+        raise _lib.Sca2Error(f"v dtype {v.dtype} unsupported (float32 or bfloat16)")
+    if v_times_beta and beta is None:
+        raise _lib.Sca2Error("v_times_beta needs beta")
+    K = k.shape[-1]
+    scale = K ** -0.5 if scale is None else float(scale)
+    return _KeyScan.apply(q, k, v, g, beta, lam, S0, scale, v_times_beta)
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size: int = 64, scale=None,
+                           initial_state=None, output_final_state: bool = False):
+    """Drop-in for fla's (naive_)chunk_gated_delta_rule as called by the reference's GDN
+    baseline (lapa/benchmarks/baselines.py:111-120): same argument order and returns.
+    chunk_size is accepted for signature compatibility; the kernel picks its own chunk
+    (the closed form is chunk-size invariant)."""
+    o, S = key_scan(q, k, v, g, beta, scale, initial_state)
+    return o, (S if output_final_state else None)
+
+
+# ======================================================================================
+#  decode step
+# ======================================================================================
+def phase_step(phw, phq, v, beta, g, lam, wr, wi, S, S_out=None):
+    """One token for every (b, h): phw, phq (B,H,Mh) fp32, v (B,H,V), beta/g (B,H) or None,
+    lam/wr/wi (H,Mh), S (B,H,2Mh,V) fp32.  Returns o (B,H,2,V) in v's dtype and the new
+    state (written into S_out, default a new tensor; pass S_out=S to update in place)."""
+    _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S)
+    B, H, Mh = phw.shape
+    V = v.shape[-1]
+    phw, phq, v = _inner(phw.float()), _inner(phq.float()), _inner(v)
+    beta, g = _f32(beta), _f32(g)
+    if S.dtype != torch.float32 or not S.is_contiguous() or tuple(S.shape) != (B, H, 2 * Mh, V):
+        raise _lib.Sca2Error("state must be a contiguous fp32 (B,H,2Mh,V) tensor")
+    a = ScanArgs()
+    a.flavor = _lib.FLAVOR_PHASE
+    a.B, a.T, a.H, a.K, a.V = B, 1, H, 2 * Mh, V
+    a.io_dtype = _DT[v.dtype]
+    a.q_scale = 1.0
+    a.phw, a.phq, a.v = _tok(phw, True), _tok(phq, True), _tok(v, True)
+    a.beta, a.g = _tok(beta, True), _tok(g, True)
+    lam = None if lam is None else lam.float().contiguous()
+    wr, wi = wr.float().contiguous(), wi.float().contiguous()
+    a.lam, a.wr, a.wi, a.S0 = _ptr(lam), _ptr(wr), _ptr(wi), None
+    o = torch.empty(B, 1, H, 2, V, device=v.device, dtype=v.dtype)
+    S_out = torch.empty_like(S) if S_out is None else S_out
+    _lib.check(_lib.load().sca2_scan_step(C_ref(a), S.data_ptr(), S_out.data_ptr(), _out(o), _stream()),
+               "scan_step")
+    return o[:, 0], S_out
+
+
+def key_step(q, k, v, g, beta, S, scale=None, S_out=None, v_times_beta=True):
+    """One GDN token (fla naive_recurrent_gated_delta_rule with T = 1): q, k (B,H,K),
+    v (B,H,V), g, beta (B,H), S (B,H,K,V) fp32 -> o (B,H,V), new state."""
+    _need_cuda(q, k, v, g, beta, S)
+    B, H, K = k.shape
+    V = v.shape[-1]
+    dt = v.dtype
+    q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
+    g, beta = _f32(g), _f32(beta)
+    if S.dtype != torch.float32 or not S.is_contiguous() or tuple(S.shape) != (B, H, K, V):
+        raise _lib.Sca2Error("state must be a contiguous fp32 (B,H,K,V) tensor")
+    a = ScanArgs()
+    a.flavor = _lib.FLAVOR_KEY
+    a.B, a.T, a.H, a.K, a.V = B, 1, H, K, V
+    a.io_dtype = _DT[dt]
+    a.v_times_beta = 1 if v_times_beta else 0
+    a.q_scale = K ** -0.5 if scale is None else float(scale)
+    a.phw, a.phq, a.v = _tok(k, True), _tok(q, True), _tok(v, True)
+    a.beta, a.g = _tok(beta, True), _tok(g, True)
+    a.lam = a.wr = a.wi = a.S0 = None
+    o = torch.empty(B, 1, H, 1, V, device=v.device, dtype=dt)
+    S_out = torch.empty_like(S) if S_out is None else S_out
+    _lib.check(_lib.load().sca2_scan_step(C_ref(a), S.data_ptr(), S_out.data_ptr(), _out(o), _stream()),
+               "scan_step")
+    return o[:, 0, :, 0], S_out
+
+
+# ======================================================================================
+#  RMS read-out
+# ======================================================================================
+class _Rms(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, eps):
+        _need_cuda(x)
+        if x.dtype not in _DT:
+            x = x.float()
+        x = x.contiguous()
+        D = x.shape[-1]
+        N = x.numel() // D
+        u = torch.empty_like(x)
+        _lib.check(_lib.load().sca2_rms_fwd(x.data_ptr(), u.data_ptr(), N, D, float(eps), _DT[x.dtype],
+                                            _stream()), "rms_fwd")
+        ctx.save_for_backward(x)
+        ctx.eps = eps
+        return u
+
+    @staticmethod
+    def backward(ctx, du):
+        (x,) = ctx.saved_tensors
+        du = du.to(x.dtype).contiguous()
+        D = x.shape[-1]
+        dx = torch.empty_like(x)
+        _lib.check(_lib.load().sca2_rms_bwd(x.data_ptr(), du.data_ptr(), dx.data_ptr(), x.numel() // D, D,
+                                            float(ctx.eps), _DT[x.dtype], _stream()), "rms_bwd")
+        return dx, None
+
+
+def rms(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """u = x * rsqrt(mean(x^2, -1) + eps) (sca2/ref.py:29-30), on the GPU kernel."""
+    return _Rms.apply(x, eps)

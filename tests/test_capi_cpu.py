@@ -1,0 +1,73 @@
+"""C ABI checks that need no GPU: the library loads, exports every function the header
+declares, and the ctypes mirror of each struct has the C layout (compiled with gcc)."""
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+import tempfile
+
+import pytest
+
+from sca2_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "sca2b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"SCA2_API\s+[\w\s\*]*?\b(sca2_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared()
+    assert names, "no SCA2_API declarations found"
+    for n in names:
+        assert hasattr(lib, n), n
+    assert sorted(n for n, _, _ in _lib.SIGNATURES) == names
+    assert b"sm_100a" in lib.sca2_version()
+    assert lib.sca2_num_chunks(4096) * 32 == 4096 and lib.sca2_num_chunks(1) == 1
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_struct_layout_matches_header():
+    probe = r"""
+#include <stddef.h>
+#include <stdio.h>
+#include "sca2b200.h"
+#define F(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
+int main(void) {
+  printf("sca2_tok %zu\nsca2_out %zu\nsca2_scan_args %zu\nsca2_scan_grads %zu\n",
+         sizeof(sca2_tok), sizeof(sca2_out), sizeof(sca2_scan_args), sizeof(sca2_scan_grads));
+  F(sca2_scan_args, q_scale) F(sca2_scan_args, phw) F(sca2_scan_args, g) F(sca2_scan_args, lam)
+  F(sca2_scan_args, S0) F(sca2_scan_grads, dg) F(sca2_scan_grads, dlam) F(sca2_scan_grads, dS0)
+  return 0;
+}
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "probe.c")
+        open(c, "w").write(probe)
+        exe = os.path.join(d, "probe")
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        out = dict(line.split() for line in subprocess.run([exe], capture_output=True, text=True,
+                                                           check=True).stdout.splitlines())
+    assert int(out["sca2_tok"]) == ctypes.sizeof(_lib.Tok)
+    assert int(out["sca2_out"]) == ctypes.sizeof(_lib.Out)
+    assert int(out["sca2_scan_args"]) == ctypes.sizeof(_lib.ScanArgs)
+    assert int(out["sca2_scan_grads"]) == ctypes.sizeof(_lib.ScanGrads)
+    for key, val in out.items():
+        if "." in key:
+            st, field = key.split(".")
+            cls = {"sca2_scan_args": _lib.ScanArgs, "sca2_scan_grads": _lib.ScanGrads}[st]
+            assert getattr(cls, field).offset == int(val), key
+
+
+def test_ops_refuse_cpu_tensors():
+    """No CPU fallback: the product path raises on CPU tensors instead of computing."""
+    import torch
+    from sca2_b200 import ops
+    x = torch.zeros(1, 4, 1, 2)
+    with pytest.raises(_lib.Sca2Error):
+        ops.phase_scan(x, x, torch.zeros(1, 4, 1, 3), wr=torch.ones(1, 2), wi=torch.zeros(1, 2))
