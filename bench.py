@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""Benchmark of the SCA2 / Laplace long-head scan on B200 (sm_100a kernels).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (one step = one pass of the hot path over one batch, inputs resident in HBM):
+  the phase-coded delta scan of the LapA long head, forward + backward,
+  B=8, T=4096, H=16, d_head=64 (Mh=32 complex modes, K=2Mh=64, V=64), per-mode decay
+  lam = min(softplus(N(0,1)), 1/16), erase gate beta = sigmoid(N(0,1)), phases
+  p*omega_rope + N(0,1), v and dO ~ N(0,1) in bf16, fp32 state.  Synthetic seeded data.
+  Multi-GPU (torchrun): every rank runs its own (batch x head) shard of the same size
+  (weak scaling, no data-path collective); time = max over ranks.
+
+Printed: one JSON line (rank 0) with the contract keys plus roofline (dominant kernel),
+cpu_baseline (numpy oracle on the host cores), e2e (public API, host buffers), clocks,
+gpu_launches and a decode block (batch 256, H=16, K=V=128, 512 steps after a 4096 prefill).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORK = dict(B=8, T=4096, H=16, Mh=32, V=64)
+DECODE = dict(B=256, T=4096, H=16, Mh=64, V=128, steps=512)
+# Algorithmic bytes per token per head (inputs read + outputs written once):
+#   fwd: phi, psi fp32 (2*Mh*4) + v bf16 (V*2) + beta (4) + o bf16 (2*V*2)
+#   bwd: dO bf16 (2*V*2) + inputs re-read (2*Mh*4 + V*2 + 4) + dphi, dpsi fp32 (2*Mh*4) + dv bf16 (V*2) + dbeta (4)
+FWD_BYTES_TOK = lambda Mh, V: 2 * Mh * 4 + V * 2 + 4 + 2 * V * 2
+BWD_BYTES_TOK = lambda Mh, V: 2 * V * 2 + (2 * Mh * 4 + V * 2 + 4) + (2 * Mh * 4 + V * 2 + 4)
+# Algorithmic MACs per token per head of the delta form, R=2 read columns, chunk C=64:
+#   R (C K/2 + C V/2 + K V) + K V + C K/2 (Gram) + K V (read-back) + C V/2 (solve); fwd+bwd = 3x
+FWD_MAC_TOK = lambda K, V, C=64, R=2: R * (C * K / 2 + C * V / 2 + K * V) + K * V + C * K / 2 + K * V + C * V / 2
+
+
+# --------------------------------------------------------------------------------------
+#  CPU baseline: the numpy oracle on the host cores (spawned pool, one sequence per task)
+# --------------------------------------------------------------------------------------
+def _cpu_one(args):
+    seed, T, Mh, V = args
+    import numpy as np
+    from oracle import scan as ora
+    rng = np.random.default_rng(seed)
+    p = np.arange(T, dtype=np.float32)[:, None]
+    om = (np.pi * 1e4 ** (-np.arange(Mh) / (Mh - 1))).astype(np.float32)
+    phw = (p * om + rng.standard_normal((T, Mh))).astype(np.float32)[None, :, None]
+    phq = (p * om + rng.standard_normal((T, Mh))).astype(np.float32)[None, :, None]
+    v = rng.standard_normal((1, T, 1, V)).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((1, T, 1))))).astype(np.float32)
+    lam = np.minimum(np.log1p(np.exp(rng.standard_normal((1, Mh)))), 1 / 16).astype(np.float32)
+    wr, wi = np.ones((1, Mh), np.float32), np.zeros((1, Mh), np.float32)
+    do = rng.standard_normal((1, T, 1, 2, V)).astype(np.float32)
+    t0 = time.perf_counter()
+    k, Q = ora.phase_codes(phw, phq, wr, wi)
+    lamf = np.concatenate([lam, lam], -1)
+    ora.forward_chunked(k, Q, v, beta, None, lamf, float(Mh), None, C=64, dtype=np.float32)
+    ora.backward_chunked(k, Q, v, beta, None, lamf, float(Mh), None, do, None, C=64, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_pool():
+    import multiprocessing as mp
+    for var in ("OMP_NUM_THREADS", "MKL_NUM_THREADS", "OPENBLAS_NUM_THREADS"):
+        os.environ[var] = "1"
+    n = len(os.sched_getaffinity(0))
+    return mp.get_context("spawn").Pool(n), n
+
+
+def cpu_sample(pool, n, seed=0):
+    """One bounded sample: n sequences of the workload (one (b,h) each, T tokens) fwd+bwd in
+    parallel; returns (tokens/s of the layer = sequence-tokens / H per second, wall s)."""
+    W = WORK
+    nseq = min(n, W["B"] * W["H"])
+    t0 = time.perf_counter()
+    pool.map(_cpu_one, [(seed + i, W["T"], W["Mh"], W["V"]) for i in range(nseq)])
+    wall = time.perf_counter() - t0
+    return nseq * W["T"] / W["H"] / wall, wall, nseq
+
+
+# --------------------------------------------------------------------------------------
+#  clocks
+# --------------------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index  # device UUID (robust to CUDA_VISIBLE_DEVICES) or ordinal
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, val in zip(names, r[5:9]) if val.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------------------
+#  GPU arm
+# --------------------------------------------------------------------------------------
+def make_inputs(torch, seed, dev, B, T, H, Mh, V, dtype, with_grad_out=True):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, device=dev, generator=g)
+    p = torch.arange(T, device=dev, dtype=torch.float32)[:, None]
+    om = math.pi * 1e4 ** (-torch.arange(Mh, device=dev, dtype=torch.float32) / (Mh - 1))
+    pw = (p * om)[None, :, None, :]
+    phw = (pw + rn(B, T, H, Mh)).contiguous()
+    phq = (pw + rn(B, T, H, Mh)).contiguous()
+    v = rn(B, T, H, V).to(dtype)
+    beta = torch.sigmoid(rn(B, T, H))
+    lam = torch.nn.functional.softplus(rn(H, Mh)).clamp(max=1 / 16)
+    wr, wi = 1 + 0.3 * rn(H, Mh), 0.3 * rn(H, Mh)
+    dO = rn(B, T, H, 2, V).to(dtype) if with_grad_out else None
+    return dict(phw=phw, phq=phq, v=v, beta=beta, lam=lam, wr=wr, wi=wi, dO=dO)
+
+
+def run_gpu(args, rank, world, local_rank, dist):
+    import torch
+    from sca2_b200 import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    W = WORK
+    B, T, H, Mh, V = W["B"], W["T"], W["H"], W["Mh"], W["V"]
+    x = make_inputs(torch, 1234 + rank, dev, B, T, H, Mh, V, torch.bfloat16)
+    plan = ops.PhaseScanPlan(x["phw"], x["phq"], x["v"], x["beta"], None, x["lam"], x["wr"], x["wi"])
+    st = torch.cuda.current_stream()
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(st)
+        plan.fwd()
+        if ev is not None:
+            ev[1].record(st)
+        plan.zero_grads()
+        if ev is not None:
+            ev[2].record(st)
+        plan.bwd(x["dO"], zero=False)
+        if ev is not None:
+            ev[3].record(st)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+    clocks = Clocks(f"GPU-{uuid}" if uuid is not None else torch.cuda.current_device()) if rank == 0 else None
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        step(evs[i])
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clk = clocks.stop() if clocks is not None else None
+    total_ms = evs[0][0].elapsed_time(evs[-1][3])
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    zero_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    if dist is not None:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_step = total_ms / args.steps
+
+    # ---- end to end through the public API: host (pinned) inputs -> device, fwd + bwd, result -> host
+    e2e = None
+    if not args.no_e2e:
+        host = {k: x[k].cpu().pin_memory() for k in ("phw", "phq", "v", "beta", "dO")}
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        res = torch.empty(B, H, 2 * Mh, V, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            d = {k: t.to(dev, non_blocking=True) for k, t in host.items()}
+            for k in ("phw", "phq", "v"):
+                d[k].requires_grad_(True)
+            o, S = ops.phase_scan(d["phw"], d["phq"], d["v"], d["beta"], None, x["lam"], x["wr"], x["wi"])
+            torch.autograd.backward(o, d["dO"])
+            res.copy_(S.detach(), non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(1, min(args.steps, 10))
+        e0.record(st)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(st)
+        torch.cuda.synchronize()
+        em = e0.elapsed_time(e1) / n_e2e
+        if dist is not None:
+            t = torch.tensor([em], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            em = float(t.item())
+        e2e = {"value": world * B * T / (em / 1e3), "unit": "tokens/s", "ms_per_step": em,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": res.numel() * 4}
+        del host
+
+    # ---- decode (config: batch 256, H=16, K=V=128, 4096-token prefill, 512 steps)
+    decode = None
+    if not args.no_decode:
+        del plan
+        torch.cuda.empty_cache()
+        decode = run_decode(torch, ops, dev, rank, world, dist)
+    return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
+                decode=decode)
+
+
+def run_decode(torch, ops, dev, rank, world, dist):
+    D = DECODE
+    B, T, H, Mh, V, n = D["B"], D["T"], D["H"], D["Mh"], D["V"], D["steps"]
+    x = make_inputs(torch, 777 + rank, dev, B, T, H, Mh, V, torch.bfloat16, with_grad_out=False)
+    with torch.no_grad():
+        _, S = ops.phase_scan(x["phw"], x["phq"], x["v"], x["beta"], None, x["lam"], x["wr"], x["wi"])
+    del x
+    torch.cuda.empty_cache()
+    y = make_inputs(torch, 999 + rank, dev, B, n, H, Mh, V, torch.float32, with_grad_out=False)
+    S = S.contiguous()
+    plan = ops.PhaseStepPlan(y["phw"], y["phq"], y["v"], y["beta"], None, y["lam"], y["wr"], y["wi"], S)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for t in range(3):
+            plan.step(t)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for t in range(n):
+            plan.step(t)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    e0.record(st)
+    graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_step = ms * 1e3 / n
+    state_bytes = B * H * 2 * Mh * V * 4
+    io_bytes = B * H * (2 * Mh * 4 + V * 4 + 4 + 2 * V * 4)
+    gbs = (2 * state_bytes + io_bytes) / (us_step * 1e-6) / 1e9
+    del graph
+    return {"value": world * B * n / (ms / 1e3), "unit": "tokens/s", "us_per_step": us_step,
+            "config": {"batch": B, "H": H, "K": 2 * Mh, "V": V, "prefill": T, "steps": n},
+            "achieved_gbs": gbs, "bytes_per_step": 2 * state_bytes + io_bytes}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    W = WORK
+    config = {"workload": "LapA long-head phase-coded delta scan fwd+bwd (phases, per-mode decay, "
+                          "delta gate), B=8 T=4096 H=16 d_head=64 (Mh=32, K=V=64) per GPU",
+              "batch_per_gpu": W["B"], "seq_len": W["T"], "heads": W["H"], "d_head": 2 * W["Mh"],
+              "parallelism": f"(batch x head) shards, {world} rank(s)",
+              "l2": "inputs larger than L2 (~0.7 GB touched per step), no flush"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        pool, n = cpu_pool()
+        try:
+            cpu_sample(pool, n, seed=0)  # warm the workers
+            for i in range(args.warmup):
+                cpu_sample(pool, n, seed=1 + i)
+            vals, walls = [], []
+            for i in range(args.steps):
+                v, w, nseq = cpu_sample(pool, n, seed=100 + i)
+                vals.append(v)
+                walls.append(w)
+        finally:
+            pool.close()
+        tot = sum(walls)
+        value = args.steps * nseq * W["T"] / W["H"] / tot
+        line = {"impl": "reference", "metric": "layer fwd+bwd tokens/s", "value": value, "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n, "kind": "port",
+                                 "sample": f"{nseq} (b,h) sequences x {W['T']} tokens fwd+bwd per step, "
+                                           f"numpy oracle float32, one process per core"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    # CPU pool first (spawned before any CUDA work)
+    pool = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        pool, ncpu = cpu_pool()
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist_
+        dist_.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist = dist_
+    try:
+        r = run_gpu(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+    if rank != 0:
+        if pool is not None:
+            pool.close()
+        return
+    cpu = None
+    if pool is not None:
+        try:
+            cpu_sample(pool, ncpu, seed=0)
+            v, w, nseq = cpu_sample(pool, ncpu, seed=7)
+            cpu = {"value": v, "unit": "tokens/s", "cores": ncpu, "kind": "port",
+                   "sample": f"{nseq} (b,h) sequences x {W['T']} tokens fwd+bwd (of the {W['B'] * W['H']} "
+                             f"per step), numpy oracle float32, one process per core, {w:.1f} s wall"}
+        finally:
+            pool.close()
+
+    hbm, tfl, src = peaks()
+    tokh = W["B"] * W["T"] * W["H"]
+    fwd_b, bwd_b = FWD_BYTES_TOK(W["Mh"], W["V"]) * tokh, BWD_BYTES_TOK(W["Mh"], W["V"]) * tokh
+    kern = {"scan_fwd": (r["fwd_ms"], fwd_b), "scan_bwd": (r["bwd_ms"], bwd_b)}
+    name = max(kern, key=lambda k: kern[k][0])
+    ms, by = kern[name]
+    achieved = by / (ms * 1e-3) / 1e9
+    mac = FWD_MAC_TOK(2 * W["Mh"], W["V"]) * tokh
+    line = {
+        "metric": "layer fwd+bwd tokens/s", "value": world * W["B"] * W["T"] / (r["ms_step"] / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["ms_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": config,
+        "roofline": {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": None, "algorithmic_bytes_per_launch": by, "ms_per_launch": ms},
+        "kernels_ms": {"scan_fwd": r["fwd_ms"], "grad_zero_fill": r["zero_ms"], "scan_bwd": r["bwd_ms"]},
+        "flops": {"algorithmic_tflop_per_step": 3 * 2 * mac / 1e12,
+                  "achieved_tflops": 3 * 2 * mac / (r["ms_step"] * 1e-3) / 1e12, "peak_tflops": tfl},
+        "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"], "gpu_launches": 2 * args.steps,
+        "decode": r["decode"],
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

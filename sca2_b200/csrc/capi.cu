@@ -63,7 +63,7 @@ int check_common(const sca2_scan_args* a, bool step) {
     if (!a->wr || !a->wi) return fail(SCA2_ERR_ARG, "phase flavour needs wr and wi");
     if (a->v_times_beta) return fail(SCA2_ERR_ARG, "v_times_beta is a key-flavour option");
   }
-  if (!a->phw.ptr || !a->phq.ptr || !a->v.ptr)
+  if (a->T > 0 && (!a->phw.ptr || !a->phq.ptr || !a->v.ptr))  // empty inputs may be null
     return fail(SCA2_ERR_ARG, "phw/k, phq/q and v must be non-null");
   if (a->v_times_beta && !a->beta.ptr) return fail(SCA2_ERR_ARG, "v_times_beta needs beta");
   return SCA2_OK;

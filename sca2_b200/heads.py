@@ -1,0 +1,387 @@
+"""Drop-in heads whose scan runs on the sm_100a kernels of libsca2b200.so.
+
+Each class keeps the reference head's parameter names, shapes and buffers, so a
+reference state_dict loads with strict=True, and its protocol:
+
+    prefill(z, h, state=None) -> (u, state)     z, h (B,T,d); u (B,T,2dv)
+    step(z_t, h_t, state)     -> (u_t, state)   one token
+    init_state(B, device[, dtype])
+    forward(z, h) = prefill(z, h)[0]
+
+The projections (K, V, bproj, a, rgate) stay ordinary cuBLAS GEMMs; the scan (phase codes,
+decays, delta-rule solve, intra-chunk read, state carry) and the RMS read-out are the
+hand-written kernels.  State dicts are the reference's: {"sr", "si"} fp32 plus a 0-dim
+"pos" tensor (graph-capturable, sca2/decode.py:36-52).
+
+  LongHead          lapa/layer.py:170-412            (per-mode decay, delta write)
+  CHeadDelta        sca2/arch_cdelta.py:92-206       (delta write)
+  CHeadDeltaDamp*   sca2/arch_damp.py:43-259         (per-mode decay, delta write)
+  CHeadGated        sca2/arch_gatedc.py:58-193       (H heads, scalar decay, additive)
+"""
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+State = Dict[str, torch.Tensor]
+
+
+# ----------------------------------------------------------------------------------------
+#  configuration and frequency grids (same values as the reference's)
+# ----------------------------------------------------------------------------------------
+@dataclass
+class LaplaceConfig:
+    """Field-for-field the reference's LaplaceConfig (lapa/layer.py:82-114)."""
+    d: int = 128
+    M: int = 190
+    dv: int = 56
+    L: int = 16
+    ff: int = 448
+    theta_scale: float = 0.02
+    persist: float = 0.5
+    learn_persist: bool = False
+    mem_range: Optional[Tuple[float, float]] = None
+    lam_max: Optional[float] = None
+    chunk: int = 128
+    rope_base: float = 10000.0
+    slow_frac: float = 0.0
+    max_len: int = 1024
+    long_path: str = "batched"
+    gemm_dtype: Optional[torch.dtype] = None
+    beta_init: float = -2.0
+
+
+def rope_grid(M: int, base: float, slow_frac: float = 0.0, max_len: int = 1024) -> torch.Tensor:
+    """omega_m = pi * base^(-m/(M-1)), optionally with a slow slice of periods
+    [2 max_len, 20 max_len] (lapa/layer.py:126-139, sca2/ref.py:113-123)."""
+    n_slow = int(round(slow_frac * M))
+    n_fast = M - n_slow
+    k = torch.arange(n_fast, dtype=torch.float32)
+    fast = math.pi * base ** (-k / max(n_fast - 1, 1))
+    if n_slow == 0:
+        return fast
+    per = torch.logspace(math.log10(2 * max_len), math.log10(20 * max_len), n_slow)
+    return torch.cat([fast, 2 * math.pi / per])
+
+
+def freq_grid(name: str, M: int, max_len: int = 128, base: float = 10000.0,
+              slow_frac: float = 0.0) -> torch.Tensor:
+    """The reference's C-head grids: dft 2 pi k/M, len 2 pi k/max_len, rope (sca2/ref.py:56-124)."""
+    k = torch.arange(M, dtype=torch.float32)
+    if name == "dft":
+        return 2 * math.pi * k / M
+    if name == "len":
+        return 2 * math.pi * k / max_len
+    if name == "rope":
+        return rope_grid(M, base, slow_frac, max_len)
+    raise ValueError(f"unknown freq grid {name!r}")
+
+
+def _wd(p: torch.Tensor) -> torch.dtype:
+    return torch.float64 if p.dtype == torch.float64 else torch.float32
+
+
+def _rms(u: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """RMS read-out on the GPU kernel (sca2/ref.py:29-30)."""
+    if u.dtype == torch.float64:
+        raise TypeError("the sm_100a scan runs in float32 / bfloat16; float64 modules are a "
+                        "reference-only configuration")
+    return ops.rms(u, eps)
+
+
+def _gated_out(head, u, z):
+    """RMS read-out, or the raw read times rscale, optionally gated (sca2/ref.py:33-50)."""
+    u = _rms(u) if getattr(head, "rms_read", True) else u * head.rscale
+    return u * F.silu(head.rgate(z)) if getattr(head, "gated_read", False) else u
+
+
+def _value_dtype(z: torch.Tensor) -> torch.dtype:
+    """Dtype handed to the kernel for v / o: the autocast dtype on CUDA (the reference's
+    gemm_dtype policy, lapa/layer.py:225-230), else float32."""
+    if torch.is_autocast_enabled() and z.is_cuda:
+        dt = torch.get_autocast_gpu_dtype()
+        return dt if dt in (torch.bfloat16, torch.float32) else torch.float32
+    return torch.bfloat16 if z.dtype == torch.bfloat16 else torch.float32
+
+
+def _positions(T: int, pos: torch.Tensor, device) -> torch.Tensor:
+    return (torch.arange(T, device=device, dtype=torch.float32) + pos.float())[:, None]
+
+
+# ----------------------------------------------------------------------------------------
+#  LapA long head
+# ----------------------------------------------------------------------------------------
+class LongHead(nn.Module):
+    """lapa.layer.LongHead on the sm_100a scan: rope grid, damped accumulator with a
+    learned per-mode decay, delta-rule write (lapa/layer.py:170-412)."""
+
+    def __init__(self, cfg: LaplaceConfig):
+        super().__init__()
+        d, M, dv = cfg.d, cfg.M, cfg.dv
+        self.d, self.M, self.dv, self.cfg = d, M, dv, cfg
+        self.K = nn.Linear(d, M, False)
+        self.V = nn.Linear(d, dv, False)
+        self.theta = nn.Parameter(torch.zeros(M) if cfg.theta_scale == 0.0
+                                  else cfg.theta_scale * torch.randn(M))
+        self.wr = nn.Parameter(torch.ones(M))
+        self.wi = nn.Parameter(torch.zeros(M))
+        self.register_buffer("omega", rope_grid(M, cfg.rope_base, cfg.slow_frac, cfg.max_len))
+        self.bproj = nn.Linear(d, 1, True)
+        nn.init.zeros_(self.bproj.weight)
+        nn.init.constant_(self.bproj.bias, cfg.beta_init)
+        self.lam_max = cfg.lam_max if cfg.lam_max is not None else 1.0 / cfg.L
+        lo, hi = cfg.mem_range if cfg.mem_range is not None else (float(cfg.L), 32.0 * cfg.L)
+        mem = torch.exp(torch.empty(M).uniform_(math.log(lo), math.log(hi)))
+        n_pin = int(round(cfg.persist * M))
+        low = self.omega.abs().argsort()[:n_pin]
+        if cfg.learn_persist:
+            a = torch.logit((1.0 / mem / self.lam_max).clamp(1e-4, 1 - 1e-4))
+            a[low] = -8.0
+            self.lam_raw = nn.Parameter(a)
+            self.register_buffer("lam_mask", torch.ones(M))
+        else:
+            self.lam_raw = nn.Parameter(torch.log(torch.expm1(1.0 / mem)))
+            mask = torch.ones(M)
+            if n_pin:
+                mask[low] = 0.0
+            self.register_buffer("lam_mask", mask)
+
+    @property
+    def wd(self) -> torch.dtype:
+        return _wd(self.wr)
+
+    def lam(self) -> torch.Tensor:
+        if self.cfg.learn_persist:
+            return self.lam_max * torch.sigmoid(self.lam_raw.float())
+        return F.softplus(self.lam_raw.float()).clamp(max=self.lam_max) * self.lam_mask.float()
+
+    def _phase(self, x: torch.Tensor, p: torch.Tensor) -> torch.Tensor:
+        return self.K(x).float() * self.theta.float() + p * self.omega.float()
+
+    def init_state(self, B: int, device) -> State:
+        z = lambda: torch.zeros(B, self.M, self.dv, device=device, dtype=torch.float32)
+        return {"sr": z(), "si": z(), "pos": torch.zeros((), device=device, dtype=torch.float32)}
+
+    def forward(self, z, h):
+        return self.prefill(z, h)[0]
+
+    def prefill(self, z, h, state: Optional[State] = None):
+        B, T, _ = z.shape
+        st = state if state is not None else self.init_state(B, z.device)
+        p = _positions(T, st["pos"], z.device)
+        phw = self._phase(h, p)[:, :, None]
+        phq = self._phase(z, p)[:, :, None]
+        v = self.V(z).to(_value_dtype(z))[:, :, None]
+        beta = torch.sigmoid(self.bproj(z).float())
+        S0 = torch.cat([st["sr"], st["si"]], 1)[:, None].float()
+        o, S = ops.phase_scan(phw, phq, v, beta, None, self.lam()[None], self.wr.float()[None],
+                              self.wi.float()[None], S0)
+        u = _rms(o.reshape(B, T, 2 * self.dv)).to(z.dtype)
+        M = self.M
+        return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": st["pos"] + T}
+
+    def step(self, z_t, h_t, state: State):
+        M = self.M
+        p = state["pos"].float()
+        phw = self._phase(h_t, p)[:, None]
+        phq = self._phase(z_t, p)[:, None]
+        v = self.V(z_t).float()[:, None]
+        beta = torch.sigmoid(self.bproj(z_t).float())
+        S = torch.cat([state["sr"], state["si"]], 1)[:, None].float().contiguous()
+        o, S = ops.phase_step(phw, phq, v, beta, None, self.lam()[None], self.wr.float()[None],
+                              self.wi.float()[None], S, S_out=S)
+        u = _rms(o.reshape(-1, 2 * self.dv)).to(z_t.dtype)
+        return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": state["pos"] + 1}
+
+
+# ----------------------------------------------------------------------------------------
+#  sca2 C heads
+# ----------------------------------------------------------------------------------------
+class CHeadBase(nn.Module):
+    """Parameter container of the reference's C heads (sca2/ref.py:130-163)."""
+
+    def __init__(self, d, M, freq="dft", theta_scale=0.0, max_len=128, dv=None,
+                 gated_read=False, rope_base=10000.0, slow_frac=0.0):
+        super().__init__()
+        self.d, self.M, self.dv = d, M, (d // 2 if dv is None else dv)
+        self.freq, self.theta_scale, self.max_len = freq, theta_scale, max_len
+        self.K = nn.Linear(d, M, False)
+        self.V = nn.Linear(d, self.dv, False)
+        self.theta = nn.Parameter(torch.zeros(M) if theta_scale == 0.0 else theta_scale * torch.randn(M))
+        self.register_buffer("omega", freq_grid(freq, M, max_len, rope_base, slow_frac))
+        self.wr = nn.Parameter(torch.ones(M))
+        self.wi = nn.Parameter(torch.zeros(M))
+        self.gated_read = gated_read
+        if gated_read:
+            self.rgate = nn.Linear(d, 2 * self.dv, bias=False)
+
+    def init_state(self, B, device, dtype=torch.float32):
+        z = torch.zeros(B, self.M, self.dv, device=device, dtype=torch.float32)
+        return {"sr": z, "si": z.clone(), "pos": torch.zeros((), device=device, dtype=torch.float32),
+                "empty": True}
+
+    def forward(self, z, h):
+        return self.prefill(z, h)[0]
+
+
+class CHeadDelta(CHeadBase):
+    """Error-correcting (delta) complex write, sca2/arch_cdelta.py:92-206."""
+    CTX = int(os.environ.get("SCA2_CTX_CHUNK", 256))
+
+    def __init__(self, *a, cdelta_init=-2.0, **kw):
+        super().__init__(*a, **kw)
+        self.bproj = nn.Linear(self.d, 1, True)
+        nn.init.zeros_(self.bproj.weight)
+        nn.init.constant_(self.bproj.bias, cdelta_init)
+
+    def _pw(self, h, p):
+        return self.K(h).float() * self.theta.float() + p * self.omega.float()
+
+    def _pq(self, z, p):
+        return self.K(z).float() * self.theta.float() + p * self.omega.float()
+
+    def _value(self, z, h):
+        return self.V(z)
+
+    def _out(self, u, z):
+        return _gated_out(self, u, z)
+
+    def _lam(self):
+        return None
+
+    def prefill(self, z, h, state=None):
+        B, T, _ = z.shape
+        st = state if state is not None else self.init_state(B, z.device)
+        p = _positions(T, st["pos"], z.device)
+        lam = self._lam()
+        S0 = None if st.get("empty", False) else torch.cat([st["sr"], st["si"]], 1)[:, None].float()
+        o, S = ops.phase_scan(self._pw(h, p)[:, :, None], self._pq(z, p)[:, :, None],
+                              self._value(z, h).to(_value_dtype(z))[:, :, None],
+                              torch.sigmoid(self.bproj(z).float()), None,
+                              None if lam is None else lam[None], self.wr.float()[None],
+                              self.wi.float()[None], S0)
+        M = self.M
+        u = self._out(o.reshape(B, T, 2 * self.dv).float(), z).to(z.dtype)
+        return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": st["pos"] + T, "empty": False}
+
+    def step(self, z_t, h_t, state):
+        M = self.M
+        p = state["pos"].float()
+        lam = self._lam()
+        S = torch.cat([state["sr"], state["si"]], 1)[:, None].float().contiguous()
+        o, S = ops.phase_step(self._pw(h_t, p)[:, None], self._pq(z_t, p)[:, None],
+                              self._value(z_t, h_t).float()[:, None], torch.sigmoid(self.bproj(z_t).float()),
+                              None, None if lam is None else lam[None], self.wr.float()[None],
+                              self.wi.float()[None], S, S_out=S)
+        u = self._out(o.reshape(-1, 2 * self.dv), z_t).to(z_t.dtype)
+        return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": state["pos"] + 1, "empty": False}
+
+
+class CHeadDeltaDamp(CHeadDelta):
+    """cdelta with a learned per-mode decay on the accumulator, sca2/arch_damp.py:43-69."""
+    LAM_MAX = 0.125
+    PERSIST = 0.0
+
+    def __init__(self, *a, mem_range=(64.0, 4096.0), **kw):
+        super().__init__(*a, **kw)
+        lo, hi = mem_range
+        mem = torch.exp(torch.empty(self.M).uniform_(math.log(lo), math.log(hi)))
+        self.lam_raw = nn.Parameter(torch.log(torch.expm1(1.0 / mem)))
+        n_pin = int(round(self.PERSIST * self.M))
+        mask = torch.ones(self.M)
+        if n_pin:
+            mask[self.omega.abs().argsort()[:n_pin]] = 0.0
+        self.register_buffer("lam_mask", mask)
+
+    def lam(self):
+        return F.softplus(self.lam_raw.float()).clamp(max=self.LAM_MAX) * self.lam_mask.float()
+
+    def _lam(self):
+        return self.lam()
+
+
+class CHeadDeltaDampHalf(CHeadDeltaDamp):
+    PERSIST = 0.5
+
+
+class CHeadDeltaDampHalfFast(CHeadDeltaDampHalf):
+    LAM_MAX = min(2.0, 60.0 / CHeadDelta.CTX)
+
+
+class CHeadGated(CHeadBase):
+    """Multi-head C head with a data-dependent scalar decay per head, optional separate
+    read key (sepq) and gated read-out (sca2/arch_gatedc.py:58-193)."""
+    CTX = int(os.environ.get("SCA2_CTX_CHUNK", 256))
+
+    def __init__(self, d, M, freq="dft", theta_scale=0.0, max_len=128, dv=None,
+                 gated_read=False, heads=1, decay=False, sepq=False, decay_init="gdn",
+                 rope_base=10000.0, slow_frac=0.0):
+        super().__init__(d, M, freq, theta_scale, max_len, dv, gated_read, rope_base, slow_frac)
+        assert M % heads == 0 and self.dv % heads == 0
+        self.H, self.Mh, self.dvh = heads, M // heads, self.dv // heads
+        self.decay, self.sepq = decay, sepq
+        if sepq:
+            self.Kq = nn.Linear(d, M, False)
+            with torch.no_grad():
+                self.Kq.weight.copy_(self.K.weight)
+        if decay:
+            self.a = nn.Linear(d, heads, False)
+            if decay_init == "soft":
+                A = torch.ones(heads)
+                dt = torch.full((heads,), 0.01)
+            else:
+                A = torch.empty(heads).uniform_(1, 16)
+                dt = torch.exp(torch.rand(heads) * (math.log(0.1) - math.log(0.001))
+                               + math.log(0.001)).clamp(min=1e-4)
+            self.A_log = nn.Parameter(torch.log(A))
+            self.dt_bias = nn.Parameter(dt + torch.log(-torch.expm1(-dt)))
+
+    def init_state(self, B, device, dtype=torch.float32):
+        z = torch.zeros(B, self.H, self.Mh, self.dvh, device=device, dtype=torch.float32)
+        return {"sr": z, "si": z.clone(), "pos": torch.zeros((), device=device, dtype=torch.float32),
+                "empty": True}
+
+    def _phases(self, z, h, p):
+        kq = self.Kq(z) if self.sepq else self.K(z)
+        th, om = self.theta.float(), self.omega.float()
+        return self.K(h).float() * th + p * om, kq.float() * th + p * om
+
+    def _logdecay(self, z):
+        return -torch.exp(self.A_log.float()) * F.softplus(self.a(z).float() + self.dt_bias.float())
+
+    def prefill(self, z, h, state=None):
+        B, T, _ = z.shape
+        H, Mh, dvh = self.H, self.Mh, self.dvh
+        st = state if state is not None else self.init_state(B, z.device)
+        p = _positions(T, st["pos"], z.device)
+        pw, pq = self._phases(z, h, p)
+        g = self._logdecay(z) if self.decay else None
+        S0 = None if st.get("empty", False) else torch.cat([st["sr"], st["si"]], 2).float()
+        o, S = ops.phase_scan(pw.view(B, T, H, Mh), pq.view(B, T, H, Mh),
+                              self.V(z).to(_value_dtype(z)).view(B, T, H, dvh), None, g, None,
+                              self.wr.float().view(H, Mh), self.wi.float().view(H, Mh), S0)
+        u = torch.cat([o[:, :, :, 0].reshape(B, T, self.dv), o[:, :, :, 1].reshape(B, T, self.dv)], -1)
+        u = _gated_out(self, u.float(), z).to(z.dtype)
+        return u, {"sr": S[:, :, :Mh], "si": S[:, :, Mh:], "pos": st["pos"] + T, "empty": False}
+
+    def step(self, z_t, h_t, state):
+        B = z_t.size(0)
+        H, Mh, dvh = self.H, self.Mh, self.dvh
+        p = state["pos"].float()
+        pw, pq = self._phases(z_t, h_t, p)
+        g = self._logdecay(z_t) if self.decay else None
+        S = torch.cat([state["sr"], state["si"]], 2).float().contiguous()
+        o, S = ops.phase_step(pw.view(B, H, Mh), pq.view(B, H, Mh), self.V(z_t).float().view(B, H, dvh),
+                              None, g, None, self.wr.float().view(H, Mh), self.wi.float().view(H, Mh),
+                              S, S_out=S)
+        u = torch.cat([o[:, :, 0].reshape(B, self.dv), o[:, :, 1].reshape(B, self.dv)], -1)
+        u = _gated_out(self, u, z_t).to(z_t.dtype)
+        return u, {"sr": S[:, :, :Mh], "si": S[:, :, Mh:], "pos": state["pos"] + 1, "empty": False}

@@ -378,3 +378,100 @@ class _Rms(torch.autograd.Function):
 def rms(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """u = x * rsqrt(mean(x^2, -1) + eps) (sca2/ref.py:29-30), on the GPU kernel."""
     return _Rms.apply(x, eps)
+
+
+# ======================================================================================
+#  preallocated plans (benchmarks, CUDA-graph capture)
+# ======================================================================================
+class PhaseScanPlan:
+    """A phase-flavour scan with every output / saved / gradient buffer allocated once, so
+    fwd() and bwd() are exactly one library call each (plus the zero-fill of the gradient
+    accumulators in bwd) and can be timed or captured in a CUDA graph."""
+
+    def __init__(self, phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None, S0=None,
+                 need_grad=True):
+        _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0)
+        _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0)
+        self.inp = dict(phw=_inner(phw.float()), phq=_inner(phq.float()), v=_inner(v),
+                        beta=_f32(beta), g=_f32(g), lam=None if lam is None else lam.float().contiguous(),
+                        wr=wr.float().contiguous(), wi=wi.float().contiguous(),
+                        S0=None if S0 is None else S0.float().contiguous())
+        i = self.inp
+        B, T, H, Mh = i["phw"].shape
+        V = i["v"].shape[-1]
+        dev, dt = i["v"].device, i["v"].dtype
+        self.shape = (B, T, H, Mh, V)
+        self.args = _phase_args(i["phw"], i["phq"], i["v"], i["beta"], i["g"], i["lam"], i["wr"], i["wi"], i["S0"])
+        self.o = torch.empty(B, T, H, 2, V, device=dev, dtype=dt)
+        self.S = torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32)
+        self.lib = _lib.load()
+        self.cs = None
+        if need_grad:
+            NC = self.lib.sca2_num_chunks(T)
+            self.cs = torch.empty(B, H, NC, 2 * Mh, V, device=dev, dtype=torch.float32)
+            z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
+            self.grads = dict(phw=z(B, T, H, Mh), phq=z(B, T, H, Mh),
+                              v=torch.empty(B, T, H, V, device=dev, dtype=dt),
+                              beta=z(B, T, H) if beta is not None else None,
+                              g=z(B, T, H) if g is not None else None,
+                              lam=z(H, Mh) if lam is not None else None, wr=z(H, Mh), wi=z(H, Mh),
+                              S0=torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32))
+            gr = ScanGrads()
+            G = self.grads
+            gr.dphw, gr.dphq, gr.dv = _tok(G["phw"]), _tok(G["phq"]), _tok(G["v"])
+            gr.dbeta, gr.dg = _tok(G["beta"]), _tok(G["g"])
+            gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(G["lam"]), _ptr(G["wr"]), _ptr(G["wi"]), _ptr(G["S0"])
+            self.gr = gr
+            self._acc = [t for k, t in G.items() if t is not None and k not in ("v", "S0")]
+
+    def fwd(self):
+        _lib.check(self.lib.sca2_scan_fwd(C_ref(self.args), _out(self.o), _ptr(self.S), _ptr(self.cs),
+                                          _stream()), "scan_fwd")
+        return self.o, self.S
+
+    def zero_grads(self):
+        for t in self._acc:
+            t.zero_()
+
+    def bwd(self, dO, dS=None, zero=True):
+        if zero:
+            self.zero_grads()
+        _lib.check(self.lib.sca2_scan_bwd(C_ref(self.args), _out(dO), _ptr(dS), _ptr(self.cs), C_ref(self.gr),
+                                          _stream()), "scan_bwd")
+        return self.grads
+
+
+class PhaseStepPlan:
+    """Decode step with fixed buffers: step(t) advances the state in place using the inputs
+    of token t from preloaded (B,T,H,...) tensors; capturable in a CUDA graph."""
+
+    def __init__(self, phw, phq, v, beta, g, lam, wr, wi, S):
+        _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S)
+        B, T, H, Mh = phw.shape
+        V = v.shape[-1]
+        if S.dtype != torch.float32 or not S.is_contiguous() or tuple(S.shape) != (B, H, 2 * Mh, V):
+            raise _lib.Sca2Error("state must be a contiguous fp32 (B,H,2Mh,V) tensor")
+        self.inp = dict(phw=_inner(phw.float()), phq=_inner(phq.float()), v=_inner(v),
+                        beta=_f32(beta), g=_f32(g), lam=None if lam is None else lam.float().contiguous(),
+                        wr=wr.float().contiguous(), wi=wi.float().contiguous())
+        self.S = S
+        self.o = torch.empty(B, 1, H, 2, V, device=v.device, dtype=v.dtype)
+        self.lib = _lib.load()
+        self.args = []
+        i = self.inp
+        for t in range(T):
+            a = ScanArgs()
+            a.flavor = _lib.FLAVOR_PHASE
+            a.B, a.T, a.H, a.K, a.V = B, 1, H, 2 * Mh, V
+            a.io_dtype = _DT[v.dtype]
+            a.q_scale = 1.0
+            sl = lambda x: None if x is None else x[:, t]
+            a.phw, a.phq, a.v = _tok(sl(i["phw"]), True), _tok(sl(i["phq"]), True), _tok(sl(i["v"]), True)
+            a.beta, a.g = _tok(sl(i["beta"]), True), _tok(sl(i["g"]), True)
+            a.lam, a.wr, a.wi, a.S0 = _ptr(i["lam"]), _ptr(i["wr"]), _ptr(i["wi"]), None
+            self.args.append(a)
+
+    def step(self, t):
+        p = self.S.data_ptr()
+        _lib.check(self.lib.sca2_scan_step(C_ref(self.args[t]), p, p, _out(self.o), _stream()), "scan_step")
+        return self.o

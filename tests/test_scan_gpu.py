@@ -161,7 +161,7 @@ def test_phase_vs_oracle_bf16(case):
     d["dO"] = torch.tensor(d["dO"]).bfloat16().double().numpy()
     o, S, gr = _run_phase(d, d["dO"], d["dS"], dtype=torch.bfloat16)
     ro, rS, rg = _oracle_phase(d)
-    u, ru = rms_np(o.double().cpu().numpy().reshape(B, T, H, -1)), rms_np(ro.reshape(B, T, H, -1))
+    u, ru = rms_np(o.detach().double().cpu().numpy().reshape(B, T, H, -1)), rms_np(ro.reshape(B, T, H, -1))
     assert np.abs(u - ru).max() < TOL_BF16_ABS and cosine(u, ru) > TOL_BF16_COS
     assert relerr(S, rS) < TOL_BF16_ABS and cosine(S, rS) > TOL_BF16_COS
     for n in ("phw", "phq", "v", "beta", "g", "lam", "wr", "wi", "S0"):
@@ -225,7 +225,7 @@ def test_empty_sequence():
     ops = _ops()
     d = seeded_phase_inputs(2, 0, 2, 8, 8)
     o, S, _ = _run_phase(d, grad=False)
-    assert o.shape[1] == 0 and relerr(S, d["S0"]) == 0.0
+    assert o.shape[1] == 0 and relerr(S, d["S0"].astype(np.float32)) == 0.0
 
 
 def test_strided_inputs():
@@ -235,7 +235,7 @@ def test_strided_inputs():
     d = seeded_phase_inputs(B, T, H, Mh, V, seed=11)
     big = torch.randn(B, T, H * Mh + 5, device="cuda")
     big[..., :H * Mh] = cuda(d["phw"]).reshape(B, T, H * Mh)
-    phw = big[..., :H * Mh].view(B, T, H, Mh) if False else big[..., :H * Mh].unflatten(-1, (H, Mh))
+    phw = big[..., :H * Mh].unflatten(-1, (H, Mh))
     vv = torch.randn(B, T, H, V + 4, device="cuda")
     vv[..., :V] = cuda(d["v"])
     o, S = ops.phase_scan(phw, cuda(d["phq"]), vv[..., :V], cuda(d["beta"]), None, cuda(d["lam"]),
@@ -275,7 +275,7 @@ def test_full_size_phase_slices_bf16():
               for k in ("phw", "phq", "v", "beta", "g", "dO")}
         sl.update(lam=d["lam"][h:h + 1], wr=d["wr"][h:h + 1], wi=d["wi"][h:h + 1], S0=None, dS=None)
         ro, rS, rg = _oracle_phase(sl)
-        oo = o[b:b + 1, :, h:h + 1].double().cpu().numpy()
+        oo = o[b:b + 1, :, h:h + 1].detach().double().cpu().numpy()
         u, ru = rms_np(oo.reshape(1, T, 1, -1)), rms_np(ro.reshape(1, T, 1, -1))
         assert np.abs(u - ru).max() < TOL_BF16_ABS and cosine(u, ru) > TOL_BF16_COS
         assert relerr(S[b:b + 1, h:h + 1], rS) < TOL_BF16_ABS
