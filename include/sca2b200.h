@@ -158,6 +158,25 @@ SCA2_API int sca2_rms_fwd(const void* x, void* u, int64_t N, int32_t D, float ep
 SCA2_API int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D,
                  float eps, int32_t io_dtype, void* stream);
 
+/* Size of the device array behind sca2_scan_fwd_bwd_noalloc (every GPU that loads the
+ * library holds it until the process exits). */
+#define SCA2_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* Forward + backward in one call that allocates nothing and takes no workspace: for
+ * callers that cannot allocate device memory (a plugin inside a runtime that owns the
+ * device memory pool, or a path where cudaMalloc must not be called).  No counterpart
+ * in the reference.  Same arguments and gradient contract as sca2_scan_fwd followed by
+ * sca2_scan_bwd (the per-token and per-head gradient buffers are accumulated into and
+ * must be zero-filled by the caller), minus chunk_states: the state entering each chunk
+ * lives in a static device array of SCA2_NOALLOC_SCRATCH_BYTES, so B*H*NC*K*V*4 bytes
+ * (NC = sca2_num_chunks(T)) must fit in it; larger problems return SCA2_ERR_ARG before
+ * any launch.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and must come before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised. */
+SCA2_API int sca2_scan_fwd_bwd_noalloc(const sca2_scan_args* a, sca2_out o, float* S_final,
+                                       sca2_out dO, const float* dS_final,
+                                       const sca2_scan_grads* gr, void* stream);
+
 /* Thread-local message of the last failing call on this thread. */
 SCA2_API const char* sca2_last_error(void);
 

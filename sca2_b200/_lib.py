@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libsca2b200.so")
 
 SCA2_OK, SCA2_ERR_ARG, SCA2_ERR_UNSUPPORTED, SCA2_ERR_CUDA = 0, 1, 2, 3
 SCA2_F32, SCA2_BF16 = 0, 1
+SCA2_NOALLOC_SCRATCH_BYTES = 16 << 20  # include/sca2b200.h
 FLAVOR_PHASE, FLAVOR_KEY = 0, 1
 
 
@@ -54,6 +55,8 @@ SIGNATURES = [
                                C.c_int32, C.c_void_p]),
     ("sca2_rms_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
                                C.c_float, C.c_int32, C.c_void_p]),
+    ("sca2_scan_fwd_bwd_noalloc", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, Out, C.c_void_p,
+                                            C.POINTER(ScanGrads), C.c_void_p]),
     ("sca2_last_error", C.c_char_p, []),
     ("sca2_version", C.c_char_p, []),
 ]

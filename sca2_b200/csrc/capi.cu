@@ -86,6 +86,11 @@ int check_scan(const sca2_scan_args* a, bool bwd) {
 
 }  // namespace
 
+namespace sca2 {
+// Lets the other entry-point files report through sca2_last_error().
+void set_last_error(const std::string& msg) { g_err = msg; }
+}  // namespace sca2
+
 extern "C" {
 
 const char* sca2_last_error(void) { return g_err.c_str(); }

@@ -475,3 +475,42 @@ class PhaseStepPlan:
         p = self.S.data_ptr()
         _lib.check(self.lib.sca2_scan_step(C_ref(self.args[t]), p, p, _out(self.o), _stream()), "scan_step")
         return self.o
+
+
+def phase_scan_fwd_bwd_noalloc(phw, phq, v, beta, g, lam, wr, wi, dO, S0=None, dS=None):
+    """Forward and backward of the phase scan in ONE library call that allocates nothing on
+    the device and takes no workspace (sca2_scan_fwd_bwd_noalloc): for callers that cannot
+    allocate device memory.  The chunk states live in the library's static 16 MiB device
+    array, so B*H*ceil(T/32)*2Mh*V*4 bytes must fit; calls that overlap on the GPU race on
+    that array.  This wrapper allocates the outputs with torch only for convenience; a caller
+    without an allocator passes its own buffers through the C ABI.  Returns
+    (o, S, grads dict) with the same meaning as phase_scan + autograd."""
+    _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0)
+    _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0, dO, dS)
+    phw, phq, v = _inner(phw.float()), _inner(phq.float()), _inner(v)
+    beta, g = _f32(beta), _f32(g)
+    lam = None if lam is None else lam.float().contiguous()
+    wr, wi = wr.float().contiguous(), wi.float().contiguous()
+    S0 = None if S0 is None else S0.float().contiguous()
+    dO = dO.to(v.dtype)
+    if dO.stride(-1) != 1:
+        dO = dO.contiguous()
+    dS = None if dS is None else dS.float().contiguous()
+    B, T, H, Mh = phw.shape
+    V = v.shape[-1]
+    dev = v.device
+    a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
+    o = torch.empty(B, T, H, 2, V, device=dev, dtype=v.dtype)
+    S = torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32)
+    z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
+    G = dict(phw=z(B, T, H, Mh), phq=z(B, T, H, Mh), v=torch.empty(B, T, H, V, device=dev, dtype=v.dtype),
+             beta=z(B, T, H) if beta is not None else None, g=z(B, T, H) if g is not None else None,
+             lam=z(H, Mh) if lam is not None else None, wr=z(H, Mh), wi=z(H, Mh),
+             S0=torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32))
+    gr = ScanGrads()
+    gr.dphw, gr.dphq, gr.dv = _tok(G["phw"]), _tok(G["phq"]), _tok(G["v"])
+    gr.dbeta, gr.dg = _tok(G["beta"]), _tok(G["g"])
+    gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(G["lam"]), _ptr(G["wr"]), _ptr(G["wi"]), _ptr(G["S0"])
+    _lib.check(_lib.load().sca2_scan_fwd_bwd_noalloc(C_ref(a), _out(o), _ptr(S), _out(dO), _ptr(dS), C_ref(gr),
+                                                     _stream()), "scan_fwd_bwd_noalloc")
+    return o, S, G
