@@ -177,6 +177,12 @@ SCA2_API int sca2_scan_fwd_bwd_noalloc(const sca2_scan_args* a, sca2_out o, floa
                                        sca2_out dO, const float* dS_final,
                                        const sca2_scan_grads* gr, void* stream);
 
+/* Read and clear the device fault word of the tensor-core kernels (synchronises the
+ * device).  Bit 0: an internal wait on the tensor core timed out; the kernel left early
+ * and its outputs are not valid.  Kernels never trap: this word is how a device-side
+ * failure reaches the host. */
+SCA2_API int sca2_fault_status(uint32_t* faults);
+
 /* Thread-local message of the last failing call on this thread. */
 SCA2_API const char* sca2_last_error(void);
 

@@ -57,6 +57,7 @@ SIGNATURES = [
                                C.c_float, C.c_int32, C.c_void_p]),
     ("sca2_scan_fwd_bwd_noalloc", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, Out, C.c_void_p,
                                             C.POINTER(ScanGrads), C.c_void_p]),
+    ("sca2_fault_status", C.c_int, [C.POINTER(C.c_uint32)]),
     ("sca2_last_error", C.c_char_p, []),
     ("sca2_version", C.c_char_p, []),
 ]
@@ -86,6 +87,13 @@ def load(path: str = LIB_PATH):
             fn.argtypes = args
         _lib = lib
         return lib
+
+
+def device_faults() -> int:
+    """Read and clear the device fault word (bit 0: a tensor-core wait timed out)."""
+    f = C.c_uint32(0)
+    check(load().sca2_fault_status(C.byref(f)), "fault_status")
+    return int(f.value)
 
 
 def check(rc: int, what: str):

@@ -24,6 +24,11 @@ cudaError_t launch_rms_fwd(const void* x, void* u, int64_t N, int D, float eps, 
                            cudaStream_t st);
 cudaError_t launch_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int D, float eps,
                            int dt, cudaStream_t st);
+// scan_tc.cu
+int tc_fwd_vb(int K, int V, int R, int max_smem);
+cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
+                        float* cstates, int NCS, cudaStream_t st);
+cudaError_t tc_read_faults(unsigned int* out);
 }  // namespace sca2
 
 namespace {
@@ -97,6 +102,15 @@ const char* sca2_last_error(void) { return g_err.c_str(); }
 
 const char* sca2_version(void) { return "sca2b200 0.1.0 (sm_100a)"; }
 
+int sca2_fault_status(uint32_t* faults) {
+  if (!faults) return fail(SCA2_ERR_ARG, "null output");
+  unsigned int f = 0;
+  cudaError_t e = sca2::tc_read_faults(&f);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_fault_status");
+  *faults = f;
+  return SCA2_OK;
+}
+
 int32_t sca2_num_chunks(int32_t T) { return sca2::f32_num_chunks(T); }
 
 int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* chunk_states,
@@ -114,7 +128,11 @@ int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* ch
     }
     return SCA2_OK;
   }
-  cudaError_t e = sca2::f32_scan_fwd(*a, o, S_final, chunk_states, st);
+  // bf16 inference (no saved chunk states) runs on the tensor cores when the shape is covered
+  const int R = a->flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
+  const int vb = (a->io_dtype == SCA2_BF16 && !chunk_states) ? sca2::tc_fwd_vb(a->K, a->V, R, max_optin_smem()) : 0;
+  cudaError_t e = vb ? sca2::tc_scan_fwd(*a, vb, o, S_final, chunk_states, sca2::f32_num_chunks(a->T), st)
+                     : sca2::f32_scan_fwd(*a, o, S_final, chunk_states, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd");
   return SCA2_OK;
 }

@@ -1,0 +1,399 @@
+// Tensor-core (tcgen05 / TMEM) forward scan for bf16 inputs on sm_100a.
+//
+// One CTA per (batch*head, block of VB value columns), 64-token chunks walked in order.
+// Per chunk (same algebra as the fp32 path and the oracle's forward_chunked):
+//
+//   state-independent   G   = KR KW^T                  (tcgen05, fp32 accumulate)
+//                       P   = QR KW^T                  (codes split hi + lo)
+//                       T   = (I + diag(beta) Gr)^{-1} (fp32, blocked, CUDA cores)
+//                       U^T = V'^T T^T                 (tcgen05)
+//                       Wk  = T Z^T, Z = beta a k e^{-lam i}/kappa
+//   state chain         X^T = (d1 .* S)^T Wk^T
+//   (S^T fp32 in regs)  Os  = QR (d1 .* S)
+//                       E^T = U^T - X^T
+//                       Op  = P E                      (P, E split hi + lo)
+//                       O   = (a / kappa) .* Os + Op
+//                       Su^T = E^T (KW diag(w))        (E split hi + lo)
+//                       S   = dCm1 .* (a_last d1 .* S + Su)
+//
+// All MMA operands are bf16 in shared memory (K-major, no swizzle, see umma.cuh); every
+// accumulator is fp32 in TMEM and the state itself stays fp32 in registers.  The products
+// whose results feed other products are oriented so that each thread's accumulator row is a
+// contiguous run of the next operand, and operands are written with 16-byte stores.  Where a
+// bf16 operand alone would miss the bf16 parity bar (the intra-chunk read kernel P and the
+// corrected values E) it is carried as a hi + lo pair (three products hi*hi + hi*lo + lo*hi),
+// which keeps about 16 mantissa bits.  Each MMA batch is issued by one thread and completes
+// on an mbarrier whose wait is bounded: on a timeout the CTA records a fault bit, waits
+// (bounded) once more for its MMAs, frees its TMEM and returns.
+//
+// The states entering chunks are saved in the (B,H,ceil(T/32),K,V) buffer of the fp32 path,
+// at slot 2c for the 64-token chunk c, so both paths share one buffer shape.
+#include "tc_common.cuh"
+
+namespace sca2 {
+namespace tc {
+
+__device__ unsigned int g_fault;  // bit 0: a bounded mbarrier wait timed out
+
+// byte offsets of the shared-memory carve-up (operands 1024-byte aligned).  The lo halves of
+// the split codes are only read by the P product and the fp32 inversion scratch is only used
+// after that product has completed, so the two share one region.
+template <int KD, int VB, int R>
+struct FwdLayout {
+  static constexpr int al(int x) { return (x + 1023) & ~1023; }
+  static constexpr int mx(int a, int b) { return a > b ? a : b; }
+  static constexpr int KR = 0;                                  // C x KD
+  static constexpr int KW = KR + al(C * KD * 2);                // C x KD (hi)
+  static constexpr int QR = KW + al(C * KD * 2);                // R*C x KD (hi)
+  static constexpr int Z = QR + al(R * C * KD * 2);             // KD x C
+  static constexpr int VT = Z + al(KD * C * 2);                 // VB x C
+  static constexpr int KWD = VT + al(VB * C * 2);               // KD x C
+  static constexpr int TB = KWD + al(KD * C * 2);               // C x C
+  static constexpr int PB = TB + al(C * C * 2);                 // R*C x C (hi)
+  static constexpr int PBL = PB + al(R * C * C * 2);            // R*C x C (lo)
+  static constexpr int WK = PBL + al(R * C * C * 2);            // C x KD
+  static constexpr int SB = WK + al(C * KD * 2);                // VB x KD: (d1 .* S)^T
+  static constexpr int EB = SB + al(VB * KD * 2);               // VB x C (hi): E^T
+  static constexpr int EBL = EB + al(VB * C * 2);               // VB x C (lo)
+  static constexpr int A0 = EBL + al(VB * C * 2);               // shared region
+  static constexpr int KWL = A0;                                //   C x KD (lo)
+  static constexpr int QRL = KWL + al(C * KD * 2);              //   R*C x KD (lo)
+  static constexpr int LS = A0;                                 //   fp32 C x LDF
+  static constexpr int TS = LS + al(C * LDF * 4);               //   fp32 C x LDF
+  static constexpr int WS = TS + al(C * LDF * 4);               //   fp32 3 x 256
+  static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(3 * 256 * 4));
+  static constexpr int SC = A0_END;
+  // scalars (floats): beta[C], Gc[C], a[C], w[C], d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD]
+  static constexpr int SC_FLOATS = 4 * C + 5 * KD;
+  static constexpr int MBAR = SC + al(SC_FLOATS * 4);
+  static constexpr int TOTAL = MBAR + 64;  // mbarrier (8 B), TMEM base (4 B), error flag (4 B)
+};
+
+// TMEM columns: [0,128) G | P, later Op ; [128,192) U^T, later X^T ; [192, 192+KD) Wk, later
+// Su^T ; then Os
+template <int KD, int VB>
+struct Cols {
+  static constexpr int G = 0, P = 64, OP = 0, UT = 128, XT = 128, WK = 192, SUT = 192, OS = 192 + KD;
+  static constexpr int NEED = OS + VB;
+  static constexpr int ALLOC = NEED <= 256 ? 256 : 512;
+};
+
+template <int FL, int KD, int VB, int R>
+__global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
+                                                    float* cstates, int NCS, int flags) {
+  using L = FwdLayout<KD, VB, R>;
+  using CO = Cols<KD, VB>;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  const int vb0 = blockIdx.y * VB;
+  const int V = p.V;
+  const bool has_g = p.g.ptr != nullptr;
+  const float kappa = FL == SCA2_FLAVOR_PHASE ? (float)(KD / 2) : 1.f;
+  const float ik = 1.f / kappa;
+  float* sc = reinterpret_cast<float*>(sm + L::SC);
+  Gates gates{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  float* s_d1 = sc + 4 * C;
+  float* s_dCm1 = s_d1 + KD;
+  float* s_lam = s_dCm1 + KD;
+  float* s_wr = s_lam + KD;
+  float* s_wi = s_wr + KD;
+  float* LS = reinterpret_cast<float*>(sm + L::LS);
+  float* TS = reinterpret_cast<float*>(sm + L::TS);
+  float* WS = reinterpret_cast<float*>(sm + L::WS);
+  bf16* VT = reinterpret_cast<bf16*>(sm + L::VT);
+  bf16* TB = reinterpret_cast<bf16*>(sm + L::TB);
+  bf16* PB = reinterpret_cast<bf16*>(sm + L::PB);
+  bf16* PBL = reinterpret_cast<bf16*>(sm + L::PBL);
+  bf16* WK = reinterpret_cast<bf16*>(sm + L::WK);
+  bf16* SB = reinterpret_cast<bf16*>(sm + L::SB);
+  bf16* EB = reinterpret_cast<bf16*>(sm + L::EB);
+  bf16* EBL = reinterpret_cast<bf16*>(sm + L::EBL);
+  CodeOps<FL, KD, R> cops{reinterpret_cast<bf16*>(sm + L::KR), reinterpret_cast<bf16*>(sm + L::KW),
+                          reinterpret_cast<bf16*>(sm + L::KWL), reinterpret_cast<bf16*>(sm + L::QR),
+                          reinterpret_cast<bf16*>(sm + L::QRL), reinterpret_cast<bf16*>(sm + L::Z),
+                          reinterpret_cast<bf16*>(sm + L::KWD)};
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
+  volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
+
+  // ---- set-up: per-head constants, mbarrier, TMEM
+  constexpr int KH = FL == SCA2_FLAVOR_PHASE ? KD / 2 : KD;
+  for (int m = tid; m < KD; m += NT) {
+    const float l = p.lam ? p.lam[h * KH + (m % KH)] : 0.f;
+    s_lam[m] = l;
+    s_d1[m] = expf(-l);
+    s_wr[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wr[h * KH + m] : 0.f;
+    s_wi[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wi[h * KH + m] : 0.f;
+  }
+  if (tid == 0) {
+    umma::mbar_init(mbar, 1);
+    umma::fence_mbar_init();
+    *s_err = 0;
+  }
+  if (tid < 32) umma::tmem_alloc(s_tmem, CO::ALLOC);
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tb = *s_tmem;
+  uint32_t phase = 0;
+
+  // ---- state S^T: fp32 registers in the layout of the Su^T accumulator (M = VB, N = KD)
+  constexpr int NS = KD / 2;
+  float Sreg[NS];
+  const int srow = frag_row<VB>();
+  const bool sown = owns_rows<VB>();
+  const int64_t bhKV = ((int64_t)b * p.H + h) * KD * (int64_t)V;
+  const int64_t sbase = bhKV + vb0 + srow;
+#pragma unroll
+  for (int q = 0; q < KD / 32; ++q) {
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = frag_col0<VB, KD>(q) + j;
+      const float s = (sown && p.S0) ? p.S0[sbase + (int64_t)m * V] : 0.f;
+      Sreg[16 * q + j] = s;
+      x[j] = s * s_d1[m];
+    }
+    if (sown) {
+      st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q), KD), x);
+      st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q) + 8, KD), x + 8);
+    }
+  }
+  float Ureg[C / 2];
+
+  auto wait_mma = [&]() -> bool {
+    if (!umma::mbar_wait(mbar, phase)) *s_err = 1;
+    phase ^= 1u;
+    __syncthreads();
+    umma::fence_after_sync();
+    return *s_err == 0;
+  };
+
+  const int NC = (p.T + C - 1) / C;
+  bool ok = true;
+  for (int c = 0; c < NC && ok; ++c) {
+    const int t0 = c * C, Cl = min(C, p.T - t0);
+    if (cstates && sown) {
+      // state entering chunk c -> slot 2c of the (B,H,NCS,K,V) buffer
+      const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0 + srow;
+#pragma unroll
+      for (int q = 0; q < KD / 32; ++q)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) cstates[cb + (int64_t)(frag_col0<VB, KD>(q) + j) * V] = Sreg[16 * q + j];
+    }
+    // ---- operands of the chunk
+    ValueLoad<VB> vl;
+    load_values<VB>(p, vl, b, h, t0, Cl, vb0);
+    load_gates(p, gates, b, h, t0, Cl);
+    for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * (float)(Cl - 1));
+    __syncthreads();
+    build_codes<FL, KD, R>(p, cops, gates, s_lam, s_wr, s_wi, flags, b, h, t0, Cl, ik);
+    store_values<VB>(p, vl, gates.beta, VT);
+    publish_smem();
+    if (tid == 0) {
+      umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
+      umma::gemm(tb + CO::P, sm + L::QR, sm + L::KW, R * 64, 64, KD, false);
+      umma::gemm(tb + CO::P, sm + L::QR, sm + L::KWL, R * 64, 64, KD, true);
+      umma::gemm(tb + CO::P, sm + L::QRL, sm + L::KW, R * 64, 64, KD, true);
+      umma::commit(mbar);
+    }
+    if (!(ok = wait_mma())) break;
+    // ---- L = beta Gr (fp32) and P (hi + lo), masked and decayed
+    for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
+      const float bi = gates.beta[i] * ik, gi = gates.Gc[i];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int jj = j0 + j;
+        const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
+        LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
+      }
+    });
+    for_frag<R * 64, 64>(tb + CO::P, [&](int row, int j0, int, const float* x) {
+      const int i = row & 63;
+      const float gi = gates.Gc[i];
+      float y[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int jj = j0 + j;
+        const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
+        y[j] = jj <= i ? x[j] * ik * dg : 0.f;
+      }
+      st8_split(PB, PBL, umma::kmaj(row, j0, C), y);
+      st8_split(PB, PBL, umma::kmaj(row, j0 + 8, C), y + 8);
+    });
+    __syncthreads();
+    invert_unit_lower(LS, TS, WS);
+    store_T<false>(TS, TB);
+    publish_smem();
+    if (tid == 0) {
+      umma::gemm(tb + CO::UT, sm + L::VT, sm + L::TB, VB, C, C, false);
+      umma::gemm(tb + CO::WK, sm + L::TB, sm + L::Z, 64, KD, C, false);
+      umma::commit(mbar);
+    }
+    if (!(ok = wait_mma())) break;
+    for_frag<VB, C>(tb + CO::UT, [&](int, int, int q, const float* x) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) Ureg[16 * q + j] = x[j];
+    });
+    for_frag<64, KD>(tb + CO::WK, [&](int i, int m0, int, const float* x) {
+      st8(WK, umma::kmaj(i, m0, KD), x);
+      st8(WK, umma::kmaj(i, m0 + 8, KD), x + 8);
+    });
+    publish_smem();
+    if (tid == 0) {
+      umma::gemm(tb + CO::XT, sm + L::SB, sm + L::WK, VB, C, KD, false);
+      umma::gemm(tb + CO::OS, sm + L::QR, sm + L::SB, R * 64, VB, KD, false);
+      umma::commit(mbar);
+    }
+    if (!(ok = wait_mma())) break;
+    for_frag<VB, C>(tb + CO::XT, [&](int v, int i0, int q, const float* x) {
+      float e[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) e[j] = Ureg[16 * q + j] - x[j];
+      st8_split(EB, EBL, umma::kmaj(v, i0, C), e);
+      st8_split(EB, EBL, umma::kmaj(v, i0 + 8, C), e + 8);
+    });
+    publish_smem();
+    if (tid == 0) {
+      umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EB, R * 64, VB, C, false);
+      umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EBL, R * 64, VB, C, true);
+      umma::gemm(tb + CO::OP, sm + L::PBL, sm + L::EB, R * 64, VB, C, true);
+      umma::gemm(tb + CO::SUT, sm + L::EB, sm + L::KWD, VB, KD, C, false);
+      umma::gemm(tb + CO::SUT, sm + L::EBL, sm + L::KWD, VB, KD, C, true);
+      umma::commit(mbar);
+    }
+    if (!(ok = wait_mma())) break;
+    // ---- state update
+    const float aC = gates.a[Cl - 1];
+    for_frag<VB, KD>(tb + CO::SUT, [&](int v, int m0, int q, const float* x) {
+      float y[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int m = m0 + j;
+        const float s = s_dCm1[m] * (aC * s_d1[m] * Sreg[16 * q + j] + x[j]);
+        Sreg[16 * q + j] = s;
+        y[j] = s * s_d1[m];
+      }
+      st8(SB, umma::kmaj(v, m0, KD), y);
+      st8(SB, umma::kmaj(v, m0 + 8, KD), y + 8);
+    });
+    // ---- outputs O = (a / kappa) .* Os + Op (both accumulators share one row layout)
+    {
+      constexpr int M = R * 64;
+      const int sub = (tid >> 5) & 3;
+      const bool own = owns_rows<M>();
+      const int row = frag_row<M>(), r = row >> 6, i = row & 63;
+#pragma unroll
+      for (int q = 0; q < VB / 32; ++q) {
+        const int v0 = frag_col0<M, VB>(q);
+        float a[16], x[16];
+        umma::ld16(umma::taddr(tb + CO::OS, 32 * sub, v0), a);
+        umma::ld16(umma::taddr(tb + CO::OP, 32 * sub, v0), x);
+        if (own && i < Cl) {
+          const float fa = gates.a[i] * ik;
+          float y[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) y[j] = fa * a[j] + x[j];
+          const int64_t off = out_off(o, b, t0 + i, h, r) + vb0 + v0;
+          if (flags & F_O_VEC) {
+            bf16* dst = reinterpret_cast<bf16*>(o.ptr) + off;
+            st8(dst, 0, y);
+            st8(dst, 8, y + 8);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (vb0 + v0 + j < V) st_io(o.ptr, off + j, y[j], p.io_dtype);
+          }
+        }
+      }
+    }
+    publish_smem();
+  }
+  if (ok && S_final && sown) {
+#pragma unroll
+    for (int q = 0; q < KD / 32; ++q)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) S_final[sbase + (int64_t)(frag_col0<VB, KD>(q) + j) * V] = Sreg[16 * q + j];
+  }
+  if (!ok) {
+    if (tid == 0) atomicOr(&g_fault, 1u);
+    umma::mbar_wait(mbar, phase ^ 1u);  // bounded: let any MMA still in flight drain
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (tid < 32) umma::tmem_dealloc(tb, CO::ALLOC);
+}
+
+template <int FL, int KD, int VB, int R>
+cudaError_t launch_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates,
+                       int NCS, int flags, cudaStream_t st) {
+  auto k = scan_fwd_tc<FL, KD, VB, R>;
+  const int smem = FwdLayout<KD, VB, R>::TOTAL;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.B * p.H, p.V / VB);
+  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags);
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+int tc_fwd_smem(int K, int VB, int R) {
+#define SCA2_TC_SMEM(KD_, VB_, R_) \
+  if (K == KD_ && VB == VB_ && R == R_) return tc::FwdLayout<KD_, VB_, R_>::TOTAL;
+  SCA2_TC_SMEM(64, 64, 1) SCA2_TC_SMEM(64, 64, 2) SCA2_TC_SMEM(64, 128, 1) SCA2_TC_SMEM(64, 128, 2)
+  SCA2_TC_SMEM(128, 64, 1)
+#undef SCA2_TC_SMEM
+  return 1 << 30;
+}
+
+// Value block of the tensor-core forward for this shape, or 0 when the shape is not covered:
+// K in {64, 128} and the value block in {64, 128} (every MMA has M = 64 or 128), V a multiple
+// of the block, shared memory within the device's opt-in limit.
+int tc_fwd_vb(int K, int V, int R, int max_smem) {
+  if (!(K == 64 || K == 128)) return 0;
+  const int cand[2] = {64, 128};
+  for (int i = 0; i < 2; ++i)
+    if (V % cand[i] == 0 && tc_fwd_smem(K, cand[i], R) <= max_smem) return cand[i];
+  return 0;
+}
+
+static int tc_flags(const sca2_scan_args& p, const sca2_out& o) {
+  int f = 0;
+  auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
+  if (p.flavor == SCA2_FLAVOR_PHASE && a16(p.phw.ptr) && a16(p.phq.ptr) && p.phw.sb % 4 == 0 &&
+      p.phw.st % 4 == 0 && p.phw.sh % 4 == 0 && p.phq.sb % 4 == 0 && p.phq.st % 4 == 0 && p.phq.sh % 4 == 0)
+    f |= tc::F_PH_VEC;
+  if (p.flavor == SCA2_FLAVOR_KEY && a16(p.phw.ptr) && a16(p.phq.ptr) && p.phw.sb % 8 == 0 &&
+      p.phw.st % 8 == 0 && p.phw.sh % 8 == 0 && p.phq.sb % 8 == 0 && p.phq.st % 8 == 0 && p.phq.sh % 8 == 0)
+    f |= tc::F_K_VEC;
+  if (a16(o.ptr) && o.sb % 8 == 0 && o.st % 8 == 0 && o.sh % 8 == 0 && o.sr % 8 == 0 && p.V % 8 == 0)
+    f |= tc::F_O_VEC;
+  return f;
+}
+
+cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
+                        float* cstates, int NCS, cudaStream_t st) {
+  const bool ph = p.flavor == SCA2_FLAVOR_PHASE;
+  const int fl = tc_flags(p, o);
+#define SCA2_TC_FWD(KD_, VB_)                                                                         \
+  if (p.K == KD_ && VB == VB_)                                                                        \
+    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, st)   \
+              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, st);
+  SCA2_TC_FWD(64, 64) SCA2_TC_FWD(64, 128)
+#undef SCA2_TC_FWD
+  if (p.K == 128 && VB == 64 && !ph)
+    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, st);
+  return cudaErrorInvalidValue;
+}
+
+// read and clear the device fault word of the tensor-core kernels (synchronous)
+cudaError_t tc_read_faults(unsigned int* out) {
+  unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(out, tc::g_fault, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(tc::g_fault, &zero, sizeof(unsigned int));
+}
+
+}  // namespace sca2

@@ -1,0 +1,343 @@
+// Shared pieces of the tensor-core (tcgen05) scan kernels: operand stores, accumulator
+// fragment iteration, the fp32 blocked inversion and the per-chunk operand prologue.
+#pragma once
+
+#include "common.cuh"
+#include "umma.cuh"
+
+namespace sca2 {
+namespace tc {
+
+constexpr int C = 64;     // chunk (tokens)
+constexpr int NT = 256;   // 8 warps
+constexpr int LDF = C + 1;
+
+using bf16 = __nv_bfloat16;
+
+// launch flags (host-computed, uniform)
+enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4 };
+
+// ---- bf16 vector stores -------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);  // .x (low address) = a
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+// 8 consecutive elements at element offset idx (a multiple of 8, so 16-byte aligned)
+__device__ __forceinline__ void st8(bf16* base, int idx, const float* x) {
+  uint4 u;
+  u.x = pack2(x[0], x[1]);
+  u.y = pack2(x[2], x[3]);
+  u.z = pack2(x[4], x[5]);
+  u.w = pack2(x[6], x[7]);
+  *reinterpret_cast<uint4*>(base + idx) = u;
+}
+// x = hi + lo (hi = bf16(x), lo = bf16(x - hi)): about 16 mantissa bits through bf16 MMAs
+__device__ __forceinline__ void st8_split(bf16* hi, bf16* lo, int idx, const float* x) {
+  float h[8], l[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    h[k] = __bfloat162float(__float2bfloat16_rn(x[k]));
+    l[k] = x[k] - h[k];
+  }
+  st8(hi, idx, h);
+  st8(lo, idx, l);
+}
+__device__ __forceinline__ void st1(bf16* base, int idx, float x) { base[idx] = __float2bfloat16_rn(x); }
+
+// ---- accumulator fragments ----------------------------------------------------------------
+// Accumulator with M rows (64 or 128) and N columns: warp w reads TMEM sub-partition w%4 and the
+// column half w/4 in blocks of 16 columns.  For M = 128 the thread's row is 32*(w%4) + lane; for
+// M = 64 it is 16*(w%4) + lane and only lanes < 16 hold rows.  f(row, col0, q, v[16]) gets the
+// 16 values of columns col0..col0+15; q (compile-time after unrolling) numbers the thread's
+// blocks, so a thread's values can live in registers indexed [16*q + j].
+template <int M>
+__device__ __forceinline__ bool owns_rows() { return M == 128 || (threadIdx.x & 31) < 16; }
+template <int M>
+__device__ __forceinline__ int frag_row() {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  return M == 128 ? 32 * (warp & 3) + lane : 16 * (warp & 3) + lane;
+}
+template <int M, int N>
+__device__ __forceinline__ int frag_col0(int q) {
+  return (threadIdx.x >> 7) * (N / 2) + 16 * q;  // warp >> 2 == threadIdx.x >> 7
+}
+template <int M, int N, class F>
+__device__ __forceinline__ void for_frag(uint32_t tbase, F f) {
+  const int warp = threadIdx.x >> 5;
+  const int sub = warp & 3;
+  const bool own = owns_rows<M>();
+  const int row = frag_row<M>();
+#pragma unroll
+  for (int q = 0; q < N / 32; ++q) {
+    float v[16];
+    umma::ld16(umma::taddr(tbase, 32 * sub, frag_col0<M, N>(q)), v);
+    if (own) f(row, frag_col0<M, N>(q), q, v);
+  }
+}
+
+__device__ __forceinline__ void publish_smem() {
+  umma::fence_async_smem();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+}
+
+// ---- blocked inversion of the unit lower-triangular (I + L), L strictly lower ---------------
+// T_bb = (I + L_bb)^{-1} for the four 16x16 diagonal blocks, then by block distance d:
+// T_ij = -T_ii * sum_{k=j}^{i-1} L_ik T_kj.  All fp32; TS receives the lower triangle.
+__device__ inline void invert_unit_lower(const float* LS, float* TS, float* WS) {
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const int o = 16 * (tid >> 4), col = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float acc = (r == col) ? 1.f : 0.f;
+#pragma unroll
+      for (int k = 0; k < r; ++k) acc = fmaf(-LS[(o + r) * LDF + o + k], x[k], acc);
+      x[r] = (r < col) ? 0.f : acc;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) TS[(o + r) * LDF + o + col] = x[r];
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    const int np = 4 - d;
+    for (int e = tid; e < np * 256; e += blockDim.x) {
+      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      const int bi = pr + d, bj = pr;
+      float acc = 0.f;
+      for (int bk = bj; bk < bi; ++bk)
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          acc = fmaf(LS[(16 * bi + r) * LDF + 16 * bk + k], TS[(16 * bk + k) * LDF + 16 * bj + cc], acc);
+      WS[e] = acc;
+    }
+    __syncthreads();
+    for (int e = tid; e < np * 256; e += blockDim.x) {
+      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      const int bi = pr + d, bj = pr;
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc = fmaf(TS[(16 * bi + r) * LDF + 16 * bi + k], WS[(pr << 8) + (k << 4) + cc], acc);
+      TS[(16 * bi + r) * LDF + 16 * bj + cc] = -acc;
+    }
+    __syncthreads();
+  }
+}
+
+// TB (bf16, K-major rows i, K = j) <- lower triangle of TS; transposed = write T^T instead
+template <bool TRANSPOSED>
+__device__ __forceinline__ void store_T(const float* TS, bf16* TB) {
+  for (int u = threadIdx.x; u < C * C / 8; u += NT) {
+    const int i = u >> 3, j0 = (u & 7) * 8;
+    float x[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = j0 + k;
+      x[k] = TRANSPOSED ? (i <= j ? TS[j * LDF + i] : 0.f) : (j <= i ? TS[i * LDF + j] : 0.f);
+    }
+    st8(TB, umma::kmaj(i, j0, C), x);
+  }
+}
+
+// ---- per-chunk gates ----------------------------------------------------------------------
+// beta, cumulative log-decay Gc, a = exp(Gc), w = exp(Gc_last - Gc) for the chunk's 64 tokens
+// (one warp); rows i >= Cl get beta = 0, g = 0, w = 0.
+struct Gates {
+  float *beta, *Gc, *a, *w;
+};
+__device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates& s, int b, int h, int t0, int Cl) {
+  if (threadIdx.x >= 32) return;
+  const int l = threadIdx.x;
+  const float* bp = reinterpret_cast<const float*>(p.beta.ptr);
+  const float* gp = reinterpret_cast<const float*>(p.g.ptr);
+  float bt[2], gg[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = l + 32 * u;
+    bt[u] = (bp && i < Cl) ? bp[tok_off(p.beta, b, t0 + i, h)] : 0.f;
+    gg[u] = (gp && i < Cl) ? gp[tok_off(p.g, b, t0 + i, h)] : 0.f;
+  }
+  const float s0 = warp_incl_scan(gg[0]);
+  const float tot0 = __shfl_sync(0xffffffffu, s0, 31);
+  const float s1 = warp_incl_scan(gg[1]) + tot0;
+  const float sel = (Cl - 1) < 32 ? s0 : s1;
+  const float Glast = __shfl_sync(0xffffffffu, sel, (Cl - 1) & 31);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = l + 32 * u;
+    const float G = u ? s1 : s0;
+    s.beta[i] = bt[u];
+    s.Gc[i] = G;
+    s.a[i] = expf(G);
+    s.w[i] = i < Cl ? exp_le0(Glast - G) : 0.f;
+  }
+}
+
+// ---- code operands of one chunk ---------------------------------------------------------------
+// Writes, for tokens i < 64 (zeros for i >= Cl):
+//   KR[i][m] = k e^{-lam i}          KW|KWL[i][m] = k e^{+lam i} (hi|lo)
+//   QR|QRL[(r,i)][m] = Q_r e^{-lam i} (hi|lo)
+//   Z[m][i] = beta a k e^{-lam i}/kappa      KWD[m][i] = w k e^{+lam i}
+// Each thread handles (token, 8 consecutive modes) units so that the [i][m] operands are
+// written with 16-byte stores; the [m][i] operands are written element-wise.
+template <int FL, int KD, int R>
+struct CodeOps {
+  bf16 *KR, *KW, *KWL, *QR, *QRL, *Z, *KWD;
+};
+template <int FL, int KD, int R>
+__device__ void build_codes(const sca2_scan_args& p, const CodeOps<FL, KD, R>& op, const Gates& g,
+                            const float* s_lam, const float* s_wr, const float* s_wi, int flags, int b,
+                            int h, int t0, int Cl, float ik) {
+  const int tid = threadIdx.x;
+  if constexpr (FL == SCA2_FLAVOR_PHASE) {
+    constexpr int Mh = KD / 2, MB = Mh / 8, NU = C * MB / NT;
+    const float* phw = reinterpret_cast<const float*>(p.phw.ptr);
+    const float* phq = reinterpret_cast<const float*>(p.phq.ptr);
+    float rw[NU][8], rq[NU][8];
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      if (i < Cl) {
+        const float* pw = phw + tok_off(p.phw, b, t0 + i, h) + m0;
+        const float* pq = phq + tok_off(p.phq, b, t0 + i, h) + m0;
+        if (flags & F_PH_VEC) {
+          const float4 a0 = reinterpret_cast<const float4*>(pw)[0], a1 = reinterpret_cast<const float4*>(pw)[1];
+          const float4 c0 = reinterpret_cast<const float4*>(pq)[0], c1 = reinterpret_cast<const float4*>(pq)[1];
+          rw[u][0] = a0.x; rw[u][1] = a0.y; rw[u][2] = a0.z; rw[u][3] = a0.w;
+          rw[u][4] = a1.x; rw[u][5] = a1.y; rw[u][6] = a1.z; rw[u][7] = a1.w;
+          rq[u][0] = c0.x; rq[u][1] = c0.y; rq[u][2] = c0.z; rq[u][3] = c0.w;
+          rq[u][4] = c1.x; rq[u][5] = c1.y; rq[u][6] = c1.z; rq[u][7] = c1.w;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) { rw[u][k] = pw[k]; rq[u][k] = pq[k]; }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { rw[u][k] = 0.f; rq[u][k] = 0.f; }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      const bool live = i < Cl;
+      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
+      float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int m = m0 + k;
+        float c = 0.f, s = 0.f, cq = 0.f, sq = 0.f;
+        if (live) {
+          sincosf(rw[u][k], &s, &c);
+          sincosf(rq[u][k], &sq, &cq);
+        }
+        const float l = s_lam[m];
+        const float ell = __expf(-l * fi), elli = __expf(l * fi);
+        const float wr = s_wr[m], wi = s_wi[m];
+        const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
+        kc[k] = c * ell; ks[k] = s * ell; wc[k] = c * elli; ws[k] = s * elli;
+        q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
+      }
+      st8(op.KR, umma::kmaj(i, m0, KD), kc);
+      st8(op.KR, umma::kmaj(i, Mh + m0, KD), ks);
+      st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
+      st8_split(op.KW, op.KWL, umma::kmaj(i, Mh + m0, KD), ws);
+      st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), q0a);
+      st8_split(op.QR, op.QRL, umma::kmaj(i, Mh + m0, KD), q0b);
+      st8_split(op.QR, op.QRL, umma::kmaj(C + i, m0, KD), q1a);
+      st8_split(op.QR, op.QRL, umma::kmaj(C + i, Mh + m0, KD), q1b);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        st1(op.Z, umma::kmaj(m0 + k, i, C), kc[k] * zb);
+        st1(op.Z, umma::kmaj(Mh + m0 + k, i, C), ks[k] * zb);
+        st1(op.KWD, umma::kmaj(m0 + k, i, C), wc[k] * wv);
+        st1(op.KWD, umma::kmaj(Mh + m0 + k, i, C), ws[k] * wv);
+      }
+    }
+  } else {
+    constexpr int MB = KD / 8, NU = C * MB / NT;
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      float kk[8], qq[8];
+      if (i < Cl) {
+        const int64_t ok = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
+        if ((flags & F_K_VEC) && p.io_dtype == SCA2_BF16) {
+          const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phw.ptr) + ok);
+          const uint4 c = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phq.ptr) + oq);
+          const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&a);
+          const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            kk[2 * k] = __low2float(ap[k]); kk[2 * k + 1] = __high2float(ap[k]);
+            qq[2 * k] = __low2float(cp[k]); qq[2 * k + 1] = __high2float(cp[k]);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            kk[k] = ld_io(p.phw.ptr, ok + k, p.io_dtype);
+            qq[k] = ld_io(p.phq.ptr, oq + k, p.io_dtype);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { kk[k] = 0.f; qq[k] = 0.f; }
+      }
+      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
+      float kc[8], wc[8], qc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float l = s_lam[m0 + k];
+        const float ell = __expf(-l * fi), elli = __expf(l * fi);
+        kc[k] = kk[k] * ell; wc[k] = kk[k] * elli; qc[k] = p.q_scale * qq[k] * ell;
+      }
+      st8(op.KR, umma::kmaj(i, m0, KD), kc);
+      st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
+      st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), qc);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        st1(op.Z, umma::kmaj(m0 + k, i, C), kc[k] * zb);
+        st1(op.KWD, umma::kmaj(m0 + k, i, C), wc[k] * wv);
+      }
+    }
+  }
+}
+
+// ---- value operand: VT[v][i] = v (beta v for the GDN write) ---------------------------------
+// Units of (8 consecutive tokens, one column): loads are coalesced over the columns and the
+// transposed operand is written with 16-byte stores.  Split in two so the loads can be issued
+// before the gates are known.
+template <int VB>
+struct ValueLoad {
+  static constexpr int NU = (C / 8) * VB / NT;
+  float x[NU][8];
+};
+template <int VB>
+__device__ __forceinline__ void load_values(const sca2_scan_args& p, ValueLoad<VB>& r, int b, int h, int t0,
+                                            int Cl, int vb0) {
+#pragma unroll
+  for (int u = 0; u < ValueLoad<VB>::NU; ++u) {
+    const int unit = threadIdx.x + u * NT, v = unit % VB, i0 = (unit / VB) * 8;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = i0 + k;
+      r.x[u][k] = (i < Cl && vb0 + v < p.V) ? ld_io(p.v.ptr, tok_off(p.v, b, t0 + i, h) + vb0 + v, p.io_dtype) : 0.f;
+    }
+  }
+}
+template <int VB>
+__device__ __forceinline__ void store_values(const sca2_scan_args& p, ValueLoad<VB>& r, const float* s_beta, bf16* VT) {
+#pragma unroll
+  for (int u = 0; u < ValueLoad<VB>::NU; ++u) {
+    const int unit = threadIdx.x + u * NT, v = unit % VB, i0 = (unit / VB) * 8;
+    if (p.v_times_beta) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) r.x[u][k] *= s_beta[i0 + k];
+    }
+    st8(VT, umma::kmaj(v, i0, C), r.x[u]);
+  }
+}
+
+}  // namespace tc
+}  // namespace sca2

@@ -1,0 +1,149 @@
+// tcgen05 (5th-generation tensor core) building blocks for sm_100a, written as inline PTX.
+//
+// Operand layout: every shared-memory MMA operand is bf16, K-major, no swizzle, in 8x8
+// "core matrices" (8 rows x 16 bytes, 128 B each).  For an R x Kt operand, element (r, k)
+// lives at element offset  ((r/8) * (Kt/8) + k/8) * 64 + (r%8) * 8 + k%8,  i.e. the core
+// matrices of one 8-row group are contiguous along K (LBO = 128 B between K-adjacent core
+// matrices) and 8-row groups are SBO = Kt/8 * 128 B apart.  One MMA instruction consumes
+// K = 16 (two core matrices along K); the next K step starts 256 B further.
+//
+// Accumulators live in tensor memory (TMEM): for M = 128 row i is TMEM lane i; for M = 64
+// row m is lane (m % 16) + 32 * (m / 16); column j is TMEM column base + j (fp32).  A warp
+// may only read the 32-lane sub-partition (warp % 4).
+//
+// Every wait on an mbarrier is bounded: after kMaxSpin polls the caller gets `false`,
+// records an error and leaves; nothing here can hang the GPU.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace sca2 {
+namespace umma {
+
+constexpr long long kMaxSpin = 1LL << 22;  // polls of mbarrier.try_wait (each may suspend briefly)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// element offset of (r, k) in a K-major no-swizzle operand with Kt columns
+__device__ __forceinline__ int kmaj(int r, int k, int Kt) {
+  return (((r >> 3) * (Kt >> 3) + (k >> 3)) << 6) + ((r & 7) << 3) + (k & 7);
+}
+
+// shared-memory matrix descriptor (sm100 format, SWIZZLE_NONE)
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm100
+  return d;                // base offset 0, legacy LBO mode, layout type 0 = SWIZZLE_NONE
+}
+
+// descriptor of a K-major operand at smem address `base` with Kt columns, positioned at K step kk
+__device__ __forceinline__ uint64_t kdesc(uint32_t base, int Kt, int kk) {
+  return sdesc(base + (uint32_t)kk * 256u, 128u, (uint32_t)(Kt >> 3) * 128u);
+}
+
+// instruction descriptor: kind::f16 with bf16 A/B, fp32 D, both operands K-major
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A * B^T for one K = 16 step; issued by ONE thread
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+      :
+      : "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D = A(M x Kt) * B(N x Kt)^T over all K steps; A, B K-major in smem; issued by ONE thread
+__device__ __forceinline__ void gemm(uint32_t tmem_d, const void* A, const void* B, int M, int N, int Kt,
+                                     bool accumulate) {
+  const uint32_t a = smem_u32(A), b = smem_u32(B), id = idesc_bf16(M, N);
+  for (int kk = 0; kk < Kt / 16; ++kk)
+    mma(tmem_d, kdesc(a, Kt, kk), kdesc(b, Kt, kk), id, (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// arrive on `mbar` once every MMA issued so far by this thread has completed
+__device__ __forceinline__ void commit(uint64_t* mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_u32(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// bounded wait for the phase `parity` of `mbar` to complete; false on timeout
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
+  const uint32_t a = smem_u32(mbar);
+  for (long long it = 0; it < kMaxSpin; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// generic-proxy smem writes -> visible to the tensor core (async proxy)
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// TMEM allocation (one full warp); writes the base address to *dst
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(dst)), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// 32 lanes x 16 consecutive fp32 columns -> 16 registers per thread (thread t = lane base + t)
+__device__ __forceinline__ void ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM address of (lane, column)
+__device__ __forceinline__ uint32_t taddr(uint32_t base, int lane, int col) {
+  return base + ((uint32_t)lane << 16) + (uint32_t)col;
+}
+
+// lane holding row m of an M-row accumulator
+__device__ __forceinline__ int row_lane(int m, int M) { return M == 128 ? m : (m & 15) + ((m >> 4) << 5); }
+
+}  // namespace umma
+}  // namespace sca2
