@@ -29,6 +29,10 @@ int tc_fwd_vb(int K, int V, int R, int max_smem);
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
                         float* cstates, int NCS, cudaStream_t st);
 cudaError_t tc_read_faults(unsigned int* out);
+// scan_tc_bwd.cu
+bool tc_train_ok(const sca2_scan_args& p, int max_smem);
+cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
+                        const sca2_scan_grads& gr, int NCS, cudaStream_t st);
 }  // namespace sca2
 
 namespace {
@@ -128,9 +132,15 @@ int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* ch
     }
     return SCA2_OK;
   }
-  // bf16 inference (no saved chunk states) runs on the tensor cores when the shape is covered
+  // bf16 runs on the tensor cores when the shape is covered; with saved chunk states (training)
+  // only where the tensor-core backward covers the shape too, so the pair stays consistent
   const int R = a->flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
-  const int vb = (a->io_dtype == SCA2_BF16 && !chunk_states) ? sca2::tc_fwd_vb(a->K, a->V, R, max_optin_smem()) : 0;
+  const int smem = max_optin_smem();
+  int vb = 0;
+  if (a->io_dtype == SCA2_BF16) {
+    if (!chunk_states) vb = sca2::tc_fwd_vb(a->K, a->V, R, smem);
+    else if (sca2::tc_train_ok(*a, smem)) vb = sca2::tc_fwd_vb(a->K, a->V, R, smem);
+  }
   cudaError_t e = vb ? sca2::tc_scan_fwd(*a, vb, o, S_final, chunk_states, sca2::f32_num_chunks(a->T), st)
                      : sca2::f32_scan_fwd(*a, o, S_final, chunk_states, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd");
@@ -158,7 +168,9 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
     return fail(SCA2_ERR_ARG, "dphw/dk, dphq/dq and dv must be non-null");
   if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
   if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
-  cudaError_t e = sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
+  cudaError_t e = sca2::tc_train_ok(*a, max_optin_smem())
+                      ? sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, *gr, sca2::f32_num_chunks(a->T), st)
+                      : sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
   return SCA2_OK;
 }
