@@ -308,14 +308,18 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
+    if args.batch is not None:
+        WORK["B"] = args.batch
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     W = WORK
     config = {"workload": "LapA long-head phase-coded delta scan fwd+bwd (phases, per-mode decay, "
-                          "delta gate), B=8 T=4096 H=16 d_head=64 (Mh=32, K=V=64) per GPU",
+                          f"delta gate), B={WORK['B']} T=4096 H=16 d_head=64 (Mh=32, K=V=64) per GPU",
               "batch_per_gpu": W["B"], "seq_len": W["T"], "heads": W["H"], "d_head": 2 * W["Mh"],
               "parallelism": f"(batch x head) shards, {world} rank(s)",
               "l2": "inputs larger than L2 (~0.7 GB touched per step), no flush"}

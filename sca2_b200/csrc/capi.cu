@@ -29,6 +29,7 @@ int tc_fwd_vb(int K, int V, int R, int max_smem);
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
                         float* cstates, int NCS, cudaStream_t st);
 cudaError_t tc_read_faults(unsigned int* out);
+cudaError_t tc_read_faults_bwd(unsigned int* out);
 // scan_tc_bwd.cu
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
@@ -109,13 +110,15 @@ const char* sca2_version(void) { return "sca2b200 0.1.0 (sm_100a)"; }
 int sca2_fault_status(uint32_t* faults) {
   if (!faults) return fail(SCA2_ERR_ARG, "null output");
   unsigned int f = 0;
+  unsigned int fb = 0;
   cudaError_t e = sca2::tc_read_faults(&f);
+  if (e == cudaSuccess) e = sca2::tc_read_faults_bwd(&fb);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_fault_status");
-  *faults = f;
+  *faults = f | fb;
   return SCA2_OK;
 }
 
-int32_t sca2_num_chunks(int32_t T) { return sca2::f32_num_chunks(T); }
+int32_t sca2_num_chunks(int32_t T) { return T > 0 ? sca2::state_slots(T) : 0; }
 
 int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* chunk_states,
                   void* stream) {
@@ -141,7 +144,7 @@ int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* ch
     if (!chunk_states) vb = sca2::tc_fwd_vb(a->K, a->V, R, smem);
     else if (sca2::tc_train_ok(*a, smem)) vb = sca2::tc_fwd_vb(a->K, a->V, R, smem);
   }
-  cudaError_t e = vb ? sca2::tc_scan_fwd(*a, vb, o, S_final, chunk_states, sca2::f32_num_chunks(a->T), st)
+  cudaError_t e = vb ? sca2::tc_scan_fwd(*a, vb, o, S_final, chunk_states, sca2::state_slots(a->T), st)
                      : sca2::f32_scan_fwd(*a, o, S_final, chunk_states, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd");
   return SCA2_OK;
@@ -169,7 +172,7 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
   if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
   if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
   cudaError_t e = sca2::tc_train_ok(*a, max_optin_smem())
-                      ? sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, *gr, sca2::f32_num_chunks(a->T), st)
+                      ? sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, *gr, sca2::state_slots(a->T), st)
                       : sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
   return SCA2_OK;

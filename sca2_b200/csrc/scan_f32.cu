@@ -230,7 +230,7 @@ __device__ __forceinline__ void solve_upper_T(const float* Gr, const float* beta
 // ======================================================================================
 template <int FL>
 __global__ void __launch_bounds__(NT) scan_fwd_kernel(sca2_scan_args p, sca2_out o,
-                                                      float* S_final, float* cstates, int NC,
+                                                      float* S_final, float* cstates, int NC, int NCS,
                                                       Layout Lo) {
   extern __shared__ float sm[];
   const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(NT) scan_fwd_kernel(sca2_scan_args p, sca2_out
   for (int c = 0; c < NC; ++c) {
     const int t0 = c * CK, Cl = min(CK, p.T - t0);
     if (cstates) {
-      const int64_t cb = (((int64_t)b * p.H + h) * NC + c) * K * (int64_t)V;
+      const int64_t cb = (((int64_t)b * p.H + h) * NCS + c) * K * (int64_t)V;
       for (int idx = threadIdx.x; idx < K * VB; idx += blockDim.x) {
         const int m = idx / VB, j = idx - (idx / VB) * VB;
         if (vb0 + j < V) cstates[cb + (int64_t)m * V + vb0 + j] = S[m * VBP + j];
@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(NT) scan_fwd_kernel(sca2_scan_args p, sca2_out
 template <int FL>
 __global__ void __launch_bounds__(NT) scan_bwd_kernel(sca2_scan_args p, sca2_out dO,
                                                       const float* dS_final, const float* cstates,
-                                                      sca2_scan_grads gr, int NC, Layout Lo) {
+                                                      sca2_scan_grads gr, int NC, int NCS, Layout Lo) {
   extern __shared__ float sm[];
   const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int vb0 = blockIdx.y * VB;
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(NT) scan_bwd_kernel(sca2_scan_args p, sca2_out
     const int t0 = c * CK, Cl = min(CK, p.T - t0);
     load_chunk<FL>(p, Lo, sm, b, h, t0, Cl, vb0);  // values land in E (as Y)
     {
-      const int64_t cb = (((int64_t)b * p.H + h) * NC + c) * K * (int64_t)V;
+      const int64_t cb = (((int64_t)b * p.H + h) * NCS + c) * K * (int64_t)V;
       for (int idx = threadIdx.x; idx < KP * VB; idx += blockDim.x) {
         const int m = idx / VB, j = idx - (idx / VB) * VB;
         float x = 0.f;
@@ -703,11 +703,11 @@ cudaError_t f32_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_fi
   if (p.flavor == SCA2_FLAVOR_PHASE) {
     auto k = f32::scan_fwd_kernel<SCA2_FLAVOR_PHASE>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, f32::NT, smem, st>>>(p, o, S_final, cstates, NC, Lo);
+    k<<<grid, f32::NT, smem, st>>>(p, o, S_final, cstates, NC, state_slots(p.T), Lo);
   } else {
     auto k = f32::scan_fwd_kernel<SCA2_FLAVOR_KEY>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, f32::NT, smem, st>>>(p, o, S_final, cstates, NC, Lo);
+    k<<<grid, f32::NT, smem, st>>>(p, o, S_final, cstates, NC, state_slots(p.T), Lo);
   }
   return cudaGetLastError();
 }
@@ -722,11 +722,11 @@ cudaError_t f32_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const floa
   if (p.flavor == SCA2_FLAVOR_PHASE) {
     auto k = f32::scan_bwd_kernel<SCA2_FLAVOR_PHASE>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, f32::NT, smem, st>>>(p, dO, dS_final, cstates, gr, NC, Lo);
+    k<<<grid, f32::NT, smem, st>>>(p, dO, dS_final, cstates, gr, NC, state_slots(p.T), Lo);
   } else {
     auto k = f32::scan_bwd_kernel<SCA2_FLAVOR_KEY>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, f32::NT, smem, st>>>(p, dO, dS_final, cstates, gr, NC, Lo);
+    k<<<grid, f32::NT, smem, st>>>(p, dO, dS_final, cstates, gr, NC, state_slots(p.T), Lo);
   }
   return cudaGetLastError();
 }

@@ -26,8 +26,10 @@
 // on an mbarrier whose wait is bounded: on a timeout the CTA records a fault bit, waits
 // (bounded) once more for its MMAs, frees its TMEM and returns.
 //
-// The states entering chunks are saved in the (B,H,ceil(T/32),K,V) buffer of the fp32 path,
-// at slot 2c for the 64-token chunk c, so both paths share one buffer shape.
+// Training runs save, per 64-token chunk c of the (B,H,slots,K,V) buffer: the state entering
+// the chunk in slot 2c (fp32) and, in slot 2c+1, T (bf16 C x C, operand layout) followed by
+// E^T (bf16, 64 x C per block of 64 value columns, operand layout; the hi part of the split).
+// The backward reads them back instead of recomputing the inversion and the corrected values.
 #include "tc_common.cuh"
 
 namespace sca2 {
@@ -77,6 +79,13 @@ struct Cols {
   static constexpr int NEED = OS + VB;
   static constexpr int ALLOC = NEED <= 256 ? 256 : 512;
 };
+
+// 16-byte copy of an operand from shared to global memory (both 16-byte aligned)
+__device__ __forceinline__ void copy_out(uint8_t* dst, const bf16* src, int nbytes) {
+  const uint8_t* s = reinterpret_cast<const uint8_t*>(src);
+  for (int u = threadIdx.x * 16; u < nbytes; u += NT * 16)
+    *reinterpret_cast<uint4*>(dst + u) = *reinterpret_cast<const uint4*>(s + u);
+}
 
 template <int FL, int KD, int VB, int R>
 __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
@@ -174,6 +183,10 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   bool ok = true;
   for (int c = 0; c < NC && ok; ++c) {
     const int t0 = c * C, Cl = min(C, p.T - t0);
+    // saved for the backward in slot 2c+1: T (bf16 [i][j]) then E^T (bf16 [v][j]) per value block
+    uint8_t* saved = cstates ? reinterpret_cast<uint8_t*>(
+                                   cstates + (((int64_t)b * p.H + h) * NCS + 2 * c + 1) * KD * (int64_t)V)
+                             : nullptr;
     if (cstates && sown) {
       // state entering chunk c -> slot 2c of the (B,H,NCS,K,V) buffer
       const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0 + srow;
@@ -226,6 +239,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     invert_unit_lower(LS, TS, WS);
     store_T<false>(TS, TB);
     publish_smem();
+    if (cstates && blockIdx.y == 0) copy_out(saved, TB, C * C * 2);
     if (tid == 0) {
       umma::gemm(tb + CO::UT, sm + L::VT, sm + L::TB, VB, C, C, false);
       umma::gemm(tb + CO::WK, sm + L::TB, sm + L::Z, 64, KD, C, false);
@@ -255,6 +269,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       st8_split(EB, EBL, umma::kmaj(v, i0 + 8, C), e + 8);
     });
     publish_smem();
+    if (cstates) copy_out(saved + C * C * 2 + blockIdx.y * (VB * C * 2), EB, VB * C * 2);
     if (tid == 0) {
       umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EB, R * 64, VB, C, false);
       umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EBL, R * 64, VB, C, true);

@@ -1,335 +1,325 @@
 // Tensor-core (tcgen05 / TMEM) backward scan for bf16 inputs on sm_100a.
 //
-// One CTA per (batch*head, block of VB value columns); chunks of 64 tokens are walked in
-// reverse.  Per chunk, with S the state entering the chunk (saved by the forward at slot 2c)
-// and dS the adjoint of the state leaving it (carried in fp32 registers):
+// One CTA per (batch*head, block of 64 value columns); chunks of 64 tokens are walked in
+// reverse.  The forward saved, per chunk c: the state entering the chunk (slot 2c of the
+// chunk-state buffer, fp32) and, in slot 2c+1, the inverse T = (I + beta Gr)^{-1} and the
+// corrected values E = T (V' - beta a kr Sp / kappa) in bf16, already in the operand layout.
+// With Sp = d1 .* S (state entering the chunk, decayed once) and dS the adjoint of the state
+// leaving the chunk (fp32 registers), one chunk is:
 //
-//   forward recompute   G = KR KW^T, T = (I + beta Gr)^{-1}, U^T = V'^T T^T, Wk = T Z^T,
-//                       X^T = Sp^T Wk^T, E = U - X, R0^T = Sp^T KR^T (a/kappa),
-//                       Os = QR Sp                                  (Sp = d1 .* S)
-//   adjoint chain       dE^T = dSc^T (KW diag w)^T + dO^T P          (dSc = dCm1 .* dS)
-//                       dY^T = dE^T T
-//                       dS0p^T = dO^T (QR a/kappa) - dY^T Z^T
-//                       dS <- a_last dCm1 d1 .* dS + d1 .* dS0p
-//   gradients           dL = -dY E^T, dP = dO E^T, dKK = beta dL .* Dg, dQK = dP .* Dg
-//                       dkr = dKK KW / kappa - (beta a / kappa) dY Sp^T
-//                       dqr = dQK KW / kappa + (a / kappa) dO Sp^T
-//                       dkw = (dKK^T KR + dQK^T QR) / kappa + w E dSc^T
-//                       Lw = (((j - i) dKK)^T KR + ((j - i) dQK)^T QR) / kappa: the
-//                       intra-chunk part of d(lam) is sum_j kw_j .* Lw_j, taken in this
-//                       relative-position form because i (kr, qr) and j (kw) weighted
-//                       sums cancel to a few percent of their size
-//                       then d(phi, psi | k, q), d(beta), d(g), d(lam), d(wr, wi), dv = dY
+//   batch 1   G = KR KW^T, P = QR KW^T, DS0 = dO^T QRA, DQR2 = dO Sp^T,
+//             DKW3 = E dSc^T, dE = KWW dSc                        (dSc = dCm1 .* dS)
+//   batch 2   dE += P^T dO          (P masked and decayed, written by the first epilogue)
+//   batch 3   dY = T^T dE           (dv = dY, beta dY for the GDN write)
+//   batch 4   DL = dY E^T, DP = dO E^T, DS0 += dY^T ZN, DKR2 = dY Sp^T
+//             -> dKK = beta (-DL) .* Dg (strict), dQK = DP .* Dg (incl),
+//                dS <- a_last dCm1 d1 .* dS + d1 .* DS0
+//   batch 5   DKR1 = dKK KW, DQR1 = dQK KW, DKW12 = dKK^T KR + dQK^T QR,
+//             DLW = ((j - i) dKK)^T KR + ((j - i) dQK)^T QR
+//   finish    dkr = DKR1 / kappa - beta a / kappa DKR2,  dqr = DQR1 / kappa + a / kappa DQR2,
+//             dkw = DKW12 / kappa + w DKW3, then the chain rule to (phi, psi | k, q), and the
+//             row reductions that give d(beta), d(a), d(w) from the same products
+//             (sum_v dY R0 = a / kappa sum_m kr DKR2, sum_v E (kw dSc) = sum_m kw DKW3, ...)
 //
-// Same algebra as the oracle's backward_chunked.  All products are bf16 MMAs with fp32
-// accumulation in TMEM; the inversion, masks, decays and reductions run on CUDA cores in
-// fp32.  Shared memory is carved into a persistent area and two pools that alias each other
-// (pool A lives until the third MMA batch completes, pool B is written after it).  Every
-// mbarrier wait is bounded: on a timeout the CTA records a fault bit, frees its TMEM and
-// returns.  Key-side gradients are accumulated into zero-filled fp32 buffers with atomics.
+// where ZN = -beta a kr / kappa, QRA = a qr / kappa, KWW = w kw.  The intra-chunk part of
+// d(lam) is sum_j kw_j .* DLW_j / kappa: the relative-position form, because the separately
+// i-weighted (kr, qr) and j-weighted (kw) sums cancel to a few percent of their size.
+//
+// Every product is a bf16 MMA with fp32 accumulation in TMEM.  Operands used both ways are
+// stored once, K-major, and read through MN-major descriptors for the transposed use.  The
+// next chunk's state, T, E and dO are copied in with cp.async while the current chunk runs;
+// its phases (keys) and gates are loaded into registers.  Every mbarrier wait is bounded: on a
+// timeout the CTA records a fault bit, frees its TMEM and returns.
 #include "tc_common.cuh"
 
 namespace sca2 {
 namespace tc {
 
-extern __device__ unsigned int g_fault;
+// bit 0: a bounded mbarrier wait of the backward timed out (one fault word per translation
+// unit: the library is built without relocatable device code)
+__device__ unsigned int g_fault_bwd;
 
-template <int KD, int VB, int R>
+constexpr int BVB = 64;  // value columns per CTA
+
+// byte offsets of the shared-memory carve-up; regions R1..R5 are reused by operands with
+// disjoint lifetimes (noted per region)
+template <int FL, int R>
 struct BwdLayout {
-  static constexpr int al(int x) { return (x + 1023) & ~1023; }
-  static constexpr int mx(int a, int b) { return a > b ? a : b; }
-  static constexpr int RC = R * C;
-  // persistent
-  static constexpr int PT = 0;                                  // C x RC   [j][(r,i)]  P^T
-  static constexpr int TBT = PT + al(C * RC * 2);               // C x C    [i][j] = T[j][i]
-  static constexpr int DOA = TBT + al(C * C * 2);               // RC x VB  [(r,i)][v]  dO
-  static constexpr int Z = DOA + al(RC * VB * 2);               // KD x C   [m][i]
-  static constexpr int POOL = Z + al(KD * C * 2);
-  // pool A: prologue .. third MMA batch
-  static constexpr int KR = POOL;                               // C x KD
-  static constexpr int KW = KR + al(C * KD * 2);                // C x KD
-  static constexpr int QR = KW + al(C * KD * 2);                // RC x KD
-  static constexpr int VT = QR + al(RC * KD * 2);               // VB x C
-  static constexpr int SB = VT + al(VB * C * 2);                // VB x KD  Sp^T
-  static constexpr int DSB = SB + al(VB * KD * 2);              // VB x KD  dSc^T
-  static constexpr int DOT = DSB + al(VB * KD * 2);             // VB x RC  dO^T
-  static constexpr int KWW = DOT + al(VB * RC * 2);             // C x KD   kw w
-  static constexpr int QRAT = KWW + al(C * KD * 2);             // KD x RC  qr a / kappa
-  static constexpr int TB = QRAT + al(KD * RC * 2);             // C x C
-  static constexpr int WK = TB + al(C * C * 2);                 // C x KD
-  static constexpr int LS = WK + al(C * KD * 2);                // fp32 C x LDF
-  static constexpr int TS = LS + al(C * LDF * 4);
-  static constexpr int WS = TS + al(C * LDF * 4);
-  static constexpr int A_END = WS + al(3 * 256 * 4);
-  // pool B: after the third batch
-  static constexpr int EA = POOL;                               // C x VB   [i][v]  E
-  static constexpr int DEB = EA + al(C * VB * 2);               // VB x C   dE^T
-  static constexpr int DYA = DEB + al(VB * C * 2);              // C x VB   dY
-  static constexpr int DYB = DYA + al(C * VB * 2);              // VB x C   -dY^T
-  static constexpr int KWT = DYB + al(VB * C * 2);              // KD x C   kw^T
-  static constexpr int KRT = KWT + al(KD * C * 2);              // KD x C   kr^T
-  static constexpr int QRT = KRT + al(KD * C * 2);              // KD x RC  qr^T
-  static constexpr int SBT = QRT + al(KD * RC * 2);             // KD x VB  Sp
-  static constexpr int DSBT = SBT + al(KD * VB * 2);            // KD x VB  dSc
-  static constexpr int DKKA = DSBT + al(KD * VB * 2);           // C x C    dKK
-  static constexpr int DKKT = DKKA + al(C * C * 2);             // C x C    dKK^T
-  static constexpr int DQKA = DKKT + al(C * C * 2);             // RC x C   dQK
-  static constexpr int DQKT = DQKA + al(RC * C * 2);            // C x RC   dQK^T
-  static constexpr int DKKWT = DQKT + al(C * RC * 2);           // C x C    ((j - i) dKK)^T
-  static constexpr int DQKWT = DKKWT + al(C * C * 2);           // C x RC   ((j - i) dQK)^T
-  static constexpr int B_END = DQKWT + al(C * RC * 2);
-  // fp32 staging of the key-side gradients (after the sixth batch, aliases pool B)
-  static constexpr int GKR = POOL;                              // C x KD
-  static constexpr int GKW = GKR + C * KD * 4;                  // C x KD
-  static constexpr int GKW3 = GKW + C * KD * 4;                 // C x KD  (w E dSc^T part)
-  static constexpr int GQR = GKW3 + C * KD * 4;                 // RC x KD
-  static constexpr int GKRS = GQR + RC * KD * 4;                // C x KD  (state part of dkr)
-  static constexpr int GQRS = GKRS + C * KD * 4;                // RC x KD (state part of dqr)
-  static constexpr int GLW = GQRS + RC * KD * 4;                // C x KD  (position-weighted dkw)
-  static constexpr int G_END = GLW + C * KD * 4;
-  static constexpr int SC = al(mx(mx(A_END, B_END), G_END));
-  // scalars (floats): beta, Gc, a, w, dbeta, da, dw, rows, cols [C each]; d1, dCm1, lam, wr,
-  // wi, dlam, dwr, dwi [KD each]; misc[8]
+  static constexpr int KD = 64, VB = BVB, RC = R * C, Mh = KD / 2;
+  static constexpr int KR = 0;                     // C x KD   kr             [i][m]
+  static constexpr int KW = KR + C * KD * 2;       // C x KD   kw             [i][m]
+  static constexpr int QR = KW + C * KD * 2;       // RC x KD  qr             [(r,i)][m]
+  static constexpr int TB = QR + RC * KD * 2;      // C x C    T (saved)      [i][j]
+  static constexpr int EB = TB + C * C * 2;        // VB x C   E^T (saved)    [v][j]
+  static constexpr int DOA = EB + VB * C * 2;      // RC x VB  dO             [(r,i)][v]
+  static constexpr int CST = DOA + RC * VB * 2;    // fp32 KD x VB staged state [m][v]
+  static constexpr int LAMS = CST + KD * VB * 4;   // fp32 KD x VB  state-side d(lam) terms [m][v]
+  static constexpr int CACHE = LAMS + KD * VB * 4; // fp32 phase: cos/sin phi, cos/sin psi [4][C][Mh]
+                                                   //      key:   k, q * scale [2][C][KD]
+  static constexpr int CACHE_BYTES = FL == SCA2_FLAVOR_PHASE ? 4 * C * Mh * 4 : 2 * C * KD * 4;
+  static constexpr int R1 = CACHE + CACHE_BYTES;   // QRA (b1) | P (epi1-b2) | dQK (epi4-b5)
+  static constexpr int R2 = R1 + RC * 64 * 2;      // KWW (b1) | dE (epi2-b3) | dKK (epi4-b5) | PQ (finish)
+  static constexpr int R3 = R2 + C * 64 * 2;       // ZN (codes-b4) | (j-i) dKK (epi4-b5)
+  static constexpr int R4 = R3 + C * 64 * 2;       // Sp^T, dSc^T [v][m] (prologue-b4) | (j-i) dQK (epi4-b5)
+  static constexpr int R5 = R4 + 2 * VB * KD * 2;  // dY [i][v] (epi3-b4)
+  static constexpr int SC = R5 + C * VB * 2;
+  // scalars (floats): beta, Gc, a, w, dbeta, da, dw, rows, cols [C]; d1, dCm1, lam, wr, wi,
+  // dlam, dwr, dwi [KD]; misc[8]
   static constexpr int SC_FLOATS = 9 * C + 8 * KD + 8;
-  static constexpr int MBAR = SC + al(SC_FLOATS * 4);
+  static constexpr int MBAR = SC + ((SC_FLOATS * 4 + 1023) & ~1023);
   static constexpr int TOTAL = MBAR + 64;
+  static_assert(RC * 64 * 2 >= RC * KD * 2, "R1 holds QRA");
+  static_assert(2 * VB * KD * 2 >= RC * C * 2, "R4 holds the weighted dQK");
+  static_assert(C * 64 * 2 >= C * Mh * 4, "R2 holds PQ");
 };
 
-// TMEM columns (see the lifetime plan in the kernel body)
+// TMEM columns (fp32).  Lifetimes: batch 1 writes G, P, DS0, DQR2, DKW3, DE; DY reuses P's
+// columns after the first epilogue; DL and DP follow DE; the batch-5 results reuse G, DY, DL, DP.
 struct BCols {
-  static constexpr int G = 0, PT = 64, UT = 192, WK = 256;                       // batches 1-2
-  static constexpr int XT = 64, R0T = 128, DE1 = 192, DE2 = 256, DS0 = 320, OS = 384;  // batch 3
-  static constexpr int DYT = 64;                                                  // batch 4
-  static constexpr int DL = 128, DP = 192;                                        // batch 5
-  static constexpr int DKR1 = 0, DKR2 = 64, DQR1 = 128, DQR2 = 192, DKW12 = 256, DKW3 = 384,
-                       DLW = 448;                                                 // batch 6
+  static constexpr int G = 0, P = 64, DS0 = 128, DQR2 = 192, DKW3 = 256, DE = 320;
+  static constexpr int DY = 64, DL = 320, DP = 384, DKR2 = 448;
+  static constexpr int DKR1 = 0, DQR1 = 64, DKW12 = 320, DLW = 384;
   static constexpr int ALLOC = 512;
 };
 
+// launch flags of the backward (host-computed)
+enum : int { B_PH_VEC = 1, B_DO_VEC = 2, B_DV_VEC = 4, B_G_VEC = 8, B_K_VEC = 16 };
 
-// ---- code operands of the backward ---------------------------------------------------------
-//   KR[i][m] = kr, KW[i][m] = kw, QR[(r,i)][m] = qr, KWW[i][m] = w kw   (16-byte stores)
-//   Z[m][i] = beta a kr / kappa, QRAT[m][(r,i)] = a qr / kappa           (element stores)
-template <int FL, int KD, int R>
-__device__ void build_codes_bwd(const sca2_scan_args& p, bf16* KR, bf16* KW, bf16* QR, bf16* Z, bf16* KWW,
-                                bf16* QRAT, const Gates& g, const float* s_lam, const float* s_wr,
-                                const float* s_wi, int flags, int b, int h, int t0, int Cl, float ik) {
-  constexpr int RC = R * C;
+// ---- per-thread register prefetch of the next chunk's codes inputs and gates ----------------
+template <int FL>
+struct CodeRegs {
+  float w[2][8], q[2][8];  // phase: one unit (phi, psi x 8 modes); key: two units (k, q x 8)
+};
+
+template <int FL, int KD>
+__device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs<FL>& r, int flags, int b, int h,
+                                               int t0, int Cl) {
   const int tid = threadIdx.x;
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
-    constexpr int Mh = KD / 2, MB = Mh / 8, NU = C * MB / NT;
-    const float* phw = reinterpret_cast<const float*>(p.phw.ptr);
-    const float* phq = reinterpret_cast<const float*>(p.phq.ptr);
+    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    const float* pw = reinterpret_cast<const float*>(p.phw.ptr);
+    const float* pq = reinterpret_cast<const float*>(p.phq.ptr);
+    if (i < Cl) {
+      const int64_t ow = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
+      if (flags & B_PH_VEC) {
+        const float4 a0 = reinterpret_cast<const float4*>(pw + ow)[0], a1 = reinterpret_cast<const float4*>(pw + ow)[1];
+        const float4 c0 = reinterpret_cast<const float4*>(pq + oq)[0], c1 = reinterpret_cast<const float4*>(pq + oq)[1];
+        r.w[0][0] = a0.x; r.w[0][1] = a0.y; r.w[0][2] = a0.z; r.w[0][3] = a0.w;
+        r.w[0][4] = a1.x; r.w[0][5] = a1.y; r.w[0][6] = a1.z; r.w[0][7] = a1.w;
+        r.q[0][0] = c0.x; r.q[0][1] = c0.y; r.q[0][2] = c0.z; r.q[0][3] = c0.w;
+        r.q[0][4] = c1.x; r.q[0][5] = c1.y; r.q[0][6] = c1.z; r.q[0][7] = c1.w;
+      } else {
 #pragma unroll
-    for (int u = 0; u < NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
-      const bool live = i < Cl;
-      float rw[8], rq[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        rw[k] = live ? phw[tok_off(p.phw, b, t0 + i, h) + m0 + k] : 0.f;
-        rq[k] = live ? phq[tok_off(p.phq, b, t0 + i, h) + m0 + k] : 0.f;
+        for (int k = 0; k < 8; ++k) { r.w[0][k] = pw[ow + k]; r.q[0][k] = pq[oq + k]; }
       }
-      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
-      float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8], wwc[8], wws[8];
+    } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int m = m0 + k;
-        float c = 0.f, s = 0.f, cq = 0.f, sq = 0.f;
-        if (live) {
-          sincosf(rw[k], &s, &c);
-          sincosf(rq[k], &sq, &cq);
-        }
-        const float l = s_lam[m];
-        const float ell = __expf(-l * fi), elli = __expf(l * fi);
-        const float c1 = s_wr[m] * cq + s_wi[m] * sq, c2 = s_wr[m] * sq - s_wi[m] * cq;
-        kc[k] = c * ell; ks[k] = s * ell; wc[k] = c * elli; ws[k] = s * elli;
-        wwc[k] = wc[k] * wv; wws[k] = ws[k] * wv;
-        q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
-      }
-      st8(KR, umma::kmaj(i, m0, KD), kc);
-      st8(KR, umma::kmaj(i, Mh + m0, KD), ks);
-      st8(KW, umma::kmaj(i, m0, KD), wc);
-      st8(KW, umma::kmaj(i, Mh + m0, KD), ws);
-      st8(KWW, umma::kmaj(i, m0, KD), wwc);
-      st8(KWW, umma::kmaj(i, Mh + m0, KD), wws);
-      st8(QR, umma::kmaj(i, m0, KD), q0a);
-      st8(QR, umma::kmaj(i, Mh + m0, KD), q0b);
-      st8(QR, umma::kmaj(C + i, m0, KD), q1a);
-      st8(QR, umma::kmaj(C + i, Mh + m0, KD), q1b);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        st1(Z, umma::kmaj(m0 + k, i, C), kc[k] * zb);
-        st1(Z, umma::kmaj(Mh + m0 + k, i, C), ks[k] * zb);
-        st1(QRAT, umma::kmaj(m0 + k, i, RC), q0a[k] * fa);
-        st1(QRAT, umma::kmaj(Mh + m0 + k, i, RC), q0b[k] * fa);
-        st1(QRAT, umma::kmaj(m0 + k, C + i, RC), q1a[k] * fa);
-        st1(QRAT, umma::kmaj(Mh + m0 + k, C + i, RC), q1b[k] * fa);
-      }
+      for (int k = 0; k < 8; ++k) { r.w[0][k] = 0.f; r.q[0][k] = 0.f; }
     }
   } else {
-    constexpr int MB = KD / 8, NU = C * MB / NT;
 #pragma unroll
-    for (int u = 0; u < NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
-      const bool live = i < Cl;
-      const int64_t ok_ = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
-      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
-      float kc[8], wc[8], qc[8], ww[8];
+    for (int u = 0; u < 2; ++u) {
+      const int unit = tid + u * NT, i = unit >> 3, m0 = (unit & 7) * 8;
+      if (i < Cl) {
+        const int64_t ok = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
+        if (flags & B_K_VEC) {
+          const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phw.ptr) + ok);
+          const uint4 c = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phq.ptr) + oq);
+          const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&a);
+          const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&c);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float kk = live ? ld_io(p.phw.ptr, ok_ + k, p.io_dtype) : 0.f;
-        const float qq = live ? p.q_scale * ld_io(p.phq.ptr, oq + k, p.io_dtype) : 0.f;
-        const float l = s_lam[m0 + k];
-        const float ell = __expf(-l * fi), elli = __expf(l * fi);
-        kc[k] = kk * ell; wc[k] = kk * elli; qc[k] = qq * ell; ww[k] = wc[k] * wv;
-      }
-      st8(KR, umma::kmaj(i, m0, KD), kc);
-      st8(KW, umma::kmaj(i, m0, KD), wc);
-      st8(KWW, umma::kmaj(i, m0, KD), ww);
-      st8(QR, umma::kmaj(i, m0, KD), qc);
+          for (int k = 0; k < 4; ++k) {
+            r.w[u][2 * k] = __low2float(ap[k]); r.w[u][2 * k + 1] = __high2float(ap[k]);
+            r.q[u][2 * k] = __low2float(cp[k]); r.q[u][2 * k + 1] = __high2float(cp[k]);
+          }
+        } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        st1(Z, umma::kmaj(m0 + k, i, C), kc[k] * zb);
-        st1(QRAT, umma::kmaj(m0 + k, i, RC), qc[k] * fa);
+          for (int k = 0; k < 8; ++k) {
+            r.w[u][k] = ld_io(p.phw.ptr, ok + k, p.io_dtype);
+            r.q[u][k] = ld_io(p.phq.ptr, oq + k, p.io_dtype);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { r.w[u][k] = 0.f; r.q[u][k] = 0.f; }
       }
     }
   }
 }
 
-// ---- transposed code operands: KWT[m][i] = kw, KRT[m][i] = kr, QRT[m][(r,i)] = qr ----------
-// Units of (one mode, 8 consecutive tokens) so every row is written with 16-byte stores.
-template <int FL, int KD, int R>
-__device__ void build_codes_T(const sca2_scan_args& p, bf16* KWT, bf16* KRT, bf16* QRT, const float* s_lam,
-                              const float* s_wr, const float* s_wi, int flags, int b, int h, int t0, int Cl) {
+struct GateRegs {
+  float bt[2], gg[2];
+};
+__device__ __forceinline__ void load_gate_regs(const sca2_scan_args& p, GateRegs& r, int b, int h, int t0, int Cl) {
+  const int l = threadIdx.x & 31;
+  const float* bp = reinterpret_cast<const float*>(p.beta.ptr);
+  const float* gp = reinterpret_cast<const float*>(p.g.ptr);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = l + 32 * u;
+    r.bt[u] = (bp && i < Cl) ? bp[tok_off(p.beta, b, t0 + i, h)] : 0.f;
+    r.gg[u] = (gp && i < Cl) ? gp[tok_off(p.g, b, t0 + i, h)] : 0.f;
+  }
+}
+// warp 0: beta, Gc (inclusive cumsum of g), a = e^Gc, w = e^{G_last - Gc} from the registers
+__device__ __forceinline__ void gates_from_regs(const GateRegs& r, const Gates& s, int Cl) {
+  const int l = threadIdx.x & 31;
+  const float s0 = warp_incl_scan(r.gg[0]);
+  const float tot0 = __shfl_sync(0xffffffffu, s0, 31);
+  const float s1 = warp_incl_scan(r.gg[1]) + tot0;
+  const float sel = (Cl - 1) < 32 ? s0 : s1;
+  const float Glast = __shfl_sync(0xffffffffu, sel, (Cl - 1) & 31);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = l + 32 * u;
+    const float G = u ? s1 : s0;
+    s.beta[i] = r.bt[u];
+    s.Gc[i] = G;
+    s.a[i] = expf(G);
+    s.w[i] = i < Cl ? exp_le0(Glast - G) : 0.f;
+  }
+}
+
+// ---- asynchronous copies of the next chunk's saved data ------------------------------------
+template <int KD>
+__device__ __forceinline__ void pf_state(uint8_t* dst, const float* cstates, int64_t slot_base, int V, int vb0) {
+  // 64 rows m of 64 fp32 columns -> [m][v] (16 copies per row)
+  for (int u = threadIdx.x; u < KD * 16; u += NT) {
+    const int m = u >> 4, v4 = (u & 15) * 4;
+    cp16(dst + (m * BVB + v4) * 4, cstates + slot_base + (int64_t)m * V + vb0 + v4, true);
+  }
+}
+__device__ __forceinline__ void pf_bytes(uint8_t* dst, const uint8_t* src, int nbytes) {
+  for (int u = threadIdx.x * 16; u < nbytes; u += NT * 16) cp16(dst + u, src + u, true);
+}
+template <int R>
+__device__ __forceinline__ void pf_dO(const sca2_scan_args& p, const sca2_out& dO, bf16* DOA, int flags, int b,
+                                      int h, int t0, int Cl, int vb0) {
   constexpr int RC = R * C;
-  const int tid = threadIdx.x;
-  if constexpr (FL == SCA2_FLAVOR_PHASE) {
-    constexpr int Mh = KD / 2, NU = Mh * (C / 8) / NT;
-    const float* phw = reinterpret_cast<const float*>(p.phw.ptr);
-    const float* phq = reinterpret_cast<const float*>(p.phq.ptr);
+  for (int u = threadIdx.x; u < RC * (BVB / 8); u += NT) {
+    const int row = u >> 3, v0 = (u & 7) * 8, r = row >> 6, i = row & 63;
+    const bool live = i < Cl;
+    const int64_t off = live ? out_off(dO, b, t0 + i, h, r) + vb0 + v0 : 0;
+    bf16* dst = DOA + umma::kmaj(row, v0, BVB);
+    if (flags & B_DO_VEC) {
+      cp16(dst, reinterpret_cast<const bf16*>(dO.ptr) + off, live);
+    } else {
+      float x[8];
 #pragma unroll
-    for (int u = 0; u < (NU > 0 ? NU : 1); ++u) {
-      const int unit = tid + u * NT;
-      if (unit >= Mh * (C / 8)) break;
-      const int m = unit % Mh, i0 = (unit / Mh) * 8;
-      const float l = s_lam[m], wr = s_wr[m], wi = s_wi[m];
-      float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = i0 + k;
-        float c = 0.f, s = 0.f, cq = 0.f, sq = 0.f;
-        if (i < Cl) {
-          sincosf(phw[tok_off(p.phw, b, t0 + i, h) + m], &s, &c);
-          sincosf(phq[tok_off(p.phq, b, t0 + i, h) + m], &sq, &cq);
-        }
-        const float ell = __expf(-l * (float)i), elli = __expf(l * (float)i);
-        const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
-        kc[k] = c * ell; ks[k] = s * ell; wc[k] = c * elli; ws[k] = s * elli;
-        q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
-      }
-      st8(KRT, umma::kmaj(m, i0, C), kc);
-      st8(KRT, umma::kmaj(Mh + m, i0, C), ks);
-      st8(KWT, umma::kmaj(m, i0, C), wc);
-      st8(KWT, umma::kmaj(Mh + m, i0, C), ws);
-      st8(QRT, umma::kmaj(m, i0, RC), q0a);
-      st8(QRT, umma::kmaj(Mh + m, i0, RC), q0b);
-      st8(QRT, umma::kmaj(m, C + i0, RC), q1a);
-      st8(QRT, umma::kmaj(Mh + m, C + i0, RC), q1b);
-    }
-  } else {
-    constexpr int NU = KD * (C / 8) / NT;
-#pragma unroll
-    for (int u = 0; u < NU; ++u) {
-      const int unit = tid + u * NT, m = unit % KD, i0 = (unit / KD) * 8;
-      const float l = s_lam[m];
-      float kc[8], wc[8], qc[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = i0 + k;
-        const float kk = i < Cl ? ld_io(p.phw.ptr, tok_off(p.phw, b, t0 + i, h) + m, p.io_dtype) : 0.f;
-        const float qq = i < Cl ? p.q_scale * ld_io(p.phq.ptr, tok_off(p.phq, b, t0 + i, h) + m, p.io_dtype) : 0.f;
-        const float ell = __expf(-l * (float)i), elli = __expf(l * (float)i);
-        kc[k] = kk * ell; wc[k] = kk * elli; qc[k] = qq * ell;
-      }
-      st8(KRT, umma::kmaj(m, i0, C), kc);
-      st8(KWT, umma::kmaj(m, i0, C), wc);
-      st8(QRT, umma::kmaj(m, i0, RC), qc);
+      for (int k = 0; k < 8; ++k) x[k] = (live && vb0 + v0 + k < p.V) ? ld_io(dO.ptr, off + k, p.io_dtype) : 0.f;
+      st8(dst, 0, x);
     }
   }
 }
 
-// ---- chain rule from the code-space gradients to the inputs, per (token, mode) --------------
+// ---- code operands and the per-chunk cache --------------------------------------------------
+//   KR[i][m] = kr, KW[i][m] = kw, QR[(r,i)][m] = qr, ZN[i][m] = -beta a kr / kappa,
+//   KWW[i][m] = w kw, QRA[(r,i)][m] = a qr / kappa; cache: cos / sin of phi and psi (phase)
+//   or k and q * scale (key), fp32 [.][i][m]
 template <int FL, int KD, int R>
-__device__ void finish_key_grads(const sca2_scan_args& p, const sca2_scan_grads& gr, const float* GKR,
-                                 const float* GKW, const float* GKW3, const float* GQR, const float* GKRS,
-                                 const float* GQRS, const float* GLW, const Gates& g,
-                                 const float* s_lam, const float* s_wr, const float* s_wi, float* s_dlam,
-                                 float* s_dwr, float* s_dwi, int b, int h, int t0, int Cl) {
+__device__ __forceinline__ void build_codes2(const CodeRegs<FL>& cr, uint8_t* sm, const Gates& g, const float* s_lam,
+                                             const float* s_wr, const float* s_wi, float q_scale, int Cl, float ik) {
+  using L = BwdLayout<FL, R>;
+  bf16* KR = reinterpret_cast<bf16*>(sm + L::KR);
+  bf16* KW = reinterpret_cast<bf16*>(sm + L::KW);
+  bf16* QR = reinterpret_cast<bf16*>(sm + L::QR);
+  bf16* QRA = reinterpret_cast<bf16*>(sm + L::R1);
+  bf16* KWW = reinterpret_cast<bf16*>(sm + L::R2);
+  bf16* ZN = reinterpret_cast<bf16*>(sm + L::R3);
+  float* cache = reinterpret_cast<float*>(sm + L::CACHE);
   const int tid = threadIdx.x;
-  const float fCl1 = (float)(Cl - 1);
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;
-    const float* phw = reinterpret_cast<const float*>(p.phw.ptr);
-    const float* phq = reinterpret_cast<const float*>(p.phq.ptr);
-    float* dphw = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
-    float* dphq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
-    for (int idx = tid; idx < C * Mh; idx += NT) {
-      const int i = idx / Mh, m = idx % Mh;
-      if (i >= Cl) continue;
-      float s, c, sq, cq;
-      sincosf(phw[tok_off(p.phw, b, t0 + i, h) + m], &s, &c);
-      sincosf(phq[tok_off(p.phq, b, t0 + i, h) + m], &sq, &cq);
-      const float l = s_lam[m], fi = (float)i;
-      const float ell = __expf(-l * fi), elli = __expf(l * fi);
-      const float wr = s_wr[m], wi = s_wi[m];
-      const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
-      const float krc = c * ell, krs = s * ell, kwc = c * elli, kws = s * elli;
-      const float q00 = c1 * ell, q01 = c2 * ell, q10 = -c2 * ell, q11 = c1 * ell;
-      const float dkrc = GKR[i * KD + m], dkrs = GKR[i * KD + m + Mh];
-      const float dkwc = GKW[i * KD + m], dkws = GKW[i * KD + m + Mh];
-      const float d3c = GKW3[i * KD + m], d3s = GKW3[i * KD + m + Mh];
-      const float dq00 = GQR[i * KD + m], dq01 = GQR[i * KD + m + Mh];
-      const float dq10 = GQR[(C + i) * KD + m], dq11 = GQR[(C + i) * KD + m + Mh];
-      const float dkc = dkrc * ell + dkwc * elli, dks = dkrs * ell + dkws * elli;
-      const float dc1 = (dq00 + dq11) * ell, dc2 = (dq01 - dq10) * ell;
-      atomicAdd(&dphw[tok_off(gr.dphw, b, t0 + i, h) + m], -s * dkc + c * dks);
-      atomicAdd(&dphq[tok_off(gr.dphq, b, t0 + i, h) + m],
-                -sq * (dc1 * wr - dc2 * wi) + cq * (dc1 * wi + dc2 * wr));
-      atomicAdd(&s_dwr[m], dc1 * cq + dc2 * sq);
-      atomicAdd(&s_dwi[m], dc1 * sq - dc2 * cq);
-      if (p.lam) {
-        // intra-chunk pairs enter through the position-weighted product GLW (no cancellation
-        // between the i-weighted read side and the j-weighted write side); the state-side
-        // parts keep their own position weights
-        const float sr0 = GKRS[i * KD + m], sr1 = GKRS[i * KD + m + Mh];
-        const float sq00 = GQRS[i * KD + m], sq01 = GQRS[i * KD + m + Mh];
-        const float sq10 = GQRS[(C + i) * KD + m], sq11 = GQRS[(C + i) * KD + m + Mh];
-        const float dl = kwc * GLW[i * KD + m] + kws * GLW[i * KD + m + Mh] -
-                         fi * (sr0 * krc + sr1 * krs + sq00 * q00 + sq01 * q01 + sq10 * q10 + sq11 * q11) +
-                         (fi - fCl1) * (kwc * d3c + kws * d3s);
-        atomicAdd(&s_dlam[m], dl);
+    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    const bool live = i < Cl;
+    const float fi = (float)i, zb = -g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
+    float c[8], s[8], cq[8], sq[8];
+    float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int m = m0 + k;
+      c[k] = s[k] = cq[k] = sq[k] = 0.f;
+      if (live) {
+        sincosf(cr.w[0][k], &s[k], &c[k]);
+        sincosf(cr.q[0][k], &sq[k], &cq[k]);
       }
+      const float l = s_lam[m];
+      const float ell = __expf(-l * fi), elli = __expf(l * fi);
+      const float c1 = s_wr[m] * cq[k] + s_wi[m] * sq[k], c2 = s_wr[m] * sq[k] - s_wi[m] * cq[k];
+      kc[k] = c[k] * ell; ks[k] = s[k] * ell; wc[k] = c[k] * elli; ws[k] = s[k] * elli;
+      q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
     }
+    float4* cw = reinterpret_cast<float4*>(cache + (0 * C + i) * Mh + m0);
+    float4* sw = reinterpret_cast<float4*>(cache + (1 * C + i) * Mh + m0);
+    float4* cqp = reinterpret_cast<float4*>(cache + (2 * C + i) * Mh + m0);
+    float4* sqp = reinterpret_cast<float4*>(cache + (3 * C + i) * Mh + m0);
+    cw[0] = make_float4(c[0], c[1], c[2], c[3]); cw[1] = make_float4(c[4], c[5], c[6], c[7]);
+    sw[0] = make_float4(s[0], s[1], s[2], s[3]); sw[1] = make_float4(s[4], s[5], s[6], s[7]);
+    cqp[0] = make_float4(cq[0], cq[1], cq[2], cq[3]); cqp[1] = make_float4(cq[4], cq[5], cq[6], cq[7]);
+    sqp[0] = make_float4(sq[0], sq[1], sq[2], sq[3]); sqp[1] = make_float4(sq[4], sq[5], sq[6], sq[7]);
+    st8(KR, umma::kmaj(i, m0, KD), kc);
+    st8(KR, umma::kmaj(i, Mh + m0, KD), ks);
+    st8(KW, umma::kmaj(i, m0, KD), wc);
+    st8(KW, umma::kmaj(i, Mh + m0, KD), ws);
+    st8(QR, umma::kmaj(i, m0, KD), q0a);
+    st8(QR, umma::kmaj(i, Mh + m0, KD), q0b);
+    st8(QR, umma::kmaj(C + i, m0, KD), q1a);
+    st8(QR, umma::kmaj(C + i, Mh + m0, KD), q1b);
+    float t[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = zb * kc[k];
+    st8(ZN, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = zb * ks[k];
+    st8(ZN, umma::kmaj(i, Mh + m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = wv * wc[k];
+    st8(KWW, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = wv * ws[k];
+    st8(KWW, umma::kmaj(i, Mh + m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = fa * q0a[k];
+    st8(QRA, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = fa * q0b[k];
+    st8(QRA, umma::kmaj(i, Mh + m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = fa * q1a[k];
+    st8(QRA, umma::kmaj(C + i, m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = fa * q1b[k];
+    st8(QRA, umma::kmaj(C + i, Mh + m0, KD), t);
   } else {
-    float* dk = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
-    float* dq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
-    for (int idx = tid; idx < C * KD; idx += NT) {
-      const int i = idx / KD, m = idx % KD;
-      if (i >= Cl) continue;
-      const float kk = ld_io(p.phw.ptr, tok_off(p.phw, b, t0 + i, h) + m, p.io_dtype);
-      const float qq = p.q_scale * ld_io(p.phq.ptr, tok_off(p.phq, b, t0 + i, h) + m, p.io_dtype);
-      const float l = s_lam[m], fi = (float)i;
-      const float ell = __expf(-l * fi), elli = __expf(l * fi);
-      const float dkr = GKR[i * KD + m], dkw = GKW[i * KD + m], dqr = GQR[i * KD + m];
-      atomicAdd(&dk[tok_off(gr.dphw, b, t0 + i, h) + m], dkr * ell + dkw * elli);
-      atomicAdd(&dq[tok_off(gr.dphq, b, t0 + i, h) + m], p.q_scale * dqr * ell);
-      if (p.lam) {
-        const float dl = kk * elli * GLW[i * KD + m] -
-                         fi * ell * (GKRS[i * KD + m] * kk + GQRS[i * KD + m] * qq) +
-                         (fi - fCl1) * kk * elli * GKW3[i * KD + m];
-        atomicAdd(&s_dlam[m], dl);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int unit = tid + u * NT, i = unit >> 3, m0 = (unit & 7) * 8;
+      const float fi = (float)i, zb = -g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
+      float kk[8], qq[8], kc[8], wc[8], qc[8], t[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float l = s_lam[m0 + k];
+        const float ell = __expf(-l * fi), elli = __expf(l * fi);
+        kk[k] = cr.w[u][k];
+        qq[k] = q_scale * cr.q[u][k];
+        kc[k] = kk[k] * ell; wc[k] = kk[k] * elli; qc[k] = qq[k] * ell;
       }
+      float4* kp = reinterpret_cast<float4*>(cache + (0 * C + i) * KD + m0);
+      float4* qp = reinterpret_cast<float4*>(cache + (1 * C + i) * KD + m0);
+      kp[0] = make_float4(kk[0], kk[1], kk[2], kk[3]); kp[1] = make_float4(kk[4], kk[5], kk[6], kk[7]);
+      qp[0] = make_float4(qq[0], qq[1], qq[2], qq[3]); qp[1] = make_float4(qq[4], qq[5], qq[6], qq[7]);
+      st8(KR, umma::kmaj(i, m0, KD), kc);
+      st8(KW, umma::kmaj(i, m0, KD), wc);
+      st8(QR, umma::kmaj(i, m0, KD), qc);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = zb * kc[k];
+      st8(ZN, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = wv * wc[k];
+      st8(KWW, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = fa * qc[k];
+      st8(QRA, umma::kmaj(i, m0, KD), t);
     }
   }
 }
@@ -341,20 +331,40 @@ __device__ __forceinline__ float sum16(float x) {
   return x;
 }
 
-template <int FL, int KD, int VB, int R>
+// fp32 gradient rows: += 8 consecutive values (plain read-add-write when this CTA is the only
+// writer, else atomics)
+__device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, bool exclusive) {
+  if (exclusive && vec) {
+    float4* d = reinterpret_cast<float4*>(dst);
+    float4 a = d[0], b = d[1];
+    a.x += x[0]; a.y += x[1]; a.z += x[2]; a.w += x[3];
+    b.x += x[4]; b.y += x[5]; b.z += x[6]; b.w += x[7];
+    d[0] = a;
+    d[1] = b;
+  } else if (exclusive) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] += x[k];
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) atomicAdd(dst + k, x[k]);
+  }
+}
+
+template <int FL, int R>
 __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                     const float* cstates, sca2_scan_grads gr, int NCS,
                                                     int flags) {
-  using L = BwdLayout<KD, VB, R>;
+  using L = BwdLayout<FL, R>;
   using CO = BCols;
-  constexpr int RC = R * C;
-  constexpr int Mh = KD / 2;
+  constexpr int KD = 64, VB = BVB, RC = R * C, Mh = KD / 2;
+  constexpr int KH = FL == SCA2_FLAVOR_PHASE ? Mh : KD;
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, sub = warp & 3;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, sub = warp & 3, half = tid >> 7;
   const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int vb0 = blockIdx.y * VB;
   const int V = p.V;
   const bool has_g = p.g.ptr != nullptr;
+  const bool excl = gridDim.y == 1;  // the only CTA writing this (b, h)'s key-side gradients
   const float kappa = FL == SCA2_FLAVOR_PHASE ? (float)Mh : 1.f;
   const float ik = 1.f / kappa;
   float* sc = reinterpret_cast<float*>(sm + L::SC);
@@ -374,22 +384,24 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   float* s_dwi = s_dwr + KD;
   float* s_misc = s_dwi + KD;
   auto BF = [&](int off) { return reinterpret_cast<bf16*>(sm + off); };
-  float* LS = reinterpret_cast<float*>(sm + L::LS);
-  float* TS = reinterpret_cast<float*>(sm + L::TS);
-  float* WS = reinterpret_cast<float*>(sm + L::WS);
-  float* GKR = reinterpret_cast<float*>(sm + L::GKR);
-  float* GKW = reinterpret_cast<float*>(sm + L::GKW);
-  float* GKW3 = reinterpret_cast<float*>(sm + L::GKW3);
-  float* GQR = reinterpret_cast<float*>(sm + L::GQR);
-  float* GKRS = reinterpret_cast<float*>(sm + L::GKRS);
-  float* GQRS = reinterpret_cast<float*>(sm + L::GQRS);
-  float* GLW = reinterpret_cast<float*>(sm + L::GLW);
+  float* CST = reinterpret_cast<float*>(sm + L::CST);
+  float* LAMS = reinterpret_cast<float*>(sm + L::LAMS);
+  float* cache = reinterpret_cast<float*>(sm + L::CACHE);
+  bf16* PA = BF(L::R1);
+  bf16* DQKA = BF(L::R1);
+  bf16* DEA = BF(L::R2);
+  bf16* DKKA = BF(L::R2);
+  float* PQ = reinterpret_cast<float*>(sm + L::R2);
+  bf16* DKKW = BF(L::R3);
+  bf16* SB = BF(L::R4);
+  bf16* DSB = BF(L::R4 + VB * KD * 2);
+  bf16* DQKW = BF(L::R4);
+  bf16* DYA = BF(L::R5);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
 
   // ---- set-up
-  constexpr int KH = FL == SCA2_FLAVOR_PHASE ? Mh : KD;
   for (int m = tid; m < KD; m += NT) {
     const float l = p.lam ? p.lam[h * KH + (m % KH)] : 0.f;
     s_lam[m] = l;
@@ -400,6 +412,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     s_dwr[m] = 0.f;
     s_dwi[m] = 0.f;
   }
+  for (int u = tid; u < KD * VB; u += NT) LAMS[u] = 0.f;
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
@@ -412,7 +425,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   const uint32_t tb = *s_tmem;
   uint32_t phase = 0;
 
-  // state-layout registers (rows v of an M = VB fragment, columns m): adjoint dS and Sp
+  // state-layout registers (rows v of an M = 64 fragment, columns m): adjoint dS and Sp
   constexpr int NS = KD / 2;
   float dSreg[NS], Spreg[NS];
   const int srow = frag_row<VB>();
@@ -425,7 +438,6 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       const int m = frag_col0<VB, KD>(q) + j;
       dSreg[16 * q + j] = (sown && dS_final) ? dS_final[bhKV + (int64_t)m * V + vb0 + srow] : 0.f;
     }
-  float Ureg[C / 2], R0reg[C / 2];
 
   auto wait_mma = [&]() -> bool {
     if (!umma::mbar_wait(mbar, phase)) *s_err = 1;
@@ -435,17 +447,33 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     return *s_err == 0;
   };
   auto Dg = [&](int i, int j) -> float { return has_g ? __expf(fminf(gates.Gc[i] - gates.Gc[j], 0.f)) : 1.f; };
+  const int64_t bhs = ((int64_t)b * p.H + h) * NCS;
+  auto slot = [&](int s) -> int64_t { return (bhs + s) * KD * (int64_t)V; };
+  auto saved = [&](int c) -> const uint8_t* { return reinterpret_cast<const uint8_t*>(cstates + slot(2 * c + 1)); };
 
   const int NC = (p.T + C - 1) / C;
+  // prefetch of the last chunk
+  CodeRegs<FL> creg;
+  GateRegs greg;
+  {
+    const int c = NC - 1, t0 = c * C, Cl = min(C, p.T - t0);
+    pf_state<KD>(sm + L::CST, cstates, slot(2 * c), V, vb0);
+    pf_bytes(sm + L::TB, saved(c), C * C * 2);
+    pf_bytes(sm + L::EB, saved(c) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
+    pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
+    cp_commit();
+    load_code_regs<FL, KD>(p, creg, flags, b, h, t0, Cl);
+    if (warp == 0) load_gate_regs(p, greg, b, h, t0, Cl);
+  }
+
   bool ok = true;
   for (int c = NC - 1; c >= 0 && ok; --c) {
     const int t0 = c * C, Cl = min(C, p.T - t0);
-    const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V;
+    const float fi_last = (float)(Cl - 1);
     // ================= prologue =================
-    ValueLoad<VB> vl;
-    load_values<VB>(p, vl, b, h, t0, Cl, vb0);
-    load_gates(p, gates, b, h, t0, Cl);
-    for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * (float)(Cl - 1));
+    cp_wait_all();
+    if (warp == 0) gates_from_regs(greg, gates, Cl);
+    for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * fi_last);
     if (tid < C) {
       s_dbeta[tid] = 0.f;
       s_da[tid] = 0.f;
@@ -454,237 +482,137 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       s_cols[tid] = 0.f;
     }
     if (tid == 0) s_misc[0] = 0.f;
-    // Sp = d1 .* S (state entering the chunk) in the state layout
-#pragma unroll
-    for (int q = 0; q < KD / 32; ++q)
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = frag_col0<VB, KD>(q) + j;
-        Spreg[16 * q + j] = sown ? cstates[cb + (int64_t)m * V + vb0 + srow] * s_d1[m] : 0.f;
-      }
-    // dO: [(r,i)][v] (16-byte loads from global when aligned) and dO^T [v][(r,i)]
-    for (int u = tid; u < RC * (VB / 8); u += NT) {
-      const int row = u / (VB / 8), v0 = (u % (VB / 8)) * 8, r = row / C, i = row % C;
-      float x[8];
-      if (i < Cl) {
-        const int64_t off = out_off(dO, b, t0 + i, h, r) + vb0 + v0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = ld_io(dO.ptr, off + k, p.io_dtype);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = 0.f;
-      }
-      st8(BF(L::DOA), umma::kmaj(row, v0, VB), x);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) st1(BF(L::DOT), umma::kmaj(v0 + k, row, RC), x[k]);
-    }
-    __syncthreads();  // gates, dCm1 ready
-    build_codes_bwd<FL, KD, R>(p, BF(L::KR), BF(L::KW), BF(L::QR), BF(L::Z), BF(L::KWW), BF(L::QRAT), gates,
-                               s_lam, s_wr, s_wi, flags, b, h, t0, Cl, ik);
-    store_values<VB>(p, vl, gates.beta, BF(L::VT));
-    // Sp^T and dSc^T (bf16, rows v)
+    __syncthreads();  // staged copies, gates and dCm1 visible
+    // Sp = d1 .* S (state layout registers) and the bf16 operands Sp^T, dSc^T [v][m]
     if (sown) {
 #pragma unroll
       for (int q = 0; q < KD / 32; ++q) {
+        const int m0 = frag_col0<VB, KD>(q);
         float xs[16], xd[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int m = frag_col0<VB, KD>(q) + j;
+          const int m = m0 + j;
+          Spreg[16 * q + j] = CST[m * VB + srow] * s_d1[m];
           xs[j] = Spreg[16 * q + j];
           xd[j] = s_dCm1[m] * dSreg[16 * q + j];
         }
-        const int m0 = frag_col0<VB, KD>(q);
-        st8(BF(L::SB), umma::kmaj(srow, m0, KD), xs);
-        st8(BF(L::SB), umma::kmaj(srow, m0 + 8, KD), xs + 8);
-        st8(BF(L::DSB), umma::kmaj(srow, m0, KD), xd);
-        st8(BF(L::DSB), umma::kmaj(srow, m0 + 8, KD), xd + 8);
+        st8(SB, umma::kmaj(srow, m0, KD), xs);
+        st8(SB, umma::kmaj(srow, m0 + 8, KD), xs + 8);
+        st8(DSB, umma::kmaj(srow, m0, KD), xd);
+        st8(DSB, umma::kmaj(srow, m0 + 8, KD), xd + 8);
       }
     }
+    build_codes2<FL, KD, R>(creg, sm, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
-    // ================= batch 1: G, P^T =================
+    // ================= batch 1 =================
     if (tid == 0) {
-      umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
-      umma::gemm(tb + CO::PT, sm + L::KW, sm + L::QR, 64, RC, KD, false);
+      umma::gemm_t(tb + CO::G, sm + L::KR, false, sm + L::KW, false, C, C, KD, false);
+      umma::gemm_t(tb + CO::P, sm + L::QR, false, sm + L::KW, false, RC, C, KD, false);
+      umma::gemm_t(tb + CO::DS0, sm + L::DOA, true, sm + L::R1, true, VB, KD, RC, false);
+      umma::gemm_t(tb + CO::DQR2, sm + L::DOA, false, SB, true, RC, KD, VB, false);
+      umma::gemm_t(tb + CO::DKW3, sm + L::EB, true, DSB, true, C, KD, VB, false);
+      umma::gemm_t(tb + CO::DE, sm + L::R2, false, DSB, false, C, VB, KD, false);
       umma::commit(mbar);
     }
+    // next chunk: staged state (CST is free once the prologue has read it), codes and gates
+    if (c > 0) {
+      const int t1 = t0 - C;
+      pf_state<KD>(sm + L::CST, cstates, slot(2 * (c - 1)), V, vb0);
+      cp_commit();
+      load_code_regs<FL, KD>(p, creg, flags, b, h, t1, C);
+      if (warp == 0) load_gate_regs(p, greg, b, h, t1, C);
+    }
     if (!(ok = wait_mma())) break;
-    for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
-      const float bi = gates.beta[i] * ik;
+    // ---- P masked, decayed, / kappa -> PA [(r,i)][j]
+    for_frag<RC, C>(tb + CO::P, [&](int row, int j0, int, const float* x) {
+      const int i = row & 63;
+      float y[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        LS[i * LDF + jj] = jj < i ? bi * x[j] * Dg(i, jj) : 0.f;
+        y[j] = jj <= i ? x[j] * ik * Dg(i, jj) : 0.f;
       }
+      st8(PA, umma::kmaj(row, j0, C), y);
+      st8(PA, umma::kmaj(row, j0 + 8, C), y + 8);
     });
-    for_frag<64, RC>(tb + CO::PT, [&](int jr, int c0, int, const float* x) {
-      float y[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int i = (c0 + k) % C;
-        y[k] = jr <= i ? x[k] * ik * Dg(i, jr) : 0.f;
-      }
-      st8(BF(L::PT), umma::kmaj(jr, c0, RC), y);
-      st8(BF(L::PT), umma::kmaj(jr, c0 + 8, RC), y + 8);
-    });
-    __syncthreads();
-    invert_unit_lower(LS, TS, WS);
-    store_T<false>(TS, BF(L::TB));
-    store_T<true>(TS, BF(L::TBT));
     publish_smem();
-    // ================= batch 2: U^T, Wk =================
+    // ================= batch 2: dE += P^T dO =================
     if (tid == 0) {
-      umma::gemm(tb + CO::UT, sm + L::VT, sm + L::TB, VB, C, C, false);
-      umma::gemm(tb + CO::WK, sm + L::TB, sm + L::Z, 64, KD, C, false);
+      umma::gemm_t(tb + CO::DE, PA, true, sm + L::DOA, true, C, VB, RC, true);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
-    for_frag<VB, C>(tb + CO::UT, [&](int, int, int q, const float* x) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) Ureg[16 * q + j] = x[j];
-    });
-    for_frag<64, KD>(tb + CO::WK, [&](int i, int m0, int, const float* x) {
-      st8(BF(L::WK), umma::kmaj(i, m0, KD), x);
-      st8(BF(L::WK), umma::kmaj(i, m0 + 8, KD), x + 8);
+    for_frag<C, VB>(tb + CO::DE, [&](int j, int v0, int, const float* x) {
+      st8(DEA, umma::kmaj(j, v0, VB), x);
+      st8(DEA, umma::kmaj(j, v0 + 8, VB), x + 8);
     });
     publish_smem();
-    // ================= batch 3: X^T, R0^T, dE^T (two parts), dS0p^T (part 1), Os =================
+    // ================= batch 3: dY = T^T dE =================
     if (tid == 0) {
-      umma::gemm(tb + CO::XT, sm + L::SB, sm + L::WK, VB, C, KD, false);
-      umma::gemm(tb + CO::R0T, sm + L::SB, sm + L::KR, VB, C, KD, false);
-      umma::gemm(tb + CO::DE1, sm + L::DSB, sm + L::KWW, VB, C, KD, false);
-      umma::gemm(tb + CO::DE2, sm + L::DOT, sm + L::PT, VB, C, RC, false);
-      umma::gemm(tb + CO::DS0, sm + L::DOT, sm + L::QRAT, VB, KD, RC, false);
-      umma::gemm(tb + CO::OS, sm + L::QR, sm + L::SB, RC, VB, KD, false);
+      umma::gemm_t(tb + CO::DY, sm + L::TB, true, DEA, true, C, VB, C, false);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
-    // ---- pool A is free from here on
-    // E = U - X (rows v) -> EA [i][v]; R0 -> regs; dE^T -> DEB; dw_j = sum_v E dE1
-    {
-#pragma unroll
-      for (int q = 0; q < C / 32; ++q) {
-        const int i0 = frag_col0<VB, C>(q);
-        float xx[16], r0[16], d1v[16], d2v[16];
-        umma::ld16(umma::taddr(tb + CO::XT, 32 * sub, i0), xx);
-        umma::ld16(umma::taddr(tb + CO::R0T, 32 * sub, i0), r0);
-        umma::ld16(umma::taddr(tb + CO::DE1, 32 * sub, i0), d1v);
-        umma::ld16(umma::taddr(tb + CO::DE2, 32 * sub, i0), d2v);
-        float e[16], de[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int i = i0 + j;
-          e[j] = Ureg[16 * q + j] - xx[j];
-          R0reg[16 * q + j] = r0[j] * gates.a[i] * ik;
-          de[j] = d1v[j] + d2v[j];
-        }
-        if (sown) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) st1(BF(L::EA), umma::kmaj(i0 + j, srow, VB), e[j]);
-          st8(BF(L::DEB), umma::kmaj(srow, i0, C), de);
-          st8(BF(L::DEB), umma::kmaj(srow, i0 + 8, C), de + 8);
-        }
-        if (has_g) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float t = sum16(sown ? e[j] * d1v[j] : 0.f);
-            if (lane == 0) atomicAdd(&s_dw[i0 + j], t);
-          }
-        }
-      }
-      // da (first term): sum_r sum_v dO * Os * a / kappa over rows (r, i)
-      if (has_g) {
-        const int row = frag_row<RC>(), i = row % C;
-#pragma unroll
-        for (int q = 0; q < VB / 32; ++q) {
-          const int v0 = frag_col0<RC, VB>(q);
-          float os[16];
-          umma::ld16(umma::taddr(tb + CO::OS, 32 * sub, v0), os);
-          if (owns_rows<RC>()) {
-            float s = 0.f;
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              s += os[j] * __bfloat162float(BF(L::DOA)[umma::kmaj(row, v0 + j, VB)]);
-            atomicAdd(&s_da[i], s * gates.a[i] * ik);
-          }
-        }
-      }
+    if (c > 0) {  // TB is free: the next chunk's T
+      pf_bytes(sm + L::TB, saved(c - 1), C * C * 2);
+      cp_commit();
     }
-    // late operands for batch 6 (pool B): kw^T, kr^T, qr^T, Sp, dSc
-    build_codes_T<FL, KD, R>(p, BF(L::KWT), BF(L::KRT), BF(L::QRT), s_lam, s_wr, s_wi, flags, b, h, t0, Cl);
-    if (sown) {
-#pragma unroll
-      for (int q = 0; q < KD / 32; ++q)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = frag_col0<VB, KD>(q) + j;
-          st1(BF(L::SBT), umma::kmaj(m, srow, VB), Spreg[16 * q + j]);
-          st1(BF(L::DSBT), umma::kmaj(m, srow, VB), s_dCm1[m] * dSreg[16 * q + j]);
-        }
-    }
-    publish_smem();
-    // ================= batch 4: dY^T = dE^T T =================
-    if (tid == 0) {
-      umma::gemm(tb + CO::DYT, sm + L::DEB, sm + L::TBT, VB, C, C, false);
-      umma::commit(mbar);
-    }
-    if (!(ok = wait_mma())) break;
     {
       const float* bp = reinterpret_cast<const float*>(p.beta.ptr);
-#pragma unroll
-      for (int q = 0; q < C / 32; ++q) {
-        const int i0 = frag_col0<VB, C>(q);
-        float dy[16];
-        umma::ld16(umma::taddr(tb + CO::DYT, 32 * sub, i0), dy);
-        float ndy[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int i = i0 + j;
-          ndy[j] = -dy[j];
-          float s = sown ? dy[j] * R0reg[16 * q + j] : 0.f;
+      for_frag<C, VB>(tb + CO::DY, [&](int i, int v0, int, const float* x) {
+        st8(DYA, umma::kmaj(i, v0, VB), x);
+        st8(DYA, umma::kmaj(i, v0 + 8, VB), x + 8);
+        if (i < Cl) {
+          float y[16];
           float sv = 0.f;
-          if (sown && i < Cl && vb0 + srow < V) {
-            const int64_t off = tok_off(p.v, b, t0 + i, h) + vb0 + srow;
-            float dv = dy[j];
-            if (p.v_times_beta) {
-              sv = dy[j] * ld_io(p.v.ptr, off, p.io_dtype);
-              dv *= bp[tok_off(p.beta, b, t0 + i, h)];
-            }
-            st_io(const_cast<void*>(gr.dv.ptr), tok_off(gr.dv, b, t0 + i, h) + vb0 + srow, dv, p.io_dtype);
+          const float bi = p.v_times_beta ? bp[tok_off(p.beta, b, t0 + i, h)] : 1.f;
+          const int64_t off = tok_off(gr.dv, b, t0 + i, h) + vb0 + v0;
+          if (p.v_times_beta) {
+            const int64_t ov = tok_off(p.v, b, t0 + i, h) + vb0 + v0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sv += x[j] * ld_io(p.v.ptr, ov + j, p.io_dtype);
+            atomicAdd(&s_dbeta[i], sv);
           }
-          s = sum16(s);
-          if (p.v_times_beta) sv = sum16(sv);
-          if (lane == 0) {
-            atomicAdd(&s_dbeta[i], sv - s);
-            atomicAdd(&s_da[i], -gates.beta[i] * s);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) y[j] = bi * x[j];
+          if (flags & B_DV_VEC) {
+            bf16* dst = reinterpret_cast<bf16*>(const_cast<void*>(gr.dv.ptr)) + off;
+            st8(dst, 0, y);
+            st8(dst, 8, y + 8);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (vb0 + v0 + j < V) st_io(const_cast<void*>(gr.dv.ptr), off + j, y[j], p.io_dtype);
           }
-          if (sown) st1(BF(L::DYA), umma::kmaj(i, srow, VB), dy[j]);
         }
-        if (sown) {
-          st8(BF(L::DYB), umma::kmaj(srow, i0, C), ndy);
-          st8(BF(L::DYB), umma::kmaj(srow, i0 + 8, C), ndy + 8);
-        }
-      }
+      });
     }
     publish_smem();
-    // ================= batch 5: dL, dP, dS0p^T (part 2) =================
+    // ================= batch 4: DL, DP, DS0 += dY^T ZN, DKR2 =================
     if (tid == 0) {
-      umma::gemm(tb + CO::DL, sm + L::DYA, sm + L::EA, 64, C, VB, false);
-      umma::gemm(tb + CO::DP, sm + L::DOA, sm + L::EA, RC, C, VB, false);
-      umma::gemm(tb + CO::DS0, sm + L::DYB, sm + L::Z, VB, KD, C, true);
+      umma::gemm_t(tb + CO::DL, DYA, false, sm + L::EB, true, C, C, VB, false);
+      umma::gemm_t(tb + CO::DP, sm + L::DOA, false, sm + L::EB, true, RC, C, VB, false);
+      umma::gemm_t(tb + CO::DS0, DYA, true, sm + L::R3, true, VB, KD, C, true);
+      umma::gemm_t(tb + CO::DKR2, DYA, false, SB, true, C, KD, VB, false);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
-    // dL with Gr -> dKK, dbeta, decay sums
+    if (c > 0) {  // EB and DOA are free: the next chunk's E and dO
+      pf_bytes(sm + L::EB, saved(c - 1) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
+      pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0 - C, C, vb0);
+      cp_commit();
+    }
+    // ---- dL with G -> dKK (+ position-weighted), d(beta) row term, decay sums
     {
+      const int i = frag_row<C>();
+      const bool own = owns_rows<C>();
 #pragma unroll
       for (int q = 0; q < C / 32; ++q) {
-        const int j0 = frag_col0<64, C>(q);
+        const int j0 = frag_col0<C, C>(q);
         float dl[16], gg[16];
         umma::ld16(umma::taddr(tb + CO::DL, 32 * sub, j0), dl);
         umma::ld16(umma::taddr(tb + CO::G, 32 * sub, j0), gg);
-        const int i = frag_row<64>();
-        const bool own = owns_rows<64>();
-        float dkk[16];
+        float dkk[16], dkw[16];
         float sb = 0.f, srow_ = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -700,6 +628,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             val = gates.beta[i] * l * d;
           }
           dkk[j] = val;
+          dkw[j] = val * (float)(jj - i);
           if (has_g) {
             const float t = sum16(gcol);
             if (lane == 0) atomicAdd(&s_cols[jj], t);
@@ -708,24 +637,23 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         if (own) {
           atomicAdd(&s_dbeta[i], sb);
           if (has_g) atomicAdd(&s_rows[i], srow_);
-          st8(BF(L::DKKA), umma::kmaj(i, j0, C), dkk);
-          st8(BF(L::DKKA), umma::kmaj(i, j0 + 8, C), dkk + 8);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            st1(BF(L::DKKT), umma::kmaj(j0 + j, i, C), dkk[j]);
-            st1(BF(L::DKKWT), umma::kmaj(j0 + j, i, C), dkk[j] * (float)(j0 + j - i));
-          }
+          st8(DKKA, umma::kmaj(i, j0, C), dkk);
+          st8(DKKA, umma::kmaj(i, j0 + 8, C), dkk + 8);
+          st8(DKKW, umma::kmaj(i, j0, C), dkw);
+          st8(DKKW, umma::kmaj(i, j0 + 8, C), dkw + 8);
         }
       }
-      // dP -> dQK and decay sums
+    }
+    // ---- dP -> dQK (+ weighted) and decay sums (P read back in place before dQK overwrites it)
+    {
+      const int row = frag_row<RC>(), i = row & 63;
+      const bool own = owns_rows<RC>();
 #pragma unroll
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<RC, C>(q);
         float dp[16];
         umma::ld16(umma::taddr(tb + CO::DP, 32 * sub, j0), dp);
-        const int row = frag_row<RC>(), i = row % C;
-        const bool own = owns_rows<RC>();
-        float dqk[16];
+        float dqk[16], dqw[16];
         float srow_ = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -734,11 +662,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           if (own && jj <= i) {
             val = dp[j] * Dg(i, jj);
             if (has_g) {
-              gcol = dp[j] * __bfloat162float(BF(L::PT)[umma::kmaj(jj, row, RC)]);
+              gcol = dp[j] * __bfloat162float(PA[umma::kmaj(row, jj, C)]);
               srow_ += gcol;
             }
           }
           dqk[j] = val;
+          dqw[j] = val * (float)(jj - i);
           if (has_g) {
             float t = gcol;
             if (RC == 128) {
@@ -752,37 +681,32 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         }
         if (own) {
           if (has_g) atomicAdd(&s_rows[i], srow_);
-          st8(BF(L::DQKA), umma::kmaj(row, j0, C), dqk);
-          st8(BF(L::DQKA), umma::kmaj(row, j0 + 8, C), dqk + 8);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            st1(BF(L::DQKT), umma::kmaj(j0 + j, row, RC), dqk[j]);
-            st1(BF(L::DQKWT), umma::kmaj(j0 + j, row, RC), dqk[j] * (float)(j0 + j - i));
-          }
+          st8(DQKA, umma::kmaj(row, j0, C), dqk);
+          st8(DQKA, umma::kmaj(row, j0 + 8, C), dqk + 8);
+          st8(DQKW, umma::kmaj(row, j0, C), dqw);
+          st8(DQKW, umma::kmaj(row, j0 + 8, C), dqw + 8);
         }
       }
-      // dS0p^T -> adjoint update, state-side decay gradients
+    }
+    // ---- DS0 -> adjoint update and state-side lambda / decay terms
+    {
       const float aC = gates.a[Cl - 1];
+      const float fCl = (float)Cl;
       float daC = 0.f;
 #pragma unroll
       for (int q = 0; q < KD / 32; ++q) {
         const int m0 = frag_col0<VB, KD>(q);
         float d0[16];
         umma::ld16(umma::taddr(tb + CO::DS0, 32 * sub, m0), d0);
+        if (sown) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + j;
-          float dl = 0.f;
-          if (sown) {
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + j;
             const float sp = Spreg[16 * q + j], ds = dSreg[16 * q + j];
             const float t = aC * s_dCm1[m] * sp * ds;
             daC += t;
-            dl = -d0[j] * sp - (float)Cl * t;
+            LAMS[m * VB + srow] += -d0[j] * sp - fCl * t;
             dSreg[16 * q + j] = aC * s_dCm1[m] * s_d1[m] * ds + s_d1[m] * d0[j];
-          }
-          if (p.lam) {
-            const float t = sum16(dl);
-            if (lane == 0) atomicAdd(&s_dlam[m], t);
           }
         }
       }
@@ -792,81 +716,232 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       }
     }
     publish_smem();
-    // ================= batch 6: dkr, dqr, dkw =================
+    // ================= batch 5: DKR1, DQR1, DKW12, DLW =================
     if (tid == 0) {
-      umma::gemm(tb + CO::DKR1, sm + L::DKKA, sm + L::KWT, 64, KD, C, false);
-      umma::gemm(tb + CO::DKR2, sm + L::DYA, sm + L::SBT, 64, KD, VB, false);
-      umma::gemm(tb + CO::DQR1, sm + L::DQKA, sm + L::KWT, RC, KD, C, false);
-      umma::gemm(tb + CO::DQR2, sm + L::DOA, sm + L::SBT, RC, KD, VB, false);
-      umma::gemm(tb + CO::DKW12, sm + L::DKKT, sm + L::KRT, 64, KD, C, false);
-      umma::gemm(tb + CO::DKW12, sm + L::DQKT, sm + L::QRT, 64, KD, RC, true);
-      umma::gemm(tb + CO::DKW3, sm + L::EA, sm + L::DSBT, 64, KD, VB, false);
+      umma::gemm_t(tb + CO::DKR1, DKKA, false, sm + L::KW, true, C, KD, C, false);
+      umma::gemm_t(tb + CO::DQR1, DQKA, false, sm + L::KW, true, RC, KD, C, false);
+      umma::gemm_t(tb + CO::DKW12, DKKA, true, sm + L::KR, true, C, KD, C, false);
+      umma::gemm_t(tb + CO::DKW12, DQKA, true, sm + L::QR, true, C, KD, RC, true);
       if (p.lam) {
-        umma::gemm(tb + CO::DLW, sm + L::DKKWT, sm + L::KRT, 64, KD, C, false);
-        umma::gemm(tb + CO::DLW, sm + L::DQKWT, sm + L::QRT, 64, KD, RC, true);
+        umma::gemm_t(tb + CO::DLW, DKKW, true, sm + L::KR, true, C, KD, C, false);
+        umma::gemm_t(tb + CO::DLW, DQKW, true, sm + L::QR, true, C, KD, RC, true);
       }
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
-    // ---- stage fp32 key-side gradients (pool B is free); tcgen05.ld is warp-collective, so
-    // every lane loads and only row owners store
+    // ================= finish =================
+    const bool gvec = flags & B_G_VEC;
+    // ---- key side (rows i of the M = 64 accumulators)
     {
-      const int i = frag_row<64>();
-      const bool own = owns_rows<64>();
+      const int i = frag_row<C>();
+      const bool own = owns_rows<C>() && i < Cl;
+      const float fi = (float)i;
+      const float bi = gates.beta[i], aik = gates.a[i] * ik, wi_ = gates.w[i];
+      float bsum = 0.f, wsum = 0.f;
+      float* dk = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
+      if constexpr (FL == SCA2_FLAVOR_PHASE) {
 #pragma unroll
-      for (int q = 0; q < KD / 32; ++q) {
-        const int m0 = frag_col0<64, KD>(q);
-        float x[16], y[16];
-        umma::ld16(umma::taddr(tb + CO::DKR1, 32 * sub, m0), x);
-        umma::ld16(umma::taddr(tb + CO::DKR2, 32 * sub, m0), y);
-        if (own) {
-          const float f = gates.beta[i] * gates.a[i] * ik;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            GKR[i * KD + m0 + j] = x[j] * ik - f * y[j];
-            GKRS[i * KD + m0 + j] = -f * y[j];
+        for (int g8 = 0; g8 < 2; ++g8) {
+          const int mg = 16 * half + 8 * g8;  // modes mg..mg+7: code columns mg (cos), Mh + mg (sin)
+          float r1c[8], r1s[8], r2c[8], r2s[8], w12c[8], w12s[8], w3c[8], w3s[8], lwc[8], lws[8];
+          umma::ld8(umma::taddr(tb + CO::DKR1, 32 * sub, mg), r1c);
+          umma::ld8(umma::taddr(tb + CO::DKR1, 32 * sub, Mh + mg), r1s);
+          umma::ld8(umma::taddr(tb + CO::DKR2, 32 * sub, mg), r2c);
+          umma::ld8(umma::taddr(tb + CO::DKR2, 32 * sub, Mh + mg), r2s);
+          umma::ld8(umma::taddr(tb + CO::DKW12, 32 * sub, mg), w12c);
+          umma::ld8(umma::taddr(tb + CO::DKW12, 32 * sub, Mh + mg), w12s);
+          umma::ld8(umma::taddr(tb + CO::DKW3, 32 * sub, mg), w3c);
+          umma::ld8(umma::taddr(tb + CO::DKW3, 32 * sub, Mh + mg), w3s);
+          if (p.lam) {
+            umma::ld8(umma::taddr(tb + CO::DLW, 32 * sub, mg), lwc);
+            umma::ld8(umma::taddr(tb + CO::DLW, 32 * sub, Mh + mg), lws);
           }
-        }
-        umma::ld16(umma::taddr(tb + CO::DKW12, 32 * sub, m0), x);
-        umma::ld16(umma::taddr(tb + CO::DKW3, 32 * sub, m0), y);
-        if (own) {
-          const float wv = gates.w[i];
+          float dl[8], dph[8];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            GKW3[i * KD + m0 + j] = wv * y[j];
-            GKW[i * KD + m0 + j] = x[j] * ik + wv * y[j];
+          for (int k = 0; k < 8; ++k) {
+            dl[k] = 0.f;
+            dph[k] = 0.f;
           }
-        }
-        if (p.lam) {
-          umma::ld16(umma::taddr(tb + CO::DLW, 32 * sub, m0), x);
           if (own) {
+            const float* cw = cache + (0 * C + i) * Mh + mg;
+            const float* sw = cache + (1 * C + i) * Mh + mg;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) GLW[i * KD + m0 + j] = x[j] * ik;
+            for (int k = 0; k < 8; ++k) {
+              const int m = mg + k;
+              const float c = cw[k], s = sw[k];
+              const float l = s_lam[m];
+              const float ell = __expf(-l * fi), elli = __expf(l * fi);
+              const float krc = c * ell, krs = s * ell, kwc = c * elli, kws = s * elli;
+              const float rc = aik * r2c[k], rs = aik * r2s[k];
+              const float dkrc = r1c[k] * ik - bi * rc, dkrs = r1s[k] * ik - bi * rs;
+              const float dkwc = w12c[k] * ik + wi_ * w3c[k], dkws = w12s[k] * ik + wi_ * w3s[k];
+              const float dkc = dkrc * ell + dkwc * elli, dks = dkrs * ell + dkws * elli;
+              dph[k] = -s * dkc + c * dks;
+              const float kr_r = krc * rc + krs * rs, kw_w3 = kwc * w3c[k] + kws * w3s[k];
+              bsum += kr_r;
+              wsum += kw_w3;
+              if (p.lam) dl[k] = ik * (kwc * lwc[k] + kws * lws[k]) + fi * bi * kr_r + (fi - fi_last) * wi_ * kw_w3;
+            }
+            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + mg, dph, gvec, excl);
+          }
+          if (p.lam) {
+            const float x = warp_transpose_sum<8>(dl);
+            if ((lane & 3) == 0) atomicAdd(&s_dlam[mg + red_index<8>(lane)], x);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int g8 = 0; g8 < 4; ++g8) {
+          const int m0 = 32 * half + 8 * g8;
+          float r1[8], r2[8], w12[8], w3[8], lw[8];
+          umma::ld8(umma::taddr(tb + CO::DKR1, 32 * sub, m0), r1);
+          umma::ld8(umma::taddr(tb + CO::DKR2, 32 * sub, m0), r2);
+          umma::ld8(umma::taddr(tb + CO::DKW12, 32 * sub, m0), w12);
+          umma::ld8(umma::taddr(tb + CO::DKW3, 32 * sub, m0), w3);
+          if (p.lam) umma::ld8(umma::taddr(tb + CO::DLW, 32 * sub, m0), lw);
+          float dl[8], dkv[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            dl[k] = 0.f;
+            dkv[k] = 0.f;
+          }
+          if (own) {
+            const float* kp = cache + (0 * C + i) * KD + m0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int m = m0 + k;
+              const float kk = kp[k];
+              const float l = s_lam[m];
+              const float ell = __expf(-l * fi), elli = __expf(l * fi);
+              const float kr = kk * ell, kw = kk * elli;
+              const float rr = aik * r2[k];
+              const float dkr = r1[k] * ik - bi * rr, dkw = w12[k] * ik + wi_ * w3[k];
+              dkv[k] = dkr * ell + dkw * elli;
+              bsum += kr * rr;
+              wsum += kw * w3[k];
+              if (p.lam) dl[k] = ik * kw * lw[k] + fi * bi * kr * rr + (fi - fi_last) * wi_ * kw * w3[k];
+            }
+            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, dkv, gvec, excl);
+          }
+          if (p.lam) {
+            const float x = warp_transpose_sum<8>(dl);
+            if ((lane & 3) == 0) atomicAdd(&s_dlam[m0 + red_index<8>(lane)], x);
           }
         }
       }
-      const int row = frag_row<RC>();
-      const bool ownq = owns_rows<RC>();
-#pragma unroll
-      for (int q = 0; q < KD / 32; ++q) {
-        const int m0 = frag_col0<RC, KD>(q);
-        float x[16], y[16];
-        umma::ld16(umma::taddr(tb + CO::DQR1, 32 * sub, m0), x);
-        umma::ld16(umma::taddr(tb + CO::DQR2, 32 * sub, m0), y);
-        if (ownq) {
-          const float f = gates.a[row % C] * ik;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            GQR[row * KD + m0 + j] = x[j] * ik + f * y[j];
-            GQRS[row * KD + m0 + j] = f * y[j];
-          }
+      if (own) {
+        atomicAdd(&s_dbeta[i], -bsum);
+        if (has_g) {
+          atomicAdd(&s_da[i], -bi * bsum);
+          atomicAdd(&s_dw[i], wi_ * wsum);
         }
       }
     }
+    // ---- query side (rows (r, i) of the M = R*64 accumulators)
+    {
+      const int row = frag_row<RC>(), r = row >> 6, i = row & 63;
+      const bool own = owns_rows<RC>() && i < Cl;
+      const float fi = (float)i, aik = gates.a[i] * ik;
+      float asum = 0.f;
+      float* dq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
+      if constexpr (FL == SCA2_FLAVOR_PHASE) {
+#pragma unroll
+        for (int g8 = 0; g8 < 2; ++g8) {
+          const int mg = 16 * half + 8 * g8;
+          float q1c[8], q1s[8], q2c[8], q2s[8];
+          umma::ld8(umma::taddr(tb + CO::DQR1, 32 * sub, mg), q1c);
+          umma::ld8(umma::taddr(tb + CO::DQR1, 32 * sub, Mh + mg), q1s);
+          umma::ld8(umma::taddr(tb + CO::DQR2, 32 * sub, mg), q2c);
+          umma::ld8(umma::taddr(tb + CO::DQR2, 32 * sub, Mh + mg), q2s);
+          float pq[8], dwr[8], dwi[8], dl[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            pq[k] = dwr[k] = dwi[k] = dl[k] = 0.f;
+          }
+          if (own) {
+            const float* cqp = cache + (2 * C + i) * Mh + mg;
+            const float* sqp = cache + (3 * C + i) * Mh + mg;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int m = mg + k;
+              const float cq = cqp[k], sq = sqp[k];
+              const float wr = s_wr[m], wi = s_wi[m];
+              const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
+              const float ell = __expf(-s_lam[m] * fi);
+              const float gc = aik * q2c[k], gs = aik * q2s[k];
+              const float dqc = (q1c[k] * ik + gc) * ell, dqs = (q1s[k] * ik + gs) * ell;
+              const float dc1 = r ? dqs : dqc, dc2 = r ? -dqc : dqs;
+              const float qrc = (r ? -c2 : c1) * ell, qrs = (r ? c1 : c2) * ell;
+              pq[k] = -sq * (dc1 * wr - dc2 * wi) + cq * (dc1 * wi + dc2 * wr);
+              dwr[k] = dc1 * cq + dc2 * sq;
+              dwi[k] = dc1 * sq - dc2 * cq;
+              const float gq = gc * qrc + gs * qrs;
+              dl[k] = -fi * gq;
+              asum += gq;
+            }
+          }
+          // combine the two read columns of (i, m): r = 1 rows hand their part to r = 0 rows
+          if (own && r == 1) {
+            float4* d = reinterpret_cast<float4*>(PQ + i * Mh + mg);
+            d[0] = make_float4(pq[0], pq[1], pq[2], pq[3]);
+            d[1] = make_float4(pq[4], pq[5], pq[6], pq[7]);
+          }
+          __syncthreads();
+          if (own && r == 0) {
+            const float* s = PQ + i * Mh + mg;
+            float y[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) y[k] = pq[k] + s[k];
+            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + mg, y, gvec, excl);
+          }
+          __syncthreads();
+          {
+            float x = warp_transpose_sum<8>(dwr);
+            if ((lane & 3) == 0) atomicAdd(&s_dwr[mg + red_index<8>(lane)], x);
+            x = warp_transpose_sum<8>(dwi);
+            if ((lane & 3) == 0) atomicAdd(&s_dwi[mg + red_index<8>(lane)], x);
+            if (p.lam) {
+              x = warp_transpose_sum<8>(dl);
+              if ((lane & 3) == 0) atomicAdd(&s_dlam[mg + red_index<8>(lane)], x);
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int g8 = 0; g8 < 4; ++g8) {
+          const int m0 = 32 * half + 8 * g8;
+          float q1[8], q2[8];
+          umma::ld8(umma::taddr(tb + CO::DQR1, 32 * sub, m0), q1);
+          umma::ld8(umma::taddr(tb + CO::DQR2, 32 * sub, m0), q2);
+          float dl[8], dqv[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            dl[k] = 0.f;
+            dqv[k] = 0.f;
+          }
+          if (own) {
+            const float* qp = cache + (1 * C + i) * KD + m0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int m = m0 + k;
+              const float ell = __expf(-s_lam[m] * fi);
+              const float gqs = aik * q2[k];
+              dqv[k] = p.q_scale * (q1[k] * ik + gqs) * ell;
+              const float gq = gqs * qp[k] * ell;
+              dl[k] = -fi * gq;
+              asum += gq;
+            }
+            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, dqv, gvec, excl);
+          }
+          if (p.lam) {
+            const float x = warp_transpose_sum<8>(dl);
+            if ((lane & 3) == 0) atomicAdd(&s_dlam[m0 + red_index<8>(lane)], x);
+          }
+        }
+      }
+      if (own && has_g) atomicAdd(&s_da[i], asum);
+    }
     __syncthreads();
-    // ---- per (token, mode): chain rule to the inputs, lambda / w gradients
-    finish_key_grads<FL, KD, R>(p, gr, GKR, GKW, GKW3, GQR, GKRS, GQRS, GLW, gates, s_lam, s_wr, s_wi, s_dlam,
-                                s_dwr, s_dwi, b, h, t0, Cl);
     // ---- per-token beta and decay gradients
     if (tid < 32) {
       float dGv[2], dwv[2];
@@ -903,6 +978,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     }
     publish_smem();
   }
+  cp_wait_all();
+  __syncthreads();
   // ---- incoming-state gradient and per-head gradients
   if (ok) {
     if (gr.dS0 && sown) {
@@ -912,6 +989,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         for (int j = 0; j < 16; ++j)
           gr.dS0[bhKV + (int64_t)(frag_col0<VB, KD>(q) + j) * V + vb0 + srow] = dSreg[16 * q + j];
     }
+    // state-side lambda terms: sum over the value columns
+    for (int m = warp; m < KD; m += NT / 32) {
+      const float x = warp_sum(LAMS[m * VB + lane] + LAMS[m * VB + 32 + lane]);
+      if (lane == 0) s_dlam[m] += x;
+    }
+    __syncthreads();
     for (int m = tid; m < KD; m += NT) {
       if (gr.dlam && p.lam) atomicAdd(&gr.dlam[h * KH + (m % KH)], s_dlam[m]);
       if (FL == SCA2_FLAVOR_PHASE && m < Mh) {
@@ -920,7 +1003,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       }
     }
   } else {
-    if (tid == 0) atomicOr(&g_fault, 1u);
+    if (tid == 0) atomicOr(&g_fault_bwd, 1u);
     umma::mbar_wait(mbar, phase ^ 1u);
   }
   umma::fence_before_sync();
@@ -928,38 +1011,59 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   if (tid < 32) umma::tmem_dealloc(tb, CO::ALLOC);
 }
 
-template <int FL, int KD, int VB, int R>
+template <int FL, int R>
 cudaError_t launch_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
                        const sca2_scan_grads& gr, int NCS, int flags, cudaStream_t st) {
-  auto k = scan_bwd_tc<FL, KD, VB, R>;
-  const int smem = BwdLayout<KD, VB, R>::TOTAL;
+  auto k = scan_bwd_tc<FL, R>;
+  const int smem = BwdLayout<FL, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.B * p.H, p.V / VB);
+  dim3 grid(p.B * p.H, p.V / BVB);
   k<<<grid, NT, smem, st>>>(p, dO, dS_final, cstates, gr, NCS, flags);
   return cudaGetLastError();
 }
 
 }  // namespace tc
 
-int tc_bwd_smem(int K, int VB, int R) {
-  if (K == 64 && VB == 64 && R == 2) return tc::BwdLayout<64, 64, 2>::TOTAL;
-  if (K == 64 && VB == 64 && R == 1) return tc::BwdLayout<64, 64, 1>::TOTAL;
-  return 1 << 30;
+int tc_bwd_smem(int K, int R) {
+  if (K != 64) return 1 << 30;
+  return R == 2 ? tc::BwdLayout<SCA2_FLAVOR_PHASE, 2>::TOTAL : tc::BwdLayout<SCA2_FLAVOR_KEY, 1>::TOTAL;
 }
 
-// Whether a bf16 training pass (forward with saved chunk states + backward) runs on the tensor
-// cores: K = 64, V a multiple of 64, both kernels within the shared-memory limit.
+// read and clear the backward's device fault word (synchronous)
+cudaError_t tc_read_faults_bwd(unsigned int* out) {
+  unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(out, tc::g_fault_bwd, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(tc::g_fault_bwd, &zero, sizeof(unsigned int));
+}
+
+// Whether a bf16 training pass (forward with saved chunk data + backward) runs on the tensor
+// cores: K = 64, V a multiple of 64, both kernels within the shared-memory limit.  The decision
+// depends on the arguments shared by the forward and the backward only, so the pair agrees.
 bool tc_train_ok(const sca2_scan_args& p, int max_smem) {
   const int R = p.flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
-  return p.io_dtype == SCA2_BF16 && p.K == 64 && p.V % 64 == 0 && tc_bwd_smem(64, 64, R) <= max_smem;
+  return p.io_dtype == SCA2_BF16 && p.K == 64 && p.V % 64 == 0 && tc_bwd_smem(64, R) <= max_smem;
 }
 
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
                         const sca2_scan_grads& gr, int NCS, cudaStream_t st) {
+  auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
+  int f = 0;
+  if (p.flavor == SCA2_FLAVOR_PHASE && a16(p.phw.ptr) && a16(p.phq.ptr) && p.phw.sb % 4 == 0 &&
+      p.phw.st % 4 == 0 && p.phw.sh % 4 == 0 && p.phq.sb % 4 == 0 && p.phq.st % 4 == 0 && p.phq.sh % 4 == 0)
+    f |= tc::B_PH_VEC;
+  if (p.flavor == SCA2_FLAVOR_KEY && a16(p.phw.ptr) && a16(p.phq.ptr) && p.phw.sb % 8 == 0 &&
+      p.phw.st % 8 == 0 && p.phw.sh % 8 == 0 && p.phq.sb % 8 == 0 && p.phq.st % 8 == 0 && p.phq.sh % 8 == 0)
+    f |= tc::B_K_VEC;
+  if (a16(dO.ptr) && dO.sb % 8 == 0 && dO.st % 8 == 0 && dO.sh % 8 == 0 && dO.sr % 8 == 0) f |= tc::B_DO_VEC;
+  if (a16(gr.dv.ptr) && gr.dv.sb % 8 == 0 && gr.dv.st % 8 == 0 && gr.dv.sh % 8 == 0) f |= tc::B_DV_VEC;
+  if (a16(gr.dphw.ptr) && a16(gr.dphq.ptr) && gr.dphw.sb % 4 == 0 && gr.dphw.st % 4 == 0 && gr.dphw.sh % 4 == 0 &&
+      gr.dphq.sb % 4 == 0 && gr.dphq.st % 4 == 0 && gr.dphq.sh % 4 == 0)
+    f |= tc::B_G_VEC;
   if (p.flavor == SCA2_FLAVOR_PHASE)
-    return tc::launch_bwd<SCA2_FLAVOR_PHASE, 64, 64, 2>(p, dO, dS_final, cstates, gr, NCS, 0, st);
-  return tc::launch_bwd<SCA2_FLAVOR_KEY, 64, 64, 1>(p, dO, dS_final, cstates, gr, NCS, 0, st);
+    return tc::launch_bwd<SCA2_FLAVOR_PHASE, 2>(p, dO, dS_final, cstates, gr, NCS, f, st);
+  return tc::launch_bwd<SCA2_FLAVOR_KEY, 1>(p, dO, dS_final, cstates, gr, NCS, f, st);
 }
 
 }  // namespace sca2

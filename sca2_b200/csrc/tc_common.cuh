@@ -75,6 +75,47 @@ __device__ __forceinline__ void for_frag(uint32_t tbase, F f) {
   }
 }
 
+// ---- asynchronous global -> shared copies (16 bytes; zero-filled when !valid) ----------------
+__device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(umma::smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// ---- warp transpose-reduce --------------------------------------------------------------------
+// Every lane holds N values (N = 8 or 16); returns, in lane l, the sum over all 32 lanes of value
+// number red_index<N>(l).  Lanes whose index bits below log2(32 / N) are zero hold distinct
+// results.  Costs N shuffles instead of 5 N.
+template <int N>
+__device__ __forceinline__ float warp_transpose_sum(float* v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int half = N / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+    const bool up = lane & bit;
+#pragma unroll
+    for (int k = 0; k < half; ++k) {
+      const float send = up ? v[k] : v[k + half];
+      const float keep = up ? v[k + half] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+  }
+  float x = v[0];
+#pragma unroll
+  for (int bit = 32 / N / 2; bit >= 1; bit >>= 1) x += __shfl_xor_sync(0xffffffffu, x, bit);
+  return x;
+}
+template <int N>
+__device__ __forceinline__ int red_index(int lane) {
+  // value k = sum of the selection bits, taken from lane bits 4, 3, ... (MSB first)
+  int k = 0;
+#pragma unroll
+  for (int half = N / 2, bit = 16; half >= 1; half >>= 1, bit >>= 1)
+    if (lane & bit) k += half;
+  return k;
+}
+
 __device__ __forceinline__ void publish_smem() {
   umma::fence_async_smem();
   umma::fence_before_sync();

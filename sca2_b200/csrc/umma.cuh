@@ -47,9 +47,22 @@ __device__ __forceinline__ uint64_t kdesc(uint32_t base, int Kt, int kk) {
   return sdesc(base + (uint32_t)kk * 256u, 128u, (uint32_t)(Kt >> 3) * 128u);
 }
 
+// descriptor of an MN-major operand at K step kk.  The buffer is the K-major layout of the
+// operand's transpose: element (mn, k) of the operand sits at kmaj(k, mn, MNt), i.e. 16-byte
+// runs along MN, 8-row groups along K are MNt * 16 bytes apart (LBO) and adjacent MN core
+// matrices 128 bytes apart (SBO).  So one K-major buffer of X serves as X (K-major) in one
+// product and as X^T (MN-major) in another.
+__device__ __forceinline__ uint64_t mdesc(uint32_t base, int MNt, int kk) {
+  return sdesc(base + (uint32_t)kk * 32u * (uint32_t)MNt, (uint32_t)MNt * 16u, 128u);
+}
+
 // instruction descriptor: kind::f16 with bf16 A/B, fp32 D, both operands K-major
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// same with the MN-major (transposed) flags for A (bit 15) and B (bit 16)
+__host__ __device__ constexpr uint32_t idesc_bf16_t(int M, int N, bool a_mn, bool b_mn) {
+  return idesc_bf16(M, N) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16);
 }
 
 // D[tmem] (+)= A * B^T for one K = 16 step; issued by ONE thread
@@ -69,6 +82,16 @@ __device__ __forceinline__ void gemm(uint32_t tmem_d, const void* A, const void*
   const uint32_t a = smem_u32(A), b = smem_u32(B), id = idesc_bf16(M, N);
   for (int kk = 0; kk < Kt / 16; ++kk)
     mma(tmem_d, kdesc(a, Kt, kk), kdesc(b, Kt, kk), id, (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// D (+)= A * B^T where each operand is K-major (rows of its own K elements) or MN-major (the
+// K-major buffer of its transpose, see mdesc).  M x Kt and N x Kt; issued by ONE thread.
+__device__ __forceinline__ void gemm_t(uint32_t tmem_d, const void* A, bool a_mn, const void* B, bool b_mn, int M,
+                                       int N, int Kt, bool accumulate) {
+  const uint32_t a = smem_u32(A), b = smem_u32(B), id = idesc_bf16_t(M, N, a_mn, b_mn);
+  for (int kk = 0; kk < Kt / 16; ++kk)
+    mma(tmem_d, a_mn ? mdesc(a, M, kk) : kdesc(a, Kt, kk), b_mn ? mdesc(b, N, kk) : kdesc(b, Kt, kk), id,
+        (accumulate || kk > 0) ? 1u : 0u);
 }
 
 // arrive on `mbar` once every MMA issued so far by this thread has completed
@@ -135,6 +158,18 @@ __device__ __forceinline__ void ld16(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 8 consecutive fp32 columns -> 8 registers per thread
+__device__ __forceinline__ void ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // TMEM address of (lane, column)

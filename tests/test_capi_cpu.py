@@ -28,7 +28,9 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, n), n
     assert sorted(n for n, _, _ in _lib.SIGNATURES) == names
     assert b"sm_100a" in lib.sca2_version()
-    assert lib.sca2_num_chunks(4096) * 32 == 4096 and lib.sca2_num_chunks(1) == 1
+    # two saved-state slots per 64-token chunk
+    assert lib.sca2_num_chunks(4096) == 128 and lib.sca2_num_chunks(1) == 2 and lib.sca2_num_chunks(65) == 4
+    assert lib.sca2_num_chunks(0) == 0
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
