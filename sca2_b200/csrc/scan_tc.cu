@@ -22,7 +22,9 @@
 // contiguous run of the next operand, and operands are written with 16-byte stores.  Where a
 // bf16 operand alone would miss the bf16 parity bar (the intra-chunk read kernel P and the
 // corrected values E) it is carried as a hi + lo pair (three products hi*hi + hi*lo + lo*hi),
-// which keeps about 16 mantissa bits.  Each MMA batch is issued by one thread and completes
+// which keeps about 16 mantissa bits.  The next chunk's values are copied in with cp.async
+// (straight into the operand layout) and its phases (keys) and gates are loaded into registers
+// while the current chunk runs.  Each MMA batch is issued by one thread and completes
 // on an mbarrier whose wait is bounded: on a timeout the CTA records a fault bit, waits
 // (bounded) once more for its MMAs, frees its TMEM and returns.
 //
@@ -47,10 +49,10 @@ struct FwdLayout {
   static constexpr int KR = 0;                                  // C x KD
   static constexpr int KW = KR + al(C * KD * 2);                // C x KD (hi)
   static constexpr int QR = KW + al(C * KD * 2);                // R*C x KD (hi)
-  static constexpr int Z = QR + al(R * C * KD * 2);             // KD x C
-  static constexpr int VT = Z + al(KD * C * 2);                 // VB x C
-  static constexpr int KWD = VT + al(VB * C * 2);               // KD x C
-  static constexpr int TB = KWD + al(KD * C * 2);               // C x C
+  static constexpr int ZA = QR + al(R * C * KD * 2);            // C x KD  beta a kr / kappa [i][m]
+  static constexpr int VA = ZA + al(C * KD * 2);                // C x VB  values [j][v]
+  static constexpr int KWW = VA + al(VB * C * 2);               // C x KD  w kw [i][m]
+  static constexpr int TB = KWW + al(KD * C * 2);               // C x C
   static constexpr int PB = TB + al(C * C * 2);                 // R*C x C (hi)
   static constexpr int PBL = PB + al(R * C * C * 2);            // R*C x C (lo)
   static constexpr int WK = PBL + al(R * C * C * 2);            // C x KD
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   using L = FwdLayout<KD, VB, R>;
   using CO = Cols<KD, VB>;
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int vb0 = blockIdx.y * VB;
   const int V = p.V;
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   float* LS = reinterpret_cast<float*>(sm + L::LS);
   float* TS = reinterpret_cast<float*>(sm + L::TS);
   float* WS = reinterpret_cast<float*>(sm + L::WS);
-  bf16* VT = reinterpret_cast<bf16*>(sm + L::VT);
+  bf16* VA = reinterpret_cast<bf16*>(sm + L::VA);
   bf16* TB = reinterpret_cast<bf16*>(sm + L::TB);
   bf16* PB = reinterpret_cast<bf16*>(sm + L::PB);
   bf16* PBL = reinterpret_cast<bf16*>(sm + L::PBL);
@@ -120,8 +122,8 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   bf16* EBL = reinterpret_cast<bf16*>(sm + L::EBL);
   CodeOps<FL, KD, R> cops{reinterpret_cast<bf16*>(sm + L::KR), reinterpret_cast<bf16*>(sm + L::KW),
                           reinterpret_cast<bf16*>(sm + L::KWL), reinterpret_cast<bf16*>(sm + L::QR),
-                          reinterpret_cast<bf16*>(sm + L::QRL), reinterpret_cast<bf16*>(sm + L::Z),
-                          reinterpret_cast<bf16*>(sm + L::KWD)};
+                          reinterpret_cast<bf16*>(sm + L::QRL), reinterpret_cast<bf16*>(sm + L::ZA),
+                          reinterpret_cast<bf16*>(sm + L::KWW)};
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
@@ -180,6 +182,18 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   };
 
   const int NC = (p.T + C - 1) / C;
+  const bool code_vec = flags & (FL == SCA2_FLAVOR_PHASE ? F_PH_VEC : F_K_VEC);
+  // chunk 0's values (cp.async), codes and gates (registers); later chunks are prefetched while
+  // the previous one runs
+  CodeRegs<FL, KD> creg;
+  GateRegs greg;
+  {
+    const int Cl0 = min(C, p.T);
+    pf_values<VB>(p, VA, flags & F_V_VEC, b, h, 0, Cl0, vb0);
+    cp_commit();
+    load_code_regs<FL, KD>(p, creg, code_vec, b, h, 0, Cl0);
+    if (warp == 0) load_gate_regs(p, greg, b, h, 0, Cl0);
+  }
   bool ok = true;
   for (int c = 0; c < NC && ok; ++c) {
     const int t0 = c * C, Cl = min(C, p.T - t0);
@@ -196,13 +210,12 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
         for (int j = 0; j < 16; ++j) cstates[cb + (int64_t)(frag_col0<VB, KD>(q) + j) * V] = Sreg[16 * q + j];
     }
     // ---- operands of the chunk
-    ValueLoad<VB> vl;
-    load_values<VB>(p, vl, b, h, t0, Cl, vb0);
-    load_gates(p, gates, b, h, t0, Cl);
+    cp_wait_all();
+    if (warp == 0) gates_from_regs(greg, gates, Cl);
     for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * (float)(Cl - 1));
     __syncthreads();
-    build_codes<FL, KD, R>(p, cops, gates, s_lam, s_wr, s_wi, flags, b, h, t0, Cl, ik);
-    store_values<VB>(p, vl, gates.beta, VT);
+    if (p.v_times_beta) scale_values<VB>(VA, gates.beta);
+    build_codes<FL, KD, R>(creg, cops, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
     if (tid == 0) {
       umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
@@ -210,6 +223,11 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       umma::gemm(tb + CO::P, sm + L::QR, sm + L::KWL, R * 64, 64, KD, true);
       umma::gemm(tb + CO::P, sm + L::QRL, sm + L::KW, R * 64, 64, KD, true);
       umma::commit(mbar);
+    }
+    if (c + 1 < NC) {  // next chunk's codes and gates into registers
+      const int t1 = t0 + C, Cl1 = min(C, p.T - t1);
+      load_code_regs<FL, KD>(p, creg, code_vec, b, h, t1, Cl1);
+      if (warp == 0) load_gate_regs(p, greg, b, h, t1, Cl1);
     }
     if (!(ok = wait_mma())) break;
     // ---- L = beta Gr (fp32) and P (hi + lo), masked and decayed
@@ -241,11 +259,16 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     publish_smem();
     if (cstates && blockIdx.y == 0) copy_out(saved, TB, C * C * 2);
     if (tid == 0) {
-      umma::gemm(tb + CO::UT, sm + L::VT, sm + L::TB, VB, C, C, false);
-      umma::gemm(tb + CO::WK, sm + L::TB, sm + L::Z, 64, KD, C, false);
+      umma::gemm_t(tb + CO::UT, VA, true, TB, false, VB, C, C, false);
+      umma::gemm_t(tb + CO::WK, TB, false, sm + L::ZA, true, 64, KD, C, false);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
+    if (c + 1 < NC) {  // VA is free: next chunk's values
+      const int t1 = t0 + C;
+      pf_values<VB>(p, VA, flags & F_V_VEC, b, h, t1, min(C, p.T - t1), vb0);
+      cp_commit();
+    }
     for_frag<VB, C>(tb + CO::UT, [&](int, int, int q, const float* x) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) Ureg[16 * q + j] = x[j];
@@ -274,8 +297,8 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EB, R * 64, VB, C, false);
       umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EBL, R * 64, VB, C, true);
       umma::gemm(tb + CO::OP, sm + L::PBL, sm + L::EB, R * 64, VB, C, true);
-      umma::gemm(tb + CO::SUT, sm + L::EB, sm + L::KWD, VB, KD, C, false);
-      umma::gemm(tb + CO::SUT, sm + L::EBL, sm + L::KWD, VB, KD, C, true);
+      umma::gemm_t(tb + CO::SUT, EB, false, sm + L::KWW, true, VB, KD, C, false);
+      umma::gemm_t(tb + CO::SUT, EBL, false, sm + L::KWW, true, VB, KD, C, true);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
@@ -299,12 +322,19 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       const int sub = (tid >> 5) & 3;
       const bool own = owns_rows<M>();
       const int row = frag_row<M>(), r = row >> 6, i = row & 63;
+      uint32_t ra[VB / 32][16], rx[VB / 32][16];
+#pragma unroll
+      for (int q = 0; q < VB / 32; ++q) {
+        umma::ld16_issue(umma::taddr(tb + CO::OS, 32 * sub, frag_col0<M, VB>(q)), ra[q]);
+        umma::ld16_issue(umma::taddr(tb + CO::OP, 32 * sub, frag_col0<M, VB>(q)), rx[q]);
+      }
+      umma::ld_wait();
 #pragma unroll
       for (int q = 0; q < VB / 32; ++q) {
         const int v0 = frag_col0<M, VB>(q);
         float a[16], x[16];
-        umma::ld16(umma::taddr(tb + CO::OS, 32 * sub, v0), a);
-        umma::ld16(umma::taddr(tb + CO::OP, 32 * sub, v0), x);
+        umma::take<16>(ra[q], a);
+        umma::take<16>(rx[q], x);
         if (own && i < Cl) {
           const float fa = gates.a[i] * ik;
           float y[16];
@@ -325,6 +355,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     }
     publish_smem();
   }
+  cp_wait_all();
   if (ok && S_final && sown) {
 #pragma unroll
     for (int q = 0; q < KD / 32; ++q)
@@ -383,6 +414,7 @@ static int tc_flags(const sca2_scan_args& p, const sca2_out& o) {
   if (p.flavor == SCA2_FLAVOR_KEY && a16(p.phw.ptr) && a16(p.phq.ptr) && p.phw.sb % 8 == 0 &&
       p.phw.st % 8 == 0 && p.phw.sh % 8 == 0 && p.phq.sb % 8 == 0 && p.phq.st % 8 == 0 && p.phq.sh % 8 == 0)
     f |= tc::F_K_VEC;
+  if (a16(p.v.ptr) && p.v.sb % 8 == 0 && p.v.st % 8 == 0 && p.v.sh % 8 == 0 && p.V % 8 == 0) f |= tc::F_V_VEC;
   if (a16(o.ptr) && o.sb % 8 == 0 && o.st % 8 == 0 && o.sh % 8 == 0 && o.sr % 8 == 0 && p.V % 8 == 0)
     f |= tc::F_O_VEC;
   return f;

@@ -85,101 +85,6 @@ struct BCols {
 // launch flags of the backward (host-computed)
 enum : int { B_PH_VEC = 1, B_DO_VEC = 2, B_DV_VEC = 4, B_G_VEC = 8, B_K_VEC = 16 };
 
-// ---- per-thread register prefetch of the next chunk's codes inputs and gates ----------------
-template <int FL>
-struct CodeRegs {
-  float w[2][8], q[2][8];  // phase: one unit (phi, psi x 8 modes); key: two units (k, q x 8)
-};
-
-template <int FL, int KD>
-__device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs<FL>& r, int flags, int b, int h,
-                                               int t0, int Cl) {
-  const int tid = threadIdx.x;
-  if constexpr (FL == SCA2_FLAVOR_PHASE) {
-    const int i = tid >> 2, m0 = (tid & 3) * 8;
-    const float* pw = reinterpret_cast<const float*>(p.phw.ptr);
-    const float* pq = reinterpret_cast<const float*>(p.phq.ptr);
-    if (i < Cl) {
-      const int64_t ow = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
-      if (flags & B_PH_VEC) {
-        const float4 a0 = reinterpret_cast<const float4*>(pw + ow)[0], a1 = reinterpret_cast<const float4*>(pw + ow)[1];
-        const float4 c0 = reinterpret_cast<const float4*>(pq + oq)[0], c1 = reinterpret_cast<const float4*>(pq + oq)[1];
-        r.w[0][0] = a0.x; r.w[0][1] = a0.y; r.w[0][2] = a0.z; r.w[0][3] = a0.w;
-        r.w[0][4] = a1.x; r.w[0][5] = a1.y; r.w[0][6] = a1.z; r.w[0][7] = a1.w;
-        r.q[0][0] = c0.x; r.q[0][1] = c0.y; r.q[0][2] = c0.z; r.q[0][3] = c0.w;
-        r.q[0][4] = c1.x; r.q[0][5] = c1.y; r.q[0][6] = c1.z; r.q[0][7] = c1.w;
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { r.w[0][k] = pw[ow + k]; r.q[0][k] = pq[oq + k]; }
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) { r.w[0][k] = 0.f; r.q[0][k] = 0.f; }
-    }
-  } else {
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int unit = tid + u * NT, i = unit >> 3, m0 = (unit & 7) * 8;
-      if (i < Cl) {
-        const int64_t ok = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
-        if (flags & B_K_VEC) {
-          const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phw.ptr) + ok);
-          const uint4 c = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phq.ptr) + oq);
-          const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&a);
-          const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&c);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            r.w[u][2 * k] = __low2float(ap[k]); r.w[u][2 * k + 1] = __high2float(ap[k]);
-            r.q[u][2 * k] = __low2float(cp[k]); r.q[u][2 * k + 1] = __high2float(cp[k]);
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            r.w[u][k] = ld_io(p.phw.ptr, ok + k, p.io_dtype);
-            r.q[u][k] = ld_io(p.phq.ptr, oq + k, p.io_dtype);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { r.w[u][k] = 0.f; r.q[u][k] = 0.f; }
-      }
-    }
-  }
-}
-
-struct GateRegs {
-  float bt[2], gg[2];
-};
-__device__ __forceinline__ void load_gate_regs(const sca2_scan_args& p, GateRegs& r, int b, int h, int t0, int Cl) {
-  const int l = threadIdx.x & 31;
-  const float* bp = reinterpret_cast<const float*>(p.beta.ptr);
-  const float* gp = reinterpret_cast<const float*>(p.g.ptr);
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int i = l + 32 * u;
-    r.bt[u] = (bp && i < Cl) ? bp[tok_off(p.beta, b, t0 + i, h)] : 0.f;
-    r.gg[u] = (gp && i < Cl) ? gp[tok_off(p.g, b, t0 + i, h)] : 0.f;
-  }
-}
-// warp 0: beta, Gc (inclusive cumsum of g), a = e^Gc, w = e^{G_last - Gc} from the registers
-__device__ __forceinline__ void gates_from_regs(const GateRegs& r, const Gates& s, int Cl) {
-  const int l = threadIdx.x & 31;
-  const float s0 = warp_incl_scan(r.gg[0]);
-  const float tot0 = __shfl_sync(0xffffffffu, s0, 31);
-  const float s1 = warp_incl_scan(r.gg[1]) + tot0;
-  const float sel = (Cl - 1) < 32 ? s0 : s1;
-  const float Glast = __shfl_sync(0xffffffffu, sel, (Cl - 1) & 31);
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int i = l + 32 * u;
-    const float G = u ? s1 : s0;
-    s.beta[i] = r.bt[u];
-    s.Gc[i] = G;
-    s.a[i] = expf(G);
-    s.w[i] = i < Cl ? exp_le0(Glast - G) : 0.f;
-  }
-}
-
 // ---- asynchronous copies of the next chunk's saved data ------------------------------------
 template <int KD>
 __device__ __forceinline__ void pf_state(uint8_t* dst, const float* cstates, int64_t slot_base, int V, int vb0) {
@@ -217,7 +122,7 @@ __device__ __forceinline__ void pf_dO(const sca2_scan_args& p, const sca2_out& d
 //   KWW[i][m] = w kw, QRA[(r,i)][m] = a qr / kappa; cache: cos / sin of phi and psi (phase)
 //   or k and q * scale (key), fp32 [.][i][m]
 template <int FL, int KD, int R>
-__device__ __forceinline__ void build_codes2(const CodeRegs<FL>& cr, uint8_t* sm, const Gates& g, const float* s_lam,
+__device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t* sm, const Gates& g, const float* s_lam,
                                              const float* s_wr, const float* s_wi, float q_scale, int Cl, float ik) {
   using L = BwdLayout<FL, R>;
   bf16* KR = reinterpret_cast<bf16*>(sm + L::KR);
@@ -240,8 +145,8 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL>& cr, uint8_t* sm
       const int m = m0 + k;
       c[k] = s[k] = cq[k] = sq[k] = 0.f;
       if (live) {
-        sincosf(cr.w[0][k], &s[k], &c[k]);
-        sincosf(cr.q[0][k], &sq[k], &cq[k]);
+        sincos_big(cr.w[0][k], &s[k], &c[k]);
+        sincos_big(cr.q[0][k], &sq[k], &cq[k]);
       }
       const float l = s_lam[m];
       const float ell = __expf(-l * fi), elli = __expf(l * fi);
@@ -453,7 +358,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
 
   const int NC = (p.T + C - 1) / C;
   // prefetch of the last chunk
-  CodeRegs<FL> creg;
+  CodeRegs<FL, KD> creg;
   GateRegs greg;
   {
     const int c = NC - 1, t0 = c * C, Cl = min(C, p.T - t0);
@@ -462,7 +367,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     pf_bytes(sm + L::EB, saved(c) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
     pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
     cp_commit();
-    load_code_regs<FL, KD>(p, creg, flags, b, h, t0, Cl);
+    load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t0, Cl);
     if (warp == 0) load_gate_regs(p, greg, b, h, t0, Cl);
   }
 
@@ -519,7 +424,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       const int t1 = t0 - C;
       pf_state<KD>(sm + L::CST, cstates, slot(2 * (c - 1)), V, vb0);
       cp_commit();
-      load_code_regs<FL, KD>(p, creg, flags, b, h, t1, C);
+      load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t1, C);
       if (warp == 0) load_gate_regs(p, greg, b, h, t1, C);
     }
     if (!(ok = wait_mma())) break;

@@ -15,7 +15,7 @@ constexpr int LDF = C + 1;
 using bf16 = __nv_bfloat16;
 
 // launch flags (host-computed, uniform)
-enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4 };
+enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8 };
 
 // ---- bf16 vector stores -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -67,12 +67,33 @@ __device__ __forceinline__ void for_frag(uint32_t tbase, F f) {
   const int sub = warp & 3;
   const bool own = owns_rows<M>();
   const int row = frag_row<M>();
+  uint32_t r[N / 32][16];
+#pragma unroll
+  for (int q = 0; q < N / 32; ++q) umma::ld16_issue(umma::taddr(tbase, 32 * sub, frag_col0<M, N>(q)), r[q]);
+  umma::ld_wait();
 #pragma unroll
   for (int q = 0; q < N / 32; ++q) {
     float v[16];
-    umma::ld16(umma::taddr(tbase, 32 * sub, frag_col0<M, N>(q)), v);
+    umma::take<16>(r[q], v);
     if (own) f(row, frag_col0<M, N>(q), q, v);
   }
+}
+
+// ---- sine and cosine of large phases -----------------------------------------------------
+// Cody and Waite's additive reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
+// Functions", 1980): r = x - k 2pi with k = rint(x / 2pi) and 2pi split into three parts, the
+// first with only 9 significant bits so k * part1 is exact for |k| < 2^15 (|x| < 2e5), then the
+// SFU sine / cosine on r in [-pi, pi] (absolute error about 1e-6 for the phases of this scan).
+__device__ __forceinline__ void sincos_big(float x, float* s, float* c) {
+  constexpr float kInv2Pi = 0.15915494309189535f;
+  constexpr float kP1 = 6.28125f;                   // 2pi rounded to 9 bits
+  constexpr float kP2 = 1.9353071795864769e-3f;     // 2pi - kP1, rounded to fp32
+  constexpr float kP3 = 1.0253131677018246e-11f;    // 2pi - kP1 - kP2, rounded to fp32
+  const float k = rintf(x * kInv2Pi);
+  float r = fmaf(-k, kP1, x);
+  r = fmaf(-k, kP2, r);
+  r = fmaf(-k, kP3, r);
+  __sincosf(r, s, c);
 }
 
 // ---- asynchronous global -> shared copies (16 bytes; zero-filled when !valid) ----------------
@@ -188,195 +209,225 @@ __device__ __forceinline__ void store_T(const float* TS, bf16* TB) {
 struct Gates {
   float *beta, *Gc, *a, *w;
 };
-__device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates& s, int b, int h, int t0, int Cl) {
-  if (threadIdx.x >= 32) return;
-  const int l = threadIdx.x;
-  const float* bp = reinterpret_cast<const float*>(p.beta.ptr);
-  const float* gp = reinterpret_cast<const float*>(p.g.ptr);
-  float bt[2], gg[2];
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int i = l + 32 * u;
-    bt[u] = (bp && i < Cl) ? bp[tok_off(p.beta, b, t0 + i, h)] : 0.f;
-    gg[u] = (gp && i < Cl) ? gp[tok_off(p.g, b, t0 + i, h)] : 0.f;
-  }
-  const float s0 = warp_incl_scan(gg[0]);
-  const float tot0 = __shfl_sync(0xffffffffu, s0, 31);
-  const float s1 = warp_incl_scan(gg[1]) + tot0;
-  const float sel = (Cl - 1) < 32 ? s0 : s1;
-  const float Glast = __shfl_sync(0xffffffffu, sel, (Cl - 1) & 31);
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int i = l + 32 * u;
-    const float G = u ? s1 : s0;
-    s.beta[i] = bt[u];
-    s.Gc[i] = G;
-    s.a[i] = expf(G);
-    s.w[i] = i < Cl ? exp_le0(Glast - G) : 0.f;
-  }
-}
-
-// ---- code operands of one chunk ---------------------------------------------------------------
-// Writes, for tokens i < 64 (zeros for i >= Cl):
-//   KR[i][m] = k e^{-lam i}          KW|KWL[i][m] = k e^{+lam i} (hi|lo)
-//   QR|QRL[(r,i)][m] = Q_r e^{-lam i} (hi|lo)
-//   Z[m][i] = beta a k e^{-lam i}/kappa      KWD[m][i] = w k e^{+lam i}
-// Each thread handles (token, 8 consecutive modes) units so that the [i][m] operands are
-// written with 16-byte stores; the [m][i] operands are written element-wise.
-template <int FL, int KD, int R>
-struct CodeOps {
-  bf16 *KR, *KW, *KWL, *QR, *QRL, *Z, *KWD;
+// ---- per-thread register prefetch of a chunk's code inputs and gates ----------------------------
+// Codes: phase flavour, thread t holds (token t/4, modes 8(t%4)..+7) of phi and psi; key flavour,
+// units t and t+256 of (token u/8, dims 8(u%8)..+7) of k and q.  vec: 16-byte loads are aligned.
+template <int FL, int KD>
+struct CodeRegs {
+  // phase: one unit (phi, psi x 8 modes); key: NU units (k, q x 8 dims)
+  static constexpr int NU = FL == SCA2_FLAVOR_PHASE ? 1 : C * KD / 8 / NT;
+  float w[NU][8], q[NU][8];
 };
-template <int FL, int KD, int R>
-__device__ void build_codes(const sca2_scan_args& p, const CodeOps<FL, KD, R>& op, const Gates& g,
-                            const float* s_lam, const float* s_wr, const float* s_wi, int flags, int b,
-                            int h, int t0, int Cl, float ik) {
+
+template <int FL, int KD>
+__device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs<FL, KD>& r, bool vec, int b, int h,
+                                               int t0, int Cl) {
   const int tid = threadIdx.x;
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
-    constexpr int Mh = KD / 2, MB = Mh / 8, NU = C * MB / NT;
-    const float* phw = reinterpret_cast<const float*>(p.phw.ptr);
-    const float* phq = reinterpret_cast<const float*>(p.phq.ptr);
-    float rw[NU][8], rq[NU][8];
-#pragma unroll
-    for (int u = 0; u < NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
-      if (i < Cl) {
-        const float* pw = phw + tok_off(p.phw, b, t0 + i, h) + m0;
-        const float* pq = phq + tok_off(p.phq, b, t0 + i, h) + m0;
-        if (flags & F_PH_VEC) {
-          const float4 a0 = reinterpret_cast<const float4*>(pw)[0], a1 = reinterpret_cast<const float4*>(pw)[1];
-          const float4 c0 = reinterpret_cast<const float4*>(pq)[0], c1 = reinterpret_cast<const float4*>(pq)[1];
-          rw[u][0] = a0.x; rw[u][1] = a0.y; rw[u][2] = a0.z; rw[u][3] = a0.w;
-          rw[u][4] = a1.x; rw[u][5] = a1.y; rw[u][6] = a1.z; rw[u][7] = a1.w;
-          rq[u][0] = c0.x; rq[u][1] = c0.y; rq[u][2] = c0.z; rq[u][3] = c0.w;
-          rq[u][4] = c1.x; rq[u][5] = c1.y; rq[u][6] = c1.z; rq[u][7] = c1.w;
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) { rw[u][k] = pw[k]; rq[u][k] = pq[k]; }
-        }
+    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    const float* pw = reinterpret_cast<const float*>(p.phw.ptr);
+    const float* pq = reinterpret_cast<const float*>(p.phq.ptr);
+    if (i < Cl) {
+      const int64_t ow = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
+      if (vec) {
+        const float4 a0 = reinterpret_cast<const float4*>(pw + ow)[0], a1 = reinterpret_cast<const float4*>(pw + ow)[1];
+        const float4 c0 = reinterpret_cast<const float4*>(pq + oq)[0], c1 = reinterpret_cast<const float4*>(pq + oq)[1];
+        r.w[0][0] = a0.x; r.w[0][1] = a0.y; r.w[0][2] = a0.z; r.w[0][3] = a0.w;
+        r.w[0][4] = a1.x; r.w[0][5] = a1.y; r.w[0][6] = a1.z; r.w[0][7] = a1.w;
+        r.q[0][0] = c0.x; r.q[0][1] = c0.y; r.q[0][2] = c0.z; r.q[0][3] = c0.w;
+        r.q[0][4] = c1.x; r.q[0][5] = c1.y; r.q[0][6] = c1.z; r.q[0][7] = c1.w;
       } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { rw[u][k] = 0.f; rq[u][k] = 0.f; }
+        for (int k = 0; k < 8; ++k) { r.w[0][k] = pw[ow + k]; r.q[0][k] = pq[oq + k]; }
       }
-    }
+    } else {
 #pragma unroll
-    for (int u = 0; u < NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
-      const bool live = i < Cl;
-      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
-      float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int m = m0 + k;
-        float c = 0.f, s = 0.f, cq = 0.f, sq = 0.f;
-        if (live) {
-          sincosf(rw[u][k], &s, &c);
-          sincosf(rq[u][k], &sq, &cq);
-        }
-        const float l = s_lam[m];
-        const float ell = __expf(-l * fi), elli = __expf(l * fi);
-        const float wr = s_wr[m], wi = s_wi[m];
-        const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
-        kc[k] = c * ell; ks[k] = s * ell; wc[k] = c * elli; ws[k] = s * elli;
-        q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
-      }
-      st8(op.KR, umma::kmaj(i, m0, KD), kc);
-      st8(op.KR, umma::kmaj(i, Mh + m0, KD), ks);
-      st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
-      st8_split(op.KW, op.KWL, umma::kmaj(i, Mh + m0, KD), ws);
-      st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), q0a);
-      st8_split(op.QR, op.QRL, umma::kmaj(i, Mh + m0, KD), q0b);
-      st8_split(op.QR, op.QRL, umma::kmaj(C + i, m0, KD), q1a);
-      st8_split(op.QR, op.QRL, umma::kmaj(C + i, Mh + m0, KD), q1b);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        st1(op.Z, umma::kmaj(m0 + k, i, C), kc[k] * zb);
-        st1(op.Z, umma::kmaj(Mh + m0 + k, i, C), ks[k] * zb);
-        st1(op.KWD, umma::kmaj(m0 + k, i, C), wc[k] * wv);
-        st1(op.KWD, umma::kmaj(Mh + m0 + k, i, C), ws[k] * wv);
-      }
+      for (int k = 0; k < 8; ++k) { r.w[0][k] = 0.f; r.q[0][k] = 0.f; }
     }
   } else {
-    constexpr int MB = KD / 8, NU = C * MB / NT;
+    constexpr int MB = KD / 8;
 #pragma unroll
-    for (int u = 0; u < NU; ++u) {
+    for (int u = 0; u < CodeRegs<FL, KD>::NU; ++u) {
       const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
-      float kk[8], qq[8];
       if (i < Cl) {
         const int64_t ok = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
-        if ((flags & F_K_VEC) && p.io_dtype == SCA2_BF16) {
+        if (vec) {
           const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phw.ptr) + ok);
           const uint4 c = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.phq.ptr) + oq);
           const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&a);
           const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&c);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            kk[2 * k] = __low2float(ap[k]); kk[2 * k + 1] = __high2float(ap[k]);
-            qq[2 * k] = __low2float(cp[k]); qq[2 * k + 1] = __high2float(cp[k]);
+            r.w[u][2 * k] = __low2float(ap[k]); r.w[u][2 * k + 1] = __high2float(ap[k]);
+            r.q[u][2 * k] = __low2float(cp[k]); r.q[u][2 * k + 1] = __high2float(cp[k]);
           }
         } else {
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            kk[k] = ld_io(p.phw.ptr, ok + k, p.io_dtype);
-            qq[k] = ld_io(p.phq.ptr, oq + k, p.io_dtype);
+            r.w[u][k] = ld_io(p.phw.ptr, ok + k, p.io_dtype);
+            r.q[u][k] = ld_io(p.phq.ptr, oq + k, p.io_dtype);
           }
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { kk[k] = 0.f; qq[k] = 0.f; }
-      }
-      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
-      float kc[8], wc[8], qc[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float l = s_lam[m0 + k];
-        const float ell = __expf(-l * fi), elli = __expf(l * fi);
-        kc[k] = kk[k] * ell; wc[k] = kk[k] * elli; qc[k] = p.q_scale * qq[k] * ell;
-      }
-      st8(op.KR, umma::kmaj(i, m0, KD), kc);
-      st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
-      st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), qc);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        st1(op.Z, umma::kmaj(m0 + k, i, C), kc[k] * zb);
-        st1(op.KWD, umma::kmaj(m0 + k, i, C), wc[k] * wv);
+        for (int k = 0; k < 8; ++k) { r.w[u][k] = 0.f; r.q[u][k] = 0.f; }
       }
     }
   }
 }
 
-// ---- value operand: VT[v][i] = v (beta v for the GDN write) ---------------------------------
-// Units of (8 consecutive tokens, one column): loads are coalesced over the columns and the
-// transposed operand is written with 16-byte stores.  Split in two so the loads can be issued
-// before the gates are known.
-template <int VB>
-struct ValueLoad {
-  static constexpr int NU = (C / 8) * VB / NT;
-  float x[NU][8];
+struct GateRegs {
+  float bt[2], gg[2];
 };
-template <int VB>
-__device__ __forceinline__ void load_values(const sca2_scan_args& p, ValueLoad<VB>& r, int b, int h, int t0,
-                                            int Cl, int vb0) {
+__device__ __forceinline__ void load_gate_regs(const sca2_scan_args& p, GateRegs& r, int b, int h, int t0, int Cl) {
+  const int l = threadIdx.x & 31;
+  const float* bp = reinterpret_cast<const float*>(p.beta.ptr);
+  const float* gp = reinterpret_cast<const float*>(p.g.ptr);
 #pragma unroll
-  for (int u = 0; u < ValueLoad<VB>::NU; ++u) {
-    const int unit = threadIdx.x + u * NT, v = unit % VB, i0 = (unit / VB) * 8;
+  for (int u = 0; u < 2; ++u) {
+    const int i = l + 32 * u;
+    r.bt[u] = (bp && i < Cl) ? bp[tok_off(p.beta, b, t0 + i, h)] : 0.f;
+    r.gg[u] = (gp && i < Cl) ? gp[tok_off(p.g, b, t0 + i, h)] : 0.f;
+  }
+}
+// warp 0: beta, Gc (inclusive cumsum of g), a = e^Gc, w = e^{G_last - Gc} from the registers
+__device__ __forceinline__ void gates_from_regs(const GateRegs& r, const Gates& s, int Cl) {
+  const int l = threadIdx.x & 31;
+  const float s0 = warp_incl_scan(r.gg[0]);
+  const float tot0 = __shfl_sync(0xffffffffu, s0, 31);
+  const float s1 = warp_incl_scan(r.gg[1]) + tot0;
+  const float sel = (Cl - 1) < 32 ? s0 : s1;
+  const float Glast = __shfl_sync(0xffffffffu, sel, (Cl - 1) & 31);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = l + 32 * u;
+    const float G = u ? s1 : s0;
+    s.beta[i] = r.bt[u];
+    s.Gc[i] = G;
+    s.a[i] = expf(G);
+    s.w[i] = i < Cl ? exp_le0(Glast - G) : 0.f;
+  }
+}
+
+// ---- code operands of one chunk (forward) -----------------------------------------------------
+// From the prefetched code registers, for tokens i < 64 (zeros for i >= Cl):
+//   KR[i][m] = k e^{-lam i}          KW|KWL[i][m] = k e^{+lam i} (hi|lo)
+//   QR|QRL[(r,i)][m] = Q_r e^{-lam i} (hi|lo)
+//   ZA[i][m] = beta a k e^{-lam i} / kappa     KWW[i][m] = w k e^{+lam i}
+// all written with 16-byte stores; ZA and KWW are read through MN-major descriptors.
+template <int FL, int KD, int R>
+struct CodeOps {
+  bf16 *KR, *KW, *KWL, *QR, *QRL, *ZA, *KWW;
+};
+template <int FL, int KD, int R>
+__device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>& op, const Gates& g, const float* s_lam,
+                            const float* s_wr, const float* s_wi, float q_scale, int Cl, float ik) {
+  const int tid = threadIdx.x;
+  if constexpr (FL == SCA2_FLAVOR_PHASE) {
+    constexpr int Mh = KD / 2;
+    static_assert(C * Mh / 8 == NT, "one (token, 8 modes) unit per thread");
+    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    const bool live = i < Cl;
+    const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
+    float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int i = i0 + k;
-      r.x[u][k] = (i < Cl && vb0 + v < p.V) ? ld_io(p.v.ptr, tok_off(p.v, b, t0 + i, h) + vb0 + v, p.io_dtype) : 0.f;
+      const int m = m0 + k;
+      float c = 0.f, s = 0.f, cq = 0.f, sq = 0.f;
+      if (live) {
+        sincos_big(cr.w[0][k], &s, &c);
+        sincos_big(cr.q[0][k], &sq, &cq);
+      }
+      const float l = s_lam[m];
+      const float ell = __expf(-l * fi), elli = __expf(l * fi);
+      const float wr = s_wr[m], wi = s_wi[m];
+      const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
+      kc[k] = c * ell; ks[k] = s * ell; wc[k] = c * elli; ws[k] = s * elli;
+      q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
+    }
+    st8(op.KR, umma::kmaj(i, m0, KD), kc);
+    st8(op.KR, umma::kmaj(i, Mh + m0, KD), ks);
+    st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
+    st8_split(op.KW, op.KWL, umma::kmaj(i, Mh + m0, KD), ws);
+    st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), q0a);
+    st8_split(op.QR, op.QRL, umma::kmaj(i, Mh + m0, KD), q0b);
+    st8_split(op.QR, op.QRL, umma::kmaj(C + i, m0, KD), q1a);
+    st8_split(op.QR, op.QRL, umma::kmaj(C + i, Mh + m0, KD), q1b);
+    float t[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = zb * kc[k];
+    st8(op.ZA, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = zb * ks[k];
+    st8(op.ZA, umma::kmaj(i, Mh + m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = wv * wc[k];
+    st8(op.KWW, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = wv * ws[k];
+    st8(op.KWW, umma::kmaj(i, Mh + m0, KD), t);
+  } else {
+    constexpr int MB = KD / 8, NU = CodeRegs<FL, KD>::NU;
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
+      float kc[8], wc[8], qc[8], t[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float l = s_lam[m0 + k];
+        const float ell = __expf(-l * fi), elli = __expf(l * fi);
+        kc[k] = cr.w[u][k] * ell; wc[k] = cr.w[u][k] * elli; qc[k] = q_scale * cr.q[u][k] * ell;
+      }
+      st8(op.KR, umma::kmaj(i, m0, KD), kc);
+      st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
+      st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), qc);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = zb * kc[k];
+      st8(op.ZA, umma::kmaj(i, m0, KD), t);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = wv * wc[k];
+      st8(op.KWW, umma::kmaj(i, m0, KD), t);
     }
   }
 }
+
+// ---- value operand VA[j][v] (K-major over v: read MN-major as V'^T) ------------------------------
+// 16-byte cp.async copies when vec (rows 16-byte aligned), else element loads; zero rows j >= Cl.
 template <int VB>
-__device__ __forceinline__ void store_values(const sca2_scan_args& p, ValueLoad<VB>& r, const float* s_beta, bf16* VT) {
+__device__ __forceinline__ void pf_values(const sca2_scan_args& p, bf16* VA, bool vec, int b, int h, int t0, int Cl,
+                                          int vb0) {
+  for (int u = threadIdx.x; u < C * (VB / 8); u += NT) {
+    const int j = u / (VB / 8), v0 = (u % (VB / 8)) * 8;
+    const bool live = j < Cl && vb0 + v0 < p.V;
+    const int64_t off = live ? tok_off(p.v, b, t0 + j, h) + vb0 + v0 : 0;
+    bf16* dst = VA + umma::kmaj(j, v0, VB);
+    if (vec) {
+      cp16(dst, reinterpret_cast<const bf16*>(p.v.ptr) + off, live);
+    } else {
+      float x[8];
 #pragma unroll
-  for (int u = 0; u < ValueLoad<VB>::NU; ++u) {
-    const int unit = threadIdx.x + u * NT, v = unit % VB, i0 = (unit / VB) * 8;
-    if (p.v_times_beta) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) r.x[u][k] *= s_beta[i0 + k];
+      for (int k = 0; k < 8; ++k) x[k] = (live && vb0 + v0 + k < p.V) ? ld_io(p.v.ptr, off + k, p.io_dtype) : 0.f;
+      st8(dst, 0, x);
     }
-    st8(VT, umma::kmaj(v, i0, C), r.x[u]);
+  }
+}
+// V' = beta v for the GDN write: scale the rows of VA in place
+template <int VB>
+__device__ __forceinline__ void scale_values(bf16* VA, const float* s_beta) {
+  for (int u = threadIdx.x; u < C * (VB / 8); u += NT) {
+    const int j = u / (VB / 8), v0 = (u % (VB / 8)) * 8;
+    bf16* q = VA + umma::kmaj(j, v0, VB);
+    const uint4 raw = *reinterpret_cast<const uint4*>(q);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float x[8];
+    const float bj = s_beta[j];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      x[2 * k] = bj * __low2float(h2[k]);
+      x[2 * k + 1] = bj * __high2float(h2[k]);
+    }
+    st8(q, 0, x);
   }
 }
 

@@ -160,6 +160,32 @@ __device__ __forceinline__ void ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Split forms: issue several loads, wait once, then take the registers.  take() passes each
+// register through an empty volatile asm that comes after the wait, so no use of a loaded
+// value can be scheduled before the wait completes.
+__device__ __forceinline__ void ld16_issue(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void ld8_issue(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void take(uint32_t* r, float* v) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    asm volatile("" : "+r"(r[i]));
+    v[i] = __uint_as_float(r[i]);
+  }
+}
+
 // 32 lanes x 8 consecutive fp32 columns -> 8 registers per thread
 __device__ __forceinline__ void ld8(uint32_t taddr, float* v) {
   uint32_t r[8];
