@@ -30,6 +30,7 @@ cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, floa
                         float* cstates, int NCS, cudaStream_t st);
 cudaError_t tc_read_faults(unsigned int* out);
 cudaError_t tc_read_faults_bwd(unsigned int* out);
+cudaError_t tc_read_faults_prep(unsigned int* out);
 // scan_tc_bwd.cu
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
@@ -110,11 +111,12 @@ const char* sca2_version(void) { return "sca2b200 0.1.0 (sm_100a)"; }
 int sca2_fault_status(uint32_t* faults) {
   if (!faults) return fail(SCA2_ERR_ARG, "null output");
   unsigned int f = 0;
-  unsigned int fb = 0;
+  unsigned int fb = 0, fp = 0;
   cudaError_t e = sca2::tc_read_faults(&f);
   if (e == cudaSuccess) e = sca2::tc_read_faults_bwd(&fb);
+  if (e == cudaSuccess) e = sca2::tc_read_faults_prep(&fp);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_fault_status");
-  *faults = f | fb;
+  *faults = f | fb | fp;
   return SCA2_OK;
 }
 

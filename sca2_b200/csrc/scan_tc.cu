@@ -187,9 +187,15 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   // the previous one runs
   CodeRegs<FL, KD> creg;
   GateRegs greg;
+  const bool prep = (flags & F_PREP) && cstates;
+  auto saved_at = [&](int cc) -> uint8_t* {
+    return reinterpret_cast<uint8_t*>(cstates + (((int64_t)b * p.H + h) * NCS + 2 * cc + 1) * KD * (int64_t)V);
+  };
   {
     const int Cl0 = min(C, p.T);
     pf_values<VB>(p, VA, flags & F_V_VEC, b, h, 0, Cl0, vb0);
+    if (prep)
+      for (int u = tid * 16; u < C * C * 2; u += NT * 16) cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(0) + u, true);
     cp_commit();
     load_code_regs<FL, KD>(p, creg, code_vec, b, h, 0, Cl0);
     if (warp == 0) load_gate_regs(p, greg, b, h, 0, Cl0);
@@ -198,9 +204,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   for (int c = 0; c < NC && ok; ++c) {
     const int t0 = c * C, Cl = min(C, p.T - t0);
     // saved for the backward in slot 2c+1: T (bf16 [i][j]) then E^T (bf16 [v][j]) per value block
-    uint8_t* saved = cstates ? reinterpret_cast<uint8_t*>(
-                                   cstates + (((int64_t)b * p.H + h) * NCS + 2 * c + 1) * KD * (int64_t)V)
-                             : nullptr;
+    uint8_t* saved = cstates ? saved_at(c) : nullptr;
     if (cstates && sown) {
       // state entering chunk c -> slot 2c of the (B,H,NCS,K,V) buffer
       const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0 + srow;
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     build_codes<FL, KD, R>(creg, cops, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
     if (tid == 0) {
-      umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
+      if (!prep) umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
       umma::gemm(tb + CO::P, sm + L::QR, sm + L::KW, R * 64, 64, KD, false);
       umma::gemm(tb + CO::P, sm + L::QR, sm + L::KWL, R * 64, 64, KD, true);
       umma::gemm(tb + CO::P, sm + L::QRL, sm + L::KW, R * 64, 64, KD, true);
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     }
     if (!(ok = wait_mma())) break;
     // ---- L = beta Gr (fp32) and P (hi + lo), masked and decayed
-    for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
+    if (!prep) for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
       const float bi = gates.beta[i] * ik, gi = gates.Gc[i];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -253,20 +257,25 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       st8_split(PB, PBL, umma::kmaj(row, j0, C), y);
       st8_split(PB, PBL, umma::kmaj(row, j0 + 8, C), y + 8);
     });
-    __syncthreads();
-    invert_unit_lower(LS, TS, WS);
-    store_T<false>(TS, TB);
+    if (!prep) {
+      __syncthreads();
+      invert_unit_lower(LS, TS, WS);
+      store_T<false>(TS, TB);
+    }
     publish_smem();
-    if (cstates && blockIdx.y == 0) copy_out(saved, TB, C * C * 2);
+    if (!prep && cstates && blockIdx.y == 0) copy_out(saved, TB, C * C * 2);
     if (tid == 0) {
       umma::gemm_t(tb + CO::UT, VA, true, TB, false, VB, C, C, false);
       umma::gemm_t(tb + CO::WK, TB, false, sm + L::ZA, true, 64, KD, C, false);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
-    if (c + 1 < NC) {  // VA is free: next chunk's values
+    if (c + 1 < NC) {  // VA and TB are free: next chunk's values (and T)
       const int t1 = t0 + C;
       pf_values<VB>(p, VA, flags & F_V_VEC, b, h, t1, min(C, p.T - t1), vb0);
+      if (prep)
+        for (int u = tid * 16; u < C * C * 2; u += NT * 16)
+          cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(c + 1) + u, true);
       cp_commit();
     }
     for_frag<VB, C>(tb + CO::UT, [&](int, int, int q, const float* x) {
@@ -420,10 +429,17 @@ static int tc_flags(const sca2_scan_args& p, const sca2_out& o) {
   return f;
 }
 
+cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, cudaStream_t st);
+
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
                         float* cstates, int NCS, cudaStream_t st) {
   const bool ph = p.flavor == SCA2_FLAVOR_PHASE;
-  const int fl = tc_flags(p, o);
+  int fl = tc_flags(p, o);
+  if (cstates && p.K == 64) {  // training: T of every chunk from the chunk-parallel kernel
+    cudaError_t e = tc_scan_prep(p, cstates, NCS, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), st);
+    if (e != cudaSuccess) return e;
+    fl |= tc::F_PREP;
+  }
 #define SCA2_TC_FWD(KD_, VB_)                                                                         \
   if (p.K == KD_ && VB == VB_)                                                                        \
     return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, st)   \

@@ -62,7 +62,10 @@ struct BwdLayout {
   static constexpr int R3 = R2 + C * 64 * 2;       // ZN (codes-b4) | (j-i) dKK (epi4-b5)
   static constexpr int R4 = R3 + C * 64 * 2;       // Sp^T, dSc^T [v][m] (prologue-b4) | (j-i) dQK (epi4-b5)
   static constexpr int R5 = R4 + 2 * VB * KD * 2;  // dY [i][v] (epi3-b4)
-  static constexpr int SC = R5 + C * VB * 2;
+  static constexpr int KH = FL == SCA2_FLAVOR_PHASE ? Mh : KD;
+  static constexpr int GRW = R5 + C * VB * 2;      // fp32 C x KH  staged dphw / dk rows of the chunk
+  static constexpr int GRQ = GRW + C * KH * 4;     // fp32 C x KH  staged dphq / dq rows
+  static constexpr int SC = GRQ + C * KH * 4;
   // scalars (floats): beta, Gc, a, w, dbeta, da, dw, rows, cols [C]; d1, dCm1, lam, wr, wi,
   // dlam, dwr, dwi [KD]; misc[8]
   static constexpr int SC_FLOATS = 9 * C + 8 * KD + 8;
@@ -114,6 +117,17 @@ __device__ __forceinline__ void pf_dO(const sca2_scan_args& p, const sca2_out& d
       for (int k = 0; k < 8; ++k) x[k] = (live && vb0 + v0 + k < p.V) ? ld_io(dO.ptr, off + k, p.io_dtype) : 0.f;
       st8(dst, 0, x);
     }
+  }
+}
+
+// the chunk's rows of an fp32 key-side gradient (accumulated into) -> G[i][m], zero rows i >= Cl
+template <int KH>
+__device__ __forceinline__ void pf_grad_rows(float* G, const sca2_tok& t, int b, int h, int t0, int Cl) {
+  const float* base = reinterpret_cast<const float*>(t.ptr);
+  for (int u = threadIdx.x; u < C * (KH / 4); u += NT) {
+    const int i = u / (KH / 4), m4 = (u % (KH / 4)) * 4;
+    const bool live = i < Cl;
+    cp16(G + i * KH + m4, base + (live ? tok_off(t, b, t0 + i, h) + m4 : 0), live);
   }
 }
 
@@ -236,10 +250,17 @@ __device__ __forceinline__ float sum16(float x) {
   return x;
 }
 
-// fp32 gradient rows: += 8 consecutive values (plain read-add-write when this CTA is the only
-// writer, else atomics)
-__device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, bool exclusive) {
-  if (exclusive && vec) {
+// fp32 gradient rows: += 8 consecutive values.  staged: the row's previous values were copied
+// into shared memory at the start of the chunk (only CTA writing them, 16-byte aligned); else
+// plain read-add-write when this CTA is the only writer, atomics otherwise.
+__device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, bool exclusive,
+                                         const float* staged) {
+  if (staged) {
+    const float4 a = reinterpret_cast<const float4*>(staged)[0], b = reinterpret_cast<const float4*>(staged)[1];
+    float4* d = reinterpret_cast<float4*>(dst);
+    d[0] = make_float4(a.x + x[0], a.y + x[1], a.z + x[2], a.w + x[3]);
+    d[1] = make_float4(b.x + x[4], b.y + x[5], b.z + x[6], b.w + x[7]);
+  } else if (exclusive && vec) {
     float4* d = reinterpret_cast<float4*>(dst);
     float4 a = d[0], b = d[1];
     a.x += x[0]; a.y += x[1]; a.z += x[2]; a.w += x[3];
@@ -302,6 +323,9 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   bf16* DSB = BF(L::R4 + VB * KD * 2);
   bf16* DQKW = BF(L::R4);
   bf16* DYA = BF(L::R5);
+  float* GRW = reinterpret_cast<float*>(sm + L::GRW);
+  float* GRQ = reinterpret_cast<float*>(sm + L::GRQ);
+  const bool gstage = excl && (flags & B_G_VEC);  // gradient rows staged in shared memory
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
@@ -388,6 +412,11 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     }
     if (tid == 0) s_misc[0] = 0.f;
     __syncthreads();  // staged copies, gates and dCm1 visible
+    if (gstage) {  // this chunk's gradient rows, needed by the finish (first group of the chunk)
+      pf_grad_rows<KH>(GRW, gr.dphw, b, h, t0, Cl);
+      pf_grad_rows<KH>(GRQ, gr.dphq, b, h, t0, Cl);
+    }
+    cp_commit();
     // Sp = d1 .* S (state layout registers) and the bf16 operands Sp^T, dSc^T [v][m]
     if (sown) {
 #pragma unroll
@@ -515,8 +544,14 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<C, C>(q);
         float dl[16], gg[16];
-        umma::ld16(umma::taddr(tb + CO::DL, 32 * sub, j0), dl);
-        umma::ld16(umma::taddr(tb + CO::G, 32 * sub, j0), gg);
+        {
+          uint32_t u[2][16];
+          umma::ld16_issue(umma::taddr(tb + CO::DL, 32 * sub, j0), u[0]);
+          umma::ld16_issue(umma::taddr(tb + CO::G, 32 * sub, j0), u[1]);
+          umma::ld_wait();
+          umma::take<16>(u[0], dl);
+          umma::take<16>(u[1], gg);
+        }
         float dkk[16], dkw[16];
         float sb = 0.f, srow_ = 0.f;
 #pragma unroll
@@ -553,11 +588,15 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     {
       const int row = frag_row<RC>(), i = row & 63;
       const bool own = owns_rows<RC>();
+      uint32_t udp[C / 32][16];
+#pragma unroll
+      for (int q = 0; q < C / 32; ++q) umma::ld16_issue(umma::taddr(tb + CO::DP, 32 * sub, frag_col0<RC, C>(q)), udp[q]);
+      umma::ld_wait();
 #pragma unroll
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<RC, C>(q);
         float dp[16];
-        umma::ld16(umma::taddr(tb + CO::DP, 32 * sub, j0), dp);
+        umma::take<16>(udp[q], dp);
         float dqk[16], dqw[16];
         float srow_ = 0.f;
 #pragma unroll
@@ -598,11 +637,15 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       const float aC = gates.a[Cl - 1];
       const float fCl = (float)Cl;
       float daC = 0.f;
+      uint32_t ud0[KD / 32][16];
+#pragma unroll
+      for (int q = 0; q < KD / 32; ++q) umma::ld16_issue(umma::taddr(tb + CO::DS0, 32 * sub, frag_col0<VB, KD>(q)), ud0[q]);
+      umma::ld_wait();
 #pragma unroll
       for (int q = 0; q < KD / 32; ++q) {
         const int m0 = frag_col0<VB, KD>(q);
         float d0[16];
-        umma::ld16(umma::taddr(tb + CO::DS0, 32 * sub, m0), d0);
+        umma::take<16>(ud0[q], d0);
         if (sown) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -633,6 +676,11 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       }
       umma::commit(mbar);
     }
+    // the gradient rows (oldest group of this chunk); later groups hold the next chunk's data
+    if (c > 0)
+      cp_wait_group<3>();
+    else
+      cp_wait_group<0>();
     if (!(ok = wait_mma())) break;
     // ================= finish =================
     const bool gvec = flags & B_G_VEC;
@@ -649,17 +697,25 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         for (int g8 = 0; g8 < 2; ++g8) {
           const int mg = 16 * half + 8 * g8;  // modes mg..mg+7: code columns mg (cos), Mh + mg (sin)
           float r1c[8], r1s[8], r2c[8], r2s[8], w12c[8], w12s[8], w3c[8], w3s[8], lwc[8], lws[8];
-          umma::ld8(umma::taddr(tb + CO::DKR1, 32 * sub, mg), r1c);
-          umma::ld8(umma::taddr(tb + CO::DKR1, 32 * sub, Mh + mg), r1s);
-          umma::ld8(umma::taddr(tb + CO::DKR2, 32 * sub, mg), r2c);
-          umma::ld8(umma::taddr(tb + CO::DKR2, 32 * sub, Mh + mg), r2s);
-          umma::ld8(umma::taddr(tb + CO::DKW12, 32 * sub, mg), w12c);
-          umma::ld8(umma::taddr(tb + CO::DKW12, 32 * sub, Mh + mg), w12s);
-          umma::ld8(umma::taddr(tb + CO::DKW3, 32 * sub, mg), w3c);
-          umma::ld8(umma::taddr(tb + CO::DKW3, 32 * sub, Mh + mg), w3s);
-          if (p.lam) {
-            umma::ld8(umma::taddr(tb + CO::DLW, 32 * sub, mg), lwc);
-            umma::ld8(umma::taddr(tb + CO::DLW, 32 * sub, Mh + mg), lws);
+          {
+            uint32_t u[10][8];
+            const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
+            umma::ld8_issue(ta + CO::DKR1 + mg, u[0]);
+            umma::ld8_issue(ta + CO::DKR1 + Mh + mg, u[1]);
+            umma::ld8_issue(ta + CO::DKR2 + mg, u[2]);
+            umma::ld8_issue(ta + CO::DKR2 + Mh + mg, u[3]);
+            umma::ld8_issue(ta + CO::DKW12 + mg, u[4]);
+            umma::ld8_issue(ta + CO::DKW12 + Mh + mg, u[5]);
+            umma::ld8_issue(ta + CO::DKW3 + mg, u[6]);
+            umma::ld8_issue(ta + CO::DKW3 + Mh + mg, u[7]);
+            umma::ld8_issue(ta + CO::DLW + mg, u[8]);
+            umma::ld8_issue(ta + CO::DLW + Mh + mg, u[9]);
+            umma::ld_wait();
+            umma::take<8>(u[0], r1c); umma::take<8>(u[1], r1s);
+            umma::take<8>(u[2], r2c); umma::take<8>(u[3], r2s);
+            umma::take<8>(u[4], w12c); umma::take<8>(u[5], w12s);
+            umma::take<8>(u[6], w3c); umma::take<8>(u[7], w3s);
+            umma::take<8>(u[8], lwc); umma::take<8>(u[9], lws);
           }
           float dl[8], dph[8];
 #pragma unroll
@@ -687,7 +743,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
               wsum += kw_w3;
               if (p.lam) dl[k] = ik * (kwc * lwc[k] + kws * lws[k]) + fi * bi * kr_r + (fi - fi_last) * wi_ * kw_w3;
             }
-            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + mg, dph, gvec, excl);
+            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + mg, dph, gvec, excl, gstage ? GRW + i * KH + mg : nullptr);
           }
           if (p.lam) {
             const float x = warp_transpose_sum<8>(dl);
@@ -699,11 +755,18 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         for (int g8 = 0; g8 < 4; ++g8) {
           const int m0 = 32 * half + 8 * g8;
           float r1[8], r2[8], w12[8], w3[8], lw[8];
-          umma::ld8(umma::taddr(tb + CO::DKR1, 32 * sub, m0), r1);
-          umma::ld8(umma::taddr(tb + CO::DKR2, 32 * sub, m0), r2);
-          umma::ld8(umma::taddr(tb + CO::DKW12, 32 * sub, m0), w12);
-          umma::ld8(umma::taddr(tb + CO::DKW3, 32 * sub, m0), w3);
-          if (p.lam) umma::ld8(umma::taddr(tb + CO::DLW, 32 * sub, m0), lw);
+          {
+            uint32_t u[5][8];
+            const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
+            umma::ld8_issue(ta + CO::DKR1 + m0, u[0]);
+            umma::ld8_issue(ta + CO::DKR2 + m0, u[1]);
+            umma::ld8_issue(ta + CO::DKW12 + m0, u[2]);
+            umma::ld8_issue(ta + CO::DKW3 + m0, u[3]);
+            umma::ld8_issue(ta + CO::DLW + m0, u[4]);
+            umma::ld_wait();
+            umma::take<8>(u[0], r1); umma::take<8>(u[1], r2); umma::take<8>(u[2], w12);
+            umma::take<8>(u[3], w3); umma::take<8>(u[4], lw);
+          }
           float dl[8], dkv[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
@@ -726,7 +789,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
               wsum += kw * w3[k];
               if (p.lam) dl[k] = ik * kw * lw[k] + fi * bi * kr * rr + (fi - fi_last) * wi_ * kw * w3[k];
             }
-            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, dkv, gvec, excl);
+            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, dkv, gvec, excl, gstage ? GRW + i * KH + m0 : nullptr);
           }
           if (p.lam) {
             const float x = warp_transpose_sum<8>(dl);
@@ -754,10 +817,17 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         for (int g8 = 0; g8 < 2; ++g8) {
           const int mg = 16 * half + 8 * g8;
           float q1c[8], q1s[8], q2c[8], q2s[8];
-          umma::ld8(umma::taddr(tb + CO::DQR1, 32 * sub, mg), q1c);
-          umma::ld8(umma::taddr(tb + CO::DQR1, 32 * sub, Mh + mg), q1s);
-          umma::ld8(umma::taddr(tb + CO::DQR2, 32 * sub, mg), q2c);
-          umma::ld8(umma::taddr(tb + CO::DQR2, 32 * sub, Mh + mg), q2s);
+          {
+            uint32_t u[4][8];
+            const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
+            umma::ld8_issue(ta + CO::DQR1 + mg, u[0]);
+            umma::ld8_issue(ta + CO::DQR1 + Mh + mg, u[1]);
+            umma::ld8_issue(ta + CO::DQR2 + mg, u[2]);
+            umma::ld8_issue(ta + CO::DQR2 + Mh + mg, u[3]);
+            umma::ld_wait();
+            umma::take<8>(u[0], q1c); umma::take<8>(u[1], q1s);
+            umma::take<8>(u[2], q2c); umma::take<8>(u[3], q2s);
+          }
           float pq[8], dwr[8], dwi[8], dl[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
@@ -797,7 +867,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             float y[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) y[k] = pq[k] + s[k];
-            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + mg, y, gvec, excl);
+            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + mg, y, gvec, excl, gstage ? GRQ + i * KH + mg : nullptr);
           }
           __syncthreads();
           {
@@ -816,8 +886,14 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         for (int g8 = 0; g8 < 4; ++g8) {
           const int m0 = 32 * half + 8 * g8;
           float q1[8], q2[8];
-          umma::ld8(umma::taddr(tb + CO::DQR1, 32 * sub, m0), q1);
-          umma::ld8(umma::taddr(tb + CO::DQR2, 32 * sub, m0), q2);
+          {
+            uint32_t u[2][8];
+            const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
+            umma::ld8_issue(ta + CO::DQR1 + m0, u[0]);
+            umma::ld8_issue(ta + CO::DQR2 + m0, u[1]);
+            umma::ld_wait();
+            umma::take<8>(u[0], q1); umma::take<8>(u[1], q2);
+          }
           float dl[8], dqv[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
@@ -836,7 +912,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
               dl[k] = -fi * gq;
               asum += gq;
             }
-            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, dqv, gvec, excl);
+            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, dqv, gvec, excl, gstage ? GRQ + i * KH + m0 : nullptr);
           }
           if (p.lam) {
             const float x = warp_transpose_sum<8>(dl);

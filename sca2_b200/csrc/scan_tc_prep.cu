@@ -1,0 +1,175 @@
+// Chunk-parallel preparation for the tensor-core training scan (sm_100a): for every 64-token
+// chunk of every (b, h), the inverse
+//
+//     T = (I + diag(beta) Gr)^{-1},   Gr = (kr kw^T / kappa) .* Dg, strictly lower
+//
+// (the delta-rule solve of the chunk, independent of the state) is computed once and written,
+// bf16 in the tcgen05 operand layout, to slot 2c+1 of the saved-state buffer.  The forward
+// and the backward copy it from there instead of inverting inside their sequential chunk walk.
+//
+// One CTA (8 warps) per chunk and about 60 KB of shared memory, so several chunks run per SM:
+// codes from the phases (keys), G = KR KW^T on the tensor cores (bounded mbarrier wait), the
+// fp32 blocked inversion of the unit lower-triangular matrix, a 16-byte copy out.
+#include "tc_common.cuh"
+
+namespace sca2 {
+namespace tc {
+
+// bit 0: a bounded mbarrier wait of the preparation kernel timed out
+__device__ unsigned int g_fault_prep;
+
+template <int KD>
+struct PrepLayout {
+  static constexpr int al(int x) { return (x + 1023) & ~1023; }
+  static constexpr int KR = 0;                     // C x KD  kr [i][m]
+  static constexpr int KW = KR + al(C * KD * 2);   // C x KD  kw [i][m]
+  static constexpr int TB = KW + al(C * KD * 2);   // C x C   T  [i][j]
+  static constexpr int LS = TB + al(C * C * 2);    // fp32 C x LDF
+  static constexpr int TS = LS + al(C * LDF * 4);  // fp32 C x LDF
+  static constexpr int WS = TS + al(C * LDF * 4);  // fp32 3 x 256
+  static constexpr int SC = WS + al(3 * 256 * 4);  // beta, Gc, a, w [C] + lam [KD]
+  static constexpr int MBAR = SC + al((4 * C + KD) * 4);
+  static constexpr int TOTAL = MBAR + 64;
+};
+
+template <int FL, int KD>
+__global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec) {
+  using L = PrepLayout<KD>;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  const int t0 = c * C, Cl = min(C, p.T - t0);
+  const bool has_g = p.g.ptr != nullptr;
+  constexpr int KH = FL == SCA2_FLAVOR_PHASE ? KD / 2 : KD;
+  const float ik = FL == SCA2_FLAVOR_PHASE ? 1.f / (float)(KD / 2) : 1.f;
+  float* sc = reinterpret_cast<float*>(sm + L::SC);
+  Gates gates{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  float* s_lam = sc + 4 * C;
+  bf16* KR = reinterpret_cast<bf16*>(sm + L::KR);
+  bf16* KW = reinterpret_cast<bf16*>(sm + L::KW);
+  bf16* TB = reinterpret_cast<bf16*>(sm + L::TB);
+  float* LS = reinterpret_cast<float*>(sm + L::LS);
+  float* TS = reinterpret_cast<float*>(sm + L::TS);
+  float* WS = reinterpret_cast<float*>(sm + L::WS);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
+
+  for (int m = tid; m < KD; m += NT) s_lam[m] = p.lam ? p.lam[h * KH + (m % KH)] : 0.f;
+  if (warp == 0) {
+    GateRegs gr;
+    load_gate_regs(p, gr, b, h, t0, Cl);
+    gates_from_regs(gr, gates, Cl);
+  }
+  if (tid == 0) {
+    umma::mbar_init(mbar, 1);
+    umma::fence_mbar_init();
+  }
+  if (warp == 0) umma::tmem_alloc(s_tmem, 64);
+  CodeRegs<FL, KD> cr;
+  load_code_regs<FL, KD>(p, cr, vec != 0, b, h, t0, Cl);
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tb = *s_tmem;
+  // ---- codes kr, kw (bf16, [i][m])
+  if constexpr (FL == SCA2_FLAVOR_PHASE) {
+    constexpr int Mh = KD / 2;
+    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    const float fi = (float)i;
+    float kc[8], ks[8], wc[8], ws[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float s = 0.f, co = 0.f;
+      if (i < Cl) sincos_big(cr.w[0][k], &s, &co);
+      const float l = s_lam[m0 + k];
+      const float ell = __expf(-l * fi), elli = __expf(l * fi);
+      kc[k] = co * ell; ks[k] = s * ell; wc[k] = co * elli; ws[k] = s * elli;
+    }
+    st8(KR, umma::kmaj(i, m0, KD), kc);
+    st8(KR, umma::kmaj(i, Mh + m0, KD), ks);
+    st8(KW, umma::kmaj(i, m0, KD), wc);
+    st8(KW, umma::kmaj(i, Mh + m0, KD), ws);
+  } else {
+    constexpr int MB = KD / 8;
+#pragma unroll
+    for (int u = 0; u < CodeRegs<FL, KD>::NU; ++u) {
+      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      const float fi = (float)i;
+      float kc[8], wc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float l = s_lam[m0 + k];
+        kc[k] = cr.w[u][k] * __expf(-l * fi);
+        wc[k] = cr.w[u][k] * __expf(l * fi);
+      }
+      st8(KR, umma::kmaj(i, m0, KD), kc);
+      st8(KW, umma::kmaj(i, m0, KD), wc);
+    }
+  }
+  publish_smem();
+  if (tid == 0) {
+    umma::gemm(tb, KR, KW, 64, 64, KD, false);
+    umma::commit(mbar);
+  }
+  const bool ok = umma::mbar_wait(mbar, 0);
+  __syncthreads();
+  umma::fence_after_sync();
+  if (ok) {
+    // L = beta Gr (fp32, strictly lower), then T
+    for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {
+      const float bi = gates.beta[i] * ik, gi = gates.Gc[i];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int jj = j0 + j;
+        const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
+        LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
+      }
+    });
+    __syncthreads();
+    invert_unit_lower(LS, TS, WS);
+    store_T<false>(TS, TB);
+    __syncthreads();
+    uint8_t* dst = reinterpret_cast<uint8_t*>(cstates + (((int64_t)b * p.H + h) * NCS + 2 * c + 1) * KD * (int64_t)p.V);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(TB);
+    for (int u = tid * 16; u < C * C * 2; u += NT * 16)
+      *reinterpret_cast<uint4*>(dst + u) = *reinterpret_cast<const uint4*>(src + u);
+  } else {
+    if (tid == 0) atomicOr(&g_fault_prep, 1u);
+    umma::mbar_wait(mbar, 0);  // bounded: let the MMA drain before the columns are freed
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tb, 64);
+}
+
+}  // namespace tc
+
+// T of every chunk into slot 2c+1 of cstates (K = 64); vec: 16-byte loads of the phases / keys
+cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, cudaStream_t st) {
+  const int NC = (p.T + tc::C - 1) / tc::C;
+  if (NC == 0) return cudaSuccess;
+  const int smem = tc::PrepLayout<64>::TOTAL;
+  dim3 grid(NC, p.B * p.H);
+  if (p.flavor == SCA2_FLAVOR_PHASE) {
+    auto k = tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec);
+  } else {
+    auto k = tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec);
+  }
+  return cudaGetLastError();
+}
+
+// read and clear the preparation kernel's device fault word (synchronous)
+cudaError_t tc_read_faults_prep(unsigned int* out) {
+  unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(out, tc::g_fault_prep, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(tc::g_fault_prep, &zero, sizeof(unsigned int));
+}
+
+}  // namespace sca2

@@ -15,7 +15,8 @@ constexpr int LDF = C + 1;
 using bf16 = __nv_bfloat16;
 
 // launch flags (host-computed, uniform)
-enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8 };
+// F_PREP: T of every chunk was written to slot 2c+1 by the preparation kernel
+enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8, F_PREP = 16 };
 
 // ---- bf16 vector stores -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -104,6 +105,9 @@ __device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// wait until at most N of this thread's most recent commit groups are still pending
+template <int N>
+__device__ __forceinline__ void cp_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ---- warp transpose-reduce --------------------------------------------------------------------
 // Every lane holds N values (N = 8 or 16); returns, in lane l, the sum over all 32 lanes of value
