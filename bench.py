@@ -13,7 +13,9 @@ Workload (one step = one pass of the hot path over one batch, inputs resident in
 
 Printed: one JSON line (rank 0) with the contract keys plus roofline (dominant kernel),
 cpu_baseline (numpy oracle on the host cores), e2e (public API, host buffers), clocks,
-gpu_launches and a decode block (batch 256, H=16, K=V=128, 512 steps after a 4096 prefill).
+gpu_launches, a decode block (batch 256, H=16, K=V=128, 512 steps after a 4096 prefill) and an
+sp_prefill block (one 131072-token sequence, H=16, d_head=64, split over the ranks: slab maps
+all-gathered over NCCL, sequence-parallel prefill).
 """
 from __future__ import annotations
 
@@ -32,6 +34,7 @@ sys.path.insert(0, ROOT)
 
 WORK = dict(B=8, T=4096, H=16, Mh=32, V=64)
 DECODE = dict(B=256, T=4096, H=16, Mh=64, V=128, steps=512)
+SP = dict(B=1, T=131072, H=16, Mh=32, V=64)  # one long sequence, split over the ranks
 # Algorithmic bytes per token per head (inputs read + outputs written once):
 #   fwd: phi, psi fp32 (2*Mh*4) + v bf16 (V*2) + beta (4) + o bf16 (2*V*2)
 #   bwd: dO bf16 (2*V*2) + inputs re-read (2*Mh*4 + V*2 + 4) + dphi, dpsi fp32 (2*Mh*4) + dv bf16 (V*2) + dbeta (4)
@@ -241,8 +244,12 @@ def run_gpu(args, rank, world, local_rank, dist):
         del plan
         torch.cuda.empty_cache()
         decode = run_decode(torch, ops, dev, rank, world, dist)
+    sp = None
+    if not args.no_sp:
+        torch.cuda.empty_cache()
+        sp = run_sp(torch, dev, rank, world, dist)
     return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
-                decode=decode)
+                decode=decode, sp=sp)
 
 
 def run_decode(torch, ops, dev, rank, world, dist):
@@ -290,6 +297,58 @@ def run_decode(torch, ops, dev, rank, world, dist):
             "achieved_gbs": gbs, "bytes_per_step": 2 * state_bytes + io_bytes}
 
 
+def run_sp(torch, dev, rank, world, dist, reps=3):
+    """Sequence-parallel prefill of one 131072-token sequence (bf16 v, fp32 state): every rank
+    holds T / N tokens; slab maps all-gathered over NCCL; time = max over ranks."""
+    from sca2_b200.sp import sp_phase_prefill
+    S = SP
+    T = S["T"] // world
+    x = make_inputs(torch, 555 + rank, dev, S["B"], T, S["H"], S["Mh"], S["V"], torch.bfloat16, with_grad_out=False)
+    # phases continue the positions of the previous ranks (omega * p with p = rank * T + t)
+    om = math.pi * 1e4 ** (-torch.arange(S["Mh"], device=dev, dtype=torch.float32) / (S["Mh"] - 1))
+    x["phw"] += (rank * T) * om
+    x["phq"] += (rank * T) * om
+    args = (x["phw"], x["phq"], x["v"], x["beta"], None, x["lam"], x["wr"], x["wi"])
+    for _ in range(2):
+        sp_phase_prefill(*args)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        sp_phase_prefill(*args)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": S["B"] * S["T"] / (ms / 1e3), "unit": "tokens/s", "ms_per_prefill": ms,
+            "config": {"batch": S["B"], "seq_len": S["T"], "tokens_per_rank": T, "H": S["H"], "d_head": 2 * S["Mh"],
+                       "ranks": world, "fwd_only": True}}
+
+
+def _quiet_stdout(fn):
+    """Run fn with file descriptor 1 on /dev/null (C-level prints included)."""
+    import ctypes
+    sys.stdout.flush()
+    saved, null = os.dup(1), os.open(os.devnull, os.O_WRONLY)
+    os.dup2(null, 1)
+    try:
+        return fn()
+    finally:
+        try:
+            ctypes.CDLL(None).fflush(None)
+        except OSError:
+            pass
+        os.dup2(saved, 1)
+        os.close(saved)
+        os.close(null)
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -308,6 +367,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sp", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
@@ -359,8 +419,14 @@ def main():
     dist = None
     if world > 1:
         import datetime
+        import torch
         import torch.distributed as dist_
-        dist_.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+        def setup():  # NCCL prints a banner on the first communicator; keep stdout to the JSON line
+            dist_.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                     device_id=torch.device("cuda", local_rank))
+            dist_.barrier()
+        _quiet_stdout(setup)
         dist = dist_
     try:
         r = run_gpu(args, rank, world, local_rank, dist)
@@ -403,6 +469,7 @@ def main():
                   "achieved_tflops": 3 * 2 * mac / (r["ms_step"] * 1e-3) / 1e12, "peak_tflops": tfl},
         "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"], "gpu_launches": 2 * args.steps,
         "decode": r["decode"],
+        "sp_prefill": r["sp"],
     }
     print(json.dumps(line))
 
