@@ -683,6 +683,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       cp_wait_group<0>();
     if (!(ok = wait_mma())) break;
     // ================= finish =================
+    // (the loops over mode groups below are deliberately not unrolled: the unrolled bodies
+    //  overflow the instruction cache and cost more than the loop overhead)
     const bool gvec = flags & B_G_VEC;
     // ---- key side (rows i of the M = 64 accumulators)
     {
@@ -693,7 +695,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       float bsum = 0.f, wsum = 0.f;
       float* dk = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
       if constexpr (FL == SCA2_FLAVOR_PHASE) {
-#pragma unroll
+#pragma unroll 1
         for (int g8 = 0; g8 < 2; ++g8) {
           const int mg = 16 * half + 8 * g8;  // modes mg..mg+7: code columns mg (cos), Mh + mg (sin)
           float r1c[8], r1s[8], r2c[8], r2s[8], w12c[8], w12s[8], w3c[8], w3s[8], lwc[8], lws[8];
@@ -751,7 +753,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           }
         }
       } else {
-#pragma unroll
+#pragma unroll 1
         for (int g8 = 0; g8 < 4; ++g8) {
           const int m0 = 32 * half + 8 * g8;
           float r1[8], r2[8], w12[8], w3[8], lw[8];
@@ -813,7 +815,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       float asum = 0.f;
       float* dq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
       if constexpr (FL == SCA2_FLAVOR_PHASE) {
-#pragma unroll
+#pragma unroll 1
         for (int g8 = 0; g8 < 2; ++g8) {
           const int mg = 16 * half + 8 * g8;
           float q1c[8], q1s[8], q2c[8], q2s[8];
@@ -882,7 +884,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           }
         }
       } else {
-#pragma unroll
+#pragma unroll 1
         for (int g8 = 0; g8 < 4; ++g8) {
           const int m0 = 32 * half + 8 * g8;
           float q1[8], q2[8];
