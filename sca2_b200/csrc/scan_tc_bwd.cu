@@ -73,7 +73,9 @@ struct BwdLayout {
   static constexpr int TOTAL = MBAR + 64;
   static_assert(RC * 64 * 2 >= RC * KD * 2, "R1 holds QRA");
   static_assert(2 * VB * KD * 2 >= RC * C * 2, "R4 holds the weighted dQK");
-  static_assert(C * 64 * 2 >= C * Mh * 4, "R2 holds PQ");
+  static_assert(C * 64 * 2 >= C * Mh * 4, "R2, R3 and R5 each hold a C x Mh fp32 staging array (phase)");
+  static_assert(2 * C * 64 * 2 >= C * KD * 4 && 2 * VB * KD * 2 >= C * KD * 4,
+                "R2..R3 and R4 hold a C x K fp32 staging array (key)");
 };
 
 // TMEM columns (fp32).  Lifetimes: batch 1 writes G, P, DS0, DQR2, DKW3, DE; DY reuses P's
@@ -685,125 +687,116 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     // ================= finish =================
     // (the loops over mode groups below are deliberately not unrolled: the unrolled bodies
     //  overflow the instruction cache and cost more than the loop overhead)
-    const bool gvec = flags & B_G_VEC;
-    // ---- key side (rows i of the M = 64 accumulators)
+    // Per-element key / query gradients go to shared memory first (PK, PQ0 | PQ1) and are
+    // written out once, coalesced, after one barrier.
+    float* PK = FL == SCA2_FLAVOR_PHASE ? reinterpret_cast<float*>(sm + L::R5) : reinterpret_cast<float*>(sm + L::R4);
+    float* PQ0 = reinterpret_cast<float*>(sm + L::R2);
+    float* PQ1 = reinterpret_cast<float*>(sm + L::R3);  // phase: second read column's part
+    // ---- key side: the 16 rows of each sub-partition over all 32 lanes (2 rows x 2 modes of an
+    // 8-column group per thread)
     {
-      const int i = frag_row<C>();
-      const bool own = owns_rows<C>() && i < Cl;
-      const float fi = (float)i;
-      const float bi = gates.beta[i], aik = gates.a[i] * ik, wi_ = gates.w[i];
-      float bsum = 0.f, wsum = 0.f;
-      float* dk = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
-      if constexpr (FL == SCA2_FLAVOR_PHASE) {
+      const int r0 = lane >> 2, qq = lane & 3;
+      const int rows[2] = {16 * sub + r0, 16 * sub + r0 + 8};
+      float bsum[2] = {0.f, 0.f}, wsum[2] = {0.f, 0.f};
+      constexpr int NG = FL == SCA2_FLAVOR_PHASE ? 2 : 4;  // groups of 8 modes (dims) per warp
 #pragma unroll 1
-        for (int g8 = 0; g8 < 2; ++g8) {
-          const int mg = 16 * half + 8 * g8;  // modes mg..mg+7: code columns mg (cos), Mh + mg (sin)
-          float r1c[8], r1s[8], r2c[8], r2s[8], w12c[8], w12s[8], w3c[8], w3s[8], lwc[8], lws[8];
-          {
-            uint32_t u[10][8];
-            const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
-            umma::ld8_issue(ta + CO::DKR1 + mg, u[0]);
-            umma::ld8_issue(ta + CO::DKR1 + Mh + mg, u[1]);
-            umma::ld8_issue(ta + CO::DKR2 + mg, u[2]);
-            umma::ld8_issue(ta + CO::DKR2 + Mh + mg, u[3]);
-            umma::ld8_issue(ta + CO::DKW12 + mg, u[4]);
-            umma::ld8_issue(ta + CO::DKW12 + Mh + mg, u[5]);
-            umma::ld8_issue(ta + CO::DKW3 + mg, u[6]);
-            umma::ld8_issue(ta + CO::DKW3 + Mh + mg, u[7]);
-            umma::ld8_issue(ta + CO::DLW + mg, u[8]);
-            umma::ld8_issue(ta + CO::DLW + Mh + mg, u[9]);
-            umma::ld_wait();
-            umma::take<8>(u[0], r1c); umma::take<8>(u[1], r1s);
-            umma::take<8>(u[2], r2c); umma::take<8>(u[3], r2s);
-            umma::take<8>(u[4], w12c); umma::take<8>(u[5], w12s);
-            umma::take<8>(u[6], w3c); umma::take<8>(u[7], w3s);
-            umma::take<8>(u[8], lwc); umma::take<8>(u[9], lws);
-          }
-          float dl[8], dph[8];
+      for (int g8 = 0; g8 < NG; ++g8) {
+        const int mg = FL == SCA2_FLAVOR_PHASE ? 16 * half + 8 * g8 : 32 * half + 8 * g8;
+        const int m0 = mg + 2 * qq;
+        constexpr int NP = FL == SCA2_FLAVOR_PHASE ? 2 : 1;  // code columns per mode (cos, sin)
+        float a1[NP][4], a2[NP][4], w12[NP][4], w3[NP][4], lw[NP][4];
+        {
+          uint32_t u[5 * NP][4];
+          const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            dl[k] = 0.f;
-            dph[k] = 0.f;
+          for (int pp = 0; pp < NP; ++pp) {
+            const int col = mg + pp * Mh;
+            umma::ld4_rows16_issue(ta + CO::DKR1 + col, u[5 * pp + 0]);
+            umma::ld4_rows16_issue(ta + CO::DKR2 + col, u[5 * pp + 1]);
+            umma::ld4_rows16_issue(ta + CO::DKW12 + col, u[5 * pp + 2]);
+            umma::ld4_rows16_issue(ta + CO::DKW3 + col, u[5 * pp + 3]);
+            umma::ld4_rows16_issue(ta + CO::DLW + col, u[5 * pp + 4]);
           }
-          if (own) {
-            const float* cw = cache + (0 * C + i) * Mh + mg;
-            const float* sw = cache + (1 * C + i) * Mh + mg;
+          umma::ld_wait();
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int m = mg + k;
-              const float c = cw[k], s = sw[k];
-              const float l = s_lam[m];
-              const float ell = __expf(-l * fi), elli = __expf(l * fi);
-              const float krc = c * ell, krs = s * ell, kwc = c * elli, kws = s * elli;
-              const float rc = aik * r2c[k], rs = aik * r2s[k];
-              const float dkrc = r1c[k] * ik - bi * rc, dkrs = r1s[k] * ik - bi * rs;
-              const float dkwc = w12c[k] * ik + wi_ * w3c[k], dkws = w12s[k] * ik + wi_ * w3s[k];
-              const float dkc = dkrc * ell + dkwc * elli, dks = dkrs * ell + dkws * elli;
-              dph[k] = -s * dkc + c * dks;
-              const float kr_r = krc * rc + krs * rs, kw_w3 = kwc * w3c[k] + kws * w3s[k];
-              bsum += kr_r;
-              wsum += kw_w3;
-              if (p.lam) dl[k] = ik * (kwc * lwc[k] + kws * lws[k]) + fi * bi * kr_r + (fi - fi_last) * wi_ * kw_w3;
-            }
-            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + mg, dph, gvec, excl, gstage ? GRW + i * KH + mg : nullptr);
-          }
-          if (p.lam) {
-            const float x = warp_transpose_sum<8>(dl);
-            if ((lane & 3) == 0) atomicAdd(&s_dlam[mg + red_index<8>(lane)], x);
+          for (int pp = 0; pp < NP; ++pp) {
+            umma::take<4>(u[5 * pp + 0], a1[pp]);
+            umma::take<4>(u[5 * pp + 1], a2[pp]);
+            umma::take<4>(u[5 * pp + 2], w12[pp]);
+            umma::take<4>(u[5 * pp + 3], w3[pp]);
+            umma::take<4>(u[5 * pp + 4], lw[pp]);
           }
         }
-      } else {
-#pragma unroll 1
-        for (int g8 = 0; g8 < 4; ++g8) {
-          const int m0 = 32 * half + 8 * g8;
-          float r1[8], r2[8], w12[8], w3[8], lw[8];
-          {
-            uint32_t u[5][8];
-            const uint32_t ta = umma::taddr(tb, 32 * sub, 0);
-            umma::ld8_issue(ta + CO::DKR1 + m0, u[0]);
-            umma::ld8_issue(ta + CO::DKR2 + m0, u[1]);
-            umma::ld8_issue(ta + CO::DKW12 + m0, u[2]);
-            umma::ld8_issue(ta + CO::DKW3 + m0, u[3]);
-            umma::ld8_issue(ta + CO::DLW + m0, u[4]);
-            umma::ld_wait();
-            umma::take<8>(u[0], r1); umma::take<8>(u[1], r2); umma::take<8>(u[2], w12);
-            umma::take<8>(u[3], w3); umma::take<8>(u[4], lw);
-          }
-          float dl[8], dkv[8];
+        float dl[2] = {0.f, 0.f};
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            dl[k] = 0.f;
-            dkv[k] = 0.f;
-          }
-          if (own) {
-            const float* kp = cache + (0 * C + i) * KD + m0;
+        for (int ri = 0; ri < 2; ++ri) {
+          const int i = rows[ri];
+          const bool own = i < Cl;
+          const float fi = (float)i, bi = gates.beta[i], aik = gates.a[i] * ik, wi_ = gates.w[i];
+          float dv2[2];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int m = m0 + k;
-              const float kk = kp[k];
-              const float l = s_lam[m];
-              const float ell = __expf(-l * fi), elli = __expf(l * fi);
+          for (int mi = 0; mi < 2; ++mi) {
+            const int e = 2 * ri + mi, m = m0 + mi;
+            const float l = s_lam[m];
+            const float ell = __expf(-l * fi), elli = __expf(l * fi);
+            float dvv = 0.f;
+            if constexpr (FL == SCA2_FLAVOR_PHASE) {
+              const float c = cache[(0 * C + i) * Mh + m], s = cache[(1 * C + i) * Mh + m];
+              const float krc = c * ell, krs = s * ell, kwc = c * elli, kws = s * elli;
+              const float rc = aik * a2[0][e], rs = aik * a2[1][e];
+              const float dkrc = a1[0][e] * ik - bi * rc, dkrs = a1[1][e] * ik - bi * rs;
+              const float dkwc = w12[0][e] * ik + wi_ * w3[0][e], dkws = w12[1][e] * ik + wi_ * w3[1][e];
+              const float dkc = dkrc * ell + dkwc * elli, dks = dkrs * ell + dkws * elli;
+              dvv = -s * dkc + c * dks;
+              const float kr_r = krc * rc + krs * rs, kw_w3 = kwc * w3[0][e] + kws * w3[1][e];
+              if (own) {
+                bsum[ri] += kr_r;
+                wsum[ri] += kw_w3;
+                if (p.lam) dl[mi] += ik * (kwc * lw[0][e] + kws * lw[1][e]) + fi * bi * kr_r + (fi - fi_last) * wi_ * kw_w3;
+              }
+            } else {
+              const float kk = cache[(0 * C + i) * KD + m];
               const float kr = kk * ell, kw = kk * elli;
-              const float rr = aik * r2[k];
-              const float dkr = r1[k] * ik - bi * rr, dkw = w12[k] * ik + wi_ * w3[k];
-              dkv[k] = dkr * ell + dkw * elli;
-              bsum += kr * rr;
-              wsum += kw * w3[k];
-              if (p.lam) dl[k] = ik * kw * lw[k] + fi * bi * kr * rr + (fi - fi_last) * wi_ * kw * w3[k];
+              const float rr = aik * a2[0][e];
+              const float dkr = a1[0][e] * ik - bi * rr, dkw = w12[0][e] * ik + wi_ * w3[0][e];
+              dvv = dkr * ell + dkw * elli;
+              if (own) {
+                bsum[ri] += kr * rr;
+                wsum[ri] += kw * w3[0][e];
+                if (p.lam) dl[mi] += ik * kw * lw[0][e] + fi * bi * kr * rr + (fi - fi_last) * wi_ * kw * w3[0][e];
+              }
             }
-            acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, dkv, gvec, excl, gstage ? GRW + i * KH + m0 : nullptr);
+            dv2[mi] = own ? dvv : 0.f;
           }
-          if (p.lam) {
-            const float x = warp_transpose_sum<8>(dl);
-            if ((lane & 3) == 0) atomicAdd(&s_dlam[m0 + red_index<8>(lane)], x);
+          *reinterpret_cast<float2*>(PK + i * KH + m0) = make_float2(dv2[0], dv2[1]);
+        }
+        if (p.lam) {  // sum over the 16 rows: lanes with the same column pair
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            dl[0] += __shfl_xor_sync(0xffffffffu, dl[0], o);
+            dl[1] += __shfl_xor_sync(0xffffffffu, dl[1], o);
+          }
+          if (r0 == 0) {
+            atomicAdd(&s_dlam[m0], dl[0]);
+            atomicAdd(&s_dlam[m0 + 1], dl[1]);
           }
         }
       }
-      if (own) {
-        atomicAdd(&s_dbeta[i], -bsum);
-        if (has_g) {
-          atomicAdd(&s_da[i], -bi * bsum);
-          atomicAdd(&s_dw[i], wi_ * wsum);
+      // row sums over this warp's modes: the four lanes of a row group
+#pragma unroll
+      for (int ri = 0; ri < 2; ++ri) {
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+          bsum[ri] += __shfl_xor_sync(0xffffffffu, bsum[ri], o);
+          if (has_g) wsum[ri] += __shfl_xor_sync(0xffffffffu, wsum[ri], o);
+        }
+        const int i = rows[ri];
+        if (qq == 0 && i < Cl) {
+          atomicAdd(&s_dbeta[i], -bsum[ri]);
+          if (has_g) {
+            atomicAdd(&s_da[i], -gates.beta[i] * bsum[ri]);
+            atomicAdd(&s_dw[i], gates.w[i] * wsum[ri]);
+          }
         }
       }
     }
@@ -813,7 +806,6 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       const bool own = owns_rows<RC>() && i < Cl;
       const float fi = (float)i, aik = gates.a[i] * ik;
       float asum = 0.f;
-      float* dq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
       if constexpr (FL == SCA2_FLAVOR_PHASE) {
 #pragma unroll 1
         for (int g8 = 0; g8 < 2; ++g8) {
@@ -857,30 +849,19 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
               asum += gq;
             }
           }
-          // combine the two read columns of (i, m): r = 1 rows hand their part to r = 0 rows
-          if (own && r == 1) {
-            float4* d = reinterpret_cast<float4*>(PQ + i * Mh + mg);
+          // each read column's part of d(psi) -> PQ0 / PQ1 (zero rows beyond the chunk)
+          {
+            float4* d = reinterpret_cast<float4*>((r ? PQ1 : PQ0) + i * Mh + mg);
             d[0] = make_float4(pq[0], pq[1], pq[2], pq[3]);
             d[1] = make_float4(pq[4], pq[5], pq[6], pq[7]);
           }
-          __syncthreads();
-          if (own && r == 0) {
-            const float* s = PQ + i * Mh + mg;
-            float y[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) y[k] = pq[k] + s[k];
-            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + mg, y, gvec, excl, gstage ? GRQ + i * KH + mg : nullptr);
-          }
-          __syncthreads();
-          {
-            float x = warp_transpose_sum<8>(dwr);
-            if ((lane & 3) == 0) atomicAdd(&s_dwr[mg + red_index<8>(lane)], x);
-            x = warp_transpose_sum<8>(dwi);
-            if ((lane & 3) == 0) atomicAdd(&s_dwi[mg + red_index<8>(lane)], x);
-            if (p.lam) {
-              x = warp_transpose_sum<8>(dl);
-              if ((lane & 3) == 0) atomicAdd(&s_dlam[mg + red_index<8>(lane)], x);
-            }
+          float x = warp_transpose_sum<8>(dwr);
+          if ((lane & 3) == 0) atomicAdd(&s_dwr[mg + red_index<8>(lane)], x);
+          x = warp_transpose_sum<8>(dwi);
+          if ((lane & 3) == 0) atomicAdd(&s_dwi[mg + red_index<8>(lane)], x);
+          if (p.lam) {
+            x = warp_transpose_sum<8>(dl);
+            if ((lane & 3) == 0) atomicAdd(&s_dlam[mg + red_index<8>(lane)], x);
           }
         }
       } else {
@@ -914,7 +895,11 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
               dl[k] = -fi * gq;
               asum += gq;
             }
-            acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, dqv, gvec, excl, gstage ? GRQ + i * KH + m0 : nullptr);
+          }
+          if (owns_rows<RC>()) {
+            float4* d = reinterpret_cast<float4*>(PQ0 + i * KD + m0);
+            d[0] = make_float4(dqv[0], dqv[1], dqv[2], dqv[3]);
+            d[1] = make_float4(dqv[4], dqv[5], dqv[6], dqv[7]);
           }
           if (p.lam) {
             const float x = warp_transpose_sum<8>(dl);
@@ -925,6 +910,24 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       if (own && has_g) atomicAdd(&s_da[i], asum);
     }
     __syncthreads();
+    // ---- key-side gradients out: 8 consecutive modes (dims) of one token per unit, coalesced
+    {
+      const bool gvec = flags & B_G_VEC;
+      float* dk = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
+      float* dq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
+      for (int u = tid; u < C * (KH / 8); u += NT) {
+        const int i = u / (KH / 8), m0 = (u % (KH / 8)) * 8;
+        if (i >= Cl) continue;
+        float y[8], z[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          y[k] = PK[i * KH + m0 + k];
+          z[k] = PQ0[i * KH + m0 + k] + (FL == SCA2_FLAVOR_PHASE ? PQ1[i * KH + m0 + k] : 0.f);
+        }
+        acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, y, gvec, excl, gstage ? GRW + i * KH + m0 : nullptr);
+        acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, z, gvec, excl, gstage ? GRQ + i * KH + m0 : nullptr);
+      }
+    }
     // ---- per-token beta and decay gradients
     if (tid < 32) {
       float dGv[2], dwv[2];

@@ -176,6 +176,14 @@ __device__ __forceinline__ void ld8_issue(uint32_t taddr, uint32_t* r) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
+// 16 lanes x 8 columns (the 16 rows of an M = 64 accumulator in one sub-partition) spread over
+// all 32 threads: thread t gets rows t/4 and t/4 + 8, columns 2(t%4) and 2(t%4) + 1, as
+// r = {(t/4, 2(t%4)), (t/4, 2(t%4)+1), (t/4+8, 2(t%4)), (t/4+8, 2(t%4)+1)} (measured layout)
+__device__ __forceinline__ void ld4_rows16_issue(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
 __device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void take(uint32_t* r, float* v) {
