@@ -204,7 +204,9 @@ def test_key_vs_oracle(shape, dtype):
 
 
 @pytest.mark.parametrize("case", [(3, 5, 2, 16, 24, True, True, True), (2, 4, 4, 64, 128, True, False, True),
-                                  (1, 3, 1, 6, 5, False, True, False)])
+                                  (1, 3, 1, 6, 5, False, True, False),
+                                  # persistent kernel, more (b, h) items than SMs (K = V = 128 and 64)
+                                  (20, 3, 16, 64, 128, True, True, True), (10, 3, 16, 32, 64, True, False, True)])
 def test_phase_step_vs_oracle(case):
     ops = _ops()
     B, T, H, Mh, V, be, g, lam = case
@@ -323,3 +325,24 @@ def test_full_size_key_slices():
         oo = o[b:b + 1, :, h:h + 1]
         assert relerr(oo, ro) < TOL_BF16_ABS and cosine(oo, ro) > TOL_BF16_COS
         assert relerr(S[b:b + 1, h:h + 1], rS) < TOL_BF16_ABS
+
+
+@pytest.mark.parametrize("shape", [(12, 3, 16, 64, 64), (3, 4, 2, 128, 128)])
+def test_key_step_vs_oracle(shape):
+    """GDN decode steps (persistent kernel for K = V = 64 / 128) against the oracle's scan."""
+    ops = _ops()
+    B, T, H, K, V = shape
+    rng = np.random.default_rng(B * K + T)
+    nrm = lambda x: x / np.linalg.norm(x, axis=-1, keepdims=True)
+    q, k = nrm(rng.standard_normal((B, T, H, K))), nrm(rng.standard_normal((B, T, H, K)))
+    v = rng.standard_normal((B, T, H, V))
+    g = -np.log1p(np.exp(rng.standard_normal((B, T, H))))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((B, T, H))))
+    S0 = 0.3 * rng.standard_normal((B, H, K, V))
+    ro, rS = ora.gdn_forward(q, k, v, g, beta, S0=S0)
+    S = cuda(S0).contiguous()
+    outs = []
+    for t in range(T):
+        o, S = ops.key_step(cuda(q[:, t]), cuda(k[:, t]), cuda(v[:, t]), cuda(g[:, t]), cuda(beta[:, t]), S, S_out=S)
+        outs.append(o)
+    assert relerr(torch.stack(outs, 1), ro) < TOL_F32 and relerr(S, rS) < TOL_F32
