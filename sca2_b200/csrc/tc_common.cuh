@@ -10,7 +10,7 @@ namespace tc {
 
 constexpr int C = 64;     // chunk (tokens)
 constexpr int NT = 256;   // 8 warps
-constexpr int LDF = C + 1;
+constexpr int LDF = C + 4;  // fp32 row stride of the inversion scratch (rows 16-byte aligned)
 
 using bf16 = __nv_bfloat16;
 
@@ -167,26 +167,49 @@ __device__ inline void invert_unit_lower(const float* LS, float* TS, float* WS) 
     for (int r = 0; r < 16; ++r) TS[(o + r) * LDF + o + col] = x[r];
   }
   __syncthreads();
+  // off-diagonal blocks by distance d: each thread a 1 x 4 tile (row r, columns cq..cq+3),
+  // float4 shared loads along K and along the tile
   for (int d = 1; d < 4; ++d) {
     const int np = 4 - d;
-    for (int e = tid; e < np * 256; e += blockDim.x) {
-      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+    for (int e = tid; e < np * 64; e += blockDim.x) {  // W_{bi,bj} = sum_bk L_{bi,bk} T_{bk,bj}
+      const int pr = e >> 6, r = (e >> 2) & 15, cq = (e & 3) * 4;
       const int bi = pr + d, bj = pr;
-      float acc = 0.f;
-      for (int bk = bj; bk < bi; ++bk)
+      const float* lrow = LS + (16 * bi + r) * LDF;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int kk = 16 * bj; kk < 16 * bi; kk += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(lrow + kk);
+        const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          acc = fmaf(LS[(16 * bi + r) * LDF + 16 * bk + k], TS[(16 * bk + k) * LDF + 16 * bj + cc], acc);
-      WS[e] = acc;
+        for (int q = 0; q < 4; ++q) {
+          const float4 bv = *reinterpret_cast<const float4*>(TS + (kk + q) * LDF + 16 * bj + cq);
+          acc.x = fmaf(av[q], bv.x, acc.x);
+          acc.y = fmaf(av[q], bv.y, acc.y);
+          acc.z = fmaf(av[q], bv.z, acc.z);
+          acc.w = fmaf(av[q], bv.w, acc.w);
+        }
+      }
+      *reinterpret_cast<float4*>(WS + (pr << 8) + (r << 4) + cq) = acc;
     }
     __syncthreads();
-    for (int e = tid; e < np * 256; e += blockDim.x) {
-      const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+    for (int e = tid; e < np * 64; e += blockDim.x) {  // T_{bi,bj} = -T_{bi,bi} W_{bi,bj}
+      const int pr = e >> 6, r = (e >> 2) & 15, cq = (e & 3) * 4;
       const int bi = pr + d, bj = pr;
-      float acc = 0.f;
+      const float* trow = TS + (16 * bi + r) * LDF + 16 * bi;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) acc = fmaf(TS[(16 * bi + r) * LDF + 16 * bi + k], WS[(pr << 8) + (k << 4) + cc], acc);
-      TS[(16 * bi + r) * LDF + 16 * bj + cc] = -acc;
+      for (int k = 0; k < 16; k += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(trow + k);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 bv = *reinterpret_cast<const float4*>(WS + (pr << 8) + ((k + q) << 4) + cq);
+          acc.x = fmaf(av[q], bv.x, acc.x);
+          acc.y = fmaf(av[q], bv.y, acc.y);
+          acc.z = fmaf(av[q], bv.z, acc.z);
+          acc.w = fmaf(av[q], bv.w, acc.w);
+        }
+      }
+      *reinterpret_cast<float4*>(TS + (16 * bi + r) * LDF + 16 * bj + cq) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     }
     __syncthreads();
   }
