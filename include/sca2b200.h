@@ -159,6 +159,51 @@ SCA2_API int sca2_rms_fwd(const void* x, void* u, int64_t N, int32_t D, float ep
 SCA2_API int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D,
                  float eps, int32_t io_dtype, void* stream);
 
+/* ---- D-head diagonal scan ---------------------------------------------------------------
+ * Complex diagonal recurrence of the SCA2 D head and its read contracted over M rows:
+ *   s_t[m,j] = a_t[m,g(j)] s_{t-1}[m,j] + v_t[j]      g(j) = j / (V/G)
+ *   A_t[j]  = mean_m (sr cr + si ci),   Bv_t[j] = mean_m (si cr - sr ci)
+ * c = the normalised query per (t,m,j) (DHeadRef, sca2/ref.py:239-275) or, with sep = 1,
+ * its separable factor per (t,m) (DHeadSepQ, sca2/arch_sepq.py:100-104).  All tensors fp32
+ * and contiguous.  M in {1,2,4,8,16,32}; V/G (channels per gate group) a multiple of 32/M. */
+typedef struct sca2_dscan_args {
+  int32_t B, T, M, G, V;
+  int32_t sep;
+  const float* a_re;    /* (B,T,M,G) complex gate */
+  const float* a_im;
+  const float* v;       /* (B,T,V) */
+  const float* c_re;    /* (B,T,M,V), or (B,T,M) with sep */
+  const float* c_im;
+  const float* S0_re;   /* (B,M,V) incoming state, or NULL = zeros */
+  const float* S0_im;
+} sca2_dscan_args;
+
+/* Gradients of sca2_dscan_bwd.  da_re, da_im and, with sep, dc_re, dc_im are ACCUMULATED
+ * INTO (the caller zero-fills them); dv, dc (without sep) and dS0 are written. */
+typedef struct sca2_dscan_grads {
+  float* da_re;
+  float* da_im;
+  float* dv;
+  float* dc_re;
+  float* dc_im;
+  float* dS0_re;        /* or NULL */
+  float* dS0_im;
+} sca2_dscan_grads;
+
+/* Checkpoint blocks for T tokens: the buffer is (B, sca2_dscan_num_ckpt(T), 2, M, V) fp32. */
+SCA2_API int32_t sca2_dscan_num_ckpt(int32_t T);
+
+/* Forward: ab (B,T,2,V) = [A | Bv] per token; S_re, S_im (B,M,V) the state after T tokens;
+ * ckpt NULL, or the checkpoint buffer kept for the backward.  T = 1 is the decode step of
+ * DHeadRef.step / DHeadSepQ.step (sca2/ref.py:259-275, sca2/arch_sepq.py:152-178). */
+SCA2_API int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im,
+                   float* ckpt, void* stream);
+
+/* Backward: dab (B,T,2,V), dS_re / dS_im (B,M,V) or NULL, ckpt as written by the forward. */
+SCA2_API int sca2_dscan_bwd(const sca2_dscan_args* a, const float* dab, const float* dS_re,
+                   const float* dS_im, const float* ckpt, const sca2_dscan_grads* g,
+                   void* stream);
+
 /* Size of the device array behind sca2_scan_fwd_bwd_noalloc (every GPU that loads the
  * library holds it until the process exits). */
 #define SCA2_NOALLOC_SCRATCH_BYTES (16u << 20)

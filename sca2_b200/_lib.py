@@ -44,6 +44,22 @@ class ScanGrads(C.Structure):
     ]
 
 
+class DScanArgs(C.Structure):
+    _fields_ = [
+        ("B", C.c_int32), ("T", C.c_int32), ("M", C.c_int32), ("G", C.c_int32), ("V", C.c_int32),
+        ("sep", C.c_int32),
+        ("a_re", C.c_void_p), ("a_im", C.c_void_p), ("v", C.c_void_p), ("c_re", C.c_void_p),
+        ("c_im", C.c_void_p), ("S0_re", C.c_void_p), ("S0_im", C.c_void_p),
+    ]
+
+
+class DScanGrads(C.Structure):
+    _fields_ = [
+        ("da_re", C.c_void_p), ("da_im", C.c_void_p), ("dv", C.c_void_p), ("dc_re", C.c_void_p),
+        ("dc_im", C.c_void_p), ("dS0_re", C.c_void_p), ("dS0_im", C.c_void_p),
+    ]
+
+
 # (name, restype, argtypes) of every exported symbol, in header order
 SIGNATURES = [
     ("sca2_scan_fwd", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, C.c_void_p, C.c_void_p]),
@@ -55,6 +71,11 @@ SIGNATURES = [
                                C.c_int32, C.c_void_p]),
     ("sca2_rms_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
                                C.c_float, C.c_int32, C.c_void_p]),
+    ("sca2_dscan_num_ckpt", C.c_int32, [C.c_int32]),
+    ("sca2_dscan_fwd", C.c_int, [C.POINTER(DScanArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p]),
+    ("sca2_dscan_bwd", C.c_int, [C.POINTER(DScanArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.POINTER(DScanGrads), C.c_void_p]),
     ("sca2_scan_fwd_bwd_noalloc", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, Out, C.c_void_p,
                                             C.POINTER(ScanGrads), C.c_void_p]),
     ("sca2_fault_status", C.c_int, [C.POINTER(C.c_uint32)]),

@@ -30,6 +30,9 @@ cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, floa
                         float* cstates, int NCS, cudaStream_t st);
 cudaError_t tc_read_faults(unsigned int* out);
 cudaError_t tc_read_faults_bwd(unsigned int* out);
+cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, cudaStream_t st);
+cudaError_t dscan_bwd(const sca2_dscan_args& p, const float* dab, const float* dS_re, const float* dS_im,
+                      const float* ckpt, const sca2_dscan_grads& g, cudaStream_t st);
 cudaError_t tc_read_faults_prep(unsigned int* out);
 // scan_tc_bwd.cu
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
@@ -194,6 +197,63 @@ int sca2_scan_step(const sca2_scan_args* a, const float* S_in, float* S_out, sca
     return fail(SCA2_ERR_UNSUPPORTED, "decode step needs too much shared memory");
   cudaError_t e = sca2::launch_step(*a, S_in, S_out, o, vec, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_step");
+  return SCA2_OK;
+}
+
+static int check_dscan(const sca2_dscan_args* a) {
+  if (!a) return fail(SCA2_ERR_ARG, "null dscan args");
+  if (a->B < 1 || a->T < 0 || a->G < 1 || a->V < 1) return fail(SCA2_ERR_ARG, "dscan: bad sizes");
+  if (a->M != 1 && a->M != 2 && a->M != 4 && a->M != 8 && a->M != 16 && a->M != 32)
+    return fail(SCA2_ERR_UNSUPPORTED, "dscan: M must be a power of two <= 32");
+  if (a->V % a->G) return fail(SCA2_ERR_ARG, "dscan: V must be a multiple of G");
+  const int gs = a->V / a->G, jw = 32 / a->M;
+  if (gs % jw) return fail(SCA2_ERR_UNSUPPORTED, "dscan: channels per gate group must be a multiple of 32/M");
+  if (a->T > 0 && (!a->a_re || !a->a_im || !a->v || !a->c_re || !a->c_im))
+    return fail(SCA2_ERR_ARG, "dscan: null input");
+  if ((a->S0_re == nullptr) != (a->S0_im == nullptr)) return fail(SCA2_ERR_ARG, "dscan: S0 needs both parts");
+  return SCA2_OK;
+}
+
+int32_t sca2_dscan_num_ckpt(int32_t T) { return T > 0 ? (T + 15) / 16 : 0; }
+
+int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im, float* ckpt, void* stream) {
+  int rc = check_dscan(a);
+  if (rc) return rc;
+  if (!S_re || !S_im || (a->T > 0 && !ab)) return fail(SCA2_ERR_ARG, "dscan: null output");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (a->T == 0) {
+    const size_t n = (size_t)a->B * a->M * a->V * sizeof(float);
+    cudaError_t e = a->S0_re ? cudaMemcpyAsync(S_re, a->S0_re, n, cudaMemcpyDeviceToDevice, st)
+                             : cudaMemsetAsync(S_re, 0, n, st);
+    if (e == cudaSuccess)
+      e = a->S0_im ? cudaMemcpyAsync(S_im, a->S0_im, n, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(S_im, 0, n, st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_fwd(T=0)");
+    return SCA2_OK;
+  }
+  cudaError_t e = sca2::dscan_fwd(*a, ab, S_re, S_im, ckpt, st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_fwd");
+  return SCA2_OK;
+}
+
+int sca2_dscan_bwd(const sca2_dscan_args* a, const float* dab, const float* dS_re, const float* dS_im,
+                   const float* ckpt, const sca2_dscan_grads* g, void* stream) {
+  int rc = check_dscan(a);
+  if (rc) return rc;
+  if (!g) return fail(SCA2_ERR_ARG, "dscan: null gradient struct");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (a->T == 0) {
+    const size_t n = (size_t)a->B * a->M * a->V * sizeof(float);
+    cudaError_t e = cudaSuccess;
+    if (g->dS0_re) e = dS_re ? cudaMemcpyAsync(g->dS0_re, dS_re, n, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(g->dS0_re, 0, n, st);
+    if (e == cudaSuccess && g->dS0_im)
+      e = dS_im ? cudaMemcpyAsync(g->dS0_im, dS_im, n, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(g->dS0_im, 0, n, st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_bwd(T=0)");
+    return SCA2_OK;
+  }
+  if (!dab || !ckpt || !g->da_re || !g->da_im || !g->dv || !g->dc_re || !g->dc_im)
+    return fail(SCA2_ERR_ARG, "dscan: dab, ckpt and gradient buffers must be non-null");
+  cudaError_t e = sca2::dscan_bwd(*a, dab, dS_re, dS_im, ckpt, *g, st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_bwd");
   return SCA2_OK;
 }
 

@@ -17,6 +17,8 @@ hand-written kernels.  State dicts are the reference's: {"sr", "si"} fp32 plus a
   CHeadDelta        sca2/arch_cdelta.py:92-206       (delta write)
   CHeadDeltaDamp*   sca2/arch_damp.py:43-259         (per-mode decay, delta write)
   CHeadGated        sca2/arch_gatedc.py:58-193       (H heads, scalar decay, additive)
+  DHeadRef          sca2/ref.py:209-275              (D head: complex diagonal scan)
+  DHeadSepQ(Polar)  sca2/arch_sepq.py:46-290         (D head, separable query; polar gate)
 """
 from __future__ import annotations
 
@@ -385,3 +387,122 @@ class CHeadGated(CHeadBase):
         u = torch.cat([o[:, :, 0].reshape(B, self.dv), o[:, :, 1].reshape(B, self.dv)], -1)
         u = _gated_out(self, u, z_t).to(z_t.dtype)
         return u, {"sr": S[:, :, :Mh], "si": S[:, :, Mh:], "pos": state["pos"] + 1, "empty": False}
+
+
+# ----------------------------------------------------------------------------------------
+#  D heads: complex diagonal scan with a read contracted over M rows (ops.dscan)
+# ----------------------------------------------------------------------------------------
+class DHeadRef(nn.Module):
+    """sca2/ref.py:209-275: s_t = a_t s_{t-1} + v_t per (m, j) with the cartesian gate
+    a = tanh(gr(h)) / sqrt 2 + i tanh(gi(h)) / sqrt 2 shared by groups of dv / G channels,
+    read with the normalised query q(z) and contracted over m; u = rms([A | Bv])."""
+
+    def __init__(self, d, M=16, G=8, dv=None, max_len=None, delta_rule=False, gated_read=False):
+        super().__init__()
+        self.d, self.M, self.G, self.dv = d, M, G, (d // 2 if dv is None else dv)
+        self.gated_read = gated_read
+        if gated_read:
+            self.rgate = nn.Linear(d, 2 * self.dv, bias=False)
+        self.max_len = max_len
+        self.delta_rule = delta_rule
+        assert self.dv % G == 0
+        self.gs = self.dv // G
+        self.V = nn.Linear(d, self.dv, False)
+        self.gr = nn.Linear(d, M * G)
+        self.gi = nn.Linear(d, M * G)
+        self.qr = nn.Linear(d, M * self.dv, False)
+        self.qi = nn.Linear(d, M * self.dv, False)
+
+    def init_state(self, B, device, dtype=torch.float32):
+        return {"sr": torch.zeros(B, self.M, self.dv, device=device, dtype=torch.float32),
+                "si": torch.zeros(B, self.M, self.dv, device=device, dtype=torch.float32)}
+
+    def _gate(self, h, B, T):
+        s2 = 1.0 / math.sqrt(2.0)
+        return (torch.tanh(self.gr(h)).view(B, T, self.M, self.G) * s2,
+                torch.tanh(self.gi(h)).view(B, T, self.M, self.G) * s2)
+
+    def _scan(self, z, h, state):
+        B, T, _ = z.shape
+        st = state if state is not None else self.init_state(B, z.device)
+        a_re, a_im = self._gate(h, B, T)
+        qr = self.qr(z).view(B, T, self.M, self.dv)
+        qi = self.qi(z).view(B, T, self.M, self.dv)
+        qn = torch.sqrt(qr.square() + qi.square() + 1e-6)
+        ab, (sr, si) = ops.dscan(a_re, a_im, self.V(z), qr / qn, qi / qn, (st["sr"], st["si"]))
+        return ab.reshape(B, T, 2 * self.dv), {"sr": sr, "si": si}
+
+    def prefill(self, z, h, state=None):
+        u, st = self._scan(z, h, state)
+        return _rms(u).to(z.dtype), st
+
+    def forward(self, z, h):
+        return self.prefill(z, h)[0]
+
+    def step(self, z_t, h_t, state):
+        u, st = self.prefill(z_t[:, None], h_t[:, None], state)
+        return u[:, 0], st
+
+
+class DHeadSepQ(nn.Module):
+    """sca2/arch_sepq.py:46-178 (plain write): the same diagonal scan with a separable
+    query, alpha (B,T,M) contracted over m inside the scan and beta (B,T,dv) applied to
+    [A | Bv] afterwards, then the (optionally gated) RMS read-out."""
+
+    def __init__(self, d, M=16, G=8, dv=None, max_len=None, delta_rule=False, gated_read=False):
+        super().__init__()
+        self.d, self.M, self.G, self.dv = d, M, G, (d // 2 if dv is None else dv)
+        self.max_len = max_len
+        self.gated_read = gated_read
+        if gated_read:
+            self.rgate = nn.Linear(d, 2 * self.dv, bias=False)
+        self.delta_rule = "exact" if delta_rule is True else delta_rule
+        if self.delta_rule:
+            raise NotImplementedError("the delta-rule D head is not on the B200 scan path")
+        assert self.dv % G == 0
+        self.gs = self.dv // G
+        self.V = nn.Linear(d, self.dv, False)
+        self.gr = nn.Linear(d, M * G)
+        self.gi = nn.Linear(d, M * G)
+        self.qa_r = nn.Linear(d, M, False)
+        self.qa_i = nn.Linear(d, M, False)
+        self.qb_r = nn.Linear(d, self.dv, False)
+        self.qb_i = nn.Linear(d, self.dv, False)
+
+    init_state = DHeadRef.init_state
+
+    def _gate(self, h, B, T):
+        s2 = 1.0 / math.sqrt(2.0)
+        return (torch.tanh(self.gr(h)).view(B, T, self.M, self.G) * s2,
+                torch.tanh(self.gi(h)).view(B, T, self.M, self.G) * s2)
+
+    def prefill(self, z, h, state=None):
+        B, T, _ = z.shape
+        st = state if state is not None else self.init_state(B, z.device)
+        a_re, a_im = self._gate(h, B, T)
+        ar, ai = self.qa_r(z), self.qa_i(z)
+        br, bi = self.qb_r(z), self.qb_i(z)
+        an = torch.rsqrt(ar.square() + ai.square() + 1e-6)
+        bn = torch.rsqrt(br.square() + bi.square() + 1e-6)
+        ab, (sr, si) = ops.dscan(a_re, a_im, self.V(z), ar * an, ai * an, (st["sr"], st["si"]), sep=True)
+        A, Bv = ab[:, :, 0], ab[:, :, 1]
+        br, bi = br * bn, bi * bn
+        u = torch.cat([br * A + bi * Bv, br * Bv - bi * A], -1)
+        return _gated_out(self, u, z).to(z.dtype), {"sr": sr, "si": si}
+
+    def forward(self, z, h):
+        return self.prefill(z, h)[0]
+
+    def step(self, z_t, h_t, state):
+        u, st = self.prefill(z_t[:, None], h_t[:, None], state)
+        return u[:, 0], st
+
+
+class DHeadSepQPolar(DHeadSepQ):
+    """sca2/arch_sepq.py:181-290: the gate emitted in log-polar form,
+    a = exp(-softplus(gr(h))) e^{i gi(h)}."""
+
+    def _gate(self, h, B, T):
+        mag = torch.exp(-F.softplus(self.gr(h))).view(B, T, self.M, self.G)
+        ph = self.gi(h).view(B, T, self.M, self.G)
+        return mag * torch.cos(ph), mag * torch.sin(ph)

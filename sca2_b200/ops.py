@@ -346,6 +346,74 @@ def key_step(q, k, v, g, beta, S, scale=None, S_out=None, v_times_beta=True):
 
 
 # ======================================================================================
+#  D-head diagonal scan
+# ======================================================================================
+def _dscan_args(a_re, a_im, v, c_re, c_im, S0, sep):
+    B, T, M, G = a_re.shape
+    a = _lib.DScanArgs()
+    a.B, a.T, a.M, a.G, a.V, a.sep = B, T, M, G, v.shape[-1], 1 if sep else 0
+    a.a_re, a.a_im, a.v, a.c_re, a.c_im = (x.data_ptr() for x in (a_re, a_im, v, c_re, c_im))
+    a.S0_re = S0[0].data_ptr() if S0 is not None else None
+    a.S0_im = S0[1].data_ptr() if S0 is not None else None
+    return a
+
+
+class _DScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep):
+        B, T, M, G = a_re.shape
+        V = v.shape[-1]
+        S0 = (S0_re, S0_im) if S0_re is not None else None
+        a = _dscan_args(a_re, a_im, v, c_re, c_im, S0, sep)
+        ab = torch.empty(B, T, 2, V, device=v.device, dtype=torch.float32)
+        S_re = torch.empty(B, M, V, device=v.device, dtype=torch.float32)
+        S_im = torch.empty_like(S_re)
+        lib = _lib.load()
+        need = any(ctx.needs_input_grad)
+        ck = torch.empty(B, lib.sca2_dscan_num_ckpt(T), 2, M, V, device=v.device) if need else None
+        _lib.check(lib.sca2_dscan_fwd(C_ref(a), ab.data_ptr(), S_re.data_ptr(), S_im.data_ptr(), _ptr(ck),
+                                      _stream()), "dscan_fwd")
+        if need:
+            ctx.save_for_backward(a_re, a_im, v, c_re, c_im, S0_re, S0_im, ck)
+            ctx.sep = sep
+        return ab, S_re, S_im
+
+    @staticmethod
+    def backward(ctx, dab, dS_re, dS_im):
+        a_re, a_im, v, c_re, c_im, S0_re, S0_im, ck = ctx.saved_tensors
+        S0 = (S0_re, S0_im) if S0_re is not None else None
+        a = _dscan_args(a_re, a_im, v, c_re, c_im, S0, ctx.sep)
+        da_re, da_im = torch.zeros_like(a_re), torch.zeros_like(a_im)
+        dv = torch.empty_like(v)
+        dc_re = torch.zeros_like(c_re) if ctx.sep else torch.empty_like(c_re)
+        dc_im = torch.zeros_like(c_im) if ctx.sep else torch.empty_like(c_im)
+        dS0_re = torch.empty_like(S0_re) if S0 is not None else None
+        dS0_im = torch.empty_like(S0_im) if S0 is not None else None
+        g = _lib.DScanGrads()
+        g.da_re, g.da_im, g.dv, g.dc_re, g.dc_im = (x.data_ptr() for x in (da_re, da_im, dv, dc_re, dc_im))
+        g.dS0_re, g.dS0_im = _ptr(dS0_re), _ptr(dS0_im)
+        dab = dab.contiguous() if dab is not None else torch.zeros(*a_re.shape[:2], 2, v.shape[-1], device=v.device)
+        dS_re = dS_re.contiguous() if dS_re is not None else None
+        dS_im = dS_im.contiguous() if dS_im is not None else None
+        _lib.check(_lib.load().sca2_dscan_bwd(C_ref(a), dab.data_ptr(), _ptr(dS_re), _ptr(dS_im), ck.data_ptr(),
+                                              C_ref(g), _stream()), "dscan_bwd")
+        return da_re, da_im, dv, dc_re, dc_im, dS0_re, dS0_im, None
+
+
+def dscan(a_re, a_im, v, c_re, c_im, S0: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, sep: bool = False):
+    """D-head diagonal scan (sca2/ref.py:239-275, sca2/arch_sepq.py:110-178): complex gate
+    a (B,T,M,G), values v (B,T,V), read coefficients c (B,T,M,V), or (B,T,M) with sep,
+    initial state (sr, si) each (B,M,V) -> ab (B,T,2,V) = [A | Bv] and the final (sr, si).
+    fp32; differentiable in every input."""
+    _need_cuda(a_re, a_im, v, c_re, c_im, *(S0 or ()))
+    f = lambda x: x.to(torch.float32).contiguous()
+    a_re, a_im, v, c_re, c_im = f(a_re), f(a_im), f(v), f(c_re), f(c_im)
+    S0_re, S0_im = (f(S0[0]), f(S0[1])) if S0 is not None else (None, None)
+    ab, S_re, S_im = _DScan.apply(a_re, a_im, v, c_re, c_im, S0_re, S0_im, bool(sep))
+    return ab, (S_re, S_im)
+
+
+# ======================================================================================
 #  RMS read-out
 # ======================================================================================
 class _Rms(torch.autograd.Function):

@@ -21,7 +21,8 @@ head-level ("head_*.npz")
     A reference head with ordinary random weights (rope grid, theta != 0) is run on
     random z, h and a random incoming state; the fixture stores its state_dict, the
     inputs, the RMS'd output u, the new state and every parameter / input gradient.
-    These pin the drop-in head classes (projections + scan + epilogue).
+    These pin the drop-in head classes (projections + scan + epilogue).  head_d*.npz are
+    the D heads (DHeadRef, DHeadSepQ, DHeadSepQPolar), with decode steps after the prefill.
 
 gdn_fla.npz
     fla 0.5.1 naive_chunk_gated_delta_rule / naive_recurrent_gated_delta_rule
@@ -349,6 +350,41 @@ def head_gated(gen, B=2, T=45, d=24, H=2, Mh=6, dvh=4, ctx=16):
                 **{"sd_" + k: v for k, v in sd.items()}, **grads)
 
 
+def head_d(gen, kind, B=2, T=45, d=24, M=4, G=4, dv=32, steps=3):
+    """A reference D head (DHeadRef, DHeadSepQ or DHeadSepQPolar; sca2/ref.py:209-275,
+    sca2/arch_sepq.py:46-290) with random weights: prefill on random z, h and a random
+    incoming state, the RMS'd output u, the new state, every parameter / input gradient of
+    sum(u * dU), then `steps` decode steps continuing from the prefill's state."""
+    from sca2.ref import DHeadRef
+    from sca2.arch_sepq import DHeadSepQ, DHeadSepQPolar
+    torch.manual_seed(int(torch.randint(0, 2**31 - 1, (1,), generator=gen)))
+    cls = {"ref": DHeadRef, "sepq": DHeadSepQ, "polar": DHeadSepQPolar}[kind]
+    gated = kind != "ref"
+    head = cls(d, M, G, dv=dv, gated_read=gated).double()
+    z = torch.randn(B, T, d, generator=gen, dtype=torch.float64).requires_grad_(True)
+    h = torch.randn(B, T, d, generator=gen, dtype=torch.float64).requires_grad_(True)
+    sr0 = torch.randn(B, M, dv, generator=gen, dtype=torch.float64) * 0.3
+    si0 = torch.randn(B, M, dv, generator=gen, dtype=torch.float64) * 0.3
+    u, st1 = head.prefill(z, h, {"sr": sr0, "si": si0})
+    dU = torch.randn(u.shape, generator=gen, dtype=torch.float64)
+    (u * dU).sum().backward()
+    sd = {k: _np(v) for k, v in head.state_dict().items()}
+    grads = {"g_" + n: _np(p.grad) for n, p in head.named_parameters() if p.grad is not None}
+    zs = torch.randn(B, steps, d, generator=gen, dtype=torch.float64)
+    hs = torch.randn(B, steps, d, generator=gen, dtype=torch.float64)
+    st = {"sr": st1["sr"].detach(), "si": st1["si"].detach()}
+    us = []
+    with torch.no_grad():
+        for t in range(steps):
+            ut, st = head.step(zs[:, t], hs[:, t], st)
+            us.append(ut)
+    return dict(z=_np(z), h=_np(h), sr0=_np(sr0), si0=_np(si0), u=_np(u), sr=_np(st1["sr"]),
+                si=_np(st1["si"]), dU=_np(dU), d_z=_np(z.grad), d_h=_np(h.grad),
+                zs=_np(zs), hs=_np(hs), us=_np(torch.stack(us, 1)), srs=_np(st["sr"]), sis=_np(st["si"]),
+                meta=np.array([B, T, d, M, G, dv, int(gated)]),
+                **{"sd_" + k: v for k, v in sd.items()}, **grads)
+
+
 def main(ref_root):
     sys.path.insert(0, ref_root)
     import sca2.arch_short  # noqa: F401  registers cdelta/damp/short (see registry import order)
@@ -364,6 +400,9 @@ def main(ref_root):
     _save("gdn_fla.npz", **gdn_fla(gen))
     _save("head_longhead.npz", **head_longhead(gen))
     _save("head_gated.npz", **head_gated(gen))
+    _save("head_dref.npz", **head_d(gen, "ref", M=4, G=4, dv=32))
+    _save("head_dsepq.npz", **head_d(gen, "sepq", M=8, G=4, dv=16))
+    _save("head_dpolar.npz", **head_d(gen, "polar", M=16, G=4, dv=16))
 
 
 if __name__ == "__main__":

@@ -45,6 +45,9 @@ int main(void) {
          sizeof(sca2_tok), sizeof(sca2_out), sizeof(sca2_scan_args), sizeof(sca2_scan_grads));
   F(sca2_scan_args, q_scale) F(sca2_scan_args, phw) F(sca2_scan_args, g) F(sca2_scan_args, lam)
   F(sca2_scan_args, S0) F(sca2_scan_grads, dg) F(sca2_scan_grads, dlam) F(sca2_scan_grads, dS0)
+  printf("sca2_dscan_args %zu\nsca2_dscan_grads %zu\n", sizeof(sca2_dscan_args), sizeof(sca2_dscan_grads));
+  F(sca2_dscan_args, sep) F(sca2_dscan_args, a_re) F(sca2_dscan_args, S0_im)
+  F(sca2_dscan_grads, dv) F(sca2_dscan_grads, dS0_im)
   return 0;
 }
 """
@@ -59,10 +62,13 @@ int main(void) {
     assert int(out["sca2_out"]) == ctypes.sizeof(_lib.Out)
     assert int(out["sca2_scan_args"]) == ctypes.sizeof(_lib.ScanArgs)
     assert int(out["sca2_scan_grads"]) == ctypes.sizeof(_lib.ScanGrads)
+    assert int(out["sca2_dscan_args"]) == ctypes.sizeof(_lib.DScanArgs)
+    assert int(out["sca2_dscan_grads"]) == ctypes.sizeof(_lib.DScanGrads)
     for key, val in out.items():
         if "." in key:
             st, field = key.split(".")
-            cls = {"sca2_scan_args": _lib.ScanArgs, "sca2_scan_grads": _lib.ScanGrads}[st]
+            cls = {"sca2_scan_args": _lib.ScanArgs, "sca2_scan_grads": _lib.ScanGrads,
+                   "sca2_dscan_args": _lib.DScanArgs, "sca2_dscan_grads": _lib.DScanGrads}[st]
             assert getattr(cls, field).offset == int(val), key
 
 

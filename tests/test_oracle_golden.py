@@ -95,3 +95,56 @@ def test_chunk_invariance():
         o, _ = ora.phase_forward(inp["phw"], inp["phq"], inp["v"], inp["beta"], None, inp["lam"],
                                  inp["wr"], inp["wi"], inp["S0"], chunked=True, C=C)
         assert _rel(o, ref) < TOL
+
+
+# ---- D heads ---------------------------------------------------------------------------------
+@pytest.mark.parametrize("name,kind", [("head_dref.npz", "ref"), ("head_dsepq.npz", "sepq"),
+                                       ("head_dpolar.npz", "polar")])
+def test_dhead_oracle_vs_reference(name, kind):
+    """The numpy D-head scan (with the heads' projections) reproduces the reference heads:
+    prefill output, new state and decode steps."""
+    from oracle import dscan as dor
+    f = fx.load(name)
+    B, T, d, M, G, dv, _ = (int(x) for x in f["meta"])
+    sd = {k[3:]: f[k] for k in f if k.startswith("sd_")}
+    u, (sr, si) = dor.d_head(kind, sd, f["z"], f["h"], (f["sr0"], f["si0"]), M, G, dv)
+    assert np.abs(u - f["u"]).max() < 1e-9 and np.abs(sr - f["sr"]).max() < 1e-9
+    assert np.abs(si - f["si"]).max() < 1e-9
+    S = (f["sr"], f["si"])
+    for t in range(f["zs"].shape[1]):
+        ut, S = dor.d_head(kind, sd, f["zs"][:, t:t + 1], f["hs"][:, t:t + 1], S, M, G, dv)
+        assert np.abs(ut[:, 0] - f["us"][:, t]).max() < 1e-9
+    assert np.abs(S[0] - f["srs"]).max() < 1e-9 and np.abs(S[1] - f["sis"]).max() < 1e-9
+
+
+@pytest.mark.parametrize("sep", [False, True])
+def test_dscan_oracle_backward_finite_difference(sep):
+    """The oracle's adjoint against central differences of its forward."""
+    from oracle import dscan as dor
+    rng = np.random.default_rng(3 + sep)
+    B, T, M, G, V = 2, 7, 4, 2, 8
+    a_re, a_im = 0.6 * rng.standard_normal((B, T, M, G)), 0.6 * rng.standard_normal((B, T, M, G))
+    v = rng.standard_normal((B, T, V))
+    cs = (B, T, M) if sep else (B, T, M, V)
+    c_re, c_im = rng.standard_normal(cs), rng.standard_normal(cs)
+    S0 = (rng.standard_normal((B, M, V)), rng.standard_normal((B, M, V)))
+    dab = rng.standard_normal((B, T, 2, V))
+    dS = (rng.standard_normal((B, M, V)), rng.standard_normal((B, M, V)))
+    g = dor.dscan_backward(a_re, a_im, v, c_re, c_im, S0, dab, dS, sep=sep)
+
+    def loss(a_re, a_im, v, c_re, c_im, s0r, s0i):
+        ab, S = dor.dscan_forward(a_re, a_im, v, c_re, c_im, (s0r, s0i), sep=sep)
+        return (ab * dab).sum() + (S[0] * dS[0]).sum() + (S[1] * dS[1]).sum()
+    args = [a_re, a_im, v, c_re, c_im, S0[0], S0[1]]
+    names = ["a_re", "a_im", "v", "c_re", "c_im", "s0r", "s0i"]
+    for k, n in enumerate(names):
+        x = args[k]
+        idx = tuple(rng.integers(0, s) for s in x.shape)
+        e = 1e-6
+        xp, xm = x.copy(), x.copy()
+        xp[idx] += e
+        xm[idx] -= e
+        fd = (loss(*[xp if i == k else args[i] for i in range(7)]) -
+              loss(*[xm if i == k else args[i] for i in range(7)])) / (2 * e)
+        an = g["S0"][0][idx] if n == "s0r" else g["S0"][1][idx] if n == "s0i" else g[n][idx]
+        assert abs(fd - an) < 1e-6 * max(1.0, abs(fd)), (n, fd, an)
