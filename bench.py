@@ -35,6 +35,7 @@ sys.path.insert(0, ROOT)
 WORK = dict(B=8, T=4096, H=16, Mh=32, V=64)
 DECODE = dict(B=256, T=4096, H=16, Mh=64, V=128, steps=512)
 SP = dict(B=1, T=131072, H=16, Mh=32, V=64)  # one long sequence, split over the ranks
+DHEAD = dict(B=8, T=4096, M=16, G=8, V=64)   # D head of the reference LayerCfg (Md=16, G=8, dv=d/2)
 # Algorithmic bytes per token per head (inputs read + outputs written once):
 #   fwd: phi, psi fp32 (2*Mh*4) + v bf16 (V*2) + beta (4) + o bf16 (2*V*2)
 #   bwd: dO bf16 (2*V*2) + inputs re-read (2*Mh*4 + V*2 + 4) + dphi, dpsi fp32 (2*Mh*4) + dv bf16 (V*2) + dbeta (4)
@@ -248,8 +249,12 @@ def run_gpu(args, rank, world, local_rank, dist):
     if not args.no_sp:
         torch.cuda.empty_cache()
         sp = run_sp(torch, dev, rank, world, dist)
+    dh = None
+    if not args.no_dhead:
+        torch.cuda.empty_cache()
+        dh = run_dhead(torch, ops, dev, rank, world, dist)
     return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
-                decode=decode, sp=sp)
+                decode=decode, sp=sp, dhead=dh)
 
 
 def run_decode(torch, ops, dev, rank, world, dist):
@@ -349,6 +354,48 @@ def _quiet_stdout(fn):
         os.close(null)
 
 
+def run_dhead(torch, ops, dev, rank, world, dist, reps=5):
+    """D-head diagonal scan fwd+bwd (separable read, fp32) on the reference layer's D-head
+    shape; algorithmic bytes: fwd reads a (2 M G), v (V), c (2 M) and writes [A|Bv] (2 V)
+    fp32 per token, bwd re-reads the inputs, reads d[A|Bv] and writes every input gradient."""
+    D = DHEAD
+    B, T, M, G, V = D["B"], D["T"], D["M"], D["G"], D["V"]
+    g = torch.Generator(device=dev).manual_seed(31 + rank)
+    rn = lambda *sh: torch.randn(*sh, device=dev, generator=g)
+    ph = rn(B, T, M, G)
+    mag = torch.exp(-torch.nn.functional.softplus(rn(B, T, M, G)))
+    x = [(mag * torch.cos(ph)).requires_grad_(True), (mag * torch.sin(ph)).requires_grad_(True),
+         rn(B, T, V).requires_grad_(True), rn(B, T, M).requires_grad_(True), rn(B, T, M).requires_grad_(True)]
+    dab = rn(B, T, 2, V)
+
+    def step():
+        ab, (sr, si) = ops.dscan(*x, sep=True)
+        torch.autograd.backward(ab, dab)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    fwd_b = (2 * M * G + V + 2 * M + 2 * V) * 4
+    bwd_b = fwd_b - 2 * V * 4 + 2 * V * 4 + (2 * M * G + V + 2 * M) * 4
+    gbs = (fwd_b + bwd_b) * B * T / (ms * 1e-3) / 1e9
+    return {"value": world * B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "config": {"batch": B, "seq_len": T, "M": M, "G": G, "dv": V, "read": "separable", "fwd+bwd": True},
+            "achieved_gbs": gbs, "algorithmic_bytes_per_step": (fwd_b + bwd_b) * B * T}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -368,6 +415,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sp", action="store_true")
+    ap.add_argument("--no-dhead", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
@@ -470,6 +518,7 @@ def main():
         "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"], "gpu_launches": 2 * args.steps,
         "decode": r["decode"],
         "sp_prefill": r["sp"],
+        "d_head": r["dhead"],
     }
     print(json.dumps(line))
 
