@@ -193,16 +193,24 @@ typedef struct sca2_dscan_grads {
 /* Checkpoint blocks for T tokens: the buffer is (B, sca2_dscan_num_ckpt(T), 2, M, V) fp32. */
 SCA2_API int32_t sca2_dscan_num_ckpt(int32_t T);
 
-/* Forward: ab (B,T,2,V) = [A | Bv] per token; S_re, S_im (B,M,V) the state after T tokens;
- * ckpt NULL, or the checkpoint buffer kept for the backward.  T = 1 is the decode step of
- * DHeadRef.step / DHeadSepQ.step (sca2/ref.py:259-275, sca2/arch_sepq.py:152-178). */
-SCA2_API int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im,
-                   float* ckpt, void* stream);
+/* Bytes of the optional device workspace of sca2_dscan_fwd / sca2_dscan_bwd.  With it, a
+ * long sequence runs as 16-token blocks in parallel joined by a pass over the blocks; with
+ * work = NULL every (b, m, j) runs its T tokens sequentially (same results up to fp32
+ * rounding order, far less parallel). */
+SCA2_API int64_t sca2_dscan_work_bytes(int32_t B, int32_t T, int32_t M, int32_t G, int32_t V);
 
-/* Backward: dab (B,T,2,V), dS_re / dS_im (B,M,V) or NULL, ckpt as written by the forward. */
+/* Forward: ab (B,T,2,V) = [A | Bv] per token; S_re, S_im (B,M,V) the state after T tokens;
+ * ckpt NULL, or the checkpoint buffer kept for the backward; work NULL or
+ * sca2_dscan_work_bytes of device memory.  T = 1 is the decode step of DHeadRef.step /
+ * DHeadSepQ.step (sca2/ref.py:259-275, sca2/arch_sepq.py:152-178). */
+SCA2_API int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im,
+                   float* ckpt, void* work, void* stream);
+
+/* Backward: dab (B,T,2,V), dS_re / dS_im (B,M,V) or NULL, ckpt as written by the forward,
+ * work as for the forward. */
 SCA2_API int sca2_dscan_bwd(const sca2_dscan_args* a, const float* dab, const float* dS_re,
                    const float* dS_im, const float* ckpt, const sca2_dscan_grads* g,
-                   void* stream);
+                   void* work, void* stream);
 
 /* Size of the device array behind sca2_scan_fwd_bwd_noalloc (every GPU that loads the
  * library holds it until the process exits). */

@@ -72,10 +72,11 @@ SIGNATURES = [
     ("sca2_rms_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
                                C.c_float, C.c_int32, C.c_void_p]),
     ("sca2_dscan_num_ckpt", C.c_int32, [C.c_int32]),
+    ("sca2_dscan_work_bytes", C.c_int64, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     ("sca2_dscan_fwd", C.c_int, [C.POINTER(DScanArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
-                                 C.c_void_p]),
+                                 C.c_void_p, C.c_void_p]),
     ("sca2_dscan_bwd", C.c_int, [C.POINTER(DScanArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
-                                 C.POINTER(DScanGrads), C.c_void_p]),
+                                 C.POINTER(DScanGrads), C.c_void_p, C.c_void_p]),
     ("sca2_scan_fwd_bwd_noalloc", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, Out, C.c_void_p,
                                             C.POINTER(ScanGrads), C.c_void_p]),
     ("sca2_fault_status", C.c_int, [C.POINTER(C.c_uint32)]),

@@ -30,9 +30,12 @@ cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, floa
                         float* cstates, int NCS, cudaStream_t st);
 cudaError_t tc_read_faults(unsigned int* out);
 cudaError_t tc_read_faults_bwd(unsigned int* out);
-cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, cudaStream_t st);
+// dscan.cu
+size_t dscan_work_floats(int B, int T, int M, int G, int V);
+cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
+                      cudaStream_t st);
 cudaError_t dscan_bwd(const sca2_dscan_args& p, const float* dab, const float* dS_re, const float* dS_im,
-                      const float* ckpt, const sca2_dscan_grads& g, cudaStream_t st);
+                      const float* ckpt, float* work, const sca2_dscan_grads& g, cudaStream_t st);
 cudaError_t tc_read_faults_prep(unsigned int* out);
 // scan_tc_bwd.cu
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
@@ -216,7 +219,13 @@ static int check_dscan(const sca2_dscan_args* a) {
 
 int32_t sca2_dscan_num_ckpt(int32_t T) { return T > 0 ? (T + 15) / 16 : 0; }
 
-int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im, float* ckpt, void* stream) {
+int64_t sca2_dscan_work_bytes(int32_t B, int32_t T, int32_t M, int32_t G, int32_t V) {
+  if (B < 1 || T < 1 || M < 1 || G < 1 || V < 1) return 0;
+  return (int64_t)(sca2::dscan_work_floats(B, T, M, G, V) * sizeof(float));
+}
+
+int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im, float* ckpt, void* work,
+                   void* stream) {
   int rc = check_dscan(a);
   if (rc) return rc;
   if (!S_re || !S_im || (a->T > 0 && !ab)) return fail(SCA2_ERR_ARG, "dscan: null output");
@@ -230,13 +239,13 @@ int sca2_dscan_fwd(const sca2_dscan_args* a, float* ab, float* S_re, float* S_im
     if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_fwd(T=0)");
     return SCA2_OK;
   }
-  cudaError_t e = sca2::dscan_fwd(*a, ab, S_re, S_im, ckpt, st);
+  cudaError_t e = sca2::dscan_fwd(*a, ab, S_re, S_im, ckpt, static_cast<float*>(work), st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_fwd");
   return SCA2_OK;
 }
 
 int sca2_dscan_bwd(const sca2_dscan_args* a, const float* dab, const float* dS_re, const float* dS_im,
-                   const float* ckpt, const sca2_dscan_grads* g, void* stream) {
+                   const float* ckpt, const sca2_dscan_grads* g, void* work, void* stream) {
   int rc = check_dscan(a);
   if (rc) return rc;
   if (!g) return fail(SCA2_ERR_ARG, "dscan: null gradient struct");
@@ -252,7 +261,7 @@ int sca2_dscan_bwd(const sca2_dscan_args* a, const float* dab, const float* dS_r
   }
   if (!dab || !ckpt || !g->da_re || !g->da_im || !g->dv || !g->dc_re || !g->dc_im)
     return fail(SCA2_ERR_ARG, "dscan: dab, ckpt and gradient buffers must be non-null");
-  cudaError_t e = sca2::dscan_bwd(*a, dab, dS_re, dS_im, ckpt, *g, st);
+  cudaError_t e = sca2::dscan_bwd(*a, dab, dS_re, dS_im, ckpt, static_cast<float*>(work), *g, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_dscan_bwd");
   return SCA2_OK;
 }

@@ -10,11 +10,13 @@
 // over j applied afterwards).  The gate a is the cartesian complex gate of the head
 // (tanh / sqrt(2) of two projections, or exp(-softplus) e^{i phase} for the polar gate).
 //
-// One thread per (b, m, j); a warp holds all M rows of 32/M consecutive channels, so the
-// contraction over m is a butterfly of shuffles.  The recurrence runs sequentially over t
-// per thread (the work per token is tiny; parallelism comes from B * M * V threads).  The
-// forward keeps the state entering every 16-token block for the backward, which recomputes
-// each block's states in registers and walks it in reverse with the adjoint of s.
+// One thread per (b, m, j) (and, for long sequences, per 16-token block); a warp holds all M
+// rows of 32/M consecutive channels, so the contraction over m is a butterfly of shuffles.
+// Short sequences and decode run the recurrence sequentially over t per thread.  Long ones
+// split T into 16-token blocks that run in parallel, joined by a short pass over the blocks
+// (the recurrence is linear, so a block is the affine map s -> P s + e).  The forward keeps
+// the state entering every block for the backward, which recomputes each block's states in
+// registers and walks it in reverse with the adjoint of s.
 #include "common.cuh"
 
 namespace sca2 {
@@ -177,51 +179,332 @@ __global__ void __launch_bounds__(NT) dscan_bwd_kernel(sca2_dscan_args p, const 
   }
 }
 
+// ---- chunk-parallel forms (long sequences) --------------------------------------------------
+// Blocks of CK tokens run in parallel.  Forward: (1) every block scans from a zero state,
+// giving its end state e and the product P of its gates; (2) one pass over the blocks folds
+// S_in(k+1) = P_k S_in(k) + e_k, which are the checkpoints; (3) every block rescans from
+// S_in(k) and writes the read.  Backward: (1) every block runs its adjoint from a zero
+// adjoint at its end, giving the adjoint q it sends to the left and the product Q of its
+// conjugate gates; (2) one reverse pass folds R(k-1) = Q_k R(k) + q_k (R = adjoint entering a
+// block from the right; R(last) = dS, R(-1) = dS0); (3) every block runs the gradient pass of
+// dscan_bwd_kernel from R(k).  Workspace (floats): fwd e, P; bwd q, Q, R.
+
 template <int M>
-cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt,
+__device__ __forceinline__ Map thread_map_c(const sca2_dscan_args& p) {
+  constexpr int JW = 32 / M;
+  Map r;
+  const int idx = blockIdx.z * NT + threadIdx.x;
+  const int lane = idx & 31, wid = idx >> 5;
+  r.b = blockIdx.x;
+  r.m = lane % M;
+  r.jj = lane / M;
+  r.j = wid * JW + r.jj;
+  r.live = r.j < p.V;
+  r.g = r.live ? r.j / (p.V / p.G) : 0;
+  return r;
+}
+
+// complex product of a block's gates, kept per (b, k, m, g) by the group's first channel
+template <int M>
+__global__ void __launch_bounds__(NT) dscan_fwd_local(sca2_dscan_args p, float* e, float* P) {
+  const Map q = thread_map_c<M>(p);
+  const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
+  const int t0 = k * CK, n = min(CK, T - t0);
+  const int jc = q.live ? q.j : 0;
+  const int64_t bT = (int64_t)q.b * T;
+  float sr = 0.f, si = 0.f, pr = 1.f, pi = 0.f;
+#pragma unroll 4
+  for (int u = 0; u < n; ++u) {
+    const int64_t tm = (bT + t0 + u) * M + q.m;
+    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+    const float vt = p.v[(bT + t0 + u) * V + jc];
+    const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
+    si = fmaf(ar, si, ai * sr);
+    sr = nr;
+    const float qr = ar * pr - ai * pi;
+    pi = ar * pi + ai * pr;
+    pr = qr;
+  }
+  if (!q.live) return;
+  const int64_t base = ((int64_t)q.b * NK + k) * 2;
+  e[base * M * V + (int64_t)q.m * V + q.j] = sr;
+  e[(base + 1) * M * V + (int64_t)q.m * V + q.j] = si;
+  if (q.j % (V / G) == 0) {
+    P[base * M * G + (int64_t)q.m * G + q.g] = pr;
+    P[(base + 1) * M * G + (int64_t)q.m * G + q.g] = pi;
+  }
+}
+
+// fold over the blocks (sequential per (b, m, j)): checkpoints and the final state
+template <int M>
+__global__ void __launch_bounds__(NT) dscan_fwd_carry(sca2_dscan_args p, const float* e, const float* P, float* ckpt,
+                                                     float* S_re, float* S_im) {
+  const Map q = thread_map<M>(p);
+  if (!q.live) return;
+  const int V = p.V, G = p.G, NK = (p.T + CK - 1) / CK;
+  const int64_t sidx = ((int64_t)q.b * M + q.m) * V + q.j;
+  float sr = p.S0_re ? p.S0_re[sidx] : 0.f, si = p.S0_im ? p.S0_im[sidx] : 0.f;
+#pragma unroll 8
+  for (int k = 0; k < NK; ++k) {
+    const int64_t base = ((int64_t)q.b * NK + k) * 2;
+    ckpt[base * M * V + (int64_t)q.m * V + q.j] = sr;
+    ckpt[(base + 1) * M * V + (int64_t)q.m * V + q.j] = si;
+    const float pr = P[base * M * G + (int64_t)q.m * G + q.g], pi = P[(base + 1) * M * G + (int64_t)q.m * G + q.g];
+    const float er = e[base * M * V + (int64_t)q.m * V + q.j], ei = e[(base + 1) * M * V + (int64_t)q.m * V + q.j];
+    const float nr = pr * sr - pi * si + er;
+    si = pr * si + pi * sr + ei;
+    sr = nr;
+  }
+  S_re[sidx] = sr;
+  S_im[sidx] = si;
+}
+
+// every block from its incoming state: the read
+template <int M, bool SEP>
+__global__ void __launch_bounds__(NT) dscan_fwd_out(sca2_dscan_args p, const float* ckpt, float* ab) {
+  const Map q = thread_map_c<M>(p);
+  const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
+  const int t0 = k * CK, n = min(CK, T - t0);
+  const int jc = q.live ? q.j : 0;
+  const int64_t bT = (int64_t)q.b * T;
+  const int64_t base = ((int64_t)q.b * NK + k) * 2;
+  float sr = ckpt[base * M * V + (int64_t)q.m * V + jc], si = ckpt[(base + 1) * M * V + (int64_t)q.m * V + jc];
+#pragma unroll 4
+  for (int u = 0; u < n; ++u) {
+    const int t = t0 + u;
+    const int64_t tm = (bT + t) * M + q.m;
+    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+    const float vt = p.v[(bT + t) * V + jc];
+    const float cr = SEP ? p.c_re[tm] : p.c_re[tm * V + jc];
+    const float ci = SEP ? p.c_im[tm] : p.c_im[tm * V + jc];
+    const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
+    si = fmaf(ar, si, ai * sr);
+    sr = nr;
+    const float pa = sum_m<M>(q.live ? sr * cr + si * ci : 0.f);
+    const float pb = sum_m<M>(q.live ? si * cr - sr * ci : 0.f);
+    if (q.m == 0 && q.live) {
+      ab[((bT + t) * 2) * V + q.j] = pa * (1.f / M);
+      ab[((bT + t) * 2 + 1) * V + q.j] = pb * (1.f / M);
+    }
+  }
+}
+
+// adjoint of a block from zero at its end: q (to the left) and Q = prod conj(a)
+template <int M, bool SEP>
+__global__ void __launch_bounds__(NT) dscan_bwd_local(sca2_dscan_args p, const float* dab, float* qv, float* Qg) {
+  const Map q = thread_map_c<M>(p);
+  const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
+  const int t0 = k * CK, n = min(CK, T - t0);
+  const int jc = q.live ? q.j : 0;
+  const int64_t bT = (int64_t)q.b * T;
+  constexpr float iM = 1.f / M;
+  float dr = 0.f, di = 0.f, Pr = 1.f, Pi = 0.f;
+#pragma unroll 4
+  for (int u = n - 1; u >= 0; --u) {
+    const int t = t0 + u;
+    const int64_t tm = (bT + t) * M + q.m;
+    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+    const float gA = dab[((bT + t) * 2) * V + jc] * iM, gB = dab[((bT + t) * 2 + 1) * V + jc] * iM;
+    const float cr = SEP ? p.c_re[tm] : p.c_re[tm * V + jc];
+    const float ci = SEP ? p.c_im[tm] : p.c_im[tm * V + jc];
+    dr += gA * cr - gB * ci;
+    di += gA * ci + gB * cr;
+    const float nr = ar * dr + ai * di;
+    di = -ai * dr + ar * di;
+    dr = nr;
+    const float qr = ar * Pr + ai * Pi;  // conj(a) * P
+    Pi = ar * Pi - ai * Pr;
+    Pr = qr;
+  }
+  if (!q.live) return;
+  const int64_t base = ((int64_t)q.b * NK + k) * 2;
+  qv[base * M * V + (int64_t)q.m * V + q.j] = dr;
+  qv[(base + 1) * M * V + (int64_t)q.m * V + q.j] = di;
+  if (q.j % (V / G) == 0) {
+    Qg[base * M * G + (int64_t)q.m * G + q.g] = Pr;
+    Qg[(base + 1) * M * G + (int64_t)q.m * G + q.g] = Pi;
+  }
+}
+
+// reverse fold: R(k) = adjoint entering block k from the right; R(-1) = dS0
+template <int M>
+__global__ void __launch_bounds__(NT) dscan_bwd_carry(sca2_dscan_args p, const float* dS_re, const float* dS_im,
+                                                     const float* qv, const float* Qg, float* R, sca2_dscan_grads gr) {
+  const Map q = thread_map<M>(p);
+  if (!q.live) return;
+  const int V = p.V, G = p.G, NK = (p.T + CK - 1) / CK;
+  const int64_t sidx = ((int64_t)q.b * M + q.m) * V + q.j;
+  float rr = dS_re ? dS_re[sidx] : 0.f, ri = dS_im ? dS_im[sidx] : 0.f;
+#pragma unroll 8
+  for (int k = NK - 1; k >= 0; --k) {
+    const int64_t base = ((int64_t)q.b * NK + k) * 2;
+    R[base * M * V + (int64_t)q.m * V + q.j] = rr;
+    R[(base + 1) * M * V + (int64_t)q.m * V + q.j] = ri;
+    const float Pr = Qg[base * M * G + (int64_t)q.m * G + q.g], Pi = Qg[(base + 1) * M * G + (int64_t)q.m * G + q.g];
+    const float xr = qv[base * M * V + (int64_t)q.m * V + q.j], xi = qv[(base + 1) * M * V + (int64_t)q.m * V + q.j];
+    const float nr = Pr * rr - Pi * ri + xr;
+    ri = Pr * ri + Pi * rr + xi;
+    rr = nr;
+  }
+  if (gr.dS0_re) gr.dS0_re[sidx] = rr;
+  if (gr.dS0_im) gr.dS0_im[sidx] = ri;
+}
+
+// gradient pass of one block from its incoming adjoint R(k)
+template <int M, bool SEP>
+__global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const float* dab, const float* ckpt,
+                                                     const float* R, sca2_dscan_grads gr) {
+  const Map q = thread_map_c<M>(p);
+  const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
+  const int t0 = k * CK, n = min(CK, T - t0);
+  const int jc = q.live ? q.j : 0;
+  const int64_t bT = (int64_t)q.b * T;
+  const int64_t base = ((int64_t)q.b * NK + k) * 2;
+  constexpr float iM = 1.f / M;
+  float dsr = q.live ? R[base * M * V + (int64_t)q.m * V + jc] : 0.f;
+  float dsi = q.live ? R[(base + 1) * M * V + (int64_t)q.m * V + jc] : 0.f;
+  float pr[CK], pi[CK];
+  {
+    float sr = ckpt[base * M * V + (int64_t)q.m * V + jc], si = ckpt[(base + 1) * M * V + (int64_t)q.m * V + jc];
+#pragma unroll
+    for (int u = 0; u < CK; ++u) {
+      pr[u] = sr;
+      pi[u] = si;
+      if (u < n) {
+        const int64_t tm = (bT + t0 + u) * M + q.m;
+        const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+        const float vt = p.v[(bT + t0 + u) * V + jc];
+        const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
+        si = fmaf(ar, si, ai * sr);
+        sr = nr;
+      }
+    }
+  }
+#pragma unroll
+  for (int u = CK - 1; u >= 0; --u) {
+    if (u >= n) continue;
+    const int t = t0 + u;
+    const int64_t tm = (bT + t) * M + q.m;
+    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+    const float vt = p.v[(bT + t) * V + jc];
+    const float sr = fmaf(ar, pr[u], fmaf(-ai, pi[u], vt)), si = fmaf(ar, pi[u], ai * pr[u]);
+    const float gA = dab[((bT + t) * 2) * V + jc] * iM, gB = dab[((bT + t) * 2 + 1) * V + jc] * iM;
+    const float cr = SEP ? p.c_re[tm] : p.c_re[tm * V + jc];
+    const float ci = SEP ? p.c_im[tm] : p.c_im[tm * V + jc];
+    dsr = q.live ? dsr + gA * cr - gB * ci : 0.f;
+    dsi = q.live ? dsi + gA * ci + gB * cr : 0.f;
+    const float dcr = q.live ? gA * sr + gB * si : 0.f, dci = q.live ? gA * si - gB * sr : 0.f;
+    if (SEP) {
+      const float xr = sum_j<M>(dcr), xi = sum_j<M>(dci);
+      if (q.jj == 0) {
+        atomicAdd(gr.dc_re + tm, xr);
+        atomicAdd(gr.dc_im + tm, xi);
+      }
+    } else if (q.live) {
+      gr.dc_re[tm * V + q.j] = dcr;
+      gr.dc_im[tm * V + q.j] = dci;
+    }
+    const float dvt = sum_m<M>(dsr);
+    if (q.m == 0 && q.live) gr.dv[(bT + t) * V + q.j] = dvt;
+    const float dar = sum_j<M>(dsr * pr[u] + dsi * pi[u]);
+    const float dai = sum_j<M>(-dsr * pi[u] + dsi * pr[u]);
+    if (q.jj == 0) {
+      atomicAdd(gr.da_re + tm * G + q.g, dar);
+      atomicAdd(gr.da_im + tm * G + q.g, dai);
+    }
+    const float ndr = ar * dsr + ai * dsi;
+    dsi = -ai * dsr + ar * dsi;
+    dsr = ndr;
+  }
+}
+
+// the chunk-parallel form pays off once there are several blocks per sequence
+inline bool use_blocks(const sca2_dscan_args& p, const float* work) {
+  return work != nullptr && p.T > 4 * CK && (p.T + CK - 1) / CK <= 65535;
+}
+
+template <int M>
+cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
                          cudaStream_t st) {
-  const int per_b = M * p.V;
-  dim3 grid(p.B, (per_b + NT - 1) / NT);
+  const int per_b = M * p.V, NK = (p.T + CK - 1) / CK;
+  if (!use_blocks(p, work)) {  // short sequences (and decode): one sequential pass
+    dim3 grid(p.B, (per_b + NT - 1) / NT);
+    if (p.sep)
+      dscan_fwd_kernel<M, true><<<grid, NT, 0, st>>>(p, ab, S_re, S_im, ckpt);
+    else
+      dscan_fwd_kernel<M, false><<<grid, NT, 0, st>>>(p, ab, S_re, S_im, ckpt);
+    return cudaGetLastError();
+  }
+  float* e = work;
+  float* P = e + (size_t)p.B * NK * 2 * M * p.V;
+  float* ck = ckpt ? ckpt : P + (size_t)p.B * NK * 2 * M * p.G;  // inference: checkpoints in the workspace
+  dim3 gl(p.B, NK, (per_b + NT - 1) / NT), gc(p.B, (per_b + NT - 1) / NT);
+  dscan_fwd_local<M><<<gl, NT, 0, st>>>(p, e, P);
+  dscan_fwd_carry<M><<<gc, NT, 0, st>>>(p, e, P, ck, S_re, S_im);
   if (p.sep)
-    dscan_fwd_kernel<M, true><<<grid, NT, 0, st>>>(p, ab, S_re, S_im, ckpt);
+    dscan_fwd_out<M, true><<<gl, NT, 0, st>>>(p, ck, ab);
   else
-    dscan_fwd_kernel<M, false><<<grid, NT, 0, st>>>(p, ab, S_re, S_im, ckpt);
+    dscan_fwd_out<M, false><<<gl, NT, 0, st>>>(p, ck, ab);
   return cudaGetLastError();
 }
 template <int M>
 cudaError_t launch_bwd_m(const sca2_dscan_args& p, const float* dab, const float* dS_re, const float* dS_im,
-                         const float* ckpt, const sca2_dscan_grads& g, cudaStream_t st) {
-  const int per_b = M * p.V;
-  dim3 grid(p.B, (per_b + NT - 1) / NT);
+                         const float* ckpt, float* work, const sca2_dscan_grads& g, cudaStream_t st) {
+  const int per_b = M * p.V, NK = (p.T + CK - 1) / CK;
+  if (!use_blocks(p, work)) {
+    dim3 grid(p.B, (per_b + NT - 1) / NT);
+    if (p.sep)
+      dscan_bwd_kernel<M, true><<<grid, NT, 0, st>>>(p, dab, dS_re, dS_im, ckpt, g);
+    else
+      dscan_bwd_kernel<M, false><<<grid, NT, 0, st>>>(p, dab, dS_re, dS_im, ckpt, g);
+    return cudaGetLastError();
+  }
+  float* qv = work;
+  float* R = qv + (size_t)p.B * NK * 2 * M * p.V;
+  float* Qg = R + (size_t)p.B * NK * 2 * M * p.V;
+  dim3 gl(p.B, NK, (per_b + NT - 1) / NT), gc(p.B, (per_b + NT - 1) / NT);
   if (p.sep)
-    dscan_bwd_kernel<M, true><<<grid, NT, 0, st>>>(p, dab, dS_re, dS_im, ckpt, g);
+    dscan_bwd_local<M, true><<<gl, NT, 0, st>>>(p, dab, qv, Qg);
   else
-    dscan_bwd_kernel<M, false><<<grid, NT, 0, st>>>(p, dab, dS_re, dS_im, ckpt, g);
+    dscan_bwd_local<M, false><<<gl, NT, 0, st>>>(p, dab, qv, Qg);
+  dscan_bwd_carry<M><<<gc, NT, 0, st>>>(p, dS_re, dS_im, qv, Qg, R, g);
+  if (p.sep)
+    dscan_bwd_block<M, true><<<gl, NT, 0, st>>>(p, dab, ckpt, R, g);
+  else
+    dscan_bwd_block<M, false><<<gl, NT, 0, st>>>(p, dab, ckpt, R, g);
   return cudaGetLastError();
 }
 
 }  // namespace dscan
 
-cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, cudaStream_t st) {
+// workspace of the chunk-parallel forms (floats): fwd e + P (+ checkpoints when the caller
+// keeps none), bwd q + R + Q
+size_t dscan_work_floats(int B, int T, int M, int G, int V) {
+  const size_t NK = (size_t)((T + dscan::CK - 1) / dscan::CK);
+  return (size_t)B * NK * 2 * (2 * (size_t)M * V + (size_t)M * G);
+}
+
+cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
+                      cudaStream_t st) {
   switch (p.M) {
-    case 1: return dscan::launch_fwd_m<1>(p, ab, S_re, S_im, ckpt, st);
-    case 2: return dscan::launch_fwd_m<2>(p, ab, S_re, S_im, ckpt, st);
-    case 4: return dscan::launch_fwd_m<4>(p, ab, S_re, S_im, ckpt, st);
-    case 8: return dscan::launch_fwd_m<8>(p, ab, S_re, S_im, ckpt, st);
-    case 16: return dscan::launch_fwd_m<16>(p, ab, S_re, S_im, ckpt, st);
-    case 32: return dscan::launch_fwd_m<32>(p, ab, S_re, S_im, ckpt, st);
+    case 1: return dscan::launch_fwd_m<1>(p, ab, S_re, S_im, ckpt, work, st);
+    case 2: return dscan::launch_fwd_m<2>(p, ab, S_re, S_im, ckpt, work, st);
+    case 4: return dscan::launch_fwd_m<4>(p, ab, S_re, S_im, ckpt, work, st);
+    case 8: return dscan::launch_fwd_m<8>(p, ab, S_re, S_im, ckpt, work, st);
+    case 16: return dscan::launch_fwd_m<16>(p, ab, S_re, S_im, ckpt, work, st);
+    case 32: return dscan::launch_fwd_m<32>(p, ab, S_re, S_im, ckpt, work, st);
   }
   return cudaErrorInvalidValue;
 }
 cudaError_t dscan_bwd(const sca2_dscan_args& p, const float* dab, const float* dS_re, const float* dS_im,
-                      const float* ckpt, const sca2_dscan_grads& g, cudaStream_t st) {
+                      const float* ckpt, float* work, const sca2_dscan_grads& g, cudaStream_t st) {
   switch (p.M) {
-    case 1: return dscan::launch_bwd_m<1>(p, dab, dS_re, dS_im, ckpt, g, st);
-    case 2: return dscan::launch_bwd_m<2>(p, dab, dS_re, dS_im, ckpt, g, st);
-    case 4: return dscan::launch_bwd_m<4>(p, dab, dS_re, dS_im, ckpt, g, st);
-    case 8: return dscan::launch_bwd_m<8>(p, dab, dS_re, dS_im, ckpt, g, st);
-    case 16: return dscan::launch_bwd_m<16>(p, dab, dS_re, dS_im, ckpt, g, st);
-    case 32: return dscan::launch_bwd_m<32>(p, dab, dS_re, dS_im, ckpt, g, st);
+    case 1: return dscan::launch_bwd_m<1>(p, dab, dS_re, dS_im, ckpt, work, g, st);
+    case 2: return dscan::launch_bwd_m<2>(p, dab, dS_re, dS_im, ckpt, work, g, st);
+    case 4: return dscan::launch_bwd_m<4>(p, dab, dS_re, dS_im, ckpt, work, g, st);
+    case 8: return dscan::launch_bwd_m<8>(p, dab, dS_re, dS_im, ckpt, work, g, st);
+    case 16: return dscan::launch_bwd_m<16>(p, dab, dS_re, dS_im, ckpt, work, g, st);
+    case 32: return dscan::launch_bwd_m<32>(p, dab, dS_re, dS_im, ckpt, work, g, st);
   }
   return cudaErrorInvalidValue;
 }

@@ -358,9 +358,16 @@ def _dscan_args(a_re, a_im, v, c_re, c_im, S0, sep):
     return a
 
 
+def _dscan_work(lib, B, T, M, G, V, device, blocks):
+    if not blocks:
+        return None
+    n = lib.sca2_dscan_work_bytes(B, T, M, G, V)
+    return torch.empty((n + 3) // 4, device=device, dtype=torch.float32) if n > 0 else None
+
+
 class _DScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep):
+    def forward(ctx, a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep, blocks):
         B, T, M, G = a_re.shape
         V = v.shape[-1]
         S0 = (S0_re, S0_im) if S0_re is not None else None
@@ -371,11 +378,12 @@ class _DScan(torch.autograd.Function):
         lib = _lib.load()
         need = any(ctx.needs_input_grad)
         ck = torch.empty(B, lib.sca2_dscan_num_ckpt(T), 2, M, V, device=v.device) if need else None
+        wk = _dscan_work(lib, B, T, M, G, V, v.device, blocks)
         _lib.check(lib.sca2_dscan_fwd(C_ref(a), ab.data_ptr(), S_re.data_ptr(), S_im.data_ptr(), _ptr(ck),
-                                      _stream()), "dscan_fwd")
+                                      _ptr(wk), _stream()), "dscan_fwd")
         if need:
             ctx.save_for_backward(a_re, a_im, v, c_re, c_im, S0_re, S0_im, ck)
-            ctx.sep = sep
+            ctx.sep, ctx.blocks = sep, blocks
         return ab, S_re, S_im
 
     @staticmethod
@@ -395,21 +403,26 @@ class _DScan(torch.autograd.Function):
         dab = dab.contiguous() if dab is not None else torch.zeros(*a_re.shape[:2], 2, v.shape[-1], device=v.device)
         dS_re = dS_re.contiguous() if dS_re is not None else None
         dS_im = dS_im.contiguous() if dS_im is not None else None
-        _lib.check(_lib.load().sca2_dscan_bwd(C_ref(a), dab.data_ptr(), _ptr(dS_re), _ptr(dS_im), ck.data_ptr(),
-                                              C_ref(g), _stream()), "dscan_bwd")
-        return da_re, da_im, dv, dc_re, dc_im, dS0_re, dS0_im, None
+        lib = _lib.load()
+        B, T, M, G = a_re.shape
+        wk = _dscan_work(lib, B, T, M, G, v.shape[-1], v.device, ctx.blocks)
+        _lib.check(lib.sca2_dscan_bwd(C_ref(a), dab.data_ptr(), _ptr(dS_re), _ptr(dS_im), ck.data_ptr(),
+                                      C_ref(g), _ptr(wk), _stream()), "dscan_bwd")
+        return da_re, da_im, dv, dc_re, dc_im, dS0_re, dS0_im, None, None
 
 
-def dscan(a_re, a_im, v, c_re, c_im, S0: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, sep: bool = False):
+def dscan(a_re, a_im, v, c_re, c_im, S0: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, sep: bool = False,
+          blocks: bool = True):
     """D-head diagonal scan (sca2/ref.py:239-275, sca2/arch_sepq.py:110-178): complex gate
     a (B,T,M,G), values v (B,T,V), read coefficients c (B,T,M,V), or (B,T,M) with sep,
     initial state (sr, si) each (B,M,V) -> ab (B,T,2,V) = [A | Bv] and the final (sr, si).
-    fp32; differentiable in every input."""
+    fp32; differentiable in every input.  blocks=True runs long sequences as 16-token blocks
+    in parallel (a small workspace); False keeps one sequential pass per (b, m, j)."""
     _need_cuda(a_re, a_im, v, c_re, c_im, *(S0 or ()))
     f = lambda x: x.to(torch.float32).contiguous()
     a_re, a_im, v, c_re, c_im = f(a_re), f(a_im), f(v), f(c_re), f(c_im)
     S0_re, S0_im = (f(S0[0]), f(S0[1])) if S0 is not None else (None, None)
-    ab, S_re, S_im = _DScan.apply(a_re, a_im, v, c_re, c_im, S0_re, S0_im, bool(sep))
+    ab, S_re, S_im = _DScan.apply(a_re, a_im, v, c_re, c_im, S0_re, S0_im, bool(sep), bool(blocks))
     return ab, (S_re, S_im)
 
 

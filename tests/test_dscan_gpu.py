@@ -11,14 +11,17 @@ from tests.golden import fixtures as fx
 
 pytestmark = pytest.mark.gpu
 
-CASES = [  # B, T, M, G, V, sep
+CASES = [  # B, T, M, G, V, sep  (T > 64: 16-token blocks in parallel; otherwise one pass)
     (2, 45, 4, 4, 32, False), (2, 37, 8, 4, 16, True), (1, 100, 16, 8, 64, True),
     (3, 16, 1, 1, 32, False), (2, 5, 32, 16, 32, False), (2, 33, 2, 2, 32, True),
+    (2, 203, 4, 4, 32, False), (2, 150, 32, 16, 32, True), (1, 1001, 16, 8, 64, True),
+    (2, 65, 8, 2, 64, False), (1, 80, 1, 1, 32, True),
 ]
 
 
+@pytest.mark.parametrize("blocks", [True, False])
 @pytest.mark.parametrize("case", CASES)
-def test_dscan_vs_oracle(case):
+def test_dscan_vs_oracle(case, blocks):
     from sca2_b200 import ops
     B, T, M, G, V, sep = case
     rng = np.random.default_rng(B * T + M)
@@ -30,7 +33,7 @@ def test_dscan_vs_oracle(case):
     dab = rng.standard_normal((B, T, 2, V))
     dS = (rng.standard_normal((B, M, V)), rng.standard_normal((B, M, V)))
     t = [cuda(x, torch.float32, True) for x in (a_re, a_im, v, c_re, c_im, S0[0], S0[1])]
-    ab, (sr, si) = ops.dscan(t[0], t[1], t[2], t[3], t[4], (t[5], t[6]), sep=sep)
+    ab, (sr, si) = ops.dscan(t[0], t[1], t[2], t[3], t[4], (t[5], t[6]), sep=sep, blocks=blocks)
     ((ab * cuda(dab)).sum() + (sr * cuda(dS[0])).sum() + (si * cuda(dS[1])).sum()).backward()
     rab, (rsr, rsi) = dor.dscan_forward(a_re, a_im, v, c_re, c_im, S0, sep=sep)
     g = dor.dscan_backward(a_re, a_im, v, c_re, c_im, S0, dab, dS, sep=sep)
@@ -74,3 +77,26 @@ def test_dscan_empty_and_unsupported():
         ops.dscan(z(1, 3, 3, 1), z(1, 3, 3, 1), z(1, 3, 32), z(1, 3, 3, 32), z(1, 3, 3, 32))
     with pytest.raises(_lib.Sca2Error):  # 4 channels per group < 32 / M = 8
         ops.dscan(z(1, 3, 4, 8), z(1, 3, 4, 8), z(1, 3, 32), z(1, 3, 4, 32), z(1, 3, 4, 32))
+
+
+@pytest.mark.parametrize("sep", [True, False])
+def test_dscan_blocks_long_sequence(sep):
+    """The block-parallel form against the sequential one on a long sequence (no oracle at
+    this size): read, final state and every gradient agree to fp32 rounding."""
+    from sca2_b200 import ops
+    B, T, M, G, V = 2, 4096, 16, 8, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rn = lambda *sh: torch.randn(*sh, device="cuda", generator=g)
+    mag = torch.exp(-torch.nn.functional.softplus(rn(B, T, M, G)))
+    ph = rn(B, T, M, G)
+    cs = (B, T, M) if sep else (B, T, M, V)
+    base = [mag * torch.cos(ph), mag * torch.sin(ph), rn(B, T, V), rn(*cs), rn(*cs), rn(B, M, V), rn(B, M, V)]
+    dab, dS = rn(B, T, 2, V), (rn(B, M, V), rn(B, M, V))
+    res = []
+    for blocks in (True, False):
+        t = [x.clone().requires_grad_(True) for x in base]
+        ab, (sr, si) = ops.dscan(*t[:5], (t[5], t[6]), sep=sep, blocks=blocks)
+        ((ab * dab).sum() + (sr * dS[0]).sum() + (si * dS[1]).sum()).backward()
+        res.append([ab.detach(), sr.detach(), si.detach()] + [x.grad for x in t])
+    for a, b in zip(*res):
+        assert relerr(a, b) < TOL_F32
