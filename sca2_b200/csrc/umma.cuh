@@ -76,22 +76,43 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, u
       : "memory");
 }
 
+// The descriptors of one operand differ between K steps only in the start-address field (low
+// 14 bits, address >> 4; shared-memory addresses stay below 256 KB so the field never carries
+// into LBO).  The issue loops therefore build the two 32-bit halves once per product and add
+// the K-step stride to the low half: one integer add per operand and step instead of the
+// 64-bit shifts and masks of sdesc, which kept the single issuing thread busy for tens of
+// cycles per instruction.
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t desc_hi(uint32_t sbo_bytes) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14);  // bit 46 of the descriptor: sm100 version
+}
+__device__ __forceinline__ uint64_t desc_pack(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+
 // D = A(M x Kt) * B(N x Kt)^T over all K steps; A, B K-major in smem; issued by ONE thread
 __device__ __forceinline__ void gemm(uint32_t tmem_d, const void* A, const void* B, int M, int N, int Kt,
                                      bool accumulate) {
-  const uint32_t a = smem_u32(A), b = smem_u32(B), id = idesc_bf16(M, N);
+  const uint32_t id = idesc_bf16(M, N), hi = desc_hi((uint32_t)(Kt >> 3) * 128u);
+  const uint32_t a = desc_lo(smem_u32(A), 128u), b = desc_lo(smem_u32(B), 128u);
+#pragma unroll
   for (int kk = 0; kk < Kt / 16; ++kk)
-    mma(tmem_d, kdesc(a, Kt, kk), kdesc(b, Kt, kk), id, (accumulate || kk > 0) ? 1u : 0u);
+    mma(tmem_d, desc_pack(a + 16u * kk, hi), desc_pack(b + 16u * kk, hi), id, (accumulate || kk > 0) ? 1u : 0u);
 }
 
 // D (+)= A * B^T where each operand is K-major (rows of its own K elements) or MN-major (the
 // K-major buffer of its transpose, see mdesc).  M x Kt and N x Kt; issued by ONE thread.
 __device__ __forceinline__ void gemm_t(uint32_t tmem_d, const void* A, bool a_mn, const void* B, bool b_mn, int M,
                                        int N, int Kt, bool accumulate) {
-  const uint32_t a = smem_u32(A), b = smem_u32(B), id = idesc_bf16_t(M, N, a_mn, b_mn);
+  const uint32_t id = idesc_bf16_t(M, N, a_mn, b_mn);
+  const uint32_t ahi = a_mn ? desc_hi(128u) : desc_hi((uint32_t)(Kt >> 3) * 128u);
+  const uint32_t bhi = b_mn ? desc_hi(128u) : desc_hi((uint32_t)(Kt >> 3) * 128u);
+  const uint32_t a = a_mn ? desc_lo(smem_u32(A), (uint32_t)M * 16u) : desc_lo(smem_u32(A), 128u);
+  const uint32_t b = b_mn ? desc_lo(smem_u32(B), (uint32_t)N * 16u) : desc_lo(smem_u32(B), 128u);
+  const uint32_t as = a_mn ? 2u * (uint32_t)M : 16u, bs = b_mn ? 2u * (uint32_t)N : 16u;  // K-step strides >> 4
+#pragma unroll
   for (int kk = 0; kk < Kt / 16; ++kk)
-    mma(tmem_d, a_mn ? mdesc(a, M, kk) : kdesc(a, Kt, kk), b_mn ? mdesc(b, N, kk) : kdesc(b, Kt, kk), id,
-        (accumulate || kk > 0) ? 1u : 0u);
+    mma(tmem_d, desc_pack(a + as * kk, ahi), desc_pack(b + bs * kk, bhi), id, (accumulate || kk > 0) ? 1u : 0u);
 }
 
 // arrive on `mbar` once every MMA issued so far by this thread has completed
