@@ -212,6 +212,56 @@ SCA2_API int sca2_dscan_bwd(const sca2_dscan_args* a, const float* dab, const fl
                    const float* dS_im, const float* ckpt, const sca2_dscan_grads* g,
                    void* work, void* stream);
 
+/* ---- short head: exact L-tap window read ---------------------------------------------------
+ *   phi_t = kh_t theta + ((pos + t) mod L) omega,   psi_t = kz_t theta + ((pos + t) mod L) omega
+ *   kappa(t,s) = (1/L) sum_m (wr + i wi)_m exp(i (phi_s - psi_t))
+ *   o_t = [ sum_{s=t-L+1..t} Re kappa(t,s) e_s | sum Im kappa(t,s) e_s ]       (B,T,2dv)
+ * The write / read / decode of lapa.layer.ShortHead (lapa/layer.py:418-545: _phase :444,
+ * _read :450, _banded :488, step :524) and sca2.arch_short.CHeadShort (sca2/arch_short.py:
+ * 45-158).  The L-1 previous writes are the ring buffer c0 = cos phi, s0 = sin phi,
+ * e0 = value (oldest first).  All tensors fp32, contiguous; 1 <= L <= 32, any dv. */
+typedef struct sca2_short_args {
+  int32_t B, T, L, dv;
+  const int64_t* pos;   /* device scalar: position of token 0 (the state's "pos"), or NULL = 0 */
+  const float* kh;      /* (B,T,L) K(h): content of the write phase */
+  const float* kz;      /* (B,T,L) K(z): content of the read phase */
+  const float* v;       /* (B,T,dv) V(z): the values written */
+  const float* theta;   /* (L) */
+  const float* omega;   /* (L) the DFT grid 2 pi m / L */
+  const float* wr;      /* (L) read weights */
+  const float* wi;
+  const float* c0;      /* (B,L-1,L) ring buffer, or NULL = init_state (c = 1, s = 0, e = 0) */
+  const float* s0;
+  const float* e0;      /* (B,L-1,dv) */
+} sca2_short_args;
+
+/* Gradients of sca2_short_bwd, all WRITTEN (no zero-fill needed); dc0/ds0/de0 may be NULL. */
+typedef struct sca2_short_grads {
+  float* dkh;           /* (B,T,L) */
+  float* dkz;           /* (B,T,L) */
+  float* dv;            /* (B,T,dv) */
+  float* dtheta;        /* (L) */
+  float* dwr;           /* (L) */
+  float* dwi;           /* (L) */
+  float* dc0;           /* (B,L-1,L) */
+  float* ds0;
+  float* de0;           /* (B,L-1,dv) */
+} sca2_short_grads;
+
+/* Forward: o (B,T,2dv), or NULL when T = 0; c1, s1 (B,L-1,L) and e1 (B,L-1,dv) the new ring
+ * buffer (the last L-1 writes of buffer + call), or NULL to skip it.  Outputs must not alias
+ * inputs.  T = 1 is the decode step (ShortHead.step, CHeadShort.step). */
+SCA2_API int sca2_short_fwd(const sca2_short_args* a, float* o, float* c1, float* s1, float* e1,
+                   void* stream);
+
+/* Bytes of the workspace sca2_short_bwd needs (per-CTA partial sums of the L-vectors). */
+SCA2_API int64_t sca2_short_work_bytes(int32_t B, int32_t T, int32_t L, int32_t dv);
+
+/* Backward: dO (B,T,2dv); dc1, ds1, de1 gradients of the new ring buffer or NULL. */
+SCA2_API int sca2_short_bwd(const sca2_short_args* a, const float* dO, const float* dc1,
+                   const float* ds1, const float* de1, const sca2_short_grads* g, void* work,
+                   void* stream);
+
 /* Size of the device array behind sca2_scan_fwd_bwd_noalloc (every GPU that loads the
  * library holds it until the process exits). */
 #define SCA2_NOALLOC_SCRATCH_BYTES (16u << 20)

@@ -53,6 +53,23 @@ class DScanArgs(C.Structure):
     ]
 
 
+class ShortArgs(C.Structure):
+    _fields_ = [
+        ("B", C.c_int32), ("T", C.c_int32), ("L", C.c_int32), ("dv", C.c_int32),
+        ("pos", C.c_void_p), ("kh", C.c_void_p), ("kz", C.c_void_p), ("v", C.c_void_p),
+        ("theta", C.c_void_p), ("omega", C.c_void_p), ("wr", C.c_void_p), ("wi", C.c_void_p),
+        ("c0", C.c_void_p), ("s0", C.c_void_p), ("e0", C.c_void_p),
+    ]
+
+
+class ShortGrads(C.Structure):
+    _fields_ = [
+        ("dkh", C.c_void_p), ("dkz", C.c_void_p), ("dv", C.c_void_p), ("dtheta", C.c_void_p),
+        ("dwr", C.c_void_p), ("dwi", C.c_void_p), ("dc0", C.c_void_p), ("ds0", C.c_void_p),
+        ("de0", C.c_void_p),
+    ]
+
+
 class DScanGrads(C.Structure):
     _fields_ = [
         ("da_re", C.c_void_p), ("da_im", C.c_void_p), ("dv", C.c_void_p), ("dc_re", C.c_void_p),
@@ -77,6 +94,11 @@ SIGNATURES = [
                                  C.c_void_p, C.c_void_p]),
     ("sca2_dscan_bwd", C.c_int, [C.POINTER(DScanArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                  C.POINTER(DScanGrads), C.c_void_p, C.c_void_p]),
+    ("sca2_short_fwd", C.c_int, [C.POINTER(ShortArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p]),
+    ("sca2_short_work_bytes", C.c_int64, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    ("sca2_short_bwd", C.c_int, [C.POINTER(ShortArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.POINTER(ShortGrads), C.c_void_p, C.c_void_p]),
     ("sca2_scan_fwd_bwd_noalloc", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, Out, C.c_void_p,
                                             C.POINTER(ScanGrads), C.c_void_p]),
     ("sca2_fault_status", C.c_int, [C.POINTER(C.c_uint32)]),

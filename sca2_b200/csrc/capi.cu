@@ -37,6 +37,13 @@ cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S
 cudaError_t dscan_bwd(const sca2_dscan_args& p, const float* dab, const float* dS_re, const float* dS_im,
                       const float* ckpt, float* work, const sca2_dscan_grads& g, cudaStream_t st);
 cudaError_t tc_read_faults_prep(unsigned int* out);
+// short.cu
+int short_tokens_per_cta(int L, bool bwd, int max_smem);
+size_t short_work_floats(int B, int T, int L, int max_smem);
+cudaError_t short_fwd(const sca2_short_args& p, float* o, float* c1, float* s1, float* e1, int max_smem,
+                      cudaStream_t st);
+cudaError_t short_bwd(const sca2_short_args& p, const float* dO, const float* dc1, const float* ds1,
+                      const float* de1, const sca2_short_grads& g, float* work, int max_smem, cudaStream_t st);
 // scan_tc_bwd.cu
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
@@ -283,6 +290,62 @@ int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D, 
   if (N == 0) return SCA2_OK;
   cudaError_t e = sca2::launch_rms_bwd(x, du, dx, N, D, eps, io_dtype, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "sca2_rms_bwd");
+  return SCA2_OK;
+}
+
+static int check_short(const sca2_short_args* a) {
+  if (!a) return fail(SCA2_ERR_ARG, "null short-head args");
+  if (a->B < 1 || a->T < 0 || a->L < 1 || a->dv < 1) return fail(SCA2_ERR_ARG, "short: bad sizes");
+  if (a->L > 32) return fail(SCA2_ERR_UNSUPPORTED, "short: window L must be <= 32");
+  if (a->T > 0 && (!a->kh || !a->kz || !a->v)) return fail(SCA2_ERR_ARG, "short: null input");
+  if (!a->theta || !a->omega || !a->wr || !a->wi) return fail(SCA2_ERR_ARG, "short: null parameter");
+  if ((a->c0 == nullptr) != (a->s0 == nullptr)) return fail(SCA2_ERR_ARG, "short: c0 and s0 go together");
+  if (sca2::short_tokens_per_cta(a->L, true, max_optin_smem()) == 0)
+    return fail(SCA2_ERR_UNSUPPORTED, "short: window too large for shared memory");
+  return SCA2_OK;
+}
+
+int sca2_short_fwd(const sca2_short_args* a, float* o, float* c1, float* s1, float* e1, void* stream) {
+  int rc = check_short(a);
+  if (rc) return rc;
+  if (a->T > 0 && !o) return fail(SCA2_ERR_ARG, "short: null output");
+  if ((c1 == nullptr) != (s1 == nullptr) || (c1 == nullptr) != (e1 == nullptr))
+    return fail(SCA2_ERR_ARG, "short: pass all of c1, s1, e1 or none");
+  cudaError_t e = sca2::short_fwd(*a, o, c1, s1, e1, max_optin_smem(), reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_short_fwd");
+  return SCA2_OK;
+}
+
+int64_t sca2_short_work_bytes(int32_t B, int32_t T, int32_t L, int32_t dv) {
+  if (B < 1 || T < 1 || L < 1 || L > 32 || dv < 1) return 0;
+  return (int64_t)(sca2::short_work_floats(B, T, L, max_optin_smem()) * sizeof(float));
+}
+
+int sca2_short_bwd(const sca2_short_args* a, const float* dO, const float* dc1, const float* ds1,
+                   const float* de1, const sca2_short_grads* g, void* work, void* stream) {
+  int rc = check_short(a);
+  if (rc) return rc;
+  if (!g || !g->dtheta || !g->dwr || !g->dwi) return fail(SCA2_ERR_ARG, "short: null gradient buffer");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int n = a->L - 1;
+  if (a->T == 0) {  // the new buffer is the old one
+    cudaError_t e = cudaSuccess;
+    const size_t nl = (size_t)a->B * n * a->L * sizeof(float), nd = (size_t)a->B * n * a->dv * sizeof(float);
+    auto pass = [&](float* dst, const float* src, size_t bytes) {
+      if (dst && e == cudaSuccess && bytes)
+        e = src ? cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(dst, 0, bytes, st);
+    };
+    pass(g->dc0, dc1, nl);
+    pass(g->ds0, ds1, nl);
+    pass(g->de0, de1, nd);
+    for (float* x : {g->dtheta, g->dwr, g->dwi})
+      if (e == cudaSuccess) e = cudaMemsetAsync(x, 0, (size_t)a->L * sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_short_bwd(T=0)");
+    return SCA2_OK;
+  }
+  if (!dO || !g->dkh || !g->dkz || !g->dv || !work) return fail(SCA2_ERR_ARG, "short: null dO, gradient or workspace");
+  cudaError_t e = sca2::short_bwd(*a, dO, dc1, ds1, de1, *g, static_cast<float*>(work), max_optin_smem(), st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_short_bwd");
   return SCA2_OK;
 }
 

@@ -19,6 +19,8 @@ hand-written kernels.  State dicts are the reference's: {"sr", "si"} fp32 plus a
   CHeadGated        sca2/arch_gatedc.py:58-193       (H heads, scalar decay, additive)
   DHeadRef          sca2/ref.py:209-275              (D head: complex diagonal scan)
   DHeadSepQ(Polar)  sca2/arch_sepq.py:46-290         (D head, separable query; polar gate)
+  ShortHead         lapa/layer.py:418-545            (exact L-tap window over a ring buffer)
+  CHeadShort        sca2/arch_short.py:45-158        (the same read in the SCA2 D slot)
 """
 from __future__ import annotations
 
@@ -506,3 +508,71 @@ class DHeadSepQPolar(DHeadSepQ):
         mag = torch.exp(-F.softplus(self.gr(h))).view(B, T, self.M, self.G)
         ph = self.gi(h).view(B, T, self.M, self.G)
         return mag * torch.cos(ph), mag * torch.sin(ph)
+
+
+# ----------------------------------------------------------------------------------------
+#  short heads: exact L-tap window read over a ring buffer (ops.short_read)
+# ----------------------------------------------------------------------------------------
+class ShortHead(nn.Module):
+    """lapa/layer.py:418-545: the DFT-grid short head.  Phases phi = K(h) theta + (p mod L)
+    omega (write) and psi = K(z) theta + (p mod L) omega (read); the read is the exact window
+    sum over the last L writes, the state the ring buffer of the L-1 previous writes.  Runs in
+    float32 with autocast off (lapa/layer.py:55-56: the Dirichlet comb cancels only in fp32)."""
+
+    def __init__(self, cfg: LaplaceConfig):
+        super().__init__()
+        d, L, dv = cfg.d, cfg.L, cfg.dv
+        self.d, self.L, self.dv = d, L, dv
+        self.K = nn.Linear(d, L, False)
+        self.V = nn.Linear(d, dv, False)
+        self.theta = nn.Parameter((cfg.theta_scale or 0.02) * torch.randn(L))
+        self.wr = nn.Parameter(torch.ones(L))
+        self.wi = nn.Parameter(torch.zeros(L))
+        self.register_buffer("omega", (torch.arange(L, dtype=torch.float64) * (2 * math.pi / L)).float())
+
+    def init_state(self, B: int, device, dtype=torch.float32) -> State:
+        n, L = self.L - 1, self.L
+        return {"c": torch.ones(B, n, L, device=device, dtype=torch.float32),
+                "s": torch.zeros(B, n, L, device=device, dtype=torch.float32),
+                "e": torch.zeros(B, n, self.dv, device=device, dtype=torch.float32),
+                "pos": torch.zeros((), device=device, dtype=torch.long)}
+
+    def _read(self, z, h, state):
+        B, T, _ = z.shape
+        st = state if state is not None else self.init_state(B, z.device)
+        with torch.autocast(device_type="cuda", enabled=False):
+            zf, hf = z.float(), h.float()
+            o, (c, s, e) = ops.short_read(self.K(hf), self.K(zf), self.V(zf), self.theta, self.omega, self.wr,
+                                          self.wi, (st["c"], st["s"], st["e"]), st["pos"])
+        return o, {"c": c, "s": s, "e": e, "pos": st["pos"] + T}
+
+    def prefill(self, z, h, state: Optional[State] = None):
+        o, st = self._read(z, h, state)
+        return _rms(o).to(z.dtype), st
+
+    def forward(self, z, h):
+        return self.prefill(z, h)[0]
+
+    def step(self, z_t, h_t, state: State):
+        u, st = self.prefill(z_t[:, None], h_t[:, None], state)
+        return u[:, 0], st
+
+
+class CHeadShort(ShortHead):
+    """sca2/arch_short.py:45-158: the same window read in the SCA2 D slot, read out through
+    _gated_out (RMS, or raw x rscale, optionally gated; sca2/ref.py:33-50)."""
+
+    def __init__(self, d, L, dv, theta_scale=0.02):
+        nn.Module.__init__(self)
+        self.d, self.L, self.dv = d, L, dv
+        self.K = nn.Linear(d, L, False)
+        self.V = nn.Linear(d, dv, False)
+        self.theta = nn.Parameter(theta_scale * torch.randn(L))
+        self.wr = nn.Parameter(torch.ones(L))
+        self.wi = nn.Parameter(torch.zeros(L))
+        self.register_buffer("omega", (torch.arange(L, dtype=torch.float64) * (2 * math.pi / L))
+                             .to(torch.get_default_dtype()))
+
+    def prefill(self, z, h, state: Optional[State] = None):
+        o, st = self._read(z, h, state)
+        return _gated_out(self, o, z).to(z.dtype), st

@@ -3,6 +3,8 @@
     phase_scan(phw, phq, v, beta, g, lam, wr, wi, S0)     -> o (B,T,H,2,V), S (B,H,2Mh,V)
     key_scan(q, k, v, g, beta, scale, S0, v_times_beta)   -> o (B,T,H,V),   S (B,H,K,V)
     phase_step(...) / key_step(...)                       one decode token, state in place
+    dscan(a_re, a_im, v, c_re, c_im, S0, sep)             D-head diagonal scan
+    short_read(kh, kz, v, theta, omega, wr, wi, state)    short-head window read
     rms(x, eps)                                           per-row RMS read-out
 
 Every op runs the CUDA kernels of libsca2b200.so on the current stream.  There is no
@@ -424,6 +426,78 @@ def dscan(a_re, a_im, v, c_re, c_im, S0: Optional[Tuple[torch.Tensor, torch.Tens
     S0_re, S0_im = (f(S0[0]), f(S0[1])) if S0 is not None else (None, None)
     ab, S_re, S_im = _DScan.apply(a_re, a_im, v, c_re, c_im, S0_re, S0_im, bool(sep), bool(blocks))
     return ab, (S_re, S_im)
+
+
+# ======================================================================================
+#  short head: exact L-tap window read
+# ======================================================================================
+def _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos):
+    B, T, L = kh.shape
+    a = _lib.ShortArgs()
+    a.B, a.T, a.L, a.dv = B, T, L, v.shape[-1]
+    a.pos = _ptr(pos)
+    a.kh, a.kz, a.v = kh.data_ptr(), kz.data_ptr(), v.data_ptr()
+    a.theta, a.omega, a.wr, a.wi = theta.data_ptr(), omega.data_ptr(), wr.data_ptr(), wi.data_ptr()
+    a.c0, a.s0, a.e0 = _ptr(c0), _ptr(s0), _ptr(e0)
+    return a
+
+
+class _ShortRead(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos):
+        B, T, L = kh.shape
+        dv = v.shape[-1]
+        n = L - 1
+        a = _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+        o = torch.empty(B, T, 2 * dv, device=v.device, dtype=torch.float32)
+        c1 = torch.empty(B, n, L, device=v.device, dtype=torch.float32)
+        s1, e1 = torch.empty_like(c1), torch.empty(B, n, dv, device=v.device, dtype=torch.float32)
+        _lib.check(_lib.load().sca2_short_fwd(C_ref(a), o.data_ptr() if T else None, c1.data_ptr(), s1.data_ptr(),
+                                              e1.data_ptr(), _stream()), "short_fwd")
+        ctx.save_for_backward(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+        return o, c1, s1, e1
+
+    @staticmethod
+    def backward(ctx, dO, dc1, ds1, de1):
+        kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos = ctx.saved_tensors
+        B, T, L = kh.shape
+        dv = v.shape[-1]
+        a = _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+        lib = _lib.load()
+        g = _lib.ShortGrads()
+        dkh, dkz, dvv = torch.empty_like(kh), torch.empty_like(kz), torch.empty_like(v)
+        dth, dwr, dwi = torch.empty_like(theta), torch.empty_like(wr), torch.empty_like(wi)
+        dc0 = torch.empty_like(c0) if c0 is not None else None
+        ds0 = torch.empty_like(s0) if s0 is not None else None
+        de0 = torch.empty_like(e0) if e0 is not None else None
+        g.dkh, g.dkz, g.dv = dkh.data_ptr(), dkz.data_ptr(), dvv.data_ptr()
+        g.dtheta, g.dwr, g.dwi = dth.data_ptr(), dwr.data_ptr(), dwi.data_ptr()
+        g.dc0, g.ds0, g.de0 = _ptr(dc0), _ptr(ds0), _ptr(de0)
+        if dO is None:
+            dO = torch.zeros(B, T, 2 * dv, device=v.device)
+        c = lambda x: x.contiguous() if x is not None else None
+        dO, dc1, ds1, de1 = c(dO), c(dc1), c(ds1), c(de1)
+        nw = lib.sca2_short_work_bytes(B, T, L, dv)
+        wk = torch.empty((nw + 3) // 4, device=v.device, dtype=torch.float32) if nw > 0 else None
+        _lib.check(lib.sca2_short_bwd(C_ref(a), dO.data_ptr(), _ptr(dc1), _ptr(ds1), _ptr(de1), C_ref(g), _ptr(wk),
+                                      _stream()), "short_bwd")
+        return dkh, dkz, dvv, dth, None, dwr, dwi, dc0, ds0, de0, None
+
+
+def short_read(kh, kz, v, theta, omega, wr, wi, state=None, pos=None):
+    """Short-head window read (lapa/layer.py:418-545, sca2/arch_short.py:45-158):
+    kh, kz (B,T,L) = K(h), K(z); v (B,T,dv) = V(z); theta, omega, wr, wi (L); state =
+    (c, s, e) ring buffer of the L-1 previous writes or None (init_state); pos a 0-dim
+    integer tensor (position of token 0) or None.  Returns o (B,T,2dv) = [Re | Im] and the
+    new buffer (c, s, e).  fp32; differentiable in kh, kz, v, theta, wr, wi and the state."""
+    _need_cuda(kh, kz, v, theta, omega, wr, wi, *(state or ()))
+    f = lambda x: x.to(torch.float32).contiguous() if x is not None else None
+    kh, kz, v, theta, omega, wr, wi = (f(x) for x in (kh, kz, v, theta, omega, wr, wi))
+    c0, s0, e0 = (f(x) for x in state) if state is not None else (None, None, None)
+    if pos is not None:
+        pos = pos.to(device=v.device, dtype=torch.int64).reshape(())
+    o, c1, s1, e1 = _ShortRead.apply(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+    return o, (c1, s1, e1)
 
 
 # ======================================================================================

@@ -22,7 +22,9 @@ head-level ("head_*.npz")
     random z, h and a random incoming state; the fixture stores its state_dict, the
     inputs, the RMS'd output u, the new state and every parameter / input gradient.
     These pin the drop-in head classes (projections + scan + epilogue).  head_d*.npz are
-    the D heads (DHeadRef, DHeadSepQ, DHeadSepQPolar), with decode steps after the prefill.
+    the D heads (DHeadRef, DHeadSepQ, DHeadSepQPolar), with decode steps after the prefill;
+    head_short_*.npz the short heads (lapa ShortHead, sca2 CHeadShort): prefill with state
+    gradients, a second prefill shorter than the window, decode steps.
 
 gdn_fla.npz
     fla 0.5.1 naive_chunk_gated_delta_rule / naive_recurrent_gated_delta_rule
@@ -385,6 +387,63 @@ def head_d(gen, kind, B=2, T=45, d=24, M=4, G=4, dv=32, steps=3):
                 **{"sd_" + k: v for k, v in sd.items()}, **grads)
 
 
+def head_short(gen, kind, B=2, T=45, d=24, L=8, dv=6, T2=3, steps=3, pos0=5):
+    """The short head's exact L-tap window read: lapa.layer.ShortHead (kind "lapa",
+    lapa/layer.py:418-545) or sca2.arch_short.CHeadShort (kind "sca2", sca2/arch_short.py:45-158),
+    random weights (wr, wi perturbed off the identity tap), a random incoming ring buffer
+    (cos / sin of random phases, random values) at position pos0.  Records the prefill's u and
+    new state with every gradient of sum(u * dU) + sum(new state * dNew) (state gradients
+    included), then a second prefill of T2 < L-1 tokens (the new buffer mixes old and new
+    writes) and `steps` decode steps, forward only."""
+    torch.manual_seed(int(torch.randint(0, 2**31 - 1, (1,), generator=gen)))
+    if kind == "lapa":
+        import lapa.layer as LL
+        head = LL.ShortHead(LL.LaplaceConfig(d=d, L=L, dv=dv, theta_scale=0.5)).double()
+    else:
+        from sca2.arch_short import CHeadShort
+        head = CHeadShort(d, L, dv, theta_scale=0.5).double()
+    with torch.no_grad():
+        head.wr.add_(0.3 * torch.randn(L, generator=gen, dtype=torch.float64))
+        head.wi.add_(0.3 * torch.randn(L, generator=gen, dtype=torch.float64))
+    n = L - 1
+    z = torch.randn(B, T, d, generator=gen, dtype=torch.float64).requires_grad_(True)
+    h = torch.randn(B, T, d, generator=gen, dtype=torch.float64).requires_grad_(True)
+    ph0 = torch.randn(B, n, L, generator=gen, dtype=torch.float64)
+    c0 = ph0.cos().requires_grad_(True)
+    s0 = ph0.sin().requires_grad_(True)
+    e0 = torch.randn(B, n, dv, generator=gen, dtype=torch.float64).requires_grad_(True)
+    st = {"c": c0, "s": s0, "e": e0, "pos": torch.tensor(pos0, dtype=torch.long)}
+    u, st1 = head.prefill(z, h, st)
+    dU = torch.randn(u.shape, generator=gen, dtype=torch.float64)
+    dc = torch.randn(B, n, L, generator=gen, dtype=torch.float64)
+    ds = torch.randn(B, n, L, generator=gen, dtype=torch.float64)
+    de = torch.randn(B, n, dv, generator=gen, dtype=torch.float64)
+    ((u * dU).sum() + (st1["c"] * dc).sum() + (st1["s"] * ds).sum() + (st1["e"] * de).sum()).backward()
+    sd = {k: _np(v) for k, v in head.state_dict().items()}
+    grads = {"g_" + nm: _np(p.grad) for nm, p in head.named_parameters() if p.grad is not None}
+    st1 = {k: v.detach() for k, v in st1.items()}
+    z2 = torch.randn(B, T2, d, generator=gen, dtype=torch.float64)
+    h2 = torch.randn(B, T2, d, generator=gen, dtype=torch.float64)
+    zs = torch.randn(B, steps, d, generator=gen, dtype=torch.float64)
+    hs = torch.randn(B, steps, d, generator=gen, dtype=torch.float64)
+    us = []
+    with torch.no_grad():
+        u2, st2 = head.prefill(z2, h2, st1)
+        st = st2
+        for t in range(steps):
+            ut, st = head.step(zs[:, t], hs[:, t], st)
+            us.append(ut)
+    return dict(z=_np(z), h=_np(h), c0=_np(c0), s0=_np(s0), e0=_np(e0), pos0=np.array(pos0),
+                u=_np(u), c1=_np(st1["c"]), s1=_np(st1["s"]), e1=_np(st1["e"]),
+                dU=_np(dU), dc1=_np(dc), ds1=_np(ds), de1=_np(de),
+                d_z=_np(z.grad), d_h=_np(h.grad), d_c0=_np(c0.grad), d_s0=_np(s0.grad), d_e0=_np(e0.grad),
+                z2=_np(z2), h2=_np(h2), u2=_np(u2), c2=_np(st2["c"]), s2=_np(st2["s"]), e2=_np(st2["e"]),
+                zs=_np(zs), hs=_np(hs), us=_np(torch.stack(us, 1)),
+                cs=_np(st["c"]), ss=_np(st["s"]), es=_np(st["e"]), pos_end=np.array(int(st["pos"])),
+                meta=np.array([B, T, d, L, dv, T2, steps]),
+                **{"sd_" + k: v for k, v in sd.items()}, **grads)
+
+
 def main(ref_root):
     sys.path.insert(0, ref_root)
     import sca2.arch_short  # noqa: F401  registers cdelta/damp/short (see registry import order)
@@ -403,6 +462,8 @@ def main(ref_root):
     _save("head_dref.npz", **head_d(gen, "ref", M=4, G=4, dv=32))
     _save("head_dsepq.npz", **head_d(gen, "sepq", M=8, G=4, dv=16))
     _save("head_dpolar.npz", **head_d(gen, "polar", M=16, G=4, dv=16))
+    _save("head_short_lapa.npz", **head_short(gen, "lapa", L=8, dv=6))
+    _save("head_short_sca2.npz", **head_short(gen, "sca2", L=16, dv=8, T=37, T2=5, pos0=13))
 
 
 if __name__ == "__main__":

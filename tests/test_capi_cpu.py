@@ -48,6 +48,9 @@ int main(void) {
   printf("sca2_dscan_args %zu\nsca2_dscan_grads %zu\n", sizeof(sca2_dscan_args), sizeof(sca2_dscan_grads));
   F(sca2_dscan_args, sep) F(sca2_dscan_args, a_re) F(sca2_dscan_args, S0_im)
   F(sca2_dscan_grads, dv) F(sca2_dscan_grads, dS0_im)
+  printf("sca2_short_args %zu\nsca2_short_grads %zu\n", sizeof(sca2_short_args), sizeof(sca2_short_grads));
+  F(sca2_short_args, pos) F(sca2_short_args, kh) F(sca2_short_args, omega) F(sca2_short_args, e0)
+  F(sca2_short_grads, dv) F(sca2_short_grads, dtheta) F(sca2_short_grads, de0)
   return 0;
 }
 """
@@ -64,11 +67,14 @@ int main(void) {
     assert int(out["sca2_scan_grads"]) == ctypes.sizeof(_lib.ScanGrads)
     assert int(out["sca2_dscan_args"]) == ctypes.sizeof(_lib.DScanArgs)
     assert int(out["sca2_dscan_grads"]) == ctypes.sizeof(_lib.DScanGrads)
+    assert int(out["sca2_short_args"]) == ctypes.sizeof(_lib.ShortArgs)
+    assert int(out["sca2_short_grads"]) == ctypes.sizeof(_lib.ShortGrads)
     for key, val in out.items():
         if "." in key:
             st, field = key.split(".")
             cls = {"sca2_scan_args": _lib.ScanArgs, "sca2_scan_grads": _lib.ScanGrads,
-                   "sca2_dscan_args": _lib.DScanArgs, "sca2_dscan_grads": _lib.DScanGrads}[st]
+                   "sca2_dscan_args": _lib.DScanArgs, "sca2_dscan_grads": _lib.DScanGrads,
+                   "sca2_short_args": _lib.ShortArgs, "sca2_short_grads": _lib.ShortGrads}[st]
             assert getattr(cls, field).offset == int(val), key
 
 

@@ -148,3 +148,51 @@ def test_dscan_oracle_backward_finite_difference(sep):
               loss(*[xm if i == k else args[i] for i in range(7)])) / (2 * e)
         an = g["S0"][0][idx] if n == "s0r" else g["S0"][1][idx] if n == "s0i" else g[n][idx]
         assert abs(fd - an) < 1e-6 * max(1.0, abs(fd)), (n, fd, an)
+
+
+# ---- short heads -----------------------------------------------------------------------------
+def _rms_bwd(o, du, eps=1e-6):
+    r = 1.0 / np.sqrt((o * o).mean(-1, keepdims=True) + eps)
+    return r * du - o * r ** 3 * (o * du).mean(-1, keepdims=True)
+
+
+@pytest.mark.parametrize("name", ["head_short_lapa.npz", "head_short_sca2.npz"])
+def test_short_oracle_vs_reference(name):
+    """The numpy window read (with the heads' projections and RMS) reproduces the reference
+    short heads: prefill output, new ring buffer, every gradient (hand-written adjoint plus
+    the projections' chain rule), a second prefill shorter than the window and decode steps."""
+    from oracle import short as so
+    f = fx.load(name)
+    B, T, d, L, dv, T2, steps = (int(x) for x in f["meta"])
+    sd = {k[3:]: f[k] for k in f if k.startswith("sd_")}
+    pos0 = int(f["pos0"])
+    st = {"c": f["c0"], "s": f["s0"], "e": f["e0"]}
+    u, st1 = so.short_head(sd, f["z"], f["h"], st, pos0)
+    assert np.abs(u - f["u"]).max() < 1e-9
+    for k in ("c", "s", "e"):
+        assert np.abs(st1[k] - f[k + "1"]).max() < 1e-9
+    # gradients: rms, the window read's adjoint, then the projections
+    K, V = sd["K.weight"], sd["V.weight"]
+    kh, kz, v = f["h"] @ K.T, f["z"] @ K.T, f["z"] @ V.T
+    o, _ = so.short_forward(kh, kz, v, sd["theta"], sd["omega"], sd["wr"], sd["wi"], f["c0"], f["s0"], f["e0"], pos0)
+    g = so.short_backward(kh, kz, v, sd["theta"], sd["omega"], sd["wr"], sd["wi"], f["c0"], f["s0"], f["e0"], pos0,
+                          _rms_bwd(o, f["dU"]), (f["dc1"], f["ds1"], f["de1"]))
+    close = lambda a, b: np.abs(a - b).max() < 1e-9 * max(1.0, np.abs(b).max())
+    assert close(g["kh"] @ K, f["d_h"])
+    assert close(g["kz"] @ K + g["v"] @ V, f["d_z"])
+    dK = np.einsum("btl,btd->ld", g["kh"], f["h"]) + np.einsum("btl,btd->ld", g["kz"], f["z"])
+    assert close(dK, f["g_K.weight"]) and close(np.einsum("btj,btd->jd", g["v"], f["z"]), f["g_V.weight"])
+    for n in ("theta", "wr", "wi"):
+        assert close(g[n], f["g_" + n]), n
+    assert close(g["c0"], f["d_c0"]) and close(g["s0"], f["d_s0"]) and close(g["e0"], f["d_e0"])
+    u2, st2 = so.short_head(sd, f["z2"], f["h2"], st1, pos0 + T)
+    assert np.abs(u2 - f["u2"]).max() < 1e-9
+    for k in ("c", "s", "e"):
+        assert np.abs(st2[k] - f[k + "2"]).max() < 1e-9
+    st, pos = st2, pos0 + T + T2
+    for t in range(steps):
+        ut, st = so.short_head(sd, f["zs"][:, t:t + 1], f["hs"][:, t:t + 1], st, pos)
+        pos += 1
+        assert np.abs(ut[:, 0] - f["us"][:, t]).max() < 1e-9
+    assert np.abs(st["c"] - f["cs"]).max() < 1e-9 and np.abs(st["e"] - f["es"]).max() < 1e-9
+    assert pos == int(f["pos_end"])
