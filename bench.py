@@ -36,6 +36,7 @@ WORK = dict(B=8, T=4096, H=16, Mh=32, V=64)
 DECODE = dict(B=256, T=4096, H=16, Mh=64, V=128, steps=512)
 SP = dict(B=1, T=131072, H=16, Mh=32, V=64)  # one long sequence, split over the ranks
 DHEAD = dict(B=8, T=4096, M=16, G=8, V=64)   # D head of the reference LayerCfg (Md=16, G=8, dv=d/2)
+SHORT = dict(B=8, T=4096, L=16, dv=64, decode_B=256)  # short head, LapA default window L=16
 # Algorithmic bytes per token per head (inputs read + outputs written once):
 #   fwd: phi, psi fp32 (2*Mh*4) + v bf16 (V*2) + beta (4) + o bf16 (2*V*2)
 #   bwd: dO bf16 (2*V*2) + inputs re-read (2*Mh*4 + V*2 + 4) + dphi, dpsi fp32 (2*Mh*4) + dv bf16 (V*2) + dbeta (4)
@@ -94,12 +95,33 @@ def cpu_sample(pool, n, seed=0):
 #  clocks
 # --------------------------------------------------------------------------------------
 class Clocks:
+    """SM clock and clock-event reasons sampled DURING the timed region: NVML (read-only
+    queries) every 10 ms on a thread, plus one sample at start and at stop, so that even a
+    timed region of a few ms is covered; nvidia-smi -lms 200 when NVML is unavailable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index):
-        self.index = index  # device UUID (robust to CUDA_VISIBLE_DEVICES) or ordinal
+        import threading
+        self.rows, self.p, self.h = [], None, None
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            self.h = (N.nvmlDeviceGetHandleByUUID(index) if isinstance(index, str)
+                      else N.nvmlDeviceGetHandleByIndex(index))
+            self.bits = (N.nvmlClocksEventReasonHwSlowdown, N.nvmlClocksEventReasonHwThermalSlowdown,
+                         N.nvmlClocksEventReasonSwThermalSlowdown, N.nvmlClocksEventReasonSwPowerCap)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self.stop_ev = threading.Event()
+            self._sample()
+            self.t = threading.Thread(target=self._loop, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.h = None
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.Q}",
@@ -108,7 +130,32 @@ class Clocks:
         except Exception:
             self.p = None
 
+    def _sample(self):
+        N = self.N
+        mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+        r = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        self.rows.append((float(mhz), float(self.max_mhz), [n for n, b in zip(self.NAMES, self.bits) if r & b]))
+
+    def _loop(self):
+        while not self.stop_ev.wait(0.01):
+            try:
+                self._sample()
+            except Exception:
+                return
+
     def stop(self):
+        if self.h is not None:
+            self.stop_ev.set()
+            self.t.join(2)
+            try:
+                self._sample()
+            except Exception:
+                pass
+            rows = self.rows
+            if not rows:
+                return None
+            return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                    "reasons": sorted({n for r in rows for n in r[2]}), "samples": len(rows), "source": "nvml"}
         if self.p is None:
             return None
         self.p.terminate()
@@ -128,10 +175,9 @@ class Clocks:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, val in zip(names, r[5:9]) if val.lower() == "active"})
+        reasons = sorted({n for r in rows for n, val in zip(self.NAMES, r[5:9]) if val.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 # --------------------------------------------------------------------------------------
@@ -253,8 +299,12 @@ def run_gpu(args, rank, world, local_rank, dist):
     if not args.no_dhead:
         torch.cuda.empty_cache()
         dh = run_dhead(torch, ops, dev, rank, world, dist)
+    sh = None
+    if not args.no_short:
+        torch.cuda.empty_cache()
+        sh = run_short(torch, ops, dev, rank, world, dist)
     return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
-                decode=decode, sp=sp, dhead=dh)
+                decode=decode, sp=sp, dhead=dh, short=sh)
 
 
 def run_decode(torch, ops, dev, rank, world, dist):
@@ -396,6 +446,81 @@ def run_dhead(torch, ops, dev, rank, world, dist, reps=5):
             "achieved_gbs": gbs, "algorithmic_bytes_per_step": (fwd_b + bwd_b) * B * T}
 
 
+def _timed(torch, dist, dev, fn, reps):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_short(torch, ops, dev, rank, world, dist, reps=10):
+    """Short-head window read (fp32) on the LapA short-head shape: prefill fwd+bwd over
+    B x T tokens, and one decode token for decode_B sequences.  Algorithmic bytes per token:
+    fwd K(h), K(z) (2 L) + V(z) (dv) read, o (2 dv) written; bwd dO (2 dv) read, inputs
+    re-read, their gradients written (all fp32)."""
+    S = SHORT
+    B, T, L, dv = S["B"], S["T"], S["L"], S["dv"]
+    n = L - 1
+    g = torch.Generator(device=dev).manual_seed(41 + rank)
+    rn = lambda *sh: torch.randn(*sh, device=dev, generator=g)
+    omega = (torch.arange(L, dtype=torch.float64) * (2 * math.pi / L)).float().to(dev)
+    par = [(0.3 * rn(L)).requires_grad_(True), (1 + 0.1 * rn(L)).requires_grad_(True), (0.1 * rn(L)).requires_grad_(True)]
+    x = [rn(B, T, L).requires_grad_(True), rn(B, T, L).requires_grad_(True), rn(B, T, dv).requires_grad_(True)]
+    ph = rn(B, n, L)
+    st = (ph.cos(), ph.sin(), rn(B, n, dv))
+    pos = torch.tensor(5, device=dev)
+    dO = rn(B, T, 2 * dv)
+
+    def step():
+        o, _ = ops.short_read(x[0], x[1], x[2], par[0], omega, par[1], par[2], st, pos)
+        torch.autograd.backward(o, dO)
+    ms = _timed(torch, dist, dev, step, reps)
+    fwd_b = (2 * L + dv + 2 * dv) * 4
+    bwd_b = (2 * dv + 2 * L + dv + 2 * L + dv) * 4
+    Bd = S["decode_B"]
+    xd = [rn(Bd, 1, L), rn(Bd, 1, L), rn(Bd, 1, dv)]
+    phd = rn(Bd, n, L)
+    std = [phd.cos(), phd.sin(), rn(Bd, n, dv)]
+
+    # one decode token as a CUDA graph (read, then the new ring buffer copied over the old)
+    def dbody():
+        with torch.no_grad():
+            o, new = ops.short_read(xd[0], xd[1], xd[2], par[0], omega, par[1], par[2], tuple(std), pos)
+            for a, b in zip(std, new):
+                a.copy_(b)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            dbody()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dbody()
+    dms = _timed(torch, dist, dev, graph.replay, 200)
+    del graph
+    return {"value": world * B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "config": {"batch": B, "seq_len": T, "L": L, "dv": dv, "fwd+bwd": True, "dtype": "f32"},
+            "achieved_gbs": (fwd_b + bwd_b) * B * T / (ms * 1e-3) / 1e9,
+            "algorithmic_bytes_per_step": (fwd_b + bwd_b) * B * T,
+            "decode": {"batch": Bd, "us_per_token_step": dms * 1e3, "cuda_graph": True,
+                       "tokens_per_s": world * Bd / (dms / 1e3)}}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -416,6 +541,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sp", action="store_true")
     ap.add_argument("--no-dhead", action="store_true")
+    ap.add_argument("--no-short", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
@@ -519,6 +645,7 @@ def main():
         "decode": r["decode"],
         "sp_prefill": r["sp"],
         "d_head": r["dhead"],
+        "short_head": r["short"],
     }
     print(json.dumps(line))
 

@@ -297,6 +297,7 @@ static int check_short(const sca2_short_args* a) {
   if (!a) return fail(SCA2_ERR_ARG, "null short-head args");
   if (a->B < 1 || a->T < 0 || a->L < 1 || a->dv < 1) return fail(SCA2_ERR_ARG, "short: bad sizes");
   if (a->L > 32) return fail(SCA2_ERR_UNSUPPORTED, "short: window L must be <= 32");
+  if (a->T > (1 << 27) - 64) return fail(SCA2_ERR_UNSUPPORTED, "short: T must be below 2^27 - 64");
   if (a->T > 0 && (!a->kh || !a->kz || !a->v)) return fail(SCA2_ERR_ARG, "short: null input");
   if (!a->theta || !a->omega || !a->wr || !a->wi) return fail(SCA2_ERR_ARG, "short: null parameter");
   if ((a->c0 == nullptr) != (a->s0 == nullptr)) return fail(SCA2_ERR_ARG, "short: c0 and s0 go together");

@@ -15,7 +15,10 @@
 // multiply-adds per token) and independent across tokens, so each CTA takes TT consecutive
 // queries of one sequence and the L-1 keys before them; the codes (sin / cos of the phases,
 // computed here from K(h), K(z), theta, omega and the position), kappa and the values sit in
-// shared memory with odd row strides so that lanes walking different keys hit different banks.
+// shared memory.  The inner products are register-blocked: a thread owns one token row and a
+// group of 4 lags, 4 modes or 8 value columns, lanes of a warp walk consecutive rows, and the
+// row strides (a multiple of 4 floats, = 4 mod 32 banks) make the 16-byte loads of 8
+// consecutive rows hit distinct banks; kappa rows have an odd stride for the scalar loads.
 // Values and output gradients are processed in slices of DS columns, so dv is unbounded.
 #include "common.cuh"
 
@@ -23,40 +26,61 @@ namespace sca2 {
 namespace shortk {
 
 constexpr int NT = 256;
-constexpr int DS = 64;  // value columns per slice
-constexpr int DSP = DS + 1;
+constexpr int DS = 32;      // value columns per slice
+constexpr int ES = DS + 4;  // row stride of value / output-gradient slices (floats)
+
+// row stride of the code arrays: L rounded up to 4 plus 4 (16-byte rows; 20 floats for L = 16)
+__host__ __device__ constexpr int code_stride(int L) { return ((L + 3) & ~3) + 4; }
+__host__ __device__ constexpr int lane_groups(int L) { return (L + 3) / 4; }
 
 __device__ __forceinline__ int pmod(long long p, int L) {
   long long r = p % L;
   return (int)(r < 0 ? r + L : r);
 }
+// floor(u / d) by a multiply-high with m = magic(d) = ceil(2^32 / d): u m / 2^32 = u / d +
+// u e / (d 2^32) with e = m d - 2^32 < d, so the floor is exact while u e < 2^32 (every use
+// here: u < 2^16 with d < 2^16, or the phase position u < 2^27 with d = L <= 32)
+// (d = 1 would need m = 2^32: it is encoded as m = 0 and returns u)
+__host__ __device__ constexpr uint32_t magic(uint32_t d) { return d > 1 ? 0xFFFFFFFFu / d + 1u : 0u; }
+__device__ __forceinline__ int qdiv(int u, uint32_t m) { return m ? (int)__umulhi((uint32_t)u, m) : u; }
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
+}
 
 struct Geo {
-  int L, n, LP, dv, T, TT, t0, tq;
+  int L, n, dv, T, t0, tq;
+  int pb;              // (pos mod L): token t >= 0 has phase position (pb + t) mod L
+  uint32_t mL, mCS;    // magic(L), magic(code stride)
 };
 __device__ __forceinline__ Geo geo(const sca2_short_args& p, int TT) {
   Geo g;
   g.L = p.L;
   g.n = p.L - 1;
-  g.LP = p.L + 1;
   g.dv = p.dv;
   g.T = p.T;
-  g.TT = TT;
   g.t0 = blockIdx.x * TT;
   g.tq = min(TT, p.T - g.t0);
+  g.pb = pmod(p.pos ? *p.pos : 0, p.L);
+  g.mL = magic(p.L);
+  g.mCS = magic(((p.L + 3) & ~3) + 4);
   return g;
 }
+// phase position (pos + t) mod L of token t >= 0 (pb + t < 2^27, checked on the host)
+__device__ __forceinline__ float ppos(const Geo& g, int t) {
+  const int a = g.pb + t;
+  return (float)(a - qdiv(a, g.mL) * g.L);
+}
 
-// cos / sin of the write phase of extended key x of this CTA (token s = t0 - n + x), from
-// the state for s < 0
-__device__ __forceinline__ void key_code(const sca2_short_args& p, const Geo& g, int b, long long p0, int s, int l,
-                                         float* c, float* sn) {
+// cos / sin of the write phase of token s (from the ring buffer for s < 0)
+__device__ __forceinline__ void key_code(const sca2_short_args& p, const Geo& g, int b, int s, int l, float* c,
+                                         float* sn) {
   if (s < 0) {
     const int64_t k = ((int64_t)b * g.n + g.n + s) * g.L + l;
     *c = p.c0 ? p.c0[k] : 1.f;
     *sn = p.s0 ? p.s0[k] : 0.f;
   } else {
-    const float ph = p.kh[((int64_t)b * g.T + s) * g.L + l] * p.theta[l] + (float)pmod(p0 + s, g.L) * p.omega[l];
+    const float ph = p.kh[((int64_t)b * g.T + s) * g.L + l] * p.theta[l] + ppos(g, s) * p.omega[l];
     sincosf(ph, sn, c);
   }
 }
@@ -65,76 +89,156 @@ __device__ __forceinline__ float key_value(const sca2_short_args& p, const Geo& 
   return p.v[((int64_t)b * g.T + s) * g.dv + j];
 }
 
+// key codes of rows x in [0, NX) (token t0 - n + x), zero in the padding columns
+__device__ __forceinline__ void load_keys(const sca2_short_args& p, const Geo& g, int b, int NX, float* KC,
+                                          float* KS) {
+  const int CS = code_stride(g.L);
+  for (int u = threadIdx.x; u < NX * CS; u += NT) {
+    const int x = qdiv(u, g.mCS), l = u - x * CS;
+    float c = 0.f, s = 0.f;
+    if (l < g.L) key_code(p, g, b, g.t0 - g.n + x, l, &c, &s);
+    KC[u] = c;
+    KS[u] = s;
+  }
+}
+// read codes c1, c2 (and cos / sin psi when CQ) of query rows y in [0, NY) (token t0 + y)
+__device__ __forceinline__ void load_queries(const sca2_short_args& p, const Geo& g, int b, int NY, float* Q1,
+                                             float* Q2, float* CQ, float* SQ) {
+  const int CS = code_stride(g.L);
+  for (int u = threadIdx.x; u < NY * CS; u += NT) {
+    const int y = qdiv(u, g.mCS), l = u - y * CS, t = g.t0 + y;
+    float c = 0.f, s = 0.f, wr = 0.f, wi = 0.f;
+    if (l < g.L) {
+      const float ph = p.kz[((int64_t)b * g.T + t) * g.L + l] * p.theta[l] + ppos(g, t) * p.omega[l];
+      sincosf(ph, &s, &c);
+      wr = p.wr[l];
+      wi = p.wi[l];
+    }
+    Q1[u] = wr * c + wi * s;
+    Q2[u] = wr * s - wi * c;
+    if (CQ) {
+      CQ[u] = c;
+      SQ[u] = s;
+    }
+  }
+}
+
+// kappa of the pairs (row y, lags 4 gq .. 4 gq + 3): key row x = y + n - lag, pairs with x >= NX
+// are zero.  Lanes walk consecutive rows y.
+__device__ __forceinline__ void kappa_pairs(const Geo& g, int NY, int NX, const float* KC, const float* KS,
+                                            const float* Q1, const float* Q2, float* KR, float* KI) {
+  const int L = g.L, n = g.n, CS = code_stride(L), KP = L + 1, NG = lane_groups(L);
+  const float iL = 1.f / (float)L;
+  const uint32_t mY = magic(NY);
+  for (int u = threadIdx.x; u < NY * NG; u += NT) {
+    const int gq = qdiv(u, mY), y = u - gq * NY;
+    float kr[4] = {0.f, 0.f, 0.f, 0.f}, ki[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int l = 0; l < CS - 4; l += 4) {
+      const float4 q1 = ld4(Q1 + y * CS + l), q2 = ld4(Q2 + y * CS + l);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int x = y + n - (4 * gq + k);
+        if (4 * gq + k < L && x < NX) {
+          const float4 kc = ld4(KC + x * CS + l), ks = ld4(KS + x * CS + l);
+          kr[k] += dot4(kc, q1) + dot4(ks, q2);
+          ki[k] += dot4(ks, q1) - dot4(kc, q2);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int lag = 4 * gq + k;
+      if (lag < L) {
+        KR[y * KP + lag] = kr[k] * iL;
+        KI[y * KP + lag] = ki[k] * iL;
+      }
+    }
+  }
+}
+
+// value slice [j0, j0 + DS) of key rows [0, NX) (zero beyond dv)
+__device__ __forceinline__ void load_values(const sca2_short_args& p, const Geo& g, int b, int NX, int j0, float* E) {
+  for (int u = threadIdx.x; u < NX * DS; u += NT) {
+    const int x = u / DS, j = u - (u / DS) * DS;
+    E[x * ES + j] = j0 + j < g.dv ? key_value(p, g, b, g.t0 - g.n + x, j0 + j) : 0.f;
+  }
+}
+// output-gradient slice of query rows [0, NY): re part to GR, im part to GI
+__device__ __forceinline__ void load_grads(const float* dO, const Geo& g, int b, int NY, int j0, float* GR, float* GI) {
+  for (int u = threadIdx.x; u < NY * DS; u += NT) {
+    const int y = u / DS, j = u - (u / DS) * DS;
+    const float* row = dO + ((int64_t)b * g.T + g.t0 + y) * 2 * g.dv;
+    GR[y * ES + j] = j0 + j < g.dv ? row[j0 + j] : 0.f;
+    GI[y * ES + j] = j0 + j < g.dv ? row[g.dv + j0 + j] : 0.f;
+  }
+}
+
+// dst += v summed over the CTA: lanes of a warp that hold the same dst (uniform) are reduced
+// by shuffles first, so the shared-memory atomic is one per warp instead of one per lane
+__device__ __forceinline__ void red_add(float* dst, float v, bool uniform) {
+  if (uniform) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(dst, v);
+  } else {
+    atomicAdd(dst, v);
+  }
+}
+
 size_t fwd_smem_floats(int L, int TT) {
-  const int n = L - 1, LP = L + 1;
-  return (size_t)(TT + n) * (2 * LP + DSP) + (size_t)TT * (2 * LP + 2 * L);
+  const int n = L - 1, CS = code_stride(L), KP = L + 1;
+  return (size_t)(TT + n) * (2 * CS + ES) + (size_t)TT * (2 * CS + 2 * KP);
 }
 size_t bwd_smem_floats(int L, int TT) {
-  const int n = L - 1, LP = L + 1, NX = TT + n;
-  return (size_t)NX * (2 * LP + DSP) + (size_t)NX * (4 * LP + 4 * L + 2 * DSP) + 3 * L;
+  const int n = L - 1, CS = code_stride(L), KP = L + 1, NX = TT + n;
+  return (size_t)NX * (6 * CS + 4 * KP + 3 * ES) + 3 * L;
 }
 
 __global__ void __launch_bounds__(NT) short_fwd_kernel(sca2_short_args p, float* o, int TT) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const Geo g = geo(p, TT);
-  const int tid = threadIdx.x, b = blockIdx.y, L = g.L, n = g.n, LP = g.LP, dv = g.dv;
-  const int NX = g.tq + n;
-  float* KC = sm;                    // keys: cos, sin  [x][l]  (stride LP)
-  float* KS = KC + (TT + n) * LP;
-  float* E = KS + (TT + n) * LP;     // values slice [x][j]  (stride DSP)
-  float* Q1 = E + (TT + n) * DSP;    // read codes c1, c2  [i][l]
-  float* Q2 = Q1 + TT * LP;
-  float* KR = Q2 + TT * LP;          // kappa [i][lag]
-  float* KI = KR + TT * L;
-  const long long p0 = p.pos ? *p.pos : 0;
-  for (int u = tid; u < NX * L; u += NT) {
-    const int x = u / L, l = u - (u / L) * L;
-    float c, s;
-    key_code(p, g, b, p0, g.t0 - n + x, l, &c, &s);
-    KC[x * LP + l] = c;
-    KS[x * LP + l] = s;
-  }
-  for (int u = tid; u < g.tq * L; u += NT) {
-    const int i = u / L, l = u - (u / L) * L, t = g.t0 + i;
-    const float ph = p.kz[((int64_t)b * g.T + t) * L + l] * p.theta[l] + (float)pmod(p0 + t, L) * p.omega[l];
-    float s, c;
-    sincosf(ph, &s, &c);
-    const float wr = p.wr[l], wi = p.wi[l];
-    Q1[i * LP + l] = wr * c + wi * s;
-    Q2[i * LP + l] = wr * s - wi * c;
-  }
+  const int tid = threadIdx.x, b = blockIdx.y, L = g.L, n = g.n, dv = g.dv;
+  const int CS = code_stride(L), KP = L + 1, NX = g.tq + n;
+  float* KC = sm;
+  float* KS = KC + (TT + n) * CS;
+  float* E = KS + (TT + n) * CS;
+  float* Q1 = E + (TT + n) * ES;
+  float* Q2 = Q1 + TT * CS;
+  float* KR = Q2 + TT * CS;
+  float* KI = KR + TT * KP;
+  load_keys(p, g, b, NX, KC, KS);
+  load_queries(p, g, b, g.tq, Q1, Q2, nullptr, nullptr);
+  const uint32_t mQ = magic(g.tq);
   __syncthreads();
-  const float iL = 1.f / (float)L;
-  for (int u = tid; u < g.tq * L; u += NT) {
-    const int i = u / L, lag = u - (u / L) * L, x = i + n - lag;
-    float kr = 0.f, ki = 0.f;
-    for (int l = 0; l < L; ++l) {
-      const float kc = KC[x * LP + l], ks = KS[x * LP + l], q1 = Q1[i * LP + l], q2 = Q2[i * LP + l];
-      kr = fmaf(kc, q1, fmaf(ks, q2, kr));
-      ki = fmaf(ks, q1, fmaf(-kc, q2, ki));
-    }
-    KR[i * L + lag] = kr * iL;
-    KI[i * L + lag] = ki * iL;
-  }
+  kappa_pairs(g, g.tq, NX, KC, KS, Q1, Q2, KR, KI);
   for (int j0 = 0; j0 < dv; j0 += DS) {
-    const int w = min(DS, dv - j0);
     __syncthreads();  // kappa written / previous slice consumed
-    for (int u = tid; u < NX * w; u += NT) {
-      const int x = u / w, j = u - (u / w) * w;
-      E[x * DSP + j] = key_value(p, g, b, g.t0 - n + x, j0 + j);
-    }
+    load_values(p, g, b, NX, j0, E);
     __syncthreads();
-    for (int u = tid; u < g.tq * w; u += NT) {
-      const int i = u / w, j = u - (u / w) * w;
-      float ar = 0.f, ai = 0.f;
+    // row i, value columns jg*8 .. +7 of the slice
+    for (int u = tid; u < g.tq * (DS / 8); u += NT) {
+      const int jg = qdiv(u, mQ), i = u - jg * g.tq, jj = jg * 8;
+      float ar[8], ai[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ar[k] = ai[k] = 0.f;
       for (int lag = 0; lag < L; ++lag) {
-        const float ev = E[(i + n - lag) * DSP + j];
-        ar = fmaf(KR[i * L + lag], ev, ar);
-        ai = fmaf(KI[i * L + lag], ev, ai);
+        const float kr = KR[i * KP + lag], ki = KI[i * KP + lag];
+        const float* e = E + (i + n - lag) * ES + jj;
+        const float4 e0 = ld4(e), e1 = ld4(e + 4);
+        const float ev[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          ar[k] = fmaf(kr, ev[k], ar[k]);
+          ai[k] = fmaf(ki, ev[k], ai[k]);
+        }
       }
-      float* orow = o + ((int64_t)b * g.T + g.t0 + i) * 2 * dv;
-      orow[j0 + j] = ar;
-      orow[dv + j0 + j] = ai;
+      float* orow = o + ((int64_t)b * g.T + g.t0 + i) * 2 * dv + j0 + jj;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (j0 + jj + k < dv) {
+          orow[k] = ar[k];
+          orow[dv + k] = ai[k];
+        }
     }
   }
 }
@@ -142,13 +246,11 @@ __global__ void __launch_bounds__(NT) short_fwd_kernel(sca2_short_args p, float*
 // new ring buffer: entry k (0 <= k < n) is extended index T + k, i.e. token T - n + k
 __global__ void __launch_bounds__(NT) short_state_kernel(sca2_short_args p, float* c1, float* s1, float* e1) {
   const int b = blockIdx.x, L = p.L, n = L - 1, dv = p.dv, T = p.T;
-  Geo g;
-  g.L = L; g.n = n; g.LP = L + 1; g.dv = dv; g.T = T; g.TT = 0; g.t0 = 0; g.tq = 0;
-  const long long p0 = p.pos ? *p.pos : 0;
+  const Geo g = geo(p, 0);
   for (int u = threadIdx.x; u < n * L; u += NT) {
     const int k = u / L, l = u - (u / L) * L;
     float c, s;
-    key_code(p, g, b, p0, T - n + k, l, &c, &s);
+    key_code(p, g, b, T - n + k, l, &c, &s);
     c1[((int64_t)b * n + k) * L + l] = c;
     s1[((int64_t)b * n + k) * L + l] = s;
   }
@@ -162,171 +264,209 @@ __global__ void __launch_bounds__(NT) short_state_kernel(sca2_short_args p, floa
 // buffered keys [-n, 0) for the first CTA.  Key s is read by queries s .. s + n, so the CTA
 // also loads the n queries after its own (up to T) and recomputes their kappa for the pairs
 // that reach its keys.  Pairs are indexed (y, lag): query t = t0 + y, key s = t - lag,
-// extended key x = y + n - lag (< NX = tq + n for the pairs this CTA needs).
-__global__ void __launch_bounds__(NT) short_bwd_kernel(sca2_short_args p, const float* dO, const float* dc1,
+// key row x = y + n - lag (< NX = tq + n for the pairs this CTA needs).
+__global__ void __launch_bounds__(NT, 3) short_bwd_kernel(sca2_short_args p, const float* dO, const float* dc1,
                                                        const float* ds1, const float* de1, sca2_short_grads gr,
                                                        float* part, int TT) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const Geo g = geo(p, TT);
-  const int tid = threadIdx.x, b = blockIdx.y, L = g.L, n = g.n, LP = g.LP, dv = g.dv, T = g.T;
-  const int NX = g.tq + n;                // keys  s = t0 - n + x
-  const int NY = min(g.tq + n, T - g.t0);  // queries t = t0 + y
+  const int tid = threadIdx.x, b = blockIdx.y, L = g.L, n = g.n, dv = g.dv, T = g.T;
+  const int CS = code_stride(L), KP = L + 1, NG = lane_groups(L);
+  const bool vec = (L & 3) == 0;           // 16-byte rows of the (B,T,L) tensors
+  const int NX = g.tq + n;                 // key rows:   s = t0 - n + x
+  const int NY = min(g.tq + n, T - g.t0);  // query rows: t = t0 + y
+  const int R = TT + n;
   float* KC = sm;
-  float* KS = KC + (TT + n) * LP;
-  float* E = KS + (TT + n) * LP;          // values slice [x][j]
-  float* Q1 = E + (TT + n) * DSP;         // [y][l]
-  float* Q2 = Q1 + (TT + n) * LP;
-  float* CQ = Q2 + (TT + n) * LP;
-  float* SQ = CQ + (TT + n) * LP;
-  float* KR = SQ + (TT + n) * LP;         // kappa and its gradient [y][lag]
-  float* KI = KR + (TT + n) * L;
-  float* DKR = KI + (TT + n) * L;
-  float* DKI = DKR + (TT + n) * L;
-  float* GR = DKI + (TT + n) * L;         // dO slice [y][j], re then im
-  float* GI = GR + (TT + n) * DSP;
-  float* RED = GI + (TT + n) * DSP;       // dtheta, dwr, dwi partials of this CTA
-  const long long p0 = p.pos ? *p.pos : 0;
+  float* KS = KC + R * CS;
+  float* Q1 = KS + R * CS;
+  float* Q2 = Q1 + R * CS;
+  float* CQ = Q2 + R * CS;
+  float* SQ = CQ + R * CS;
+  float* KR = SQ + R * CS;   // kappa and its gradient [y][lag]
+  float* KI = KR + R * KP;
+  float* DKR = KI + R * KP;
+  float* DKI = DKR + R * KP;
+  float* E = DKI + R * KP;   // value slice [x][j]
+  float* GR = E + R * ES;    // output-gradient slice [y][j]
+  float* GI = GR + R * ES;
+  float* RED = GI + R * ES;  // dtheta, dwr, dwi partials of this CTA
   const float iL = 1.f / (float)L;
+  const uint32_t mY = magic(NY), mQ = magic(g.tq);
   for (int u = tid; u < 3 * L; u += NT) RED[u] = 0.f;
-  for (int u = tid; u < NX * L; u += NT) {
-    const int x = u / L, l = u - (u / L) * L;
-    float c, s;
-    key_code(p, g, b, p0, g.t0 - n + x, l, &c, &s);
-    KC[x * LP + l] = c;
-    KS[x * LP + l] = s;
-  }
-  for (int u = tid; u < NY * L; u += NT) {
-    const int y = u / L, l = u - (u / L) * L, t = g.t0 + y;
-    const float ph = p.kz[((int64_t)b * T + t) * L + l] * p.theta[l] + (float)pmod(p0 + t, L) * p.omega[l];
-    float s, c;
-    sincosf(ph, &s, &c);
-    const float wr = p.wr[l], wi = p.wi[l];
-    CQ[y * LP + l] = c;
-    SQ[y * LP + l] = s;
-    Q1[y * LP + l] = wr * c + wi * s;
-    Q2[y * LP + l] = wr * s - wi * c;
-  }
+  load_keys(p, g, b, NX, KC, KS);
+  load_queries(p, g, b, NY, Q1, Q2, CQ, SQ);
   __syncthreads();
-  // kappa of every needed pair (zero for the pairs outside this CTA's keys)
-  for (int u = tid; u < NY * L; u += NT) {
-    const int y = u / L, lag = u - (u / L) * L, x = y + n - lag;
-    float kr = 0.f, ki = 0.f;
-    if (x < NX) {
-      for (int l = 0; l < L; ++l) {
-        const float kc = KC[x * LP + l], ks = KS[x * LP + l], q1 = Q1[y * LP + l], q2 = Q2[y * LP + l];
-        kr = fmaf(kc, q1, fmaf(ks, q2, kr));
-        ki = fmaf(ks, q1, fmaf(-kc, q2, ki));
-      }
-    }
-    KR[y * L + lag] = kr * iL;
-    KI[y * L + lag] = ki * iL;
-    DKR[y * L + lag] = 0.f;
-    DKI[y * L + lag] = 0.f;
-  }
-  // d kappa(t, s) = dO_t . e_s, accumulated over value slices (each thread keeps its pairs)
+  kappa_pairs(g, NY, NX, KC, KS, Q1, Q2, KR, KI);
+  // d kappa(t, s) = dO_t . e_s over the value slices; a thread keeps its pairs (row y, lags
+  // 4 gq .. 4 gq + 3) in registers across the slices
+  constexpr int MAXU = 3;  // NY * NG <= 3 * NT for the tile sizes used (checked on the host)
+  float dr[MAXU][4], di[MAXU][4];
+#pragma unroll
+  for (int q = 0; q < MAXU; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dr[q][k] = di[q][k] = 0.f;
   for (int j0 = 0; j0 < dv; j0 += DS) {
-    const int w = min(DS, dv - j0);
     __syncthreads();
-    for (int u = tid; u < NX * w; u += NT) {
-      const int x = u / w, j = u - (u / w) * w;
-      E[x * DSP + j] = key_value(p, g, b, g.t0 - n + x, j0 + j);
-    }
-    for (int u = tid; u < NY * w; u += NT) {
-      const int y = u / w, j = u - (u / w) * w;
-      const float* row = dO + ((int64_t)b * T + g.t0 + y) * 2 * dv;
-      GR[y * DSP + j] = row[j0 + j];
-      GI[y * DSP + j] = row[dv + j0 + j];
-    }
+    load_values(p, g, b, NX, j0, E);
+    load_grads(dO, g, b, NY, j0, GR, GI);
     __syncthreads();
-    for (int u = tid; u < NY * L; u += NT) {
-      const int y = u / L, lag = u - (u / L) * L, x = y + n - lag;
-      if (x >= NX) continue;
-      float ar = 0.f, ai = 0.f;
-      for (int j = 0; j < w; ++j) {
-        const float ev = E[x * DSP + j];
-        ar = fmaf(GR[y * DSP + j], ev, ar);
-        ai = fmaf(GI[y * DSP + j], ev, ai);
+#pragma unroll
+    for (int q = 0; q < MAXU; ++q) {
+      const int u = tid + q * NT;
+      if (u >= NY * NG) break;
+      const int gq = qdiv(u, mY), y = u - gq * NY;
+      for (int j = 0; j < DS; j += 4) {
+        const float4 a = ld4(GR + y * ES + j), c = ld4(GI + y * ES + j);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int x = y + n - (4 * gq + k);
+          if (4 * gq + k < L && x < NX) {
+            const float4 e = ld4(E + x * ES + j);
+            dr[q][k] += dot4(a, e);
+            di[q][k] += dot4(c, e);
+          }
+        }
       }
-      DKR[y * L + lag] += ar;
-      DKI[y * L + lag] += ai;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < MAXU; ++q) {
+    const int u = tid + q * NT;
+    if (u >= NY * NG) break;
+    const int gq = qdiv(u, mY), y = u - gq * NY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int lag = 4 * gq + k;
+      if (lag < L) {
+        const bool ok = y + n - lag < NX;
+        DKR[y * KP + lag] = ok ? dr[q][k] : 0.f;
+        DKI[y * KP + lag] = ok ? di[q][k] : 0.f;
+      }
     }
   }
   __syncthreads();
-  // queries: d c1, d c2 -> d psi -> d K(z), and the theta / wr / wi partials
-  for (int u = tid; u < g.tq * L; u += NT) {
-    const int y = u / L, l = u - (u / L) * L, t = g.t0 + y;
-    float a1 = 0.f, a2 = 0.f;
+  // queries (row y < tq, modes 4 gl .. 4 gl + 3): d c1, d c2 -> d psi -> d K(z); theta / wr /
+  // wi partials.  With tq a multiple of 32 every warp holds one mode group.
+  const bool quni = (g.tq & 31) == 0;
+  for (int u = tid; u < g.tq * NG; u += NT) {
+    const int lg = qdiv(u, mQ), y = u - lg * g.tq, l0 = 4 * lg, t = g.t0 + y;
+    float a1[4] = {0.f, 0.f, 0.f, 0.f}, a2[4] = {0.f, 0.f, 0.f, 0.f};
     for (int lag = 0; lag < L; ++lag) {
       const int x = y + n - lag;
-      const float dr = DKR[y * L + lag], di = DKI[y * L + lag], kc = KC[x * LP + l], ks = KS[x * LP + l];
-      a1 = fmaf(dr, kc, fmaf(di, ks, a1));
-      a2 = fmaf(dr, ks, fmaf(-di, kc, a2));
+      const float r = DKR[y * KP + lag], i = DKI[y * KP + lag];
+      const float4 kc = ld4(KC + x * CS + l0), ks = ld4(KS + x * CS + l0);
+      const float c4[4] = {kc.x, kc.y, kc.z, kc.w}, s4[4] = {ks.x, ks.y, ks.z, ks.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        a1[k] = fmaf(r, c4[k], fmaf(i, s4[k], a1[k]));
+        a2[k] = fmaf(r, s4[k], fmaf(-i, c4[k], a2[k]));
+      }
     }
-    a1 *= iL;
-    a2 *= iL;
-    const float cq = CQ[y * LP + l], sq = SQ[y * LP + l], wr = p.wr[l], wi = p.wi[l];
-    const float dcq = a1 * wr - a2 * wi, dsq = a1 * wi + a2 * wr;
-    const float dpsi = -sq * dcq + cq * dsq;
-    const int64_t ti = ((int64_t)b * T + t) * L + l;
-    gr.dkz[ti] = dpsi * p.theta[l];
-    atomicAdd(RED + l, dpsi * p.kz[ti]);
-    atomicAdd(RED + L + l, a1 * cq + a2 * sq);
-    atomicAdd(RED + 2 * L + l, a1 * sq - a2 * cq);
+#pragma unroll
+    const int64_t t0i = ((int64_t)b * T + t) * L + l0;
+    float kz[4], dk[4];
+    if (vec) {
+      const float4 q = ld4(p.kz + t0i);
+      kz[0] = q.x; kz[1] = q.y; kz[2] = q.z; kz[3] = q.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) kz[k] = l0 + k < L ? p.kz[t0i + k] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int l = l0 + k;
+      if (l >= L) break;
+      const float d1 = a1[k] * iL, d2 = a2[k] * iL;
+      const float cq = CQ[y * CS + l], sq = SQ[y * CS + l], wr = p.wr[l], wi = p.wi[l];
+      const float dcq = d1 * wr - d2 * wi, dsq = d1 * wi + d2 * wr;
+      const float dpsi = -sq * dcq + cq * dsq;
+      dk[k] = dpsi * p.theta[l];
+      red_add(RED + l, dpsi * kz[k], quni);
+      red_add(RED + L + l, d1 * cq + d2 * sq, quni);
+      red_add(RED + 2 * L + l, d1 * sq - d2 * cq, quni);
+    }
+    if (vec) {
+      *reinterpret_cast<float4*>(gr.dkz + t0i) = make_float4(dk[0], dk[1], dk[2], dk[3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (l0 + k < L) gr.dkz[t0i + k] = dk[k];
+    }
   }
-  // owned keys: x in [n, NX) (s = t0 .. t0 + tq - 1) and, for the first CTA, [0, n) (the buffer)
+  // owned keys: rows x in [x0, NX) (s = t0 .. t0 + tq - 1, and the buffer for the first CTA)
   const int x0 = g.t0 == 0 ? 0 : n;
-  for (int u = tid; u < (NX - x0) * L; u += NT) {
-    const int x = x0 + u / L, l = u - (u / L) * L, s = g.t0 - n + x;
-    float dcw = 0.f, dsw = 0.f;
+  const int NO = NX - x0;
+  const bool kuni = (NO & 31) == 0 && x0 == n;  // one mode group per warp, every key s >= 0
+  const uint32_t mO = magic(NO);
+  for (int u = tid; u < NO * NG; u += NT) {
+    const int lg = qdiv(u, mO), x = x0 + u - lg * NO, l0 = 4 * lg, s = g.t0 - n + x;
+    float cw[4] = {0.f, 0.f, 0.f, 0.f}, sw[4] = {0.f, 0.f, 0.f, 0.f};
     for (int lag = 0; lag < L; ++lag) {
       const int y = x - n + lag;
       if (y < 0 || y >= NY) continue;
-      const float dr = DKR[y * L + lag], di = DKI[y * L + lag], q1 = Q1[y * LP + l], q2 = Q2[y * LP + l];
-      dcw = fmaf(dr, q1, fmaf(-di, q2, dcw));
-      dsw = fmaf(dr, q2, fmaf(di, q1, dsw));
+      const float r = DKR[y * KP + lag], i = DKI[y * KP + lag];
+      const float4 q1 = ld4(Q1 + y * CS + l0), q2 = ld4(Q2 + y * CS + l0);
+      const float a4[4] = {q1.x, q1.y, q1.z, q1.w}, b4[4] = {q2.x, q2.y, q2.z, q2.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        cw[k] = fmaf(r, a4[k], fmaf(-i, b4[k], cw[k]));
+        sw[k] = fmaf(r, b4[k], fmaf(i, a4[k], sw[k]));
+      }
     }
-    dcw *= iL;
-    dsw *= iL;
-    if (s >= T - n) {  // the key is also in the new ring buffer
-      const int64_t k = ((int64_t)b * n + (s - (T - n))) * L + l;
-      if (dc1) dcw += dc1[k];
-      if (ds1) dsw += ds1[k];
-    }
-    if (s >= 0) {
-      const float dphi = -KS[x * LP + l] * dcw + KC[x * LP + l] * dsw;
-      const int64_t si = ((int64_t)b * T + s) * L + l;
-      gr.dkh[si] = dphi * p.theta[l];
-      atomicAdd(RED + l, dphi * p.kh[si]);
-    } else {
-      const int64_t k = ((int64_t)b * n + n + s) * L + l;
-      if (gr.dc0) gr.dc0[k] = dcw;
-      if (gr.ds0) gr.ds0[k] = dsw;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int l = l0 + k;
+      if (l >= L) break;
+      float dcw = cw[k] * iL, dsw = sw[k] * iL;
+      if (s >= T - n) {  // the key is also in the new ring buffer
+        const int64_t kk = ((int64_t)b * n + (s - (T - n))) * L + l;
+        if (dc1) dcw += dc1[kk];
+        if (ds1) dsw += ds1[kk];
+      }
+      if (s >= 0) {
+        const float dphi = -KS[x * CS + l] * dcw + KC[x * CS + l] * dsw;
+        const int64_t si = ((int64_t)b * T + s) * L + l;
+        gr.dkh[si] = dphi * p.theta[l];
+        red_add(RED + l, dphi * p.kh[si], kuni);
+      } else {
+        const int64_t kk = ((int64_t)b * n + n + s) * L + l;
+        if (gr.dc0) gr.dc0[kk] = dcw;
+        if (gr.ds0) gr.ds0[kk] = dsw;
+      }
     }
   }
-  // owned keys' values: d e_s = sum over the queries reading s of kappa . dO
+  // owned keys' values: d e_s = sum over the queries reading s of kappa . dO (8 columns a thread)
   for (int j0 = 0; j0 < dv; j0 += DS) {
-    const int w = min(DS, dv - j0);
     __syncthreads();
-    for (int u = tid; u < NY * w; u += NT) {
-      const int y = u / w, j = u - (u / w) * w;
-      const float* row = dO + ((int64_t)b * T + g.t0 + y) * 2 * dv;
-      GR[y * DSP + j] = row[j0 + j];
-      GI[y * DSP + j] = row[dv + j0 + j];
-    }
+    load_grads(dO, g, b, NY, j0, GR, GI);
     __syncthreads();
-    for (int u = tid; u < (NX - x0) * w; u += NT) {
-      const int x = x0 + u / w, j = u - (u / w) * w, s = g.t0 - n + x;
-      float acc = 0.f;
+    for (int u = tid; u < NO * (DS / 8); u += NT) {
+      const int jg = qdiv(u, mO), x = x0 + u - jg * NO, jj = jg * 8, s = g.t0 - n + x;
+      float acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
       for (int lag = 0; lag < L; ++lag) {
         const int y = x - n + lag;
         if (y < 0 || y >= NY) continue;
-        acc = fmaf(KR[y * L + lag], GR[y * DSP + j], fmaf(KI[y * L + lag], GI[y * DSP + j], acc));
+        const float r = KR[y * KP + lag], i = KI[y * KP + lag];
+        const float4 a0 = ld4(GR + y * ES + jj), a1 = ld4(GR + y * ES + jj + 4);
+        const float4 c0 = ld4(GI + y * ES + jj), c1 = ld4(GI + y * ES + jj + 4);
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = fmaf(r, av[k], fmaf(i, cv[k], acc[k]));
       }
-      if (s >= T - n && de1) acc += de1[((int64_t)b * n + (s - (T - n))) * dv + j0 + j];
-      if (s >= 0)
-        gr.dv[((int64_t)b * T + s) * dv + j0 + j] = acc;
-      else if (gr.de0)
-        gr.de0[((int64_t)b * n + n + s) * dv + j0 + j] = acc;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int j = j0 + jj + k;
+        if (j >= dv) break;
+        float a = acc[k];
+        if (s >= T - n && de1) a += de1[((int64_t)b * n + (s - (T - n))) * dv + j];
+        if (s >= 0)
+          gr.dv[((int64_t)b * T + s) * dv + j] = a;
+        else if (gr.de0)
+          gr.de0[((int64_t)b * n + n + s) * dv + j] = a;
+      }
     }
   }
   __syncthreads();
@@ -334,23 +474,37 @@ __global__ void __launch_bounds__(NT) short_bwd_kernel(sca2_short_args p, const 
   for (int u = tid; u < 3 * L; u += NT) dst[u] = RED[u];
 }
 
-// dtheta, dwr, dwi = sums of the per-CTA partials (fixed order: deterministic)
-__global__ void short_reduce_kernel(const float* part, int nparts, int L, sca2_short_grads gr) {
-  const int u = blockIdx.x * blockDim.x + threadIdx.x;
-  if (u >= 3 * L) return;
+// dtheta, dwr, dwi: one block per output, a fixed-order tree over the per-CTA partials
+__global__ void __launch_bounds__(256) short_reduce_kernel(const float* part, int nparts, int L, sca2_short_grads gr) {
+  __shared__ float red[256];
+  const int u = blockIdx.x;
   float acc = 0.f;
-  for (int k = 0; k < nparts; ++k) acc += part[(int64_t)k * 3 * L + u];
-  float* out = u < L ? gr.dtheta : u < 2 * L ? gr.dwr : gr.dwi;
-  out[u % L] = acc;
+  for (int k = threadIdx.x; k < nparts; k += 256) acc += part[(int64_t)k * 3 * L + u];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    float* out = u < L ? gr.dtheta : u < 2 * L ? gr.dwr : gr.dwi;
+    out[u % L] = red[0];
+  }
 }
 
 }  // namespace shortk
 
+// Tokens per CTA: the largest of 64 / 32 / 16 whose shared memory lets two forward CTAs or
+// three backward CTAs (its register bound) share an SM (16 whenever it fits at all), with the
+// backward's pair groups within its register budget.
 int short_tokens_per_cta(int L, bool bwd, int max_smem) {
   const int cand[3] = {64, 32, 16};
-  for (int i = 0; i < 3; ++i) {
-    const size_t f = bwd ? shortk::bwd_smem_floats(L, cand[i]) : shortk::fwd_smem_floats(L, cand[i]);
-    if (f * sizeof(float) <= 112u * 1024u || (i == 2 && f * sizeof(float) <= (size_t)max_smem)) return cand[i];
+  const size_t lim = bwd ? 75u * 1024u : 112u * 1024u;
+  for (int i = bwd ? 0 : 1; i < 3; ++i) {
+    const int TT = cand[i];
+    const size_t f = bwd ? shortk::bwd_smem_floats(L, TT) : shortk::fwd_smem_floats(L, TT);
+    if (bwd && (TT + L - 1) * shortk::lane_groups(L) > 3 * shortk::NT) continue;
+    if (f * sizeof(float) <= lim || (i == 2 && f * sizeof(float) <= (size_t)max_smem)) return TT;
   }
   return 0;
 }
@@ -391,7 +545,7 @@ cudaError_t short_bwd(const sca2_short_args& p, const float* dO, const float* dc
   shortk::short_bwd_kernel<<<grid, shortk::NT, smem, st>>>(p, dO, dc1, ds1, de1, g, work, TT);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  shortk::short_reduce_kernel<<<(3 * p.L + 127) / 128, 128, 0, st>>>(work, p.B * nch, p.L, g);
+  shortk::short_reduce_kernel<<<3 * p.L, 256, 0, st>>>(work, p.B * nch, p.L, g);
   return cudaGetLastError();
 }
 

@@ -57,11 +57,47 @@ def build(name, cfg=None, seed=0, device="cpu", dtype=torch.float32):
     return v["wrap"](m) if v["wrap"] else m
 
 
+# short-window layers of the reference (sca2/arch_short.py:161-214): a long C head with the
+# short DFT head CHeadShort in the D slot.  The layer class fixes its C head (C_CLS), so the
+# B200 variant subclasses it with this package's C head and swaps the D slot after building.
+SHORT_LAYERS = {
+    "b200_cshort": ("ShortLayer", heads.CHeadDelta, "cshort (sca2/arch_short.py:161-177) on sm_100a"),
+    "b200_cshort_damph": ("ShortLayerDampH", heads.CHeadDeltaDampHalf,
+                          "cshort_damph (sca2/arch_short.py:199-201) on sm_100a"),
+}
+
+
+def use_b200_short(layer):
+    """wrap= hook: replace the reference CHeadShort in a built layer's D slot (`dh`) by
+    heads.CHeadShort with the same weights and read-out attributes."""
+    old = layer.dh
+    new = heads.CHeadShort(old.d, old.L, old.dv)
+    for a in ("rms_read", "gated_read", "rscale", "rgate"):
+        if hasattr(old, a):
+            setattr(new, a, getattr(old, a))
+    new.load_state_dict(old.state_dict(), strict=True)
+    p = next(old.parameters())
+    layer.dh = new.to(device=p.device, dtype=p.dtype)
+    return layer
+
+
 def install(target=None, d_cls=None, layer_cls=None):
     """Register this package's C heads into `target` (a registry module with the reference's
-    register(), e.g. sca2.registry), or into this module when target is None."""
+    register(), e.g. sca2.registry), or into this module when target is None.  With the
+    reference registry as target, the short-window layers are registered too (B200 C head
+    and B200 short head)."""
     reg = target.register if target is not None else register
     names = []
     for name, (cls, note) in C_HEADS.items():
         names.append(reg(name, c_cls=cls, d_cls=d_cls, note=note, layer_cls=layer_cls))
+    if target is not None:
+        import importlib
+        try:
+            ash = importlib.import_module(target.__name__.rsplit(".", 1)[0] + ".arch_short")
+        except ImportError:
+            ash = None
+        for name, (base, c_cls, note) in SHORT_LAYERS.items() if ash is not None else ():
+            lcls = type(name + "_layer", (getattr(ash, base),), {"C_CLS": c_cls})
+            names.append(reg(name, c_cls=c_cls, d_cls=None, note=note, wrap=use_b200_short,
+                             layer_cls=lcls, arch=True))
     return names

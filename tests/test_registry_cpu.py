@@ -60,3 +60,20 @@ def test_local_registry_build():
     registry.install(layer_cls=Layer)
     m = registry.build("b200_delta", {"d": 32, "M": 16, "dv": 16}, seed=1)
     assert isinstance(m.c, heads.CHeadDelta)
+
+
+def test_install_short_layers_into_reference():
+    """The short-window layers build through the reference registry with this package's C
+    head and short head, and load the reference layer's weights unchanged."""
+    ref = _ref_registry()
+    from sca2.ref import LayerCfg
+    registry.install(ref)
+    cfg = LayerCfg(d=64, Mc=32, Md=4, G=4, dv=32)
+    for name, ref_name in (("b200_cshort", "cshort"), ("b200_cshort_damph", "cshort_damph")):
+        mine = ref.build(name, cfg, seed=0)
+        assert isinstance(mine.dh, heads.CHeadShort)
+        assert isinstance(mine.c, registry.SHORT_LAYERS[name][1])
+        theirs = ref.build(ref_name, cfg, seed=0)
+        mine.load_state_dict(theirs.state_dict(), strict=True)
+        for k, v in theirs.state_dict().items():
+            assert torch.equal(mine.state_dict()[k], v), k
