@@ -14,6 +14,7 @@ hand-written kernels.  State dicts are the reference's: {"sr", "si"} fp32 plus a
 "pos" tensor (graph-capturable, sca2/decode.py:36-52).
 
   LongHead          lapa/layer.py:170-412            (per-mode decay, delta write)
+  CHeadRef          sca2/ref.py:164-206              (additive write)
   CHeadDelta        sca2/arch_cdelta.py:92-206       (delta write)
   CHeadDeltaDamp*   sca2/arch_damp.py:43-259         (per-mode decay, delta write)
   CHeadGated        sca2/arch_gatedc.py:58-193       (H heads, scalar decay, additive)
@@ -111,7 +112,7 @@ def _value_dtype(z: torch.Tensor) -> torch.dtype:
     """Dtype handed to the kernel for v / o: the autocast dtype on CUDA (the reference's
     gemm_dtype policy, lapa/layer.py:225-230), else float32."""
     if torch.is_autocast_enabled() and z.is_cuda:
-        dt = torch.get_autocast_gpu_dtype()
+        dt = torch.get_autocast_dtype("cuda")
         return dt if dt in (torch.bfloat16, torch.float32) else torch.float32
     return torch.bfloat16 if z.dtype == torch.bfloat16 else torch.float32
 
@@ -236,15 +237,12 @@ class CHeadBase(nn.Module):
         return self.prefill(z, h)[0]
 
 
-class CHeadDelta(CHeadBase):
-    """Error-correcting (delta) complex write, sca2/arch_cdelta.py:92-206."""
-    CTX = int(os.environ.get("SCA2_CTX_CHUNK", 256))
+class _PhaseHead(CHeadBase):
+    """Single-head phase-coded C head on ops.phase_scan / ops.phase_step; subclasses choose
+    the write gate (_beta), the decay (_lam), the value (_value) and the read-out (_out)."""
 
-    def __init__(self, *a, cdelta_init=-2.0, **kw):
-        super().__init__(*a, **kw)
-        self.bproj = nn.Linear(self.d, 1, True)
-        nn.init.zeros_(self.bproj.weight)
-        nn.init.constant_(self.bproj.bias, cdelta_init)
+    def _beta(self, z):
+        return None
 
     def _pw(self, h, p):
         return self.K(h).float() * self.theta.float() + p * self.omega.float()
@@ -269,7 +267,7 @@ class CHeadDelta(CHeadBase):
         S0 = None if st.get("empty", False) else torch.cat([st["sr"], st["si"]], 1)[:, None].float()
         o, S = ops.phase_scan(self._pw(h, p)[:, :, None], self._pq(z, p)[:, :, None],
                               self._value(z, h).to(_value_dtype(z))[:, :, None],
-                              torch.sigmoid(self.bproj(z).float()), None,
+                              self._beta(z), None,
                               None if lam is None else lam[None], self.wr.float()[None],
                               self.wi.float()[None], S0)
         M = self.M
@@ -282,11 +280,33 @@ class CHeadDelta(CHeadBase):
         lam = self._lam()
         S = torch.cat([state["sr"], state["si"]], 1)[:, None].float().contiguous()
         o, S = ops.phase_step(self._pw(h_t, p)[:, None], self._pq(z_t, p)[:, None],
-                              self._value(z_t, h_t).float()[:, None], torch.sigmoid(self.bproj(z_t).float()),
+                              self._value(z_t, h_t).float()[:, None], self._beta(z_t),
                               None, None if lam is None else lam[None], self.wr.float()[None],
                               self.wi.float()[None], S, S_out=S)
         u = self._out(o.reshape(-1, 2 * self.dv), z_t).to(z_t.dtype)
         return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": state["pos"] + 1, "empty": False}
+
+
+class CHeadRef(_PhaseHead):
+    """Additive complex write read with wr + i wi, sca2/ref.py:164-206 (the default C head
+    of SCA2Layer): the scan with no erase gate and no decay; u = rms(o)."""
+
+    def _out(self, u, z):
+        return _rms(u)
+
+
+class CHeadDelta(_PhaseHead):
+    """Error-correcting (delta) complex write, sca2/arch_cdelta.py:92-206."""
+    CTX = int(os.environ.get("SCA2_CTX_CHUNK", 256))
+
+    def __init__(self, *a, cdelta_init=-2.0, **kw):
+        super().__init__(*a, **kw)
+        self.bproj = nn.Linear(self.d, 1, True)
+        nn.init.zeros_(self.bproj.weight)
+        nn.init.constant_(self.bproj.bias, cdelta_init)
+
+    def _beta(self, z):
+        return torch.sigmoid(self.bproj(z).float())
 
 
 class CHeadDeltaDamp(CHeadDelta):

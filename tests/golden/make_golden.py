@@ -26,6 +26,11 @@ head-level ("head_*.npz")
     head_short_*.npz the short heads (lapa ShortHead, sca2 CHeadShort): prefill with state
     gradients, a second prefill shorter than the window, decode steps.
 
+layer-level ("layer_*.npz", "lm_lapa.npz")
+    Whole reference layers (SCA2Layer, GatedLayer, LaplaceAttention) with random weights:
+    output, new state, every gradient, decode steps; and a 2-layer LaplaceLM: logits,
+    cross-entropy gradients and a greedy generation.
+
 gdn_fla.npz
     fla 0.5.1 naive_chunk_gated_delta_rule / naive_recurrent_gated_delta_rule
     (the GDN baseline as called at lapa/benchmarks/baselines.py:111-120,142-144).
@@ -444,6 +449,105 @@ def head_short(gen, kind, B=2, T=45, d=24, L=8, dv=6, T2=3, steps=3, pos0=5):
                 **{"sd_" + k: v for k, v in sd.items()}, **grads)
 
 
+def _tree_np(prefix, x, out):
+    if isinstance(x, dict):
+        for k, v in x.items():
+            _tree_np(f"{prefix}.{k}", v, out)
+    elif isinstance(x, (list, tuple)):
+        for i, v in enumerate(x):
+            _tree_np(f"{prefix}.{i}", v, out)
+    elif torch.is_tensor(x):
+        out[prefix] = _np(x)
+    elif isinstance(x, (int, float)) and not isinstance(x, bool):
+        out[prefix] = np.array(x)
+    return out
+
+
+def layer_fixture(gen, kind, B=2, T=45, steps=3):
+    """A reference layer with random weights: prefill from its initial state, the output,
+    the new state, every parameter and input gradient of sum(y * dY), then `steps` decode
+    steps continuing from the prefill's state.  kind: "sca2" (SCA2Layer: CHeadRef + DHeadRef,
+    sca2/ref.py:333-390), "gated" (GatedLayer: CHeadGated 2 heads with decay + DHeadSepQPolar
+    + causal conv, sca2/arch_gatedc.py:199-256), "lapa" (LaplaceAttention, lapa/layer.py:551-600)."""
+    torch.manual_seed(int(torch.randint(0, 2**31 - 1, (1,), generator=gen)))
+    if kind == "lapa":
+        import lapa.layer as LL
+        layer = LL.LaplaceAttention(LL.LaplaceConfig(d=32, M=12, dv=8, L=8, ff=48, chunk=16,
+                                                     theta_scale=0.3)).double()
+        d = 32
+    else:
+        from sca2.ref import LayerCfg, SCA2Layer
+        from sca2.arch_gatedc import GatedLayer
+        if kind == "sca2":
+            cfg = LayerCfg(d=32, Mc=16, Md=4, G=4, ff=48, freq="rope", theta_scale=0.3, max_len=64, dv=32)
+            layer = SCA2Layer(cfg).double()
+        else:
+            # the reference's SCA2Layer passes rope_base / slow_frac, which its CHeadGated does not
+            # take: build through a shim that drops them (the GatedLayer itself is unchanged)
+            import sca2.arch_gatedc as AG
+            orig = AG.CHeadGated
+            AG.CHeadGated = lambda *a, rope_base=None, slow_frac=None, **kw: orig(*a, **kw)
+            try:
+                cfg = LayerCfg(d=32, Mc=16, Md=4, G=4, ff=48, freq="rope", theta_scale=0.3, max_len=64, dv=32,
+                               c_heads=2, c_decay=True, conv=3)
+                layer = GatedLayer(cfg).double()
+            finally:
+                AG.CHeadGated = orig
+        d = cfg.d
+    with torch.no_grad():  # move the read weights off their identity init
+        for n, p in layer.named_parameters():
+            if n.endswith("wr") or n.endswith("wi"):
+                p.add_(0.3 * torch.randn(p.shape, generator=gen, dtype=torch.float64))
+    x = torch.randn(B, T, d, generator=gen, dtype=torch.float64).requires_grad_(True)
+    y, st = layer.prefill(x)
+    dY = torch.randn(y.shape, generator=gen, dtype=torch.float64)
+    (y * dY).sum().backward()
+    out = dict(x=_np(x), y=_np(y), dY=_np(dY), d_x=_np(x.grad), meta=np.array([B, T, d, steps]))
+    out.update({"sd_" + k: _np(v) for k, v in layer.state_dict().items()})
+    out.update({"g_" + n: _np(p.grad) for n, p in layer.named_parameters() if p.grad is not None})
+    _tree_np("st", st, out)
+    xs = torch.randn(B, steps, d, generator=gen, dtype=torch.float64)
+    st = {k: (v.detach() if torch.is_tensor(v) else v) for k, v in st.items()}
+    st = _detach(st)
+    ys = []
+    with torch.no_grad():
+        for t in range(steps):
+            yt, st = layer.step(xs[:, t], st)
+            ys.append(yt)
+    out.update(xs=_np(xs), ys=_np(torch.stack(ys, 1)))
+    _tree_np("sts", st, out)
+    return out
+
+
+def _detach(x):
+    if isinstance(x, dict):
+        return {k: _detach(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return type(x)(_detach(v) for v in x)
+    return x.detach() if torch.is_tensor(x) else x
+
+
+def lm_fixture(gen, B=2, T=30, vocab=40, n_new=6):
+    """lapa.model.LaplaceLM (2 LaplaceAttention layers, lapa/model.py): logits of a token
+    batch, the gradients of the next-token cross entropy for every parameter, and a greedy
+    continuation of a prompt (prefill + steps)."""
+    import lapa.model as LM
+    torch.manual_seed(int(torch.randint(0, 2**31 - 1, (1,), generator=gen)))
+    lm = LM.LaplaceLM(vocab, d=32, n_layers=2, M=12, dv=8, L=8, ff=48, chunk=16, theta_scale=0.3).double()
+    tok = torch.randint(0, vocab, (B, T + 1), generator=gen)
+    logits = lm(tok[:, :-1])
+    loss = torch.nn.functional.cross_entropy(logits.reshape(-1, vocab), tok[:, 1:].reshape(-1))
+    loss.backward()
+    prompt = torch.randint(0, vocab, (B, 9), generator=gen)
+    with torch.no_grad():
+        gen_ids = lm.generate(prompt, n_new, greedy=True)
+    out = dict(tok=tok.numpy(), logits=_np(logits), loss=_np(loss), prompt=prompt.numpy(), gen=gen_ids.numpy(),
+               meta=np.array([B, T, vocab, 32, 2, n_new]))
+    out.update({"sd_" + k: _np(v) for k, v in lm.state_dict().items()})
+    out.update({"g_" + n: _np(p.grad) for n, p in lm.named_parameters() if p.grad is not None})
+    return out
+
+
 def main(ref_root):
     sys.path.insert(0, ref_root)
     import sca2.arch_short  # noqa: F401  registers cdelta/damp/short (see registry import order)
@@ -464,6 +568,10 @@ def main(ref_root):
     _save("head_dpolar.npz", **head_d(gen, "polar", M=16, G=4, dv=16))
     _save("head_short_lapa.npz", **head_short(gen, "lapa", L=8, dv=6))
     _save("head_short_sca2.npz", **head_short(gen, "sca2", L=16, dv=8, T=37, T2=5, pos0=13))
+    _save("layer_sca2.npz", **layer_fixture(gen, "sca2"))
+    _save("layer_gated.npz", **layer_fixture(gen, "gated"))
+    _save("layer_lapa.npz", **layer_fixture(gen, "lapa"))
+    _save("lm_lapa.npz", **lm_fixture(gen))
 
 
 if __name__ == "__main__":
