@@ -37,6 +37,12 @@ DECODE = dict(B=256, T=4096, H=16, Mh=64, V=128, steps=512)
 SP = dict(B=1, T=131072, H=16, Mh=32, V=64)  # one long sequence, split over the ranks
 DHEAD = dict(B=8, T=4096, M=16, G=8, V=64)   # D head of the reference LayerCfg (Md=16, G=8, dv=d/2)
 SHORT = dict(B=8, T=4096, L=16, dv=64, decode_B=256)  # short head, LapA default window L=16
+# one SCA2 layer (GatedLayer: 16 gated heads of d_head 64 + D head + mix + FFN), d_model 1024
+LAYER = dict(B=8, T=4096, d=1024, heads=16, Mh=32, dvh=64, Md=4, G=8, ff=4096)
+# 12-layer SCA2 LM training step (GatedLayer stack), d_model 768, 12 heads of d_head 64,
+# vocab 16384, T=2048, 32 sequences per GPU, Zipf(1.1) tokens, bf16 autocast, AdamW
+LMCFG = dict(B=32, T=2048, d=768, heads=12, Mh=32, dvh=64, Md=4, G=8, ff=3072, n_layers=12, vocab=16384,
+             steps=3, warmup=2, decode_B=64, prompt=128, decode_steps=64)
 # Algorithmic bytes per token per head (inputs read + outputs written once):
 #   fwd: phi, psi fp32 (2*Mh*4) + v bf16 (V*2) + beta (4) + o bf16 (2*V*2)
 #   bwd: dO bf16 (2*V*2) + inputs re-read (2*Mh*4 + V*2 + 4) + dphi, dpsi fp32 (2*Mh*4) + dv bf16 (V*2) + dbeta (4)
@@ -303,8 +309,16 @@ def run_gpu(args, rank, world, local_rank, dist):
     if not args.no_short:
         torch.cuda.empty_cache()
         sh = run_short(torch, ops, dev, rank, world, dist)
+    ly = None
+    if not args.no_layer:
+        torch.cuda.empty_cache()
+        ly = run_layer(torch, dev, rank, world, dist)
+    lmr = None
+    if not args.no_lm:
+        torch.cuda.empty_cache()
+        lmr = run_lm(torch, dev, rank, world, local_rank, dist)
     return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
-                decode=decode, sp=sp, dhead=dh, short=sh)
+                decode=decode, sp=sp, dhead=dh, short=sh, layer=ly, lm=lmr)
 
 
 def run_decode(torch, ops, dev, rank, world, dist):
@@ -521,6 +535,124 @@ def run_short(torch, ops, dev, rank, world, dist, reps=10):
                        "tokens_per_s": world * Bd / (dms / 1e3)}}
 
 
+def _gated_cfg(C, max_len):
+    from sca2_b200.layers import LayerCfg
+    return LayerCfg(d=C["d"], Mc=C["heads"] * C["Mh"], Md=C["Md"], G=C["G"], ff=C["ff"], freq="rope",
+                    theta_scale=0.02, max_len=max_len, dv=C["heads"] * C["dvh"], c_heads=C["heads"], c_decay=True)
+
+
+def run_layer(torch, dev, rank, world, dist, reps=5):
+    """One SCA2 layer (GatedLayer with this package's heads) forward + backward under bf16
+    autocast on B x T tokens per GPU: norm, 16-head gated C head (projections, phase scan on
+    the tensor-core kernels, read-out), D head, mix, FFN.  Weights N(0, 0.02^2)."""
+    from sca2_b200 import layers, lm as L
+    C = LAYER
+    torch.manual_seed(7 + rank)
+    layer = layers.GatedLayer(_gated_cfg(C, C["T"])).to(dev)
+    L.init_weights(layer)
+    x = torch.randn(C["B"], C["T"], C["d"], device=dev, requires_grad=True)
+    dy = torch.randn(C["B"], C["T"], C["d"], device=dev)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = layer(x)
+        torch.autograd.backward(y, dy)
+    ms = _timed(torch, dist, dev, step, reps)
+    n_par = sum(p.numel() for p in layer.parameters())
+    tok = C["B"] * C["T"]
+    return {"value": world * tok / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "config": {"layer": "GatedLayer", "batch": C["B"], "seq_len": C["T"], "d_model": C["d"],
+                       "heads": C["heads"], "d_head": 2 * C["Mh"], "ff": C["ff"], "dtype": "bf16 autocast",
+                       "fwd+bwd": True},
+            "params": n_par}
+
+
+def run_lm(torch, dev, rank, world, local_rank, dist):
+    """12-layer SCA2 LM training step (GatedLM) with AdamW under bf16 autocast, DDP over the
+    ranks when N > 1 (gradient all-reduce over NCCL, overlapped with the backward); then
+    greedy decoding of decode_B sequences with the whole stack's step in one CUDA graph."""
+    from sca2_b200 import lm as L
+    C = LMCFG
+    torch.manual_seed(11)
+    model = L.GatedLM(C["vocab"], _gated_cfg(C, C["T"]), n_layers=C["n_layers"]).to(dev)
+    L.init_weights(model)
+    n_par = sum(p.numel() for p in model.parameters())
+    net = model
+    if dist is not None:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank])
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+    tok = L.zipf_tokens(C["B"], C["T"] + 1, C["vocab"], seed=100 + rank, device=dev)
+    for _ in range(C["warmup"]):
+        L.train_step(net, opt, tok)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(C["steps"]):
+        loss = L.train_step(net, opt, tok)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / C["steps"]
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = C["B"] * C["T"]
+    flops = 6.0 * n_par * tokens * world
+    bf16_peak = _bf16_sustained()
+    out = {"value": world * tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "loss": float(loss),
+           "config": {"model": "GatedLM (12 x GatedLayer)", "n_layers": C["n_layers"], "d_model": C["d"],
+                      "heads": C["heads"], "d_head": 2 * C["Mh"], "vocab": C["vocab"], "ff": C["ff"],
+                      "seq_len": C["T"], "batch_per_gpu": C["B"], "dtype": "bf16 autocast", "optimizer": "AdamW",
+                      "data": "Zipf(1.1) token ids, seeded", "parallelism": f"ddp{world}" if world > 1 else "single"},
+           "params": n_par,
+           "model_tflops_per_s": flops / (ms * 1e-3) / 1e12,
+           "frac_of_bf16_peak": (flops / (ms * 1e-3) / 1e12) / (world * bf16_peak[0]),
+           "bf16_peak_tflops": bf16_peak[0], "bf16_peak_source": bf16_peak[1],
+           "flop_convention": "6 x parameters x tokens (scan FLOP not added)"}
+    del opt, net
+    torch.cuda.empty_cache()
+    # decode: prefill a prompt, then greedy tokens from one CUDA graph of the whole step
+    Bd = C["decode_B"]
+    model.eval()
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=False):
+        prompt = L.zipf_tokens(Bd, C["prompt"], C["vocab"], seed=200 + rank, device=dev)
+        logits, state = model.prefill(prompt)
+        dec = L.GraphDecoder(model, state)
+        first = logits[:, -1].argmax(-1)
+        for _ in range(3):
+            dec.step(first)
+        torch.cuda.synchronize()
+        e0.record(st)
+        tok_ = first
+        for _ in range(C["decode_steps"]):
+            tok_ = dec.step(tok_)
+        e1.record(st)
+        torch.cuda.synchronize()
+    dms = e0.elapsed_time(e1) / C["decode_steps"]
+    if dist is not None:
+        t = torch.tensor([dms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dms = float(t.item())
+    out["decode"] = {"batch": Bd, "prompt": C["prompt"], "ms_per_token_step": dms,
+                     "tokens_per_s": world * Bd / (dms / 1e3), "cuda_graph": True}
+    del dec
+    return out
+
+
+def _bf16_sustained():
+    """bf16 dense peak for a kernel mix timed inside a long step: the sustained cuBLAS figure."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m.get("bf16_tflops_sustained", m["bf16_tflops"])), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -542,6 +674,8 @@ def main():
     ap.add_argument("--no-sp", action="store_true")
     ap.add_argument("--no-dhead", action="store_true")
     ap.add_argument("--no-short", action="store_true")
+    ap.add_argument("--no-layer", action="store_true")
+    ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
@@ -646,6 +780,8 @@ def main():
         "sp_prefill": r["sp"],
         "d_head": r["dhead"],
         "short_head": r["short"],
+        "layer": r["layer"],
+        "lm_train": r["lm"],
     }
     print(json.dumps(line))
 
