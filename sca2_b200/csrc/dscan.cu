@@ -351,9 +351,16 @@ __global__ void __launch_bounds__(NT) dscan_bwd_carry(sca2_dscan_args p, const f
 }
 
 // gradient pass of one block from its incoming adjoint R(k)
+// Gate groups a CTA's channels can touch: its 256 / M channels in groups of gs = V / G
+__host__ __device__ inline int ngl_max(int M, int gs) { return (NT / M) / gs + 2; }
+
+// The gradients summed over channels (da per (t, m, g), and dc per (t, m) with the separable
+// read) are reduced per warp by shuffles, then across the CTA's warps with shared-memory
+// atomics, and leave the CTA as one global atomic per (t, m[, g]) instead of one per warp.
 template <int M, bool SEP>
 __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const float* dab, const float* ckpt,
                                                      const float* R, sca2_dscan_grads gr) {
+  extern __shared__ float sred[];
   const Map q = thread_map_c<M>(p);
   const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
   const int t0 = k * CK, n = min(CK, T - t0);
@@ -361,6 +368,13 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
   const int64_t bT = (int64_t)q.b * T;
   const int64_t base = ((int64_t)q.b * NK + k) * 2;
   constexpr float iM = 1.f / M;
+  const int gs = V / G, NGL = ngl_max(M, gs);
+  const int g0 = (blockIdx.z * (NT / M)) / gs;     // first gate group of this CTA's channels
+  float* sdc = sred;                              // [CK][M][2]            (separable read)
+  float* sda = sred + (SEP ? CK * M * 2 : 0);     // [CK][M][NGL][2]
+  const int nred = (SEP ? CK * M * 2 : 0) + CK * M * NGL * 2;
+  for (int u = threadIdx.x; u < nred; u += NT) sred[u] = 0.f;
+  __syncthreads();
   float dsr = q.live ? R[base * M * V + (int64_t)q.m * V + jc] : 0.f;
   float dsi = q.live ? R[(base + 1) * M * V + (int64_t)q.m * V + jc] : 0.f;
   float pr[CK], pi[CK];
@@ -396,9 +410,9 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
     const float dcr = q.live ? gA * sr + gB * si : 0.f, dci = q.live ? gA * si - gB * sr : 0.f;
     if (SEP) {
       const float xr = sum_j<M>(dcr), xi = sum_j<M>(dci);
-      if (q.jj == 0) {
-        atomicAdd(gr.dc_re + tm, xr);
-        atomicAdd(gr.dc_im + tm, xi);
+      if (q.jj == 0 && q.live) {  // lane jj = 0 holds the warp's first channel
+        atomicAdd(sdc + (u * M + q.m) * 2, xr);
+        atomicAdd(sdc + (u * M + q.m) * 2 + 1, xi);
       }
     } else if (q.live) {
       gr.dc_re[tm * V + q.j] = dcr;
@@ -408,13 +422,31 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
     if (q.m == 0 && q.live) gr.dv[(bT + t) * V + q.j] = dvt;
     const float dar = sum_j<M>(dsr * pr[u] + dsi * pi[u]);
     const float dai = sum_j<M>(-dsr * pi[u] + dsi * pr[u]);
-    if (q.jj == 0) {
-      atomicAdd(gr.da_re + tm * G + q.g, dar);
-      atomicAdd(gr.da_im + tm * G + q.g, dai);
+    if (q.jj == 0 && q.live) {
+      float* d = sda + ((u * M + q.m) * NGL + (q.g - g0)) * 2;
+      atomicAdd(d, dar);
+      atomicAdd(d + 1, dai);
     }
     const float ndr = ar * dsr + ai * dsi;
     dsi = -ai * dsr + ar * dsi;
     dsr = ndr;
+  }
+  __syncthreads();
+  if (SEP)
+    for (int u = threadIdx.x; u < n * M; u += NT) {
+      const int64_t tm = (bT + t0 + u / M) * M + (u % M);
+      atomicAdd(gr.dc_re + tm, sdc[u * 2]);
+      atomicAdd(gr.dc_im + tm, sdc[u * 2 + 1]);
+    }
+  for (int u = threadIdx.x; u < n * M * NGL; u += NT) {
+    const int gl = u % NGL, um = u / NGL, g = g0 + gl;
+    if (g >= G) continue;
+    const int64_t idx = ((bT + t0 + um / M) * M + (um % M)) * G + g;
+    const float xr = sda[u * 2], xi = sda[u * 2 + 1];
+    if (xr != 0.f || xi != 0.f) {  // groups outside this CTA's channels stay untouched
+      atomicAdd(gr.da_re + idx, xr);
+      atomicAdd(gr.da_im + idx, xi);
+    }
   }
 }
 
@@ -468,10 +500,11 @@ cudaError_t launch_bwd_m(const sca2_dscan_args& p, const float* dab, const float
   else
     dscan_bwd_local<M, false><<<gl, NT, 0, st>>>(p, dab, qv, Qg);
   dscan_bwd_carry<M><<<gc, NT, 0, st>>>(p, dS_re, dS_im, qv, Qg, R, g);
+  const int red = ((p.sep ? CK * M * 2 : 0) + CK * M * ngl_max(M, p.V / p.G) * 2) * (int)sizeof(float);
   if (p.sep)
-    dscan_bwd_block<M, true><<<gl, NT, 0, st>>>(p, dab, ckpt, R, g);
+    dscan_bwd_block<M, true><<<gl, NT, red, st>>>(p, dab, ckpt, R, g);
   else
-    dscan_bwd_block<M, false><<<gl, NT, 0, st>>>(p, dab, ckpt, R, g);
+    dscan_bwd_block<M, false><<<gl, NT, red, st>>>(p, dab, ckpt, R, g);
   return cudaGetLastError();
 }
 
