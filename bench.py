@@ -643,6 +643,17 @@ def run_lm(torch, dev, rank, world, local_rank, dist):
     return out
 
 
+def _traffic(kernel, B):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (captured at B=2,
+    scaled by the number of sequences), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            t = json.load(f)
+        return t[kernel]["captured_bytes_B2"] * B / 2
+    except Exception:
+        return None
+
+
 def _bf16_sustained():
     """bf16 dense peak for a kernel mix timed inside a long step: the sustained cuBLAS figure."""
     try:
@@ -771,11 +782,13 @@ def main():
         "dtype": "bf16", "data": "synthetic", "config": config,
         "roofline": {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
-                     "traffic": None, "algorithmic_bytes_per_launch": by, "ms_per_launch": ms},
+                     "traffic": _traffic(name, W["B"]), "traffic_source": "ncu dram bytes per launch, "
+                     "profiles/roofline_traffic.json (B=2 capture x B/2)",
+                     "algorithmic_bytes_per_launch": by, "ms_per_launch": ms},
         "kernels_ms": {"scan_fwd": r["fwd_ms"], "grad_zero_fill": r["zero_ms"], "scan_bwd": r["bwd_ms"]},
         "flops": {"algorithmic_tflop_per_step": 3 * 2 * mac / 1e12,
                   "achieved_tflops": 3 * 2 * mac / (r["ms_step"] * 1e-3) / 1e12, "peak_tflops": tfl},
-        "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"], "gpu_launches": 2 * args.steps,
+        "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"], "gpu_launches": 3 * args.steps,
         "decode": r["decode"],
         "sp_prefill": r["sp"],
         "d_head": r["dhead"],
