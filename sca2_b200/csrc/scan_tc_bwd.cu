@@ -54,9 +54,12 @@ struct BwdLayout {
   static constexpr int DOA = EB + VB * C * 2;      // RC x VB  dO             [(r,i)][v]
   static constexpr int CST = DOA + RC * VB * 2;    // fp32 KD x VB staged state [m][v]
   static constexpr int LAMS = CST + KD * VB * 4;   // fp32 KD x VB  state-side d(lam) terms [m][v]
-  static constexpr int CACHE = LAMS + KD * VB * 4; // fp32 phase: cos/sin phi, cos/sin psi [4][C][Mh]
-                                                   //      key:   k, q * scale [2][C][KD]
-  static constexpr int CACHE_BYTES = FL == SCA2_FLAVOR_PHASE ? 4 * C * Mh * 4 : 2 * C * KD * 4;
+  static constexpr int CACHE = LAMS + KD * VB * 4; // fp32 phase: cos/sin phi, cos/sin psi [4][C][CS]
+                                                   //      key:   k, q * scale [2][C][CS]
+  // cache row stride: 4 floats of padding put the rows of 8 consecutive tokens in distinct
+  // 16-byte bank groups, so the finish's 16-byte loads (one token row per lane) do not conflict
+  static constexpr int CS = (FL == SCA2_FLAVOR_PHASE ? Mh : KD) + 4;
+  static constexpr int CACHE_BYTES = FL == SCA2_FLAVOR_PHASE ? 4 * C * CS * 4 : 2 * C * CS * 4;
   static constexpr int R1 = CACHE + CACHE_BYTES;   // QRA (b1) | P (epi1-b2) | dQK (epi4-b5)
   static constexpr int R2 = R1 + RC * 64 * 2;      // KWW (b1) | dE (epi2-b3) | dKK (epi4-b5) | PQ (finish)
   static constexpr int R3 = R2 + C * 64 * 2;       // ZN (codes-b4) | (j-i) dKK (epi4-b5)
@@ -151,7 +154,8 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
   const int tid = threadIdx.x;
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;
-    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    int i, m0;
+    code_unit<Mh / 8>(tid, i, m0);
     const bool live = i < Cl;
     const float fi = (float)i, zb = -g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
     float c[8], s[8], cq[8], sq[8];
@@ -170,10 +174,11 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
       kc[k] = c[k] * ell; ks[k] = s[k] * ell; wc[k] = c[k] * elli; ws[k] = s[k] * elli;
       q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
     }
-    float4* cw = reinterpret_cast<float4*>(cache + (0 * C + i) * Mh + m0);
-    float4* sw = reinterpret_cast<float4*>(cache + (1 * C + i) * Mh + m0);
-    float4* cqp = reinterpret_cast<float4*>(cache + (2 * C + i) * Mh + m0);
-    float4* sqp = reinterpret_cast<float4*>(cache + (3 * C + i) * Mh + m0);
+    constexpr int CS = L::CS;
+    float4* cw = reinterpret_cast<float4*>(cache + (0 * C + i) * CS + m0);
+    float4* sw = reinterpret_cast<float4*>(cache + (1 * C + i) * CS + m0);
+    float4* cqp = reinterpret_cast<float4*>(cache + (2 * C + i) * CS + m0);
+    float4* sqp = reinterpret_cast<float4*>(cache + (3 * C + i) * CS + m0);
     cw[0] = make_float4(c[0], c[1], c[2], c[3]); cw[1] = make_float4(c[4], c[5], c[6], c[7]);
     sw[0] = make_float4(s[0], s[1], s[2], s[3]); sw[1] = make_float4(s[4], s[5], s[6], s[7]);
     cqp[0] = make_float4(cq[0], cq[1], cq[2], cq[3]); cqp[1] = make_float4(cq[4], cq[5], cq[6], cq[7]);
@@ -214,7 +219,8 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
   } else {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int unit = tid + u * NT, i = unit >> 3, m0 = (unit & 7) * 8;
+      int i, m0;
+      code_unit<KD / 8>(tid + u * NT, i, m0);
       const float fi = (float)i, zb = -g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
       float kk[8], qq[8], kc[8], wc[8], qc[8], t[8];
 #pragma unroll
@@ -225,8 +231,8 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
         qq[k] = q_scale * cr.q[u][k];
         kc[k] = kk[k] * ell; wc[k] = kk[k] * elli; qc[k] = qq[k] * ell;
       }
-      float4* kp = reinterpret_cast<float4*>(cache + (0 * C + i) * KD + m0);
-      float4* qp = reinterpret_cast<float4*>(cache + (1 * C + i) * KD + m0);
+      float4* kp = reinterpret_cast<float4*>(cache + (0 * C + i) * L::CS + m0);
+      float4* qp = reinterpret_cast<float4*>(cache + (1 * C + i) * L::CS + m0);
       kp[0] = make_float4(kk[0], kk[1], kk[2], kk[3]); kp[1] = make_float4(kk[4], kk[5], kk[6], kk[7]);
       qp[0] = make_float4(qq[0], qq[1], qq[2], qq[3]); qp[1] = make_float4(qq[4], qq[5], qq[6], qq[7]);
       st8(KR, umma::kmaj(i, m0, KD), kc);
@@ -244,6 +250,11 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
     }
   }
 }
+
+// Position of element m of token row i in the finish's fp32 staging arrays (rows of KH >= 32
+// floats): the 16-byte chunk index is XORed with i mod 8, so the rows of 8 consecutive tokens
+// put a given chunk in 8 distinct bank groups (the staging stores have one token row per lane).
+__device__ __forceinline__ int swz(int i, int m) { return ((((m >> 2) ^ (i & 7))) << 2) | (m & 3); }
 
 // sum over the 16 row-owning lanes of an M = 64 fragment (lanes 0..15); result in lane 0
 __device__ __forceinline__ float sum16(float x) {
@@ -733,6 +744,11 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           const int i = rows[ri];
           const bool own = i < Cl;
           const float fi = (float)i, bi = gates.beta[i], aik = gates.a[i] * ik, wi_ = gates.w[i];
+          // the two modes' cached codes as one 8-byte load (rows padded: conflict-free)
+          const float2 c2 = *reinterpret_cast<const float2*>(cache + (0 * C + i) * L::CS + m0);
+          const float2 s2 = FL == SCA2_FLAVOR_PHASE
+                                ? *reinterpret_cast<const float2*>(cache + (1 * C + i) * L::CS + m0)
+                                : c2;
           float dv2[2];
 #pragma unroll
           for (int mi = 0; mi < 2; ++mi) {
@@ -741,7 +757,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             const float ell = __expf(-l * fi), elli = __expf(l * fi);
             float dvv = 0.f;
             if constexpr (FL == SCA2_FLAVOR_PHASE) {
-              const float c = cache[(0 * C + i) * Mh + m], s = cache[(1 * C + i) * Mh + m];
+              const float c = mi ? c2.y : c2.x, s = mi ? s2.y : s2.x;
               const float krc = c * ell, krs = s * ell, kwc = c * elli, kws = s * elli;
               const float rc = aik * a2[0][e], rs = aik * a2[1][e];
               const float dkrc = a1[0][e] * ik - bi * rc, dkrs = a1[1][e] * ik - bi * rs;
@@ -755,7 +771,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
                 if (p.lam) dl[mi] += ik * (kwc * lw[0][e] + kws * lw[1][e]) + fi * bi * kr_r + (fi - fi_last) * wi_ * kw_w3;
               }
             } else {
-              const float kk = cache[(0 * C + i) * KD + m];
+              const float kk = mi ? c2.y : c2.x;
               const float kr = kk * ell, kw = kk * elli;
               const float rr = aik * a2[0][e];
               const float dkr = a1[0][e] * ik - bi * rr, dkw = w12[0][e] * ik + wi_ * w3[0][e];
@@ -768,7 +784,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             }
             dv2[mi] = own ? dvv : 0.f;
           }
-          *reinterpret_cast<float2*>(PK + i * KH + m0) = make_float2(dv2[0], dv2[1]);
+          *reinterpret_cast<float2*>(PK + i * KH + swz(i, m0)) = make_float2(dv2[0], dv2[1]);
         }
         if (p.lam) {  // sum over the 16 rows: lanes with the same column pair
 #pragma unroll
@@ -828,8 +844,14 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             pq[k] = dwr[k] = dwi[k] = dl[k] = 0.f;
           }
           if (own) {
-            const float* cqp = cache + (2 * C + i) * Mh + mg;
-            const float* sqp = cache + (3 * C + i) * Mh + mg;
+            float cqp[8], sqp[8];
+            {
+              const float4* c4 = reinterpret_cast<const float4*>(cache + (2 * C + i) * L::CS + mg);
+              const float4* s4 = reinterpret_cast<const float4*>(cache + (3 * C + i) * L::CS + mg);
+              const float4 a = c4[0], b = c4[1], cc = s4[0], d = s4[1];
+              cqp[0] = a.x; cqp[1] = a.y; cqp[2] = a.z; cqp[3] = a.w; cqp[4] = b.x; cqp[5] = b.y; cqp[6] = b.z; cqp[7] = b.w;
+              sqp[0] = cc.x; sqp[1] = cc.y; sqp[2] = cc.z; sqp[3] = cc.w; sqp[4] = d.x; sqp[5] = d.y; sqp[6] = d.z; sqp[7] = d.w;
+            }
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int m = mg + k;
@@ -851,9 +873,9 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           }
           // each read column's part of d(psi) -> PQ0 / PQ1 (zero rows beyond the chunk)
           {
-            float4* d = reinterpret_cast<float4*>((r ? PQ1 : PQ0) + i * Mh + mg);
-            d[0] = make_float4(pq[0], pq[1], pq[2], pq[3]);
-            d[1] = make_float4(pq[4], pq[5], pq[6], pq[7]);
+            float* d = (r ? PQ1 : PQ0) + i * Mh;
+            *reinterpret_cast<float4*>(d + swz(i, mg)) = make_float4(pq[0], pq[1], pq[2], pq[3]);
+            *reinterpret_cast<float4*>(d + swz(i, mg + 4)) = make_float4(pq[4], pq[5], pq[6], pq[7]);
           }
           float x = warp_transpose_sum<8>(dwr);
           if ((lane & 3) == 0) atomicAdd(&s_dwr[mg + red_index<8>(lane)], x);
@@ -884,7 +906,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             dqv[k] = 0.f;
           }
           if (own) {
-            const float* qp = cache + (1 * C + i) * KD + m0;
+            float qp[8];
+            {
+              const float4* q4 = reinterpret_cast<const float4*>(cache + (1 * C + i) * L::CS + m0);
+              const float4 a = q4[0], b = q4[1];
+              qp[0] = a.x; qp[1] = a.y; qp[2] = a.z; qp[3] = a.w; qp[4] = b.x; qp[5] = b.y; qp[6] = b.z; qp[7] = b.w;
+            }
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int m = m0 + k;
@@ -897,9 +924,9 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             }
           }
           if (owns_rows<RC>()) {
-            float4* d = reinterpret_cast<float4*>(PQ0 + i * KD + m0);
-            d[0] = make_float4(dqv[0], dqv[1], dqv[2], dqv[3]);
-            d[1] = make_float4(dqv[4], dqv[5], dqv[6], dqv[7]);
+            float* d = PQ0 + i * KD;
+            *reinterpret_cast<float4*>(d + swz(i, m0)) = make_float4(dqv[0], dqv[1], dqv[2], dqv[3]);
+            *reinterpret_cast<float4*>(d + swz(i, m0 + 4)) = make_float4(dqv[4], dqv[5], dqv[6], dqv[7]);
           }
           if (p.lam) {
             const float x = warp_transpose_sum<8>(dl);
@@ -920,9 +947,16 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         if (i >= Cl) continue;
         float y[8], z[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          y[k] = PK[i * KH + m0 + k];
-          z[k] = PQ0[i * KH + m0 + k] + (FL == SCA2_FLAVOR_PHASE ? PQ1[i * KH + m0 + k] : 0.f);
+        for (int hh = 0; hh < 2; ++hh) {
+          const int o = i * KH + swz(i, m0 + 4 * hh);
+          const float4 a = *reinterpret_cast<const float4*>(PK + o);
+          float4 q = *reinterpret_cast<const float4*>(PQ0 + o);
+          if (FL == SCA2_FLAVOR_PHASE) {
+            const float4 q1 = *reinterpret_cast<const float4*>(PQ1 + o);
+            q.x += q1.x; q.y += q1.y; q.z += q1.z; q.w += q1.w;
+          }
+          y[4 * hh] = a.x; y[4 * hh + 1] = a.y; y[4 * hh + 2] = a.z; y[4 * hh + 3] = a.w;
+          z[4 * hh] = q.x; z[4 * hh + 1] = q.y; z[4 * hh + 2] = q.z; z[4 * hh + 3] = q.w;
         }
         acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, y, gvec, excl, gstage ? GRW + i * KH + m0 : nullptr);
         acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, z, gvec, excl, gstage ? GRQ + i * KH + m0 : nullptr);

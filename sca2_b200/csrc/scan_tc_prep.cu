@@ -74,7 +74,8 @@ __global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* c
   // ---- codes kr, kw (bf16, [i][m])
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;
-    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    int i, m0;
+    code_unit<KD / 16>(tid, i, m0);
     const float fi = (float)i;
     float kc[8], ks[8], wc[8], ws[8];
 #pragma unroll
@@ -93,7 +94,8 @@ __global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* c
     constexpr int MB = KD / 8;
 #pragma unroll
     for (int u = 0; u < CodeRegs<FL, KD>::NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      int i, m0;
+      code_unit<MB>(tid + u * NT, i, m0);
       const float fi = (float)i;
       float kc[8], wc[8];
 #pragma unroll

@@ -230,6 +230,17 @@ __device__ __forceinline__ void store_T(const float* TS, bf16* TB) {
   }
 }
 
+// ---- code units ---------------------------------------------------------------------------
+// Code unit u = (token i, 8 consecutive modes / dims from m0), MB units per token: the 8 lanes of
+// a quarter-warp take 8 consecutive tokens of the same 8 modes, so their 16-byte stores into a
+// K-major operand (token rows 16 bytes apart within a core-matrix group) fill one 128-byte line
+// instead of hitting one bank group 4 or 8 times.
+template <int MB>
+__device__ __forceinline__ void code_unit(int u, int& i, int& m0) {
+  i = (u & 7) + 8 * (u / (8 * MB));
+  m0 = ((u >> 3) % MB) * 8;
+}
+
 // ---- per-chunk gates ----------------------------------------------------------------------
 // beta, cumulative log-decay Gc, a = exp(Gc), w = exp(Gc_last - Gc) for the chunk's 64 tokens
 // (one warp); rows i >= Cl get beta = 0, g = 0, w = 0.
@@ -251,7 +262,8 @@ __device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs
                                                int t0, int Cl) {
   const int tid = threadIdx.x;
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
-    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    int i, m0;
+    code_unit<KD / 16>(tid, i, m0);
     const float* pw = reinterpret_cast<const float*>(p.phw.ptr);
     const float* pq = reinterpret_cast<const float*>(p.phq.ptr);
     if (i < Cl) {
@@ -275,7 +287,8 @@ __device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs
     constexpr int MB = KD / 8;
 #pragma unroll
     for (int u = 0; u < CodeRegs<FL, KD>::NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      int i, m0;
+      code_unit<MB>(tid + u * NT, i, m0);
       if (i < Cl) {
         const int64_t ok = tok_off(p.phw, b, t0 + i, h) + m0, oq = tok_off(p.phq, b, t0 + i, h) + m0;
         if (vec) {
@@ -353,7 +366,8 @@ __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;
     static_assert(C * Mh / 8 == NT, "one (token, 8 modes) unit per thread");
-    const int i = tid >> 2, m0 = (tid & 3) * 8;
+    int i, m0;
+    code_unit<KD / 16>(tid, i, m0);
     const bool live = i < Cl;
     const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
     float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
@@ -397,7 +411,8 @@ __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>
     constexpr int MB = KD / 8, NU = CodeRegs<FL, KD>::NU;
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
-      const int unit = tid + u * NT, i = unit / MB, m0 = (unit % MB) * 8;
+      int i, m0;
+      code_unit<MB>(tid + u * NT, i, m0);
       const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
       float kc[8], wc[8], qc[8], t[8];
 #pragma unroll
