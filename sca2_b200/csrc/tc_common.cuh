@@ -219,7 +219,7 @@ __device__ inline void invert_unit_lower(const float* LS, float* TS, float* WS) 
 template <bool TRANSPOSED>
 __device__ __forceinline__ void store_T(const float* TS, bf16* TB) {
   for (int u = threadIdx.x; u < C * C / 8; u += NT) {
-    const int i = u >> 3, j0 = (u & 7) * 8;
+    const int i = (u & 7) + 8 * (u >> 6), j0 = ((u >> 3) & 7) * 8;  // conflict-free 16-byte stores
     float x[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -440,7 +440,8 @@ template <int VB>
 __device__ __forceinline__ void pf_values(const sca2_scan_args& p, bf16* VA, bool vec, int b, int h, int t0, int Cl,
                                           int vb0) {
   for (int u = threadIdx.x; u < C * (VB / 8); u += NT) {
-    const int j = u / (VB / 8), v0 = (u % (VB / 8)) * 8;
+    // 8 consecutive rows of the same 8 columns per quarter-warp: conflict-free 16-byte writes
+    const int j = (u & 7) + 8 * (u / VB), v0 = ((u >> 3) % (VB / 8)) * 8;
     const bool live = j < Cl && vb0 + v0 < p.V;
     const int64_t off = live ? tok_off(p.v, b, t0 + j, h) + vb0 + v0 : 0;
     bf16* dst = VA + umma::kmaj(j, v0, VB);
@@ -458,7 +459,7 @@ __device__ __forceinline__ void pf_values(const sca2_scan_args& p, bf16* VA, boo
 template <int VB>
 __device__ __forceinline__ void scale_values(bf16* VA, const float* s_beta) {
   for (int u = threadIdx.x; u < C * (VB / 8); u += NT) {
-    const int j = u / (VB / 8), v0 = (u % (VB / 8)) * 8;
+    const int j = (u & 7) + 8 * (u / VB), v0 = ((u >> 3) % (VB / 8)) * 8;
     bf16* q = VA + umma::kmaj(j, v0, VB);
     const uint4 raw = *reinterpret_cast<const uint4*>(q);
     const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
