@@ -255,31 +255,58 @@ def run_gpu(args, rank, world, local_rank, dist):
         total_ms = float(t.item())
     ms_step = total_ms / args.steps
 
-    # ---- end to end through the public API: host (pinned) inputs -> device, fwd + bwd, result -> host
+    # ---- end to end through the public API: host (pinned) inputs -> device, fwd + bwd, result -> host.
+    # Two device input sets: the next step's host-to-device copies run on a copy stream while
+    # the current step computes (every step's inputs still cross PCIe inside the timed region).
     e2e = None
     if not args.no_e2e:
-        host = {k: x[k].cpu().pin_memory() for k in ("phw", "phq", "v", "beta", "dO")}
+        keys = ("phw", "phq", "v", "beta", "dO")
+        host = {k: x[k].cpu().pin_memory() for k in keys}
         h2d = sum(t.numel() * t.element_size() for t in host.values())
         res = torch.empty(B, H, 2 * Mh, V, dtype=torch.float32).pin_memory()
+        bufs = [{k: torch.empty_like(x[k]) for k in keys} for _ in range(2)]
+        cs = torch.cuda.Stream(device=dev)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        used = [False, False]
 
-        def e2e_step():
-            d = {k: t.to(dev, non_blocking=True) for k, t in host.items()}
+        def copy_in(i):
+            sl = i % 2
+            with torch.cuda.stream(cs):
+                if used[sl]:
+                    cs.wait_event(free[sl])
+                for k in keys:
+                    bufs[sl][k].copy_(host[k], non_blocking=True)
+                ready[sl].record(cs)
+
+        def compute(i):
+            sl = i % 2
+            st.wait_event(ready[sl])
+            d = dict(bufs[sl])
             for k in ("phw", "phq", "v"):
-                d[k].requires_grad_(True)
+                d[k] = d[k].detach().requires_grad_(True)  # leaf over the buffer's storage
             o, S = ops.phase_scan(d["phw"], d["phq"], d["v"], d["beta"], None, x["lam"], x["wr"], x["wi"])
             torch.autograd.backward(o, d["dO"])
             res.copy_(S.detach(), non_blocking=True)
+            free[sl].record(st)
+            used[sl] = True
 
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
+        def run(n):
+            copy_in(0)
+            for i in range(n):
+                if i + 1 < n:
+                    copy_in(i + 1)
+                compute(i)
+
+        run(max(1, args.warmup))
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n_e2e = max(1, min(args.steps, 10))
+        n_e2e = max(2, min(args.steps, 10))
         e0.record(st)
-        for _ in range(n_e2e):
-            e2e_step()
+        cs.wait_stream(st)  # the first copy starts inside the timed region
+        run(n_e2e)
         e1.record(st)
         torch.cuda.synchronize()
         em = e0.elapsed_time(e1) / n_e2e
@@ -288,8 +315,9 @@ def run_gpu(args, rank, world, local_rank, dist):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             em = float(t.item())
         e2e = {"value": world * B * T / (em / 1e3), "unit": "tokens/s", "ms_per_step": em,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": res.numel() * 4}
-        del host
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": res.numel() * 4,
+               "pipelining": "next step's H2D on a copy stream overlaps the current step's compute"}
+        del host, bufs
 
     # ---- decode (config: batch 256, H=16, K=V=128, 4096-token prefill, 512 steps)
     decode = None
