@@ -105,65 +105,115 @@ def _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0):
         raise _lib.Sca2Error(f"S0 must be (B,H,2Mh,V), got {tuple(S0.shape)}")
 
 
-class _PhaseScan(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, phw, phq, v, beta, g, lam, wr, wi, S0):
-        _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0)
-        phw, phq = _inner(phw.float()), _inner(phq.float())
-        v = _inner(v)
-        beta, g = _f32(beta), _f32(g)
-        lam = None if lam is None else lam.float().contiguous()
-        wr, wi = wr.float().contiguous(), wi.float().contiguous()
-        S0 = None if S0 is None else S0.float().contiguous()
-        a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
-        B, T, H, Mh = phw.shape
-        V = v.shape[-1]
-        o = torch.empty(B, T, H, 2, V, device=v.device, dtype=v.dtype)
-        S = torch.empty(B, H, 2 * Mh, V, device=v.device, dtype=torch.float32)
-        lib = _lib.load()
-        need = any(ctx.needs_input_grad)
-        cs = None
-        if need:
-            NC = lib.sca2_num_chunks(T)
-            cs = torch.empty(B, H, NC, 2 * Mh, V, device=v.device, dtype=torch.float32)
-        _lib.check(lib.sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs), _stream()), "scan_fwd")
-        if need:
-            ctx.save_for_backward(phw, phq, v, beta, g, lam, wr, wi, S0, cs)
-        return o, S
+def _slots(T: int) -> int:
+    """Saved-state slots of the chunk-state buffer (the library's sca2_num_chunks)."""
+    return 2 * ((T + 63) // 64) if T > 0 else 0
 
-    @staticmethod
-    def backward(ctx, do, dS):
-        phw, phq, v, beta, g, lam, wr, wi, S0, cs = ctx.saved_tensors
-        B, T, H, Mh = phw.shape
-        V = v.shape[-1]
-        dev = v.device
-        if do is None:
-            do = torch.zeros(B, T, H, 2, V, device=dev, dtype=v.dtype)
-        do = do.to(v.dtype)
-        if do.stride(-1) != 1:
-            do = do.contiguous()
-        dS = None if dS is None else dS.float().contiguous()
-        a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
-        z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
-        dphw, dphq = z(B, T, H, Mh), z(B, T, H, Mh)
-        dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
-        dbeta = z(B, T, H) if beta is not None else None
-        dg = z(B, T, H) if g is not None else None
-        dlam = z(H, Mh) if lam is not None else None
-        dwr, dwi = z(H, Mh), z(H, Mh)
-        dS0 = torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32)
-        gr = ScanGrads()
-        gr.dphw, gr.dphq, gr.dv = _tok(dphw), _tok(dphq), _tok(dv)
-        gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
-        gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), _ptr(dwr), _ptr(dwi), _ptr(dS0)
-        lib = _lib.load()
-        _lib.check(lib.sca2_scan_bwd(C_ref(a), _out(do), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
-                   "scan_bwd")
-        ni = ctx.needs_input_grad
-        return (dphw if ni[0] else None, dphq if ni[1] else None, dv if ni[2] else None,
-                dbeta if ni[3] else None, dg if ni[4] else None, dlam if ni[5] else None,
-                dwr if ni[6] else None, dwi if ni[7] else None,
-                dS0 if (ni[8] and S0 is not None) else None)
+
+@torch.library.custom_op("sca2b200::phase_scan_fwd", mutates_args=())
+def _phase_scan_fwd(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
+                    g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
+                    S0: Optional[torch.Tensor], save: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_scan_fwd: o (B,T,H,2,V), S (B,H,2Mh,V) and, with save, the chunk-state buffer
+    for the backward (else an empty tensor)."""
+    _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0)
+    phw, phq = _inner(phw.float()), _inner(phq.float())
+    v = _inner(v)
+    beta, g = _f32(beta), _f32(g)
+    lam = None if lam is None else lam.float().contiguous()
+    wr, wi = wr.float().contiguous(), wi.float().contiguous()
+    S0 = None if S0 is None else S0.float().contiguous()
+    a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
+    B, T, H, Mh = phw.shape
+    V = v.shape[-1]
+    o = torch.empty(B, T, H, 2, V, device=v.device, dtype=v.dtype)
+    S = torch.empty(B, H, 2 * Mh, V, device=v.device, dtype=torch.float32)
+    cs = (torch.empty(B, H, _slots(T), 2 * Mh, V, device=v.device, dtype=torch.float32) if save
+          else torch.empty(0, device=v.device, dtype=torch.float32))
+    _lib.check(_lib.load().sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs) if save else None, _stream()),
+               "scan_fwd")
+    return o, S, cs
+
+
+@_phase_scan_fwd.register_fake
+def _(phw, phq, v, beta, g, lam, wr, wi, S0, save):
+    B, T, H, Mh = phw.shape
+    V = v.shape[-1]
+    return (v.new_empty(B, T, H, 2, V), v.new_empty(B, H, 2 * Mh, V, dtype=torch.float32),
+            v.new_empty((B, H, _slots(T), 2 * Mh, V) if save else (0,), dtype=torch.float32))
+
+
+@torch.library.custom_op("sca2b200::phase_scan_bwd", mutates_args=())
+def _phase_scan_bwd(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
+                    g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
+                    S0: Optional[torch.Tensor], cs: torch.Tensor, do: torch.Tensor, dS: Optional[torch.Tensor]
+                    ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                               torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_scan_bwd: gradients of (phw, phq, v, beta, g, lam, wr, wi, S0); an input given
+    as None gets an empty gradient."""
+    phw, phq = _inner(phw.float()), _inner(phq.float())
+    v = _inner(v)
+    beta, g = _f32(beta), _f32(g)
+    lam = None if lam is None else lam.float().contiguous()
+    wr, wi = wr.float().contiguous(), wi.float().contiguous()
+    S0 = None if S0 is None else S0.float().contiguous()
+    B, T, H, Mh = phw.shape
+    V = v.shape[-1]
+    dev = v.device
+    do = do.to(v.dtype)
+    if do.stride(-1) != 1:
+        do = do.contiguous()
+    dS = None if dS is None else dS.float().contiguous()
+    a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
+    z = lambda *sh: torch.zeros(*sh, device=dev, dtype=torch.float32)
+    E = lambda: torch.empty(0, device=dev, dtype=torch.float32)  # the gradient of an absent input
+    dphw, dphq = z(B, T, H, Mh), z(B, T, H, Mh)
+    dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
+    dbeta = z(B, T, H) if beta is not None else None
+    dg = z(B, T, H) if g is not None else None
+    dlam = z(H, Mh) if lam is not None else None
+    dwr, dwi = z(H, Mh), z(H, Mh)
+    dS0 = torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32)
+    gr = ScanGrads()
+    gr.dphw, gr.dphq, gr.dv = _tok(dphw), _tok(dphq), _tok(dv)
+    gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
+    gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), _ptr(dwr), _ptr(dwi), _ptr(dS0)
+    _lib.check(_lib.load().sca2_scan_bwd(C_ref(a), _out(do), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
+               "scan_bwd")
+    return (dphw, dphq, dv, E() if dbeta is None else dbeta, E() if dg is None else dg,
+            E() if dlam is None else dlam, dwr, dwi, dS0 if S0 is not None else E())
+
+
+@_phase_scan_bwd.register_fake
+def _(phw, phq, v, beta, g, lam, wr, wi, S0, cs, do, dS):
+    B, T, H, Mh = phw.shape
+    V = v.shape[-1]
+    f = lambda *sh: v.new_empty(*sh, dtype=torch.float32)
+    return (f(B, T, H, Mh), f(B, T, H, Mh), v.new_empty(B, T, H, V), f(B, T, H) if beta is not None else f(0),
+            f(B, T, H) if g is not None else f(0), f(H, Mh) if lam is not None else f(0), f(H, Mh), f(H, Mh),
+            f(B, H, 2 * Mh, V) if S0 is not None else f(0))
+
+
+def _phase_setup(ctx, inputs, output):
+    phw, phq, v, beta, g, lam, wr, wi, S0, save = inputs
+    ctx.save_for_backward(phw, phq, v, beta, g, lam, wr, wi, S0, output[2])
+
+
+def _phase_backward(ctx, do, dS, dcs):
+    phw, phq, v, beta, g, lam, wr, wi, S0, cs = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*phw.shape[:3], 2, v.shape[-1], device=v.device, dtype=v.dtype)
+    grads = torch.ops.sca2b200.phase_scan_bwd(phw, phq, v, beta, g, lam, wr, wi, S0, cs, do, dS)
+    ni = ctx.needs_input_grad
+    ins = (phw, phq, v, beta, g, lam, wr, wi, S0)
+    return tuple(gd if (ni[k] and ins[k] is not None) else None for k, gd in enumerate(grads)) + (None,)
+
+
+_phase_scan_fwd.register_autograd(_phase_backward, setup_context=_phase_setup)
+
+
+def _wants_grad(*ts):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
 
 
 def C_ref(x):
@@ -184,7 +234,10 @@ def phase_scan(phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None, S0=No
     _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0)
     if wr is None or wi is None:
         raise _lib.Sca2Error("wr and wi are required")
-    return _PhaseScan.apply(phw, phq, v, beta, g, lam, wr, wi, S0)
+    _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0)
+    save = _wants_grad(phw, phq, v, beta, g, lam, wr, wi, S0)
+    o, S, _ = torch.ops.sca2b200.phase_scan_fwd(phw, phq, v, beta, g, lam, wr, wi, S0, save)
+    return o, S
 
 
 # ======================================================================================
@@ -204,63 +257,103 @@ def _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta):
     return a
 
 
-class _KeyScan(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, q, k, v, g, beta, lam, S0, scale, v_times_beta):
-        _need_cuda(q, k, v, g, beta, lam, S0)
-        dt = v.dtype
-        q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
-        g, beta = _f32(g), _f32(beta)
-        lam = None if lam is None else lam.float().contiguous()
-        S0 = None if S0 is None else S0.float().contiguous()
-        a = _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta)
-        B, T, H, K = k.shape
-        V = v.shape[-1]
-        o = torch.empty(B, T, H, 1, V, device=v.device, dtype=dt)
-        S = torch.empty(B, H, K, V, device=v.device, dtype=torch.float32)
-        lib = _lib.load()
-        need = any(ctx.needs_input_grad)
-        cs = None
-        if need:
-            cs = torch.empty(B, H, lib.sca2_num_chunks(T), K, V, device=v.device, dtype=torch.float32)
-        _lib.check(lib.sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs), _stream()), "scan_fwd")
-        if need:
-            ctx.save_for_backward(q, k, v, g, beta, lam, S0, cs)
-            ctx.scale, ctx.vtb = scale, v_times_beta
-        return o[:, :, :, 0], S
+@torch.library.custom_op("sca2b200::key_scan_fwd", mutates_args=())
+def _key_scan_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional[torch.Tensor],
+                  beta: Optional[torch.Tensor], lam: Optional[torch.Tensor], S0: Optional[torch.Tensor], scale: float,
+                  v_times_beta: bool, save: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_scan_fwd, key flavour: o (B,T,H,V), S (B,H,K,V), chunk states (or empty)."""
+    _need_cuda(q, k, v, g, beta, lam, S0)
+    dt = v.dtype
+    q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
+    g, beta = _f32(g), _f32(beta)
+    lam = None if lam is None else lam.float().contiguous()
+    S0 = None if S0 is None else S0.float().contiguous()
+    a = _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta)
+    B, T, H, K = k.shape
+    V = v.shape[-1]
+    o = torch.empty(B, T, H, V, device=v.device, dtype=dt)
+    S = torch.empty(B, H, K, V, device=v.device, dtype=torch.float32)
+    cs = (torch.empty(B, H, _slots(T), K, V, device=v.device, dtype=torch.float32) if save
+          else torch.empty(0, device=v.device, dtype=torch.float32))
+    _lib.check(_lib.load().sca2_scan_fwd(C_ref(a), _out(o.unsqueeze(3)), _ptr(S), _ptr(cs) if save else None,
+                                         _stream()), "scan_fwd")
+    return o, S, cs
 
-    @staticmethod
-    def backward(ctx, do, dS):
-        q, k, v, g, beta, lam, S0, cs = ctx.saved_tensors
-        B, T, H, K = k.shape
-        V = v.shape[-1]
-        dev = v.device
-        if do is None:
-            do = torch.zeros(B, T, H, V, device=dev, dtype=v.dtype)
-        do = do.to(v.dtype)
-        if do.stride(-1) != 1:
-            do = do.contiguous()
-        do5 = do.unsqueeze(3)
-        dS = None if dS is None else dS.float().contiguous()
-        a = _key_args(q, k, v, g, beta, lam, S0, ctx.scale, ctx.vtb)
-        z = lambda *s: torch.zeros(*s, device=dev, dtype=torch.float32)
-        dk, dq = z(B, T, H, K), z(B, T, H, K)
-        dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
-        dbeta = z(B, T, H) if beta is not None else None
-        dg = z(B, T, H) if g is not None else None
-        dlam = z(H, K) if lam is not None else None
-        dS0 = torch.empty(B, H, K, V, device=dev, dtype=torch.float32)
-        gr = ScanGrads()
-        gr.dphw, gr.dphq, gr.dv = _tok(dk), _tok(dq), _tok(dv)
-        gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
-        gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), None, None, _ptr(dS0)
-        lib = _lib.load()
-        _lib.check(lib.sca2_scan_bwd(C_ref(a), _out(do5), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
-                   "scan_bwd")
-        ni = ctx.needs_input_grad
-        return (dq if ni[0] else None, dk if ni[1] else None, dv if ni[2] else None,
-                dg if ni[3] else None, dbeta if ni[4] else None, dlam if ni[5] else None,
-                dS0 if (ni[6] and S0 is not None) else None, None, None)
+
+@_key_scan_fwd.register_fake
+def _(q, k, v, g, beta, lam, S0, scale, v_times_beta, save):
+    B, T, H, K = k.shape
+    V = v.shape[-1]
+    return (v.new_empty(B, T, H, V), v.new_empty(B, H, K, V, dtype=torch.float32),
+            v.new_empty((B, H, _slots(T), K, V) if save else (0,), dtype=torch.float32))
+
+
+@torch.library.custom_op("sca2b200::key_scan_bwd", mutates_args=())
+def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional[torch.Tensor],
+                  beta: Optional[torch.Tensor], lam: Optional[torch.Tensor], S0: Optional[torch.Tensor], scale: float,
+                  v_times_beta: bool, cs: torch.Tensor, do: torch.Tensor, dS: Optional[torch.Tensor]
+                  ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                             torch.Tensor]:
+    """sca2_scan_bwd, key flavour: gradients of (q, k, v, g, beta, lam, S0)."""
+    dt = v.dtype
+    q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
+    g, beta = _f32(g), _f32(beta)
+    lam = None if lam is None else lam.float().contiguous()
+    S0 = None if S0 is None else S0.float().contiguous()
+    B, T, H, K = k.shape
+    V = v.shape[-1]
+    dev = v.device
+    do = do.to(dt)
+    if do.stride(-1) != 1:
+        do = do.contiguous()
+    do5 = do.unsqueeze(3)
+    dS = None if dS is None else dS.float().contiguous()
+    a = _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta)
+    z = lambda *sh: torch.zeros(*sh, device=dev, dtype=torch.float32)
+    E = lambda: torch.empty(0, device=dev, dtype=torch.float32)
+    dk, dq = z(B, T, H, K), z(B, T, H, K)
+    dv = torch.empty(B, T, H, V, device=dev, dtype=dt)
+    dbeta = z(B, T, H) if beta is not None else None
+    dg = z(B, T, H) if g is not None else None
+    dlam = z(H, K) if lam is not None else None
+    dS0 = torch.empty(B, H, K, V, device=dev, dtype=torch.float32)
+    gr = ScanGrads()
+    gr.dphw, gr.dphq, gr.dv = _tok(dk), _tok(dq), _tok(dv)
+    gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
+    gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), None, None, _ptr(dS0)
+    _lib.check(_lib.load().sca2_scan_bwd(C_ref(a), _out(do5), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
+               "scan_bwd")
+    return (dq, dk, dv, E() if dg is None else dg, E() if dbeta is None else dbeta, E() if dlam is None else dlam,
+            dS0 if S0 is not None else E())
+
+
+@_key_scan_bwd.register_fake
+def _(q, k, v, g, beta, lam, S0, scale, v_times_beta, cs, do, dS):
+    B, T, H, K = k.shape
+    V = v.shape[-1]
+    f = lambda *sh: v.new_empty(*sh, dtype=torch.float32)
+    return (f(B, T, H, K), f(B, T, H, K), v.new_empty(B, T, H, V), f(B, T, H) if g is not None else f(0),
+            f(B, T, H) if beta is not None else f(0), f(H, K) if lam is not None else f(0),
+            f(B, H, K, V) if S0 is not None else f(0))
+
+
+def _key_setup(ctx, inputs, output):
+    q, k, v, g, beta, lam, S0, scale, vtb, save = inputs
+    ctx.save_for_backward(q, k, v, g, beta, lam, S0, output[2])
+    ctx.scale, ctx.vtb = scale, vtb
+
+
+def _key_backward(ctx, do, dS, dcs):
+    q, k, v, g, beta, lam, S0, cs = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*k.shape[:3], v.shape[-1], device=v.device, dtype=v.dtype)
+    grads = torch.ops.sca2b200.key_scan_bwd(q, k, v, g, beta, lam, S0, ctx.scale, ctx.vtb, cs, do, dS)
+    ni = ctx.needs_input_grad
+    ins = (q, k, v, g, beta, lam, S0)
+    return tuple(gd if (ni[j] and ins[j] is not None) else None for j, gd in enumerate(grads)) + (None, None, None)
+
+
+_key_scan_fwd.register_autograd(_key_backward, setup_context=_key_setup)
 
 
 def key_scan(q, k, v, g=None, beta=None, scale=None, S0=None, lam=None, v_times_beta=True):
@@ -276,7 +369,10 @@ def key_scan(q, k, v, g=None, beta=None, scale=None, S0=None, lam=None, v_times_
         raise _lib.Sca2Error("v_times_beta needs beta")
     K = k.shape[-1]
     scale = K ** -0.5 if scale is None else float(scale)
-    return _KeyScan.apply(q, k, v, g, beta, lam, S0, scale, v_times_beta)
+    _need_cuda(q, k, v, g, beta, lam, S0)
+    save = _wants_grad(q, k, v, g, beta, lam, S0)
+    o, S, _ = torch.ops.sca2b200.key_scan_fwd(q, k, v, g, beta, lam, S0, scale, bool(v_times_beta), save)
+    return o, S
 
 
 def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size: int = 64, scale=None,
@@ -292,6 +388,58 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size: int = 64, scale=None,
 # ======================================================================================
 #  decode step
 # ======================================================================================
+def _phase_step_args(phw, phq, v, beta, g, lam, wr, wi):
+    B, H, Mh = phw.shape
+    a = ScanArgs()
+    a.flavor = _lib.FLAVOR_PHASE
+    a.B, a.T, a.H, a.K, a.V = B, 1, H, 2 * Mh, v.shape[-1]
+    a.io_dtype = _DT[v.dtype]
+    a.q_scale = 1.0
+    a.phw, a.phq, a.v = _tok(phw, True), _tok(phq, True), _tok(v, True)
+    a.beta, a.g = _tok(beta, True), _tok(g, True)
+    a.lam, a.wr, a.wi, a.S0 = _ptr(lam), _ptr(wr), _ptr(wi), None
+    return a
+
+
+def _phase_step_run(phw, phq, v, beta, g, lam, wr, wi, S, S_out):
+    B, H, Mh = phw.shape
+    V = v.shape[-1]
+    phw, phq, v = _inner(phw.float()), _inner(phq.float()), _inner(v)
+    beta, g = _f32(beta), _f32(g)
+    lam = None if lam is None else lam.float().contiguous()
+    wr, wi = wr.float().contiguous(), wi.float().contiguous()
+    a = _phase_step_args(phw, phq, v, beta, g, lam, wr, wi)
+    o = torch.empty(B, H, 2, V, device=v.device, dtype=v.dtype)
+    _lib.check(_lib.load().sca2_scan_step(C_ref(a), S.data_ptr(), S_out.data_ptr(), _out(o.unsqueeze(1)),
+                                          _stream()), "scan_step")
+    return o
+
+
+@torch.library.custom_op("sca2b200::phase_step", mutates_args=("S_out",))
+def _phase_step_out(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
+                    g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
+                    S: torch.Tensor, S_out: torch.Tensor) -> torch.Tensor:
+    """sca2_scan_step, phase flavour: reads S, writes the new state into S_out, returns o."""
+    return _phase_step_run(phw, phq, v, beta, g, lam, wr, wi, S, S_out)
+
+
+@torch.library.custom_op("sca2b200::phase_step_", mutates_args=("S",))
+def _phase_step_inplace(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
+                        g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
+                        S: torch.Tensor) -> torch.Tensor:
+    """sca2_scan_step with the state updated in place."""
+    return _phase_step_run(phw, phq, v, beta, g, lam, wr, wi, S, S)
+
+
+def _phase_step_fake(phw, phq, v, beta, g, lam, wr, wi, S, S_out=None):
+    B, H, Mh = phw.shape
+    return v.new_empty(B, H, 2, v.shape[-1])
+
+
+_phase_step_out.register_fake(_phase_step_fake)
+_phase_step_inplace.register_fake(_phase_step_fake)
+
+
 def phase_step(phw, phq, v, beta, g, lam, wr, wi, S, S_out=None):
     """One token for every (b, h): phw, phq (B,H,Mh) fp32, v (B,H,V), beta/g (B,H) or None,
     lam/wr/wi (H,Mh), S (B,H,2Mh,V) fp32.  Returns o (B,H,2,V) in v's dtype and the new
@@ -299,25 +447,58 @@ def phase_step(phw, phq, v, beta, g, lam, wr, wi, S, S_out=None):
     _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S)
     B, H, Mh = phw.shape
     V = v.shape[-1]
-    phw, phq, v = _inner(phw.float()), _inner(phq.float()), _inner(v)
-    beta, g = _f32(beta), _f32(g)
     if S.dtype != torch.float32 or not S.is_contiguous() or tuple(S.shape) != (B, H, 2 * Mh, V):
         raise _lib.Sca2Error("state must be a contiguous fp32 (B,H,2Mh,V) tensor")
-    a = ScanArgs()
-    a.flavor = _lib.FLAVOR_PHASE
-    a.B, a.T, a.H, a.K, a.V = B, 1, H, 2 * Mh, V
-    a.io_dtype = _DT[v.dtype]
-    a.q_scale = 1.0
-    a.phw, a.phq, a.v = _tok(phw, True), _tok(phq, True), _tok(v, True)
-    a.beta, a.g = _tok(beta, True), _tok(g, True)
-    lam = None if lam is None else lam.float().contiguous()
-    wr, wi = wr.float().contiguous(), wi.float().contiguous()
-    a.lam, a.wr, a.wi, a.S0 = _ptr(lam), _ptr(wr), _ptr(wi), None
-    o = torch.empty(B, 1, H, 2, V, device=v.device, dtype=v.dtype)
+    if S_out is S:
+        return torch.ops.sca2b200.phase_step_(phw, phq, v, beta, g, lam, wr, wi, S), S
     S_out = torch.empty_like(S) if S_out is None else S_out
-    _lib.check(_lib.load().sca2_scan_step(C_ref(a), S.data_ptr(), S_out.data_ptr(), _out(o), _stream()),
-               "scan_step")
-    return o[:, 0], S_out
+    return torch.ops.sca2b200.phase_step(phw, phq, v, beta, g, lam, wr, wi, S, S_out), S_out
+
+
+def _key_step_run(q, k, v, g, beta, S, S_out, scale, v_times_beta):
+    B, H, K = k.shape
+    V = v.shape[-1]
+    dt = v.dtype
+    q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
+    g, beta = _f32(g), _f32(beta)
+    a = ScanArgs()
+    a.flavor = _lib.FLAVOR_KEY
+    a.B, a.T, a.H, a.K, a.V = B, 1, H, K, V
+    a.io_dtype = _DT[dt]
+    a.v_times_beta = 1 if v_times_beta else 0
+    a.q_scale = float(scale)
+    a.phw, a.phq, a.v = _tok(k, True), _tok(q, True), _tok(v, True)
+    a.beta, a.g = _tok(beta, True), _tok(g, True)
+    a.lam = a.wr = a.wi = a.S0 = None
+    o = torch.empty(B, H, V, device=v.device, dtype=dt)
+    _lib.check(_lib.load().sca2_scan_step(C_ref(a), S.data_ptr(), S_out.data_ptr(), _out(o[:, None, :, None]),
+                                          _stream()), "scan_step")
+    return o
+
+
+@torch.library.custom_op("sca2b200::key_step", mutates_args=("S_out",))
+def _key_step_out(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional[torch.Tensor],
+                  beta: Optional[torch.Tensor], S: torch.Tensor, S_out: torch.Tensor, scale: float,
+                  v_times_beta: bool) -> torch.Tensor:
+    """sca2_scan_step, key flavour: reads S, writes the new state into S_out, returns o."""
+    return _key_step_run(q, k, v, g, beta, S, S_out, scale, v_times_beta)
+
+
+@torch.library.custom_op("sca2b200::key_step_", mutates_args=("S",))
+def _key_step_inplace(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional[torch.Tensor],
+                      beta: Optional[torch.Tensor], S: torch.Tensor, scale: float, v_times_beta: bool) -> torch.Tensor:
+    """sca2_scan_step, key flavour, state updated in place."""
+    return _key_step_run(q, k, v, g, beta, S, S, scale, v_times_beta)
+
+
+@_key_step_out.register_fake
+def _(q, k, v, g, beta, S, S_out, scale, v_times_beta):
+    return v.new_empty(*k.shape[:2], v.shape[-1])
+
+
+@_key_step_inplace.register_fake
+def _(q, k, v, g, beta, S, scale, v_times_beta):
+    return v.new_empty(*k.shape[:2], v.shape[-1])
 
 
 def key_step(q, k, v, g, beta, S, scale=None, S_out=None, v_times_beta=True):
@@ -326,25 +507,13 @@ def key_step(q, k, v, g, beta, S, scale=None, S_out=None, v_times_beta=True):
     _need_cuda(q, k, v, g, beta, S)
     B, H, K = k.shape
     V = v.shape[-1]
-    dt = v.dtype
-    q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
-    g, beta = _f32(g), _f32(beta)
     if S.dtype != torch.float32 or not S.is_contiguous() or tuple(S.shape) != (B, H, K, V):
         raise _lib.Sca2Error("state must be a contiguous fp32 (B,H,K,V) tensor")
-    a = ScanArgs()
-    a.flavor = _lib.FLAVOR_KEY
-    a.B, a.T, a.H, a.K, a.V = B, 1, H, K, V
-    a.io_dtype = _DT[dt]
-    a.v_times_beta = 1 if v_times_beta else 0
-    a.q_scale = K ** -0.5 if scale is None else float(scale)
-    a.phw, a.phq, a.v = _tok(k, True), _tok(q, True), _tok(v, True)
-    a.beta, a.g = _tok(beta, True), _tok(g, True)
-    a.lam = a.wr = a.wi = a.S0 = None
-    o = torch.empty(B, 1, H, 1, V, device=v.device, dtype=dt)
+    scale = K ** -0.5 if scale is None else float(scale)
+    if S_out is S:
+        return torch.ops.sca2b200.key_step_(q, k, v, g, beta, S, scale, bool(v_times_beta)), S
     S_out = torch.empty_like(S) if S_out is None else S_out
-    _lib.check(_lib.load().sca2_scan_step(C_ref(a), S.data_ptr(), S_out.data_ptr(), _out(o), _stream()),
-               "scan_step")
-    return o[:, 0, :, 0], S_out
+    return torch.ops.sca2b200.key_step(q, k, v, g, beta, S, S_out, scale, bool(v_times_beta)), S_out
 
 
 # ======================================================================================
@@ -367,50 +536,91 @@ def _dscan_work(lib, B, T, M, G, V, device, blocks):
     return torch.empty((n + 3) // 4, device=device, dtype=torch.float32) if n > 0 else None
 
 
-class _DScan(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep, blocks):
-        B, T, M, G = a_re.shape
-        V = v.shape[-1]
-        S0 = (S0_re, S0_im) if S0_re is not None else None
-        a = _dscan_args(a_re, a_im, v, c_re, c_im, S0, sep)
-        ab = torch.empty(B, T, 2, V, device=v.device, dtype=torch.float32)
-        S_re = torch.empty(B, M, V, device=v.device, dtype=torch.float32)
-        S_im = torch.empty_like(S_re)
-        lib = _lib.load()
-        need = any(ctx.needs_input_grad)
-        ck = torch.empty(B, lib.sca2_dscan_num_ckpt(T), 2, M, V, device=v.device) if need else None
-        wk = _dscan_work(lib, B, T, M, G, V, v.device, blocks)
-        _lib.check(lib.sca2_dscan_fwd(C_ref(a), ab.data_ptr(), S_re.data_ptr(), S_im.data_ptr(), _ptr(ck),
-                                      _ptr(wk), _stream()), "dscan_fwd")
-        if need:
-            ctx.save_for_backward(a_re, a_im, v, c_re, c_im, S0_re, S0_im, ck)
-            ctx.sep, ctx.blocks = sep, blocks
-        return ab, S_re, S_im
+@torch.library.custom_op("sca2b200::dscan_fwd", mutates_args=())
+def _dscan_fwd(a_re: torch.Tensor, a_im: torch.Tensor, v: torch.Tensor, c_re: torch.Tensor, c_im: torch.Tensor,
+               S0_re: Optional[torch.Tensor], S0_im: Optional[torch.Tensor], sep: bool, blocks: bool, save: bool
+               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_dscan_fwd: ab (B,T,2,V), S_re, S_im (B,M,V), checkpoints (or empty)."""
+    B, T, M, G = a_re.shape
+    V = v.shape[-1]
+    S0 = (S0_re, S0_im) if S0_re is not None else None
+    a = _dscan_args(a_re, a_im, v, c_re, c_im, S0, sep)
+    ab = torch.empty(B, T, 2, V, device=v.device, dtype=torch.float32)
+    S_re = torch.empty(B, M, V, device=v.device, dtype=torch.float32)
+    S_im = torch.empty_like(S_re)
+    lib = _lib.load()
+    ck = (torch.empty(B, lib.sca2_dscan_num_ckpt(T), 2, M, V, device=v.device) if save
+          else torch.empty(0, device=v.device))
+    wk = _dscan_work(lib, B, T, M, G, V, v.device, blocks)
+    _lib.check(lib.sca2_dscan_fwd(C_ref(a), ab.data_ptr(), S_re.data_ptr(), S_im.data_ptr(),
+                                  ck.data_ptr() if save else None, _ptr(wk), _stream()), "dscan_fwd")
+    return ab, S_re, S_im, ck
 
-    @staticmethod
-    def backward(ctx, dab, dS_re, dS_im):
-        a_re, a_im, v, c_re, c_im, S0_re, S0_im, ck = ctx.saved_tensors
-        S0 = (S0_re, S0_im) if S0_re is not None else None
-        a = _dscan_args(a_re, a_im, v, c_re, c_im, S0, ctx.sep)
-        da_re, da_im = torch.zeros_like(a_re), torch.zeros_like(a_im)
-        dv = torch.empty_like(v)
-        dc_re = torch.zeros_like(c_re) if ctx.sep else torch.empty_like(c_re)
-        dc_im = torch.zeros_like(c_im) if ctx.sep else torch.empty_like(c_im)
-        dS0_re = torch.empty_like(S0_re) if S0 is not None else None
-        dS0_im = torch.empty_like(S0_im) if S0 is not None else None
-        g = _lib.DScanGrads()
-        g.da_re, g.da_im, g.dv, g.dc_re, g.dc_im = (x.data_ptr() for x in (da_re, da_im, dv, dc_re, dc_im))
-        g.dS0_re, g.dS0_im = _ptr(dS0_re), _ptr(dS0_im)
-        dab = dab.contiguous() if dab is not None else torch.zeros(*a_re.shape[:2], 2, v.shape[-1], device=v.device)
-        dS_re = dS_re.contiguous() if dS_re is not None else None
-        dS_im = dS_im.contiguous() if dS_im is not None else None
-        lib = _lib.load()
-        B, T, M, G = a_re.shape
-        wk = _dscan_work(lib, B, T, M, G, v.shape[-1], v.device, ctx.blocks)
-        _lib.check(lib.sca2_dscan_bwd(C_ref(a), dab.data_ptr(), _ptr(dS_re), _ptr(dS_im), ck.data_ptr(),
-                                      C_ref(g), _ptr(wk), _stream()), "dscan_bwd")
-        return da_re, da_im, dv, dc_re, dc_im, dS0_re, dS0_im, None, None
+
+@_dscan_fwd.register_fake
+def _(a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep, blocks, save):
+    B, T, M, G = a_re.shape
+    V = v.shape[-1]
+    f = lambda *sh: v.new_empty(*sh, dtype=torch.float32)
+    return f(B, T, 2, V), f(B, M, V), f(B, M, V), (f(B, (T + 15) // 16, 2, M, V) if save else f(0))
+
+
+@torch.library.custom_op("sca2b200::dscan_bwd", mutates_args=())
+def _dscan_bwd(a_re: torch.Tensor, a_im: torch.Tensor, v: torch.Tensor, c_re: torch.Tensor, c_im: torch.Tensor,
+               S0_re: Optional[torch.Tensor], S0_im: Optional[torch.Tensor], sep: bool, blocks: bool,
+               ck: torch.Tensor, dab: torch.Tensor, dS_re: Optional[torch.Tensor], dS_im: Optional[torch.Tensor]
+               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                          torch.Tensor]:
+    """sca2_dscan_bwd: gradients of (a_re, a_im, v, c_re, c_im, S0_re, S0_im)."""
+    S0 = (S0_re, S0_im) if S0_re is not None else None
+    a = _dscan_args(a_re, a_im, v, c_re, c_im, S0, sep)
+    da_re, da_im = torch.zeros_like(a_re), torch.zeros_like(a_im)
+    dv = torch.empty_like(v)
+    dc_re = torch.zeros_like(c_re) if sep else torch.empty_like(c_re)
+    dc_im = torch.zeros_like(c_im) if sep else torch.empty_like(c_im)
+    dS0_re = torch.empty_like(S0_re) if S0 is not None else None
+    dS0_im = torch.empty_like(S0_im) if S0 is not None else None
+    g = _lib.DScanGrads()
+    g.da_re, g.da_im, g.dv, g.dc_re, g.dc_im = (x.data_ptr() for x in (da_re, da_im, dv, dc_re, dc_im))
+    g.dS0_re, g.dS0_im = _ptr(dS0_re), _ptr(dS0_im)
+    dab = dab.contiguous()
+    dS_re = dS_re.contiguous() if dS_re is not None else None
+    dS_im = dS_im.contiguous() if dS_im is not None else None
+    lib = _lib.load()
+    B, T, M, G = a_re.shape
+    wk = _dscan_work(lib, B, T, M, G, v.shape[-1], v.device, blocks)
+    _lib.check(lib.sca2_dscan_bwd(C_ref(a), dab.data_ptr(), _ptr(dS_re), _ptr(dS_im), ck.data_ptr(),
+                                  C_ref(g), _ptr(wk), _stream()), "dscan_bwd")
+    E = lambda: torch.empty(0, device=v.device)
+    return (da_re, da_im, dv, dc_re, dc_im, dS0_re if dS0_re is not None else E(),
+            dS0_im if dS0_im is not None else E())
+
+
+@_dscan_bwd.register_fake
+def _(a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep, blocks, ck, dab, dS_re, dS_im):
+    e = lambda t: torch.empty_like(t) if t is not None else v.new_empty(0)
+    return (torch.empty_like(a_re), torch.empty_like(a_im), torch.empty_like(v), torch.empty_like(c_re),
+            torch.empty_like(c_im), e(S0_re), e(S0_im))
+
+
+def _dscan_setup(ctx, inputs, output):
+    a_re, a_im, v, c_re, c_im, S0_re, S0_im, sep, blocks, save = inputs
+    ctx.save_for_backward(a_re, a_im, v, c_re, c_im, S0_re, S0_im, output[3])
+    ctx.sep, ctx.blocks = sep, blocks
+
+
+def _dscan_backward(ctx, dab, dS_re, dS_im, dck):
+    a_re, a_im, v, c_re, c_im, S0_re, S0_im, ck = ctx.saved_tensors
+    if dab is None:
+        dab = torch.zeros(*a_re.shape[:2], 2, v.shape[-1], device=v.device)
+    g = torch.ops.sca2b200.dscan_bwd(a_re, a_im, v, c_re, c_im, S0_re, S0_im, ctx.sep, ctx.blocks, ck, dab,
+                                     dS_re, dS_im)
+    ni = ctx.needs_input_grad
+    ins = (a_re, a_im, v, c_re, c_im, S0_re, S0_im)
+    return tuple(x if (ni[j] and ins[j] is not None) else None for j, x in enumerate(g)) + (None, None, None)
+
+
+_dscan_fwd.register_autograd(_dscan_backward, setup_context=_dscan_setup)
 
 
 def dscan(a_re, a_im, v, c_re, c_im, S0: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, sep: bool = False,
@@ -424,7 +634,9 @@ def dscan(a_re, a_im, v, c_re, c_im, S0: Optional[Tuple[torch.Tensor, torch.Tens
     f = lambda x: x.to(torch.float32).contiguous()
     a_re, a_im, v, c_re, c_im = f(a_re), f(a_im), f(v), f(c_re), f(c_im)
     S0_re, S0_im = (f(S0[0]), f(S0[1])) if S0 is not None else (None, None)
-    ab, S_re, S_im = _DScan.apply(a_re, a_im, v, c_re, c_im, S0_re, S0_im, bool(sep), bool(blocks))
+    save = _wants_grad(a_re, a_im, v, c_re, c_im, S0_re, S0_im)
+    ab, S_re, S_im, _ = torch.ops.sca2b200.dscan_fwd(a_re, a_im, v, c_re, c_im, S0_re, S0_im, bool(sep),
+                                                      bool(blocks), save)
     return ab, (S_re, S_im)
 
 
@@ -442,46 +654,89 @@ def _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos):
     return a
 
 
-class _ShortRead(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos):
-        B, T, L = kh.shape
-        dv = v.shape[-1]
-        n = L - 1
-        a = _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
-        o = torch.empty(B, T, 2 * dv, device=v.device, dtype=torch.float32)
-        c1 = torch.empty(B, n, L, device=v.device, dtype=torch.float32)
-        s1, e1 = torch.empty_like(c1), torch.empty(B, n, dv, device=v.device, dtype=torch.float32)
-        _lib.check(_lib.load().sca2_short_fwd(C_ref(a), o.data_ptr() if T else None, c1.data_ptr(), s1.data_ptr(),
-                                              e1.data_ptr(), _stream()), "short_fwd")
-        ctx.save_for_backward(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
-        return o, c1, s1, e1
+@torch.library.custom_op("sca2b200::short_fwd", mutates_args=())
+def _short_fwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, theta: torch.Tensor, omega: torch.Tensor,
+               wr: torch.Tensor, wi: torch.Tensor, c0: Optional[torch.Tensor], s0: Optional[torch.Tensor],
+               e0: Optional[torch.Tensor], pos: Optional[torch.Tensor]
+               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_short_fwd: o (B,T,2dv) and the new ring buffer (c, s, e)."""
+    B, T, L = kh.shape
+    dv = v.shape[-1]
+    n = L - 1
+    a = _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+    o = torch.empty(B, T, 2 * dv, device=v.device, dtype=torch.float32)
+    c1 = torch.empty(B, n, L, device=v.device, dtype=torch.float32)
+    s1, e1 = torch.empty_like(c1), torch.empty(B, n, dv, device=v.device, dtype=torch.float32)
+    _lib.check(_lib.load().sca2_short_fwd(C_ref(a), o.data_ptr() if T else None, _ptr(c1) if n else None,
+                                          _ptr(s1) if n else None, _ptr(e1) if n else None, _stream()), "short_fwd")
+    return o, c1, s1, e1
 
-    @staticmethod
-    def backward(ctx, dO, dc1, ds1, de1):
-        kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos = ctx.saved_tensors
-        B, T, L = kh.shape
-        dv = v.shape[-1]
-        a = _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
-        lib = _lib.load()
-        g = _lib.ShortGrads()
-        dkh, dkz, dvv = torch.empty_like(kh), torch.empty_like(kz), torch.empty_like(v)
-        dth, dwr, dwi = torch.empty_like(theta), torch.empty_like(wr), torch.empty_like(wi)
-        dc0 = torch.empty_like(c0) if c0 is not None else None
-        ds0 = torch.empty_like(s0) if s0 is not None else None
-        de0 = torch.empty_like(e0) if e0 is not None else None
-        g.dkh, g.dkz, g.dv = dkh.data_ptr(), dkz.data_ptr(), dvv.data_ptr()
-        g.dtheta, g.dwr, g.dwi = dth.data_ptr(), dwr.data_ptr(), dwi.data_ptr()
-        g.dc0, g.ds0, g.de0 = _ptr(dc0), _ptr(ds0), _ptr(de0)
-        if dO is None:
-            dO = torch.zeros(B, T, 2 * dv, device=v.device)
-        c = lambda x: x.contiguous() if x is not None else None
-        dO, dc1, ds1, de1 = c(dO), c(dc1), c(ds1), c(de1)
-        nw = lib.sca2_short_work_bytes(B, T, L, dv)
-        wk = torch.empty((nw + 3) // 4, device=v.device, dtype=torch.float32) if nw > 0 else None
-        _lib.check(lib.sca2_short_bwd(C_ref(a), dO.data_ptr(), _ptr(dc1), _ptr(ds1), _ptr(de1), C_ref(g), _ptr(wk),
-                                      _stream()), "short_bwd")
-        return dkh, dkz, dvv, dth, None, dwr, dwi, dc0, ds0, de0, None
+
+@_short_fwd.register_fake
+def _(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos):
+    B, T, L = kh.shape
+    dv = v.shape[-1]
+    f = lambda *sh: v.new_empty(*sh, dtype=torch.float32)
+    return f(B, T, 2 * dv), f(B, L - 1, L), f(B, L - 1, L), f(B, L - 1, dv)
+
+
+@torch.library.custom_op("sca2b200::short_bwd", mutates_args=())
+def _short_bwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, theta: torch.Tensor, omega: torch.Tensor,
+               wr: torch.Tensor, wi: torch.Tensor, c0: Optional[torch.Tensor], s0: Optional[torch.Tensor],
+               e0: Optional[torch.Tensor], pos: Optional[torch.Tensor], dO: torch.Tensor,
+               dc1: Optional[torch.Tensor], ds1: Optional[torch.Tensor], de1: Optional[torch.Tensor]
+               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                          torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_short_bwd: gradients of (kh, kz, v, theta, wr, wi, c0, s0, e0)."""
+    B, T, L = kh.shape
+    dv = v.shape[-1]
+    a = _short_args(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+    lib = _lib.load()
+    g = _lib.ShortGrads()
+    dkh, dkz, dvv = torch.empty_like(kh), torch.empty_like(kz), torch.empty_like(v)
+    dth, dwr, dwi = torch.empty_like(theta), torch.empty_like(wr), torch.empty_like(wi)
+    E = lambda: torch.empty(0, device=v.device)
+    dc0 = torch.empty_like(c0) if c0 is not None else E()
+    ds0 = torch.empty_like(s0) if s0 is not None else E()
+    de0 = torch.empty_like(e0) if e0 is not None else E()
+    g.dkh, g.dkz, g.dv = dkh.data_ptr(), dkz.data_ptr(), dvv.data_ptr()
+    g.dtheta, g.dwr, g.dwi = dth.data_ptr(), dwr.data_ptr(), dwi.data_ptr()
+    g.dc0 = dc0.data_ptr() if c0 is not None and dc0.numel() else None
+    g.ds0 = ds0.data_ptr() if s0 is not None and ds0.numel() else None
+    g.de0 = de0.data_ptr() if e0 is not None and de0.numel() else None
+    c = lambda x: x.contiguous() if x is not None and x.numel() else None
+    dO, dc1, ds1, de1 = dO.contiguous(), c(dc1), c(ds1), c(de1)
+    nw = lib.sca2_short_work_bytes(B, T, L, dv)
+    wk = torch.empty((nw + 3) // 4, device=v.device, dtype=torch.float32) if nw > 0 else None
+    _lib.check(lib.sca2_short_bwd(C_ref(a), dO.data_ptr() if T else None, _ptr(dc1), _ptr(ds1), _ptr(de1),
+                                  C_ref(g), _ptr(wk), _stream()), "short_bwd")
+    return dkh, dkz, dvv, dth, dwr, dwi, dc0, ds0, de0
+
+
+@_short_bwd.register_fake
+def _(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos, dO, dc1, ds1, de1):
+    e = lambda t: torch.empty_like(t) if t is not None else v.new_empty(0)
+    return (torch.empty_like(kh), torch.empty_like(kz), torch.empty_like(v), torch.empty_like(theta),
+            torch.empty_like(wr), torch.empty_like(wi), e(c0), e(s0), e(e0))
+
+
+def _short_setup(ctx, inputs, output):
+    ctx.save_for_backward(*inputs)
+
+
+def _short_backward(ctx, dO, dc1, ds1, de1):
+    kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos = ctx.saved_tensors
+    if dO is None:
+        dO = torch.zeros(*kh.shape[:2], 2 * v.shape[-1], device=v.device)
+    g = torch.ops.sca2b200.short_bwd(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos, dO, dc1, ds1, de1)
+    dkh, dkz, dvv, dth, dwr, dwi, dc0, ds0, de0 = g
+    ni = ctx.needs_input_grad
+    out = [dkh, dkz, dvv, dth, None, dwr, dwi, dc0 if c0 is not None else None, ds0 if s0 is not None else None,
+           de0 if e0 is not None else None, None]
+    return tuple(x if ni[j] else None for j, x in enumerate(out))
+
+
+_short_fwd.register_autograd(_short_backward, setup_context=_short_setup)
 
 
 def short_read(kh, kz, v, theta, omega, wr, wi, state=None, pos=None):
@@ -496,43 +751,63 @@ def short_read(kh, kz, v, theta, omega, wr, wi, state=None, pos=None):
     c0, s0, e0 = (f(x) for x in state) if state is not None else (None, None, None)
     if pos is not None:
         pos = pos.to(device=v.device, dtype=torch.int64).reshape(())
-    o, c1, s1, e1 = _ShortRead.apply(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
+    o, c1, s1, e1 = torch.ops.sca2b200.short_fwd(kh, kz, v, theta, omega, wr, wi, c0, s0, e0, pos)
     return o, (c1, s1, e1)
 
 
 # ======================================================================================
 #  RMS read-out
 # ======================================================================================
-class _Rms(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, eps):
-        _need_cuda(x)
-        if x.dtype not in _DT:
-            x = x.float()
-        x = x.contiguous()
-        D = x.shape[-1]
-        N = x.numel() // D
-        u = torch.empty_like(x)
-        _lib.check(_lib.load().sca2_rms_fwd(x.data_ptr(), u.data_ptr(), N, D, float(eps), _DT[x.dtype],
-                                            _stream()), "rms_fwd")
-        ctx.save_for_backward(x)
-        ctx.eps = eps
-        return u
+@torch.library.custom_op("sca2b200::rms_fwd", mutates_args=())
+def _rms_fwd(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """sca2_rms_fwd on a contiguous fp32 / bf16 tensor, rows over the last dimension."""
+    D = x.shape[-1]
+    u = torch.empty_like(x)
+    _lib.check(_lib.load().sca2_rms_fwd(x.data_ptr(), u.data_ptr(), x.numel() // D, D, float(eps), _DT[x.dtype],
+                                        _stream()), "rms_fwd")
+    return u
 
-    @staticmethod
-    def backward(ctx, du):
-        (x,) = ctx.saved_tensors
-        du = du.to(x.dtype).contiguous()
-        D = x.shape[-1]
-        dx = torch.empty_like(x)
-        _lib.check(_lib.load().sca2_rms_bwd(x.data_ptr(), du.data_ptr(), dx.data_ptr(), x.numel() // D, D,
-                                            float(ctx.eps), _DT[x.dtype], _stream()), "rms_bwd")
-        return dx, None
+
+@_rms_fwd.register_fake
+def _(x, eps):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("sca2b200::rms_bwd", mutates_args=())
+def _rms_bwd(x: torch.Tensor, du: torch.Tensor, eps: float) -> torch.Tensor:
+    """sca2_rms_bwd: dx from x and du (same shape and dtype)."""
+    D = x.shape[-1]
+    du = du.to(x.dtype).contiguous()
+    dx = torch.empty_like(x)
+    _lib.check(_lib.load().sca2_rms_bwd(x.data_ptr(), du.data_ptr(), dx.data_ptr(), x.numel() // D, D, float(eps),
+                                        _DT[x.dtype], _stream()), "rms_bwd")
+    return dx
+
+
+@_rms_bwd.register_fake
+def _(x, du, eps):
+    return torch.empty_like(x)
+
+
+def _rms_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[0])
+    ctx.eps = inputs[1]
+
+
+def _rms_backward(ctx, du):
+    (x,) = ctx.saved_tensors
+    return torch.ops.sca2b200.rms_bwd(x, du, ctx.eps), None
+
+
+_rms_fwd.register_autograd(_rms_backward, setup_context=_rms_setup)
 
 
 def rms(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """u = x * rsqrt(mean(x^2, -1) + eps) (sca2/ref.py:29-30), on the GPU kernel."""
-    return _Rms.apply(x, eps)
+    _need_cuda(x)
+    if x.dtype not in _DT:
+        x = x.float()
+    return torch.ops.sca2b200.rms_fwd(x.contiguous(), float(eps))
 
 
 # ======================================================================================
