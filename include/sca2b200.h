@@ -159,6 +159,41 @@ SCA2_API int sca2_rms_fwd(const void* x, void* u, int64_t N, int32_t D, float ep
 SCA2_API int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D,
                  float eps, int32_t io_dtype, void* stream);
 
+/* ---- projected phases (the fused phase prologue) -------------------------------------------
+ * The phase-flavour scan with its phases formed inside the kernels from the head's
+ * projections instead of read as phi / psi tensors: a->phw and a->phq then hold K(h) and
+ * K(z) (B,T,H,Mh) in `dtype`, and
+ *     phi_t = K(h)_t theta + (pos + t) omega,    psi_t = K(z)_t theta + (pos + t) omega
+ * in fp32 (each product rounded, then the sum: the expression of LongHead._phase,
+ * lapa/layer.py:221-223, and CHeadGated._phases, sca2/arch_gatedc.py:91-95).  Covers the
+ * tensor-core path (bf16 values, K = 2 Mh = 64; sca2_scan_proj_supported says whether a call
+ * is covered); the projections' rows must be 16-byte aligned. */
+typedef struct sca2_phase_proj {
+  int32_t dtype;        /* of K(h), K(z) and their gradients: SCA2_F32 or SCA2_BF16 */
+  const float* theta;   /* (H, Mh) */
+  const float* omega;   /* (H, Mh) */
+  const float* pos;     /* device fp32 scalar: position of token 0 (the state's "pos"), or NULL = 0 */
+} sca2_phase_proj;
+
+/* 1 if sca2_scan_fwd_proj (training != 0: with chunk states, and sca2_scan_bwd_proj) covers
+ * these arguments, else 0. */
+SCA2_API int sca2_scan_proj_supported(const sca2_scan_args* a, const sca2_phase_proj* pp,
+                   int32_t training);
+
+/* Forward with projected phases; otherwise as sca2_scan_fwd. */
+SCA2_API int sca2_scan_fwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out o,
+                   float* S_final, float* chunk_states, void* stream);
+
+/* Bytes of the workspace of sca2_scan_bwd_proj. */
+SCA2_API int64_t sca2_scan_proj_work_bytes(int32_t B, int32_t T, int32_t H, int32_t Mh);
+
+/* Backward with projected phases: as sca2_scan_bwd, except that gr->dphw / gr->dphq receive
+ * the gradients of K(h) / K(z) in pp->dtype (WRITTEN, not accumulated) and dtheta (H, Mh)
+ * the gradient of theta (written). */
+SCA2_API int sca2_scan_bwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out dO,
+                   const float* dS_final, const float* chunk_states, const sca2_scan_grads* gr,
+                   float* dtheta, void* work, void* stream);
+
 /* ---- D-head diagonal scan ---------------------------------------------------------------
  * Complex diagonal recurrence of the SCA2 D head and its read contracted over M rows:
  *   s_t[m,j] = a_t[m,g(j)] s_{t-1}[m,j] + v_t[j]      g(j) = j / (V/G)

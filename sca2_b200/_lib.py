@@ -53,6 +53,10 @@ class DScanArgs(C.Structure):
     ]
 
 
+class PhaseProj(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("theta", C.c_void_p), ("omega", C.c_void_p), ("pos", C.c_void_p)]
+
+
 class ShortArgs(C.Structure):
     _fields_ = [
         ("B", C.c_int32), ("T", C.c_int32), ("L", C.c_int32), ("dv", C.c_int32),
@@ -94,6 +98,12 @@ SIGNATURES = [
                                  C.c_void_p, C.c_void_p]),
     ("sca2_dscan_bwd", C.c_int, [C.POINTER(DScanArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                  C.POINTER(DScanGrads), C.c_void_p, C.c_void_p]),
+    ("sca2_scan_proj_supported", C.c_int, [C.POINTER(ScanArgs), C.POINTER(PhaseProj), C.c_int32]),
+    ("sca2_scan_fwd_proj", C.c_int, [C.POINTER(ScanArgs), C.POINTER(PhaseProj), Out, C.c_void_p, C.c_void_p,
+                                     C.c_void_p]),
+    ("sca2_scan_proj_work_bytes", C.c_int64, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    ("sca2_scan_bwd_proj", C.c_int, [C.POINTER(ScanArgs), C.POINTER(PhaseProj), Out, C.c_void_p, C.c_void_p,
+                                     C.POINTER(ScanGrads), C.c_void_p, C.c_void_p, C.c_void_p]),
     ("sca2_short_fwd", C.c_int, [C.POINTER(ShortArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                  C.c_void_p]),
     ("sca2_short_work_bytes", C.c_int64, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),

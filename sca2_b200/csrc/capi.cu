@@ -27,7 +27,7 @@ cudaError_t launch_rms_bwd(const void* x, const void* du, void* dx, int64_t N, i
 // scan_tc.cu
 int tc_fwd_vb(int K, int V, int R, int max_smem);
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
-                        float* cstates, int NCS, cudaStream_t st);
+                        float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp = PhaseProj{});
 cudaError_t tc_read_faults(unsigned int* out);
 cudaError_t tc_read_faults_bwd(unsigned int* out);
 // dscan.cu
@@ -47,7 +47,12 @@ cudaError_t short_bwd(const sca2_short_args& p, const float* dO, const float* dc
 // scan_tc_bwd.cu
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
-                        const sca2_scan_grads& gr, int NCS, cudaStream_t st);
+                        const sca2_scan_grads& gr, int NCS, cudaStream_t st, const PhaseProj& pp = PhaseProj{});
+// phase_proj.cu
+size_t proj_work_floats(int B, int T, int H, int Mh);
+cudaError_t proj_bwd(int B, int T, int H, int Mh, int dtype, const float* work, const sca2_tok& kh,
+                     const sca2_tok& kz, const float* theta, const sca2_tok& dkh, const sca2_tok& dkz, float* dtheta,
+                     cudaStream_t st);
 }  // namespace sca2
 
 namespace {
@@ -190,6 +195,85 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
                       ? sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, *gr, sca2::state_slots(a->T), st)
                       : sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
+  return SCA2_OK;
+}
+
+static bool proj_rows_ok(const sca2_tok& t, int dtype) {
+  const int64_t q = dtype == SCA2_BF16 ? 8 : 4;  // elements per 16 bytes
+  return t.ptr && ((uintptr_t)t.ptr & 15u) == 0 && t.sb % q == 0 && t.st % q == 0 && t.sh % q == 0;
+}
+
+static bool proj_covered(const sca2_scan_args* a, const sca2_phase_proj* pp, bool training) {
+  if (!a || !pp || a->flavor != SCA2_FLAVOR_PHASE || a->io_dtype != SCA2_BF16 || a->K != 64) return false;
+  if (pp->dtype != SCA2_F32 && pp->dtype != SCA2_BF16) return false;
+  if (!pp->theta || !pp->omega || !proj_rows_ok(a->phw, pp->dtype) || !proj_rows_ok(a->phq, pp->dtype)) return false;
+  const int smem = max_optin_smem();
+  if (training) return sca2::tc_train_ok(*a, smem) && sca2::tc_fwd_vb(a->K, a->V, 2, smem) > 0;
+  return sca2::tc_fwd_vb(a->K, a->V, 2, smem) > 0;
+}
+
+static sca2::PhaseProj to_pp(const sca2_phase_proj* pp) {
+  return sca2::PhaseProj{1, pp->dtype, pp->theta, pp->omega, pp->pos};
+}
+
+int sca2_scan_proj_supported(const sca2_scan_args* a, const sca2_phase_proj* pp, int32_t training) {
+  return (check_scan(a, training != 0) == SCA2_OK && proj_covered(a, pp, training != 0)) ? 1 : 0;
+}
+
+int sca2_scan_fwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out o, float* S_final,
+                       float* chunk_states, void* stream) {
+  int rc = check_scan(a, false);
+  if (rc) return rc;
+  if (a->T == 0) return sca2_scan_fwd(a, o, S_final, chunk_states, stream);
+  if (!o.ptr) return fail(SCA2_ERR_ARG, "output o must be non-null");
+  if (!proj_covered(a, pp, chunk_states != nullptr))
+    return fail(SCA2_ERR_UNSUPPORTED, "projected phases need the tensor-core path (bf16 values, K = 64) and "
+                                      "16-byte aligned projection rows");
+  const int vb = sca2::tc_fwd_vb(a->K, a->V, 2, max_optin_smem());
+  cudaError_t e = sca2::tc_scan_fwd(*a, vb, o, S_final, chunk_states, sca2::state_slots(a->T),
+                                    reinterpret_cast<cudaStream_t>(stream), to_pp(pp));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd_proj");
+  return SCA2_OK;
+}
+
+int64_t sca2_scan_proj_work_bytes(int32_t B, int32_t T, int32_t H, int32_t Mh) {
+  if (B < 1 || T < 1 || H < 1 || Mh < 1) return 0;
+  return (int64_t)(sca2::proj_work_floats(B, T, H, Mh) * sizeof(float));
+}
+
+int sca2_scan_bwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out dO, const float* dS_final,
+                       const float* chunk_states, const sca2_scan_grads* gr, float* dtheta, void* work,
+                       void* stream) {
+  int rc = check_scan(a, true);
+  if (rc) return rc;
+  if (!gr || !dtheta) return fail(SCA2_ERR_ARG, "null gradient struct or dtheta");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int Mh = a->K / 2;
+  if (a->T == 0) {
+    cudaError_t e = cudaMemsetAsync(dtheta, 0, (size_t)a->H * Mh * sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd_proj(T=0)");
+    return sca2_scan_bwd(a, dO, dS_final, chunk_states, gr, stream);
+  }
+  if (!dO.ptr || !chunk_states || !work) return fail(SCA2_ERR_ARG, "dO, chunk_states and work must be non-null");
+  if (!proj_covered(a, pp, true) || !proj_rows_ok(gr->dphw, pp->dtype) || !proj_rows_ok(gr->dphq, pp->dtype))
+    return fail(SCA2_ERR_UNSUPPORTED, "projected phases need the tensor-core path (bf16 values, K = 64) and "
+                                      "16-byte aligned projection rows");
+  if (!gr->dv.ptr) return fail(SCA2_ERR_ARG, "dv must be non-null");
+  if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
+  if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
+  // d(phi), d(psi) into the zero-filled workspace, then the projections' gradients
+  float* w = static_cast<float*>(work);
+  const size_t n = (size_t)a->B * a->T * a->H * Mh;
+  cudaError_t e = cudaMemsetAsync(w, 0, 2 * n * sizeof(float), st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd_proj");
+  sca2_scan_grads g2 = *gr;
+  const int64_t sh = Mh, stt = (int64_t)a->H * Mh, sb = (int64_t)a->T * stt;
+  g2.dphw = sca2_tok{w, sb, stt, sh};
+  g2.dphq = sca2_tok{w + n, sb, stt, sh};
+  e = sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, g2, sca2::state_slots(a->T), st, to_pp(pp));
+  if (e == cudaSuccess)
+    e = sca2::proj_bwd(a->B, a->T, a->H, Mh, pp->dtype, w, a->phw, a->phq, pp->theta, gr->dphw, gr->dphq, dtheta, st);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd_proj");
   return SCA2_OK;
 }
 

@@ -32,6 +32,17 @@ __device__ __forceinline__ int64_t out_off(const sca2_out& t, int b, int tt, int
 // the state entering its 64-token chunk c in slot 2c and its saved T and E in slot 2c+1.
 __host__ __device__ inline int state_slots(int T) { return 2 * ((T + 63) / 64); }
 
+// Phases formed inside the kernels from the head's projections (phase flavour): when `on`,
+// phw / phq hold K(h) / K(z) in `dtype` and phi = K(h) theta + (pos + t) omega, psi likewise,
+// each product rounded to fp32 and then summed (the reference's fp32 expression).
+struct PhaseProj {
+  int on;
+  int dtype;             // SCA2_F32 or SCA2_BF16
+  const float* theta;    // (H, Mh)
+  const float* omega;    // (H, Mh)
+  const float* pos;      // device scalar, or nullptr = 0
+};
+
 // exp of a difference of cumulative log-decays, clamped at 0 before exp so masked
 // (anti-causal) entries never overflow (sca2/versions/README.md:69-75).
 __device__ __forceinline__ float exp_le0(float x) { return expf(fminf(x, 0.f)); }

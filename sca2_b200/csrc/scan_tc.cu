@@ -91,7 +91,7 @@ __device__ __forceinline__ void copy_out(uint8_t* dst, const bf16* src, int nbyt
 
 template <int FL, int KD, int VB, int R>
 __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
-                                                    float* cstates, int NCS, int flags) {
+                                                    float* cstates, int NCS, int flags, PhaseProj pp) {
   using L = FwdLayout<KD, VB, R>;
   using CO = Cols<KD, VB>;
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     if (prep)
       for (int u = tid * 16; u < C * C * 2; u += NT * 16) cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(0) + u, true);
     cp_commit();
-    load_code_regs<FL, KD>(p, creg, code_vec, b, h, 0, Cl0);
+    load_code_regs<FL, KD>(p, creg, code_vec, b, h, 0, Cl0, pp);
     if (warp == 0) load_gate_regs(p, greg, b, h, 0, Cl0);
   }
   bool ok = true;
@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     }
     if (c + 1 < NC) {  // next chunk's codes and gates into registers
       const int t1 = t0 + C, Cl1 = min(C, p.T - t1);
-      load_code_regs<FL, KD>(p, creg, code_vec, b, h, t1, Cl1);
+      load_code_regs<FL, KD>(p, creg, code_vec, b, h, t1, Cl1, pp);
       if (warp == 0) load_gate_regs(p, greg, b, h, t1, Cl1);
     }
     if (!(ok = wait_mma())) break;
@@ -382,13 +382,13 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
 
 template <int FL, int KD, int VB, int R>
 cudaError_t launch_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates,
-                       int NCS, int flags, cudaStream_t st) {
+                       int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
   auto k = scan_fwd_tc<FL, KD, VB, R>;
   const int smem = FwdLayout<KD, VB, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, p.V / VB);
-  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags);
+  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags, pp);
   return cudaGetLastError();
 }
 
@@ -429,25 +429,26 @@ static int tc_flags(const sca2_scan_args& p, const sca2_out& o) {
   return f;
 }
 
-cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, cudaStream_t st);
+cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, const PhaseProj& pp,
+                         cudaStream_t st);
 
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
-                        float* cstates, int NCS, cudaStream_t st) {
+                        float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp) {
   const bool ph = p.flavor == SCA2_FLAVOR_PHASE;
   int fl = tc_flags(p, o);
   if (cstates && p.K == 64) {  // training: T of every chunk from the chunk-parallel kernel
-    cudaError_t e = tc_scan_prep(p, cstates, NCS, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), st);
+    cudaError_t e = tc_scan_prep(p, cstates, NCS, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), pp, st);
     if (e != cudaSuccess) return e;
     fl |= tc::F_PREP;
   }
 #define SCA2_TC_FWD(KD_, VB_)                                                                         \
   if (p.K == KD_ && VB == VB_)                                                                        \
-    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, st)   \
-              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, st);
+    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, pp, st)   \
+              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, pp, st);
   SCA2_TC_FWD(64, 64) SCA2_TC_FWD(64, 128)
 #undef SCA2_TC_FWD
   if (p.K == 128 && VB == 64 && !ph)
-    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, st);
+    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, pp, st);
   return cudaErrorInvalidValue;
 }
 

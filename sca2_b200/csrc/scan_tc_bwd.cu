@@ -292,7 +292,7 @@ __device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, b
 template <int FL, int R>
 __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                     const float* cstates, sca2_scan_grads gr, int NCS,
-                                                    int flags) {
+                                                    int flags, PhaseProj pp) {
   using L = BwdLayout<FL, R>;
   using CO = BCols;
   constexpr int KD = 64, VB = BVB, RC = R * C, Mh = KD / 2;
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     pf_bytes(sm + L::EB, saved(c) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
     pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
     cp_commit();
-    load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t0, Cl);
+    load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t0, Cl, pp);
     if (warp == 0) load_gate_regs(p, greg, b, h, t0, Cl);
   }
 
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       const int t1 = t0 - C;
       pf_state<KD>(sm + L::CST, cstates, slot(2 * (c - 1)), V, vb0);
       cp_commit();
-      load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t1, C);
+      load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t1, C, pp);
       if (warp == 0) load_gate_regs(p, greg, b, h, t1, C);
     }
     if (!(ok = wait_mma())) break;
@@ -1033,13 +1033,13 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
 
 template <int FL, int R>
 cudaError_t launch_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
-                       const sca2_scan_grads& gr, int NCS, int flags, cudaStream_t st) {
+                       const sca2_scan_grads& gr, int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
   auto k = scan_bwd_tc<FL, R>;
   const int smem = BwdLayout<FL, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, p.V / BVB);
-  k<<<grid, NT, smem, st>>>(p, dO, dS_final, cstates, gr, NCS, flags);
+  k<<<grid, NT, smem, st>>>(p, dO, dS_final, cstates, gr, NCS, flags, pp);
   return cudaGetLastError();
 }
 
@@ -1067,7 +1067,7 @@ bool tc_train_ok(const sca2_scan_args& p, int max_smem) {
 }
 
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
-                        const sca2_scan_grads& gr, int NCS, cudaStream_t st) {
+                        const sca2_scan_grads& gr, int NCS, cudaStream_t st, const PhaseProj& pp) {
   auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
   int f = 0;
   if (p.flavor == SCA2_FLAVOR_PHASE && a16(p.phw.ptr) && a16(p.phq.ptr) && p.phw.sb % 4 == 0 &&
@@ -1082,8 +1082,8 @@ cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float
       gr.dphq.sb % 4 == 0 && gr.dphq.st % 4 == 0 && gr.dphq.sh % 4 == 0)
     f |= tc::B_G_VEC;
   if (p.flavor == SCA2_FLAVOR_PHASE)
-    return tc::launch_bwd<SCA2_FLAVOR_PHASE, 2>(p, dO, dS_final, cstates, gr, NCS, f, st);
-  return tc::launch_bwd<SCA2_FLAVOR_KEY, 1>(p, dO, dS_final, cstates, gr, NCS, f, st);
+    return tc::launch_bwd<SCA2_FLAVOR_PHASE, 2>(p, dO, dS_final, cstates, gr, NCS, f, pp, st);
+  return tc::launch_bwd<SCA2_FLAVOR_KEY, 1>(p, dO, dS_final, cstates, gr, NCS, f, pp, st);
 }
 
 }  // namespace sca2

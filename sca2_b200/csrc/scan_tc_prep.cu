@@ -33,7 +33,8 @@ struct PrepLayout {
 };
 
 template <int FL, int KD>
-__global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec) {
+__global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec,
+                                                     PhaseProj pp) {
   using L = PrepLayout<KD>;
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* c
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 64);
   CodeRegs<FL, KD> cr;
-  load_code_regs<FL, KD>(p, cr, vec != 0, b, h, t0, Cl);
+  load_code_regs<FL, KD>(p, cr, vec != 0, b, h, t0, Cl, pp);
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
@@ -147,7 +148,8 @@ __global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* c
 }  // namespace tc
 
 // T of every chunk into slot 2c+1 of cstates (K = 64); vec: 16-byte loads of the phases / keys
-cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, cudaStream_t st) {
+cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, const PhaseProj& pp,
+                         cudaStream_t st) {
   const int NC = (p.T + tc::C - 1) / tc::C;
   if (NC == 0) return cudaSuccess;
   const int smem = tc::PrepLayout<64>::TOTAL;
@@ -156,12 +158,12 @@ cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int v
     auto k = tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec);
+    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec, pp);
   } else {
     auto k = tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec);
+    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec, pp);
   }
   return cudaGetLastError();
 }

@@ -257,13 +257,59 @@ struct CodeRegs {
   float w[NU][8], q[NU][8];
 };
 
+// 8 projection values of one token row (bf16 or fp32, 16-byte loads when vec)
+__device__ __forceinline__ void load8(const void* base, int64_t off, int dtype, bool vec, float* x) {
+  if (dtype == SCA2_BF16) {
+    const bf16* q = reinterpret_cast<const bf16*>(base) + off;
+    if (vec) {
+      const uint4 u = *reinterpret_cast<const uint4*>(q);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { x[2 * k] = __low2float(h2[k]); x[2 * k + 1] = __high2float(h2[k]); }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = __bfloat162float(q[k]);
+    }
+  } else {
+    const float* q = reinterpret_cast<const float*>(base) + off;
+    if (vec) {
+      const float4 a = reinterpret_cast<const float4*>(q)[0], c = reinterpret_cast<const float4*>(q)[1];
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = q[k];
+    }
+  }
+}
+
 template <int FL, int KD>
 __device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs<FL, KD>& r, bool vec, int b, int h,
-                                               int t0, int Cl) {
+                                               int t0, int Cl, const PhaseProj& pp = PhaseProj{}) {
   const int tid = threadIdx.x;
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     int i, m0;
     code_unit<KD / 16>(tid, i, m0);
+    if (pp.on) {  // phases from the projections: phi = K(h) theta + (pos + t) omega
+      if (i < Cl) {
+        constexpr int Mh = KD / 2;
+        float kh[8], kz[8];
+        load8(p.phw.ptr, tok_off(p.phw, b, t0 + i, h) + m0, pp.dtype, vec, kh);
+        load8(p.phq.ptr, tok_off(p.phq, b, t0 + i, h) + m0, pp.dtype, vec, kz);
+        const float pt = __fadd_rn(pp.pos ? *pp.pos : 0.f, (float)(t0 + i));
+        const float* th = pp.theta + h * Mh + m0;
+        const float* om = pp.omega + h * Mh + m0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float po = __fmul_rn(pt, om[k]);
+          r.w[0][k] = __fadd_rn(__fmul_rn(kh[k], th[k]), po);
+          r.q[0][k] = __fadd_rn(__fmul_rn(kz[k], th[k]), po);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { r.w[0][k] = 0.f; r.q[0][k] = 0.f; }
+      }
+      return;
+    }
     const float* pw = reinterpret_cast<const float*>(p.phw.ptr);
     const float* pq = reinterpret_cast<const float*>(p.phq.ptr);
     if (i < Cl) {

@@ -181,14 +181,13 @@ class LongHead(nn.Module):
     def prefill(self, z, h, state: Optional[State] = None):
         B, T, _ = z.shape
         st = state if state is not None else self.init_state(B, z.device)
-        p = _positions(T, st["pos"], z.device)
-        phw = self._phase(h, p)[:, :, None]
-        phq = self._phase(z, p)[:, :, None]
         v = self.V(z).to(_value_dtype(z))[:, :, None]
         beta = torch.sigmoid(self.bproj(z).float())
         S0 = torch.cat([st["sr"], st["si"]], 1)[:, None].float()
-        o, S = ops.phase_scan(phw, phq, v, beta, None, self.lam()[None], self.wr.float()[None],
-                              self.wi.float()[None], S0)
+        # phases K(x) theta + p omega formed inside the scan kernels where they cover the call
+        o, S = ops.phase_scan_proj(self.K(h)[:, :, None], self.K(z)[:, :, None], self.theta[None], self.omega[None],
+                                   st["pos"], v, beta, None, self.lam()[None], self.wr.float()[None],
+                                   self.wi.float()[None], S0)
         u = _rms(o.reshape(B, T, 2 * self.dv)).to(z.dtype)
         M = self.M
         return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": st["pos"] + T}
@@ -262,14 +261,20 @@ class _PhaseHead(CHeadBase):
     def prefill(self, z, h, state=None):
         B, T, _ = z.shape
         st = state if state is not None else self.init_state(B, z.device)
-        p = _positions(T, st["pos"], z.device)
         lam = self._lam()
         S0 = None if st.get("empty", False) else torch.cat([st["sr"], st["si"]], 1)[:, None].float()
-        o, S = ops.phase_scan(self._pw(h, p)[:, :, None], self._pq(z, p)[:, :, None],
-                              self._value(z, h).to(_value_dtype(z))[:, :, None],
-                              self._beta(z), None,
-                              None if lam is None else lam[None], self.wr.float()[None],
-                              self.wi.float()[None], S0)
+        v = self._value(z, h).to(_value_dtype(z))[:, :, None]
+        if type(self)._pw is _PhaseHead._pw and type(self)._pq is _PhaseHead._pq:
+            # phases K(x) theta + p omega formed inside the scan kernels where they cover the call
+            o, S = ops.phase_scan_proj(self.K(h)[:, :, None], self.K(z)[:, :, None], self.theta[None],
+                                       self.omega[None], st["pos"], v, self._beta(z), None,
+                                       None if lam is None else lam[None], self.wr.float()[None],
+                                       self.wi.float()[None], S0)
+        else:
+            p = _positions(T, st["pos"], z.device)
+            o, S = ops.phase_scan(self._pw(h, p)[:, :, None], self._pq(z, p)[:, :, None], v, self._beta(z), None,
+                                  None if lam is None else lam[None], self.wr.float()[None],
+                                  self.wi.float()[None], S0)
         M = self.M
         u = self._out(o.reshape(B, T, 2 * self.dv).float(), z).to(z.dtype)
         return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": st["pos"] + T, "empty": False}
@@ -385,13 +390,14 @@ class CHeadGated(CHeadBase):
         B, T, _ = z.shape
         H, Mh, dvh = self.H, self.Mh, self.dvh
         st = state if state is not None else self.init_state(B, z.device)
-        p = _positions(T, st["pos"], z.device)
-        pw, pq = self._phases(z, h, p)
         g = self._logdecay(z) if self.decay else None
         S0 = None if st.get("empty", False) else torch.cat([st["sr"], st["si"]], 2).float()
-        o, S = ops.phase_scan(pw.view(B, T, H, Mh), pq.view(B, T, H, Mh),
-                              self.V(z).to(_value_dtype(z)).view(B, T, H, dvh), None, g, None,
-                              self.wr.float().view(H, Mh), self.wi.float().view(H, Mh), S0)
+        kq = self.Kq(z) if self.sepq else self.K(z)
+        # phases K(x) theta + p omega formed inside the scan kernels where they cover the call
+        o, S = ops.phase_scan_proj(self.K(h).view(B, T, H, Mh), kq.view(B, T, H, Mh), self.theta.view(H, Mh),
+                                   self.omega.view(H, Mh), st["pos"],
+                                   self.V(z).to(_value_dtype(z)).view(B, T, H, dvh), None, g, None,
+                                   self.wr.float().view(H, Mh), self.wi.float().view(H, Mh), S0)
         u = torch.cat([o[:, :, :, 0].reshape(B, T, self.dv), o[:, :, :, 1].reshape(B, T, self.dv)], -1)
         u = _gated_out(self, u.float(), z).to(z.dtype)
         return u, {"sr": S[:, :, :Mh], "si": S[:, :, Mh:], "pos": st["pos"] + T, "empty": False}

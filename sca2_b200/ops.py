@@ -241,6 +241,151 @@ def phase_scan(phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None, S0=No
 
 
 # ======================================================================================
+#  phase-coded scan with the phases formed in the kernels from the projections
+# ======================================================================================
+def _pp(kh, theta, omega, pos):
+    pp = _lib.PhaseProj()
+    pp.dtype = _DT[kh.dtype]
+    pp.theta, pp.omega, pp.pos = theta.data_ptr(), omega.data_ptr(), _ptr(pos)
+    return pp
+
+
+@torch.library.custom_op("sca2b200::phase_scan_proj_fwd", mutates_args=())
+def _phase_scan_proj_fwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
+                         g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
+                         S0: Optional[torch.Tensor], theta: torch.Tensor, omega: torch.Tensor,
+                         pos: Optional[torch.Tensor], save: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_scan_fwd_proj: as phase_scan_fwd with phi = kh theta + (pos + t) omega and psi
+    = kz theta + (pos + t) omega formed inside the kernels."""
+    a = _phase_args(kh, kz, v, beta, g, lam, wr, wi, S0)
+    B, T, H, Mh = kh.shape
+    V = v.shape[-1]
+    o = torch.empty(B, T, H, 2, V, device=v.device, dtype=v.dtype)
+    S = torch.empty(B, H, 2 * Mh, V, device=v.device, dtype=torch.float32)
+    cs = (torch.empty(B, H, _slots(T), 2 * Mh, V, device=v.device, dtype=torch.float32) if save
+          else torch.empty(0, device=v.device, dtype=torch.float32))
+    _lib.check(_lib.load().sca2_scan_fwd_proj(C_ref(a), C_ref(_pp(kh, theta, omega, pos)), _out(o), _ptr(S),
+                                              _ptr(cs) if save else None, _stream()), "scan_fwd_proj")
+    return o, S, cs
+
+
+@_phase_scan_proj_fwd.register_fake
+def _(kh, kz, v, beta, g, lam, wr, wi, S0, theta, omega, pos, save):
+    B, T, H, Mh = kh.shape
+    V = v.shape[-1]
+    return (v.new_empty(B, T, H, 2, V), v.new_empty(B, H, 2 * Mh, V, dtype=torch.float32),
+            v.new_empty((B, H, _slots(T), 2 * Mh, V) if save else (0,), dtype=torch.float32))
+
+
+@torch.library.custom_op("sca2b200::phase_scan_proj_bwd", mutates_args=())
+def _phase_scan_proj_bwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
+                         g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
+                         S0: Optional[torch.Tensor], theta: torch.Tensor, omega: torch.Tensor,
+                         pos: Optional[torch.Tensor], cs: torch.Tensor, do: torch.Tensor, dS: Optional[torch.Tensor]
+                         ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                    torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_scan_bwd_proj: gradients of (kh, kz, v, beta, g, lam, wr, wi, S0, theta)."""
+    B, T, H, Mh = kh.shape
+    V = v.shape[-1]
+    dev = v.device
+    do = do.to(v.dtype)
+    if do.stride(-1) != 1:
+        do = do.contiguous()
+    dS = None if dS is None else dS.float().contiguous()
+    a = _phase_args(kh, kz, v, beta, g, lam, wr, wi, S0)
+    z = lambda *sh: torch.zeros(*sh, device=dev, dtype=torch.float32)
+    E = lambda: torch.empty(0, device=dev, dtype=torch.float32)
+    dkh, dkz = torch.empty_like(kh), torch.empty_like(kz)
+    dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
+    dbeta = z(B, T, H) if beta is not None else None
+    dg = z(B, T, H) if g is not None else None
+    dlam = z(H, Mh) if lam is not None else None
+    dwr, dwi = z(H, Mh), z(H, Mh)
+    dS0 = torch.empty(B, H, 2 * Mh, V, device=dev, dtype=torch.float32)
+    dth = torch.empty(H, Mh, device=dev, dtype=torch.float32)
+    gr = ScanGrads()
+    gr.dphw, gr.dphq, gr.dv = _tok(dkh), _tok(dkz), _tok(dv)
+    gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
+    gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), _ptr(dwr), _ptr(dwi), _ptr(dS0)
+    lib = _lib.load()
+    wk = torch.empty((lib.sca2_scan_proj_work_bytes(B, T, H, Mh) + 3) // 4, device=dev, dtype=torch.float32)
+    _lib.check(lib.sca2_scan_bwd_proj(C_ref(a), C_ref(_pp(kh, theta, omega, pos)), _out(do), _ptr(dS), _ptr(cs),
+                                      C_ref(gr), dth.data_ptr(), wk.data_ptr(), _stream()), "scan_bwd_proj")
+    return (dkh, dkz, dv, E() if dbeta is None else dbeta, E() if dg is None else dg,
+            E() if dlam is None else dlam, dwr, dwi, dS0 if S0 is not None else E(), dth)
+
+
+@_phase_scan_proj_bwd.register_fake
+def _(kh, kz, v, beta, g, lam, wr, wi, S0, theta, omega, pos, cs, do, dS):
+    B, T, H, Mh = kh.shape
+    V = v.shape[-1]
+    f = lambda *sh: v.new_empty(*sh, dtype=torch.float32)
+    return (torch.empty_like(kh), torch.empty_like(kz), v.new_empty(B, T, H, V),
+            f(B, T, H) if beta is not None else f(0), f(B, T, H) if g is not None else f(0),
+            f(H, Mh) if lam is not None else f(0), f(H, Mh), f(H, Mh), f(B, H, 2 * Mh, V) if S0 is not None else f(0),
+            f(H, Mh))
+
+
+def _proj_setup(ctx, inputs, output):
+    ctx.save_for_backward(*inputs[:12], output[2])
+
+
+def _proj_backward(ctx, do, dS, dcs):
+    kh, kz, v, beta, g, lam, wr, wi, S0, theta, omega, pos, cs = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*kh.shape[:3], 2, v.shape[-1], device=v.device, dtype=v.dtype)
+    gr = torch.ops.sca2b200.phase_scan_proj_bwd(kh, kz, v, beta, g, lam, wr, wi, S0, theta, omega, pos, cs, do, dS)
+    ni = ctx.needs_input_grad
+    ins = (kh, kz, v, beta, g, lam, wr, wi, S0)
+    out = [gd if (ni[j] and ins[j] is not None) else None for j, gd in enumerate(gr[:9])]
+    return tuple(out) + (gr[9] if ni[9] else None, None, None, None)
+
+
+_phase_scan_proj_fwd.register_autograd(_proj_backward, setup_context=_proj_setup)
+
+
+def _proj_ok(kh, v) -> bool:
+    """Whether the projected-phase kernels cover this call (the rule of
+    sca2_scan_proj_supported): tensor-core path (bf16 values, K = 2 Mh = 64, V a multiple
+    of 64) and 16-byte aligned projection rows."""
+    if kh.dim() != 4 or kh.shape[-1] != 32 or v.dtype != torch.bfloat16 or v.shape[-1] % 64 or kh.shape[1] == 0:
+        return False
+    if kh.dtype not in _DT or kh.stride(-1) != 1:
+        return False
+    q = 8 if kh.dtype == torch.bfloat16 else 4
+    return kh.data_ptr() % 16 == 0 and all(s % q == 0 for s in kh.stride()[:3])
+
+
+def phase_scan_proj(kh, kz, theta, omega, pos, v, beta=None, g=None, lam=None, wr=None, wi=None, S0=None):
+    """The phase scan fed by the head's projections: kh, kz (B,T,H,Mh) = K(h), K(z) (fp32 or
+    bf16), theta, omega (H,Mh), pos a 0-dim fp32 tensor (position of token 0) or None; the
+    phases phi = kh theta + (pos + t) omega, psi = kz theta + (pos + t) omega are formed inside
+    the kernels when the tensor-core path covers the call, and in torch otherwise (same
+    expression, then ops.phase_scan).  Returns (o, S) as phase_scan; differentiable in kh, kz,
+    theta and the scan's inputs."""
+    if wr is None or wi is None:
+        raise _lib.Sca2Error("wr and wi are required")
+    _need_cuda(kh, kz, theta, omega, pos, v, beta, g, lam, wr, wi, S0)
+    if _proj_ok(kh, v) and _proj_ok(kz, v) and kh.dtype == kz.dtype and kh.shape == kz.shape:
+        th, om = theta.float().contiguous(), omega.float().contiguous()
+        ps = None if pos is None else pos.float().reshape(())
+        lam_ = None if lam is None else lam.float().contiguous()
+        w1, w2 = wr.float().contiguous(), wi.float().contiguous()
+        S0_ = None if S0 is None else S0.float().contiguous()
+        b_, g_ = _f32(beta), _f32(g)
+        _check_phase(kh, kz, v, b_, g_, lam_, w1, w2, S0_)
+        save = _wants_grad(kh, kz, v, b_, g_, lam_, w1, w2, S0_, th)
+        o, S, _ = torch.ops.sca2b200.phase_scan_proj_fwd(kh, kz, v, b_, g_, lam_, w1, w2, S0_, th, om, ps, save)
+        return o, S
+    T = kh.shape[1]
+    p = torch.arange(T, device=kh.device, dtype=torch.float32)[:, None, None]
+    if pos is not None:
+        p = p + pos.float()
+    th, om = theta.float(), omega.float()
+    return phase_scan(kh.float() * th + p * om, kz.float() * th + p * om, v, beta, g, lam, wr, wi, S0)
+
+
+# ======================================================================================
 #  explicit-key (GDN) scan
 # ======================================================================================
 def _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta):

@@ -51,6 +51,8 @@ int main(void) {
   printf("sca2_short_args %zu\nsca2_short_grads %zu\n", sizeof(sca2_short_args), sizeof(sca2_short_grads));
   F(sca2_short_args, pos) F(sca2_short_args, kh) F(sca2_short_args, omega) F(sca2_short_args, e0)
   F(sca2_short_grads, dv) F(sca2_short_grads, dtheta) F(sca2_short_grads, de0)
+  printf("sca2_phase_proj %zu\n", sizeof(sca2_phase_proj));
+  F(sca2_phase_proj, theta) F(sca2_phase_proj, pos)
   return 0;
 }
 """
@@ -69,12 +71,14 @@ int main(void) {
     assert int(out["sca2_dscan_grads"]) == ctypes.sizeof(_lib.DScanGrads)
     assert int(out["sca2_short_args"]) == ctypes.sizeof(_lib.ShortArgs)
     assert int(out["sca2_short_grads"]) == ctypes.sizeof(_lib.ShortGrads)
+    assert int(out["sca2_phase_proj"]) == ctypes.sizeof(_lib.PhaseProj)
     for key, val in out.items():
         if "." in key:
             st, field = key.split(".")
             cls = {"sca2_scan_args": _lib.ScanArgs, "sca2_scan_grads": _lib.ScanGrads,
                    "sca2_dscan_args": _lib.DScanArgs, "sca2_dscan_grads": _lib.DScanGrads,
-                   "sca2_short_args": _lib.ShortArgs, "sca2_short_grads": _lib.ShortGrads}[st]
+                   "sca2_short_args": _lib.ShortArgs, "sca2_short_grads": _lib.ShortGrads,
+                   "sca2_phase_proj": _lib.PhaseProj}[st]
             assert getattr(cls, field).offset == int(val), key
 
 
