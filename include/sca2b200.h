@@ -129,6 +129,11 @@ typedef struct sca2_scan_grads {
   float* dwr;
   float* dwi;
   float* dS0;
+  /* 0: the fp32 gradients are accumulated into (caller zero-fills them, as above).
+   * 1: every gradient is WRITTEN: the library initialises the buffers itself (the
+   *    tensor-core backward writes the per-token rows directly where one CTA owns them)
+   *    and all per-token gradient tensors must be dense (B,T,H,C). */
+  int32_t overwrite;
 } sca2_scan_grads;
 
 /* Backward scan: reverse chunk sweep of the adjoint state, all per-token

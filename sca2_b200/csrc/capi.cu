@@ -170,6 +170,49 @@ int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* ch
   return SCA2_OK;
 }
 
+static bool tok_dense(const sca2_tok& t, const sca2_scan_args* a, int C) {
+  return t.sh == C && t.st == (int64_t)a->H * C && t.sb == (int64_t)a->T * a->H * C;
+}
+
+// Overwrite mode: zero the gradients the kernels accumulate into.  The per-token key-side rows
+// are left alone when the tensor-core backward writes them itself (one CTA per (b, h)).
+static cudaError_t init_grads(const sca2_scan_args* a, const sca2_scan_grads* gr, bool rows_written,
+                              cudaStream_t st) {
+  const int KH = a->flavor == SCA2_FLAVOR_PHASE ? a->K / 2 : a->K;
+  const size_t tok = (size_t)a->B * a->T * a->H * sizeof(float);
+  cudaError_t e = cudaSuccess;
+  auto z = [&](const void* p, size_t bytes) {
+    if (p && bytes && e == cudaSuccess) e = cudaMemsetAsync(const_cast<void*>(p), 0, bytes, st);
+  };
+  if (!rows_written) {
+    z(gr->dphw.ptr, tok * KH);
+    z(gr->dphq.ptr, tok * KH);
+  }
+  if (a->beta.ptr) z(gr->dbeta.ptr, tok);
+  if (a->g.ptr) z(gr->dg.ptr, tok);
+  if (a->lam) z(gr->dlam, (size_t)a->H * KH * sizeof(float));
+  if (a->flavor == SCA2_FLAVOR_PHASE) {
+    z(gr->dwr, (size_t)a->H * KH * sizeof(float));
+    z(gr->dwi, (size_t)a->H * KH * sizeof(float));
+  }
+  return e;
+}
+
+static int check_overwrite(const sca2_scan_args* a, const sca2_scan_grads* gr) {
+  const int KH = a->flavor == SCA2_FLAVOR_PHASE ? a->K / 2 : a->K;
+  if (!tok_dense(gr->dphw, a, KH) || !tok_dense(gr->dphq, a, KH) ||
+      (a->beta.ptr && !tok_dense(gr->dbeta, a, 1)) || (a->g.ptr && !tok_dense(gr->dg, a, 1)))
+    return fail(SCA2_ERR_ARG, "overwrite mode needs dense (B,T,H,C) gradient tensors");
+  return SCA2_OK;
+}
+
+// whether the tensor-core backward writes the key-side rows itself in overwrite mode
+static bool tc_rows_written(const sca2_scan_args* a, const sca2_tok& dphw, const sca2_tok& dphq) {
+  auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
+  return a->V == 64 && a16(dphw.ptr) && a16(dphq.ptr) && dphw.sb % 4 == 0 && dphw.st % 4 == 0 &&
+         dphw.sh % 4 == 0 && dphq.sb % 4 == 0 && dphq.st % 4 == 0 && dphq.sh % 4 == 0;
+}
+
 int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
                   const float* chunk_states, const sca2_scan_grads* gr, void* stream) {
   int rc = check_scan(a, true);
@@ -191,9 +234,14 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
     return fail(SCA2_ERR_ARG, "dphw/dk, dphq/dq and dv must be non-null");
   if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
   if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
-  cudaError_t e = sca2::tc_train_ok(*a, max_optin_smem())
-                      ? sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, *gr, sca2::state_slots(a->T), st)
-                      : sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
+  const bool tc = sca2::tc_train_ok(*a, max_optin_smem());
+  if (gr->overwrite) {
+    if ((rc = check_overwrite(a, gr))) return rc;
+    cudaError_t e = init_grads(a, gr, tc && tc_rows_written(a, gr->dphw, gr->dphq), st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd(init)");
+  }
+  cudaError_t e = tc ? sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, *gr, sca2::state_slots(a->T), st)
+                     : sca2::f32_scan_bwd(*a, dO, dS_final, chunk_states, *gr, st);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
   return SCA2_OK;
 }
@@ -261,15 +309,21 @@ int sca2_scan_bwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_
   if (!gr->dv.ptr) return fail(SCA2_ERR_ARG, "dv must be non-null");
   if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
   if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
-  // d(phi), d(psi) into the zero-filled workspace, then the projections' gradients
+  // d(phi), d(psi) into the workspace (written by the kernel when one CTA owns each row, else
+  // zero-filled and accumulated into), then the projections' gradients
   float* w = static_cast<float*>(work);
   const size_t n = (size_t)a->B * a->T * a->H * Mh;
-  cudaError_t e = cudaMemsetAsync(w, 0, 2 * n * sizeof(float), st);
-  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd_proj");
   sca2_scan_grads g2 = *gr;
   const int64_t sh = Mh, stt = (int64_t)a->H * Mh, sb = (int64_t)a->T * stt;
   g2.dphw = sca2_tok{w, sb, stt, sh};
   g2.dphq = sca2_tok{w + n, sb, stt, sh};
+  g2.overwrite = tc_rows_written(a, g2.dphw, g2.dphq) ? 1 : 0;
+  cudaError_t e = g2.overwrite ? cudaSuccess : cudaMemsetAsync(w, 0, 2 * n * sizeof(float), st);
+  if (e == cudaSuccess && gr->overwrite) {
+    if ((rc = check_overwrite(a, &g2))) return rc;
+    e = init_grads(a, &g2, true, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd_proj");
   e = sca2::tc_scan_bwd(*a, dO, dS_final, chunk_states, g2, sca2::state_slots(a->T), st, to_pp(pp));
   if (e == cudaSuccess)
     e = sca2::proj_bwd(a->B, a->T, a->H, Mh, pp->dtype, w, a->phw, a->phq, pp->theta, gr->dphw, gr->dphq, dtheta, st);

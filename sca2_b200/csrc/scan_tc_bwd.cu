@@ -91,7 +91,8 @@ struct BCols {
 };
 
 // launch flags of the backward (host-computed)
-enum : int { B_PH_VEC = 1, B_DO_VEC = 2, B_DV_VEC = 4, B_G_VEC = 8, B_K_VEC = 16 };
+// B_OVERWRITE: write the key-side gradient rows instead of accumulating (this CTA owns them)
+enum : int { B_PH_VEC = 1, B_DO_VEC = 2, B_DV_VEC = 4, B_G_VEC = 8, B_K_VEC = 16, B_OVERWRITE = 32 };
 
 // ---- asynchronous copies of the next chunk's saved data ------------------------------------
 template <int KD>
@@ -338,7 +339,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   bf16* DYA = BF(L::R5);
   float* GRW = reinterpret_cast<float*>(sm + L::GRW);
   float* GRQ = reinterpret_cast<float*>(sm + L::GRQ);
-  const bool gstage = excl && (flags & B_G_VEC);  // gradient rows staged in shared memory
+  const bool gwrite = excl && (flags & B_OVERWRITE) && (flags & B_G_VEC);  // rows written, not accumulated
+  const bool gstage = excl && (flags & B_G_VEC) && !gwrite;  // gradient rows staged in shared memory
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
@@ -958,8 +960,17 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           y[4 * hh] = a.x; y[4 * hh + 1] = a.y; y[4 * hh + 2] = a.z; y[4 * hh + 3] = a.w;
           z[4 * hh] = q.x; z[4 * hh + 1] = q.y; z[4 * hh + 2] = q.z; z[4 * hh + 3] = q.w;
         }
-        acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, y, gvec, excl, gstage ? GRW + i * KH + m0 : nullptr);
-        acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, z, gvec, excl, gstage ? GRQ + i * KH + m0 : nullptr);
+        if (gwrite) {
+          float4* dk4 = reinterpret_cast<float4*>(dk + tok_off(gr.dphw, b, t0 + i, h) + m0);
+          float4* dq4 = reinterpret_cast<float4*>(dq + tok_off(gr.dphq, b, t0 + i, h) + m0);
+          dk4[0] = make_float4(y[0], y[1], y[2], y[3]);
+          dk4[1] = make_float4(y[4], y[5], y[6], y[7]);
+          dq4[0] = make_float4(z[0], z[1], z[2], z[3]);
+          dq4[1] = make_float4(z[4], z[5], z[6], z[7]);
+        } else {
+          acc_row8(dk + tok_off(gr.dphw, b, t0 + i, h) + m0, y, gvec, excl, gstage ? GRW + i * KH + m0 : nullptr);
+          acc_row8(dq + tok_off(gr.dphq, b, t0 + i, h) + m0, z, gvec, excl, gstage ? GRQ + i * KH + m0 : nullptr);
+        }
       }
     }
     // ---- per-token beta and decay gradients
@@ -1081,6 +1092,7 @@ cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float
   if (a16(gr.dphw.ptr) && a16(gr.dphq.ptr) && gr.dphw.sb % 4 == 0 && gr.dphw.st % 4 == 0 && gr.dphw.sh % 4 == 0 &&
       gr.dphq.sb % 4 == 0 && gr.dphq.st % 4 == 0 && gr.dphq.sh % 4 == 0)
     f |= tc::B_G_VEC;
+  if (gr.overwrite && p.V == tc::BVB && (f & tc::B_G_VEC)) f |= tc::B_OVERWRITE;
   if (p.flavor == SCA2_FLAVOR_PHASE)
     return tc::launch_bwd<SCA2_FLAVOR_PHASE, 2>(p, dO, dS_final, cstates, gr, NCS, f, pp, st);
   return tc::launch_bwd<SCA2_FLAVOR_KEY, 1>(p, dO, dS_final, cstates, gr, NCS, f, pp, st);

@@ -165,7 +165,7 @@ def _phase_scan_bwd(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta:
         do = do.contiguous()
     dS = None if dS is None else dS.float().contiguous()
     a = _phase_args(phw, phq, v, beta, g, lam, wr, wi, S0)
-    z = lambda *sh: torch.zeros(*sh, device=dev, dtype=torch.float32)
+    z = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # written (overwrite mode)
     E = lambda: torch.empty(0, device=dev, dtype=torch.float32)  # the gradient of an absent input
     dphw, dphq = z(B, T, H, Mh), z(B, T, H, Mh)
     dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
@@ -178,6 +178,7 @@ def _phase_scan_bwd(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta:
     gr.dphw, gr.dphq, gr.dv = _tok(dphw), _tok(dphq), _tok(dv)
     gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
     gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), _ptr(dwr), _ptr(dwi), _ptr(dS0)
+    gr.overwrite = 1
     _lib.check(_lib.load().sca2_scan_bwd(C_ref(a), _out(do), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
                "scan_bwd")
     return (dphw, dphq, dv, E() if dbeta is None else dbeta, E() if dg is None else dg,
@@ -293,7 +294,7 @@ def _phase_scan_proj_bwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, be
         do = do.contiguous()
     dS = None if dS is None else dS.float().contiguous()
     a = _phase_args(kh, kz, v, beta, g, lam, wr, wi, S0)
-    z = lambda *sh: torch.zeros(*sh, device=dev, dtype=torch.float32)
+    z = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # written (overwrite mode)
     E = lambda: torch.empty(0, device=dev, dtype=torch.float32)
     dkh, dkz = torch.empty_like(kh), torch.empty_like(kz)
     dv = torch.empty(B, T, H, V, device=dev, dtype=v.dtype)
@@ -307,6 +308,7 @@ def _phase_scan_proj_bwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, be
     gr.dphw, gr.dphq, gr.dv = _tok(dkh), _tok(dkz), _tok(dv)
     gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
     gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), _ptr(dwr), _ptr(dwi), _ptr(dS0)
+    gr.overwrite = 1
     lib = _lib.load()
     wk = torch.empty((lib.sca2_scan_proj_work_bytes(B, T, H, Mh) + 3) // 4, device=dev, dtype=torch.float32)
     _lib.check(lib.sca2_scan_bwd_proj(C_ref(a), C_ref(_pp(kh, theta, omega, pos)), _out(do), _ptr(dS), _ptr(cs),
@@ -454,7 +456,7 @@ def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional
     do5 = do.unsqueeze(3)
     dS = None if dS is None else dS.float().contiguous()
     a = _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta)
-    z = lambda *sh: torch.zeros(*sh, device=dev, dtype=torch.float32)
+    z = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # written (overwrite mode)
     E = lambda: torch.empty(0, device=dev, dtype=torch.float32)
     dk, dq = z(B, T, H, K), z(B, T, H, K)
     dv = torch.empty(B, T, H, V, device=dev, dtype=dt)
@@ -466,6 +468,7 @@ def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional
     gr.dphw, gr.dphq, gr.dv = _tok(dk), _tok(dq), _tok(dv)
     gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
     gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), None, None, _ptr(dS0)
+    gr.overwrite = 1
     _lib.check(_lib.load().sca2_scan_bwd(C_ref(a), _out(do5), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
                "scan_bwd")
     return (dq, dk, dv, E() if dg is None else dg, E() if dbeta is None else dbeta, E() if dlam is None else dlam,
@@ -960,11 +963,12 @@ def rms(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
 # ======================================================================================
 class PhaseScanPlan:
     """A phase-flavour scan with every output / saved / gradient buffer allocated once, so
-    fwd() and bwd() are exactly one library call each (plus the zero-fill of the gradient
-    accumulators in bwd) and can be timed or captured in a CUDA graph."""
+    fwd() and bwd() are exactly one library call each and can be timed or captured in a CUDA
+    graph.  overwrite=True: the gradients are written (the library initialises them); False:
+    they accumulate and bwd() zero-fills them first."""
 
     def __init__(self, phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None, S0=None,
-                 need_grad=True):
+                 need_grad=True, overwrite=True):
         _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0)
         _need_cuda(phw, phq, v, beta, g, lam, wr, wi, S0)
         self.inp = dict(phw=_inner(phw.float()), phq=_inner(phq.float()), v=_inner(v),
@@ -996,8 +1000,10 @@ class PhaseScanPlan:
             gr.dphw, gr.dphq, gr.dv = _tok(G["phw"]), _tok(G["phq"]), _tok(G["v"])
             gr.dbeta, gr.dg = _tok(G["beta"]), _tok(G["g"])
             gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(G["lam"]), _ptr(G["wr"]), _ptr(G["wi"]), _ptr(G["S0"])
+            gr.overwrite = 1 if overwrite else 0
             self.gr = gr
-            self._acc = [t for k, t in G.items() if t is not None and k not in ("v", "S0")]
+            # overwrite: the library initialises every gradient itself; else they accumulate
+            self._acc = [] if overwrite else [t for k, t in G.items() if t is not None and k not in ("v", "S0")]
 
     def fwd(self):
         _lib.check(self.lib.sca2_scan_fwd(C_ref(self.args), _out(self.o), _ptr(self.S), _ptr(self.cs),
