@@ -302,6 +302,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, sub = warp & 3, half = tid >> 7;
   const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int vb0 = blockIdx.y * VB;
+  // MMA issue: lane 0 of warps 0..NISS-1 each issue the products of their own accumulators and
+  // commit (or arrive, when they have none in a batch) on the batch's mbarrier
+  constexpr int NISS = 4;
+  const bool issuer = lane == 0 && warp < NISS;
   const int V = p.V;
   const bool has_g = p.g.ptr != nullptr;
   const bool excl = gridDim.y == 1;  // the only CTA writing this (b, h)'s key-side gradients
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   }
   for (int u = tid; u < KD * VB; u += NT) LAMS[u] = 0.f;
   if (tid == 0) {
-    umma::mbar_init(mbar, 1);
+    umma::mbar_init(mbar, NISS);
     umma::fence_mbar_init();
     *s_err = 0;
   }
@@ -454,13 +458,18 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     build_codes2<FL, KD, R>(creg, sm, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
     // ================= batch 1 =================
-    if (tid == 0) {
-      umma::gemm_t(tb + CO::G, sm + L::KR, false, sm + L::KW, false, C, C, KD, false);
-      umma::gemm_t(tb + CO::P, sm + L::QR, false, sm + L::KW, false, RC, C, KD, false);
-      umma::gemm_t(tb + CO::DS0, sm + L::DOA, true, sm + L::R1, true, VB, KD, RC, false);
-      umma::gemm_t(tb + CO::DQR2, sm + L::DOA, false, SB, true, RC, KD, VB, false);
-      umma::gemm_t(tb + CO::DKW3, sm + L::EB, true, DSB, true, C, KD, VB, false);
-      umma::gemm_t(tb + CO::DE, sm + L::R2, false, DSB, false, C, VB, KD, false);
+    if (issuer) {  // independent accumulators issued from NISS threads in parallel
+      if (warp == 0) {
+        umma::gemm_t(tb + CO::G, sm + L::KR, false, sm + L::KW, false, C, C, KD, false);
+        umma::gemm_t(tb + CO::P, sm + L::QR, false, sm + L::KW, false, RC, C, KD, false);
+      } else if (warp == 1) {
+        umma::gemm_t(tb + CO::DS0, sm + L::DOA, true, sm + L::R1, true, VB, KD, RC, false);
+      } else if (warp == 2) {
+        umma::gemm_t(tb + CO::DQR2, sm + L::DOA, false, SB, true, RC, KD, VB, false);
+        umma::gemm_t(tb + CO::DKW3, sm + L::EB, true, DSB, true, C, KD, VB, false);
+      } else {
+        umma::gemm_t(tb + CO::DE, sm + L::R2, false, DSB, false, C, VB, KD, false);
+      }
       umma::commit(mbar);
     }
     // next chunk: staged state (CST is free once the prologue has read it), codes and gates
@@ -486,9 +495,13 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     });
     publish_smem();
     // ================= batch 2: dE += P^T dO =================
-    if (tid == 0) {
-      umma::gemm_t(tb + CO::DE, PA, true, sm + L::DOA, true, C, VB, RC, true);
-      umma::commit(mbar);
+    if (issuer) {
+      if (warp == 0) {
+        umma::gemm_t(tb + CO::DE, PA, true, sm + L::DOA, true, C, VB, RC, true);
+        umma::commit(mbar);
+      } else {
+        umma::mbar_arrive(mbar);
+      }
     }
     if (!(ok = wait_mma())) break;
     for_frag<C, VB>(tb + CO::DE, [&](int j, int v0, int, const float* x) {
@@ -497,9 +510,13 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     });
     publish_smem();
     // ================= batch 3: dY = T^T dE =================
-    if (tid == 0) {
-      umma::gemm_t(tb + CO::DY, sm + L::TB, true, DEA, true, C, VB, C, false);
-      umma::commit(mbar);
+    if (issuer) {
+      if (warp == 0) {
+        umma::gemm_t(tb + CO::DY, sm + L::TB, true, DEA, true, C, VB, C, false);
+        umma::commit(mbar);
+      } else {
+        umma::mbar_arrive(mbar);
+      }
     }
     if (!(ok = wait_mma())) break;
     if (c > 0) {  // TB is free: the next chunk's T
@@ -538,11 +555,15 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     }
     publish_smem();
     // ================= batch 4: DL, DP, DS0 += dY^T ZN, DKR2 =================
-    if (tid == 0) {
-      umma::gemm_t(tb + CO::DL, DYA, false, sm + L::EB, true, C, C, VB, false);
-      umma::gemm_t(tb + CO::DP, sm + L::DOA, false, sm + L::EB, true, RC, C, VB, false);
-      umma::gemm_t(tb + CO::DS0, DYA, true, sm + L::R3, true, VB, KD, C, true);
-      umma::gemm_t(tb + CO::DKR2, DYA, false, SB, true, C, KD, VB, false);
+    if (issuer) {
+      if (warp == 0)
+        umma::gemm_t(tb + CO::DL, DYA, false, sm + L::EB, true, C, C, VB, false);
+      else if (warp == 1)
+        umma::gemm_t(tb + CO::DP, sm + L::DOA, false, sm + L::EB, true, RC, C, VB, false);
+      else if (warp == 2)
+        umma::gemm_t(tb + CO::DS0, DYA, true, sm + L::R3, true, VB, KD, C, true);
+      else
+        umma::gemm_t(tb + CO::DKR2, DYA, false, SB, true, C, KD, VB, false);
       umma::commit(mbar);
     }
     if (!(ok = wait_mma())) break;
@@ -680,16 +701,22 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     }
     publish_smem();
     // ================= batch 5: DKR1, DQR1, DKW12, DLW =================
-    if (tid == 0) {
-      umma::gemm_t(tb + CO::DKR1, DKKA, false, sm + L::KW, true, C, KD, C, false);
-      umma::gemm_t(tb + CO::DQR1, DQKA, false, sm + L::KW, true, RC, KD, C, false);
-      umma::gemm_t(tb + CO::DKW12, DKKA, true, sm + L::KR, true, C, KD, C, false);
-      umma::gemm_t(tb + CO::DKW12, DQKA, true, sm + L::QR, true, C, KD, RC, true);
-      if (p.lam) {
+    if (issuer) {
+      if (warp == 0) {
+        umma::gemm_t(tb + CO::DKR1, DKKA, false, sm + L::KW, true, C, KD, C, false);
+      } else if (warp == 1) {
+        umma::gemm_t(tb + CO::DQR1, DQKA, false, sm + L::KW, true, RC, KD, C, false);
+      } else if (warp == 2) {
+        umma::gemm_t(tb + CO::DKW12, DKKA, true, sm + L::KR, true, C, KD, C, false);
+        umma::gemm_t(tb + CO::DKW12, DQKA, true, sm + L::QR, true, C, KD, RC, true);
+      } else if (p.lam) {
         umma::gemm_t(tb + CO::DLW, DKKW, true, sm + L::KR, true, C, KD, C, false);
         umma::gemm_t(tb + CO::DLW, DQKW, true, sm + L::QR, true, C, KD, RC, true);
       }
-      umma::commit(mbar);
+      if (warp < 3 || p.lam)
+        umma::commit(mbar);
+      else
+        umma::mbar_arrive(mbar);
     }
     // the gradient rows (oldest group of this chunk); later groups hold the next chunk's data
     if (c > 0)

@@ -146,6 +146,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
   return false;
 }
 
+// plain arrive (one count) on `mbar`: an issuing thread with no MMAs in a batch signals with it
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" :: "r"(smem_u32(mbar)) : "memory");
+}
+
 // generic-proxy smem writes -> visible to the tensor core (async proxy)
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
