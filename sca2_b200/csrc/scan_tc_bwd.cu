@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     {
       const int i = frag_row<C>();
       const bool own = owns_rows<C>();
-#pragma unroll
+#pragma unroll 1  // rolled: the body is long and the backward is instruction-fetch bound
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<C, C>(q);
         float dl[16], gg[16];
@@ -624,15 +624,16 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     {
       const int row = frag_row<RC>(), i = row & 63;
       const bool own = owns_rows<RC>();
-      uint32_t udp[C / 32][16];
-#pragma unroll
-      for (int q = 0; q < C / 32; ++q) umma::ld16_issue(umma::taddr(tb + CO::DP, 32 * sub, frag_col0<RC, C>(q)), udp[q]);
-      umma::ld_wait();
-#pragma unroll
+#pragma unroll 1  // rolled: the body is long and the backward is instruction-fetch bound
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<RC, C>(q);
         float dp[16];
-        umma::take<16>(udp[q], dp);
+        {
+          uint32_t udp[16];
+          umma::ld16_issue(umma::taddr(tb + CO::DP, 32 * sub, j0), udp);
+          umma::ld_wait();
+          umma::take<16>(udp, dp);
+        }
         float dqk[16], dqw[16];
         float srow_ = 0.f;
 #pragma unroll
