@@ -24,9 +24,14 @@
 // corrected values E) it is carried as a hi + lo pair (three products hi*hi + hi*lo + lo*hi),
 // which keeps about 16 mantissa bits.  The next chunk's values are copied in with cp.async
 // (straight into the operand layout) and its phases (keys) and gates are loaded into registers
-// while the current chunk runs.  Each MMA batch is issued by one thread and completes
-// on an mbarrier whose wait is bounded: on a timeout the CTA records a fault bit, waits
-// (bounded) once more for its MMAs, frees its TMEM and returns.
+// while the current chunk runs.  The MMAs of a batch are issued by two threads (warps 0 and
+// 1, independent accumulators: a thread issues one instruction in about 50 cycles, about what
+// an M = 128, N = 64 instruction takes on the tensor core) and complete on an mbarrier whose
+// wait is bounded: on a timeout the CTA records a fault bit, waits (bounded) once more for its
+// MMAs, frees its TMEM and returns.  Os only needs the state entering the chunk, so it is
+// issued with P; when T is read back (training), U^T and Wk are issued right behind Os and
+// complete on a second mbarrier, so they run during the P epilogue and only X^T (then Op,
+// Su^T) waits on the state chain.
 //
 // Training runs save, per 64-token chunk c of the (B,H,slots,K,V) buffer: the state entering
 // the chunk in slot 2c (fp32) and, in slot 2c+1, T (bf16 C x C, operand layout) followed by
@@ -66,20 +71,28 @@ struct FwdLayout {
   static constexpr int TS = LS + al(C * LDF * 4);               //   fp32 C x LDF
   static constexpr int WS = TS + al(C * LDF * 4);               //   fp32 3 x 256
   static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(3 * 256 * 4));
-  static constexpr int SC = A0_END;
-  // scalars (floats): beta[C], Gc[C], a[C], w[C], d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD]
-  static constexpr int SC_FLOATS = 4 * C + 5 * KD;
+  // scalars (floats): beta[C], Gc[C], a[C], w[C], d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD],
+  // a of the previous chunk [C]
+  static constexpr int SC_FLOATS = 5 * C + 5 * KD;
+  // fp32 KD x VB staging of the state to save [m][v], where it fits the 227 KB opt-in limit
+  static constexpr bool STAGE = A0_END + al(KD * VB * 4) + al(SC_FLOATS * 4) + 64 <= 227 * 1024;
+  static constexpr int ST = A0_END;
+  static constexpr int SC = ST + (STAGE ? al(KD * VB * 4) : 0);
   static constexpr int MBAR = SC + al(SC_FLOATS * 4);
   static constexpr int TOTAL = MBAR + 64;  // mbarrier (8 B), TMEM base (4 B), error flag (4 B)
 };
 
-// TMEM columns: [0,128) G | P, later Op ; [128,192) U^T, later X^T ; [192, 192+KD) Wk, later
-// Su^T ; then Os
+// TMEM columns: [0,64) Op ; [64,128) P ; [128,192) G, later U^T, later X^T ; [192, 192+KD) Wk,
+// later Su^T ; then Os (two buffers when the outputs are deferred)
 template <int KD, int VB>
 struct Cols {
-  static constexpr int G = 0, P = 64, OP = 0, UT = 128, XT = 128, WK = 192, SUT = 192, OS = 192 + KD;
-  static constexpr int NEED = OS + VB;
+  // With VB = 64 the outputs of a chunk are formed while the next chunk's first MMA batch runs,
+  // so Os is double-buffered (chunk c in OS + (c & 1) VB) and nothing in that batch writes Op.
+  static constexpr bool DEFER = VB == 64;
+  static constexpr int G = 128, P = 64, OP = 0, UT = 128, XT = 128, WK = 192, SUT = 192, OS = 192 + KD;
+  static constexpr int NEED = OS + (DEFER ? 2 : 1) * VB;
   static constexpr int ALLOC = NEED <= 256 ? 256 : 512;
+  static_assert(NEED <= 512, "TMEM columns");
 };
 
 // 16-byte copy of an operand from shared to global memory (both 16-byte aligned)
@@ -109,6 +122,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   float* s_lam = s_dCm1 + KD;
   float* s_wr = s_lam + KD;
   float* s_wi = s_wr + KD;
+  float* s_aprev = s_wi + KD;
   float* LS = reinterpret_cast<float*>(sm + L::LS);
   float* TS = reinterpret_cast<float*>(sm + L::TS);
   float* WS = reinterpret_cast<float*>(sm + L::WS);
@@ -127,6 +141,12 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
+  uint64_t* mbar2 = reinterpret_cast<uint64_t*>(sm + L::MBAR + 16);  // U^T / Wk batch (training)
+  float* ST = reinterpret_cast<float*>(sm + L::ST);
+  // MMA issuers: thread 0 and thread 32 (warps 0 and 1) issue independent products in parallel;
+  // each mbar phase takes one arrival from each (a commit, or a plain arrive when it has none)
+  constexpr int NISS = 2;
+  const bool issuer = (tid & 31) == 0 && warp < NISS;
 
   // ---- set-up: per-head constants, mbarrier, TMEM
   constexpr int KH = FL == SCA2_FLAVOR_PHASE ? KD / 2 : KD;
@@ -138,7 +158,8 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     s_wi[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wi[h * KH + m] : 0.f;
   }
   if (tid == 0) {
-    umma::mbar_init(mbar, 1);
+    umma::mbar_init(mbar, NISS);
+    umma::mbar_init(mbar2, 1);
     umma::fence_mbar_init();
     *s_err = 0;
   }
@@ -147,7 +168,8 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = *s_tmem;
-  uint32_t phase = 0;
+  uint32_t phase = 0, phase2 = 0;
+  bool pending2 = false;  // a U^T / Wk batch was committed to mbar2 and not yet waited for
 
   // ---- state S^T: fp32 registers in the layout of the Su^T accumulator (M = VB, N = KD)
   constexpr int NS = KD / 2;
@@ -169,8 +191,19 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     if (sown) {
       st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q), KD), x);
       st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q) + 8, KD), x + 8);
+      if (L::STAGE && cstates && (flags & F_CS16))
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ST[(frag_col0<VB, KD>(q) + j) * VB + srow] = Sreg[16 * q + j];
     }
   }
+  // The state entering each chunk goes to slot 2c.  Staged: in ST (fp32 [m][v]), written with
+  // bulk copies (one for the whole block when VB == V, else one per row m) issued at the top of
+  // the chunk; the copies have read ST before the chunk's state update rewrites it.  Otherwise
+  // (no room for ST) with plain stores from the state registers.
+  const bool st_one = VB == V;
+  const bool stage = L::STAGE && cstates && (flags & F_CS16);
+  const bool st_issuer = stage && (st_one ? tid == 0 : tid < KD);
+  publish_smem();
   float Ureg[C / 2];
 
   auto wait_mma = [&]() -> bool {
@@ -179,6 +212,54 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     __syncthreads();
     umma::fence_after_sync();
     return *s_err == 0;
+  };
+  auto wait_mma2 = [&]() -> bool {  // on a timeout the phase stays pending for the drain
+    if (!umma::mbar_wait(mbar2, phase2)) *s_err = 1;
+    __syncthreads();
+    umma::fence_after_sync();
+    if (*s_err != 0) return false;
+    phase2 ^= 1u;
+    pending2 = false;
+    return true;
+  };
+
+  // ---- outputs O = (a / kappa) .* Os + Op of chunk cc (both accumulators share one row layout)
+  auto emit_out = [&](int cc, uint32_t os_col, const float* av) {
+    constexpr int M = R * 64;
+    const int t0o = cc * C, Clo = min(C, p.T - t0o);
+    const int sub = (tid >> 5) & 3;
+    const bool own = owns_rows<M>();
+    const int row = frag_row<M>(), r = row >> 6, i = row & 63;
+    uint32_t ra[VB / 32][16], rx[VB / 32][16];
+#pragma unroll
+    for (int q = 0; q < VB / 32; ++q) {
+      umma::ld16_issue(umma::taddr(os_col, 32 * sub, frag_col0<M, VB>(q)), ra[q]);
+      umma::ld16_issue(umma::taddr(tb + CO::OP, 32 * sub, frag_col0<M, VB>(q)), rx[q]);
+    }
+    umma::ld_wait();
+#pragma unroll
+    for (int q = 0; q < VB / 32; ++q) {
+      const int v0 = frag_col0<M, VB>(q);
+      float a[16], x[16];
+      umma::take<16>(ra[q], a);
+      umma::take<16>(rx[q], x);
+      if (own && i < Clo) {
+        const float fa = av[i] * ik;
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = fa * a[j] + x[j];
+        const int64_t off = out_off(o, b, t0o + i, h, r) + vb0 + v0;
+        if (flags & F_O_VEC) {
+          bf16* dst = reinterpret_cast<bf16*>(o.ptr) + off;
+          st8(dst, 0, y);
+          st8(dst, 8, y + 8);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (vb0 + v0 + j < V) st_io(o.ptr, off + j, y[j], p.io_dtype);
+        }
+      }
+    }
   };
 
   const int NC = (p.T + C - 1) / C;
@@ -205,8 +286,16 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     const int t0 = c * C, Cl = min(C, p.T - t0);
     // saved for the backward in slot 2c+1: T (bf16 [i][j]) then E^T (bf16 [v][j]) per value block
     uint8_t* saved = cstates ? saved_at(c) : nullptr;
-    if (cstates && sown) {
-      // state entering chunk c -> slot 2c of the (B,H,NCS,K,V) buffer
+    if (st_issuer) {
+      // state entering chunk c (staged in ST) -> slot 2c of the (B,H,NCS,K,V) buffer
+      float* cb = cstates + (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0;
+      if (st_one)
+        bulk_store(cb, ST, KD * VB * 4);
+      else
+        bulk_store(cb + (int64_t)tid * V, ST + tid * VB, VB * 4);
+      bulk_commit();
+    }
+    if (!stage && cstates && sown) {
       const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0 + srow;
 #pragma unroll
       for (int q = 0; q < KD / 32; ++q)
@@ -221,18 +310,31 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     if (p.v_times_beta) scale_values<VB>(VA, gates.beta);
     build_codes<FL, KD, R>(creg, cops, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
-    if (tid == 0) {
-      if (!prep) umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
-      umma::gemm(tb + CO::P, sm + L::QR, sm + L::KW, R * 64, 64, KD, false);
-      umma::gemm(tb + CO::P, sm + L::QR, sm + L::KWL, R * 64, 64, KD, true);
-      umma::gemm(tb + CO::P, sm + L::QRL, sm + L::KW, R * 64, 64, KD, true);
-      umma::commit(mbar);
+    if (issuer) {
+      if (warp == 0) {
+        if (!prep) umma::gemm(tb + CO::G, sm + L::KR, sm + L::KW, 64, 64, KD, false);
+        umma::gemm(tb + CO::P, sm + L::QR, sm + L::KW, R * 64, 64, KD, false);
+        umma::gemm(tb + CO::P, sm + L::QR, sm + L::KWL, R * 64, 64, KD, true);
+        umma::gemm(tb + CO::P, sm + L::QRL, sm + L::KW, R * 64, 64, KD, true);
+        umma::commit(mbar);
+      } else {
+        umma::gemm(tb + CO::OS + (CO::DEFER ? (c & 1) * VB : 0), sm + L::QR, sm + L::SB, R * 64, VB, KD, false);
+        umma::commit(mbar);
+        if (prep) {  // T is already in place: U^T and Wk run while the P epilogue does
+          umma::gemm_t(tb + CO::UT, VA, true, TB, false, VB, C, C, false);
+          umma::gemm_t(tb + CO::WK, TB, false, sm + L::ZA, true, 64, KD, C, false);
+          umma::commit(mbar2);
+        }
+      }
     }
+    pending2 = prep;
     if (c + 1 < NC) {  // next chunk's codes and gates into registers
       const int t1 = t0 + C, Cl1 = min(C, p.T - t1);
       load_code_regs<FL, KD>(p, creg, code_vec, b, h, t1, Cl1, pp);
       if (warp == 0) load_gate_regs(p, greg, b, h, t1, Cl1);
     }
+    // the previous chunk's outputs while this chunk's first batch runs
+    if (CO::DEFER && c > 0) emit_out(c - 1, tb + CO::OS + ((c - 1) & 1) * VB, s_aprev);
     if (!(ok = wait_mma())) break;
     // ---- L = beta Gr (fp32) and P (hi + lo), masked and decayed
     if (!prep) for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
@@ -244,32 +346,40 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
         LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
       }
     });
-    for_frag<R * 64, 64>(tb + CO::P, [&](int row, int j0, int, const float* x) {
-      const int i = row & 63;
-      const float gi = gates.Gc[i];
-      float y[16];
+    {
+      auto p_epi = [&](int row, int j0, int, const float* x) {
+        const int i = row & 63;
+        const float gi = gates.Gc[i];
+        float y[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
-        y[j] = jj <= i ? x[j] * ik * dg : 0.f;
-      }
-      st8_split(PB, PBL, umma::kmaj(row, j0, C), y);
-      st8_split(PB, PBL, umma::kmaj(row, j0 + 8, C), y + 8);
-    });
+        for (int j = 0; j < 16; ++j) {
+          const int jj = j0 + j;
+          const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
+          y[j] = jj <= i ? x[j] * ik * dg : 0.f;
+        }
+        st8_split(PB, PBL, umma::kmaj(row, j0, C), y);
+        st8_split(PB, PBL, umma::kmaj(row, j0 + 8, C), y + 8);
+      };
+      for_frag<R * 64, 64>(tb + CO::P, p_epi);
+    }
     if (!prep) {
       __syncthreads();
       invert_unit_lower(LS, TS, WS);
       store_T<false>(TS, TB);
+      publish_smem();
+      if (cstates && blockIdx.y == 0) copy_out(saved, TB, C * C * 2);
+      if (issuer) {
+        if (warp == 0)
+          umma::gemm_t(tb + CO::UT, VA, true, TB, false, VB, C, C, false);
+        else
+          umma::gemm_t(tb + CO::WK, TB, false, sm + L::ZA, true, 64, KD, C, false);
+        umma::commit(mbar);
+      }
+      if (!(ok = wait_mma())) break;
+    } else {
+      // (the P stores reach the async proxy with the publish before the product that reads them)
+      if (!(ok = wait_mma2())) break;
     }
-    publish_smem();
-    if (!prep && cstates && blockIdx.y == 0) copy_out(saved, TB, C * C * 2);
-    if (tid == 0) {
-      umma::gemm_t(tb + CO::UT, VA, true, TB, false, VB, C, C, false);
-      umma::gemm_t(tb + CO::WK, TB, false, sm + L::ZA, true, 64, KD, C, false);
-      umma::commit(mbar);
-    }
-    if (!(ok = wait_mma())) break;
     if (c + 1 < NC) {  // VA and TB are free: next chunk's values (and T)
       const int t1 = t0 + C;
       pf_values<VB>(p, VA, flags & F_V_VEC, b, h, t1, min(C, p.T - t1), vb0);
@@ -287,10 +397,13 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       st8(WK, umma::kmaj(i, m0 + 8, KD), x + 8);
     });
     publish_smem();
-    if (tid == 0) {
-      umma::gemm(tb + CO::XT, sm + L::SB, sm + L::WK, VB, C, KD, false);
-      umma::gemm(tb + CO::OS, sm + L::QR, sm + L::SB, R * 64, VB, KD, false);
-      umma::commit(mbar);
+    if (issuer) {
+      if (warp == 0) {
+        umma::gemm(tb + CO::XT, sm + L::SB, sm + L::WK, VB, C, KD, false);
+        umma::commit(mbar);
+      } else {
+        umma::mbar_arrive(mbar);
+      }
     }
     if (!(ok = wait_mma())) break;
     for_frag<VB, C>(tb + CO::XT, [&](int v, int i0, int q, const float* x) {
@@ -302,16 +415,21 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     });
     publish_smem();
     if (cstates) copy_out(saved + C * C * 2 + blockIdx.y * (VB * C * 2), EB, VB * C * 2);
-    if (tid == 0) {
-      umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EB, R * 64, VB, C, false);
-      umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EBL, R * 64, VB, C, true);
-      umma::gemm(tb + CO::OP, sm + L::PBL, sm + L::EB, R * 64, VB, C, true);
-      umma::gemm_t(tb + CO::SUT, EB, false, sm + L::KWW, true, VB, KD, C, false);
-      umma::gemm_t(tb + CO::SUT, EBL, false, sm + L::KWW, true, VB, KD, C, true);
+    if (issuer) {
+      if (warp == 0) {
+        umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EB, R * 64, VB, C, false);
+        umma::gemm(tb + CO::OP, sm + L::PB, sm + L::EBL, R * 64, VB, C, true);
+        umma::gemm(tb + CO::OP, sm + L::PBL, sm + L::EB, R * 64, VB, C, true);
+      } else {
+        umma::gemm_t(tb + CO::SUT, EB, false, sm + L::KWW, true, VB, KD, C, false);
+        umma::gemm_t(tb + CO::SUT, EBL, false, sm + L::KWW, true, VB, KD, C, true);
+      }
       umma::commit(mbar);
     }
+    if (st_issuer) bulk_wait_read();  // ST is rewritten by the state update below
     if (!(ok = wait_mma())) break;
     // ---- state update
+    if (CO::DEFER && tid < C) s_aprev[tid] = gates.a[tid];
     const float aC = gates.a[Cl - 1];
     for_frag<VB, KD>(tb + CO::SUT, [&](int v, int m0, int q, const float* x) {
       float y[16];
@@ -324,47 +442,16 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       }
       st8(SB, umma::kmaj(v, m0, KD), y);
       st8(SB, umma::kmaj(v, m0 + 8, KD), y + 8);
+      if (stage && c + 1 < NC)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ST[(m0 + j) * VB + v] = Sreg[16 * q + j];
     });
-    // ---- outputs O = (a / kappa) .* Os + Op (both accumulators share one row layout)
-    {
-      constexpr int M = R * 64;
-      const int sub = (tid >> 5) & 3;
-      const bool own = owns_rows<M>();
-      const int row = frag_row<M>(), r = row >> 6, i = row & 63;
-      uint32_t ra[VB / 32][16], rx[VB / 32][16];
-#pragma unroll
-      for (int q = 0; q < VB / 32; ++q) {
-        umma::ld16_issue(umma::taddr(tb + CO::OS, 32 * sub, frag_col0<M, VB>(q)), ra[q]);
-        umma::ld16_issue(umma::taddr(tb + CO::OP, 32 * sub, frag_col0<M, VB>(q)), rx[q]);
-      }
-      umma::ld_wait();
-#pragma unroll
-      for (int q = 0; q < VB / 32; ++q) {
-        const int v0 = frag_col0<M, VB>(q);
-        float a[16], x[16];
-        umma::take<16>(ra[q], a);
-        umma::take<16>(rx[q], x);
-        if (own && i < Cl) {
-          const float fa = gates.a[i] * ik;
-          float y[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) y[j] = fa * a[j] + x[j];
-          const int64_t off = out_off(o, b, t0 + i, h, r) + vb0 + v0;
-          if (flags & F_O_VEC) {
-            bf16* dst = reinterpret_cast<bf16*>(o.ptr) + off;
-            st8(dst, 0, y);
-            st8(dst, 8, y + 8);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (vb0 + v0 + j < V) st_io(o.ptr, off + j, y[j], p.io_dtype);
-          }
-        }
-      }
-    }
+    if (!CO::DEFER) emit_out(c, tb + CO::OS, gates.a);
     publish_smem();
   }
+  if (CO::DEFER && ok && NC > 0) emit_out(NC - 1, tb + CO::OS + ((NC - 1) & 1) * VB, s_aprev);
   cp_wait_all();
+  if (st_issuer) bulk_wait_all();
   if (ok && S_final && sown) {
 #pragma unroll
     for (int q = 0; q < KD / 32; ++q)
@@ -373,7 +460,9 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   }
   if (!ok) {
     if (tid == 0) atomicOr(&g_fault, 1u);
-    umma::mbar_wait(mbar, phase ^ 1u);  // bounded: let any MMA still in flight drain
+    // bounded: let any MMA still in flight drain
+    umma::mbar_wait(mbar, phase ^ 1u);
+    if (pending2) umma::mbar_wait(mbar2, phase2);
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -436,6 +525,7 @@ cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, floa
                         float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp) {
   const bool ph = p.flavor == SCA2_FLAVOR_PHASE;
   int fl = tc_flags(p, o);
+  if (cstates && ((uintptr_t)cstates & 15u) == 0) fl |= tc::F_CS16;
   if (cstates && p.K == 64) {  // training: T of every chunk from the chunk-parallel kernel
     cudaError_t e = tc_scan_prep(p, cstates, NCS, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), pp, st);
     if (e != cudaSuccess) return e;

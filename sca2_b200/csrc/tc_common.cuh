@@ -16,7 +16,8 @@ using bf16 = __nv_bfloat16;
 
 // launch flags (host-computed, uniform)
 // F_PREP: T of every chunk was written to slot 2c+1 by the preparation kernel
-enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8, F_PREP = 16 };
+// F_CS16: the chunk-state buffer is 16-byte aligned (bulk copies may write it)
+enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8, F_PREP = 16, F_CS16 = 32 };
 
 // ---- bf16 vector stores -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -108,6 +109,18 @@ __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;
 // wait until at most N of this thread's most recent commit groups are still pending
 template <int N>
 __device__ __forceinline__ void cp_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// ---- bulk shared -> global copies (one thread; 16-byte aligned addresses, size a multiple of 16)
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t nbytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(umma::smem_u32(src)), "r"(nbytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the sources of this thread's bulk copies have been read (the shared memory may be rewritten)
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's bulk copies are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- warp transpose-reduce --------------------------------------------------------------------
 // Every lane holds N values (N = 8 or 16); returns, in lane l, the sum over all 32 lanes of value
