@@ -71,9 +71,9 @@ struct FwdLayout {
   static constexpr int TS = LS + al(C * LDF * 4);               //   fp32 C x LDF
   static constexpr int WS = TS + al(C * LDF * 4);               //   fp32 3 x 256
   static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(3 * 256 * 4));
-  // scalars (floats): beta[C], Gc[C], a[C], w[C], d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD],
-  // a of the previous chunk [C]
-  static constexpr int SC_FLOATS = 5 * C + 5 * KD;
+  // scalars (floats): two sets of gates beta[C], Gc[C], a[C], w[C] (this chunk, next chunk),
+  // d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD], a of the previous chunk [C]
+  static constexpr int SC_FLOATS = 9 * C + 5 * KD;
   // fp32 KD x VB staging of the state to save [m][v], where it fits the 227 KB opt-in limit
   static constexpr bool STAGE = A0_END + al(KD * VB * 4) + al(SC_FLOATS * 4) + 64 <= 227 * 1024;
   static constexpr int ST = A0_END;
@@ -116,8 +116,12 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   const float kappa = FL == SCA2_FLAVOR_PHASE ? (float)(KD / 2) : 1.f;
   const float ik = 1.f / kappa;
   float* sc = reinterpret_cast<float*>(sm + L::SC);
-  Gates gates{sc, sc + C, sc + 2 * C, sc + 3 * C};
-  float* s_d1 = sc + 4 * C;
+  // gates of chunk c in set c & 1: the next chunk's are formed while this one runs
+  auto gset = [&](int k) -> Gates {
+    float* g0 = sc + 4 * C * (k & 1);
+    return Gates{g0, g0 + C, g0 + 2 * C, g0 + 3 * C};
+  };
+  float* s_d1 = sc + 8 * C;
   float* s_dCm1 = s_d1 + KD;
   float* s_lam = s_dCm1 + KD;
   float* s_wr = s_lam + KD;
@@ -279,8 +283,15 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       for (int u = tid * 16; u < C * C * 2; u += NT * 16) cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(0) + u, true);
     cp_commit();
     load_code_regs<FL, KD>(p, creg, code_vec, b, h, 0, Cl0, pp);
-    if (warp == 0) load_gate_regs(p, greg, b, h, 0, Cl0);
+    if (warp == 0) {
+      load_gate_regs(p, greg, b, h, 0, Cl0);
+      gates_from_regs(greg, gset(0), Cl0);
+    }
+    __syncthreads();
+    build_codes<FL, KD, R>(creg, cops, gset(0), s_lam, s_wr, s_wi, p.q_scale, Cl0, ik, !prep);
   }
+  // Per chunk c: the codes of chunk c (but KWW) and its gates were formed while chunk c - 1's
+  // last MMA batches ran (nothing in flight then reads them); KWW = w KW is formed at the top.
   bool ok = true;
   for (int c = 0; c < NC && ok; ++c) {
     const int t0 = c * C, Cl = min(C, p.T - t0);
@@ -303,12 +314,14 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
         for (int j = 0; j < 16; ++j) cstates[cb + (int64_t)(frag_col0<VB, KD>(q) + j) * V] = Sreg[16 * q + j];
     }
     // ---- operands of the chunk
+    const Gates gates = gset(c);
     cp_wait_all();
-    if (warp == 0) gates_from_regs(greg, gates, Cl);
     for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * (float)(Cl - 1));
-    __syncthreads();
-    if (p.v_times_beta) scale_values<VB>(VA, gates.beta);
-    build_codes<FL, KD, R>(creg, cops, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
+    kww_from_kw<FL, KD, R>(cops, gates);
+    if (p.v_times_beta) {
+      __syncthreads();  // every thread's value copies have landed
+      scale_values<VB>(VA, gates.beta);
+    }
     publish_smem();
     if (issuer) {
       if (warp == 0) {
@@ -405,6 +418,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
         umma::mbar_arrive(mbar);
       }
     }
+    if (warp == 0 && c + 1 < NC) gates_from_regs(greg, gset(c + 1), min(C, p.T - t0 - C));
     if (!(ok = wait_mma())) break;
     for_frag<VB, C>(tb + CO::XT, [&](int v, int i0, int q, const float* x) {
       float e[16];
@@ -427,6 +441,10 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       umma::commit(mbar);
     }
     if (st_issuer) bulk_wait_read();  // ST is rewritten by the state update below
+    // the next chunk's codes (their buffers are free: only KWW is read by this batch)
+    if (c + 1 < NC)
+      build_codes<FL, KD, R>(creg, cops, gset(c + 1), s_lam, s_wr, s_wi, p.q_scale, min(C, p.T - t0 - C), ik,
+                             !prep);
     if (!(ok = wait_mma())) break;
     // ---- state update
     if (CO::DEFER && tid < C) s_aprev[tid] = gates.a[tid];

@@ -418,9 +418,11 @@ template <int FL, int KD, int R>
 struct CodeOps {
   bf16 *KR, *KW, *KWL, *QR, *QRL, *ZA, *KWW;
 };
+// Codes of one chunk from its phases (keys) and gates: KR (when kr), KW + KWL, QR + QRL, ZA.
+// KWW = w KW is formed separately (kww_from_kw), right before the chunk's first MMA batch.
 template <int FL, int KD, int R>
 __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>& op, const Gates& g, const float* s_lam,
-                            const float* s_wr, const float* s_wi, float q_scale, int Cl, float ik) {
+                            const float* s_wr, const float* s_wi, float q_scale, int Cl, float ik, bool kr) {
   const int tid = threadIdx.x;
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;
@@ -445,8 +447,10 @@ __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>
       kc[k] = c * ell; ks[k] = s * ell; wc[k] = c * elli; ws[k] = s * elli;
       q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
     }
-    st8(op.KR, umma::kmaj(i, m0, KD), kc);
-    st8(op.KR, umma::kmaj(i, Mh + m0, KD), ks);
+    if (kr) {
+      st8(op.KR, umma::kmaj(i, m0, KD), kc);
+      st8(op.KR, umma::kmaj(i, Mh + m0, KD), ks);
+    }
     st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
     st8_split(op.KW, op.KWL, umma::kmaj(i, Mh + m0, KD), ws);
     st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), q0a);
@@ -460,19 +464,13 @@ __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>
 #pragma unroll
     for (int k = 0; k < 8; ++k) t[k] = zb * ks[k];
     st8(op.ZA, umma::kmaj(i, Mh + m0, KD), t);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) t[k] = wv * wc[k];
-    st8(op.KWW, umma::kmaj(i, m0, KD), t);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) t[k] = wv * ws[k];
-    st8(op.KWW, umma::kmaj(i, Mh + m0, KD), t);
   } else {
     constexpr int MB = KD / 8, NU = CodeRegs<FL, KD>::NU;
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
       int i, m0;
       code_unit<MB>(tid + u * NT, i, m0);
-      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
+      const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik;
       float kc[8], wc[8], qc[8], t[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -480,15 +478,46 @@ __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>
         const float ell = __expf(-l * fi), elli = __expf(l * fi);
         kc[k] = cr.w[u][k] * ell; wc[k] = cr.w[u][k] * elli; qc[k] = q_scale * cr.q[u][k] * ell;
       }
-      st8(op.KR, umma::kmaj(i, m0, KD), kc);
+      if (kr) st8(op.KR, umma::kmaj(i, m0, KD), kc);
       st8_split(op.KW, op.KWL, umma::kmaj(i, m0, KD), wc);
       st8_split(op.QR, op.QRL, umma::kmaj(i, m0, KD), qc);
 #pragma unroll
       for (int k = 0; k < 8; ++k) t[k] = zb * kc[k];
       st8(op.ZA, umma::kmaj(i, m0, KD), t);
+    }
+  }
+}
+
+// KWW = w .* (KW + KWL) for the units this thread wrote in build_codes (same unit map, so no
+// barrier is needed between the two)
+__device__ __forceinline__ void ld8_bf16(const bf16* base, int idx, float* x) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(base + idx);
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) t[k] = wv * wc[k];
-      st8(op.KWW, umma::kmaj(i, m0, KD), t);
+  for (int k = 0; k < 4; ++k) {
+    x[2 * k] = __low2float(h2[k]);
+    x[2 * k + 1] = __high2float(h2[k]);
+  }
+}
+template <int FL, int KD, int R>
+__device__ void kww_from_kw(const CodeOps<FL, KD, R>& op, const Gates& g) {
+  constexpr int MB = FL == SCA2_FLAVOR_PHASE ? KD / 16 : KD / 8;
+  constexpr int NU = FL == SCA2_FLAVOR_PHASE ? 1 : CodeRegs<FL, KD>::NU;
+  constexpr int NH = FL == SCA2_FLAVOR_PHASE ? 2 : 1;  // phase: cos and sin halves
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    int i, m0;
+    code_unit<MB>(threadIdx.x + u * NT, i, m0);
+    const float wv = g.w[i];
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+      const int idx = umma::kmaj(i, hh * (KD / 2) + m0, KD);
+      float a[8], l[8];
+      ld8_bf16(op.KW, idx, a);
+      ld8_bf16(op.KWL, idx, l);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = wv * (a[k] + l[k]);
+      st8(op.KWW, idx, a);
     }
   }
 }
