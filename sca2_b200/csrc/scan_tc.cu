@@ -69,8 +69,8 @@ struct FwdLayout {
   static constexpr int QRL = KWL + al(C * KD * 2);              //   R*C x KD (lo)
   static constexpr int LS = A0;                                 //   fp32 C x LDF
   static constexpr int TS = LS + al(C * LDF * 4);               //   fp32 C x LDF
-  static constexpr int WS = TS + al(C * LDF * 4);               //   fp32 3 x 256
-  static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(3 * 256 * 4));
+  static constexpr int WS = TS + al(C * LDF * 4);               //   fp32 1024
+  static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(1024 * 4));
   // scalars (floats): two sets of gates beta[C], Gc[C], a[C], w[C] (this chunk, next chunk),
   // d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD], a of the previous chunk [C]
   static constexpr int SC_FLOATS = 9 * C + 5 * KD;

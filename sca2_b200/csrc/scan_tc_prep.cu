@@ -18,22 +18,25 @@ namespace tc {
 // bit 0: a bounded mbarrier wait of the preparation kernel timed out
 __device__ unsigned int g_fault_prep;
 
+// The codes are dead once G has been computed, so T (bf16) and the inversion's scratch WS
+// reuse their region; about 52 KB in all, four CTAs per SM.
 template <int KD>
 struct PrepLayout {
   static constexpr int al(int x) { return (x + 1023) & ~1023; }
   static constexpr int KR = 0;                     // C x KD  kr [i][m]
   static constexpr int KW = KR + al(C * KD * 2);   // C x KD  kw [i][m]
-  static constexpr int TB = KW + al(C * KD * 2);   // C x C   T  [i][j]
-  static constexpr int LS = TB + al(C * C * 2);    // fp32 C x LDF
+  static constexpr int TB = 0;                     // C x C   T  [i][j]       (after G)
+  static constexpr int WS = TB + al(C * C * 2);    // fp32 1024               (after G)
+  static constexpr int LS = KW + al(C * KD * 2);   // fp32 C x LDF
   static constexpr int TS = LS + al(C * LDF * 4);  // fp32 C x LDF
-  static constexpr int WS = TS + al(C * LDF * 4);  // fp32 3 x 256
-  static constexpr int SC = WS + al(3 * 256 * 4);  // beta, Gc, a, w [C] + lam [KD]
-  static constexpr int MBAR = SC + al((4 * C + KD) * 4);
-  static constexpr int TOTAL = MBAR + 64;
+  static constexpr int SC = TS + al(C * LDF * 4);  // beta, Gc, a, w [C] + lam [KD]
+  static constexpr int MBAR = SC + ((4 * C + KD) * 4 + 15) / 16 * 16;
+  static constexpr int TOTAL = MBAR + 16;
+  static_assert(WS + 1024 * 4 <= LS, "T and WS fit the code region");
 };
 
 template <int FL, int KD>
-__global__ void __launch_bounds__(NT, 3) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec,
+__global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec,
                                                      PhaseProj pp) {
   using L = PrepLayout<KD>;
   extern __shared__ __align__(1024) uint8_t sm[];

@@ -161,71 +161,86 @@ __device__ __forceinline__ void publish_smem() {
   umma::fence_after_sync();
 }
 
-// ---- blocked inversion of the unit lower-triangular (I + L), L strictly lower ---------------
-// T_bb = (I + L_bb)^{-1} for the four 16x16 diagonal blocks, then by block distance d:
-// T_ij = -T_ii * sum_{k=j}^{i-1} L_ik T_kj.  All fp32; TS receives the lower triangle.
+// ---- inversion of the unit lower-triangular (I + L), L strictly lower, by recursive doubling --
+// The eight 8x8 diagonal blocks are solved by forward substitution (one column per thread, zeros
+// written above the diagonal), then pairs of inverted blocks of size N = 8, 16, 32 merge into
+// blocks of 2N with the block formula of a lower-triangular inverse
+//
+//     [[A, 0], [B, D]]^{-1} = [[A^{-1}, 0], [-D^{-1} B A^{-1}, D^{-1}]]
+//
+// in two passes over all threads (W = B A^{-1}, then -D^{-1} W), each thread a 1 x 4 tile with
+// float4 shared loads and paired fp32 FMAs.  The sums skip the zero triangles: A^{-1}[k][c] = 0 for k < c and
+// D^{-1}[r][k] = 0 for k > r (beyond r's group of four the entries lie in the zero-written upper
+// triangle of an 8x8 diagonal block).  All fp32; TS receives the lower triangle; WS holds 1024
+// floats.
+// c + a * (b.x, b.y) with one paired fp32 FMA (fma.rn.f32x2, sm_100): each lane rounds like fmaf
+__device__ __forceinline__ float2 fma2_bcast(float a, float2 b, float2 c) {
+  uint64_t d;
+  const uint64_t aa = ((uint64_t)__float_as_uint(a) << 32) | __float_as_uint(a);
+  const uint64_t bb = ((uint64_t)__float_as_uint(b.y) << 32) | __float_as_uint(b.x);
+  const uint64_t cc = ((uint64_t)__float_as_uint(c.y) << 32) | __float_as_uint(c.x);
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(aa), "l"(bb), "l"(cc));
+  return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
+}
+// acc (4 lanes as two pairs) += a * b
+__device__ __forceinline__ void fma4_bcast(float a, const float4& b, float2& lo, float2& hi) {
+  lo = fma2_bcast(a, make_float2(b.x, b.y), lo);
+  hi = fma2_bcast(a, make_float2(b.z, b.w), hi);
+}
+
+template <int N>
+__device__ __forceinline__ void merge_inverse_blocks(const float* LS, float* TS, float* WS) {
+  constexpr int Q = N / 4, ITEMS = (64 / (2 * N)) * N * Q;
+  for (int e = threadIdx.x; e < ITEMS; e += blockDim.x) {  // W = L21 T11
+    const int pr = e / (N * Q), rem = e - pr * (N * Q), r = rem / Q, cq = (rem - r * Q) * 4;
+    const int base = pr * 2 * N;
+    const float* lrow = LS + (base + N + r) * LDF + base;
+    float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+    for (int k = cq; k < N; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(lrow + k);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        fma4_bcast(av[q], *reinterpret_cast<const float4*>(TS + (base + k + q) * LDF + base + cq), lo, hi);
+    }
+    *reinterpret_cast<float4*>(WS + (pr * N + r) * N + cq) = make_float4(lo.x, lo.y, hi.x, hi.y);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ITEMS; e += blockDim.x) {  // T21 = -T22 W
+    const int pr = e / (N * Q), rem = e - pr * (N * Q), r = rem / Q, cq = (rem - r * Q) * 4;
+    const int base = pr * 2 * N;
+    const float* trow = TS + (base + N + r) * LDF + base + N;
+    float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+    for (int k = 0; k <= r; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(trow + k);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        fma4_bcast(av[q], *reinterpret_cast<const float4*>(WS + (pr * N + k + q) * N + cq), lo, hi);
+    }
+    *reinterpret_cast<float4*>(TS + (base + N + r) * LDF + base + cq) = make_float4(-lo.x, -lo.y, -hi.x, -hi.y);
+  }
+  __syncthreads();
+}
 __device__ inline void invert_unit_lower(const float* LS, float* TS, float* WS) {
   const int tid = threadIdx.x;
   if (tid < 64) {
-    const int o = 16 * (tid >> 4), col = tid & 15;
-    float x[16];
+    const int o = 8 * (tid >> 3), col = tid & 7;
+    float x[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
+    for (int r = 0; r < 8; ++r) {
       float acc = (r == col) ? 1.f : 0.f;
 #pragma unroll
       for (int k = 0; k < r; ++k) acc = fmaf(-LS[(o + r) * LDF + o + k], x[k], acc);
       x[r] = (r < col) ? 0.f : acc;
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) TS[(o + r) * LDF + o + col] = x[r];
+    for (int r = 0; r < 8; ++r) TS[(o + r) * LDF + o + col] = x[r];
   }
   __syncthreads();
-  // off-diagonal blocks by distance d: each thread a 1 x 4 tile (row r, columns cq..cq+3),
-  // float4 shared loads along K and along the tile
-  for (int d = 1; d < 4; ++d) {
-    const int np = 4 - d;
-    for (int e = tid; e < np * 64; e += blockDim.x) {  // W_{bi,bj} = sum_bk L_{bi,bk} T_{bk,bj}
-      const int pr = e >> 6, r = (e >> 2) & 15, cq = (e & 3) * 4;
-      const int bi = pr + d, bj = pr;
-      const float* lrow = LS + (16 * bi + r) * LDF;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int kk = 16 * bj; kk < 16 * bi; kk += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(lrow + kk);
-        const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 bv = *reinterpret_cast<const float4*>(TS + (kk + q) * LDF + 16 * bj + cq);
-          acc.x = fmaf(av[q], bv.x, acc.x);
-          acc.y = fmaf(av[q], bv.y, acc.y);
-          acc.z = fmaf(av[q], bv.z, acc.z);
-          acc.w = fmaf(av[q], bv.w, acc.w);
-        }
-      }
-      *reinterpret_cast<float4*>(WS + (pr << 8) + (r << 4) + cq) = acc;
-    }
-    __syncthreads();
-    for (int e = tid; e < np * 64; e += blockDim.x) {  // T_{bi,bj} = -T_{bi,bi} W_{bi,bj}
-      const int pr = e >> 6, r = (e >> 2) & 15, cq = (e & 3) * 4;
-      const int bi = pr + d, bj = pr;
-      const float* trow = TS + (16 * bi + r) * LDF + 16 * bi;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int k = 0; k < 16; k += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(trow + k);
-        const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 bv = *reinterpret_cast<const float4*>(WS + (pr << 8) + ((k + q) << 4) + cq);
-          acc.x = fmaf(av[q], bv.x, acc.x);
-          acc.y = fmaf(av[q], bv.y, acc.y);
-          acc.z = fmaf(av[q], bv.z, acc.z);
-          acc.w = fmaf(av[q], bv.w, acc.w);
-        }
-      }
-      *reinterpret_cast<float4*>(TS + (16 * bi + r) * LDF + 16 * bj + cq) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
-    }
-    __syncthreads();
-  }
+  merge_inverse_blocks<8>(LS, TS, WS);
+  merge_inverse_blocks<16>(LS, TS, WS);
+  merge_inverse_blocks<32>(LS, TS, WS);
 }
 
 // TB (bf16, K-major rows i, K = j) <- lower triangle of TS; transposed = write T^T instead
