@@ -273,6 +273,10 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   CodeRegs<FL, KD> creg;
   GateRegs greg;
   const bool prep = (flags & F_PREP) && cstates;
+  // training: each chunk's P (hi part, operand layout) goes to slot 2 NC + c for the backward,
+  // one bulk copy issued by thread 32 (plain 16-byte stores when the buffer is not aligned)
+  const bool p_save = prep && blockIdx.y == 0;
+  const bool p_issuer = p_save && (flags & F_CS16) && tid == 32;
   auto saved_at = [&](int cc) -> uint8_t* {
     return reinterpret_cast<uint8_t*>(cstates + (((int64_t)b * p.H + h) * NCS + 2 * cc + 1) * KD * (int64_t)V);
   };
@@ -348,6 +352,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     }
     // the previous chunk's outputs while this chunk's first batch runs
     if (CO::DEFER && c > 0) emit_out(c - 1, tb + CO::OS + ((c - 1) & 1) * VB, s_aprev);
+    if (p_issuer) bulk_wait_read();  // the P epilogue below rewrites PB
     if (!(ok = wait_mma())) break;
     // ---- L = beta Gr (fp32) and P (hi + lo), masked and decayed
     if (!prep) for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
@@ -410,6 +415,17 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       st8(WK, umma::kmaj(i, m0 + 8, KD), x + 8);
     });
     publish_smem();
+    if (p_save) {
+      float* dst = cstates + (((int64_t)b * p.H + h) * NCS + 2 * NC + c) * KD * (int64_t)V;
+      if (flags & F_CS16) {
+        if (p_issuer) {
+          bulk_store(dst, PB, R * C * C * 2);
+          bulk_commit();
+        }
+      } else {
+        copy_out(reinterpret_cast<uint8_t*>(dst), PB, R * C * C * 2);
+      }
+    }
     if (issuer) {
       if (warp == 0) {
         umma::gemm(tb + CO::XT, sm + L::SB, sm + L::WK, VB, C, KD, false);
@@ -469,7 +485,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   }
   if (CO::DEFER && ok && NC > 0) emit_out(NC - 1, tb + CO::OS + ((NC - 1) & 1) * VB, s_aprev);
   cp_wait_all();
-  if (st_issuer) bulk_wait_all();
+  if (st_issuer || p_issuer) bulk_wait_all();
   if (ok && S_final && sown) {
 #pragma unroll
     for (int q = 0; q < KD / 32; ++q)

@@ -3,13 +3,13 @@
 // One CTA per (batch*head, block of 64 value columns); chunks of 64 tokens are walked in
 // reverse.  The forward saved, per chunk c: the state entering the chunk (slot 2c of the
 // chunk-state buffer, fp32) and, in slot 2c+1, the inverse T = (I + beta Gr)^{-1} and the
-// corrected values E = T (V' - beta a kr Sp / kappa) in bf16, already in the operand layout.
+// corrected values E = T (V' - beta a kr Sp / kappa) in bf16, already in the operand layout,
+// and in slot 2 NC + c the masked, decayed read kernel P = (QR KW^T / kappa) .* Dg (bf16).
 // With Sp = d1 .* S (state entering the chunk, decayed once) and dS the adjoint of the state
 // leaving the chunk (fp32 registers), one chunk is:
 //
-//   batch 1   G = KR KW^T, P = QR KW^T, DS0 = dO^T QRA, DQR2 = dO Sp^T,
-//             DKW3 = E dSc^T, dE = KWW dSc                        (dSc = dCm1 .* dS)
-//   batch 2   dE += P^T dO          (P masked and decayed, written by the first epilogue)
+//   batch 1   G = KR KW^T, DS0 = dO^T QRA, DQR2 = dO Sp^T, DKW3 = E dSc^T,
+//             dE = KWW dSc + P^T dO                              (dSc = dCm1 .* dS)
 //   batch 3   dY = T^T dE           (dv = dY, beta dY for the GDN write)
 //   batch 4   DL = dY E^T, DP = dO E^T, DS0 += dY^T ZN, DKR2 = dY Sp^T
 //             -> dKK = beta (-DL) .* Dg (strict), dQK = DP .* Dg (incl),
@@ -27,7 +27,7 @@
 //
 // Every product is a bf16 MMA with fp32 accumulation in TMEM.  Operands used both ways are
 // stored once, K-major, and read through MN-major descriptors for the transposed use.  The
-// next chunk's state, T, E and dO are copied in with cp.async while the current chunk runs;
+// next chunk's state, T, E, P and dO are copied in with cp.async while the current chunk runs;
 // its phases (keys) and gates are loaded into registers.  Every mbarrier wait is bounded: on a
 // timeout the CTA records a fault bit, frees its TMEM and returns.
 #include "tc_common.cuh"
@@ -53,14 +53,14 @@ struct BwdLayout {
   static constexpr int EB = TB + C * C * 2;        // VB x C   E^T (saved)    [v][j]
   static constexpr int DOA = EB + VB * C * 2;      // RC x VB  dO             [(r,i)][v]
   static constexpr int CST = DOA + RC * VB * 2;    // fp32 KD x VB staged state [m][v]
-  static constexpr int LAMS = CST + KD * VB * 4;   // fp32 KD x VB  state-side d(lam) terms [m][v]
-  static constexpr int CACHE = LAMS + KD * VB * 4; // fp32 phase: cos/sin phi, cos/sin psi [4][C][CS]
+  static constexpr int PP = CST + KD * VB * 4;     // RC x C   P (saved)      [(r,i)][j]
+  static constexpr int CACHE = PP + RC * C * 2;    // fp32 phase: cos/sin phi, cos/sin psi [4][C][CS]
                                                    //      key:   k, q * scale [2][C][CS]
   // cache row stride: 4 floats of padding put the rows of 8 consecutive tokens in distinct
   // 16-byte bank groups, so the finish's 16-byte loads (one token row per lane) do not conflict
   static constexpr int CS = (FL == SCA2_FLAVOR_PHASE ? Mh : KD) + 4;
   static constexpr int CACHE_BYTES = FL == SCA2_FLAVOR_PHASE ? 4 * C * CS * 4 : 2 * C * CS * 4;
-  static constexpr int R1 = CACHE + CACHE_BYTES;   // QRA (b1) | P (epi1-b2) | dQK (epi4-b5)
+  static constexpr int R1 = CACHE + CACHE_BYTES;   // QRA (b1) | dQK (epi4-b5)
   static constexpr int R2 = R1 + RC * 64 * 2;      // KWW (b1) | dE (epi2-b3) | dKK (epi4-b5) | PQ (finish)
   static constexpr int R3 = R2 + C * 64 * 2;       // ZN (codes-b4) | (j-i) dKK (epi4-b5)
   static constexpr int R4 = R3 + C * 64 * 2;       // Sp^T, dSc^T [v][m] (prologue-b4) | (j-i) dQK (epi4-b5)
@@ -329,9 +329,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   float* s_misc = s_dwi + KD;
   auto BF = [&](int off) { return reinterpret_cast<bf16*>(sm + off); };
   float* CST = reinterpret_cast<float*>(sm + L::CST);
-  float* LAMS = reinterpret_cast<float*>(sm + L::LAMS);
   float* cache = reinterpret_cast<float*>(sm + L::CACHE);
-  bf16* PA = BF(L::R1);
+  bf16* PA = BF(L::PP);
   bf16* DQKA = BF(L::R1);
   bf16* DEA = BF(L::R2);
   bf16* DKKA = BF(L::R2);
@@ -360,7 +359,6 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     s_dwr[m] = 0.f;
     s_dwi[m] = 0.f;
   }
-  for (int u = tid; u < KD * VB; u += NT) LAMS[u] = 0.f;
   if (tid == 0) {
     umma::mbar_init(mbar, NISS);
     umma::fence_mbar_init();
@@ -375,7 +373,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
 
   // state-layout registers (rows v of an M = 64 fragment, columns m): adjoint dS and Sp
   constexpr int NS = KD / 2;
-  float dSreg[NS], Spreg[NS];
+  float dSreg[NS], Spreg[NS], Lreg[NS];  // Lreg: state-side d(lam) terms summed over the chunks
   const int srow = frag_row<VB>();
   const bool sown = owns_rows<VB>();
   const int64_t bhKV = ((int64_t)b * p.H + h) * KD * (int64_t)V;
@@ -385,6 +383,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     for (int j = 0; j < 16; ++j) {
       const int m = frag_col0<VB, KD>(q) + j;
       dSreg[16 * q + j] = (sown && dS_final) ? dS_final[bhKV + (int64_t)m * V + vb0 + srow] : 0.f;
+      Lreg[16 * q + j] = 0.f;
     }
 
   auto wait_mma = [&]() -> bool {
@@ -398,8 +397,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   const int64_t bhs = ((int64_t)b * p.H + h) * NCS;
   auto slot = [&](int s) -> int64_t { return (bhs + s) * KD * (int64_t)V; };
   auto saved = [&](int c) -> const uint8_t* { return reinterpret_cast<const uint8_t*>(cstates + slot(2 * c + 1)); };
-
   const int NC = (p.T + C - 1) / C;
+  // the chunk's masked, decayed read kernel P as the forward formed it (slot 2 NC + c)
+  auto saved_P = [&](int c) -> const uint8_t* {
+    return reinterpret_cast<const uint8_t*>(cstates + slot(2 * NC + c));
+  };
+
   // prefetch of the last chunk
   CodeRegs<FL, KD> creg;
   GateRegs greg;
@@ -408,6 +411,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     pf_state<KD>(sm + L::CST, cstates, slot(2 * c), V, vb0);
     pf_bytes(sm + L::TB, saved(c), C * C * 2);
     pf_bytes(sm + L::EB, saved(c) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
+    pf_bytes(sm + L::PP, saved_P(c), RC * C * 2);
     pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
     cp_commit();
     load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t0, Cl, pp);
@@ -461,7 +465,6 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     if (issuer) {  // independent accumulators issued from NISS threads in parallel
       if (warp == 0) {
         umma::gemm_t(tb + CO::G, sm + L::KR, false, sm + L::KW, false, C, C, KD, false);
-        umma::gemm_t(tb + CO::P, sm + L::QR, false, sm + L::KW, false, RC, C, KD, false);
       } else if (warp == 1) {
         umma::gemm_t(tb + CO::DS0, sm + L::DOA, true, sm + L::R1, true, VB, KD, RC, false);
       } else if (warp == 2) {
@@ -469,6 +472,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         umma::gemm_t(tb + CO::DKW3, sm + L::EB, true, DSB, true, C, KD, VB, false);
       } else {
         umma::gemm_t(tb + CO::DE, sm + L::R2, false, DSB, false, C, VB, KD, false);
+        umma::gemm_t(tb + CO::DE, PA, true, sm + L::DOA, true, C, VB, RC, true);  // += P^T dO
       }
       umma::commit(mbar);
     }
@@ -479,29 +483,6 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       cp_commit();
       load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t1, C, pp);
       if (warp == 0) load_gate_regs(p, greg, b, h, t1, C);
-    }
-    if (!(ok = wait_mma())) break;
-    // ---- P masked, decayed, / kappa -> PA [(r,i)][j]
-    for_frag<RC, C>(tb + CO::P, [&](int row, int j0, int, const float* x) {
-      const int i = row & 63;
-      float y[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int jj = j0 + j;
-        y[j] = jj <= i ? x[j] * ik * Dg(i, jj) : 0.f;
-      }
-      st8(PA, umma::kmaj(row, j0, C), y);
-      st8(PA, umma::kmaj(row, j0 + 8, C), y + 8);
-    });
-    publish_smem();
-    // ================= batch 2: dE += P^T dO =================
-    if (issuer) {
-      if (warp == 0) {
-        umma::gemm_t(tb + CO::DE, PA, true, sm + L::DOA, true, C, VB, RC, true);
-        umma::commit(mbar);
-      } else {
-        umma::mbar_arrive(mbar);
-      }
     }
     if (!(ok = wait_mma())) break;
     for_frag<C, VB>(tb + CO::DE, [&](int j, int v0, int, const float* x) {
@@ -620,7 +601,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         }
       }
     }
-    // ---- dP -> dQK (+ weighted) and decay sums (P read back in place before dQK overwrites it)
+    // ---- dP -> dQK (+ weighted) and decay sums
     {
       const int row = frag_row<RC>(), i = row & 63;
       const bool own = owns_rows<RC>();
@@ -690,7 +671,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
             const float sp = Spreg[16 * q + j], ds = dSreg[16 * q + j];
             const float t = aC * s_dCm1[m] * sp * ds;
             daC += t;
-            LAMS[m * VB + srow] += -d0[j] * sp - fCl * t;
+            Lreg[16 * q + j] += -d0[j] * sp - fCl * t;
             dSreg[16 * q + j] = aC * s_dCm1[m] * s_d1[m] * ds + s_d1[m] * d0[j];
           }
         }
@@ -701,6 +682,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       }
     }
     publish_smem();
+    if (c > 0) {  // every thread is past the dP epilogue, PA's last reader: the next chunk's P
+      pf_bytes(sm + L::PP, saved_P(c - 1), RC * C * 2);
+      cp_commit();
+    }
     // ================= batch 5: DKR1, DQR1, DKW12, DLW =================
     if (issuer) {
       if (warp == 0) {
@@ -721,7 +706,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     }
     // the gradient rows (oldest group of this chunk); later groups hold the next chunk's data
     if (c > 0)
-      cp_wait_group<3>();
+      cp_wait_group<4>();
     else
       cp_wait_group<0>();
     if (!(ok = wait_mma())) break;
@@ -1048,12 +1033,17 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         for (int j = 0; j < 16; ++j)
           gr.dS0[bhKV + (int64_t)(frag_col0<VB, KD>(q) + j) * V + vb0 + srow] = dSreg[16 * q + j];
     }
-    // state-side lambda terms: sum over the value columns
-    for (int m = warp; m < KD; m += NT / 32) {
-      const float x = warp_sum(LAMS[m * VB + lane] + LAMS[m * VB + 32 + lane]);
-      if (lane == 0) s_dlam[m] += x;
+    if (p.lam) {  // state-side lambda terms: sum over the value rows (lanes of each warp)
+#pragma unroll
+      for (int q = 0; q < KD / 32; ++q) {
+        float lv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) lv[j] = sown ? Lreg[16 * q + j] : 0.f;
+        const float x = warp_transpose_sum<16>(lv);
+        if ((lane & 1) == 0) atomicAdd(&s_dlam[frag_col0<VB, KD>(q) + red_index<16>(lane)], x);
+      }
+      __syncthreads();
     }
-    __syncthreads();
     for (int m = tid; m < KD; m += NT) {
       if (gr.dlam && p.lam) atomicAdd(&gr.dlam[h * KH + (m % KH)], s_dlam[m]);
       if (FL == SCA2_FLAVOR_PHASE && m < Mh) {

@@ -28,8 +28,8 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, n), n
     assert sorted(n for n, _, _ in _lib.SIGNATURES) == names
     assert b"sm_100a" in lib.sca2_version()
-    # two saved-state slots per 64-token chunk
-    assert lib.sca2_num_chunks(4096) == 128 and lib.sca2_num_chunks(1) == 2 and lib.sca2_num_chunks(65) == 4
+    # three saved-state slots per 64-token chunk
+    assert lib.sca2_num_chunks(4096) == 192 and lib.sca2_num_chunks(1) == 3 and lib.sca2_num_chunks(65) == 6
     assert lib.sca2_num_chunks(0) == 0
 
 
