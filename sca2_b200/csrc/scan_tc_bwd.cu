@@ -68,12 +68,14 @@ struct BwdLayout {
   static constexpr int KH = FL == SCA2_FLAVOR_PHASE ? Mh : KD;
   static constexpr int GRW = R5 + C * VB * 2;      // fp32 C x KH  staged dphw / dk rows of the chunk
   static constexpr int GRQ = GRW + C * KH * 4;     // fp32 C x KH  staged dphq / dq rows
-  static constexpr int SC = GRQ + C * KH * 4;
+  static constexpr int ELL = GRQ + C * KH * 4;     // fp32 C x CS  exp(-lam_m i), chunk-independent
+  static constexpr int SC = ELL + C * CS * 4;
   // scalars (floats): beta, Gc, a, w, dbeta, da, dw, rows, cols [C]; d1, dCm1, lam, wr, wi,
-  // dlam, dwr, dwi [KD]; misc[8]
-  static constexpr int SC_FLOATS = 9 * C + 8 * KD + 8;
+  // dlam, dwr, dwi [KD]; misc[8]; a second set of beta, Gc, a, w [C] (the next chunk's)
+  static constexpr int SC_FLOATS = 13 * C + 8 * KD + 8;
   static constexpr int MBAR = SC + ((SC_FLOATS * 4 + 1023) & ~1023);
   static constexpr int TOTAL = MBAR + 64;
+  static_assert(TOTAL <= 227 * 1024, "shared memory");
   static_assert(RC * 64 * 2 >= RC * KD * 2, "R1 holds QRA");
   static_assert(2 * VB * KD * 2 >= RC * C * 2, "R4 holds the weighted dQK");
   static_assert(C * 64 * 2 >= C * Mh * 4, "R2, R3 and R5 each hold a C x Mh fp32 staging array (phase)");
@@ -144,6 +146,7 @@ __device__ __forceinline__ void pf_grad_rows(float* G, const sca2_tok& t, int b,
 template <int FL, int KD, int R>
 __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t* sm, const Gates& g, const float* s_lam,
                                              const float* s_wr, const float* s_wi, float q_scale, int Cl, float ik) {
+  const float* ELL = reinterpret_cast<const float*>(sm + BwdLayout<FL, R>::ELL);
   using L = BwdLayout<FL, R>;
   bf16* KR = reinterpret_cast<bf16*>(sm + L::KR);
   bf16* KW = reinterpret_cast<bf16*>(sm + L::KW);
@@ -161,6 +164,12 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
     const float fi = (float)i, zb = -g.beta[i] * g.a[i] * ik, fa = g.a[i] * ik, wv = g.w[i];
     float c[8], s[8], cq[8], sq[8];
     float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
+    float el[8];
+    {
+      const float4 e0 = *reinterpret_cast<const float4*>(ELL + i * L::CS + m0);
+      const float4 e1 = *reinterpret_cast<const float4*>(ELL + i * L::CS + m0 + 4);
+      el[0] = e0.x; el[1] = e0.y; el[2] = e0.z; el[3] = e0.w; el[4] = e1.x; el[5] = e1.y; el[6] = e1.z; el[7] = e1.w;
+    }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int m = m0 + k;
@@ -170,7 +179,7 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
         sincos_big(cr.q[0][k], &sq[k], &cq[k]);
       }
       const float l = s_lam[m];
-      const float ell = __expf(-l * fi), elli = __expf(l * fi);
+      const float ell = el[k], elli = __expf(l * fi);
       const float c1 = s_wr[m] * cq[k] + s_wi[m] * sq[k], c2 = s_wr[m] * sq[k] - s_wi[m] * cq[k];
       kc[k] = c[k] * ell; ks[k] = s[k] * ell; wc[k] = c[k] * elli; ws[k] = s[k] * elli;
       q0a[k] = c1 * ell; q0b[k] = c2 * ell; q1a[k] = -c2 * ell; q1b[k] = c1 * ell;
@@ -227,7 +236,7 @@ __device__ __forceinline__ void build_codes2(const CodeRegs<FL, KD>& cr, uint8_t
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const float l = s_lam[m0 + k];
-        const float ell = __expf(-l * fi), elli = __expf(l * fi);
+        const float ell = ELL[i * L::CS + m0 + k], elli = __expf(l * fi);
         kk[k] = cr.w[u][k];
         qq[k] = q_scale * cr.q[u][k];
         kc[k] = kk[k] * ell; wc[k] = kk[k] * elli; qc[k] = qq[k] * ell;
@@ -312,7 +321,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   const float kappa = FL == SCA2_FLAVOR_PHASE ? (float)Mh : 1.f;
   const float ik = 1.f / kappa;
   float* sc = reinterpret_cast<float*>(sm + L::SC);
-  Gates gates{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  // gates of chunk c in set c & 1: the next chunk's are formed while this one runs
+  auto gset = [&](int k) -> Gates {
+    float* g0 = (k & 1) ? sc + 9 * C + 8 * KD + 8 : sc;
+    return Gates{g0, g0 + C, g0 + 2 * C, g0 + 3 * C};
+  };
+  Gates gates = gset(0);
   float* s_dbeta = sc + 4 * C;
   float* s_da = sc + 5 * C;
   float* s_dw = sc + 6 * C;
@@ -330,6 +344,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   auto BF = [&](int off) { return reinterpret_cast<bf16*>(sm + off); };
   float* CST = reinterpret_cast<float*>(sm + L::CST);
   float* cache = reinterpret_cast<float*>(sm + L::CACHE);
+  float* ELL = reinterpret_cast<float*>(sm + L::ELL);
   bf16* PA = BF(L::PP);
   bf16* DQKA = BF(L::R1);
   bf16* DEA = BF(L::R2);
@@ -370,6 +385,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   umma::fence_after_sync();
   const uint32_t tb = *s_tmem;
   uint32_t phase = 0;
+  // exp(-lam_m i) for the 64 positions of a chunk (read from here by the code build and the
+  // finish; visible after the first chunk's barriers)
+  for (int u = tid; u < C * KH; u += NT) {
+    const int i = u / KH, m = u - (u / KH) * KH;
+    ELL[i * L::CS + m] = __expf(-s_lam[m] * (float)i);
+  }
 
   // state-layout registers (rows v of an M = 64 fragment, columns m): adjoint dS and Sp
   constexpr int NS = KD / 2;
@@ -415,7 +436,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
     cp_commit();
     load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t0, Cl, pp);
-    if (warp == 0) load_gate_regs(p, greg, b, h, t0, Cl);
+    if (warp == 0) {
+      load_gate_regs(p, greg, b, h, t0, Cl);
+      gates_from_regs(greg, gset(c), Cl);
+    }
   }
 
   bool ok = true;
@@ -424,7 +448,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     const float fi_last = (float)(Cl - 1);
     // ================= prologue =================
     cp_wait_all();
-    if (warp == 0) gates_from_regs(greg, gates, Cl);
+    gates = gset(c);
     for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * fi_last);
     if (tid < C) {
       s_dbeta[tid] = 0.f;
@@ -499,6 +523,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         umma::mbar_arrive(mbar);
       }
     }
+    if (warp == 0 && c > 0) gates_from_regs(greg, gset(c - 1), C);  // the next chunk's gates
     if (!(ok = wait_mma())) break;
     if (c > 0) {  // TB is free: the next chunk's T
       pf_bytes(sm + L::TB, saved(c - 1), C * C * 2);
@@ -769,7 +794,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           for (int mi = 0; mi < 2; ++mi) {
             const int e = 2 * ri + mi, m = m0 + mi;
             const float l = s_lam[m];
-            const float ell = __expf(-l * fi), elli = __expf(l * fi);
+            const float ell = ELL[i * L::CS + m], elli = __expf(l * fi);
             float dvv = 0.f;
             if constexpr (FL == SCA2_FLAVOR_PHASE) {
               const float c = mi ? c2.y : c2.x, s = mi ? s2.y : s2.x;
@@ -873,7 +898,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
               const float cq = cqp[k], sq = sqp[k];
               const float wr = s_wr[m], wi = s_wi[m];
               const float c1 = wr * cq + wi * sq, c2 = wr * sq - wi * cq;
-              const float ell = __expf(-s_lam[m] * fi);
+              const float ell = ELL[i * L::CS + m];
               const float gc = aik * q2c[k], gs = aik * q2s[k];
               const float dqc = (q1c[k] * ik + gc) * ell, dqs = (q1s[k] * ik + gs) * ell;
               const float dc1 = r ? dqs : dqc, dc2 = r ? -dqc : dqs;
@@ -930,7 +955,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int m = m0 + k;
-              const float ell = __expf(-s_lam[m] * fi);
+              const float ell = ELL[i * L::CS + m];
               const float gqs = aik * q2[k];
               dqv[k] = p.q_scale * (q1[k] * ik + gqs) * ell;
               const float gq = gqs * qp[k] * ell;
