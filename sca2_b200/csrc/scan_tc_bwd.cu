@@ -977,12 +977,13 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       if (own && has_g) atomicAdd(&s_da[i], asum);
     }
     __syncthreads();
-    // ---- key-side gradients out: 8 consecutive modes (dims) of one token per unit, coalesced
-    {
+    // ---- key-side gradients out: 8 consecutive modes (dims) of one token per unit, coalesced;
+    // warps 1..7 (warp 0 forms the per-token gradients below at the same time)
+    if (warp > 0) {
       const bool gvec = flags & B_G_VEC;
       float* dk = reinterpret_cast<float*>(const_cast<void*>(gr.dphw.ptr));
       float* dq = reinterpret_cast<float*>(const_cast<void*>(gr.dphq.ptr));
-      for (int u = tid; u < C * (KH / 8); u += NT) {
+      for (int u = tid - 32; u < C * (KH / 8); u += NT - 32) {
         const int i = u / (KH / 8), m0 = (u % (KH / 8)) * 8;
         if (i >= Cl) continue;
         float y[8], z[8];
