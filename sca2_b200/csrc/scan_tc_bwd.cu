@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     {
       const int i = frag_row<C>();
       const bool own = owns_rows<C>();
-#pragma unroll 1  // rolled: the body is long and the backward is instruction-fetch bound
+#pragma unroll
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<C, C>(q);
         float dl[16], gg[16];
@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     {
       const int row = frag_row<RC>(), i = row & 63;
       const bool own = owns_rows<RC>();
-#pragma unroll 1  // rolled: the body is long and the backward is instruction-fetch bound
+#pragma unroll
       for (int q = 0; q < C / 32; ++q) {
         const int j0 = frag_col0<RC, C>(q);
         float dp[16];
