@@ -15,7 +15,9 @@ Printed: one JSON line (rank 0) with the contract keys plus roofline (dominant k
 cpu_baseline (numpy oracle on the host cores), e2e (public API, host buffers), clocks,
 gpu_launches, a decode block (batch 256, H=16, K=V=128, 512 steps after a 4096 prefill) and an
 sp_prefill block (one 131072-token sequence, H=16, d_head=64, split over the ranks: slab maps
-all-gathered over NCCL, sequence-parallel prefill).
+all-gathered over NCCL, sequence-parallel prefill), a gdn_delta block (the delta rule in the
+gated-delta-rule form with explicit keys: B=4, T=8192, H=8, d_k=d_v=128, bf16 fwd+bwd), and the
+D-head, short-head, layer and LM blocks.
 """
 from __future__ import annotations
 
@@ -37,6 +39,8 @@ DECODE = dict(B=256, T=4096, H=16, Mh=64, V=128, steps=512)
 SP = dict(B=1, T=131072, H=16, Mh=32, V=64)  # one long sequence, split over the ranks
 DHEAD = dict(B=8, T=4096, M=16, G=8, V=64)   # D head of the reference LayerCfg (Md=16, G=8, dv=d/2)
 SHORT = dict(B=8, T=4096, L=16, dv=64, decode_B=256)  # short head, LapA default window L=16
+# delta-rule (GDN form) scan: explicit L2-normalised keys, per-token scalar decay and beta
+GDN = dict(B=4, T=8192, H=8, K=128, V=128)
 # one SCA2 layer (GatedLayer: 16 gated heads of d_head 64 + D head + mix + FFN), d_model 1024
 LAYER = dict(B=8, T=4096, d=1024, heads=16, Mh=32, dvh=64, Md=4, G=8, ff=4096)
 # 12-layer SCA2 LM training step (GatedLayer stack), d_model 768, 12 heads of d_head 64,
@@ -337,6 +341,10 @@ def run_gpu(args, rank, world, local_rank, dist):
     if not args.no_short:
         torch.cuda.empty_cache()
         sh = run_short(torch, ops, dev, rank, world, dist)
+    gd = None
+    if not args.no_gdn:
+        torch.cuda.empty_cache()
+        gd = run_gdn(torch, ops, dev, rank, world, dist)
     ly = None
     if not args.no_layer:
         torch.cuda.empty_cache()
@@ -346,7 +354,7 @@ def run_gpu(args, rank, world, local_rank, dist):
         torch.cuda.empty_cache()
         lmr = run_lm(torch, dev, rank, world, local_rank, dist)
     return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
-                decode=decode, sp=sp, dhead=dh, short=sh, layer=ly, lm=lmr)
+                decode=decode, sp=sp, dhead=dh, short=sh, gdn=gd, layer=ly, lm=lmr)
 
 
 def run_decode(torch, ops, dev, rank, world, dist):
@@ -486,6 +494,41 @@ def run_dhead(torch, ops, dev, rank, world, dist, reps=5):
     return {"value": world * B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "config": {"batch": B, "seq_len": T, "M": M, "G": G, "dv": V, "read": "separable", "fwd+bwd": True},
             "achieved_gbs": gbs, "algorithmic_bytes_per_step": (fwd_b + bwd_b) * B * T}
+
+
+def run_gdn(torch, ops, dev, rank, world, dist, reps=3):
+    """Delta-rule scan in the gated-delta-rule form (explicit keys, K = V = 128), fwd+bwd,
+    bf16 q/k/v/dO with fp32 state; q, k L2-normalised per head, beta = sigmoid(N(0,1)),
+    g = -softplus(N(0,1)).  Algorithmic bytes per token and head: fwd q, k, v (3 x 128 bf16)
+    + g, beta (2 x 4) read, o (128 bf16) written = 1,032 B; bwd dO read, inputs re-read,
+    dq, dk, dv, dg, dbeta written = 1,808 B."""
+    D = GDN
+    B, T, H, K, V = D["B"], D["T"], D["H"], D["K"], D["V"]
+    gen = torch.Generator(device=dev).manual_seed(51 + rank)
+    rn = lambda *sh: torch.randn(*sh, device=dev, generator=gen)
+    nrm = lambda x: (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    q = nrm(rn(B, T, H, K)).requires_grad_(True)
+    k = nrm(rn(B, T, H, K)).requires_grad_(True)
+    v = rn(B, T, H, V).to(torch.bfloat16).requires_grad_(True)
+    beta = torch.sigmoid(rn(B, T, H)).requires_grad_(True)
+    g = (-torch.nn.functional.softplus(rn(B, T, H))).requires_grad_(True)
+    dO = rn(B, T, H, V).to(torch.bfloat16)
+
+    def step():
+        o, _ = ops.key_scan(q, k, v, g, beta)
+        torch.autograd.backward(o, dO)
+        for t in (q, k, v, beta, g):
+            t.grad = None
+    ms = _timed(torch, dist, dev, step, reps)
+    fwd_b, bwd_b = 3 * K * 2 + 8 + V * 2, V * 2 + (3 * K * 2 + 8) + (3 * K * 2 + 8)
+    tokh = B * T * H
+    mac = FWD_MAC_TOK(K, V, R=1) * tokh
+    return {"value": world * B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "config": {"batch": B, "seq_len": T, "heads": H, "d_k": K, "d_v": V, "dtype": "bf16",
+                       "form": "gated delta rule (v_times_beta), scalar decay g", "fwd+bwd": True},
+            "achieved_gbs": (fwd_b + bwd_b) * tokh / (ms * 1e-3) / 1e9,
+            "algorithmic_bytes_per_step": (fwd_b + bwd_b) * tokh,
+            "achieved_tflops": 3 * 2 * mac / (ms * 1e-3) / 1e12}
 
 
 def _timed(torch, dist, dev, fn, reps):
@@ -733,6 +776,7 @@ def main():
     ap.add_argument("--no-short", action="store_true")
     ap.add_argument("--no-layer", action="store_true")
     ap.add_argument("--no-lm", action="store_true")
+    ap.add_argument("--no-gdn", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
@@ -839,6 +883,7 @@ def main():
         "sp_prefill": r["sp"],
         "d_head": r["dhead"],
         "short_head": r["short"],
+        "gdn_delta": r["gdn"],
         "layer": r["layer"],
         "lm_train": r["lm"],
     }
