@@ -109,7 +109,7 @@ typedef struct sca2_scan_args {
 SCA2_API int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final,
                   float* chunk_states, void* stream);
 
-/* Number of slots of the saved-state buffer for T tokens (three per 64-token chunk: the
+/* Number of slots of the saved-state buffer for T tokens (four per 64-token chunk: the
  * state entering the chunk, and the chunk's saved intermediates for the backward). */
 SCA2_API int32_t sca2_num_chunks(int32_t T);
 

@@ -48,6 +48,13 @@ cudaError_t short_bwd(const sca2_short_args& p, const float* dO, const float* dc
 bool tc_train_ok(const sca2_scan_args& p, int max_smem);
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
                         const sca2_scan_grads& gr, int NCS, cudaStream_t st, const PhaseProj& pp = PhaseProj{});
+// gdn_cp.cu
+bool cp_covers(const sca2_scan_args& p);
+cudaError_t cp_scan_fwd(const sca2_scan_args& p, sca2_out o, float* S_final, float* cstates, int NS,
+                        cudaStream_t st);
+cudaError_t cp_scan_bwd(const sca2_scan_args& p, sca2_out dO, const float* dS_final, float* cstates,
+                        const sca2_scan_grads& gr, int NS, cudaStream_t st);
+cudaError_t cp_read_faults(unsigned int* out);
 // phase_proj.cu
 size_t proj_work_floats(int B, int T, int H, int Mh);
 cudaError_t proj_bwd(int B, int T, int H, int Mh, int dtype, const float* work, const sca2_tok& kh,
@@ -129,12 +136,13 @@ const char* sca2_version(void) { return "sca2b200 0.1.0 (sm_100a)"; }
 int sca2_fault_status(uint32_t* faults) {
   if (!faults) return fail(SCA2_ERR_ARG, "null output");
   unsigned int f = 0;
-  unsigned int fb = 0, fp = 0;
+  unsigned int fb = 0, fp = 0, fc = 0;
   cudaError_t e = sca2::tc_read_faults(&f);
   if (e == cudaSuccess) e = sca2::tc_read_faults_bwd(&fb);
   if (e == cudaSuccess) e = sca2::tc_read_faults_prep(&fp);
+  if (e == cudaSuccess) e = sca2::cp_read_faults(&fc);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_fault_status");
-  *faults = f | fb | fp;
+  *faults = f | fb | fp | fc;
   return SCA2_OK;
 }
 
@@ -153,6 +161,12 @@ int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* ch
                             : cudaMemsetAsync(S_final, 0, sbytes, st);
       if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd(T=0)");
     }
+    return SCA2_OK;
+  }
+  // training of the explicit-key form at K = V = 128: chunk-parallel tensor-core path
+  if (chunk_states && sca2::cp_covers(*a)) {
+    cudaError_t e = sca2::cp_scan_fwd(*a, o, S_final, chunk_states, sca2::state_slots(a->T), st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd");
     return SCA2_OK;
   }
   // bf16 runs on the tensor cores when the shape is covered; with saved chunk states (training)
@@ -234,6 +248,17 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
     return fail(SCA2_ERR_ARG, "dphw/dk, dphq/dq and dv must be non-null");
   if (a->beta.ptr && !gr->dbeta.ptr) return fail(SCA2_ERR_ARG, "beta given but dbeta is null");
   if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
+  if (sca2::cp_covers(*a)) {  // the chunk-parallel path (its forward saved the chunk data)
+    auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
+    auto rows4 = [&](const sca2_tok& t) { return a16(t.ptr) && t.sb % 4 == 0 && t.st % 4 == 0 && t.sh % 4 == 0; };
+    if (!rows4(gr->dphw) || !rows4(gr->dphq))
+      return fail(SCA2_ERR_ARG, "dk and dq rows must be 16-byte aligned for K = V = 128 explicit-key training");
+    if (gr->overwrite && (rc = check_overwrite(a, gr))) return rc;
+    cudaError_t e = sca2::cp_scan_bwd(*a, dO, dS_final, const_cast<float*>(chunk_states), *gr,
+                                      sca2::state_slots(a->T), st);
+    if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
+    return SCA2_OK;
+  }
   const bool tc = sca2::tc_train_ok(*a, max_optin_smem());
   if (gr->overwrite) {
     if ((rc = check_overwrite(a, gr))) return rc;

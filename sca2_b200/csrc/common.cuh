@@ -27,11 +27,12 @@ __device__ __forceinline__ int64_t out_off(const sca2_out& t, int b, int tt, int
   return (int64_t)b * t.sb + (int64_t)tt * t.st + (int64_t)h * t.sh + (int64_t)r * t.sr;
 }
 
-// Slots of the saved-state buffer (B,H,slots,K,V) for T tokens: three per 64-token chunk.  The
+// Slots of the saved-state buffer (B,H,slots,K,V) for T tokens: four per 64-token chunk.  The
 // fp32 path keeps the state entering its 32-token chunk c in slot c; the tensor-core path keeps
 // the state entering its 64-token chunk c in slot 2c, its saved T and E in slot 2c+1 and its
-// masked, decayed read kernel P (bf16, operand layout) in slot 2 NC + c.
-__host__ __device__ inline int state_slots(int T) { return 3 * ((T + 63) / 64); }
+// masked, decayed read kernel P (bf16, operand layout) in slot 2 NC + c; the chunk-parallel
+// explicit-key path (K = V = 128) uses slots 4c .. 4c+3 (gdn_cp.cu).
+__host__ __device__ inline int state_slots(int T) { return 4 * ((T + 63) / 64); }
 
 // Phases formed inside the kernels from the head's projections (phase flavour): when `on`,
 // phw / phq hold K(h) / K(z) in `dtype` and phi = K(h) theta + (pos + t) omega, psi likewise,

@@ -107,7 +107,7 @@ def _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0):
 
 def _slots(T: int) -> int:
     """Saved-state slots of the chunk-state buffer (the library's sca2_num_chunks)."""
-    return 3 * ((T + 63) // 64) if T > 0 else 0
+    return 4 * ((T + 63) // 64) if T > 0 else 0
 
 
 @torch.library.custom_op("sca2b200::phase_scan_fwd", mutates_args=())

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     assert sorted(n for n, _, _ in _lib.SIGNATURES) == names
     assert b"sm_100a" in lib.sca2_version()
     # three saved-state slots per 64-token chunk
-    assert lib.sca2_num_chunks(4096) == 192 and lib.sca2_num_chunks(1) == 3 and lib.sca2_num_chunks(65) == 6
+    assert lib.sca2_num_chunks(4096) == 256 and lib.sca2_num_chunks(1) == 4 and lib.sca2_num_chunks(65) == 8
     assert lib.sca2_num_chunks(0) == 0
 
 
