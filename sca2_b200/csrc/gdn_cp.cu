@@ -26,10 +26,15 @@
 // called at lapa/benchmarks/baselines.py:111-120), regrouped so that the sequential part is
 // two small products per chunk.  Tensor-core operands are single bf16 (the state chain itself
 // stays fp32); the saved per-chunk data live in the four slots of each chunk:
-//   slot 4c    S_c (K x V)
-//   slot 4c+1  E_c (64 x V) | T (64 x 64, zeros above the diagonal)
-//   slot 4c+2  W (64 x K) | U (64 x V)        backward: Mt (64 x K) | Yo, then dY (64 x V)
-//   slot 4c+3  backward: dS' (K x V)
+//   slot 4c    S_c (K x V, fp32)
+//   slot 4c+1  E_c (64 x V, fp32) | T (64 x 64 fp32, zeros above the diagonal); the backward
+//              replaces T by [q_scale a .* q ; -beta a .* k] (128 x K bf16, operand layout)
+//   slot 4c+2  W | w .* k (64 x K bf16 each, operand layout) | U (64 x V fp32)
+//              backward: Mt (64 x K bf16, operand layout) | Yo, then dY (64 x V fp32)
+//   slot 4c+3  backward: dS' (K x V, fp32)
+// The two recurrences also run on the tensor cores: per chunk one product into TMEM for the
+// token rows (E or dY, M = 64) and one for the state rows (M = 128); the state and its adjoint
+// stay in fp32 registers (one key row per thread) and enter the products as hi + lo bf16 pairs.
 #include "tc_common.cuh"
 
 namespace sca2 {
@@ -44,6 +49,8 @@ using tc::bf16;
 constexpr int KD = 128, VD = 128, KV = KD * VD;
 constexpr int VB = 32;  // value columns per CTA of the sequential passes
 constexpr int OFF_T = C * VD, OFF_U = C * KD;
+constexpr int OFF_KW = C * KD / 2;  // floats: w .* k (bf16) after W (bf16) in slot 4c+2
+constexpr int OFF_A2 = C * VD;      // floats: the stacked backward operand in slot 4c+1
 
 // bit 0: a bounded mbarrier wait of a chunk-parallel kernel timed out
 __device__ unsigned int g_fault_cp;
@@ -113,12 +120,13 @@ __device__ __forceinline__ void unpack8(const bf16* p, float* x) {
 }
 
 // bounded wait on the batch mbarrier; on timeout the fault word is set and false returned
+// (the result is the same in every thread of the CTA)
 __device__ __forceinline__ bool batch_wait(uint64_t* mbar, uint32_t parity) {
   const bool ok = umma::mbar_wait(mbar, parity);
-  __syncthreads();
+  const bool bad = __syncthreads_or(!ok) != 0;
   umma::fence_after_sync();
-  if (!ok && threadIdx.x == 0) atomicOr(&g_fault_cp, 1u);
-  return ok;
+  if (bad && threadIdx.x == 0) atomicOr(&g_fault_cp, 1u);
+  return !bad;
 }
 
 __device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates& g, int b, int h, int t0, int Cl) {
@@ -221,11 +229,21 @@ __global__ void __launch_bounds__(NT, 2) cp_prep(sca2_scan_args p, float* cs, in
     ok = batch_wait(mbar, 1);
     if (ok) {
       float* Wg = slot(cs, bh, NS, c, 2);
+      bf16* Wb = reinterpret_cast<bf16*>(Wg);
+      bf16* KWg = reinterpret_cast<bf16*>(Wg + OFF_KW);
       tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {
-        float4* d = reinterpret_cast<float4*>(Wg + i * KD + j0);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) d[k] = make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+        tc::st8(Wb, umma::kmaj(i, j0, KD), x);
+        tc::st8(Wb, umma::kmaj(i, j0 + 8, KD), x + 8);
       });
+      for (int u = tid; u < C * KD / 8; u += NT) {  // w .* k, same layout
+        const int i = u >> 4, m0 = (u & 15) * 8;
+        float x[8];
+        unpack8(KBf + umma::kmaj(i, m0, KD), x);
+        const float wi = gt.w[i];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] *= wi;
+        tc::st8(KWg, umma::kmaj(i, m0, KD), x);
+      }
       tc::for_frag<64, 128>(tb + 128, [&](int i, int j0, int, const float* x) {
         float4* d = reinterpret_cast<float4*>(Wg + OFF_U + i * VD + j0);
 #pragma unroll
@@ -280,153 +298,160 @@ __device__ __forceinline__ void gates_from_g(const float* gbuf, float* Gc, float
   if (l == 0) *aL = expf(Gl);
 }
 
+// The state recurrence on the tensor cores, one CTA of 4 warps per (b, h, 32 value columns):
+//   E = U - W (S_hi + S_lo)         M = 64 tokens, N = 32, K = 128 keys
+//   S' = a_last S + (w .* k)^T E    M = 128 keys, N = 32, K = 64 tokens
+// Thread t keeps key row t of S (32 fp32 registers).  The next chunk's W, w .* k, U and g are
+// prefetched with cp.async while the current chunk runs.
+constexpr int NQ = 128;  // threads of the recurrence kernels
 struct StateFL {
-  static constexpr int WP = KD + 4;   // W row stride (floats)
-  static constexpr int SP = VB;       // S row stride
-  static constexpr int EP = VB + 4;   // E row stride
-  static constexpr int S = 0, E = S + KD * SP * 4, W = E + C * EP * 4, U = W + 2 * C * WP * 4,
-                       K = U + 2 * C * VB * 4, G = K + 2 * C * KD * 2, SC = G + 2 * C * 4,
-                       TOTAL = SC + (3 * C + 4) * 4;
+  static constexpr int WB = 0, KW = WB + 2 * C * KD * 2, U = KW + 2 * C * KD * 2, SH = U + 2 * C * VB * 4,
+                       SL = SH + KD * VB * 2, EB = SL + KD * VB * 2, G = EB + C * VB * 2, SC = G + 2 * C * 4,
+                       MBAR = SC + 16, TOTAL = MBAR + 16;
 };
 
-__global__ void __launch_bounds__(NT, 1) cp_state_fwd(sca2_scan_args p, float* cs, int NS, float* S_final) {
+// warp 0: exp of the chunk's summed log-decay (g = 0 past the chunk's end)
+__device__ __forceinline__ void chunk_decay(const float* gbuf, float* aL) {
+  if ((threadIdx.x >> 5) != 0) return;
+  const int l = threadIdx.x & 31;
+  const float s = warp_sum(gbuf[l] + gbuf[l + 32]);
+  if (l == 0) *aL = expf(s);
+}
+
+// 32 fp32 columns of an M = 128 accumulator row (thread t = row t; warps 0-3)
+__device__ __forceinline__ void ld_row32(uint32_t tbase, float* v) {
+  const int w = threadIdx.x >> 5;
+  uint32_t r[2][16];
+  umma::ld16_issue(umma::taddr(tbase, 32 * w, 0), r[0]);
+  umma::ld16_issue(umma::taddr(tbase, 32 * w, 16), r[1]);
+  umma::ld_wait();
+  umma::take<16>(r[0], v);
+  umma::take<16>(r[1], v + 16);
+}
+
+__global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* cs, int NS, float* S_final) {
   using L = StateFL;
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int vb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int NC = (p.T + C - 1) / C, n_base = vb * VB;
-  float* Ss = reinterpret_cast<float*>(sm + L::S);
-  float* Es = reinterpret_cast<float*>(sm + L::E);
-  float* Wb = reinterpret_cast<float*>(sm + L::W);
+  bf16* WB = reinterpret_cast<bf16*>(sm + L::WB);
+  bf16* KWB = reinterpret_cast<bf16*>(sm + L::KW);
   float* Ub = reinterpret_cast<float*>(sm + L::U);
-  bf16* Kb = reinterpret_cast<bf16*>(sm + L::K);
+  bf16* SH = reinterpret_cast<bf16*>(sm + L::SH);
+  bf16* SL = reinterpret_cast<bf16*>(sm + L::SL);
+  bf16* EB = reinterpret_cast<bf16*>(sm + L::EB);
   float* Gb = reinterpret_cast<float*>(sm + L::G);
-  float* Gc = reinterpret_cast<float*>(sm + L::SC);
-  float* av = Gc + C;
-  float* wv = av + C;
-  float* aL = wv + C;
+  float* aL = reinterpret_cast<float*>(sm + L::SC);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
 
-  // initial state
-  for (int u = tid; u < KD * VB / 4; u += NT) {
-    const int m = u / (VB / 4), n = (u % (VB / 4)) * 4;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p.S0) x = *reinterpret_cast<const float4*>(p.S0 + (int64_t)bh * KV + m * VD + n_base + n);
-    *reinterpret_cast<float4*>(Ss + m * L::SP + n) = x;
+  if (tid == 0) {
+    umma::mbar_init(mbar, 1);
+    umma::fence_mbar_init();
+  }
+  if (warp == 0) umma::tmem_alloc(s_tmem, 64);
+  // key row tid of the incoming state, and its hi / lo operand copy
+  float S[VB];
+  {
+    const float* src = p.S0 ? p.S0 + (int64_t)bh * KV + tid * VD + n_base : nullptr;
+#pragma unroll
+    for (int k = 0; k < VB; k += 4) {
+      const float4 x = src ? *reinterpret_cast<const float4*>(src + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      S[k] = x.x; S[k + 1] = x.y; S[k + 2] = x.z; S[k + 3] = x.w;
+    }
+#pragma unroll
+    for (int k = 0; k < VB; k += 8) tc::st8_split(SH, SL, umma::kmaj(tid, k, VB), S + k);
   }
   auto prefetch = [&](int c) {
     const int buf = c & 1, t0 = c * C, Cl = min(C, p.T - t0);
     const float* Wg = slot(cs, bh, NS, c, 2);
-    float* wd = Wb + buf * C * L::WP;
-    for (int u = tid; u < C * KD / 4; u += NT) {
-      const int i = u >> 5, m = (u & 31) * 4;
-      tc::cp16(wd + i * L::WP + m, Wg + i * KD + m, true);
+    const uint4* wsrc = reinterpret_cast<const uint4*>(Wg);
+    uint4* wd = reinterpret_cast<uint4*>(WB + buf * C * KD);
+    uint4* kd = reinterpret_cast<uint4*>(KWB + buf * C * KD);
+    for (int u = tid; u < C * KD / 8; u += NQ) {
+      tc::cp16(wd + u, wsrc + u, true);
+      tc::cp16(kd + u, wsrc + C * KD / 8 + u, true);
     }
     float* ud = Ub + buf * C * VB;
-    for (int u = tid; u < C * VB / 4; u += NT) {
+    for (int u = tid; u < C * VB / 4; u += NQ) {
       const int i = u >> 3, n = (u & 7) * 4;
       tc::cp16(ud + i * VB + n, Wg + OFF_U + i * VD + n_base + n, true);
-    }
-    bf16* kd = Kb + buf * C * KD;
-    const bf16* kg = reinterpret_cast<const bf16*>(p.phw.ptr);
-    for (int u = tid; u < C * KD / 8; u += NT) {
-      const int i = u >> 4, m = (u & 15) * 8;
-      const bool live = i < Cl;
-      tc::cp16(kd + i * KD + m, kg + (live ? tok_off(p.phw, b, t0 + i, h) + m : 0), live);
     }
     prefetch_gates(p, Gb + buf * C, nullptr, b, h, t0, Cl);
     tc::cp_commit();
   };
   prefetch(0);
-  // thread tiles: E (64 x 32): row i = tid / 4, columns n0..n0+7 with n0 = 8 (tid % 4);
-  //               S (128 x 32): rows m0, m0+1 with m0 = 2 (tid / 4), the same columns
-  const int ti = tid >> 2, n0 = (tid & 3) * 8, m0 = 2 * (tid >> 2);
-  for (int c = 0; c < NC; ++c) {
-    const int buf = c & 1, Cl = min(C, p.T - c * C);
-    tc::cp_wait_all();
-    __syncthreads();
-    if (c + 1 < NC) prefetch(c + 1);
-    gates_from_g(Gb + buf * C, Gc, av, wv, aL, Cl);
-    // the state entering chunk c
-    float* Sg = slot(cs, bh, NS, c, 0);
-    for (int u = tid; u < KD * VB / 4; u += NT) {
-      const int m = u / (VB / 4), n = (u % (VB / 4)) * 4;
-      *reinterpret_cast<float4*>(Sg + m * VD + n_base + n) = *reinterpret_cast<const float4*>(Ss + m * L::SP + n);
-    }
-    // E = U - W S
-    {
-      const float* Wr = Wb + buf * C * L::WP + ti * L::WP;
-      float acc[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-#pragma unroll 4
-      for (int m = 0; m < KD; m += 4) {
-        const float4 wq = *reinterpret_cast<const float4*>(Wr + m);
-        const float wk[4] = {wq.x, wq.y, wq.z, wq.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 s0 = *reinterpret_cast<const float4*>(Ss + (m + q) * L::SP + n0);
-          const float4 s1 = *reinterpret_cast<const float4*>(Ss + (m + q) * L::SP + n0 + 4);
-          acc[0] = fmaf(wk[q], s0.x, acc[0]); acc[1] = fmaf(wk[q], s0.y, acc[1]);
-          acc[2] = fmaf(wk[q], s0.z, acc[2]); acc[3] = fmaf(wk[q], s0.w, acc[3]);
-          acc[4] = fmaf(wk[q], s1.x, acc[4]); acc[5] = fmaf(wk[q], s1.y, acc[5]);
-          acc[6] = fmaf(wk[q], s1.z, acc[6]); acc[7] = fmaf(wk[q], s1.w, acc[7]);
-        }
-      }
-      const float* Ur = Ub + buf * C * VB + ti * VB + n0;
-      float e[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = Ur[k] - acc[k];
-      *reinterpret_cast<float4*>(Es + ti * L::EP + n0) = make_float4(e[0], e[1], e[2], e[3]);
-      *reinterpret_cast<float4*>(Es + ti * L::EP + n0 + 4) = make_float4(e[4], e[5], e[6], e[7]);
-      float* Eg = slot(cs, bh, NS, c, 1) + ti * VD + n_base + n0;
-      *reinterpret_cast<float4*>(Eg) = make_float4(e[0], e[1], e[2], e[3]);
-      *reinterpret_cast<float4*>(Eg + 4) = make_float4(e[4], e[5], e[6], e[7]);
-    }
-    __syncthreads();
-    // S' = a_last S + (w .* k)^T E
-    {
-      const bf16* kr = Kb + buf * C * KD + m0;
-      float acc[2][8];
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[r][k] = 0.f;
-#pragma unroll 4
-      for (int i = 0; i < C; ++i) {
-        const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162*>(kr + i * KD);
-        const float wi = wv[i];
-        const float k0 = wi * __low2float(k2), k1 = wi * __high2float(k2);
-        const float4 e0 = *reinterpret_cast<const float4*>(Es + i * L::EP + n0);
-        const float4 e1 = *reinterpret_cast<const float4*>(Es + i * L::EP + n0 + 4);
-        const float ev[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          acc[0][k] = fmaf(k0, ev[k], acc[0][k]);
-          acc[1][k] = fmaf(k1, ev[k], acc[1][k]);
-        }
-      }
-      const float al_ = *aL;
-      __syncthreads();  // every thread has read S for E
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        float* srow = Ss + (m0 + r) * L::SP + n0;
-        float4 x0 = *reinterpret_cast<float4*>(srow), x1 = *reinterpret_cast<float4*>(srow + 4);
-        x0.x = fmaf(al_, x0.x, acc[r][0]); x0.y = fmaf(al_, x0.y, acc[r][1]);
-        x0.z = fmaf(al_, x0.z, acc[r][2]); x0.w = fmaf(al_, x0.w, acc[r][3]);
-        x1.x = fmaf(al_, x1.x, acc[r][4]); x1.y = fmaf(al_, x1.y, acc[r][5]);
-        x1.z = fmaf(al_, x1.z, acc[r][6]); x1.w = fmaf(al_, x1.w, acc[r][7]);
-        *reinterpret_cast<float4*>(srow) = x0;
-        *reinterpret_cast<float4*>(srow + 4) = x1;
-      }
-    }
-  }
+  umma::fence_before_sync();
   __syncthreads();
-  if (S_final)
-    for (int u = tid; u < KD * VB / 4; u += NT) {
-      const int m = u / (VB / 4), n = (u % (VB / 4)) * 4;
-      *reinterpret_cast<float4*>(S_final + (int64_t)bh * KV + m * VD + n_base + n) =
-          *reinterpret_cast<const float4*>(Ss + m * L::SP + n);
+  umma::fence_after_sync();
+  const uint32_t tb = *s_tmem, tE = tb, tS = tb + 32;
+  uint32_t ph = 0;
+  bool ok = true;
+  for (int c = 0; c < NC && ok; ++c) {
+    const int buf = c & 1;
+    tc::cp_wait_all();
+    tc::publish_smem();
+    if (tid == 0) {
+      umma::gemm_t(tE, WB + buf * C * KD, false, SH, true, 64, VB, KD, false);
+      umma::gemm_t(tE, WB + buf * C * KD, false, SL, true, 64, VB, KD, true);
+      umma::commit(mbar);
     }
+    if (c + 1 < NC) prefetch(c + 1);
+    chunk_decay(Gb + buf * C, aL);
+    {  // the state entering chunk c
+      float* Sg = slot(cs, bh, NS, c, 0) + tid * VD + n_base;
+#pragma unroll
+      for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(Sg + k) = make_float4(S[k], S[k + 1], S[k + 2], S[k + 3]);
+    }
+    ok = batch_wait(mbar, ph);
+    ph ^= 1;
+    if (!ok) break;
+    {  // E rows: lanes 0-15 of warp w hold tokens 16 w .. 16 w + 15 (the loads are warp-wide)
+      uint32_t r[2][16];
+      umma::ld16_issue(umma::taddr(tE, 32 * warp, 0), r[0]);
+      umma::ld16_issue(umma::taddr(tE, 32 * warp, 16), r[1]);
+      umma::ld_wait();
+      float e[VB];
+      umma::take<16>(r[0], e);
+      umma::take<16>(r[1], e + 16);
+      const int i = 16 * warp + (lane & 15);
+      const float* ur = Ub + buf * C * VB + i * VB;
+#pragma unroll
+      for (int k = 0; k < VB; ++k) e[k] = ur[k] - e[k];
+      float* Eg = slot(cs, bh, NS, c, 1) + i * VD + n_base;
+      if (lane < 16) {
+#pragma unroll
+        for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(Eg + k) = make_float4(e[k], e[k + 1], e[k + 2], e[k + 3]);
+#pragma unroll
+        for (int k = 0; k < VB; k += 8) tc::st8(EB, umma::kmaj(i, k, VB), e + k);
+      }
+    }
+    tc::publish_smem();
+    if (tid == 0) {
+      umma::gemm_t(tS, KWB + buf * C * KD, true, EB, true, 128, VB, C, false);
+      umma::commit(mbar);
+    }
+    ok = batch_wait(mbar, ph);
+    ph ^= 1;
+    if (!ok) break;
+    float acc[VB];
+    ld_row32(tS, acc);
+    const float al_ = *aL;
+#pragma unroll
+    for (int k = 0; k < VB; ++k) S[k] = fmaf(al_, S[k], acc[k]);
+#pragma unroll
+    for (int k = 0; k < VB; k += 8) tc::st8_split(SH, SL, umma::kmaj(tid, k, VB), S + k);
+  }
+  if (ok && S_final) {
+    float* dst = S_final + (int64_t)bh * KV + tid * VD + n_base;
+#pragma unroll
+    for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(S[k], S[k + 1], S[k + 2], S[k + 3]);
+  }
+  tc::cp_wait_all();
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tb, 64);
 }
 
 // ======================================================================================
@@ -611,15 +636,26 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
     ok = batch_wait(mbar, 1);
     if (ok) {
       float* Mg = slot(cs, bh, NS, c, 2);
+      bf16* Mb = reinterpret_cast<bf16*>(Mg);
       tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {
         tc::st8(Z1, umma::kmaj(i, j0, VD), x);
         tc::st8(Z1, umma::kmaj(i, j0 + 8, VD), x + 8);
       });
       tc::for_frag<64, 128>(tb + 128, [&](int i, int j0, int, const float* x) {
-        float4* d = reinterpret_cast<float4*>(Mg + i * KD + j0);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) d[k] = make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+        tc::st8(Mb, umma::kmaj(i, j0, KD), x);
+        tc::st8(Mb, umma::kmaj(i, j0 + 8, KD), x + 8);
       });
+      // [q_scale a .* q ; -beta a .* k] (T has been read: it shares the slot)
+      bf16* A2 = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 1) + OFF_A2);
+      for (int u = tid; u < 2 * C * KD / 8; u += NT) {
+        const int r = u >> 4, m0 = (u & 15) * 8, i = r & (C - 1);
+        float x[8];
+        unpack8((r < C ? QB : KBf) + umma::kmaj(i, m0, KD), x);
+        const float f = r < C ? qs * gt.a[i] : -gt.beta[i] * gt.a[i];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] *= f;
+        tc::st8(A2, umma::kmaj(r, m0, KD), x);
+      }
       tc::publish_smem();
       if (tid == 0) {
         umma::gemm_t(tb, TB, true, Z1, true, 64, VD, C, false);  // Yo = T^T (P^T dO)
@@ -641,193 +677,168 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
 }
 
 // ======================================================================================
-//  B2: the adjoint state recurrence (reverse over chunks, 32 value columns per CTA, fp32)
+//  B2: the adjoint state recurrence on the tensor cores (reverse over chunks)
 // ======================================================================================
+//   dY = Yo + Mt (dS'_hi + dS'_lo)                                 M = 64, N = 32, K = 128
+//   dS = a_last dS' + [q_scale a .* q ; -beta a .* k]^T [dO ; dY]  M = 128, N = 32, K = 128
+//        (+ the dY lo part over the second 64 rows)
 struct StateBL {
-  static constexpr int MP = KD + 4, SP = VB, YP = VB + 4;
-  static constexpr int DS = 0, DY = DS + KD * SP * 4, DOF = DY + C * YP * 4, M = DOF + C * YP * 4,
-                       Y = M + 2 * C * MP * 4, Q = Y + 2 * C * VB * 4, K = Q + 2 * C * KD * 2,
-                       DO = K + 2 * C * KD * 2, G = DO + 2 * C * VB * 2, BT = G + 2 * C * 4, SC = BT + 2 * C * 4,
-                       TOTAL = SC + (5 * C + 4) * 4;
+  static constexpr int MB = 0, A2 = MB + 2 * C * KD * 2, Y = A2 + 2 * 2 * C * KD * 2, BS = Y + 2 * C * VB * 4,
+                       YL = BS + 2 * 2 * C * VB * 2, DH = YL + C * VB * 2, DL = DH + KD * VB * 2,
+                       G = DL + KD * VB * 2, SC = G + 2 * C * 4, MBAR = SC + 16, TOTAL = MBAR + 16;
 };
 
-__global__ void __launch_bounds__(NT, 1) cp_state_bwd(sca2_scan_args p, sca2_out dO, const float* dS_final,
+__global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                       float* cs, int NS, float* dS0, int dvec) {
   using L = StateBL;
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int vb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int NC = (p.T + C - 1) / C, n_base = vb * VB;
-  float* dSs = reinterpret_cast<float*>(sm + L::DS);
-  float* dYs = reinterpret_cast<float*>(sm + L::DY);
-  float* dOf = reinterpret_cast<float*>(sm + L::DOF);
-  float* Mb = reinterpret_cast<float*>(sm + L::M);
+  bf16* MB = reinterpret_cast<bf16*>(sm + L::MB);
+  bf16* A2 = reinterpret_cast<bf16*>(sm + L::A2);
   float* Yb = reinterpret_cast<float*>(sm + L::Y);
-  bf16* Qb = reinterpret_cast<bf16*>(sm + L::Q);
-  bf16* Kb = reinterpret_cast<bf16*>(sm + L::K);
-  bf16* DOb = reinterpret_cast<bf16*>(sm + L::DO);
+  bf16* BS = reinterpret_cast<bf16*>(sm + L::BS);  // [dO ; dY_hi] (128 x 32), two buffers
+  bf16* YL = reinterpret_cast<bf16*>(sm + L::YL);
+  bf16* DH = reinterpret_cast<bf16*>(sm + L::DH);
+  bf16* DL = reinterpret_cast<bf16*>(sm + L::DL);
   float* Gb = reinterpret_cast<float*>(sm + L::G);
-  float* Bb = reinterpret_cast<float*>(sm + L::BT);
-  float* Gc = reinterpret_cast<float*>(sm + L::SC);
-  float* av = Gc + C;
-  float* wv = av + C;
-  float* ca = wv + C;
-  float* cb = ca + C;
-  float* aL = cb + C;
-  const float qs = p.q_scale;
-  const bool has_beta = p.beta.ptr != nullptr;
+  float* aL = reinterpret_cast<float*>(sm + L::SC);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
 
-  for (int u = tid; u < KD * VB / 4; u += NT) {
-    const int m = u / (VB / 4), n = (u % (VB / 4)) * 4;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (dS_final) x = *reinterpret_cast<const float4*>(dS_final + (int64_t)bh * KV + m * VD + n_base + n);
-    *reinterpret_cast<float4*>(dSs + m * L::SP + n) = x;
+  if (tid == 0) {
+    umma::mbar_init(mbar, 1);
+    umma::fence_mbar_init();
+  }
+  if (warp == 0) umma::tmem_alloc(s_tmem, 64);
+  float D[VB];  // key row tid of the adjoint state
+  {
+    const float* src = dS_final ? dS_final + (int64_t)bh * KV + tid * VD + n_base : nullptr;
+#pragma unroll
+    for (int k = 0; k < VB; k += 4) {
+      const float4 x = src ? *reinterpret_cast<const float4*>(src + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      D[k] = x.x; D[k + 1] = x.y; D[k + 2] = x.z; D[k + 3] = x.w;
+    }
+#pragma unroll
+    for (int k = 0; k < VB; k += 8) tc::st8_split(DH, DL, umma::kmaj(tid, k, VB), D + k);
   }
   auto prefetch = [&](int c) {
     const int buf = c & 1, t0 = c * C, Cl = min(C, p.T - t0);
     const float* Mg = slot(cs, bh, NS, c, 2);
-    float* md = Mb + buf * C * L::MP;
-    for (int u = tid; u < C * KD / 4; u += NT) {
-      const int i = u >> 5, m = (u & 31) * 4;
-      tc::cp16(md + i * L::MP + m, Mg + i * KD + m, true);
+    const uint4* msrc = reinterpret_cast<const uint4*>(Mg);
+    const uint4* asrc = reinterpret_cast<const uint4*>(slot(cs, bh, NS, c, 1) + OFF_A2);
+    uint4* md = reinterpret_cast<uint4*>(MB + buf * C * KD);
+    uint4* ad = reinterpret_cast<uint4*>(A2 + buf * 2 * C * KD);
+    for (int u = tid; u < C * KD / 8; u += NQ) {
+      tc::cp16(md + u, msrc + u, true);
+      tc::cp16(ad + u, asrc + u, true);
+      tc::cp16(ad + C * KD / 8 + u, asrc + C * KD / 8 + u, true);
     }
     float* yd = Yb + buf * C * VB;
-    for (int u = tid; u < C * VB / 4; u += NT) {
+    for (int u = tid; u < C * VB / 4; u += NQ) {
       const int i = u >> 3, n = (u & 7) * 4;
       tc::cp16(yd + i * VB + n, Mg + OFF_U + i * VD + n_base + n, true);
     }
-    bf16* qd = Qb + buf * C * KD;
-    bf16* kd = Kb + buf * C * KD;
-    const bf16* qg = reinterpret_cast<const bf16*>(p.phq.ptr);
-    const bf16* kg = reinterpret_cast<const bf16*>(p.phw.ptr);
-    for (int u = tid; u < C * KD / 8; u += NT) {
-      const int i = u >> 4, m = (u & 15) * 8;
-      const bool live = i < Cl;
-      tc::cp16(qd + i * KD + m, qg + (live ? tok_off(p.phq, b, t0 + i, h) + m : 0), live);
-      tc::cp16(kd + i * KD + m, kg + (live ? tok_off(p.phw, b, t0 + i, h) + m : 0), live);
-    }
-    bf16* dd = DOb + buf * C * VB;
+    bf16* dd = BS + buf * 2 * C * VB;
     const bf16* dg = reinterpret_cast<const bf16*>(dO.ptr);
-    for (int u = tid; u < C * VB / 8; u += NT) {
+    for (int u = tid; u < C * VB / 8; u += NQ) {
       const int i = u >> 2, n = (u & 3) * 8;
       const bool live = i < Cl;
       const bf16* src = dg + (live ? out_off(dO, b, t0 + i, h, 0) + n_base + n : 0);
+      bf16* d = dd + umma::kmaj(i, n, VB);
       if (dvec) {
-        tc::cp16(dd + i * VB + n, src, live);
+        tc::cp16(d, src, live);
       } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) dd[i * VB + n + k] = live ? src[k] : __float2bfloat16_rn(0.f);
+        for (int k = 0; k < 8; ++k) d[k] = live ? src[k] : __float2bfloat16_rn(0.f);
       }
     }
-    prefetch_gates(p, Gb + buf * C, Bb + buf * C, b, h, t0, Cl);
+    prefetch_gates(p, Gb + buf * C, nullptr, b, h, t0, Cl);
     tc::cp_commit();
   };
   prefetch(NC - 1);
-  const int ti = tid >> 2, n0 = (tid & 3) * 8, m0 = 2 * (tid >> 2);
-  for (int c = NC - 1; c >= 0; --c) {
-    const int buf = c & 1, Cl = min(C, p.T - c * C);
-    tc::cp_wait_all();
-    __syncthreads();
-    if (c > 0) prefetch(c - 1);
-    gates_from_g(Gb + buf * C, Gc, av, wv, aL, Cl);
-    // dO (bf16) of this block of value columns to fp32
-    for (int u = tid; u < C * VB; u += NT) {
-      const int i = u / VB, n = u % VB;
-      dOf[i * L::YP + n] = __bfloat162float(DOb[buf * C * VB + i * VB + n]);
-    }
-    // the adjoint of the state leaving chunk c
-    float* dSg = slot(cs, bh, NS, c, 3);
-    for (int u = tid; u < KD * VB / 4; u += NT) {
-      const int m = u / (VB / 4), n = (u % (VB / 4)) * 4;
-      *reinterpret_cast<float4*>(dSg + m * VD + n_base + n) = *reinterpret_cast<const float4*>(dSs + m * L::SP + n);
-    }
-    __syncthreads();
-    if (tid < C) {
-      const float bt = has_beta ? Bb[buf * C + tid] : 0.f;
-      ca[tid] = qs * av[tid];
-      cb[tid] = -bt * av[tid];
-    }
-    // dY = Yo + Mt dS'
-    {
-      const float* Mr = Mb + buf * C * L::MP + ti * L::MP;
-      float acc[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-#pragma unroll 4
-      for (int m = 0; m < KD; m += 4) {
-        const float4 wq = *reinterpret_cast<const float4*>(Mr + m);
-        const float wk[4] = {wq.x, wq.y, wq.z, wq.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 s0 = *reinterpret_cast<const float4*>(dSs + (m + q) * L::SP + n0);
-          const float4 s1 = *reinterpret_cast<const float4*>(dSs + (m + q) * L::SP + n0 + 4);
-          acc[0] = fmaf(wk[q], s0.x, acc[0]); acc[1] = fmaf(wk[q], s0.y, acc[1]);
-          acc[2] = fmaf(wk[q], s0.z, acc[2]); acc[3] = fmaf(wk[q], s0.w, acc[3]);
-          acc[4] = fmaf(wk[q], s1.x, acc[4]); acc[5] = fmaf(wk[q], s1.y, acc[5]);
-          acc[6] = fmaf(wk[q], s1.z, acc[6]); acc[7] = fmaf(wk[q], s1.w, acc[7]);
-        }
-      }
-      const float* Yr = Yb + buf * C * VB + ti * VB + n0;
-      float y[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] = Yr[k] + acc[k];
-      *reinterpret_cast<float4*>(dYs + ti * L::YP + n0) = make_float4(y[0], y[1], y[2], y[3]);
-      *reinterpret_cast<float4*>(dYs + ti * L::YP + n0 + 4) = make_float4(y[4], y[5], y[6], y[7]);
-      float* Yg = slot(cs, bh, NS, c, 2) + OFF_U + ti * VD + n_base + n0;
-      *reinterpret_cast<float4*>(Yg) = make_float4(y[0], y[1], y[2], y[3]);
-      *reinterpret_cast<float4*>(Yg + 4) = make_float4(y[4], y[5], y[6], y[7]);
-    }
-    __syncthreads();
-    // dS = a_last dS' + (q_scale a .* q)^T dO - (beta a .* k)^T dY
-    {
-      const bf16* qr = Qb + buf * C * KD + m0;
-      const bf16* kr = Kb + buf * C * KD + m0;
-      float acc[2][8];
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[r][k] = 0.f;
-#pragma unroll 2
-      for (int i = 0; i < C; ++i) {
-        const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(qr + i * KD);
-        const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162*>(kr + i * KD);
-        const float ci = ca[i], di = cb[i];
-        const float q0 = ci * __low2float(q2), q1 = ci * __high2float(q2);
-        const float k0 = di * __low2float(k2), k1 = di * __high2float(k2);
-        const float4 o0 = *reinterpret_cast<const float4*>(dOf + i * L::YP + n0);
-        const float4 o1 = *reinterpret_cast<const float4*>(dOf + i * L::YP + n0 + 4);
-        const float4 y0 = *reinterpret_cast<const float4*>(dYs + i * L::YP + n0);
-        const float4 y1 = *reinterpret_cast<const float4*>(dYs + i * L::YP + n0 + 4);
-        const float ov[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
-        const float yv[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          acc[0][k] = fmaf(q0, ov[k], fmaf(k0, yv[k], acc[0][k]));
-          acc[1][k] = fmaf(q1, ov[k], fmaf(k1, yv[k], acc[1][k]));
-        }
-      }
-      const float al_ = *aL;
-      __syncthreads();
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        float* srow = dSs + (m0 + r) * L::SP + n0;
-        float4 x0 = *reinterpret_cast<float4*>(srow), x1 = *reinterpret_cast<float4*>(srow + 4);
-        x0.x = fmaf(al_, x0.x, acc[r][0]); x0.y = fmaf(al_, x0.y, acc[r][1]);
-        x0.z = fmaf(al_, x0.z, acc[r][2]); x0.w = fmaf(al_, x0.w, acc[r][3]);
-        x1.x = fmaf(al_, x1.x, acc[r][4]); x1.y = fmaf(al_, x1.y, acc[r][5]);
-        x1.z = fmaf(al_, x1.z, acc[r][6]); x1.w = fmaf(al_, x1.w, acc[r][7]);
-        *reinterpret_cast<float4*>(srow) = x0;
-        *reinterpret_cast<float4*>(srow + 4) = x1;
-      }
-    }
-  }
+  umma::fence_before_sync();
   __syncthreads();
-  if (dS0)
-    for (int u = tid; u < KD * VB / 4; u += NT) {
-      const int m = u / (VB / 4), n = (u % (VB / 4)) * 4;
-      *reinterpret_cast<float4*>(dS0 + (int64_t)bh * KV + m * VD + n_base + n) =
-          *reinterpret_cast<const float4*>(dSs + m * L::SP + n);
+  umma::fence_after_sync();
+  const uint32_t tb = *s_tmem, tY = tb, tD = tb + 32;
+  uint32_t ph = 0;
+  bool ok = true;
+  for (int c = NC - 1; c >= 0 && ok; --c) {
+    const int buf = c & 1;
+    tc::cp_wait_all();
+    tc::publish_smem();
+    if (tid == 0) {
+      umma::gemm_t(tY, MB + buf * C * KD, false, DH, true, 64, VB, KD, false);
+      umma::gemm_t(tY, MB + buf * C * KD, false, DL, true, 64, VB, KD, true);
+      umma::commit(mbar);
     }
+    if (c > 0) prefetch(c - 1);
+    chunk_decay(Gb + buf * C, aL);
+    {  // the adjoint of the state leaving chunk c
+      float* dSg = slot(cs, bh, NS, c, 3) + tid * VD + n_base;
+#pragma unroll
+      for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dSg + k) = make_float4(D[k], D[k + 1], D[k + 2], D[k + 3]);
+    }
+    ok = batch_wait(mbar, ph);
+    ph ^= 1;
+    if (!ok) break;
+    {
+      uint32_t r[2][16];
+      umma::ld16_issue(umma::taddr(tY, 32 * warp, 0), r[0]);
+      umma::ld16_issue(umma::taddr(tY, 32 * warp, 16), r[1]);
+      umma::ld_wait();
+      float y[VB];
+      umma::take<16>(r[0], y);
+      umma::take<16>(r[1], y + 16);
+      const int i = 16 * warp + (lane & 15);
+      const float* yr = Yb + buf * C * VB + i * VB;
+#pragma unroll
+      for (int k = 0; k < VB; ++k) y[k] += yr[k];
+      if (lane < 16) {
+        float* Yg = slot(cs, bh, NS, c, 2) + OFF_U + i * VD + n_base;
+#pragma unroll
+        for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(Yg + k) = make_float4(y[k], y[k + 1], y[k + 2], y[k + 3]);
+#pragma unroll
+        for (int k = 0; k < VB; k += 8) {  // dY hi below dO in the stacked operand, dY lo apart
+          float hv[8], lv[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            hv[q] = __bfloat162float(__float2bfloat16_rn(y[k + q]));
+            lv[q] = y[k + q] - hv[q];
+          }
+          tc::st8(BS + buf * 2 * C * VB, umma::kmaj(C + i, k, VB), hv);
+          tc::st8(YL, umma::kmaj(i, k, VB), lv);
+        }
+      }
+    }
+    tc::publish_smem();
+    if (tid == 0) {
+      const bf16* a2 = A2 + buf * 2 * C * KD;
+      umma::gemm_t(tD, a2, true, BS + buf * 2 * C * VB, true, 128, VB, 2 * C, false);
+      umma::gemm_t(tD, a2 + umma::kmaj(C, 0, KD), true, YL, true, 128, VB, C, true);
+      umma::commit(mbar);
+    }
+    ok = batch_wait(mbar, ph);
+    ph ^= 1;
+    if (!ok) break;
+    float acc[VB];
+    ld_row32(tD, acc);
+    const float al_ = *aL;
+#pragma unroll
+    for (int k = 0; k < VB; ++k) D[k] = fmaf(al_, D[k], acc[k]);
+#pragma unroll
+    for (int k = 0; k < VB; k += 8) tc::st8_split(DH, DL, umma::kmaj(tid, k, VB), D + k);
+  }
+  if (ok && dS0) {
+    float* dst = dS0 + (int64_t)bh * KV + tid * VD + n_base;
+#pragma unroll
+    for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(D[k], D[k + 1], D[k + 2], D[k + 3]);
+  }
+  tc::cp_wait_all();
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tb, 64);
 }
 
 // ======================================================================================
@@ -1115,7 +1126,7 @@ cudaError_t cp_scan_fwd(const sca2_scan_args& p, sca2_out o, float* S_final, flo
   if ((e = set_smem(cp::cp_state_fwd, cp::StateFL::TOTAL)) != cudaSuccess) return e;
   if ((e = set_smem(cp::cp_out, cp::OutL::TOTAL)) != cudaSuccess) return e;
   cp::cp_prep<<<gc, cp::NT, cp::PrepL::TOTAL, st>>>(p, cstates, NS, 1);
-  cp::cp_state_fwd<<<gs, cp::NT, cp::StateFL::TOTAL, st>>>(p, cstates, NS, S_final);
+  cp::cp_state_fwd<<<gs, cp::NQ, cp::StateFL::TOTAL, st>>>(p, cstates, NS, S_final);
   cp::cp_out<<<gc, cp::NT, cp::OutL::TOTAL, st>>>(p, o, cstates, NS, 1, out_rows16(o) ? 1 : 0);
   return cudaGetLastError();
 }
@@ -1130,7 +1141,7 @@ cudaError_t cp_scan_bwd(const sca2_scan_args& p, sca2_out dO, const float* dS_fi
   if ((e = set_smem(cp::cp_state_bwd, cp::StateBL::TOTAL)) != cudaSuccess) return e;
   if ((e = set_smem(cp::cp_grads, cp::GradL::TOTAL)) != cudaSuccess) return e;
   cp::cp_bprep<<<gc, cp::NT, cp::BPrepL::TOTAL, st>>>(p, dO, cstates, NS, 1, dvec);
-  cp::cp_state_bwd<<<gs, cp::NT, cp::StateBL::TOTAL, st>>>(p, dO, dS_final, cstates, NS, gr.dS0, dvec);
+  cp::cp_state_bwd<<<gs, cp::NQ, cp::StateBL::TOTAL, st>>>(p, dO, dS_final, cstates, NS, gr.dS0, dvec);
   cp::cp_grads<<<gc, cp::NT, cp::GradL::TOTAL, st>>>(p, dO, cstates, NS, gr, 1, dvec);
   return cudaGetLastError();
 }

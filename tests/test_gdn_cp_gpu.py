@@ -79,17 +79,35 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("case", CASES)
-def test_cp_train_vs_oracle(case):
-    from sca2_b200 import _lib
+def test_cp_kernels_are_what_runs():
+    """Training forward (saved chunk data) and backward dispatch to the chunk-parallel kernels
+    (kernel names from the CUDA profiler; the custom ops are called on this thread)."""
     from torch.profiler import ProfilerActivity, profile
-    B, T, H, g, be, vtb, s0, ds = case
-    d = _inputs(B, T, H, seed=B * T + H, g=g, beta=be, S0=s0, dS=ds)
+
+    from sca2_b200 import ops  # noqa: F401  (registers torch.ops.sca2b200)
+    d = _inputs(1, 130, 2, seed=1)
+    t = {n: cuda(d[n], torch.bfloat16 if n in "qkv" else torch.float32) for n in ("q", "k", "v", "g", "beta")}
+    dO = cuda(d["dO"], torch.bfloat16)
+    sc = K ** -0.5
+
+    def run():
+        o, S, cs = torch.ops.sca2b200.key_scan_fwd(t["q"], t["k"], t["v"], t["g"], t["beta"], None, None, sc, True,
+                                                   True)
+        torch.ops.sca2b200.key_scan_bwd(t["q"], t["k"], t["v"], t["g"], t["beta"], None, None, sc, True, cs, dO, None)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        o, S, gr = _run(d, vtb)
+        run()
+        torch.cuda.synchronize()
     names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
     for k in ("cp_prep", "cp_state_fwd", "cp_out", "cp_bprep", "cp_state_bwd", "cp_grads"):
         assert any(k in n for n in names), (k, names)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_cp_train_vs_oracle(case):
+    from sca2_b200 import _lib
+    B, T, H, g, be, vtb, s0, ds = case
+    d = _inputs(B, T, H, seed=B * T + H, g=g, beta=be, S0=s0, dS=ds)
+    o, S, gr = _run(d, vtb)
     assert _lib.device_faults() == 0
     ro, rS, rg = _oracle(d, vtb)
     _check("o", o, ro)
