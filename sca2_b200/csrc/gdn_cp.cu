@@ -26,12 +26,13 @@
 // called at lapa/benchmarks/baselines.py:111-120), regrouped so that the sequential part is
 // two small products per chunk.  Tensor-core operands are single bf16 (the state chain itself
 // stays fp32); the saved per-chunk data live in the four slots of each chunk:
-//   slot 4c    S_c (K x V, fp32)
-//   slot 4c+1  E_c (64 x V, fp32) | T (64 x 64 fp32, zeros above the diagonal); the backward
+//   slot 4c    S_c as hi | lo (K x V bf16 each, operand layout)
+//   slot 4c+1  E_c (64 x V bf16, operand layout) | T (64 x 64 fp32, zeros above the diagonal); the backward
 //              replaces T by [q_scale a .* q ; -beta a .* k] (128 x K bf16, operand layout)
 //   slot 4c+2  W | w .* k (64 x K bf16 each, operand layout) | U (64 x V fp32)
 //              backward: Mt (64 x K bf16, operand layout) | Yo, then dY (64 x V fp32)
-//   slot 4c+3  backward: dS' (K x V, fp32)
+//   slot 4c+3  backward: dS' (K x V bf16, operand layout) | sum(S_c .* dS') per block of 32 value
+//              columns (fp32, from the fp32 adjoint and the hi + lo state)
 // The two recurrences also run on the tensor cores: per chunk one product into TMEM for the
 // token rows (E or dY, M = 64) and one for the state rows (M = 128); the state and its adjoint
 // stay in fp32 registers (one key row per thread) and enter the products as hi + lo bf16 pairs.
@@ -51,6 +52,7 @@ constexpr int VB = 32;  // value columns per CTA of the sequential passes
 constexpr int OFF_T = C * VD, OFF_U = C * KD;
 constexpr int OFF_KW = C * KD / 2;  // floats: w .* k (bf16) after W (bf16) in slot 4c+2
 constexpr int OFF_A2 = C * VD;      // floats: the stacked backward operand in slot 4c+1
+constexpr int OFF_LO = KD * VD / 2; // floats: the state's lo part in slot 4c; the S .* dS' partial sums in 4c+3
 
 // bit 0: a bounded mbarrier wait of a chunk-parallel kernel timed out
 __device__ unsigned int g_fault_cp;
@@ -78,20 +80,6 @@ __device__ __forceinline__ void load_rows(bf16* dst, const bf16* base, int64_t s
   }
 }
 
-// R x 128 fp32 rows (row-major, 16-byte aligned) into a K-major bf16 operand, rows scaled by
-// scale(r); returns nothing
-template <class F>
-__device__ __forceinline__ void f32_rows_to_op(bf16* dst, const float* src, int R, F scale) {
-  for (int u = threadIdx.x; u < R * 16; u += NT) {
-    const int r = (u & 7) + 8 * (u >> 7), c0 = ((u >> 3) & 15) * 8;
-    const float4 x0 = *reinterpret_cast<const float4*>(src + r * 128 + c0);
-    const float4 x1 = *reinterpret_cast<const float4*>(src + r * 128 + c0 + 4);
-    const float s = scale(r);
-    float x[8] = {s * x0.x, s * x0.y, s * x0.z, s * x0.w, s * x1.x, s * x1.y, s * x1.z, s * x1.w};
-    tc::st8(dst, umma::kmaj(r, c0, 128), x);
-  }
-}
-
 // M = 64 accumulators read together: NA bases, N columns; f(row, col0, v[NA][16]) on lanes < 16
 template <int N, int NA, class F>
 __device__ __forceinline__ void frag_multi(const uint32_t* tb, F f) {
@@ -110,6 +98,14 @@ __device__ __forceinline__ void frag_multi(const uint32_t* tb, F f) {
     for (int a = 0; a < NA; ++a) umma::take<16>(r[a], v[a]);
     if (own) f(row, col0, v);
   }
+}
+
+// nbytes (a multiple of 16 * NTHR) from global to shared, 16-byte async copies
+template <int NTHR>
+__device__ __forceinline__ void flat_copy(void* dst, const void* src, int nbytes) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  const uint4* g = reinterpret_cast<const uint4*>(src);
+  for (int u = threadIdx.x; u < nbytes / 16; u += NTHR) tc::cp16(d + u, g + u, true);
 }
 
 __device__ __forceinline__ void unpack8(const bf16* p, float* x) {
@@ -399,10 +395,10 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
     }
     if (c + 1 < NC) prefetch(c + 1);
     chunk_decay(Gb + buf * C, aL);
-    {  // the state entering chunk c
-      float* Sg = slot(cs, bh, NS, c, 0) + tid * VD + n_base;
+    {  // the state entering chunk c: hi (the operand of q S and dY S^T) and lo, operand layout
+      bf16* Sg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 0));
 #pragma unroll
-      for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(Sg + k) = make_float4(S[k], S[k + 1], S[k + 2], S[k + 3]);
+      for (int k = 0; k < VB; k += 8) tc::st8_split(Sg, Sg + 2 * OFF_LO, umma::kmaj(tid, n_base + k, VD), S + k);
     }
     ok = batch_wait(mbar, ph);
     ph ^= 1;
@@ -419,12 +415,13 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
       const float* ur = Ub + buf * C * VB + i * VB;
 #pragma unroll
       for (int k = 0; k < VB; ++k) e[k] = ur[k] - e[k];
-      float* Eg = slot(cs, bh, NS, c, 1) + i * VD + n_base;
+      bf16* Eg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 1));
       if (lane < 16) {
 #pragma unroll
-        for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(Eg + k) = make_float4(e[k], e[k + 1], e[k + 2], e[k + 3]);
-#pragma unroll
-        for (int k = 0; k < VB; k += 8) tc::st8(EB, umma::kmaj(i, k, VB), e + k);
+        for (int k = 0; k < VB; k += 8) {
+          tc::st8(Eg, umma::kmaj(i, n_base + k, VD), e + k);
+          tc::st8(EB, umma::kmaj(i, k, VB), e + k);
+        }
       }
     }
     tc::publish_smem();
@@ -491,9 +488,9 @@ __global__ void __launch_bounds__(NT, 2) cp_out(sca2_scan_args p, sca2_out o, co
   if (warp == 0) umma::tmem_alloc(s_tmem, 256);
   load_rows(QB, reinterpret_cast<const bf16*>(p.phq.ptr), p.phq.sb, p.phq.st, p.phq.sh, b, t0, h, Cl, vec);
   load_rows(KBf, reinterpret_cast<const bf16*>(p.phw.ptr), p.phw.sb, p.phw.st, p.phw.sh, b, t0, h, Cl, vec);
+  flat_copy<NT>(SB, slot(cs, bh, NS, c, 0), KD * VD * 2);
+  flat_copy<NT>(EB, slot(cs, bh, NS, c, 1), C * VD * 2);
   tc::cp_commit();
-  f32_rows_to_op(SB, slot(cs, bh, NS, c, 0), KD, [](int) { return 1.f; });
-  f32_rows_to_op(EB, slot(cs, bh, NS, c, 1), C, [](int) { return 1.f; });
   tc::cp_wait_all();
   tc::publish_smem();
   const uint32_t tb = *s_tmem;
@@ -685,7 +682,8 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
 struct StateBL {
   static constexpr int MB = 0, A2 = MB + 2 * C * KD * 2, Y = A2 + 2 * 2 * C * KD * 2, BS = Y + 2 * C * VB * 4,
                        YL = BS + 2 * 2 * C * VB * 2, DH = YL + C * VB * 2, DL = DH + KD * VB * 2,
-                       G = DL + KD * VB * 2, SC = G + 2 * C * 4, MBAR = SC + 16, TOTAL = MBAR + 16;
+                       SR = DL + KD * VB * 2, G = SR + 2 * 2 * KD * VB * 2, SC = G + 2 * C * 4, MBAR = SC + 32,
+                       TOTAL = MBAR + 16;
 };
 
 __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out dO, const float* dS_final,
@@ -702,8 +700,10 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
   bf16* YL = reinterpret_cast<bf16*>(sm + L::YL);
   bf16* DH = reinterpret_cast<bf16*>(sm + L::DH);
   bf16* DL = reinterpret_cast<bf16*>(sm + L::DL);
+  bf16* SR = reinterpret_cast<bf16*>(sm + L::SR);  // [buf][hi, lo][key row][32] of the state entering the chunk
   float* Gb = reinterpret_cast<float*>(sm + L::G);
   float* aL = reinterpret_cast<float*>(sm + L::SC);
+  float* red = aL + 1;
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
 
@@ -754,6 +754,15 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
         for (int k = 0; k < 8; ++k) d[k] = live ? src[k] : __float2bfloat16_rn(0.f);
       }
     }
+    {  // key row tid of the state entering the chunk, this CTA's 32 columns, hi and lo
+      const bf16* sg = reinterpret_cast<const bf16*>(slot(cs, bh, NS, c, 0));
+      bf16* sr = SR + buf * 2 * KD * VB + tid * VB;
+#pragma unroll
+      for (int k = 0; k < VB; k += 8) {
+        tc::cp16(sr + k, sg + umma::kmaj(tid, n_base + k, VD), true);
+        tc::cp16(sr + KD * VB + k, sg + 2 * OFF_LO + umma::kmaj(tid, n_base + k, VD), true);
+      }
+    }
     prefetch_gates(p, Gb + buf * C, nullptr, b, h, t0, Cl);
     tc::cp_commit();
   };
@@ -775,14 +784,27 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     }
     if (c > 0) prefetch(c - 1);
     chunk_decay(Gb + buf * C, aL);
-    {  // the adjoint of the state leaving chunk c
-      float* dSg = slot(cs, bh, NS, c, 3) + tid * VD + n_base;
+    {  // the adjoint of the state leaving chunk c (bf16, operand layout), and sum(S_c .* dS')
+      bf16* dSg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 3));
 #pragma unroll
-      for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dSg + k) = make_float4(D[k], D[k + 1], D[k + 2], D[k + 3]);
+      for (int k = 0; k < VB; k += 8) tc::st8(dSg, umma::kmaj(tid, n_base + k, VD), D + k);
+      const bf16* sr = SR + buf * 2 * KD * VB + tid * VB;
+      float sd = 0.f;
+#pragma unroll
+      for (int k = 0; k < VB; k += 8) {
+        float hi[8], lo[8];
+        unpack8(sr + k, hi);
+        unpack8(sr + KD * VB + k, lo);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sd = fmaf(D[k + q], hi[q] + lo[q], sd);
+      }
+      sd = warp_sum(sd);
+      if (lane == 0) red[warp] = sd;
     }
     ok = batch_wait(mbar, ph);
     ph ^= 1;
     if (!ok) break;
+    if (tid == 0) slot(cs, bh, NS, c, 3)[OFF_LO + vb] = red[0] + red[1] + red[2] + red[3];
     {
       uint32_t r[2][16];
       umma::ld16_issue(umma::taddr(tY, 32 * warp, 0), r[0]);
@@ -845,11 +867,11 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
 //  B3: per-token gradients of every chunk
 // ======================================================================================
 struct GradL {
-  static constexpr int DDP = C + 1;
+  static constexpr int DDP = C + 1, YFP = VD + 4;  // padded fp32 rows (dDg, dY)
   static constexpr int QB = 0, KB = QB + al(C * KD * 2), DOB = KB + al(C * KD * 2), DYB = DOB + al(C * VD * 2),
                        EB = DYB + al(C * VD * 2), SB = EB + al(C * VD * 2), DSB = SB + al(KD * VD * 2),
-                       DKK = DSB + al(KD * VD * 2), DQK = DKK + al(C * C * 2), DDG = DQK + al(C * C * 2),
-                       SC = DDG + C * DDP * 4, NSC = 4 * C + 12 * C + 16, MBAR = SC + NSC * 4,
+                       DKK = DSB + al(KD * VD * 2), DQK = DKK + al(C * C * 2), DYF = DQK + al(C * C * 2),
+                       DDG = DYF + C * YFP * 4, SC = DDG + C * DDP * 4, NSC = 4 * C + 12 * C + 16, MBAR = SC + NSC * 4,
                        TOTAL = MBAR + 16;
 };
 
@@ -871,6 +893,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   bf16* DKK = reinterpret_cast<bf16*>(sm + L::DKK);
   bf16* DQK = reinterpret_cast<bf16*>(sm + L::DQK);
   float* DDG = reinterpret_cast<float*>(sm + L::DDG);
+  float* DYF = reinterpret_cast<float*>(sm + L::DYF);
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   const Gates gt{sc, sc + C, sc + 2 * C, sc + 3 * C};
   float* rsum = sc + 4 * C;          // [2 halves][6 sums][C]: dbeta1, rowDg, rY, rE, rO, (spare)
@@ -893,31 +916,30 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   load_rows(QB, reinterpret_cast<const bf16*>(p.phq.ptr), p.phq.sb, p.phq.st, p.phq.sh, b, t0, h, Cl, vec);
   load_rows(KBf, reinterpret_cast<const bf16*>(p.phw.ptr), p.phw.sb, p.phw.st, p.phw.sh, b, t0, h, Cl, vec);
   load_rows(DOB, reinterpret_cast<const bf16*>(dO.ptr), dO.sb, dO.st, dO.sh, b, t0, h, Cl, dvec);
-  tc::cp_commit();
-  const float* Sg = slot(cs, bh, NS, c, 0);
-  const float* Eg = slot(cs, bh, NS, c, 1);
+  flat_copy<NT>(SB, slot(cs, bh, NS, c, 0), KD * VD * 2);
+  flat_copy<NT>(DSB, slot(cs, bh, NS, c, 3), KD * VD * 2);
+  flat_copy<NT>(EB, slot(cs, bh, NS, c, 1), C * VD * 2);
   const float* Yg = slot(cs, bh, NS, c, 2) + OFF_U;
-  const float* dSg = slot(cs, bh, NS, c, 3);
-  f32_rows_to_op(DYB, Yg, C, [](int) { return 1.f; });
-  f32_rows_to_op(EB, Eg, C, [](int) { return 1.f; });
-  // S and dS' with the chunk's sum of S .* dS' (the gradient of a_last through the carry)
-  float sds = 0.f;
-  for (int u = tid; u < KD * 16; u += NT) {
-    const int r = (u & 7) + 8 * (u >> 7), c0 = ((u >> 3) & 15) * 8;
-    const float4 s0 = *reinterpret_cast<const float4*>(Sg + r * VD + c0);
-    const float4 s1 = *reinterpret_cast<const float4*>(Sg + r * VD + c0 + 4);
-    const float4 d0 = *reinterpret_cast<const float4*>(dSg + r * VD + c0);
-    const float4 d1 = *reinterpret_cast<const float4*>(dSg + r * VD + c0 + 4);
-    float xs[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    float xd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) sds = fmaf(xs[k], xd[k], sds);
-    tc::st8(SB, umma::kmaj(r, c0, VD), xs);
-    tc::st8(DSB, umma::kmaj(r, c0, VD), xd);
+  for (int u = tid; u < C * VD / 4; u += NT) {  // dY (fp32) into padded rows
+    const int i = u >> 5, n = (u & 31) * 4;
+    tc::cp16(DYF + i * L::YFP + n, Yg + i * VD + n, true);
   }
-  sds = warp_sum(sds);
-  if (lane == 0) red[warp] = sds;
+  tc::cp_commit();
   tc::cp_wait_all();
+  __syncthreads();
+  // dY as an operand; the chunk's sum of S .* dS' (the gradient of a_last through the carry)
+  auto dy_to_op = [&](auto scale) {
+    for (int u = tid; u < C * 16; u += NT) {
+      const int r = (u & 7) + 8 * (u >> 7), c0 = ((u >> 3) & 15) * 8;
+      const float4 x0 = *reinterpret_cast<const float4*>(DYF + r * L::YFP + c0);
+      const float4 x1 = *reinterpret_cast<const float4*>(DYF + r * L::YFP + c0 + 4);
+      const float f = scale(r);
+      float x[8] = {f * x0.x, f * x0.y, f * x0.z, f * x0.w, f * x1.x, f * x1.y, f * x1.z, f * x1.w};
+      tc::st8(DYB, umma::kmaj(r, c0, VD), x);
+    }
+  };
+  dy_to_op([](int) { return 1.f; });
+  if (tid < VD / VB) red[tid] = slot(cs, bh, NS, c, 3)[OFF_LO + tid];
   tc::publish_smem();
   const uint32_t tb = *s_tmem;
   if (tid == 0) {
@@ -978,9 +1000,17 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
     }
     umma::fence_before_sync();
     __syncthreads();
-    // operands of the second batch: dY -> -beta a .* dY, E -> w .* E (from the fp32 copies)
-    f32_rows_to_op(DYB, Yg, C, [&](int r) { return -gt.beta[r] * gt.a[r]; });
-    f32_rows_to_op(EB, Eg, C, [&](int r) { return gt.w[r]; });
+    // operands of the second batch: dY -> -beta a .* dY, E -> w .* E (in place)
+    dy_to_op([&](int r) { return -gt.beta[r] * gt.a[r]; });
+    for (int u = tid; u < C * VD / 8; u += NT) {
+      const int r = ((u >> 7) << 3) + (u & 7);
+      float x[8];
+      unpack8(EB + 8 * u, x);
+      const float f = gt.w[r];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] *= f;
+      tc::st8(EB, 8 * u, x);
+    }
     tc::publish_smem();
     if (tid == 0) {
       umma::gemm_t(tb, DKK, false, KBf, true, 64, KD, C, false);   // dKK k
@@ -1035,7 +1065,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
     bf16* dvg = reinterpret_cast<bf16*>(const_cast<void*>(gr.dv.ptr));
     for (int i = warp; i < Cl; i += NT / 32) {
       const float bi = gt.beta[i];
-      const float4 y = *reinterpret_cast<const float4*>(Yg + i * VD + 4 * lane);
+      const float4 y = *reinterpret_cast<const float4*>(DYF + i * L::YFP + 4 * lane);
       const bf16* vr = vg + tok_off(p.v, b, t0 + i, h) + 4 * lane;
       const float yv[4] = {y.x, y.y, y.z, y.w};
       float s = 0.f;
@@ -1071,7 +1101,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
     }
     float sdsum = 0.f;
 #pragma unroll
-    for (int k = 0; k < NT / 32; ++k) sdsum += red[k];
+    for (int k = 0; k < VD / VB; ++k) sdsum += red[k];
     if (i == Cl - 1) dGc += dwsum + gt.a[Cl - 1] * sdsum;
     if (i >= Cl) dGc = 0.f;
     // reverse inclusive scan over 64 tokens (two warps)
