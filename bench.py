@@ -523,10 +523,14 @@ def run_gdn(torch, ops, dev, rank, world, dist, reps=3):
     fwd_b, bwd_b = 3 * K * 2 + 8 + V * 2, V * 2 + (3 * K * 2 + 8) + (3 * K * 2 + 8)
     tokh = B * T * H
     mac = FWD_MAC_TOK(K, V, R=1) * tokh
+    hbm = peaks()[0]
+    gbs = (fwd_b + bwd_b) * tokh / (ms * 1e-3) / 1e9
     return {"value": world * B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "config": {"batch": B, "seq_len": T, "heads": H, "d_k": K, "d_v": V, "dtype": "bf16",
                        "form": "gated delta rule (v_times_beta), scalar decay g", "fwd+bwd": True},
-            "achieved_gbs": (fwd_b + bwd_b) * tokh / (ms * 1e-3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "basis": "algorithmic bytes of the whole fwd+bwd step / step time"},
+            "achieved_gbs": gbs,
             "algorithmic_bytes_per_step": (fwd_b + bwd_b) * tokh,
             "achieved_tflops": 3 * 2 * mac / (ms * 1e-3) / 1e12}
 
@@ -777,6 +781,8 @@ def main():
     ap.add_argument("--no-layer", action="store_true")
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-gdn", action="store_true")
+    ap.add_argument("--gdn-only", action="store_true",
+                    help="run only the delta-rule (K = V = 128) block on one GPU and print its JSON (profiling)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 8); smaller values make profiler-sized cases")
     args = ap.parse_args()
@@ -787,6 +793,13 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     W = WORK
+    if args.gdn_only:
+        import torch
+        from sca2_b200 import ops
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"gdn_delta": run_gdn(torch, ops, dev, 0, 1, None, reps=max(1, args.steps))}))
+        return
     config = {"workload": "LapA long-head phase-coded delta scan fwd+bwd (phases, per-mode decay, "
                           f"delta gate), B={WORK['B']} T=4096 H=16 d_head=64 (Mh=32, K=V=64) per GPU",
               "batch_per_gpu": W["B"], "seq_len": W["T"], "heads": W["H"], "d_head": 2 * W["Mh"],

@@ -134,6 +134,10 @@ typedef struct sca2_scan_grads {
    *    tensor-core backward writes the per-token rows directly where one CTA owns them)
    *    and all per-token gradient tensors must be dense (B,T,H,C). */
   int32_t overwrite;
+  /* 0: dk / dq (key flavour) are fp32.  1: they are written in the io dtype, like dv (key
+   * flavour, overwrite mode; supported where the chunk-parallel path runs: bf16, K = V = 128,
+   * no lam, 16-byte aligned rows); elsewhere the call fails with SCA2_ERR_UNSUPPORTED. */
+  int32_t grad_io_dtype;
 } sca2_scan_grads;
 
 /* Backward scan: reverse chunk sweep of the adjoint state, all per-token

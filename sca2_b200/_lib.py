@@ -41,7 +41,7 @@ class ScanGrads(C.Structure):
     _fields_ = [
         ("dphw", Tok), ("dphq", Tok), ("dv", Tok), ("dbeta", Tok), ("dg", Tok),
         ("dlam", C.c_void_p), ("dwr", C.c_void_p), ("dwi", C.c_void_p), ("dS0", C.c_void_p),
-        ("overwrite", C.c_int32),
+        ("overwrite", C.c_int32), ("grad_io_dtype", C.c_int32),
     ]
 
 

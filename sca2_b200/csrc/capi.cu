@@ -250,15 +250,21 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
   if (a->g.ptr && !gr->dg.ptr) return fail(SCA2_ERR_ARG, "g given but dg is null");
   if (sca2::cp_covers(*a)) {  // the chunk-parallel path (its forward saved the chunk data)
     auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
-    auto rows4 = [&](const sca2_tok& t) { return a16(t.ptr) && t.sb % 4 == 0 && t.st % 4 == 0 && t.sh % 4 == 0; };
-    if (!rows4(gr->dphw) || !rows4(gr->dphq))
+    const int64_t q = gr->grad_io_dtype ? 8 : 4;  // elements per 16 bytes
+    auto rows = [&](const sca2_tok& t) { return a16(t.ptr) && t.sb % q == 0 && t.st % q == 0 && t.sh % q == 0; };
+    if (!rows(gr->dphw) || !rows(gr->dphq))
       return fail(SCA2_ERR_ARG, "dk and dq rows must be 16-byte aligned for K = V = 128 explicit-key training");
+    if (gr->grad_io_dtype && !gr->overwrite)
+      return fail(SCA2_ERR_UNSUPPORTED, "dk / dq in the io dtype are written, not accumulated (set overwrite)");
     if (gr->overwrite && (rc = check_overwrite(a, gr))) return rc;
     cudaError_t e = sca2::cp_scan_bwd(*a, dO, dS_final, const_cast<float*>(chunk_states), *gr,
                                       sca2::state_slots(a->T), st);
     if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
     return SCA2_OK;
   }
+  if (gr->grad_io_dtype)
+    return fail(SCA2_ERR_UNSUPPORTED, "dk / dq in the io dtype need explicit-key bf16 training at K = V = 128 "
+                                      "without lam (16-byte aligned rows)");
   const bool tc = sca2::tc_train_ok(*a, max_optin_smem());
   if (gr->overwrite) {
     if ((rc = check_overwrite(a, gr))) return rc;

@@ -49,6 +49,8 @@ using tc::bf16;
 
 constexpr int KD = 128, VD = 128, KV = KD * VD;
 constexpr int VB = 32;  // value columns per CTA of the sequential passes
+constexpr int VBP = VB + 4;  // fp32 staging row stride (rows 16-byte aligned, 4 banks apart)
+constexpr int VBR = VB + 8;  // bf16 staging row stride (rows 16-byte aligned, 20 banks apart)
 constexpr int OFF_T = C * VD, OFF_U = C * KD;
 constexpr int OFF_KW = C * KD / 2;  // floats: w .* k (bf16) after W (bf16) in slot 4c+2
 constexpr int OFF_A2 = C * VD;      // floats: the stacked backward operand in slot 4c+1
@@ -301,7 +303,7 @@ __device__ __forceinline__ void gates_from_g(const float* gbuf, float* Gc, float
 // prefetched with cp.async while the current chunk runs.
 constexpr int NQ = 128;  // threads of the recurrence kernels
 struct StateFL {
-  static constexpr int WB = 0, KW = WB + 2 * C * KD * 2, U = KW + 2 * C * KD * 2, SH = U + 2 * C * VB * 4,
+  static constexpr int WB = 0, KW = WB + 2 * C * KD * 2, U = KW + 2 * C * KD * 2, SH = U + 2 * C * VBP * 4,
                        SL = SH + KD * VB * 2, EB = SL + KD * VB * 2, G = EB + C * VB * 2, SC = G + 2 * C * 4,
                        MBAR = SC + 16, TOTAL = MBAR + 16;
 };
@@ -369,10 +371,10 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
       tc::cp16(wd + u, wsrc + u, true);
       tc::cp16(kd + u, wsrc + C * KD / 8 + u, true);
     }
-    float* ud = Ub + buf * C * VB;
+    float* ud = Ub + buf * C * VBP;
     for (int u = tid; u < C * VB / 4; u += NQ) {
       const int i = u >> 3, n = (u & 7) * 4;
-      tc::cp16(ud + i * VB + n, Wg + OFF_U + i * VD + n_base + n, true);
+      tc::cp16(ud + i * VBP + n, Wg + OFF_U + i * VD + n_base + n, true);
     }
     prefetch_gates(p, Gb + buf * C, nullptr, b, h, t0, Cl);
     tc::cp_commit();
@@ -412,9 +414,13 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
       umma::take<16>(r[0], e);
       umma::take<16>(r[1], e + 16);
       const int i = 16 * warp + (lane & 15);
-      const float* ur = Ub + buf * C * VB + i * VB;
+      const float4* ur = reinterpret_cast<const float4*>(Ub + buf * C * VBP + i * VBP);
 #pragma unroll
-      for (int k = 0; k < VB; ++k) e[k] = ur[k] - e[k];
+      for (int k = 0; k < VB / 4; ++k) {
+        const float4 u4 = ur[k];
+        e[4 * k] = u4.x - e[4 * k]; e[4 * k + 1] = u4.y - e[4 * k + 1];
+        e[4 * k + 2] = u4.z - e[4 * k + 2]; e[4 * k + 3] = u4.w - e[4 * k + 3];
+      }
       bf16* Eg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 1));
       if (lane < 16) {
 #pragma unroll
@@ -680,9 +686,9 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
 //   dS = a_last dS' + [q_scale a .* q ; -beta a .* k]^T [dO ; dY]  M = 128, N = 32, K = 128
 //        (+ the dY lo part over the second 64 rows)
 struct StateBL {
-  static constexpr int MB = 0, A2 = MB + 2 * C * KD * 2, Y = A2 + 2 * 2 * C * KD * 2, BS = Y + 2 * C * VB * 4,
+  static constexpr int MB = 0, A2 = MB + 2 * C * KD * 2, Y = A2 + 2 * 2 * C * KD * 2, BS = Y + 2 * C * VBP * 4,
                        YL = BS + 2 * 2 * C * VB * 2, DH = YL + C * VB * 2, DL = DH + KD * VB * 2,
-                       SR = DL + KD * VB * 2, G = SR + 2 * 2 * KD * VB * 2, SC = G + 2 * C * 4, MBAR = SC + 32,
+                       SR = DL + KD * VB * 2, G = SR + 2 * 2 * KD * VBR * 2, SC = G + 2 * C * 4, MBAR = SC + 32,
                        TOTAL = MBAR + 16;
 };
 
@@ -735,10 +741,10 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
       tc::cp16(ad + u, asrc + u, true);
       tc::cp16(ad + C * KD / 8 + u, asrc + C * KD / 8 + u, true);
     }
-    float* yd = Yb + buf * C * VB;
+    float* yd = Yb + buf * C * VBP;
     for (int u = tid; u < C * VB / 4; u += NQ) {
       const int i = u >> 3, n = (u & 7) * 4;
-      tc::cp16(yd + i * VB + n, Mg + OFF_U + i * VD + n_base + n, true);
+      tc::cp16(yd + i * VBP + n, Mg + OFF_U + i * VD + n_base + n, true);
     }
     bf16* dd = BS + buf * 2 * C * VB;
     const bf16* dg = reinterpret_cast<const bf16*>(dO.ptr);
@@ -756,11 +762,11 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     }
     {  // key row tid of the state entering the chunk, this CTA's 32 columns, hi and lo
       const bf16* sg = reinterpret_cast<const bf16*>(slot(cs, bh, NS, c, 0));
-      bf16* sr = SR + buf * 2 * KD * VB + tid * VB;
+      bf16* sr = SR + buf * 2 * KD * VBR + tid * VBR;
 #pragma unroll
       for (int k = 0; k < VB; k += 8) {
         tc::cp16(sr + k, sg + umma::kmaj(tid, n_base + k, VD), true);
-        tc::cp16(sr + KD * VB + k, sg + 2 * OFF_LO + umma::kmaj(tid, n_base + k, VD), true);
+        tc::cp16(sr + KD * VBR + k, sg + 2 * OFF_LO + umma::kmaj(tid, n_base + k, VD), true);
       }
     }
     prefetch_gates(p, Gb + buf * C, nullptr, b, h, t0, Cl);
@@ -788,13 +794,13 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
       bf16* dSg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 3));
 #pragma unroll
       for (int k = 0; k < VB; k += 8) tc::st8(dSg, umma::kmaj(tid, n_base + k, VD), D + k);
-      const bf16* sr = SR + buf * 2 * KD * VB + tid * VB;
+      const bf16* sr = SR + buf * 2 * KD * VBR + tid * VBR;
       float sd = 0.f;
 #pragma unroll
       for (int k = 0; k < VB; k += 8) {
         float hi[8], lo[8];
         unpack8(sr + k, hi);
-        unpack8(sr + KD * VB + k, lo);
+        unpack8(sr + KD * VBR + k, lo);
 #pragma unroll
         for (int q = 0; q < 8; ++q) sd = fmaf(D[k + q], hi[q] + lo[q], sd);
       }
@@ -814,9 +820,12 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
       umma::take<16>(r[0], y);
       umma::take<16>(r[1], y + 16);
       const int i = 16 * warp + (lane & 15);
-      const float* yr = Yb + buf * C * VB + i * VB;
+      const float4* yr = reinterpret_cast<const float4*>(Yb + buf * C * VBP + i * VBP);
 #pragma unroll
-      for (int k = 0; k < VB; ++k) y[k] += yr[k];
+      for (int k = 0; k < VB / 4; ++k) {
+        const float4 y4 = yr[k];
+        y[4 * k] += y4.x; y[4 * k + 1] += y4.y; y[4 * k + 2] += y4.z; y[4 * k + 3] += y4.w;
+      }
       if (lane < 16) {
         float* Yg = slot(cs, bh, NS, c, 2) + OFF_U + i * VD + n_base;
 #pragma unroll
@@ -901,7 +910,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   const bool has_g = p.g.ptr != nullptr, has_beta = p.beta.ptr != nullptr;
-  const bool vtb = p.v_times_beta != 0, ow = gr.overwrite != 0;
+  const bool vtb = p.v_times_beta != 0, ow = gr.overwrite != 0, gio = gr.grad_io_dtype != 0;
   const float qs = p.q_scale;
   enum { R_DB = 0, R_DG = 1, R_Y = 2, R_E = 3, R_O = 4 };
   auto rs = [&](int half, int which) { return rsum + (half * 6 + which) * C; };
@@ -942,6 +951,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   if (tid < VD / VB) red[tid] = slot(cs, bh, NS, c, 3)[OFF_LO + tid];
   tc::publish_smem();
   const uint32_t tb = *s_tmem;
+  uint2 vreg[C / 8];
   if (tid == 0) {
     umma::gemm(tb, QB, KBf, 64, 64, KD, false);          // q k^T
     umma::gemm(tb + 64, KBf, KBf, 64, 64, KD, false);    // k k^T
@@ -1012,6 +1022,14 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
       tc::st8(EB, 8 * u, x);
     }
     tc::publish_smem();
+    // the value rows for sum_v dY v, loaded while the second batch runs (one warp per 8 rows)
+#pragma unroll
+    for (int j = 0; j < C / 8; ++j) {
+      const int i = warp + 8 * j;
+      vreg[j] = i < Cl ? *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(p.v.ptr) +
+                                                          tok_off(p.v, b, t0 + i, h) + 4 * lane)
+                       : make_uint2(0u, 0u);
+    }
     if (tid == 0) {
       umma::gemm_t(tb, DKK, false, KBf, true, 64, KD, C, false);   // dKK k
       umma::gemm_t(tb, DKK, true, KBf, true, 64, KD, C, true);     // dKK^T k
@@ -1037,6 +1055,16 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
         rs(half, R_O)[i] += qs * ro;
         if (i >= Cl) return;
         const float sa = qs * gt.a[i];
+        if (gio) {  // io dtype (bf16), written
+          float yk[16], yq[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) { yk[j] = v[0][j]; yq[j] = fmaf(sa, v[2][j], v[1][j]); }
+          bf16* kb = reinterpret_cast<bf16*>(dk) + tok_off(gr.dphw, b, t0 + i, h) + col0;
+          bf16* qb = reinterpret_cast<bf16*>(dq) + tok_off(gr.dphq, b, t0 + i, h) + col0;
+          tc::st8(kb, 0, yk); tc::st8(kb, 8, yk + 8);
+          tc::st8(qb, 0, yq); tc::st8(qb, 8, yq + 8);
+          return;
+        }
         float* kd = dk + tok_off(gr.dphw, b, t0 + i, h) + col0;
         float* qd = dq + tok_off(gr.dphq, b, t0 + i, h) + col0;
 #pragma unroll
@@ -1060,19 +1088,22 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tb, 512);
   // ---- dv = [beta] dY and sum_v dY v (one warp per token row)
-  {
-    const bf16* vg = reinterpret_cast<const bf16*>(p.v.ptr);
+  if (ok) {
     bf16* dvg = reinterpret_cast<bf16*>(const_cast<void*>(gr.dv.ptr));
-    for (int i = warp; i < Cl; i += NT / 32) {
+#pragma unroll
+    for (int j = 0; j < C / 8; ++j) {
+      const int i = warp + 8 * j;
+      if (i >= Cl) break;
       const float bi = gt.beta[i];
       const float4 y = *reinterpret_cast<const float4*>(DYF + i * L::YFP + 4 * lane);
-      const bf16* vr = vg + tok_off(p.v, b, t0 + i, h) + 4 * lane;
       const float yv[4] = {y.x, y.y, y.z, y.w};
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vreg[j]);
+      const float vv[4] = {__low2float(v2[0]), __high2float(v2[0]), __low2float(v2[1]), __high2float(v2[1])};
       float s = 0.f;
       bf16* dr = dvg + tok_off(gr.dv, b, t0 + i, h) + 4 * lane;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        s = fmaf(yv[k], __bfloat162float(vr[k]), s);
+        s = fmaf(yv[k], vv[k], s);
         dr[k] = __float2bfloat16_rn(vtb ? bi * yv[k] : yv[k]);
       }
       s = warp_sum(s);

@@ -435,6 +435,17 @@ def _(q, k, v, g, beta, lam, S0, scale, v_times_beta, save):
             v.new_empty((B, H, _slots(T), K, V) if save else (0,), dtype=torch.float32))
 
 
+def _key_grads_io(v, K, lam):
+    """Whether the key-flavour backward returns dq, dk in the io dtype: bf16 at K = V = 128
+    without lam (the chunk-parallel path writes them so); otherwise fp32."""
+    return v.dtype == torch.bfloat16 and K == 128 and v.shape[-1] == 128 and lam is None
+
+
+def _rows16(x):
+    """16-byte aligned rows of a (B,T,H,C) tensor with a contiguous channel axis."""
+    return x.data_ptr() % 16 == 0 and all(s % 8 == 0 for s in x.stride()[:3])
+
+
 @torch.library.custom_op("sca2b200::key_scan_bwd", mutates_args=())
 def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional[torch.Tensor],
                   beta: Optional[torch.Tensor], lam: Optional[torch.Tensor], S0: Optional[torch.Tensor], scale: float,
@@ -458,7 +469,10 @@ def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional
     a = _key_args(q, k, v, g, beta, lam, S0, scale, v_times_beta)
     z = lambda *sh: torch.empty(*sh, device=dev, dtype=torch.float32)  # written (overwrite mode)
     E = lambda: torch.empty(0, device=dev, dtype=torch.float32)
-    dk, dq = z(B, T, H, K), z(B, T, H, K)
+    # dq, dk come back in the io dtype where the kernels write it (bf16, K = V = 128, no lam)
+    gio = _key_grads_io(v, K, lam)
+    direct = gio and all(_rows16(x) for x in (q, k, v))
+    dk, dq = (torch.empty(B, T, H, K, device=dev, dtype=dt) for _ in range(2)) if direct else (z(B, T, H, K), z(B, T, H, K))
     dv = torch.empty(B, T, H, V, device=dev, dtype=dt)
     dbeta = z(B, T, H) if beta is not None else None
     dg = z(B, T, H) if g is not None else None
@@ -469,8 +483,11 @@ def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional
     gr.dbeta, gr.dg = _tok(dbeta), _tok(dg)
     gr.dlam, gr.dwr, gr.dwi, gr.dS0 = _ptr(dlam), None, None, _ptr(dS0)
     gr.overwrite = 1
+    gr.grad_io_dtype = 1 if direct else 0
     _lib.check(_lib.load().sca2_scan_bwd(C_ref(a), _out(do5), _ptr(dS), _ptr(cs), C_ref(gr), _stream()),
                "scan_bwd")
+    if gio and not direct:
+        dq, dk = dq.to(dt), dk.to(dt)
     return (dq, dk, dv, E() if dg is None else dg, E() if dbeta is None else dbeta, E() if dlam is None else dlam,
             dS0 if S0 is not None else E())
 
@@ -480,6 +497,10 @@ def _(q, k, v, g, beta, lam, S0, scale, v_times_beta, cs, do, dS):
     B, T, H, K = k.shape
     V = v.shape[-1]
     f = lambda *sh: v.new_empty(*sh, dtype=torch.float32)
+    if _key_grads_io(v, K, lam):
+        return (v.new_empty(B, T, H, K), v.new_empty(B, T, H, K), v.new_empty(B, T, H, V),
+                f(B, T, H) if g is not None else f(0), f(B, T, H) if beta is not None else f(0), f(0),
+                f(B, H, K, V) if S0 is not None else f(0))
     return (f(B, T, H, K), f(B, T, H, K), v.new_empty(B, T, H, V), f(B, T, H) if g is not None else f(0),
             f(B, T, H) if beta is not None else f(0), f(H, K) if lam is not None else f(0),
             f(B, H, K, V) if S0 is not None else f(0))
