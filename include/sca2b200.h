@@ -144,7 +144,9 @@ typedef struct sca2_scan_grads {
  * gradients of a chunk from (state entering the chunk, adjoint leaving it).
  *   dO            (b,t,h,r,V) io dtype, upstream gradient of o
  *   dS_final      (B,H,K,V) fp32 upstream gradient of S_final, or NULL
- *   chunk_states  as written by sca2_scan_fwd for the same inputs.
+ *   chunk_states  as written by sca2_scan_fwd for the same inputs.  The explicit-key path at
+ *                 K = V = 128 also uses its free parts as the backward's workspace (the
+ *                 forward's saved data stay intact, so the backward may be repeated).
  * Replaces torch autograd through the reference's prefill (sca2/arch_damp.py:141-198,
  * lapa/layer.py:298-366). */
 SCA2_API int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,

@@ -27,12 +27,15 @@
 // two small products per chunk.  Tensor-core operands are single bf16 (the state chain itself
 // stays fp32); the saved per-chunk data live in the four slots of each chunk:
 //   slot 4c    S_c as hi | lo (K x V bf16 each, operand layout)
-//   slot 4c+1  E_c (64 x V bf16, operand layout) | T (64 x 64 fp32, zeros above the diagonal); the backward
-//              replaces T by [q_scale a .* q ; -beta a .* k] (128 x K bf16, operand layout)
+//   slot 4c+1  E_c (64 x V bf16, operand layout) | backward: sum(S_c .* dS') per block of 32 value
+//              columns (fp32, from the fp32 adjoint and the hi + lo state) | T (64 x 64 fp32, zeros
+//              above the diagonal)
 //   slot 4c+2  W | w .* k (64 x K bf16 each, operand layout) | U (64 x V fp32)
 //              backward: Mt (64 x K bf16, operand layout) | Yo, then dY (64 x V fp32)
-//   slot 4c+3  backward: dS' (K x V bf16, operand layout) | sum(S_c .* dS') per block of 32 value
-//              columns (fp32, from the fp32 adjoint and the hi + lo state)
+//   slot 4c+3  backward: dS' (K x V bf16, operand layout) | [q_scale a .* q ; -beta a .* k] (128 x K
+//              bf16, operand layout)
+// The backward overwrites only what it recomputes (W, U by Mt, Yo; nothing the forward saved for
+// it), so it can run more than once on one forward's data.
 // The two recurrences also run on the tensor cores: per chunk one product into TMEM for the
 // token rows (E or dY, M = 64) and one for the state rows (M = 128); the state and its adjoint
 // stay in fp32 registers (one key row per thread) and enter the products as hi + lo bf16 pairs.
@@ -53,8 +56,9 @@ constexpr int VBP = VB + 4;  // fp32 staging row stride (rows 16-byte aligned, 4
 constexpr int VBR = VB + 8;  // bf16 staging row stride (rows 16-byte aligned, 20 banks apart)
 constexpr int OFF_T = C * VD, OFF_U = C * KD;
 constexpr int OFF_KW = C * KD / 2;  // floats: w .* k (bf16) after W (bf16) in slot 4c+2
-constexpr int OFF_A2 = C * VD;      // floats: the stacked backward operand in slot 4c+1
-constexpr int OFF_LO = KD * VD / 2; // floats: the state's lo part in slot 4c; the S .* dS' partial sums in 4c+3
+constexpr int OFF_A2 = KD * VD / 2; // floats: the stacked backward operand in slot 4c+3, after dS'
+constexpr int OFF_LO = KD * VD / 2; // floats: the state's lo part in slot 4c
+constexpr int OFF_P = C * VD / 2;   // floats: the S .* dS' partial sums in slot 4c+1, after E
 
 // bit 0: a bounded mbarrier wait of a chunk-parallel kernel timed out
 __device__ unsigned int g_fault_cp;
@@ -138,13 +142,16 @@ __device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates&
 // ======================================================================================
 //  F1: T, W = T diag(beta a) k, U = T v_eff per chunk
 // ======================================================================================
+// 75 KB of shared memory and 128 TMEM columns: three CTAs per SM.  T's two scaled operand
+// copies reuse the region of L (dead after the inversion); W and U take turns in TMEM.
 struct PrepL {
-  static constexpr int KB = 0, VBUF = KB + al(C * KD * 2), TW = VBUF + al(C * VD * 2), TV = TW + al(C * C * 2),
-                       LS = TV + al(C * C * 2), TS = LS + al(C * LDF * 4), WS = TS + al(C * LDF * 4),
-                       SC = WS + 4096, MBAR = SC + 4 * C * 4, TOTAL = MBAR + 16;
+  static constexpr int KB = 0, VBUF = KB + al(C * KD * 2), LS = VBUF + al(C * VD * 2), TW = LS, TV = TW + C * C * 2,
+                       TS = LS + al(C * LDF * 4), WS = TS + al(C * LDF * 4), SC = WS + 4096, MBAR = SC + 4 * C * 4,
+                       TOTAL = MBAR + 16;
+  static_assert(2 * C * C * 2 <= C * LDF * 4, "T's operand copies fit the region of L");
 };
 
-__global__ void __launch_bounds__(NT, 2) cp_prep(sca2_scan_args p, float* cs, int NS, int vec) {
+__global__ void __launch_bounds__(NT, 3) cp_prep(sca2_scan_args p, float* cs, int NS, int vec) {
   using L = PrepL;
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -168,7 +175,7 @@ __global__ void __launch_bounds__(NT, 2) cp_prep(sca2_scan_args p, float* cs, in
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
   }
-  if (warp == 0) umma::tmem_alloc(s_tmem, 256);
+  if (warp == 0) umma::tmem_alloc(s_tmem, 128);
   load_rows(KBf, reinterpret_cast<const bf16*>(p.phw.ptr), p.phw.sb, p.phw.st, p.phw.sh, b, t0, h, Cl, vec);
   load_rows(VBf, reinterpret_cast<const bf16*>(p.v.ptr), p.v.sb, p.v.st, p.v.sh, b, t0, h, Cl, vec);
   tc::cp_commit();
@@ -221,7 +228,6 @@ __global__ void __launch_bounds__(NT, 2) cp_prep(sca2_scan_args p, float* cs, in
     tc::publish_smem();
     if (tid == 0) {
       umma::gemm_t(tb, TW, false, KBf, true, 64, KD, C, false);         // W = (T beta a) k
-      umma::gemm_t(tb + 128, TV, false, VBf, true, 64, VD, C, false);   // U = (T [beta]) v
       umma::commit(mbar);
     }
     ok = batch_wait(mbar, 1);
@@ -242,17 +248,26 @@ __global__ void __launch_bounds__(NT, 2) cp_prep(sca2_scan_args p, float* cs, in
         for (int k = 0; k < 8; ++k) x[k] *= wi;
         tc::st8(KWg, umma::kmaj(i, m0, KD), x);
       }
-      tc::for_frag<64, 128>(tb + 128, [&](int i, int j0, int, const float* x) {
-        float4* d = reinterpret_cast<float4*>(Wg + OFF_U + i * VD + j0);
+      umma::fence_before_sync();
+      __syncthreads();
+      umma::fence_after_sync();
+      if (tid == 0) {
+        umma::gemm_t(tb, TV, false, VBf, true, 64, VD, C, false);  // U = (T [beta]) v
+        umma::commit(mbar);
+      }
+      ok = batch_wait(mbar, 0);
+      if (ok)
+        tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {
+          float4* d = reinterpret_cast<float4*>(Wg + OFF_U + i * VD + j0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) d[k] = make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
-      });
+          for (int k = 0; k < 4; ++k) d[k] = make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+        });
     }
   }
   if (!ok) umma::mbar_wait(mbar, 0), umma::mbar_wait(mbar, 1);  // bounded: let the MMAs drain
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tb, 256);
+  if (warp == 0) umma::tmem_dealloc(tb, 128);
 }
 
 // ======================================================================================
@@ -648,8 +663,8 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
         tc::st8(Mb, umma::kmaj(i, j0, KD), x);
         tc::st8(Mb, umma::kmaj(i, j0 + 8, KD), x + 8);
       });
-      // [q_scale a .* q ; -beta a .* k] (T has been read: it shares the slot)
-      bf16* A2 = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 1) + OFF_A2);
+      // [q_scale a .* q ; -beta a .* k]
+      bf16* A2 = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 3) + OFF_A2);
       for (int u = tid; u < 2 * C * KD / 8; u += NT) {
         const int r = u >> 4, m0 = (u & 15) * 8, i = r & (C - 1);
         float x[8];
@@ -733,7 +748,7 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     const int buf = c & 1, t0 = c * C, Cl = min(C, p.T - t0);
     const float* Mg = slot(cs, bh, NS, c, 2);
     const uint4* msrc = reinterpret_cast<const uint4*>(Mg);
-    const uint4* asrc = reinterpret_cast<const uint4*>(slot(cs, bh, NS, c, 1) + OFF_A2);
+    const uint4* asrc = reinterpret_cast<const uint4*>(slot(cs, bh, NS, c, 3) + OFF_A2);
     uint4* md = reinterpret_cast<uint4*>(MB + buf * C * KD);
     uint4* ad = reinterpret_cast<uint4*>(A2 + buf * 2 * C * KD);
     for (int u = tid; u < C * KD / 8; u += NQ) {
@@ -810,7 +825,7 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     ok = batch_wait(mbar, ph);
     ph ^= 1;
     if (!ok) break;
-    if (tid == 0) slot(cs, bh, NS, c, 3)[OFF_LO + vb] = red[0] + red[1] + red[2] + red[3];
+    if (tid == 0) slot(cs, bh, NS, c, 1)[OFF_P + vb] = red[0] + red[1] + red[2] + red[3];
     {
       uint32_t r[2][16];
       umma::ld16_issue(umma::taddr(tY, 32 * warp, 0), r[0]);
@@ -948,7 +963,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
     }
   };
   dy_to_op([](int) { return 1.f; });
-  if (tid < VD / VB) red[tid] = slot(cs, bh, NS, c, 3)[OFF_LO + tid];
+  if (tid < VD / VB) red[tid] = slot(cs, bh, NS, c, 1)[OFF_P + tid];
   tc::publish_smem();
   const uint32_t tb = *s_tmem;
   uint2 vreg[C / 8];

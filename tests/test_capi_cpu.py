@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, n), n
     assert sorted(n for n, _, _ in _lib.SIGNATURES) == names
     assert b"sm_100a" in lib.sca2_version()
-    # three saved-state slots per 64-token chunk
+    # four saved-state slots per 64-token chunk
     assert lib.sca2_num_chunks(4096) == 256 and lib.sca2_num_chunks(1) == 4 and lib.sca2_num_chunks(65) == 8
     assert lib.sca2_num_chunks(0) == 0
 
@@ -45,6 +45,7 @@ int main(void) {
          sizeof(sca2_tok), sizeof(sca2_out), sizeof(sca2_scan_args), sizeof(sca2_scan_grads));
   F(sca2_scan_args, q_scale) F(sca2_scan_args, phw) F(sca2_scan_args, g) F(sca2_scan_args, lam)
   F(sca2_scan_args, S0) F(sca2_scan_grads, dg) F(sca2_scan_grads, dlam) F(sca2_scan_grads, dS0)
+  F(sca2_scan_grads, overwrite) F(sca2_scan_grads, grad_io_dtype)
   printf("sca2_dscan_args %zu\nsca2_dscan_grads %zu\n", sizeof(sca2_dscan_args), sizeof(sca2_dscan_grads));
   F(sca2_dscan_args, sep) F(sca2_dscan_args, a_re) F(sca2_dscan_args, S0_im)
   F(sca2_dscan_grads, dv) F(sca2_dscan_grads, dS0_im)

@@ -136,3 +136,44 @@ def test_cp_full_size_slices():
         _check("S", S[b:b + 1, h:h + 1], rS)
         for n, x in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
             _check(n, x.grad[b:b + 1, :, h:h + 1], rg[n])
+
+
+def test_cp_grad_dtypes_agree():
+    """dq / dk written in bf16 (grad_io_dtype = 1, what the torch op uses) equal the fp32 ones of the
+    same backward (grad_io_dtype = 0) up to bf16 rounding; grad_io_dtype = 1 is refused where the
+    chunk-parallel path does not run."""
+    from sca2_b200 import _lib, ops
+    d = _inputs(2, 150, 2, seed=4)
+    t = {n: cuda(d[n], torch.bfloat16 if n in "qkv" else torch.float32) for n in ("q", "k", "v", "g", "beta")}
+    dO = cuda(d["dO"], torch.bfloat16)
+    sc = K ** -0.5
+    o, S, cs = torch.ops.sca2b200.key_scan_fwd(t["q"], t["k"], t["v"], t["g"], t["beta"], None, None, sc, True, True)
+    dq16, dk16 = torch.ops.sca2b200.key_scan_bwd(t["q"], t["k"], t["v"], t["g"], t["beta"], None, None, sc, True, cs,
+                                                 dO, None)[:2]
+    assert dq16.dtype == torch.bfloat16 and dk16.dtype == torch.bfloat16
+
+    def bwd(gio, k_width=K, cs_=cs, tt=t):
+        B, T, H = 2, 150, 2
+        a = ops._key_args(tt["q"], tt["k"], tt["v"], tt["g"], tt["beta"], None, None, sc, True)
+        f = lambda *sh, dt=torch.float32: torch.empty(*sh, device="cuda", dtype=dt)
+        gdt = torch.bfloat16 if gio else torch.float32
+        dk, dq, dv = f(B, T, H, k_width, dt=gdt), f(B, T, H, k_width, dt=gdt), f(B, T, H, V, dt=torch.bfloat16)
+        db, dg = f(B, T, H), f(B, T, H)
+        gr = _lib.ScanGrads()
+        gr.dphw, gr.dphq, gr.dv = ops._tok(dk), ops._tok(dq), ops._tok(dv)
+        gr.dbeta, gr.dg = ops._tok(db), ops._tok(dg)
+        gr.overwrite, gr.grad_io_dtype = 1, gio
+        rc = _lib.load().sca2_scan_bwd(ops.C_ref(a), ops._out(dO.unsqueeze(3)), None, ops._ptr(cs_), ops.C_ref(gr),
+                                       ops._stream())
+        return rc, dq, dk
+    rc, dq32, dk32 = bwd(0)
+    assert rc == 0
+    torch.cuda.synchronize()
+    for a16, a32 in ((dq16, dq32), (dk16, dk32)):  # one bf16 rounding apart
+        assert (a16.float() - a32).abs().max() <= 2 ** -8 * a32.abs().max()
+    # K = 64: the tensor-core walk runs instead, which writes fp32 only
+    d64 = {n: x[..., :64].contiguous() if n in "qk" else x for n, x in t.items()}
+    o2, S2, cs2 = torch.ops.sca2b200.key_scan_fwd(d64["q"], d64["k"], d64["v"], d64["g"], d64["beta"], None, None,
+                                                  sc, True, True)
+    rc, _, _ = bwd(1, 64, cs2, d64)
+    assert rc == _lib.SCA2_ERR_UNSUPPORTED
