@@ -572,13 +572,15 @@ __global__ void __launch_bounds__(NT, 2) cp_out(sca2_scan_args p, sca2_out o, co
 // ======================================================================================
 //  B1: Yo = T^T P^T dO and Mt = T^T diag(w) k per chunk
 // ======================================================================================
+// 73 KB of shared memory (P^T dO takes the place of dO once formed) and 128 TMEM columns, the
+// products one after another: three CTAs per SM.
 struct BPrepL {
   static constexpr int QB = 0, KB = QB + al(C * KD * 2), DOB = KB + al(C * KD * 2), PB = DOB + al(C * VD * 2),
-                       TB = PB + al(C * C * 2), TWB = TB + al(C * C * 2), Z1 = TWB + al(C * C * 2),
-                       SC = Z1 + al(C * VD * 2), MBAR = SC + 4 * C * 4, TOTAL = MBAR + 16;
+                       TB = PB + al(C * C * 2), TWB = TB + al(C * C * 2), Z1 = DOB,
+                       SC = TWB + al(C * C * 2), MBAR = SC + 4 * C * 4, TOTAL = MBAR + 16;
 };
 
-__global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO, float* cs, int NS, int vec,
+__global__ void __launch_bounds__(NT, 3) cp_bprep(sca2_scan_args p, sca2_out dO, float* cs, int NS, int vec,
                                                   int dvec) {
   using L = BPrepL;
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -604,7 +606,7 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
   }
-  if (warp == 0) umma::tmem_alloc(s_tmem, 256);
+  if (warp == 0) umma::tmem_alloc(s_tmem, 128);
   load_rows(QB, reinterpret_cast<const bf16*>(p.phq.ptr), p.phq.sb, p.phq.st, p.phq.sh, b, t0, h, Cl, vec);
   load_rows(KBf, reinterpret_cast<const bf16*>(p.phw.ptr), p.phw.sb, p.phw.st, p.phw.sh, b, t0, h, Cl, vec);
   load_rows(DOB, reinterpret_cast<const bf16*>(dO.ptr), dO.sb, dO.st, dO.sh, b, t0, h, Cl, dvec);
@@ -648,21 +650,29 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
     tc::publish_smem();
     if (tid == 0) {
       umma::gemm_t(tb, PB, true, DOB, true, 64, VD, C, false);         // P^T dO
-      umma::gemm_t(tb + 128, TWB, true, KBf, true, 64, KD, C, false);  // (diag(w) T)^T k
       umma::commit(mbar);
     }
     ok = batch_wait(mbar, 1);
     if (ok) {
       float* Mg = slot(cs, bh, NS, c, 2);
       bf16* Mb = reinterpret_cast<bf16*>(Mg);
-      tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {
+      tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {  // over dO (read by the product)
         tc::st8(Z1, umma::kmaj(i, j0, VD), x);
         tc::st8(Z1, umma::kmaj(i, j0 + 8, VD), x + 8);
       });
-      tc::for_frag<64, 128>(tb + 128, [&](int i, int j0, int, const float* x) {
-        tc::st8(Mb, umma::kmaj(i, j0, KD), x);
-        tc::st8(Mb, umma::kmaj(i, j0 + 8, KD), x + 8);
-      });
+      umma::fence_before_sync();
+      __syncthreads();
+      umma::fence_after_sync();
+      if (tid == 0) {
+        umma::gemm_t(tb, TWB, true, KBf, true, 64, KD, C, false);  // (diag(w) T)^T k
+        umma::commit(mbar);
+      }
+      ok = batch_wait(mbar, 0);
+      if (ok)
+        tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {
+          tc::st8(Mb, umma::kmaj(i, j0, KD), x);
+          tc::st8(Mb, umma::kmaj(i, j0 + 8, KD), x + 8);
+        });
       // [q_scale a .* q ; -beta a .* k]
       bf16* A2 = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 3) + OFF_A2);
       for (int u = tid; u < 2 * C * KD / 8; u += NT) {
@@ -675,11 +685,11 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
         tc::st8(A2, umma::kmaj(r, m0, KD), x);
       }
       tc::publish_smem();
-      if (tid == 0) {
+      if (ok && tid == 0) {
         umma::gemm_t(tb, TB, true, Z1, true, 64, VD, C, false);  // Yo = T^T (P^T dO)
         umma::commit(mbar);
       }
-      ok = batch_wait(mbar, 0);
+      if (ok) ok = batch_wait(mbar, 1);
       if (ok)
         tc::for_frag<64, 128>(tb, [&](int i, int j0, int, const float* x) {
           float4* d = reinterpret_cast<float4*>(Mg + OFF_U + i * VD + j0);
@@ -691,7 +701,7 @@ __global__ void __launch_bounds__(NT, 2) cp_bprep(sca2_scan_args p, sca2_out dO,
   if (!ok) umma::mbar_wait(mbar, 0), umma::mbar_wait(mbar, 1);
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tb, 256);
+  if (warp == 0) umma::tmem_dealloc(tb, 128);
 }
 
 // ======================================================================================
