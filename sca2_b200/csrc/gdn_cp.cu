@@ -121,6 +121,18 @@ __device__ __forceinline__ void unpack8(const bf16* p, float* x) {
   for (int k = 0; k < 4; ++k) { x[2 * k] = __low2float(h2[k]); x[2 * k + 1] = __high2float(h2[k]); }
 }
 
+// one bulk copy global -> shared (16-byte aligned, size a multiple of 16) completing on `bar`;
+// the issuing thread first announces the bytes with bulk_expect
+__device__ __forceinline__ void bulk_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(umma::smem_u32(dst)), "l"(src), "r"(bytes), "r"(umma::smem_u32(bar))
+               : "memory");
+}
+
 // bounded wait on the batch mbarrier; on timeout the fault word is set and false returned
 // (the result is the same in every thread of the CTA)
 __device__ __forceinline__ bool batch_wait(uint64_t* mbar, uint32_t parity) {
@@ -320,7 +332,7 @@ constexpr int NQ = 128;  // threads of the recurrence kernels
 struct StateFL {
   static constexpr int WB = 0, KW = WB + 2 * C * KD * 2, U = KW + 2 * C * KD * 2, SH = U + 2 * C * VBP * 4,
                        SL = SH + KD * VB * 2, EB = SL + KD * VB * 2, G = EB + C * VB * 2, SC = G + 2 * C * 4,
-                       MBAR = SC + 16, TOTAL = MBAR + 16;
+                       MBAR = SC + 16, LBAR = MBAR + 16, TOTAL = LBAR + 16;
 };
 
 // warp 0: exp of the chunk's summed log-decay (g = 0 past the chunk's end)
@@ -358,9 +370,12 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
   float* aL = reinterpret_cast<float*>(sm + L::SC);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
+  uint64_t* lbar = reinterpret_cast<uint64_t*>(sm + L::LBAR);  // bulk loads of W, w .* k per buffer
 
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
+    umma::mbar_init(lbar, 1);
+    umma::mbar_init(lbar + 1, 1);
     umma::fence_mbar_init();
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 64);
@@ -376,15 +391,15 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
 #pragma unroll
     for (int k = 0; k < VB; k += 8) tc::st8_split(SH, SL, umma::kmaj(tid, k, VB), S + k);
   }
+  uint32_t pend = 0;  // buffers with a bulk load not yet waited for
   auto prefetch = [&](int c) {
     const int buf = c & 1, t0 = c * C, Cl = min(C, p.T - t0);
     const float* Wg = slot(cs, bh, NS, c, 2);
-    const uint4* wsrc = reinterpret_cast<const uint4*>(Wg);
-    uint4* wd = reinterpret_cast<uint4*>(WB + buf * C * KD);
-    uint4* kd = reinterpret_cast<uint4*>(KWB + buf * C * KD);
-    for (int u = tid; u < C * KD / 8; u += NQ) {
-      tc::cp16(wd + u, wsrc + u, true);
-      tc::cp16(kd + u, wsrc + C * KD / 8 + u, true);
+    pend |= 1u << buf;
+    if (tid == 0) {  // W and w .* k: two contiguous 16 KB operand tiles
+      bulk_expect(lbar + buf, 2 * C * KD * 2);
+      bulk_load(WB + buf * C * KD, Wg, C * KD * 2, lbar + buf);
+      bulk_load(KWB + buf * C * KD, Wg + OFF_KW, C * KD * 2, lbar + buf);
     }
     float* ud = Ub + buf * C * VBP;
     for (int u = tid; u < C * VB / 4; u += NQ) {
@@ -399,11 +414,15 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = *s_tmem, tE = tb, tS = tb + 32;
-  uint32_t ph = 0;
+  uint32_t ph = 0, lph = 0;
   bool ok = true;
   for (int c = 0; c < NC && ok; ++c) {
     const int buf = c & 1;
     tc::cp_wait_all();
+    ok = batch_wait(lbar + buf, (lph >> buf) & 1);
+    lph ^= 1u << buf;
+    pend &= ~(1u << buf);
+    if (!ok) break;
     tc::publish_smem();
     if (tid == 0) {
       umma::gemm_t(tE, WB + buf * C * KD, false, SH, true, 64, VB, KD, false);
@@ -467,6 +486,8 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
     for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(S[k], S[k + 1], S[k + 2], S[k + 3]);
   }
   tc::cp_wait_all();
+  for (int q = 0; q < 2; ++q)  // after a fault: let issued bulk loads land before the CTA exits (bounded)
+    if ((pend >> q) & 1) umma::mbar_wait(lbar + q, (lph >> q) & 1);
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tb, 64);
@@ -714,7 +735,7 @@ struct StateBL {
   static constexpr int MB = 0, A2 = MB + 2 * C * KD * 2, Y = A2 + 2 * 2 * C * KD * 2, BS = Y + 2 * C * VBP * 4,
                        YL = BS + 2 * 2 * C * VB * 2, DH = YL + C * VB * 2, DL = DH + KD * VB * 2,
                        SR = DL + KD * VB * 2, G = SR + 2 * 2 * KD * VBR * 2, SC = G + 2 * C * 4, MBAR = SC + 32,
-                       TOTAL = MBAR + 16;
+                       LBAR = MBAR + 16, TOTAL = LBAR + 16;
 };
 
 __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out dO, const float* dS_final,
@@ -737,9 +758,12 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
   float* red = aL + 1;
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
+  uint64_t* lbar = reinterpret_cast<uint64_t*>(sm + L::LBAR);  // bulk loads of Mt and the stacked operand
 
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
+    umma::mbar_init(lbar, 1);
+    umma::mbar_init(lbar + 1, 1);
     umma::fence_mbar_init();
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 64);
@@ -754,17 +778,15 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
 #pragma unroll
     for (int k = 0; k < VB; k += 8) tc::st8_split(DH, DL, umma::kmaj(tid, k, VB), D + k);
   }
+  uint32_t pend = 0;  // buffers with a bulk load not yet waited for
   auto prefetch = [&](int c) {
     const int buf = c & 1, t0 = c * C, Cl = min(C, p.T - t0);
     const float* Mg = slot(cs, bh, NS, c, 2);
-    const uint4* msrc = reinterpret_cast<const uint4*>(Mg);
-    const uint4* asrc = reinterpret_cast<const uint4*>(slot(cs, bh, NS, c, 3) + OFF_A2);
-    uint4* md = reinterpret_cast<uint4*>(MB + buf * C * KD);
-    uint4* ad = reinterpret_cast<uint4*>(A2 + buf * 2 * C * KD);
-    for (int u = tid; u < C * KD / 8; u += NQ) {
-      tc::cp16(md + u, msrc + u, true);
-      tc::cp16(ad + u, asrc + u, true);
-      tc::cp16(ad + C * KD / 8 + u, asrc + C * KD / 8 + u, true);
+    pend |= 1u << buf;
+    if (tid == 0) {  // Mt (16 KB) and the stacked operand (32 KB), contiguous operand tiles
+      bulk_expect(lbar + buf, 3 * C * KD * 2);
+      bulk_load(MB + buf * C * KD, Mg, C * KD * 2, lbar + buf);
+      bulk_load(A2 + buf * 2 * C * KD, slot(cs, bh, NS, c, 3) + OFF_A2, 2 * C * KD * 2, lbar + buf);
     }
     float* yd = Yb + buf * C * VBP;
     for (int u = tid; u < C * VB / 4; u += NQ) {
@@ -802,11 +824,15 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = *s_tmem, tY = tb, tD = tb + 32;
-  uint32_t ph = 0;
+  uint32_t ph = 0, lph = 0;
   bool ok = true;
   for (int c = NC - 1; c >= 0 && ok; --c) {
     const int buf = c & 1;
     tc::cp_wait_all();
+    ok = batch_wait(lbar + buf, (lph >> buf) & 1);
+    lph ^= 1u << buf;
+    pend &= ~(1u << buf);
+    if (!ok) break;
     tc::publish_smem();
     if (tid == 0) {
       umma::gemm_t(tY, MB + buf * C * KD, false, DH, true, 64, VB, KD, false);
@@ -892,6 +918,8 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(D[k], D[k + 1], D[k + 2], D[k + 3]);
   }
   tc::cp_wait_all();
+  for (int q = 0; q < 2; ++q)  // after a fault: let issued bulk loads land before the CTA exits (bounded)
+    if ((pend >> q) & 1) umma::mbar_wait(lbar + q, (lph >> q) & 1);
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tb, 64);
