@@ -354,10 +354,14 @@ __device__ __forceinline__ void ld_row32(uint32_t tbase, float* v) {
   umma::take<16>(r[1], v + 16);
 }
 
-__global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* cs, int NS, float* S_final) {
+// 8 warps: warp w reads TMEM sub-partition w % 4 and owns value columns 16 (w / 4) .. + 15 of its
+// rows, so each epilogue handles 16 columns per thread.
+constexpr int NQF = 256;
+__global__ void __launch_bounds__(NQF, 1) cp_state_fwd(sca2_scan_args p, float* cs, int NS, float* S_final) {
   using L = StateFL;
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, sub = warp & 3, c0 = (warp >> 2) * 16;
+  const int m = 32 * sub + lane;  // key row of this thread's state columns
   const int vb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int NC = (p.T + C - 1) / C, n_base = vb * VB;
   bf16* WB = reinterpret_cast<bf16*>(sm + L::WB);
@@ -379,17 +383,17 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
     umma::fence_mbar_init();
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 64);
-  // key row tid of the incoming state, and its hi / lo operand copy
-  float S[VB];
+  // 16 columns of key row m of the incoming state, and their hi / lo operand copy
+  float S[16];
   {
-    const float* src = p.S0 ? p.S0 + (int64_t)bh * KV + tid * VD + n_base : nullptr;
+    const float* src = p.S0 ? p.S0 + (int64_t)bh * KV + m * VD + n_base + c0 : nullptr;
 #pragma unroll
-    for (int k = 0; k < VB; k += 4) {
+    for (int k = 0; k < 16; k += 4) {
       const float4 x = src ? *reinterpret_cast<const float4*>(src + k) : make_float4(0.f, 0.f, 0.f, 0.f);
       S[k] = x.x; S[k + 1] = x.y; S[k + 2] = x.z; S[k + 3] = x.w;
     }
 #pragma unroll
-    for (int k = 0; k < VB; k += 8) tc::st8_split(SH, SL, umma::kmaj(tid, k, VB), S + k);
+    for (int k = 0; k < 16; k += 8) tc::st8_split(SH, SL, umma::kmaj(m, c0 + k, VB), S + k);
   }
   uint32_t pend = 0;  // buffers with a bulk load not yet waited for
   auto prefetch = [&](int c) {
@@ -402,7 +406,7 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
       bulk_load(KWB + buf * C * KD, Wg + OFF_KW, C * KD * 2, lbar + buf);
     }
     float* ud = Ub + buf * C * VBP;
-    for (int u = tid; u < C * VB / 4; u += NQ) {
+    for (int u = tid; u < C * VB / 4; u += NQF) {
       const int i = u >> 3, n = (u & 7) * 4;
       tc::cp16(ud + i * VBP + n, Wg + OFF_U + i * VD + n_base + n, true);
     }
@@ -434,23 +438,21 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
     {  // the state entering chunk c: hi (the operand of q S and dY S^T) and lo, operand layout
       bf16* Sg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 0));
 #pragma unroll
-      for (int k = 0; k < VB; k += 8) tc::st8_split(Sg, Sg + 2 * OFF_LO, umma::kmaj(tid, n_base + k, VD), S + k);
+      for (int k = 0; k < 16; k += 8) tc::st8_split(Sg, Sg + 2 * OFF_LO, umma::kmaj(m, n_base + c0 + k, VD), S + k);
     }
     ok = batch_wait(mbar, ph);
     ph ^= 1;
     if (!ok) break;
-    {  // E rows: lanes 0-15 of warp w hold tokens 16 w .. 16 w + 15 (the loads are warp-wide)
-      uint32_t r[2][16];
-      umma::ld16_issue(umma::taddr(tE, 32 * warp, 0), r[0]);
-      umma::ld16_issue(umma::taddr(tE, 32 * warp, 16), r[1]);
+    {  // E rows: lanes 0-15 of warp w hold tokens 16 (w % 4) .. + 15 (the loads are warp-wide)
+      uint32_t r[16];
+      umma::ld16_issue(umma::taddr(tE, 32 * sub, c0), r);
       umma::ld_wait();
-      float e[VB];
-      umma::take<16>(r[0], e);
-      umma::take<16>(r[1], e + 16);
-      const int i = 16 * warp + (lane & 15);
-      const float4* ur = reinterpret_cast<const float4*>(Ub + buf * C * VBP + i * VBP);
+      float e[16];
+      umma::take<16>(r, e);
+      const int i = 16 * sub + (lane & 15);
+      const float4* ur = reinterpret_cast<const float4*>(Ub + buf * C * VBP + i * VBP + c0);
 #pragma unroll
-      for (int k = 0; k < VB / 4; ++k) {
+      for (int k = 0; k < 4; ++k) {
         const float4 u4 = ur[k];
         e[4 * k] = u4.x - e[4 * k]; e[4 * k + 1] = u4.y - e[4 * k + 1];
         e[4 * k + 2] = u4.z - e[4 * k + 2]; e[4 * k + 3] = u4.w - e[4 * k + 3];
@@ -458,9 +460,9 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
       bf16* Eg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 1));
       if (lane < 16) {
 #pragma unroll
-        for (int k = 0; k < VB; k += 8) {
-          tc::st8(Eg, umma::kmaj(i, n_base + k, VD), e + k);
-          tc::st8(EB, umma::kmaj(i, k, VB), e + k);
+        for (int k = 0; k < 16; k += 8) {
+          tc::st8(Eg, umma::kmaj(i, n_base + c0 + k, VD), e + k);
+          tc::st8(EB, umma::kmaj(i, c0 + k, VB), e + k);
         }
       }
     }
@@ -472,18 +474,21 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_fwd(sca2_scan_args p, float* c
     ok = batch_wait(mbar, ph);
     ph ^= 1;
     if (!ok) break;
-    float acc[VB];
-    ld_row32(tS, acc);
+    uint32_t r[16];
+    umma::ld16_issue(umma::taddr(tS, 32 * sub, c0), r);
+    umma::ld_wait();
+    float acc[16];
+    umma::take<16>(r, acc);
     const float al_ = *aL;
 #pragma unroll
-    for (int k = 0; k < VB; ++k) S[k] = fmaf(al_, S[k], acc[k]);
+    for (int k = 0; k < 16; ++k) S[k] = fmaf(al_, S[k], acc[k]);
 #pragma unroll
-    for (int k = 0; k < VB; k += 8) tc::st8_split(SH, SL, umma::kmaj(tid, k, VB), S + k);
+    for (int k = 0; k < 16; k += 8) tc::st8_split(SH, SL, umma::kmaj(m, c0 + k, VB), S + k);
   }
   if (ok && S_final) {
-    float* dst = S_final + (int64_t)bh * KV + tid * VD + n_base;
+    float* dst = S_final + (int64_t)bh * KV + m * VD + n_base + c0;
 #pragma unroll
-    for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(S[k], S[k + 1], S[k + 2], S[k + 3]);
+    for (int k = 0; k < 16; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(S[k], S[k + 1], S[k + 2], S[k + 3]);
   }
   tc::cp_wait_all();
   for (int q = 0; q < 2; ++q)  // after a fault: let issued bulk loads land before the CTA exits (bounded)
@@ -1240,7 +1245,7 @@ cudaError_t cp_scan_fwd(const sca2_scan_args& p, sca2_out o, float* S_final, flo
   if ((e = set_smem(cp::cp_state_fwd, cp::StateFL::TOTAL)) != cudaSuccess) return e;
   if ((e = set_smem(cp::cp_out, cp::OutL::TOTAL)) != cudaSuccess) return e;
   cp::cp_prep<<<gc, cp::NT, cp::PrepL::TOTAL, st>>>(p, cstates, NS, 1);
-  cp::cp_state_fwd<<<gs, cp::NQ, cp::StateFL::TOTAL, st>>>(p, cstates, NS, S_final);
+  cp::cp_state_fwd<<<gs, cp::NQF, cp::StateFL::TOTAL, st>>>(p, cstates, NS, S_final);
   cp::cp_out<<<gc, cp::NT, cp::OutL::TOTAL, st>>>(p, o, cstates, NS, 1, out_rows16(o) ? 1 : 0);
   return cudaGetLastError();
 }
