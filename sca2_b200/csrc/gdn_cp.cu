@@ -323,12 +323,11 @@ __device__ __forceinline__ void gates_from_g(const float* gbuf, float* Gc, float
   if (l == 0) *aL = expf(Gl);
 }
 
-// The state recurrence on the tensor cores, one CTA of 4 warps per (b, h, 32 value columns):
+// The state recurrence on the tensor cores, one CTA of 8 warps per (b, h, 32 value columns):
 //   E = U - W (S_hi + S_lo)         M = 64 tokens, N = 32, K = 128 keys
 //   S' = a_last S + (w .* k)^T E    M = 128 keys, N = 32, K = 64 tokens
-// Thread t keeps key row t of S (32 fp32 registers).  The next chunk's W, w .* k, U and g are
-// prefetched with cp.async while the current chunk runs.
-constexpr int NQ = 128;  // threads of the recurrence kernels
+// A thread keeps 16 columns of one key row of S in fp32 registers.  The next chunk's W, w .* k
+// (bulk copies), U and g (cp.async) are prefetched while the current chunk runs.
 struct StateFL {
   static constexpr int WB = 0, KW = WB + 2 * C * KD * 2, U = KW + 2 * C * KD * 2, SH = U + 2 * C * VBP * 4,
                        SL = SH + KD * VB * 2, EB = SL + KD * VB * 2, G = EB + C * VB * 2, SC = G + 2 * C * 4,
@@ -354,8 +353,8 @@ __device__ __forceinline__ void ld_row32(uint32_t tbase, float* v) {
   umma::take<16>(r[1], v + 16);
 }
 
-// 8 warps: warp w reads TMEM sub-partition w % 4 and owns value columns 16 (w / 4) .. + 15 of its
-// rows, so each epilogue handles 16 columns per thread.
+// 8 warps (both recurrences): warp w reads TMEM sub-partition w % 4 and owns value columns
+// 16 (w / 4) .. + 15 of its rows, so each epilogue handles 16 columns per thread.
 constexpr int NQF = 256;
 __global__ void __launch_bounds__(NQF, 1) cp_state_fwd(sca2_scan_args p, float* cs, int NS, float* S_final) {
   using L = StateFL;
@@ -739,15 +738,16 @@ __global__ void __launch_bounds__(NT, 3) cp_bprep(sca2_scan_args p, sca2_out dO,
 struct StateBL {
   static constexpr int MB = 0, A2 = MB + 2 * C * KD * 2, Y = A2 + 2 * 2 * C * KD * 2, BS = Y + 2 * C * VBP * 4,
                        YL = BS + 2 * 2 * C * VB * 2, DH = YL + C * VB * 2, DL = DH + KD * VB * 2,
-                       SR = DL + KD * VB * 2, G = SR + 2 * 2 * KD * VBR * 2, SC = G + 2 * C * 4, MBAR = SC + 32,
+                       SR = DL + KD * VB * 2, G = SR + 2 * 2 * KD * VBR * 2, SC = G + 2 * C * 4, MBAR = SC + 48,
                        LBAR = MBAR + 16, TOTAL = LBAR + 16;
 };
 
-__global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out dO, const float* dS_final,
+__global__ void __launch_bounds__(NQF, 1) cp_state_bwd(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                       float* cs, int NS, float* dS0, int dvec) {
   using L = StateBL;
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, sub = warp & 3, c0 = (warp >> 2) * 16;
+  const int m = 32 * sub + lane;  // key row of this thread's adjoint columns
   const int vb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int NC = (p.T + C - 1) / C, n_base = vb * VB;
   bf16* MB = reinterpret_cast<bf16*>(sm + L::MB);
@@ -772,16 +772,16 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     umma::fence_mbar_init();
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 64);
-  float D[VB];  // key row tid of the adjoint state
+  float D[16];  // 16 columns of key row m of the adjoint state
   {
-    const float* src = dS_final ? dS_final + (int64_t)bh * KV + tid * VD + n_base : nullptr;
+    const float* src = dS_final ? dS_final + (int64_t)bh * KV + m * VD + n_base + c0 : nullptr;
 #pragma unroll
-    for (int k = 0; k < VB; k += 4) {
+    for (int k = 0; k < 16; k += 4) {
       const float4 x = src ? *reinterpret_cast<const float4*>(src + k) : make_float4(0.f, 0.f, 0.f, 0.f);
       D[k] = x.x; D[k + 1] = x.y; D[k + 2] = x.z; D[k + 3] = x.w;
     }
 #pragma unroll
-    for (int k = 0; k < VB; k += 8) tc::st8_split(DH, DL, umma::kmaj(tid, k, VB), D + k);
+    for (int k = 0; k < 16; k += 8) tc::st8_split(DH, DL, umma::kmaj(m, c0 + k, VB), D + k);
   }
   uint32_t pend = 0;  // buffers with a bulk load not yet waited for
   auto prefetch = [&](int c) {
@@ -794,13 +794,13 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
       bulk_load(A2 + buf * 2 * C * KD, slot(cs, bh, NS, c, 3) + OFF_A2, 2 * C * KD * 2, lbar + buf);
     }
     float* yd = Yb + buf * C * VBP;
-    for (int u = tid; u < C * VB / 4; u += NQ) {
+    for (int u = tid; u < C * VB / 4; u += NQF) {
       const int i = u >> 3, n = (u & 7) * 4;
       tc::cp16(yd + i * VBP + n, Mg + OFF_U + i * VD + n_base + n, true);
     }
     bf16* dd = BS + buf * 2 * C * VB;
     const bf16* dg = reinterpret_cast<const bf16*>(dO.ptr);
-    for (int u = tid; u < C * VB / 8; u += NQ) {
+    for (int u = tid; u < C * VB / 8; u += NQF) {
       const int i = u >> 2, n = (u & 3) * 8;
       const bool live = i < Cl;
       const bf16* src = dg + (live ? out_off(dO, b, t0 + i, h, 0) + n_base + n : 0);
@@ -812,13 +812,13 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
         for (int k = 0; k < 8; ++k) d[k] = live ? src[k] : __float2bfloat16_rn(0.f);
       }
     }
-    {  // key row tid of the state entering the chunk, this CTA's 32 columns, hi and lo
+    {  // key row m of the state entering the chunk, this thread's 16 columns, hi and lo
       const bf16* sg = reinterpret_cast<const bf16*>(slot(cs, bh, NS, c, 0));
-      bf16* sr = SR + buf * 2 * KD * VBR + tid * VBR;
+      bf16* sr = SR + buf * 2 * KD * VBR + m * VBR + c0;
 #pragma unroll
-      for (int k = 0; k < VB; k += 8) {
-        tc::cp16(sr + k, sg + umma::kmaj(tid, n_base + k, VD), true);
-        tc::cp16(sr + KD * VBR + k, sg + 2 * OFF_LO + umma::kmaj(tid, n_base + k, VD), true);
+      for (int k = 0; k < 16; k += 8) {
+        tc::cp16(sr + k, sg + umma::kmaj(m, n_base + c0 + k, VD), true);
+        tc::cp16(sr + KD * VBR + k, sg + 2 * OFF_LO + umma::kmaj(m, n_base + c0 + k, VD), true);
       }
     }
     prefetch_gates(p, Gb + buf * C, nullptr, b, h, t0, Cl);
@@ -849,11 +849,11 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     {  // the adjoint of the state leaving chunk c (bf16, operand layout), and sum(S_c .* dS')
       bf16* dSg = reinterpret_cast<bf16*>(slot(cs, bh, NS, c, 3));
 #pragma unroll
-      for (int k = 0; k < VB; k += 8) tc::st8(dSg, umma::kmaj(tid, n_base + k, VD), D + k);
-      const bf16* sr = SR + buf * 2 * KD * VBR + tid * VBR;
+      for (int k = 0; k < 16; k += 8) tc::st8(dSg, umma::kmaj(m, n_base + c0 + k, VD), D + k);
+      const bf16* sr = SR + buf * 2 * KD * VBR + m * VBR + c0;
       float sd = 0.f;
 #pragma unroll
-      for (int k = 0; k < VB; k += 8) {
+      for (int k = 0; k < 16; k += 8) {
         float hi[8], lo[8];
         unpack8(sr + k, hi);
         unpack8(sr + KD * VBR + k, lo);
@@ -866,36 +866,39 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     ok = batch_wait(mbar, ph);
     ph ^= 1;
     if (!ok) break;
-    if (tid == 0) slot(cs, bh, NS, c, 1)[OFF_P + vb] = red[0] + red[1] + red[2] + red[3];
-    {
-      uint32_t r[2][16];
-      umma::ld16_issue(umma::taddr(tY, 32 * warp, 0), r[0]);
-      umma::ld16_issue(umma::taddr(tY, 32 * warp, 16), r[1]);
-      umma::ld_wait();
-      float y[VB];
-      umma::take<16>(r[0], y);
-      umma::take<16>(r[1], y + 16);
-      const int i = 16 * warp + (lane & 15);
-      const float4* yr = reinterpret_cast<const float4*>(Yb + buf * C * VBP + i * VBP);
+    if (tid == 0) {
+      float t = 0.f;
 #pragma unroll
-      for (int k = 0; k < VB / 4; ++k) {
+      for (int q = 0; q < NQF / 32; ++q) t += red[q];
+      slot(cs, bh, NS, c, 1)[OFF_P + vb] = t;
+    }
+    {
+      uint32_t r[16];
+      umma::ld16_issue(umma::taddr(tY, 32 * sub, c0), r);
+      umma::ld_wait();
+      float y[16];
+      umma::take<16>(r, y);
+      const int i = 16 * sub + (lane & 15);
+      const float4* yr = reinterpret_cast<const float4*>(Yb + buf * C * VBP + i * VBP + c0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
         const float4 y4 = yr[k];
         y[4 * k] += y4.x; y[4 * k + 1] += y4.y; y[4 * k + 2] += y4.z; y[4 * k + 3] += y4.w;
       }
       if (lane < 16) {
-        float* Yg = slot(cs, bh, NS, c, 2) + OFF_U + i * VD + n_base;
+        float* Yg = slot(cs, bh, NS, c, 2) + OFF_U + i * VD + n_base + c0;
 #pragma unroll
-        for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(Yg + k) = make_float4(y[k], y[k + 1], y[k + 2], y[k + 3]);
+        for (int k = 0; k < 16; k += 4) *reinterpret_cast<float4*>(Yg + k) = make_float4(y[k], y[k + 1], y[k + 2], y[k + 3]);
 #pragma unroll
-        for (int k = 0; k < VB; k += 8) {  // dY hi below dO in the stacked operand, dY lo apart
+        for (int k = 0; k < 16; k += 8) {  // dY hi below dO in the stacked operand, dY lo apart
           float hv[8], lv[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             hv[q] = __bfloat162float(__float2bfloat16_rn(y[k + q]));
             lv[q] = y[k + q] - hv[q];
           }
-          tc::st8(BS + buf * 2 * C * VB, umma::kmaj(C + i, k, VB), hv);
-          tc::st8(YL, umma::kmaj(i, k, VB), lv);
+          tc::st8(BS + buf * 2 * C * VB, umma::kmaj(C + i, c0 + k, VB), hv);
+          tc::st8(YL, umma::kmaj(i, c0 + k, VB), lv);
         }
       }
     }
@@ -909,18 +912,21 @@ __global__ void __launch_bounds__(NQ, 1) cp_state_bwd(sca2_scan_args p, sca2_out
     ok = batch_wait(mbar, ph);
     ph ^= 1;
     if (!ok) break;
-    float acc[VB];
-    ld_row32(tD, acc);
+    uint32_t r[16];
+    umma::ld16_issue(umma::taddr(tD, 32 * sub, c0), r);
+    umma::ld_wait();
+    float acc[16];
+    umma::take<16>(r, acc);
     const float al_ = *aL;
 #pragma unroll
-    for (int k = 0; k < VB; ++k) D[k] = fmaf(al_, D[k], acc[k]);
+    for (int k = 0; k < 16; ++k) D[k] = fmaf(al_, D[k], acc[k]);
 #pragma unroll
-    for (int k = 0; k < VB; k += 8) tc::st8_split(DH, DL, umma::kmaj(tid, k, VB), D + k);
+    for (int k = 0; k < 16; k += 8) tc::st8_split(DH, DL, umma::kmaj(m, c0 + k, VB), D + k);
   }
   if (ok && dS0) {
-    float* dst = dS0 + (int64_t)bh * KV + tid * VD + n_base;
+    float* dst = dS0 + (int64_t)bh * KV + m * VD + n_base + c0;
 #pragma unroll
-    for (int k = 0; k < VB; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(D[k], D[k + 1], D[k + 2], D[k + 3]);
+    for (int k = 0; k < 16; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(D[k], D[k + 1], D[k + 2], D[k + 3]);
   }
   tc::cp_wait_all();
   for (int q = 0; q < 2; ++q)  // after a fault: let issued bulk loads land before the CTA exits (bounded)
@@ -1260,7 +1266,7 @@ cudaError_t cp_scan_bwd(const sca2_scan_args& p, sca2_out dO, const float* dS_fi
   if ((e = set_smem(cp::cp_state_bwd, cp::StateBL::TOTAL)) != cudaSuccess) return e;
   if ((e = set_smem(cp::cp_grads, cp::GradL::TOTAL)) != cudaSuccess) return e;
   cp::cp_bprep<<<gc, cp::NT, cp::BPrepL::TOTAL, st>>>(p, dO, cstates, NS, 1, dvec);
-  cp::cp_state_bwd<<<gs, cp::NQ, cp::StateBL::TOTAL, st>>>(p, dO, dS_final, cstates, NS, gr.dS0, dvec);
+  cp::cp_state_bwd<<<gs, cp::NQF, cp::StateBL::TOTAL, st>>>(p, dO, dS_final, cstates, NS, gr.dS0, dvec);
   cp::cp_grads<<<gc, cp::NT, cp::GradL::TOTAL, st>>>(p, dO, cstates, NS, gr, 1, dvec);
   return cudaGetLastError();
 }
