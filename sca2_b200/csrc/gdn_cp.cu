@@ -500,13 +500,16 @@ __global__ void __launch_bounds__(NQF, 1) cp_state_fwd(sca2_scan_args p, float* 
 // ======================================================================================
 //  F3: outputs O = q_scale (a .* (q S_c) + ((q k^T) .* Dg) E_c)
 // ======================================================================================
+// 73 KB of shared memory (E is fetched into k's place once q k^T is done) and 128 TMEM columns:
+// three CTAs per SM.  The decay a enters as a row scale of q, so q S and P E share one
+// accumulator.
 struct OutL {
-  static constexpr int QB = 0, KB = QB + al(C * KD * 2), SB = KB + al(C * KD * 2), EB = SB + al(KD * VD * 2),
-                       PB = EB + al(C * VD * 2), SC = PB + al(C * C * 2), MBAR = SC + 4 * C * 4,
+  static constexpr int QB = 0, KB = QB + al(C * KD * 2), EB = KB, SB = KB + al(C * KD * 2),
+                       PB = SB + al(KD * VD * 2), SC = PB + al(C * C * 2), MBAR = SC + 4 * C * 4,
                        TOTAL = MBAR + 16;
 };
 
-__global__ void __launch_bounds__(NT, 2) cp_out(sca2_scan_args p, sca2_out o, const float* cs_, int NS, int vec,
+__global__ void __launch_bounds__(NT, 3) cp_out(sca2_scan_args p, sca2_out o, const float* cs_, int NS, int vec,
                                                 int ovec) {
   using L = OutL;
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -531,23 +534,23 @@ __global__ void __launch_bounds__(NT, 2) cp_out(sca2_scan_args p, sca2_out o, co
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
   }
-  if (warp == 0) umma::tmem_alloc(s_tmem, 256);
+  if (warp == 0) umma::tmem_alloc(s_tmem, 128);
   load_rows(QB, reinterpret_cast<const bf16*>(p.phq.ptr), p.phq.sb, p.phq.st, p.phq.sh, b, t0, h, Cl, vec);
   load_rows(KBf, reinterpret_cast<const bf16*>(p.phw.ptr), p.phw.sb, p.phw.st, p.phw.sh, b, t0, h, Cl, vec);
   flat_copy<NT>(SB, slot(cs, bh, NS, c, 0), KD * VD * 2);
-  flat_copy<NT>(EB, slot(cs, bh, NS, c, 1), C * VD * 2);
   tc::cp_commit();
   tc::cp_wait_all();
   tc::publish_smem();
   const uint32_t tb = *s_tmem;
   if (tid == 0) {
-    umma::gemm(tb + 128, QB, KBf, 64, 64, KD, false);            // q k^T
-    umma::gemm_t(tb, QB, false, SB, true, 64, VD, KD, false);    // q S
+    umma::gemm(tb, QB, KBf, 64, 64, KD, false);  // q k^T
     umma::commit(mbar);
   }
   bool ok = batch_wait(mbar, 0);
   if (ok) {
-    tc::for_frag<64, 64>(tb + 128, [&](int i, int j0, int, const float* x) {
+    flat_copy<NT>(EB, slot(cs, bh, NS, c, 1), C * VD * 2);  // over k (read by the product)
+    tc::cp_commit();
+    tc::for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {
       const float gi = gt.Gc[i];
       float y[16];
 #pragma unroll
@@ -559,21 +562,30 @@ __global__ void __launch_bounds__(NT, 2) cp_out(sca2_scan_args p, sca2_out o, co
       tc::st8(PB, umma::kmaj(i, j0, C), y);
       tc::st8(PB, umma::kmaj(i, j0 + 8, C), y + 8);
     });
+    for (int u = tid; u < C * KD / 8; u += NT) {  // q -> a .* q in place
+      const int r = ((u >> 7) << 3) + (u & 7);
+      float xv[8];
+      unpack8(QB + 8 * u, xv);
+      const float f = gt.a[r];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) xv[k] *= f;
+      tc::st8(QB, 8 * u, xv);
+    }
+    tc::cp_wait_all();
     tc::publish_smem();
     if (tid == 0) {
-      umma::gemm_t(tb + 128, PB, false, EB, true, 64, VD, C, false);  // P E
+      umma::gemm_t(tb, QB, false, SB, true, 64, VD, KD, false);  // (a .* q) S
+      umma::gemm_t(tb, PB, false, EB, true, 64, VD, C, true);    // + P E
       umma::commit(mbar);
     }
     ok = batch_wait(mbar, 1);
     if (ok) {
-      const uint32_t bases[2] = {tb, tb + 128};
       bf16* ob = reinterpret_cast<bf16*>(o.ptr);
-      frag_multi<128, 2>(bases, [&](int i, int col0, float (*v)[16]) {
+      tc::for_frag<64, 128>(tb, [&](int i, int col0, int, const float* v) {
         if (i >= Cl) return;
-        const float ai = gt.a[i];
         float y[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = qs * fmaf(ai, v[0][j], v[1][j]);
+        for (int j = 0; j < 16; ++j) y[j] = qs * v[j];
         bf16* dst = ob + out_off(o, b, t0 + i, h, 0) + col0;
         if (ovec) {
           uint4 u0, u1;
@@ -589,9 +601,10 @@ __global__ void __launch_bounds__(NT, 2) cp_out(sca2_scan_args p, sca2_out o, co
     }
   }
   if (!ok) umma::mbar_wait(mbar, 0), umma::mbar_wait(mbar, 1);
+  tc::cp_wait_all();
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tb, 256);
+  if (warp == 0) umma::tmem_dealloc(tb, 128);
 }
 
 // ======================================================================================
