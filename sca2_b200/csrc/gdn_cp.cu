@@ -10,15 +10,15 @@
 //            Dg_ij = e^{min(Gc_i - Gc_j, 0)}, v_eff = beta v (write-gated form) or v):
 //     T  = (I + diag(beta) (k k^T .* Dg)_strict)^{-1}            delta solve, fp32
 //     W  = T diag(beta a) k,   U = T v_eff                         (so E = U - W S)
-//   sequential over c (per 32 value columns, fp32 on the CUDA cores):
+//   sequential over c (per 32 value columns; state in fp32, products on the tensor cores):
 //     E_c = U_c - W_c S_c,   S_{c+1} = a_last S_c + (w .* k)^T E_c
 //   chunk-parallel again:
-//     O = q_scale (a .* (q S_c) + ((q k^T) .* Dg) E_c)
+//     O = q_scale ((a .* q) S_c + ((q k^T) .* Dg) E_c)
 //
 // Backward (dS' = adjoint of the state leaving chunk c, P = q_scale (q k^T) .* Dg):
 //     Yo = T^T P^T dO,   Mt = T^T diag(w) k                        chunk-parallel
 //     dY_c = Yo_c + Mt_c dS',   dS = a_last dS' + q_scale (a .* q)^T dO - (beta a .* k)^T dY_c
-//                                                                  sequential, fp32
+//                                                                  sequential
 //     every per-token gradient of chunk c from (S_c, E_c, dY_c, dS')   chunk-parallel
 //
 // This is the algebra of the reference's chunk closed form (lapa/layer.py:298-366 with the
@@ -38,7 +38,8 @@
 // it), so it can run more than once on one forward's data.
 // The two recurrences also run on the tensor cores: per chunk one product into TMEM for the
 // token rows (E or dY, M = 64) and one for the state rows (M = 128); the state and its adjoint
-// stay in fp32 registers (one key row per thread) and enter the products as hi + lo bf16 pairs.
+// stay in fp32 registers (16 columns of a key row per thread) and enter the products as hi + lo
+// bf16 pairs.
 #include "tc_common.cuh"
 
 namespace sca2 {
