@@ -150,7 +150,7 @@ typedef struct sca2_scan_grads {
  * Replaces torch autograd through the reference's prefill (sca2/arch_damp.py:141-198,
  * lapa/layer.py:298-366). */
 SCA2_API int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
-                  const float* chunk_states, const sca2_scan_grads* gr, void* stream);
+                  float* chunk_states, const sca2_scan_grads* gr, void* stream);
 
 /* Single-token decode step for every (b, h): read S (B,H,K,V) fp32, write the new
  * state to S_out (may equal S_in) and the read o (b,h,r,V).  Per-token inputs use

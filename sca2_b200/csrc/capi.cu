@@ -228,7 +228,7 @@ static bool tc_rows_written(const sca2_scan_args* a, const sca2_tok& dphw, const
 }
 
 int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
-                  const float* chunk_states, const sca2_scan_grads* gr, void* stream) {
+                  float* chunk_states, const sca2_scan_grads* gr, void* stream) {
   int rc = check_scan(a, true);
   if (rc) return rc;
   if (!gr) return fail(SCA2_ERR_ARG, "null gradient struct");
@@ -257,7 +257,7 @@ int sca2_scan_bwd(const sca2_scan_args* a, sca2_out dO, const float* dS_final,
     if (gr->grad_io_dtype && !gr->overwrite)
       return fail(SCA2_ERR_UNSUPPORTED, "dk / dq in the io dtype are written, not accumulated (set overwrite)");
     if (gr->overwrite && (rc = check_overwrite(a, gr))) return rc;
-    cudaError_t e = sca2::cp_scan_bwd(*a, dO, dS_final, const_cast<float*>(chunk_states), *gr,
+    cudaError_t e = sca2::cp_scan_bwd(*a, dO, dS_final, chunk_states, *gr,
                                       sca2::state_slots(a->T), st);
     if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd");
     return SCA2_OK;
@@ -331,7 +331,8 @@ int sca2_scan_bwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_
   if (a->T == 0) {
     cudaError_t e = cudaMemsetAsync(dtheta, 0, (size_t)a->H * Mh * sizeof(float), st);
     if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_bwd_proj(T=0)");
-    return sca2_scan_bwd(a, dO, dS_final, chunk_states, gr, stream);
+    // T = 0 reads and writes no chunk state
+    return sca2_scan_bwd(a, dO, dS_final, const_cast<float*>(chunk_states), gr, stream);
   }
   if (!dO.ptr || !chunk_states || !work) return fail(SCA2_ERR_ARG, "dO, chunk_states and work must be non-null");
   if (!proj_covered(a, pp, true) || !proj_rows_ok(gr->dphw, pp->dtype) || !proj_rows_ok(gr->dphq, pp->dtype))
