@@ -317,10 +317,12 @@ SCA2_API int sca2_short_bwd(const sca2_short_args* a, const float* dO, const flo
  * device memory pool, or a path where cudaMalloc must not be called).  No counterpart
  * in the reference.  Same arguments and gradient contract as sca2_scan_fwd followed by
  * sca2_scan_bwd (the per-token and per-head gradient buffers are accumulated into and
- * must be zero-filled by the caller), minus chunk_states: the state entering each chunk
- * lives in a static device array of SCA2_NOALLOC_SCRATCH_BYTES, so B*H*NC*K*V*4 bytes
- * (NC = sca2_num_chunks(T)) must fit in it; larger problems return SCA2_ERR_ARG before
- * any launch.  The first call on a device looks up the array's device address
+ * must be zero-filled by the caller), minus chunk_states: the buffer that the two-call API
+ * takes from the caller -- sca2_num_chunks(T) slots of K*V fp32 per (b, h), holding the
+ * state entering each chunk, the chunk's saved intermediates and, on the explicit-key
+ * K = V = 128 path, the backward's workspace -- lives in a static device array of
+ * SCA2_NOALLOC_SCRATCH_BYTES, so B*H*sca2_num_chunks(T)*K*V*4 bytes must fit in it; larger
+ * problems return SCA2_ERR_ARG before any launch.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) and must come before any stream capture.  All calls share the
  * array: calls that overlap on the GPU race and must be serialised. */
 SCA2_API int sca2_scan_fwd_bwd_noalloc(const sca2_scan_args* a, sca2_out o, float* S_final,

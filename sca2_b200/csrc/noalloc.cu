@@ -5,9 +5,11 @@
 // workspace -- e.g. a plugin inside a runtime that owns the whole device memory pool
 // (an XLA/JAX process that pre-allocated the GPU, a serving engine with a fixed arena),
 // or code that must not call cudaMalloc on its path.  Such a caller still passes the
-// inputs and the outputs (o, S_final, the gradient buffers); the state entering every
-// chunk, which the backward needs and which the two-call API keeps in a caller buffer,
-// lives here in g_noalloc_chunk_states.
+// inputs and the outputs (o, S_final, the gradient buffers); the chunk-state buffer that the
+// two-call API takes from the caller -- sca2_num_chunks(T) slots of K*V fp32 per (b, h): the
+// state entering every chunk, the chunk's saved intermediates for the backward and, on the
+// explicit-key K = V = 128 path, the backward's workspace -- lives here in
+// g_noalloc_chunk_states.
 //
 // Limits and rules
 //   * The array holds SCA2_NOALLOC_SCRATCH_BYTES (16 MiB) on every GPU that loads this

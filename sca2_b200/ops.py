@@ -446,13 +446,18 @@ def _rows16(x):
     return x.data_ptr() % 16 == 0 and all(s % 8 == 0 for s in x.stride()[:3])
 
 
-@torch.library.custom_op("sca2b200::key_scan_bwd", mutates_args=())
+@torch.library.custom_op("sca2b200::key_scan_bwd", mutates_args=("cs",))
 def _key_scan_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional[torch.Tensor],
                   beta: Optional[torch.Tensor], lam: Optional[torch.Tensor], S0: Optional[torch.Tensor], scale: float,
                   v_times_beta: bool, cs: torch.Tensor, do: torch.Tensor, dS: Optional[torch.Tensor]
                   ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                              torch.Tensor]:
-    """sca2_scan_bwd, key flavour: gradients of (q, k, v, g, beta, lam, S0)."""
+    """sca2_scan_bwd, key flavour: gradients of (q, k, v, g, beta, lam, S0).
+
+    cs is declared mutated: on the chunk-parallel path (bf16, K = V = 128, no lam) the backward
+    uses the slots of the chunk-state buffer that the forward leaves free as its workspace.
+    What the forward saved there is left intact, so the backward may run again on the same
+    buffer (retain_graph)."""
     dt = v.dtype
     q, k, v = _inner(q.to(dt)), _inner(k.to(dt)), _inner(v)
     g, beta = _f32(g), _f32(beta)
@@ -508,12 +513,17 @@ def _(q, k, v, g, beta, lam, S0, scale, v_times_beta, cs, do, dS):
 
 def _key_setup(ctx, inputs, output):
     q, k, v, g, beta, lam, S0, scale, vtb, save = inputs
-    ctx.save_for_backward(q, k, v, g, beta, lam, S0, output[2])
+    ctx.save_for_backward(q, k, v, g, beta, lam, S0)
+    # the chunk-state buffer is kept outside save_for_backward: key_scan_bwd declares it mutated
+    # (its free slots are the backward's workspace), which would otherwise make autograd refuse
+    # a second backward over a retained graph although the saved slots are untouched
+    ctx.cs = output[2].detach()
     ctx.scale, ctx.vtb = scale, vtb
 
 
 def _key_backward(ctx, do, dS, dcs):
-    q, k, v, g, beta, lam, S0, cs = ctx.saved_tensors
+    q, k, v, g, beta, lam, S0 = ctx.saved_tensors
+    cs = ctx.cs
     if do is None:
         do = torch.zeros(*k.shape[:3], v.shape[-1], device=v.device, dtype=v.dtype)
     grads = torch.ops.sca2b200.key_scan_bwd(q, k, v, g, beta, lam, S0, ctx.scale, ctx.vtb, cs, do, dS)
@@ -1082,9 +1092,9 @@ class PhaseStepPlan:
 def phase_scan_fwd_bwd_noalloc(phw, phq, v, beta, g, lam, wr, wi, dO, S0=None, dS=None):
     """Forward and backward of the phase scan in ONE library call that allocates nothing on
     the device and takes no workspace (sca2_scan_fwd_bwd_noalloc): for callers that cannot
-    allocate device memory.  The chunk states live in the library's static 16 MiB device
-    array, so B*H*ceil(T/32)*2Mh*V*4 bytes must fit; calls that overlap on the GPU race on
-    that array.  This wrapper allocates the outputs with torch only for convenience; a caller
+    allocate device memory.  The saved chunk data live in the library's static 16 MiB device
+    array: sca2_num_chunks(T) = 4*ceil(T/64) slots of 2Mh*V fp32 per (b, h), so
+    B*H*4*ceil(T/64)*2Mh*V*4 bytes must fit; calls that overlap on the GPU race on that array.  This wrapper allocates the outputs with torch only for convenience; a caller
     without an allocator passes its own buffers through the C ABI.  Returns
     (o, S, grads dict) with the same meaning as phase_scan + autograd."""
     _check_phase(phw, phq, v, beta, g, lam, wr, wi, S0)

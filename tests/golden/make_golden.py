@@ -575,4 +575,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SCA2_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py /path/to/reference   (or set SCA2_REFERENCE)")
+    main(ref)

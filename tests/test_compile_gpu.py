@@ -30,6 +30,32 @@ def test_opcheck_phase_scan():
                           test_utils=("test_schema", "test_autograd_registration", "test_faketensor"))
 
 
+def test_opcheck_key_scan_bwd_chunk_parallel():
+    """The explicit-key backward at bf16, K = V = 128 writes its workspace into the chunk-state
+    buffer: opcheck's schema test checks that the op declares that mutation."""
+    from sca2_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(2)
+    rn = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    B, T, H, K = 1, 130, 2, 128
+    q = torch.nn.functional.normalize(rn(B, T, H, K), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(rn(B, T, H, K), dim=-1).bfloat16()
+    v = rn(B, T, H, K).bfloat16()
+    gg = -torch.nn.functional.softplus(rn(B, T, H))
+    beta = torch.sigmoid(rn(B, T, H))
+    o, S, cs = torch.ops.sca2b200.key_scan_fwd(q, k, v, gg, beta, None, None, K ** -0.5, True, True)
+    do = rn(B, T, H, K).bfloat16()
+    args = (q, k, v, gg, beta, None, None, K ** -0.5, True, cs, do, None)
+    torch.library.opcheck(torch.ops.sca2b200.key_scan_bwd, args, test_utils=("test_schema", "test_faketensor"))
+    # a second backward over the retained graph reads the forward's saved slots, which the
+    # first backward left intact: it gives the same gradients again
+    vv = v.clone().requires_grad_(True)
+    o2, _ = ops.key_scan(q, k, vv, gg, beta)
+    o2.backward(do, retain_graph=True)
+    g1 = vv.grad.clone()
+    o2.backward(do)
+    assert relerr(vv.grad, 2 * g1) < 1e-2
+
+
 @pytest.mark.parametrize("op", ["rms", "dscan", "short"])
 def test_opcheck_small_ops(op):
     from sca2_b200 import ops  # noqa: F401

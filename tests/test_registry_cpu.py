@@ -10,7 +10,10 @@ import torch
 
 from sca2_b200 import heads, registry
 
-REF = "/root/reference"
+# the reference checkout: SCA2_REFERENCE, else a folder named "reference" beside this
+# repository; the tests skip when neither exists (e.g. on a machine without the sources)
+REF = os.environ.get("SCA2_REFERENCE") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
 
 
 def _ref_registry():

@@ -53,6 +53,83 @@ def test_noalloc_matches_two_call_path(dtype):
                     assert relerr(G[k], rg[k]) < TOL_BF16_ABS and cosine(G[k], rg[k]) > TOL_BF16_COS, (call, k)
 
 
+def test_noalloc_phase_tensor_core_shape():
+    """bf16, K = 2 Mh = 64, V = 64: the tensor-core path (chunk-parallel inversion, saved T, E
+    and P in the shared array)."""
+    from sca2_b200 import ops
+    d = seeded_phase_inputs(1, 200, 2, 32, 64, seed=32, beta=True, g=False, lam=True)
+    ro, rS, rg, t = _two_call(d, torch.bfloat16)
+    for call in range(2):
+        o, S, G = ops.phase_scan_fwd_bwd_noalloc(t["phw"], t["phq"], t["v"], t["beta"], t["g"], t["lam"],
+                                                 t["wr"], t["wi"], cuda(d["dO"], torch.bfloat16), t["S0"],
+                                                 cuda(d["dS"]))
+        torch.cuda.synchronize()
+        assert relerr(o, ro) < TOL_BF16_ABS and cosine(o, ro) > TOL_BF16_COS, call
+        assert relerr(S, rS) < TOL_BF16_ABS and cosine(S, rS) > TOL_BF16_COS, call
+        for k in rg:
+            if rg[k] is not None:
+                assert relerr(G[k], rg[k]) < TOL_BF16_ABS and cosine(G[k], rg[k]) > TOL_BF16_COS, (call, k)
+
+
+def _key_call(lib, a, o, S, cs, do, grads, noalloc):
+    """One forward + backward of the explicit-key scan through the C ABI: the two-call path
+    with a caller chunk-state buffer, or the allocation-free entry point."""
+    from sca2_b200 import _lib, ops
+    st = torch.cuda.current_stream().cuda_stream
+    gr = _lib.ScanGrads()
+    gr.dphw, gr.dphq, gr.dv = ops._tok(grads["k"]), ops._tok(grads["q"]), ops._tok(grads["v"])
+    gr.dbeta, gr.dg = ops._tok(grads["beta"]), ops._tok(grads["g"])
+    gr.dS0 = grads["S0"].data_ptr()
+    gr.overwrite = 1
+    oo, dd = ops._out(o.unsqueeze(3)), ops._out(do.unsqueeze(3))
+    if noalloc:
+        rc = lib.sca2_scan_fwd_bwd_noalloc(ctypes.byref(a), oo, S.data_ptr(), dd, None, ctypes.byref(gr), st)
+        assert rc == 0, lib.sca2_last_error().decode()
+        return
+    assert lib.sca2_scan_fwd(ctypes.byref(a), oo, S.data_ptr(), cs.data_ptr(), st) == 0, lib.sca2_last_error()
+    assert lib.sca2_scan_bwd(ctypes.byref(a), dd, None, cs.data_ptr(), ctypes.byref(gr), st) == 0, \
+        lib.sca2_last_error()
+
+
+def test_noalloc_key_chunk_parallel_shape():
+    """bf16 explicit keys at K = V = 128 (B = 1, H = 2, T = 256: 2 MiB of the array): the
+    chunk-parallel path, whose backward also uses the shared array as its workspace."""
+    from sca2_b200 import _lib, ops
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(33)
+    rn = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    B, T, H, K = 1, 256, 2, 128
+    q = torch.nn.functional.normalize(rn(B, T, H, K), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(rn(B, T, H, K), dim=-1).bfloat16()
+    v = rn(B, T, H, K).bfloat16()
+    gg = -torch.nn.functional.softplus(rn(B, T, H))
+    beta = torch.sigmoid(rn(B, T, H))
+    S0 = 0.3 * rn(B, H, K, K)
+    do = rn(B, T, H, K).bfloat16()
+    a = ops._key_args(q, k, v, gg, beta, None, S0, K ** -0.5, True)
+    need = B * H * lib.sca2_num_chunks(T) * K * K * 4
+    assert need <= _lib.SCA2_NOALLOC_SCRATCH_BYTES
+
+    def buffers():
+        f = lambda *s: torch.empty(*s, device="cuda", dtype=torch.float32)
+        return (torch.empty(B, T, H, K, device="cuda", dtype=torch.bfloat16), f(B, H, K, K),
+                dict(k=f(B, T, H, K), q=f(B, T, H, K), v=torch.empty(B, T, H, K, device="cuda", dtype=torch.bfloat16),
+                     beta=f(B, T, H), g=f(B, T, H), S0=f(B, H, K, K)))
+
+    ro, rS, rg = buffers()
+    cs = torch.empty(B, H, lib.sca2_num_chunks(T), K, K, device="cuda", dtype=torch.float32)
+    _key_call(lib, a, ro, rS, cs, do, rg, noalloc=False)
+    for call in range(2):
+        o, S, G = buffers()
+        _key_call(lib, a, o, S, None, do, G, noalloc=True)
+        torch.cuda.synchronize()
+        assert relerr(o, ro) < TOL_BF16_ABS and cosine(o, ro) > TOL_BF16_COS, call
+        assert relerr(S, rS) < TOL_BF16_ABS and cosine(S, rS) > TOL_BF16_COS, call
+        for name in rg:
+            assert relerr(G[name], rg[name]) < TOL_BF16_ABS and cosine(G[name], rg[name]) > TOL_BF16_COS, \
+                (call, name)
+
+
 def test_noalloc_rejects_oversized_problems():
     """A problem whose chunk states exceed the static array is refused before any launch."""
     from sca2_b200 import _lib, ops
