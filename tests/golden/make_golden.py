@@ -519,6 +519,45 @@ def layer_fixture(gen, kind, B=2, T=45, steps=3):
     return out
 
 
+def config1_fixture():
+    """The first benchmark configuration at its own shape (tests/golden/config1.py): the
+    reference GatedLayer (CHeadGated with 4 heads and decay, DHeadSepQPolar, chunk CTX = 64),
+    built through the shim that drops rope_base / slow_frac, state dict from torch seed 0 with
+    every 2-D weight re-drawn N(0, 0.02^2) and x ~ N(0, 1) by config1.draw, run in float64.
+    Stored: the output y, the final state of both heads and z_prev, the gradient of
+    sum(y * dY) for x and for every C-head parameter, and the state-dict entries that draw()
+    does not regenerate."""
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    import config1 as C1
+    import sca2.arch_gatedc as AG
+    from sca2.ref import LayerCfg
+    orig, ctx = AG.CHeadGated, AG.CHeadGated.CTX
+    AG.CHeadGated.CTX = C1.CHUNK
+    AG.CHeadGated = lambda *a, rope_base=None, slow_frac=None, **kw: orig(*a, **kw)
+    try:
+        torch.manual_seed(C1.SEED)
+        layer = AG.GatedLayer(LayerCfg(**C1.LAYER))
+        sd = layer.state_dict()
+        w, x, dY = C1.draw(sd)
+        sd.update(w)
+        layer.load_state_dict(sd, strict=True)
+        layer = layer.double()
+        xd = x.double().requires_grad_(True)
+        y, st = layer.prefill(xd)
+        (y * dY.double()).sum().backward()
+    finally:
+        AG.CHeadGated = orig
+        orig.CTX = ctx
+    keep = set(C1.redrawn(sd))
+    out = dict(y=_np(y).astype(np.float32), d_x=_np(xd.grad).astype(np.float32),
+               meta=np.array([C1.B, C1.T, C1.LAYER["d"], C1.LAYER["c_heads"], C1.CHUNK]))
+    out.update({"sd_" + k: _np(v) for k, v in layer.state_dict().items() if k not in keep})
+    out.update({"g_" + n: _np(p.grad).astype(np.float32) for n, p in layer.named_parameters()
+                if n.startswith("c.") and p.grad is not None})
+    _tree_np("st", _detach(st), out)
+    return out
+
+
 def _detach(x):
     if isinstance(x, dict):
         return {k: _detach(v) for k, v in x.items()}
@@ -572,6 +611,7 @@ def main(ref_root):
     _save("layer_gated.npz", **layer_fixture(gen, "gated"))
     _save("layer_lapa.npz", **layer_fixture(gen, "lapa"))
     _save("lm_lapa.npz", **lm_fixture(gen))
+    _save("layer_gated_config1.npz", **config1_fixture())
 
 
 if __name__ == "__main__":
