@@ -55,6 +55,8 @@ cudaError_t cp_scan_fwd(const sca2_scan_args& p, sca2_out o, float* S_final, flo
 cudaError_t cp_scan_bwd(const sca2_scan_args& p, sca2_out dO, const float* dS_final, float* cstates,
                         const sca2_scan_grads& gr, int NS, cudaStream_t st);
 cudaError_t cp_read_faults(unsigned int* out);
+// phase_cp.cu
+cudaError_t pcp_read_faults(unsigned int* out);
 // phase_proj.cu
 size_t proj_work_floats(int B, int T, int H, int Mh);
 cudaError_t proj_bwd(int B, int T, int H, int Mh, int dtype, const float* work, const sca2_tok& kh,
@@ -136,13 +138,14 @@ const char* sca2_version(void) { return "sca2b200 0.1.0 (sm_100a)"; }
 int sca2_fault_status(uint32_t* faults) {
   if (!faults) return fail(SCA2_ERR_ARG, "null output");
   unsigned int f = 0;
-  unsigned int fb = 0, fp = 0, fc = 0;
+  unsigned int fb = 0, fp = 0, fc = 0, fq = 0;
   cudaError_t e = sca2::tc_read_faults(&f);
   if (e == cudaSuccess) e = sca2::tc_read_faults_bwd(&fb);
   if (e == cudaSuccess) e = sca2::tc_read_faults_prep(&fp);
   if (e == cudaSuccess) e = sca2::cp_read_faults(&fc);
+  if (e == cudaSuccess) e = sca2::pcp_read_faults(&fq);
   if (e != cudaSuccess) return cuda_fail(e, "sca2_fault_status");
-  *faults = f | fb | fp | fc;
+  *faults = f | fb | fp | fc | fq;
   return SCA2_OK;
 }
 

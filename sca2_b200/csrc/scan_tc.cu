@@ -554,11 +554,18 @@ static int tc_flags(const sca2_scan_args& p, const sca2_out& o) {
 
 cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, const PhaseProj& pp,
                          cudaStream_t st);
+// phase_cp.cu: the chunk-parallel training forward of the phase flavour at K = V = 64
+bool pcp_covers(const sca2_scan_args& p, const float* cstates);
+cudaError_t pcp_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates, int NS,
+                         int flags, const PhaseProj& pp, cudaStream_t st);
 
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
                         float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp) {
   const bool ph = p.flavor == SCA2_FLAVOR_PHASE;
   int fl = tc_flags(p, o);
+  // training of the phase flavour at K = V = 64: chunk-parallel, its saved data in the layout the
+  // tensor-core backward reads
+  if (pcp_covers(p, cstates)) return pcp_scan_fwd(p, o, S_final, cstates, NCS, fl, pp, st);
   if (cstates && ((uintptr_t)cstates & 15u) == 0) fl |= tc::F_CS16;
   if (cstates && p.K == 64) {  // training: T of every chunk from the chunk-parallel kernel
     cudaError_t e = tc_scan_prep(p, cstates, NCS, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), pp, st);

@@ -163,7 +163,10 @@ def test_tc_phase_train(case):
         o, S = run()
         torch.cuda.synchronize()
     names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
-    assert any("scan_fwd_tc" in n for n in names) and any("scan_bwd_tc" in n for n in names), names
+    # training at K = V = 64 runs the chunk-parallel forward (prep, state recurrence, outputs);
+    # other value widths the sequential tensor-core forward
+    fwd = ("pcp_prep", "pcp_state", "pcp_out") if V == 64 else ("scan_fwd_tc",)
+    assert all(any(k in n for n in names) for k in fwd) and any("scan_bwd_tc" in n for n in names), names
     _no_faults()
     ro, rS = ora.phase_forward(d["phw"].astype(np.float64), d["phq"].astype(np.float64), d["v"], d["beta"],
                                d["g"], d["lam"], d["wr"], d["wi"], d["S0"], chunked=True, C=64)
@@ -198,3 +201,35 @@ def test_tc_key_train():
     rg = ora.gdn_backward(q, k, v, g, beta, dO, S0=S0, chunked=True, C=64)
     assert relerr(o, ro) < TOL_BF16_ABS and cosine(o, ro) > TOL_BF16_COS
     _check_grads({n: t[n].grad for n in t}, rg, ("q", "k", "v", "g", "beta", "S0"))
+
+
+def test_chunk_parallel_forward_full_length():
+    """Few sequences of the benchmark's length (B = 1, T = 4096, H = 16: the chunk-parallel
+    training forward) fwd + bwd: two sequences against the oracle at the bf16 bar."""
+    from sca2_b200 import ops
+    B, T, H, Mh, V = 1, 4096, 16, 32, 64
+    d = seeded_phase_inputs(B, T, H, Mh, V, seed=4096, S0=True)
+    d["v"] = _bf16r(d["v"])
+    d["dO"] = _bf16r(d["dO"])
+    t = {k: cuda(d[k], torch.float32, True) for k in ("phw", "phq", "beta", "lam", "wr", "wi", "S0")}
+    t["v"] = cuda(d["v"], torch.bfloat16, True)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        o, S = ops.phase_scan(t["phw"], t["phq"], t["v"], t["beta"], None, t["lam"], t["wr"], t["wi"], t["S0"])
+        ((o.float() * cuda(d["dO"])).sum() + (S * cuda(d["dS"])).sum()).backward()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+    assert any("pcp_state" in n for n in names), names
+    _no_faults()
+    for h in (0, 11):
+        sl = lambda x: None if x is None else x[:, :, h:h + 1]
+        args = (sl(d["phw"]).astype(np.float64), sl(d["phq"]).astype(np.float64), sl(d["v"]), sl(d["beta"]), None,
+                d["lam"][h:h + 1], d["wr"][h:h + 1], d["wi"][h:h + 1], d["S0"][:, h:h + 1])
+        ro, rS = ora.phase_forward(*args, chunked=True, C=64)
+        rg = ora.phase_backward(*args, sl(d["dO"]), d["dS"][:, h:h + 1], chunked=True, C=64)
+        u = rms_np(o[:, :, h:h + 1].detach().double().cpu().numpy().reshape(B, T, 1, -1))
+        ru = rms_np(ro.reshape(B, T, 1, -1))
+        assert np.abs(u - ru).max() < TOL_BF16_ABS and cosine(u, ru) > TOL_BF16_COS, h
+        assert relerr(S[:, h:h + 1], rS) < TOL_BF16_ABS, h
+        got = {k: (None if t[k].grad is None else t[k].grad[:, :, h:h + 1]) for k in ("phw", "phq", "v", "beta")}
+        got["S0"] = t["S0"].grad[:, h:h + 1]
+        _check_grads(got, rg, ("phw", "phq", "v", "beta", "S0"))
