@@ -117,6 +117,15 @@ def _value_dtype(z: torch.Tensor) -> torch.dtype:
     return torch.bfloat16 if z.dtype == torch.bfloat16 else torch.float32
 
 
+def _linear_f32(lin: nn.Linear, x: torch.Tensor) -> torch.Tensor:
+    """lin(x) in float32 whatever the autocast state.  The decay and gate projections feed
+    exponentials whose products run over the whole sequence, so a bf16 rounding of their
+    outputs would compound along it; these projections are a few outputs wide, so float32
+    costs nothing measurable (the state, phases and solve are float32 for the same reason)."""
+    with torch.autocast(device_type=x.device.type, enabled=False):
+        return F.linear(x.float(), lin.weight.float(), None if lin.bias is None else lin.bias.float())
+
+
 def _positions(T: int, pos: torch.Tensor, device) -> torch.Tensor:
     return (torch.arange(T, device=device, dtype=torch.float32) + pos.float())[:, None]
 
@@ -384,7 +393,7 @@ class CHeadGated(CHeadBase):
         return self.K(h).float() * th + p * om, kq.float() * th + p * om
 
     def _logdecay(self, z):
-        return -torch.exp(self.A_log.float()) * F.softplus(self.a(z).float() + self.dt_bias.float())
+        return -torch.exp(self.A_log.float()) * F.softplus(_linear_f32(self.a, z) + self.dt_bias.float())
 
     def prefill(self, z, h, state=None):
         B, T, _ = z.shape
@@ -447,8 +456,8 @@ class DHeadRef(nn.Module):
 
     def _gate(self, h, B, T):
         s2 = 1.0 / math.sqrt(2.0)
-        return (torch.tanh(self.gr(h)).view(B, T, self.M, self.G) * s2,
-                torch.tanh(self.gi(h)).view(B, T, self.M, self.G) * s2)
+        return (torch.tanh(_linear_f32(self.gr, h)).view(B, T, self.M, self.G) * s2,
+                torch.tanh(_linear_f32(self.gi, h)).view(B, T, self.M, self.G) * s2)
 
     def _scan(self, z, h, state):
         B, T, _ = z.shape
@@ -501,15 +510,18 @@ class DHeadSepQ(nn.Module):
 
     def _gate(self, h, B, T):
         s2 = 1.0 / math.sqrt(2.0)
-        return (torch.tanh(self.gr(h)).view(B, T, self.M, self.G) * s2,
-                torch.tanh(self.gi(h)).view(B, T, self.M, self.G) * s2)
+        return (torch.tanh(_linear_f32(self.gr, h)).view(B, T, self.M, self.G) * s2,
+                torch.tanh(_linear_f32(self.gi, h)).view(B, T, self.M, self.G) * s2)
 
     def prefill(self, z, h, state=None):
         B, T, _ = z.shape
         st = state if state is not None else self.init_state(B, z.device)
         a_re, a_im = self._gate(h, B, T)
-        ar, ai = self.qa_r(z), self.qa_i(z)
-        br, bi = self.qb_r(z), self.qb_i(z)
+        # the separable query is normalised per (token, mode) and per (token, channel); the
+        # gradient of q / |q| scales with 1 / |q|, which turns a bf16 rounding of small q into
+        # a large error, so the query projections run in float32 as well
+        ar, ai = _linear_f32(self.qa_r, z), _linear_f32(self.qa_i, z)
+        br, bi = _linear_f32(self.qb_r, z), _linear_f32(self.qb_i, z)
         an = torch.rsqrt(ar.square() + ai.square() + 1e-6)
         bn = torch.rsqrt(br.square() + bi.square() + 1e-6)
         ab, (sr, si) = ops.dscan(a_re, a_im, self.V(z), ar * an, ai * an, (st["sr"], st["si"]), sep=True)
@@ -531,8 +543,8 @@ class DHeadSepQPolar(DHeadSepQ):
     a = exp(-softplus(gr(h))) e^{i gi(h)}."""
 
     def _gate(self, h, B, T):
-        mag = torch.exp(-F.softplus(self.gr(h))).view(B, T, self.M, self.G)
-        ph = self.gi(h).view(B, T, self.M, self.G)
+        mag = torch.exp(-F.softplus(_linear_f32(self.gr, h))).view(B, T, self.M, self.G)
+        ph = _linear_f32(self.gi, h).view(B, T, self.M, self.G)
         return mag * torch.cos(ph), mag * torch.sin(ph)
 
 

@@ -1,5 +1,5 @@
-"""Language model on the layer protocol (lapa/model.py:24-109), a training step, and decoding
-with the whole stack's single-token step captured in one CUDA graph.
+"""Language model on the layer protocol (the role of lapa/model.py:24-109), a training step,
+and decoding with the whole stack's single-token step captured in one CUDA graph.
 
     LM(layer_factory, n_layers, vocab, d, tie_embeddings=False)
         forward(tokens) -> logits; prefill(tokens, state) -> (logits, state);
@@ -25,12 +25,19 @@ from .layers import GatedLayer, LaplaceAttention, LayerCfg
 
 
 class LM(nn.Module):
+    """Token embedding -> a stack of protocol layers -> final LayerNorm -> vocabulary projection.
+
+    Any layer with the prefill / step / init_state protocol stacks here (layer_factory(i)
+    builds layer i).  Parameter names (embed, layers.<i>, norm, head) and the optional tying
+    of the head to the embedding are those of lapa/model.py, so a reference LM's state_dict
+    loads with strict=True; the decode state is the list of the layers' states."""
+
     def __init__(self, layer_factory: Callable[[int], nn.Module], n_layers: int, vocab: int, d: int,
                  tie_embeddings: bool = False):
         super().__init__()
         self.d, self.vocab = d, vocab
         self.embed = nn.Embedding(vocab, d)
-        self.layers = nn.ModuleList([layer_factory(i) for i in range(n_layers)])
+        self.layers = nn.ModuleList(layer_factory(i) for i in range(n_layers))
         self.norm = nn.LayerNorm(d)
         self.head = nn.Linear(d, vocab, bias=False)
         if tie_embeddings:
@@ -39,56 +46,61 @@ class LM(nn.Module):
     def init_state(self, B: int, device) -> List[Dict]:
         return [layer.init_state(B, device) for layer in self.layers]
 
+    def _through(self, x: torch.Tensor, state: List[Dict], method: str):
+        """Run x through every layer's `method` ("prefill" or "step"); the layers' new states."""
+        new = []
+        for layer, st in zip(self.layers, state):
+            x, st = getattr(layer, method)(x, st)
+            new.append(st)
+        return self.head(self.norm(x)), new
+
     def forward(self, tokens: torch.Tensor) -> torch.Tensor:
         return self.prefill(tokens)[0]
 
     def prefill(self, tokens: torch.Tensor, state: Optional[List[Dict]] = None):
-        B = tokens.size(0)
-        st = state if state is not None else self.init_state(B, tokens.device)
-        x = self.embed(tokens)
-        new = []
-        for layer, s in zip(self.layers, st):
-            x, s = layer.prefill(x, s)
-            new.append(s)
-        return self.head(self.norm(x)), new
+        """tokens (B,T) -> logits (B,T,vocab) and the state after the last token."""
+        state = state if state is not None else self.init_state(tokens.size(0), tokens.device)
+        return self._through(self.embed(tokens), state, "prefill")
 
     def step(self, token: torch.Tensor, state: List[Dict]):
-        """token (B,) -> logits (B, vocab)."""
-        x = self.embed(token)
-        new = []
-        for layer, s in zip(self.layers, state):
-            x, s = layer.step(x, s)
-            new.append(s)
-        return self.head(self.norm(x)), new
+        """token (B,) -> logits (B,vocab) and the advanced state."""
+        return self._through(self.embed(token), state, "step")
 
     @torch.no_grad()
     def generate(self, prompt: torch.Tensor, n: int, temperature: float = 1.0, top_k: int = 0,
                  greedy: bool = False) -> torch.Tensor:
-        """prompt (B,T) or (T,) -> (B,T+n) or (T+n,), lapa/model.py:68-95 (eager steps)."""
-        squeeze = prompt.dim() == 1
-        ids = prompt[None] if squeeze else prompt
-        logits, st = self.prefill(ids)
-        out = [ids]
-        nxt = logits[:, -1]
+        """Prefill the prompt ((B,T) or (T,) ids), then n decode steps; returns the prompt with
+        the n new ids appended, in the prompt's layout (the contract of lapa/model.py:68-95)."""
+        ids = prompt if prompt.dim() == 2 else prompt.unsqueeze(0)
+        logits, state = self.prefill(ids)
+        last, picked = logits[:, -1], []
         for _ in range(n):
-            tok = _sample(nxt, temperature, top_k, greedy)
-            out.append(tok[:, None])
-            nxt, st = self.step(tok, st)
-        res = torch.cat(out, 1)
-        return res[0] if squeeze else res
+            tok = next_token(last, temperature, top_k, greedy)
+            picked.append(tok)
+            last, state = self.step(tok, state)
+        out = torch.cat([ids, torch.stack(picked, 1)], 1) if picked else ids
+        return out if prompt.dim() == 2 else out[0]
 
     def layer_params(self) -> int:
         return sum(p.numel() for p in self.layers.parameters())
 
+    def state_floats(self) -> Optional[int]:
+        """Decode-state floats per sequence over all layers, or None when a layer does not
+        report a fixed size."""
+        sizes = [getattr(layer, "state_floats", lambda: None)() for layer in self.layers]
+        return None if any(v is None for v in sizes) else sum(sizes)
 
-def _sample(logits, temperature, top_k, greedy):
+
+def next_token(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0, greedy: bool = False) -> torch.Tensor:
+    """(B, vocab) logits -> (B,) ids: the arg-max when greedy (or temperature <= 0), else a draw
+    from softmax(logits / temperature), restricted to the top_k most likely ids when top_k > 0."""
     if greedy or temperature <= 0:
         return logits.argmax(-1)
-    lg = logits / temperature
-    if top_k:
-        v, _ = lg.topk(min(top_k, lg.size(-1)))
-        lg = lg.masked_fill(lg < v[:, -1:], float("-inf"))
-    return torch.multinomial(F.softmax(lg.float(), -1), 1)[:, 0]
+    probs = torch.softmax(logits.float() / temperature, -1)
+    if not top_k or top_k >= probs.size(-1):
+        return torch.multinomial(probs, 1).squeeze(-1)
+    top_p, top_i = probs.topk(top_k, -1)
+    return top_i.gather(-1, torch.multinomial(top_p, 1)).squeeze(-1)
 
 
 class LaplaceLM(LM):
