@@ -12,10 +12,14 @@ Two levels use this:
     rows (a view, no copy), so a single sequence fills the SMs instead of one CTA per head;
   * across ranks (torch.distributed, NCCL), every rank holds one slab of the sequence;
     the ranks' slab maps are all-gathered (K x (V + K) fp32 per (b, h)) and each rank
-    folds the maps of the ranks before it into its incoming state.
-Then every sub-slab is scanned once more from its true incoming state, which gives the
-outputs.  This is the long-sequence path of lapa/layer.py:298-366 (the same chunk scan
-over a 131072-token sequence), spread over the GPUs of one box.
+    composes the maps of the ranks before it into its incoming state.
+Maps are composed on the device as an inclusive prefix of affine maps in log2(n) rounds of
+batched products.  Then every sub-slab is scanned once more from its true incoming state,
+which gives the outputs.  (The reads are affine in the incoming state as well, and the map
+scan's outputs for the identity columns are their linear part, but those outputs are rounded
+to the values' bf16: a correction built from them missed the bf16 bar, so the outputs come
+from the second scan.)  This is the long-sequence path of lapa/layer.py:298-366 (the same
+chunk scan over a 131072-token sequence), spread over the GPUs of one box.
 """
 from __future__ import annotations
 
@@ -38,15 +42,24 @@ def _slab_map(scan, phw, phq, v, beta, g, lam, wr, wi, sdt):
     return S[..., :V], S[..., V:]
 
 
-def _fold(P, S, S_in):
-    """Incoming states of consecutive segments: S_in(0) = S_in, S_in(s+1) = P_s S_in(s) + S_s.
-    P (n, ..., K, K), S (n, ..., K, V); returns (n, ..., K, V) and the state leaving the last."""
-    out = []
-    cur = S_in
-    for s in range(P.shape[0]):
-        out.append(cur)
-        cur = torch.matmul(P[s], cur) + S[s]
-    return torch.stack(out, 0), cur
+def _compose_prefix(P, S):
+    """Inclusive prefix of affine maps x -> P_s x + S_s over the leading axis (segments in
+    sequence order): (P~_s, S~_s) maps the state entering segment 0 to the state leaving
+    segment s.  log2(n) rounds of batched products (Hillis-Steele), all on the device, no
+    per-segment host loop.  P (n, ..., K, K), S (n, ..., K, V)."""
+    n, o = P.shape[0], 1
+    while o < n:
+        P, S = (torch.cat([P[:o], torch.matmul(P[o:], P[:-o])], 0),
+                torch.cat([S[:o], torch.matmul(P[o:], S[:-o]) + S[o:]], 0))
+        o *= 2
+    return P, S
+
+
+def _entering(Pp, Sp, S_in):
+    """States entering each segment, given the inclusive prefix (Pp, Sp) of the segments' maps
+    and the state entering the first: S_in, then Pp[s - 1] S_in + Sp[s - 1]."""
+    later = torch.matmul(Pp[:-1], S_in.unsqueeze(0)) + Sp[:-1]
+    return torch.cat([S_in.unsqueeze(0), later], 0)
 
 
 def _as_rows(x, split):
@@ -82,18 +95,14 @@ def sp_phase_prefill(phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None,
         raise ValueError(f"slab length {T} is not a multiple of split={split}")
     rows = lambda x: _as_rows(x, split)
     with torch.no_grad():
-        # 1. map of every sub-slab, then of this rank's slab
+        # 1. map of every sub-slab, then of this rank's slab (the prefix over its sub-slabs)
         sdt = state_dtype
         Sr, P = _slab_map(scan, rows(phw), rows(phq), rows(v), rows(beta), rows(g), lam, wr, wi, sdt)
         Sr = Sr.reshape(B, split, H, K, V).transpose(0, 1)   # (split, B, H, K, V)
         P = P.reshape(B, split, H, K, K).transpose(0, 1)     # (split, B, H, K, K)
-        zeros = torch.zeros(B, H, K, V, device=v.device, dtype=sdt)
-        _, slab_S = _fold(P, Sr, zeros)                      # S_r of the slab
-        slab_P = torch.eye(K, device=v.device, dtype=sdt).expand(B, H, K, K)
-        for s in range(split):
-            slab_P = torch.matmul(P[s], slab_P)
+        Pp, Sp = _compose_prefix(P, Sr)
         # 2. exchange the slab maps
-        mine = torch.cat([slab_S, slab_P], -1).contiguous()  # (B, H, K, V + K)
+        mine = torch.cat([Sp[-1], Pp[-1]], -1).contiguous()  # (B, H, K, V + K)
         if world > 1:
             every = [torch.empty_like(mine) for _ in range(world)]
             dist.all_gather(every, mine, group=group)
@@ -101,10 +110,12 @@ def sp_phase_prefill(phw, phq, v, beta=None, g=None, lam=None, wr=None, wi=None,
         else:
             every = mine[None]
         # 3. incoming state of this rank, then of each sub-slab
-        S_first = zeros if S0 is None else S0.to(sdt)
-        S_in_ranks, S_end = _fold(every[..., V:], every[..., :V], S_first)
-        S_in_subs, _ = _fold(P, Sr, S_in_ranks[rank])        # (split, B, H, K, V)
+        S_first = torch.zeros(B, H, K, V, device=v.device, dtype=sdt) if S0 is None else S0.to(sdt)
+        Rp, Rs = _compose_prefix(every[..., V:], every[..., :V])
+        S_end = torch.matmul(Rp[-1], S_first) + Rs[-1]
+        S_rank = _entering(Rp, Rs, S_first)[rank]
+        S_in_subs = _entering(Pp, Sp, S_rank)                # (split, B, H, K, V)
         S_in_rows = S_in_subs.transpose(0, 1).reshape(B * split, H, K, V).contiguous()
-        # 4. outputs from the true incoming states
+        # 4. outputs: every sub-slab scanned again from its true incoming state
         o, _ = scan(rows(phw), rows(phq), rows(v), rows(beta), rows(g), lam, wr, wi, S_in_rows)
     return o.reshape(B, T, *o.shape[2:]), S_end
