@@ -109,6 +109,13 @@ typedef struct sca2_scan_args {
 SCA2_API int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final,
                   float* chunk_states, void* stream);
 
+/* 1 if a training forward (sca2_scan_fwd with a 16-byte aligned chunk_states buffer) of these
+ * arguments runs the chunk-parallel kernels with the value tile of every full 64-token chunk
+ * loaded by one TMA tensor copy (phase flavour, bf16 values, K = V = 64, few sequences,
+ * T % 8 == 0, 16-byte aligned value rows with the batches contiguous), else 0.  A diagnostic:
+ * no counterpart in the reference. */
+SCA2_API int sca2_scan_value_tma(const sca2_scan_args* a);
+
 /* Number of slots of the saved-state buffer for T tokens (four per 64-token chunk: the
  * state entering the chunk, and the chunk's saved intermediates for the backward). */
 SCA2_API int32_t sca2_num_chunks(int32_t T);

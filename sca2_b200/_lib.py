@@ -85,6 +85,7 @@ class DScanGrads(C.Structure):
 # (name, restype, argtypes) of every exported symbol, in header order
 SIGNATURES = [
     ("sca2_scan_fwd", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("sca2_scan_value_tma", C.c_int, [C.POINTER(ScanArgs)]),
     ("sca2_num_chunks", C.c_int32, [C.c_int32]),
     ("sca2_scan_bwd", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, C.c_void_p,
                                 C.POINTER(ScanGrads), C.c_void_p]),

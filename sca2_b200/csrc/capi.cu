@@ -57,6 +57,7 @@ cudaError_t cp_scan_bwd(const sca2_scan_args& p, sca2_out dO, const float* dS_fi
 cudaError_t cp_read_faults(unsigned int* out);
 // phase_cp.cu
 cudaError_t pcp_read_faults(unsigned int* out);
+bool pcp_value_tma(const sca2_scan_args& p, const float* cstates);
 // phase_proj.cu
 size_t proj_work_floats(int B, int T, int H, int Mh);
 cudaError_t proj_bwd(int B, int T, int H, int Mh, int dtype, const float* work, const sca2_tok& kh,
@@ -150,6 +151,12 @@ int sca2_fault_status(uint32_t* faults) {
 }
 
 int32_t sca2_num_chunks(int32_t T) { return T > 0 ? sca2::state_slots(T) : 0; }
+
+int sca2_scan_value_tma(const sca2_scan_args* a) {
+  if (!a || check_scan(a, false) != SCA2_OK) return 0;
+  // any 16-byte aligned address stands for the caller's chunk-state buffer
+  return sca2::pcp_value_tma(*a, reinterpret_cast<const float*>(static_cast<uintptr_t>(256))) ? 1 : 0;
+}
 
 int sca2_scan_fwd(const sca2_scan_args* a, sca2_out o, float* S_final, float* chunk_states,
                   void* stream) {

@@ -39,6 +39,12 @@
 // with every chunk operand single bf16 (the bar is 2e-2).
 // Every mbarrier wait is bounded; on a timeout the CTA sets a fault bit, drains its products
 // and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "tc_common.cuh"
 
 namespace sca2 {
@@ -66,6 +72,23 @@ __device__ __forceinline__ bool batch_wait(uint64_t* mbar, uint32_t parity) {
   umma::fence_after_sync();
   if (bad && threadIdx.x == 0) atomicOr(&g_fault_pcp, 1u);
   return !bad;
+}
+
+// The value tile of a chunk (64 tokens x 64 bf16 values of one (b, h)) by one TMA load: the
+// 5-D tensor map (value % 8, token % 8, value / 8, row / 8, head), row = b T + t, with strides
+// (2 B, st, 16 B, 8 st, sh) traverses the tile in exactly the order of the K-major, no-swizzle
+// tcgen05 operand layout (8 x 8 core matrices of 128 B), so the copy lands in operand layout.
+// Used for full chunks when T % 8 == 0 and the rows of consecutive batches are contiguous
+// (b T + t addresses every row); the box never leaves the tensor.  No cluster multicast.
+__device__ __forceinline__ void tma_value_tile(void* dst, const CUtensorMap* map, int row0, int h, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)),
+               "r"((uint32_t)(C * VD * 2))
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+      ::"r"(umma::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(0), "r"(row0 >> 3), "r"(h),
+        "r"(umma::smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void copy16(uint8_t* dst, const uint8_t* src, int nbytes, int nthr) {
@@ -102,13 +125,14 @@ struct PrepL {
   static constexpr int TS = TB + C * C * 2;        // fp32 C x LDF
   static constexpr int WS = TS + C * LDF * 4;      // fp32 1024
   static constexpr int SC = WS + 1024 * 4;         // beta, Gc, a, w [C], lam [KD]
-  static constexpr int MBAR = SC + (4 * C + KD) * 4;
-  static constexpr int TOTAL = MBAR + 16;
+  static constexpr int MBAR = SC + (4 * C + KD) * 4;  // batch mbarrier, TMEM base, value-tile mbarrier
+  static constexpr int TOTAL = MBAR + 32;
   static_assert(2 * C * KD * 2 <= A_BYTES, "KR and KW fit region A");
   static_assert(TOTAL <= 74 * 1024, "three CTAs per SM");
 };
 
-__global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, int NS, int flags, PhaseProj pp) {
+__global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, int NS, int flags, PhaseProj pp,
+                                                  const __grid_constant__ CUtensorMap vmap, int use_tma) {
   using L = PrepL;
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -135,6 +159,8 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
   float* WS = reinterpret_cast<float*>(sm + L::WS);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
+  uint64_t* vbar = reinterpret_cast<uint64_t*>(sm + L::MBAR + 16);
+  const bool tma = use_tma && Cl == C;  // full chunks take the value tile by TMA
 
   load_head(p, h, s_lam, nullptr, nullptr);
   if (warp == 0) {
@@ -144,10 +170,12 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
   }
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
+    umma::mbar_init(vbar, 1);
     umma::fence_mbar_init();
+    if (tma) tma_value_tile(VA, &vmap, b * p.T + t0, h, vbar);
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 128);
-  tc::pf_values<VD>(p, VA, flags & tc::F_V_VEC, b, h, t0, Cl, 0);
+  if (!tma) tc::pf_values<VD>(p, VA, flags & tc::F_V_VEC, b, h, t0, Cl, 0);
   tc::cp_commit();
   tc::CodeRegs<SCA2_FLAVOR_PHASE, KD> cr;
   tc::load_code_regs<SCA2_FLAVOR_PHASE, KD>(p, cr, flags & tc::F_PH_VEC, b, h, t0, Cl, pp);
@@ -184,13 +212,18 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
     tc::st8(KC, umma::kmaj(i, MH + m0, KD), cs8);
   }
   tc::cp_wait_all();
+  bool ok = !tma || batch_wait(vbar, 0);
+  const bool tma_pending = tma && !ok;  // the tile copy must land before the CTA leaves
+  int inflight = -1;                    // parity of a batch issued and not yet waited for
   tc::publish_smem();
-  if (tid == 0) {
+  if (ok && tid == 0) {
     umma::gemm(tb, KR, KW, 64, 64, KD, false);  // G = KR KW^T
     umma::commit(mbar);
   }
-  bool ok = batch_wait(mbar, 0);
-  uint32_t drain = 0;
+  if (ok) {
+    inflight = 0;
+    if ((ok = batch_wait(mbar, 0))) inflight = -1;
+  }
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {  // L = beta G .* Dg, strict
       const float bi = gt.beta[i] * ik, gi = gt.Gc[i];
@@ -212,8 +245,8 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
     }
     copy16(reinterpret_cast<uint8_t*>(slot(cs, bh, NS, 2 * c + 1)), reinterpret_cast<const uint8_t*>(TB),
            C * C * 2, NT);
-    drain = 1;
-    ok = batch_wait(mbar, 1);
+    inflight = 1;
+    if ((ok = batch_wait(mbar, 1))) inflight = -1;
   }
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int i, int m0, int, const float* x) {
@@ -242,8 +275,8 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
       umma::gemm_t(tb + 64, KCL, true, UB, true, KD, VD, C, true);
       umma::commit(mbar);
     }
-    drain = 0;
-    ok = batch_wait(mbar, 0);
+    inflight = 0;
+    if ((ok = batch_wait(mbar, 0))) inflight = -1;
   }
   if (ok) {
     bf16* Mg = reinterpret_cast<bf16*>(slot(cs, bh, NS, 3 * NC + c));
@@ -261,9 +294,10 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
       float* dg = slot(cs, bh, NS, 3 * NC + c) + KD * KD / 2;
       dg[tid] = gt.a[Cl - 1] * expf(-s_lam[tid] * (float)Cl);
     }
-  } else {
-    umma::mbar_wait(mbar, drain);  // bounded: let the batch in flight finish before freeing TMEM
   }
+  // after a timeout: bounded waits for what is still in flight before TMEM and shared memory go
+  if (inflight >= 0) umma::mbar_wait(mbar, (uint32_t)inflight);
+  if (tma_pending) umma::mbar_wait(vbar, 0);
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tb, 128);
@@ -400,14 +434,14 @@ struct OutL {
   static constexpr int XR = TB + C * C * 2;        // (8 KB, second half of Qa lo)
   static constexpr int EB = ZA, EL = VA, PB = QR, PL = QRL, YB = KW, YL = KWL, QA = KW, QAL = TB;
   static constexpr int SC = XR + C * KD * 2;       // beta, Gc, a, w [C], lam [KD], wr, wi [MH]
-  static constexpr int MBAR = SC + (4 * C + KD + 2 * MH) * 4;
-  static constexpr int TOTAL = MBAR + 16;
+  static constexpr int MBAR = SC + (4 * C + KD + 2 * MH) * 4;  // batch mbarrier, TMEM base, value-tile mbarrier
+  static constexpr int TOTAL = MBAR + 32;
   static_assert(2 * C * KD * 2 == 2 * C * C * 2, "P hi / lo take the places of qr hi / lo");
   static_assert(TOTAL <= 113 * 1024, "two CTAs per SM");
 };
 
 __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, float* cs, int NS, int flags,
-                                                 PhaseProj pp) {
+                                                 PhaseProj pp, const __grid_constant__ CUtensorMap vmap, int use_tma) {
   using L = OutL;
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -440,6 +474,8 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
   bf16* QAL = reinterpret_cast<bf16*>(sm + L::QAL);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
+  uint64_t* vbar = reinterpret_cast<uint64_t*>(sm + L::MBAR + 16);
+  const bool tma = use_tma && Cl == C;  // full chunks take the value tile by TMA
 
   load_head(p, h, s_lam, s_wr, s_wi);
   if (warp == 0) {
@@ -449,10 +485,12 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
   }
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
+    umma::mbar_init(vbar, 1);
     umma::fence_mbar_init();
+    if (tma) tma_value_tile(VA, &vmap, b * p.T + t0, h, vbar);
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 128);
-  tc::pf_values<VD>(p, VA, flags & tc::F_V_VEC, b, h, t0, Cl, 0);
+  if (!tma) tc::pf_values<VD>(p, VA, flags & tc::F_V_VEC, b, h, t0, Cl, 0);
   {
     const uint8_t* tg = reinterpret_cast<const uint8_t*>(slot(cs, bh, NS, 2 * c + 1));
     for (int u = tid; u < C * C * 2 / 16; u += NT) tc::cp16(reinterpret_cast<uint8_t*>(TB) + 16 * u, tg + 16 * u, true);
@@ -509,8 +547,11 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     tc::st8_split(QR, QRL, umma::kmaj(C + ci, MH + cm0, KD), r1b);
   }
   tc::cp_wait_all();
+  bool ok = !tma || batch_wait(vbar, 0);
+  const bool tma_pending = tma && !ok;  // the tile copy must land before the CTA leaves
+  int inflight = -1;                    // parity of a batch issued and not yet waited for
   tc::publish_smem();
-  if (tid == 0) {
+  if (ok && tid == 0) {
     umma::gemm_t(tb, ZA, false, SH, true, 64, VD, KD, false);  // X0 = Z S  [i][v]
     umma::gemm_t(tb, ZA, false, SL, true, 64, VD, KD, true);
     umma::gemm(tb + 64, QR, KW, 2 * 64, C, KD, false);        // P = qr kw^T [(r,i)][j] (codes hi + lo)
@@ -518,8 +559,10 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     umma::gemm(tb + 64, QRL, KW, 2 * 64, C, KD, true);
     umma::commit(mbar);
   }
-  bool ok = batch_wait(mbar, 0);
-  uint32_t drain = 0;
+  if (ok) {
+    inflight = 0;
+    if ((ok = batch_wait(mbar, 0))) inflight = -1;
+  }
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int i, int v0, int, const float* x) {  // Y = v - X0
       float vv[16];
@@ -552,8 +595,8 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     // P for the backward (slot 2 NC + c), while E^T is computed
     copy16(reinterpret_cast<uint8_t*>(slot(cs, bh, NS, 2 * NC + c)), reinterpret_cast<const uint8_t*>(PB),
            2 * C * C * 2, NT);
-    drain = 1;
-    ok = batch_wait(mbar, 1);
+    inflight = 1;
+    if ((ok = batch_wait(mbar, 1))) inflight = -1;
   }
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int v, int i0, int, const float* x) {
@@ -586,8 +629,8 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     // E^T for the backward, after T in slot 2c+1
     copy16(reinterpret_cast<uint8_t*>(slot(cs, bh, NS, 2 * c + 1)) + C * C * 2, reinterpret_cast<const uint8_t*>(EB),
            VD * C * 2, NT);
-    drain = 0;
-    ok = batch_wait(mbar, 0);
+    inflight = 0;
+    if ((ok = batch_wait(mbar, 0))) inflight = -1;
   }
   if (ok) {
     tc::for_frag<2 * 64, 64>(tb + 64, [&](int row, int v0, int, const float* x) {
@@ -604,9 +647,10 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
         }
       }
     });
-  } else {
-    umma::mbar_wait(mbar, drain);
   }
+  // after a timeout: bounded waits for what is still in flight before TMEM and shared memory go
+  if (inflight >= 0) umma::mbar_wait(mbar, (uint32_t)inflight);
+  if (tma_pending) umma::mbar_wait(vbar, 0);
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tb, 128);
@@ -631,21 +675,62 @@ bool pcp_covers(const sca2_scan_args& p, const float* cstates) {
          cstates && ((uintptr_t)cstates & 15u) == 0 && p.T > 0 && (int64_t)p.B * p.H <= PCP_MAX_SEQ;
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no link against
+// the driver library); nullptr where the driver does not provide it
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Tensor map of the value tile (tma_value_tile): v bf16 with 16-byte aligned rows, T % 8 == 0 and
+// rows of consecutive batches contiguous (sb == T st), so row = b T + t addresses every token.
+// false (cp.async copies instead) where these do not hold or the encoder refuses the map.
+static bool value_tile_map(const sca2_scan_args& p, CUtensorMap* map) {
+  const sca2_tok& v = p.v;
+  if (p.T % 8 || v.sb != (int64_t)p.T * v.st || v.st % 8 || v.sh % 8 || ((uintptr_t)v.ptr & 15u)) return false;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[5] = {8, 8, pcp::VD / 8, (cuuint64_t)p.B * p.T / 8, (cuuint64_t)p.H};
+  const cuuint64_t strides[4] = {(cuuint64_t)v.st * 2, 16, (cuuint64_t)v.st * 16, (cuuint64_t)v.sh * 2};
+  const cuuint32_t box[5] = {8, 8, pcp::VD / 8, tc::C / 8, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(v.ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // flags: tc::F_PH_VEC / F_V_VEC / F_O_VEC as computed for the tensor-core forward
 cudaError_t pcp_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates, int NS,
                          int flags, const PhaseProj& pp, cudaStream_t st) {
   const int NC = (p.T + tc::C - 1) / tc::C;
   const int BH = p.B * p.H;
+  alignas(64) CUtensorMap vmap;
+  memset(&vmap, 0, sizeof(vmap));
+  const int use_tma = value_tile_map(p, &vmap) ? 1 : 0;
   cudaError_t e = cudaFuncSetAttribute(pcp::pcp_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, pcp::PrepL::TOTAL);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(pcp::pcp_out, cudaFuncAttributeMaxDynamicSharedMemorySize, pcp::OutL::TOTAL);
   if (e != cudaSuccess) return e;
-  pcp::pcp_prep<<<dim3(NC, BH), tc::NT, pcp::PrepL::TOTAL, st>>>(p, cstates, NS, flags, pp);
+  pcp::pcp_prep<<<dim3(NC, BH), tc::NT, pcp::PrepL::TOTAL, st>>>(p, cstates, NS, flags, pp, vmap, use_tma);
   e = cudaFuncSetAttribute(pcp::pcp_state, cudaFuncAttributeMaxDynamicSharedMemorySize, pcp::StateL::TOTAL);
   if (e != cudaSuccess) return e;
   pcp::pcp_state<<<dim3(BH, pcp::VD / pcp::VBS), pcp::NTS, pcp::StateL::TOTAL, st>>>(p, cstates, NS, S_final);
-  pcp::pcp_out<<<dim3(NC, BH), tc::NT, pcp::OutL::TOTAL, st>>>(p, o, cstates, NS, flags, pp);
+  pcp::pcp_out<<<dim3(NC, BH), tc::NT, pcp::OutL::TOTAL, st>>>(p, o, cstates, NS, flags, pp, vmap, use_tma);
   return cudaGetLastError();
+}
+
+// whether a training forward of these arguments runs chunk-parallel with its value tiles by TMA
+bool pcp_value_tma(const sca2_scan_args& p, const float* cstates) {
+  alignas(64) CUtensorMap map;
+  return pcp_covers(p, cstates) && value_tile_map(p, &map);
 }
 
 // read and clear the device fault word of the chunk-parallel phase kernels (synchronous)

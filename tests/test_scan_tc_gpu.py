@@ -219,6 +219,9 @@ def test_chunk_parallel_forward_full_length():
         torch.cuda.synchronize()
     names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
     assert any("pcp_state" in n for n in names), names
+    from sca2_b200 import _lib
+    a = ops._phase_args(t["phw"], t["phq"], t["v"], t["beta"], None, t["lam"], t["wr"], t["wi"], t["S0"])
+    assert _lib.load().sca2_scan_value_tma(ops.C_ref(a)) == 1  # value tiles came by TMA
     _no_faults()
     for h in (0, 11):
         sl = lambda x: None if x is None else x[:, :, h:h + 1]
