@@ -28,7 +28,7 @@ from __future__ import annotations
 import math
 import os
 from dataclasses import dataclass
-from typing import Dict, Optional, Tuple
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.nn as nn
@@ -124,6 +124,24 @@ def _linear_f32(lin: nn.Linear, x: torch.Tensor) -> torch.Tensor:
     costs nothing measurable (the state, phases and solve are float32 for the same reason)."""
     with torch.autocast(device_type=x.device.type, enabled=False):
         return F.linear(x.float(), lin.weight.float(), None if lin.bias is None else lin.bias.float())
+
+
+def _linear_split(lins: Sequence[nn.Linear], x: torch.Tensor) -> List[torch.Tensor]:
+    """[lin(x) for lin in lins] to about 16 mantissa bits on bf16 tensor cores: x and the
+    stacked weights are each split into bf16 hi + lo parts and the three products hi*hi +
+    hi*lo + lo*hi (fp32 accumulation) are summed in fp32; one product chain for all the
+    projections.  Autocast's plain bf16 projection rounds x and the weight first, which leaves
+    an error of about 2^-9 of the typical output size in every output; where an output is
+    itself small (a query normalised by its length), that error dominates it.  With the split,
+    only each product's own result is rounded: the error is relative to the output."""
+    w = torch.cat([lin.weight for lin in lins], 0).float()
+    xf = x.float()
+    xh, wh = xf.to(torch.bfloat16), w.to(torch.bfloat16)
+    xl, wl = (xf - xh.float()).to(torch.bfloat16), (w - wh.float()).to(torch.bfloat16)
+    with torch.autocast(device_type=x.device.type, enabled=False):
+        y = F.linear(xh, wh).float() + F.linear(xh, wl).float() + F.linear(xl, wh).float()
+    outs = list(y.split([lin.out_features for lin in lins], -1))
+    return [o if lin.bias is None else o + lin.bias.float() for o, lin in zip(outs, lins)]
 
 
 def _positions(T: int, pos: torch.Tensor, device) -> torch.Tensor:
@@ -517,11 +535,14 @@ class DHeadSepQ(nn.Module):
         B, T, _ = z.shape
         st = state if state is not None else self.init_state(B, z.device)
         a_re, a_im = self._gate(h, B, T)
-        # the separable query is normalised per (token, mode) and per (token, channel); the
-        # gradient of q / |q| scales with 1 / |q|, which turns a bf16 rounding of small q into
-        # a large error, so the query projections run in float32 as well
-        ar, ai = _linear_f32(self.qa_r, z), _linear_f32(self.qa_i, z)
-        br, bi = _linear_f32(self.qb_r, z), _linear_f32(self.qb_i, z)
+        # the separable query is normalised per (token, mode) and per (token, channel), and the
+        # gradient of q / |q| scales with 1 / |q|: under autocast the query projections keep
+        # about 16 bits (bf16 hi + lo products), so a small q keeps its relative precision
+        if torch.is_autocast_enabled() and z.is_cuda:
+            ar, ai, br, bi = _linear_split((self.qa_r, self.qa_i, self.qb_r, self.qb_i), z)
+        else:
+            ar, ai = self.qa_r(z), self.qa_i(z)
+            br, bi = self.qb_r(z), self.qb_i(z)
         an = torch.rsqrt(ar.square() + ai.square() + 1e-6)
         bn = torch.rsqrt(br.square() + bi.square() + 1e-6)
         ab, (sr, si) = ops.dscan(a_re, a_im, self.V(z), ar * an, ai * an, (st["sr"], st["si"]), sep=True)
