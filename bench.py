@@ -366,16 +366,19 @@ def run_gpu(args, rank, world, local_rank, dist):
     if not args.no_gdn:
         torch.cuda.empty_cache()
         gd = run_gdn(torch, ops, dev, rank, world, dist)
-    ly = None
+    ly = lt = None
     if not args.no_layer:
         torch.cuda.empty_cache()
         ly = run_layer(torch, dev, rank, world, dist)
+        if world > 1:
+            torch.cuda.empty_cache()
+            lt = run_layer_tp(torch, dev, rank, world, dist)
     lmr = None
     if not args.no_lm:
         torch.cuda.empty_cache()
         lmr = run_lm(torch, dev, rank, world, local_rank, dist)
     return dict(ms_step=ms_step, fwd_ms=fwd_ms, bwd_ms=bwd_ms, zero_ms=zero_ms, clocks=clk, e2e=e2e,
-                decode=decode, sp=sp, dhead=dh, short=sh, gdn=gd, layer=ly, lm=lmr)
+                decode=decode, sp=sp, dhead=dh, short=sh, gdn=gd, layer=ly, layer_tp=lt, lm=lmr)
 
 
 def run_decode(torch, ops, dev, rank, world, dist):
@@ -739,6 +742,31 @@ def run_layer(torch, dev, rank, world, dist, reps=5):
             "params": n_par}
 
 
+def run_layer_tp(torch, dev, rank, world, dist, reps=5):
+    """The GatedLayer of the layer block with its 16 C heads sharded over the N ranks
+    (tensor-parallel heads, sca2_b200.tp) for a batch smaller than N: B = 1, T = 4096, bf16
+    autocast, forward + backward with the sharded gradients summed; time = max over ranks."""
+    from sca2_b200 import layers, lm as L, tp
+    C = LAYER
+    torch.manual_seed(7)  # the same weights on every rank
+    layer = tp.shard_layer(layers.GatedLayer(_gated_cfg(C, C["T"])).to(dev), None)
+    L.init_weights(layer)
+    g = torch.Generator(device=dev).manual_seed(8)
+    x = torch.randn(1, C["T"], C["d"], device=dev, generator=g, requires_grad=True)
+    dy = torch.randn(1, C["T"], C["d"], device=dev, generator=g)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = layer(x)
+        torch.autograd.backward(y, dy)
+        tp.reduce_sharded_grads(layer)
+    ms = _timed(torch, dist, dev, step, reps)
+    return {"value": C["T"] / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "config": {"layer": "GatedLayer, C heads sharded over the ranks", "batch": 1, "seq_len": C["T"],
+                       "d_model": C["d"], "heads": C["heads"], "heads_per_rank": C["heads"] // world,
+                       "ranks": world, "dtype": "bf16 autocast", "fwd+bwd": True}}
+
+
 def run_lm(torch, dev, rank, world, local_rank, dist):
     """12-layer SCA2 LM training step (GatedLM) with AdamW under bf16 autocast, DDP over the
     ranks when N > 1 (gradient all-reduce over NCCL, overlapped with the backward); then
@@ -980,6 +1008,7 @@ def main():
         "short_head": r["short"],
         "gdn_delta": r["gdn"],
         "layer": r["layer"],
+        "layer_tp": r["layer_tp"],
         "lm_train": r["lm"],
     }
     print(json.dumps(line))
