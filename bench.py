@@ -266,16 +266,29 @@ def run_gpu(args, rank, world, local_rank, dist):
     # the current step computes (every step's inputs still cross PCIe inside the timed region).
     e2e = None
     if not args.no_e2e:
-        keys = ("phw", "phq", "v", "beta", "dO")
-        host = {k: x[k].cpu().pin_memory() for k in keys}
+        # The heads' own call: the projections K(h), K(z) in bf16 (theta = 1 per mode, so the phases
+        # K theta + p omega have the workload's distribution) through ops.phase_scan_proj, which
+        # forms the phases inside the kernels and returns dK(h), dK(z).
+        g = torch.Generator(device=dev).manual_seed(4321 + rank)
+        kh = torch.randn(B, T, H, Mh, device=dev, generator=g).bfloat16()
+        kz = torch.randn(B, T, H, Mh, device=dev, generator=g).bfloat16()
+        theta = torch.ones(H, Mh, device=dev)
+        omega = (math.pi * 1e4 ** (-torch.arange(Mh, device=dev, dtype=torch.float32) / (Mh - 1))).expand(H, Mh)
+        omega = omega.contiguous()
+        pos0 = torch.zeros((), device=dev)
+        src = dict(kh=kh, kz=kz, v=x["v"], beta=x["beta"], dO=x["dO"])
+        keys = tuple(src)
+        host = {k: src[k].cpu().pin_memory() for k in keys}
         h2d = sum(t.numel() * t.element_size() for t in host.values())
         # every step's results come back to pinned host memory: the read o, the final state and
-        # the gradients of every per-token input (phi, psi, v, beta)
+        # the gradients of every per-token input (K(h), K(z), v, beta)
         pin = lambda *s, dt=torch.float32: torch.empty(*s, dtype=dt).pin_memory()
-        res = dict(o=pin(B, T, H, 2, V, dt=torch.bfloat16), S=pin(B, H, 2 * Mh, V), phw=pin(B, T, H, Mh),
-                   phq=pin(B, T, H, Mh), v=pin(B, T, H, V, dt=torch.bfloat16), beta=pin(B, T, H))
+        res = dict(o=pin(B, T, H, 2, V, dt=torch.bfloat16), S=pin(B, H, 2 * Mh, V),
+                   kh=pin(B, T, H, Mh, dt=torch.bfloat16), kz=pin(B, T, H, Mh, dt=torch.bfloat16),
+                   v=pin(B, T, H, V, dt=torch.bfloat16), beta=pin(B, T, H))
         d2h = sum(t.numel() * t.element_size() for t in res.values())
-        bufs = [{k: torch.empty_like(x[k]) for k in keys} for _ in range(2)]
+        bufs = [{k: torch.empty_like(src[k]) for k in keys} for _ in range(2)]
+        del kh, kz, src
         cs = torch.cuda.Stream(device=dev)
         ds = torch.cuda.Stream(device=dev)  # device -> host copies of the results
         ready = [torch.cuda.Event() for _ in range(2)]
@@ -295,11 +308,12 @@ def run_gpu(args, rank, world, local_rank, dist):
             sl = i % 2
             st.wait_event(ready[sl])
             d = dict(bufs[sl])
-            for k in ("phw", "phq", "v", "beta"):
+            for k in ("kh", "kz", "v", "beta"):
                 d[k] = d[k].detach().requires_grad_(True)  # leaf over the buffer's storage
-            o, S = ops.phase_scan(d["phw"], d["phq"], d["v"], d["beta"], None, x["lam"], x["wr"], x["wi"])
+            o, S = ops.phase_scan_proj(d["kh"], d["kz"], theta, omega, pos0, d["v"], d["beta"], None, x["lam"],
+                                       x["wr"], x["wi"])
             torch.autograd.backward(o, d["dO"])
-            out = dict(o=o.detach(), S=S.detach(), phw=d["phw"].grad, phq=d["phq"].grad, v=d["v"].grad,
+            out = dict(o=o.detach(), S=S.detach(), kh=d["kh"].grad, kz=d["kz"].grad, v=d["v"].grad,
                        beta=d["beta"].grad)
             done = torch.cuda.Event()
             done.record(st)
@@ -338,8 +352,9 @@ def run_gpu(args, rank, world, local_rank, dist):
             em = float(t.item())
         e2e = {"value": world * B * T / (em / 1e3), "unit": "tokens/s", "ms_per_step": em,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "api": "ops.phase_scan + torch.autograd.backward (fp32 phases, bf16 v / dO)",
-               "copied_out": "o, S, d phi, d psi, dv, d beta",
+               "api": "ops.phase_scan_proj + torch.autograd.backward (the heads' call: bf16 K(h), K(z), v, dO; "
+                      "fp32 beta; phases formed in the kernels)",
+               "copied_out": "o, S, dK(h), dK(z), dv, d beta",
                "pipelining": "next step's H2D on a copy stream and the previous step's D2H on another "
                              "overlap the current step's compute"}
         del host, bufs
