@@ -24,7 +24,8 @@
 //              M (bf16, operand layout) with d to slot 3 NC + c.
 //   pcp_state  one CTA of 4 warps per (b, h, 32 value columns), sequential over chunks: the
 //              state in fp32 registers, M S as one tcgen05 product per chunk with the state
-//              split hi + lo, the M, B, d of the chunk two ahead copied in meanwhile.  Writes the state
+//              split hi + lo (stacked along N), the M, B, d of the chunk two ahead copied in
+//              meanwhile.  Writes the state
 //              entering chunk c over B_c in slot 2c, and the final state.
 //   pcp_out    one CTA per (b, h, chunk), two per SM: E = T (v - Z S) and O = Qa S + P E
 //              (tcgen05), the outputs, and E^T and P (hi parts) for the backward (slot 2c+1
@@ -307,14 +308,17 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
 //  pcp_state: S' = d .* S - M S + B over the chunks of one (b, h, 32 value columns)
 // ======================================================================================
 // NSTG stages of (M, B, d): chunk c + 2 is copied in while chunk c runs, so a copy has two
-// chunk steps (a few microseconds) to arrive.
+// chunk steps to arrive.  The state enters its product as [S hi | S lo] stacked along N (one
+// 64 x 64 x 64 product, the two halves summed after), the B rows are padded by 4 floats (rows
+// of 8 consecutive key rows fall in distinct bank groups), and the issuing thread does not
+// take part in the copies (it is on the chain's critical path).
 constexpr int NSTG = 3;
+constexpr int BSR = VBS + 4;  // padded fp32 row of a stage's B
 struct StateL {
-  static constexpr int MA = 0;                         // NSTG x M (bf16 KD x KD, operand layout)
-  static constexpr int BS = MA + NSTG * KD * KD * 2;   // NSTG x B (fp32 KD x VBS)
-  static constexpr int SH = BS + NSTG * KD * VBS * 4;  // S hi (bf16 [m][v], read MN-major)
-  static constexpr int SL = SH + KD * VBS * 2;         // S lo
-  static constexpr int DS = SL + KD * VBS * 2;         // NSTG x d [KD]
+  static constexpr int MA = 0;                          // NSTG x M (bf16 KD x KD, operand layout)
+  static constexpr int BS = MA + NSTG * KD * KD * 2;    // NSTG x B (fp32 KD x BSR)
+  static constexpr int SB = BS + NSTG * KD * BSR * 4;   // [S hi | S lo] (bf16 [m][2 VBS], read MN-major)
+  static constexpr int DS = SB + KD * 2 * VBS * 2;      // NSTG x d [KD]
   static constexpr int MBAR = DS + NSTG * KD * 4;
   static constexpr int TOTAL = MBAR + 16;
 };
@@ -325,29 +329,30 @@ __global__ void __launch_bounds__(NTS) pcp_state(sca2_scan_args p, float* cs, in
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, vb0 = blockIdx.y * VBS;
   const int NC = (p.T + C - 1) / C;
-  bf16* SH = reinterpret_cast<bf16*>(sm + L::SH);
-  bf16* SL = reinterpret_cast<bf16*>(sm + L::SL);
+  bf16* SB = reinterpret_cast<bf16*>(sm + L::SB);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   // rows of the M = 64 accumulator: warp w's sub-partition, lanes < 16 hold rows 16 w + lane
   const bool own = lane < 16;
   const int m = 16 * warp + (lane & 15);
 
-  // copy chunk cc's M, B (this CTA's columns) and d into stage cc % NSTG; always one commit
-  // group per call (empty past the last chunk) so that the wait_group counts stay uniform
+  // copy chunk cc's M, B (this CTA's columns) and d into stage cc % NSTG, spread over threads
+  // 1..NTS-1; every thread commits one group per call (empty past the last chunk or for the
+  // issuing thread) so that the wait_group counts stay uniform
   auto prefetch = [&](int cc) {
-    if (cc < NC) {
-      const int st = cc % NSTG;
+    if (cc < NC && tid > 0) {
+      const int st = cc % NSTG, w = tid - 1;
+      constexpr int NW = NTS - 1;
       const uint8_t* mg = reinterpret_cast<const uint8_t*>(slot(cs, bh, NS, 3 * NC + cc));
       uint8_t* ma = sm + L::MA + st * KD * KD * 2;
-      for (int u = tid; u < KD * KD * 2 / 16; u += NTS) tc::cp16(ma + 16 * u, mg + 16 * u, true);
+      for (int u = w; u < KD * KD * 2 / 16; u += NW) tc::cp16(ma + 16 * u, mg + 16 * u, true);
       const float* bg = slot(cs, bh, NS, 2 * cc) + vb0;
-      float* bs = reinterpret_cast<float*>(sm + L::BS) + st * KD * VBS;
-      for (int u = tid; u < KD * VBS / 4; u += NTS) {
+      float* bs = reinterpret_cast<float*>(sm + L::BS) + st * KD * BSR;
+      for (int u = w; u < KD * VBS / 4; u += NW) {
         const int r = u / (VBS / 4), c4 = (u % (VBS / 4)) * 4;
-        tc::cp16(bs + r * VBS + c4, bg + r * VD + c4, true);
+        tc::cp16(bs + r * BSR + c4, bg + r * VD + c4, true);
       }
-      if (tid < KD / 4) tc::cp16(sm + L::DS + st * KD * 4 + 16 * tid, mg + KD * KD * 2 + 16 * tid, true);
+      if (w < KD / 4) tc::cp16(sm + L::DS + st * KD * 4 + 16 * w, mg + KD * KD * 2 + 16 * w, true);
     }
     tc::cp_commit();
   };
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(NTS) pcp_state(sca2_scan_args p, float* cs, in
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
   }
-  if (warp == 0) umma::tmem_alloc(s_tmem, 32);
+  if (warp == 0) umma::tmem_alloc(s_tmem, 2 * VBS);
   for (int k = 0; k < NSTG - 1; ++k) prefetch(k);
   umma::fence_before_sync();
   __syncthreads();
@@ -373,35 +378,52 @@ __global__ void __launch_bounds__(NTS) pcp_state(sca2_scan_args p, float* cs, in
     tc::cp_wait_group<NSTG - 2>();  // this thread's copies of chunk c have landed
     if (own)
 #pragma unroll
-      for (int v0 = 0; v0 < VBS; v0 += 8) tc::st8_split(SH, SL, umma::kmaj(m, v0, VBS), S + v0);
+      for (int v0 = 0; v0 < VBS; v0 += 8) {
+        float h[8], l[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          h[k] = __bfloat162float(__float2bfloat16_rn(S[v0 + k]));
+          l[k] = S[v0 + k] - h[k];
+        }
+        tc::st8(SB, umma::kmaj(m, v0, 2 * VBS), h);
+        tc::st8(SB, umma::kmaj(m, VBS + v0, 2 * VBS), l);
+      }
     tc::publish_smem();  // every thread's copies of chunk c and its S operand are visible
+    if (tid == 0) {
+      const bf16* ma = reinterpret_cast<const bf16*>(sm + L::MA + st * KD * KD * 2);
+      umma::gemm_t(tb, ma, false, SB, true, KD, 2 * VBS, KD, false);  // M [S hi | S lo]
+      umma::commit(mbar);
+    }
     if (own) {
       // the state entering chunk c replaces B_c in slot 2c: every copy of B_c has landed (above)
       float4* dst = reinterpret_cast<float4*>(slot(cs, bh, NS, 2 * c) + m * VD + vb0);
 #pragma unroll
       for (int k = 0; k < VBS / 4; ++k) dst[k] = make_float4(S[4 * k], S[4 * k + 1], S[4 * k + 2], S[4 * k + 3]);
     }
-    if (tid == 0) {
-      const bf16* ma = reinterpret_cast<const bf16*>(sm + L::MA + st * KD * KD * 2);
-      umma::gemm_t(tb, ma, false, SH, true, KD, VBS, KD, false);  // M S  (S = hi + lo)
-      umma::gemm_t(tb, ma, false, SL, true, KD, VBS, KD, true);
-      umma::commit(mbar);
-    }
     prefetch(c + NSTG - 1);  // into the stage of chunk c - 1, whose reads ended before the barrier
     if (!(ok = batch_wait(mbar, phase))) break;
     phase ^= 1u;
-    uint32_t r0[16], r1[16];
-    umma::ld16_issue(umma::taddr(tb, 32 * warp, 0), r0);
-    umma::ld16_issue(umma::taddr(tb, 32 * warp, 16), r1);
+    uint32_t r[4][16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) umma::ld16_issue(umma::taddr(tb, 32 * warp, 16 * q), r[q]);
     umma::ld_wait();
-    float x[VBS];
-    umma::take<16>(r0, x);
-    umma::take<16>(r1, x + 16);
+    float x[2 * VBS];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) umma::take<16>(r[q], x + 16 * q);
     if (own) {
       const float d = reinterpret_cast<const float*>(sm + L::DS)[st * KD + m];
-      const float* bs = reinterpret_cast<const float*>(sm + L::BS) + st * KD * VBS + m * VBS;
+      const float4* bs = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(sm + L::BS) +
+                                                         st * KD * BSR + m * BSR);
 #pragma unroll
-      for (int j = 0; j < VBS; ++j) S[j] = fmaf(d, S[j], bs[j] - x[j]);
+      for (int k = 0; k < VBS / 4; ++k) {
+        const float4 b4 = bs[k];
+        const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 4 * k + e;
+          S[j] = fmaf(d, S[j], bb[e] - (x[j] + x[VBS + j]));
+        }
+      }
     }
     umma::fence_before_sync();
   }
@@ -414,7 +436,7 @@ __global__ void __launch_bounds__(NTS) pcp_state(sca2_scan_args p, float* cs, in
   }
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tb, 32);
+  if (warp == 0) umma::tmem_dealloc(tb, 2 * VBS);
 }
 
 // ======================================================================================
