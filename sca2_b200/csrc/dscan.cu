@@ -204,20 +204,94 @@ __device__ __forceinline__ Map thread_map_c(const sca2_dscan_args& p) {
   return r;
 }
 
+// Gate groups a CTA's channels can touch: its 256 / M channels in groups of gs = V / G
+__host__ __device__ inline int ngl_max(int M, int gs) { return (NT / M) / gs + 2; }
+
+// Inputs of one 16-token block for a CTA's channels [j0, j0 + 256 / M), staged in shared memory
+// with coalesced loads before the dependent passes: v and dab [CK][JC] per token row, the gates
+// of the groups those channels touch [CK][M][NGL][re, im] and the separable read factor
+// [CK][M][re, im] (each part on request); zeros past the sequence, the value width or the gate
+// groups.
+template <int M>
+struct Stage {
+  static constexpr int JC = NT / M;
+  float *v, *d, *a, *c;
+  int g0, ngl;
+  __host__ __device__ static constexpr int floats(int ngl) { return CK * JC * 3 + CK * M * ngl * 2 + CK * M * 2; }
+  __device__ void load(const sca2_dscan_args& p, const float* dab, int b, int t0, int n, int j0, float* base,
+                       int ngl_max, bool with_v = true, bool with_c = true) {
+    const int V = p.V, G = p.G, gs = V / G;
+    ngl = ngl_max;
+    g0 = j0 / gs;
+    v = base;
+    d = v + CK * JC;
+    a = d + 2 * CK * JC;
+    c = a + CK * M * ngl * 2;
+    const int64_t bT = (int64_t)b * p.T;
+    for (int u = threadIdx.x; u < CK * JC; u += NT) {
+      const int t = u / JC, jl = u % JC, j = j0 + jl;
+      const bool live = t < n && j < V;
+      const int64_t row = bT + t0 + t;
+      if (with_v) v[u] = live ? p.v[row * V + j] : 0.f;
+      if (dab) {
+        d[t * 2 * JC + jl] = live ? dab[(row * 2) * V + j] : 0.f;
+        d[t * 2 * JC + JC + jl] = live ? dab[(row * 2 + 1) * V + j] : 0.f;
+      }
+    }
+    for (int u = threadIdx.x; u < CK * M * ngl; u += NT) {
+      const int gl = u % ngl, tm = u / ngl, t = tm / M, m = tm % M, g = g0 + gl;
+      const bool live = t < n && g < G;
+      const int64_t idx = ((bT + t0 + t) * M + m) * G + g;
+      a[2 * u] = live ? p.a_re[idx] : 0.f;
+      a[2 * u + 1] = live ? p.a_im[idx] : 0.f;
+    }
+    for (int u = threadIdx.x; with_c && u < CK * M; u += NT) {
+      const int t = u / M;
+      const int64_t idx = (bT + t0 + t) * M + (u % M);
+      c[2 * u] = t < n ? p.c_re[idx] : 0.f;
+      c[2 * u + 1] = t < n ? p.c_im[idx] : 0.f;
+    }
+  }
+  __device__ float2 gate(int t, int m, int g) const {
+    const float* q = a + ((t * M + m) * ngl + (g - g0)) * 2;
+    return make_float2(q[0], q[1]);
+  }
+};
+
+// The folds reduce nothing over rows and read no per-token input, so their threads take channels
+// fastest: their loads and stores of the [M][V] planes coalesce.  `blk` is the grid index that
+// enumerates (m, j) tiles of NT threads.
+template <int M>
+__device__ __forceinline__ Map chan_map(const sca2_dscan_args& p, int blk) {
+  Map r;
+  const int idx = blk * NT + threadIdx.x;
+  r.b = blockIdx.x;
+  r.m = idx / p.V;
+  r.j = idx - r.m * p.V;
+  r.jj = 0;
+  r.live = r.m < M;
+  if (!r.live) r.m = M - 1, r.j = 0;  // idle threads of the last tile read row M - 1, channel 0
+  r.g = r.j / (p.V / p.G);
+  return r;
+}
+
 // complex product of a block's gates, kept per (b, k, m, g) by the group's first channel
 template <int M>
 __global__ void __launch_bounds__(NT) dscan_fwd_local(sca2_dscan_args p, float* e, float* P) {
+  extern __shared__ float sst[];
   const Map q = thread_map_c<M>(p);
   const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
   const int t0 = k * CK, n = min(CK, T - t0);
-  const int jc = q.live ? q.j : 0;
-  const int64_t bT = (int64_t)q.b * T;
+  Stage<M> sg;
+  sg.load(p, nullptr, q.b, t0, n, blockIdx.z * (NT / M), sst, ngl_max(M, V / G), true, false);
+  __syncthreads();
+  const int jl = q.j - blockIdx.z * (NT / M), gq = q.live ? q.g : sg.g0;
   float sr = 0.f, si = 0.f, pr = 1.f, pi = 0.f;
 #pragma unroll 4
   for (int u = 0; u < n; ++u) {
-    const int64_t tm = (bT + t0 + u) * M + q.m;
-    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
-    const float vt = p.v[(bT + t0 + u) * V + jc];
+    const float2 a = sg.gate(u, q.m, gq);
+    const float ar = a.x, ai = a.y;
+    const float vt = sg.v[u * Stage<M>::JC + jl];
     const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
     si = fmaf(ar, si, ai * sr);
     sr = nr;
@@ -235,25 +309,39 @@ __global__ void __launch_bounds__(NT) dscan_fwd_local(sca2_dscan_args p, float* 
   }
 }
 
-// fold over the blocks (sequential per (b, m, j)): checkpoints and the final state
+// fold over the blocks (sequential per (b, m, j)): checkpoints and the final state.  The fold's
+// inputs are loaded CU blocks at a time into registers before the dependent updates, so a
+// thread waits for one round of loads per CU blocks instead of one per block.
+constexpr int CU = 16;
 template <int M>
-__global__ void __launch_bounds__(NT) dscan_fwd_carry(sca2_dscan_args p, const float* e, const float* P, float* ckpt,
+__global__ void __launch_bounds__(NT) dscan_fwd_carry(sca2_dscan_args p, const float* __restrict__ e,
+                                                     const float* __restrict__ P, float* __restrict__ ckpt,
                                                      float* S_re, float* S_im) {
-  const Map q = thread_map<M>(p);
+  const Map q = chan_map<M>(p, blockIdx.y);
   if (!q.live) return;
   const int V = p.V, G = p.G, NK = (p.T + CK - 1) / CK;
   const int64_t sidx = ((int64_t)q.b * M + q.m) * V + q.j;
   float sr = p.S0_re ? p.S0_re[sidx] : 0.f, si = p.S0_im ? p.S0_im[sidx] : 0.f;
-#pragma unroll 8
-  for (int k = 0; k < NK; ++k) {
-    const int64_t base = ((int64_t)q.b * NK + k) * 2;
-    ckpt[base * M * V + (int64_t)q.m * V + q.j] = sr;
-    ckpt[(base + 1) * M * V + (int64_t)q.m * V + q.j] = si;
-    const float pr = P[base * M * G + (int64_t)q.m * G + q.g], pi = P[(base + 1) * M * G + (int64_t)q.m * G + q.g];
-    const float er = e[base * M * V + (int64_t)q.m * V + q.j], ei = e[(base + 1) * M * V + (int64_t)q.m * V + q.j];
-    const float nr = pr * sr - pi * si + er;
-    si = pr * si + pi * sr + ei;
-    sr = nr;
+  for (int k0 = 0; k0 < NK; k0 += CU) {
+    float pr[CU], pi[CU], er[CU], ei[CU];
+#pragma unroll
+    for (int u = 0; u < CU; ++u) {
+      const int64_t base = ((int64_t)q.b * NK + min(k0 + u, NK - 1)) * 2;
+      pr[u] = P[base * M * G + (int64_t)q.m * G + q.g];
+      pi[u] = P[(base + 1) * M * G + (int64_t)q.m * G + q.g];
+      er[u] = e[base * M * V + (int64_t)q.m * V + q.j];
+      ei[u] = e[(base + 1) * M * V + (int64_t)q.m * V + q.j];
+    }
+#pragma unroll
+    for (int u = 0; u < CU; ++u) {
+      if (k0 + u >= NK) break;
+      const int64_t base = ((int64_t)q.b * NK + k0 + u) * 2;
+      ckpt[base * M * V + (int64_t)q.m * V + q.j] = sr;
+      ckpt[(base + 1) * M * V + (int64_t)q.m * V + q.j] = si;
+      const float nr = pr[u] * sr - pi[u] * si + er[u];
+      si = pr[u] * si + pi[u] * sr + ei[u];
+      sr = nr;
+    }
   }
   S_re[sidx] = sr;
   S_im[sidx] = si;
@@ -262,21 +350,37 @@ __global__ void __launch_bounds__(NT) dscan_fwd_carry(sca2_dscan_args p, const f
 // every block from its incoming state: the read
 template <int M, bool SEP>
 __global__ void __launch_bounds__(NT) dscan_fwd_out(sca2_dscan_args p, const float* ckpt, float* ab) {
+  extern __shared__ float sst[];
   const Map q = thread_map_c<M>(p);
   const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
   const int t0 = k * CK, n = min(CK, T - t0);
   const int jc = q.live ? q.j : 0;
   const int64_t bT = (int64_t)q.b * T;
   const int64_t base = ((int64_t)q.b * NK + k) * 2;
+  Stage<M> sg;
+  if (SEP) {  // separable read: the block's inputs staged once, coalesced
+    sg.load(p, nullptr, q.b, t0, n, blockIdx.z * (NT / M), sst, ngl_max(M, V / G));
+    __syncthreads();
+  }
+  const int jl = q.j - blockIdx.z * (NT / M);
   float sr = ckpt[base * M * V + (int64_t)q.m * V + jc], si = ckpt[(base + 1) * M * V + (int64_t)q.m * V + jc];
 #pragma unroll 4
   for (int u = 0; u < n; ++u) {
     const int t = t0 + u;
     const int64_t tm = (bT + t) * M + q.m;
-    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
-    const float vt = p.v[(bT + t) * V + jc];
-    const float cr = SEP ? p.c_re[tm] : p.c_re[tm * V + jc];
-    const float ci = SEP ? p.c_im[tm] : p.c_im[tm * V + jc];
+    float ar, ai, vt, cr, ci;
+    if (SEP) {
+      const float2 a = sg.gate(u, q.m, q.live ? q.g : sg.g0);
+      ar = a.x, ai = a.y;
+      vt = sg.v[u * Stage<M>::JC + jl];
+      cr = sg.c[(u * M + q.m) * 2];
+      ci = sg.c[(u * M + q.m) * 2 + 1];
+    } else {
+      ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+      vt = p.v[(bT + t) * V + jc];
+      cr = p.c_re[tm * V + jc];
+      ci = p.c_im[tm * V + jc];
+    }
     const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
     si = fmaf(ar, si, ai * sr);
     sr = nr;
@@ -292,21 +396,28 @@ __global__ void __launch_bounds__(NT) dscan_fwd_out(sca2_dscan_args p, const flo
 // adjoint of a block from zero at its end: q (to the left) and Q = prod conj(a)
 template <int M, bool SEP>
 __global__ void __launch_bounds__(NT) dscan_bwd_local(sca2_dscan_args p, const float* dab, float* qv, float* Qg) {
+  extern __shared__ float sst[];
   const Map q = thread_map_c<M>(p);
   const int k = blockIdx.y, NK = gridDim.y, T = p.T, V = p.V, G = p.G;
   const int t0 = k * CK, n = min(CK, T - t0);
   const int jc = q.live ? q.j : 0;
   const int64_t bT = (int64_t)q.b * T;
   constexpr float iM = 1.f / M;
+  constexpr int JC = Stage<M>::JC;
+  Stage<M> sg;
+  sg.load(p, dab, q.b, t0, n, blockIdx.z * JC, sst, ngl_max(M, V / G), false, SEP);
+  __syncthreads();
+  const int jl = q.j - blockIdx.z * JC, gq = q.live ? q.g : sg.g0;
   float dr = 0.f, di = 0.f, Pr = 1.f, Pi = 0.f;
 #pragma unroll 4
   for (int u = n - 1; u >= 0; --u) {
     const int t = t0 + u;
     const int64_t tm = (bT + t) * M + q.m;
-    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
-    const float gA = dab[((bT + t) * 2) * V + jc] * iM, gB = dab[((bT + t) * 2 + 1) * V + jc] * iM;
-    const float cr = SEP ? p.c_re[tm] : p.c_re[tm * V + jc];
-    const float ci = SEP ? p.c_im[tm] : p.c_im[tm * V + jc];
+    const float2 a = sg.gate(u, q.m, gq);
+    const float ar = a.x, ai = a.y;
+    const float gA = sg.d[u * 2 * JC + jl] * iM, gB = sg.d[u * 2 * JC + JC + jl] * iM;
+    const float cr = SEP ? sg.c[(u * M + q.m) * 2] : p.c_re[tm * V + jc];
+    const float ci = SEP ? sg.c[(u * M + q.m) * 2 + 1] : p.c_im[tm * V + jc];
     dr += gA * cr - gB * ci;
     di += gA * ci + gB * cr;
     const float nr = ar * dr + ai * di;
@@ -326,37 +437,46 @@ __global__ void __launch_bounds__(NT) dscan_bwd_local(sca2_dscan_args p, const f
   }
 }
 
-// reverse fold: R(k) = adjoint entering block k from the right; R(-1) = dS0
+// reverse fold: R(k) = adjoint entering block k from the right; R(-1) = dS0 (inputs loaded CU
+// blocks at a time, as in the forward fold)
 template <int M>
 __global__ void __launch_bounds__(NT) dscan_bwd_carry(sca2_dscan_args p, const float* dS_re, const float* dS_im,
-                                                     const float* qv, const float* Qg, float* R, sca2_dscan_grads gr) {
-  const Map q = thread_map<M>(p);
+                                                     const float* __restrict__ qv, const float* __restrict__ Qg,
+                                                     float* __restrict__ R, sca2_dscan_grads gr) {
+  const Map q = chan_map<M>(p, blockIdx.y);
   if (!q.live) return;
   const int V = p.V, G = p.G, NK = (p.T + CK - 1) / CK;
   const int64_t sidx = ((int64_t)q.b * M + q.m) * V + q.j;
   float rr = dS_re ? dS_re[sidx] : 0.f, ri = dS_im ? dS_im[sidx] : 0.f;
-#pragma unroll 8
-  for (int k = NK - 1; k >= 0; --k) {
-    const int64_t base = ((int64_t)q.b * NK + k) * 2;
-    R[base * M * V + (int64_t)q.m * V + q.j] = rr;
-    R[(base + 1) * M * V + (int64_t)q.m * V + q.j] = ri;
-    const float Pr = Qg[base * M * G + (int64_t)q.m * G + q.g], Pi = Qg[(base + 1) * M * G + (int64_t)q.m * G + q.g];
-    const float xr = qv[base * M * V + (int64_t)q.m * V + q.j], xi = qv[(base + 1) * M * V + (int64_t)q.m * V + q.j];
-    const float nr = Pr * rr - Pi * ri + xr;
-    ri = Pr * ri + Pi * rr + xi;
-    rr = nr;
+  for (int k1 = NK - 1; k1 >= 0; k1 -= CU) {
+    float Pr[CU], Pi[CU], xr[CU], xi[CU];
+#pragma unroll
+    for (int u = 0; u < CU; ++u) {
+      const int64_t base = ((int64_t)q.b * NK + max(k1 - u, 0)) * 2;
+      Pr[u] = Qg[base * M * G + (int64_t)q.m * G + q.g];
+      Pi[u] = Qg[(base + 1) * M * G + (int64_t)q.m * G + q.g];
+      xr[u] = qv[base * M * V + (int64_t)q.m * V + q.j];
+      xi[u] = qv[(base + 1) * M * V + (int64_t)q.m * V + q.j];
+    }
+#pragma unroll
+    for (int u = 0; u < CU; ++u) {
+      if (k1 - u < 0) break;
+      const int64_t base = ((int64_t)q.b * NK + k1 - u) * 2;
+      R[base * M * V + (int64_t)q.m * V + q.j] = rr;
+      R[(base + 1) * M * V + (int64_t)q.m * V + q.j] = ri;
+      const float nr = Pr[u] * rr - Pi[u] * ri + xr[u];
+      ri = Pr[u] * ri + Pi[u] * rr + xi[u];
+      rr = nr;
+    }
   }
   if (gr.dS0_re) gr.dS0_re[sidx] = rr;
   if (gr.dS0_im) gr.dS0_im[sidx] = ri;
 }
 
-// gradient pass of one block from its incoming adjoint R(k)
-// Gate groups a CTA's channels can touch: its 256 / M channels in groups of gs = V / G
-__host__ __device__ inline int ngl_max(int M, int gs) { return (NT / M) / gs + 2; }
-
-// The gradients summed over channels (da per (t, m, g), and dc per (t, m) with the separable
-// read) are reduced per warp by shuffles, then across the CTA's warps with shared-memory
-// atomics, and leave the CTA as one global atomic per (t, m[, g]) instead of one per warp.
+// gradient pass of one block from its incoming adjoint R(k).  The gradients summed over
+// channels (da per (t, m, g), and dc per (t, m) with the separable read) are reduced per warp by
+// shuffles, then across the CTA's warps with shared-memory atomics, and leave the CTA as one
+// global atomic per (t, m[, g]) instead of one per warp.
 template <int M, bool SEP>
 __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const float* dab, const float* ckpt,
                                                      const float* R, sca2_dscan_grads gr) {
@@ -374,7 +494,14 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
   float* sda = sred + (SEP ? CK * M * 2 : 0);     // [CK][M][NGL][2]
   const int nred = (SEP ? CK * M * 2 : 0) + CK * M * NGL * 2;
   for (int u = threadIdx.x; u < nred; u += NT) sred[u] = 0.f;
+  Stage<M> sg;
+  if (SEP) sg.load(p, dab, q.b, t0, n, blockIdx.z * (NT / M), sred + nred, NGL);
   __syncthreads();
+  const int jl = q.j - blockIdx.z * (NT / M);  // channel within the CTA
+  auto gate = [&](int u, int64_t tm) -> float2 {
+    return SEP ? sg.gate(u, q.m, q.live ? q.g : sg.g0) : make_float2(p.a_re[tm * G + q.g], p.a_im[tm * G + q.g]);
+  };
+  auto val = [&](int u, int t) -> float { return SEP ? sg.v[u * Stage<M>::JC + jl] : p.v[(bT + t) * V + jc]; };
   float dsr = q.live ? R[base * M * V + (int64_t)q.m * V + jc] : 0.f;
   float dsi = q.live ? R[(base + 1) * M * V + (int64_t)q.m * V + jc] : 0.f;
   float pr[CK], pi[CK];
@@ -386,10 +513,10 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
       pi[u] = si;
       if (u < n) {
         const int64_t tm = (bT + t0 + u) * M + q.m;
-        const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
-        const float vt = p.v[(bT + t0 + u) * V + jc];
-        const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
-        si = fmaf(ar, si, ai * sr);
+        const float2 a = gate(u, tm);
+        const float vt = val(u, t0 + u);
+        const float nr = fmaf(a.x, sr, fmaf(-a.y, si, vt));
+        si = fmaf(a.x, si, a.y * sr);
         sr = nr;
       }
     }
@@ -399,12 +526,14 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
     if (u >= n) continue;
     const int t = t0 + u;
     const int64_t tm = (bT + t) * M + q.m;
-    const float ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
-    const float vt = p.v[(bT + t) * V + jc];
+    const float2 a = gate(u, tm);
+    const float ar = a.x, ai = a.y;
+    const float vt = val(u, t);
     const float sr = fmaf(ar, pr[u], fmaf(-ai, pi[u], vt)), si = fmaf(ar, pi[u], ai * pr[u]);
-    const float gA = dab[((bT + t) * 2) * V + jc] * iM, gB = dab[((bT + t) * 2 + 1) * V + jc] * iM;
-    const float cr = SEP ? p.c_re[tm] : p.c_re[tm * V + jc];
-    const float ci = SEP ? p.c_im[tm] : p.c_im[tm * V + jc];
+    const float gA = (SEP ? sg.d[u * 2 * Stage<M>::JC + jl] : dab[((bT + t) * 2) * V + jc]) * iM;
+    const float gB = (SEP ? sg.d[u * 2 * Stage<M>::JC + Stage<M>::JC + jl] : dab[((bT + t) * 2 + 1) * V + jc]) * iM;
+    const float cr = SEP ? sg.c[(u * M + q.m) * 2] : p.c_re[tm * V + jc];
+    const float ci = SEP ? sg.c[(u * M + q.m) * 2 + 1] : p.c_im[tm * V + jc];
     dsr = q.live ? dsr + gA * cr - gB * ci : 0.f;
     dsi = q.live ? dsi + gA * ci + gB * cr : 0.f;
     const float dcr = q.live ? gA * sr + gB * si : 0.f, dci = q.live ? gA * si - gB * sr : 0.f;
@@ -455,6 +584,16 @@ inline bool use_blocks(const sca2_dscan_args& p, const float* work) {
   return work != nullptr && p.T > 4 * CK && (p.T + CK - 1) / CK <= 65535;
 }
 
+// dynamic shared memory of a staged block pass, and the opt-in for more than 48 KB
+template <int M>
+inline int stage_bytes(const sca2_dscan_args& p) {
+  return Stage<M>::floats(ngl_max(M, p.V / p.G)) * (int)sizeof(float);
+}
+template <typename Kernel>
+inline cudaError_t allow_smem(Kernel k, int bytes) {
+  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 template <int M>
 cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
                          cudaStream_t st) {
@@ -471,12 +610,17 @@ cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float
   float* P = e + (size_t)p.B * NK * 2 * M * p.V;
   float* ck = ckpt ? ckpt : P + (size_t)p.B * NK * 2 * M * p.G;  // inference: checkpoints in the workspace
   dim3 gl(p.B, NK, (per_b + NT - 1) / NT), gc(p.B, (per_b + NT - 1) / NT);
-  dscan_fwd_local<M><<<gl, NT, 0, st>>>(p, e, P);
+  const int sm = stage_bytes<M>(p);
+  cudaError_t err = allow_smem(dscan_fwd_local<M>, sm);
+  if (err != cudaSuccess) return err;
+  dscan_fwd_local<M><<<gl, NT, sm, st>>>(p, e, P);
   dscan_fwd_carry<M><<<gc, NT, 0, st>>>(p, e, P, ck, S_re, S_im);
-  if (p.sep)
-    dscan_fwd_out<M, true><<<gl, NT, 0, st>>>(p, ck, ab);
-  else
+  if (p.sep) {
+    if ((err = allow_smem(dscan_fwd_out<M, true>, sm)) != cudaSuccess) return err;
+    dscan_fwd_out<M, true><<<gl, NT, sm, st>>>(p, ck, ab);
+  } else {
     dscan_fwd_out<M, false><<<gl, NT, 0, st>>>(p, ck, ab);
+  }
   return cudaGetLastError();
 }
 template <int M>
@@ -495,16 +639,17 @@ cudaError_t launch_bwd_m(const sca2_dscan_args& p, const float* dab, const float
   float* R = qv + (size_t)p.B * NK * 2 * M * p.V;
   float* Qg = R + (size_t)p.B * NK * 2 * M * p.V;
   dim3 gl(p.B, NK, (per_b + NT - 1) / NT), gc(p.B, (per_b + NT - 1) / NT);
-  if (p.sep)
-    dscan_bwd_local<M, true><<<gl, NT, 0, st>>>(p, dab, qv, Qg);
-  else
-    dscan_bwd_local<M, false><<<gl, NT, 0, st>>>(p, dab, qv, Qg);
+  const int sm = stage_bytes<M>(p);
+  auto kl = p.sep ? dscan_bwd_local<M, true> : dscan_bwd_local<M, false>;
+  cudaError_t err = allow_smem(kl, sm);
+  if (err != cudaSuccess) return err;
+  kl<<<gl, NT, sm, st>>>(p, dab, qv, Qg);
   dscan_bwd_carry<M><<<gc, NT, 0, st>>>(p, dS_re, dS_im, qv, Qg, R, g);
-  const int red = ((p.sep ? CK * M * 2 : 0) + CK * M * ngl_max(M, p.V / p.G) * 2) * (int)sizeof(float);
-  if (p.sep)
-    dscan_bwd_block<M, true><<<gl, NT, red, st>>>(p, dab, ckpt, R, g);
-  else
-    dscan_bwd_block<M, false><<<gl, NT, red, st>>>(p, dab, ckpt, R, g);
+  const int ngl = ngl_max(M, p.V / p.G);
+  const int red = ((p.sep ? CK * M * 2 : 0) + CK * M * ngl * 2) * (int)sizeof(float) + (p.sep ? sm : 0);
+  auto kb = p.sep ? dscan_bwd_block<M, true> : dscan_bwd_block<M, false>;
+  if ((err = allow_smem(kb, red)) != cudaSuccess) return err;
+  kb<<<gl, NT, red, st>>>(p, dab, ckpt, R, g);
   return cudaGetLastError();
 }
 
