@@ -299,7 +299,7 @@ __device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, b
   }
 }
 
-template <int FL, int R>
+template <int FL, int R, bool HG>
 __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                     const float* cstates, sca2_scan_grads gr, int NCS,
                                                     int flags, PhaseProj pp) {
@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   constexpr int NISS = 4;
   const bool issuer = lane == 0 && warp < NISS;
   const int V = p.V;
-  const bool has_g = p.g.ptr != nullptr;
+  constexpr bool has_g = HG;  // a per-token scalar decay (p.g) is present: its gradient terms
   const bool excl = gridDim.y == 1;  // the only CTA writing this (b, h)'s key-side gradients
   const float kappa = FL == SCA2_FLAVOR_PHASE ? (float)Mh : 1.f;
   const float ik = 1.f / kappa;
@@ -594,27 +594,28 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           umma::take<16>(u[0], dl);
           umma::take<16>(u[1], gg);
         }
-        float dkk[16], dkw[16];
+        float dkk[16], dkw[16], gcol[16];
         float sb = 0.f, srow_ = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int jj = j0 + j;
-          float val = 0.f, gcol = 0.f;
+          float val = 0.f;
+          gcol[j] = 0.f;
           if (own && jj < i) {
             const float d = Dg(i, jj);
             const float l = -dl[j];
             const float grv = gg[j] * ik * d;
             sb += l * grv;
-            gcol = gates.beta[i] * l * grv;
-            srow_ += gcol;
+            gcol[j] = gates.beta[i] * l * grv;
+            srow_ += gcol[j];
             val = gates.beta[i] * l * d;
           }
           dkk[j] = val;
           dkw[j] = val * (float)(jj - i);
-          if (has_g) {
-            const float t = sum16(gcol);
-            if (lane == 0) atomicAdd(&s_cols[jj], t);
-          }
+        }
+        if (has_g) {  // column sums of the 16 columns over the warp's rows: one transpose-reduce
+          const float t = warp_transpose_sum<16>(gcol);
+          if ((lane & 1) == 0) atomicAdd(&s_cols[j0 + red_index<16>(lane)], t);
         }
         if (own) {
           atomicAdd(&s_dbeta[i], sb);
@@ -640,31 +641,31 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
           umma::ld_wait();
           umma::take<16>(udp, dp);
         }
-        float dqk[16], dqw[16];
+        float dqk[16], dqw[16], gcol[16];
         float srow_ = 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int jj = j0 + j;
-          float val = 0.f, gcol = 0.f;
-          if (own && jj <= i) {
-            val = dp[j] * Dg(i, jj);
-            if (has_g) {
-              gcol = dp[j] * __bfloat162float(PA[umma::kmaj(row, jj, C)]);
-              srow_ += gcol;
-            }
-          }
-          dqk[j] = val;
-          dqw[j] = val * (float)(jj - i);
-          if (has_g) {
-            float t = gcol;
-            if (RC == 128) {
+        for (int hh = 0; hh < 2; ++hh) {
+          float pa[8];  // P of the row's 8 columns (one 16-byte load)
+          if (has_g && own) ld8_bf16(PA, umma::kmaj(row, j0 + 8 * hh, C), pa);
 #pragma unroll
-              for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-            } else {
-              t = sum16(t);
+          for (int j8 = 0; j8 < 8; ++j8) {
+            const int j = 8 * hh + j8, jj = j0 + j;
+            float val = 0.f;
+            gcol[j] = 0.f;
+            if (own && jj <= i) {
+              val = dp[j] * Dg(i, jj);
+              if (has_g) {
+                gcol[j] = dp[j] * pa[j8];
+                srow_ += gcol[j];
+              }
             }
-            if (lane == 0) atomicAdd(&s_cols[jj], t);
+            dqk[j] = val;
+            dqw[j] = val * (float)(jj - i);
           }
+        }
+        if (has_g) {  // column sums over the warp's rows (lanes without rows add zeros)
+          const float t = warp_transpose_sum<16>(gcol);
+          if ((lane & 1) == 0) atomicAdd(&s_cols[j0 + red_index<16>(lane)], t);
         }
         if (own) {
           if (has_g) atomicAdd(&s_rows[i], srow_);
@@ -1089,7 +1090,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
 template <int FL, int R>
 cudaError_t launch_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
                        const sca2_scan_grads& gr, int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
-  auto k = scan_bwd_tc<FL, R>;
+  auto k = p.g.ptr ? scan_bwd_tc<FL, R, true> : scan_bwd_tc<FL, R, false>;
   const int smem = BwdLayout<FL, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
