@@ -177,6 +177,28 @@ SCA2_API int sca2_rms_fwd(const void* x, void* u, int64_t N, int32_t D, float ep
 SCA2_API int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D,
                  float eps, int32_t io_dtype, void* stream);
 
+/* Separable D-head read-out with the RMS fused (sca2/arch_sepq.py:93-104 then
+ * sca2/ref.py:29-30, the read-out of DHeadSepQ / DHeadSepQPolar.prefill, arch_sepq.py:150):
+ * per row r and channel j < dv, n = rsqrt(br^2 + bi^2 + eps_q),
+ *   u = [ n (br A + bi Bv) | n (br Bv - bi A) ],   out = u * rsqrt(mean(u^2) + eps)
+ * ab (rows, 2, dv) fp32 = [A | Bv] contiguous; br, bi rows of dv fp32 with row stride ld_q
+ * (unit column stride); out (rows, 2 dv) fp32 contiguous. */
+SCA2_API int sca2_sepq_read_fwd(const float* ab, const float* br, const float* bi, int64_t ld_q,
+                       float* out, int64_t rows, int32_t dv, float eps_q, float eps,
+                       void* stream);
+/* Its gradients from dout (rows, 2 dv): dab (rows, 2, dv) contiguous, dbr / dbi rows of dv
+ * with row stride ld_dq. */
+SCA2_API int sca2_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_t ld_q,
+                       const float* dout, float* dab, float* dbr, float* dbi, int64_t ld_dq,
+                       int64_t rows, int32_t dv, float eps_q, float eps, void* stream);
+/* bf16 hi / lo split of an fp32 matrix x (rows, cols), row stride ld_x: hi = bf16(x),
+ * lo = bf16(x - hi).  out (rows, nblk * cols) bf16, row stride ld_out: column block b
+ * (b < nblk <= 8) receives lo when bit b of lo_mask is set, else hi.  Operand preparation of
+ * the 16-bit projections that replace the heads' fp32 / autocast nn.Linear calls
+ * (sca2/arch_sepq.py:94-95: qa_r, qa_i, qb_r, qb_i). */
+SCA2_API int sca2_split_bf16(const float* x, int64_t rows, int32_t cols, int64_t ld_x, void* out,
+                    int64_t ld_out, int32_t nblk, uint32_t lo_mask, void* stream);
+
 /* ---- projected phases (the fused phase prologue) -------------------------------------------
  * The phase-flavour scan with its phases formed inside the kernels from the head's
  * projections instead of read as phi / psi tensors: a->phw and a->phq then hold K(h) and

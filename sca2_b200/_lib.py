@@ -90,6 +90,13 @@ SIGNATURES = [
     ("sca2_scan_bwd", C.c_int, [C.POINTER(ScanArgs), Out, C.c_void_p, C.c_void_p,
                                 C.POINTER(ScanGrads), C.c_void_p]),
     ("sca2_scan_step", C.c_int, [C.POINTER(ScanArgs), C.c_void_p, C.c_void_p, Out, C.c_void_p]),
+    ("sca2_sepq_read_fwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                     C.c_int32, C.c_float, C.c_float, C.c_void_p]),
+    ("sca2_sepq_read_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_float, C.c_float,
+                                     C.c_void_p]),
+    ("sca2_split_bf16", C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int64, C.c_void_p, C.c_int64, C.c_int32,
+                                  C.c_uint32, C.c_void_p]),
     ("sca2_rms_fwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_float,
                                C.c_int32, C.c_void_p]),
     ("sca2_rms_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,

@@ -30,6 +30,14 @@ cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, floa
                         float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp = PhaseProj{});
 cudaError_t tc_read_faults(unsigned int* out);
 cudaError_t tc_read_faults_bwd(unsigned int* out);
+// readout.cu
+cudaError_t launch_sepq_read_fwd(const float* ab, const float* br, const float* bi, int64_t ldq, float* out,
+                                 int64_t rows, int dv, float eps_q, float eps, cudaStream_t st);
+cudaError_t launch_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_t ldq, const float* dout,
+                                 float* dab, float* dbr, float* dbi, int64_t lddq, int64_t rows, int dv, float eps_q,
+                                 float eps, cudaStream_t st);
+cudaError_t launch_split_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo, int nblk,
+                              uint32_t lo_mask, cudaStream_t st);
 // dscan.cu
 size_t dscan_work_floats(int B, int T, int M, int G, int V);
 cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
@@ -470,6 +478,41 @@ int sca2_rms_bwd(const void* x, const void* du, void* dx, int64_t N, int32_t D, 
   if (N == 0) return SCA2_OK;
   cudaError_t e = sca2::launch_rms_bwd(x, du, dx, N, D, eps, io_dtype, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "sca2_rms_bwd");
+  return SCA2_OK;
+}
+
+int sca2_sepq_read_fwd(const float* ab, const float* br, const float* bi, int64_t ld_q, float* out, int64_t rows,
+                       int32_t dv, float eps_q, float eps, void* stream) {
+  if (rows < 0 || dv < 1 || ld_q < dv) return fail(SCA2_ERR_ARG, "sepq_read: bad sizes");
+  if (rows == 0) return SCA2_OK;
+  if (!ab || !br || !bi || !out) return fail(SCA2_ERR_ARG, "sepq_read: null pointer");
+  cudaError_t e = sca2::launch_sepq_read_fwd(ab, br, bi, ld_q, out, rows, dv, eps_q, eps,
+                                             reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_sepq_read_fwd");
+  return SCA2_OK;
+}
+
+int sca2_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_t ld_q, const float* dout,
+                       float* dab, float* dbr, float* dbi, int64_t ld_dq, int64_t rows, int32_t dv, float eps_q,
+                       float eps, void* stream) {
+  if (rows < 0 || dv < 1 || ld_q < dv || ld_dq < dv) return fail(SCA2_ERR_ARG, "sepq_read: bad sizes");
+  if (rows == 0) return SCA2_OK;
+  if (!ab || !br || !bi || !dout || !dab || !dbr || !dbi) return fail(SCA2_ERR_ARG, "sepq_read: null pointer");
+  cudaError_t e = sca2::launch_sepq_read_bwd(ab, br, bi, ld_q, dout, dab, dbr, dbi, ld_dq, rows, dv, eps_q, eps,
+                                             reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_sepq_read_bwd");
+  return SCA2_OK;
+}
+
+int sca2_split_bf16(const float* x, int64_t rows, int32_t cols, int64_t ld_x, void* out, int64_t ld_out,
+                    int32_t nblk, uint32_t lo_mask, void* stream) {
+  if (rows < 0 || cols < 1 || ld_x < cols || nblk < 1 || nblk > 8 || ld_out < (int64_t)nblk * cols)
+    return fail(SCA2_ERR_ARG, "split_bf16: bad sizes");
+  if (rows == 0) return SCA2_OK;
+  if (!x || !out) return fail(SCA2_ERR_ARG, "split_bf16: null pointer");
+  cudaError_t e = sca2::launch_split_bf16(x, rows, cols, ld_x, out, ld_out, nblk, lo_mask,
+                                          reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_split_bf16");
   return SCA2_OK;
 }
 

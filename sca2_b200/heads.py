@@ -28,7 +28,7 @@ from __future__ import annotations
 import math
 import os
 from dataclasses import dataclass
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -124,24 +124,6 @@ def _linear_f32(lin: nn.Linear, x: torch.Tensor) -> torch.Tensor:
     costs nothing measurable (the state, phases and solve are float32 for the same reason)."""
     with torch.autocast(device_type=x.device.type, enabled=False):
         return F.linear(x.float(), lin.weight.float(), None if lin.bias is None else lin.bias.float())
-
-
-def _linear_split(lins: Sequence[nn.Linear], x: torch.Tensor) -> List[torch.Tensor]:
-    """[lin(x) for lin in lins] to about 16 mantissa bits on bf16 tensor cores: x and the
-    stacked weights are each split into bf16 hi + lo parts and the three products hi*hi +
-    hi*lo + lo*hi (fp32 accumulation) are summed in fp32; one product chain for all the
-    projections.  Autocast's plain bf16 projection rounds x and the weight first, which leaves
-    an error of about 2^-9 of the typical output size in every output; where an output is
-    itself small (a query normalised by its length), that error dominates it.  With the split,
-    only each product's own result is rounded: the error is relative to the output."""
-    w = torch.cat([lin.weight for lin in lins], 0).float()
-    xf = x.float()
-    xh, wh = xf.to(torch.bfloat16), w.to(torch.bfloat16)
-    xl, wl = (xf - xh.float()).to(torch.bfloat16), (w - wh.float()).to(torch.bfloat16)
-    with torch.autocast(device_type=x.device.type, enabled=False):
-        y = F.linear(xh, wh).float() + F.linear(xh, wl).float() + F.linear(xl, wh).float()
-    outs = list(y.split([lin.out_features for lin in lins], -1))
-    return [o if lin.bias is None else o + lin.bias.float() for o, lin in zip(outs, lins)]
 
 
 def _positions(T: int, pos: torch.Tensor, device) -> torch.Tensor:
@@ -531,25 +513,41 @@ class DHeadSepQ(nn.Module):
         return (torch.tanh(_linear_f32(self.gr, h)).view(B, T, self.M, self.G) * s2,
                 torch.tanh(_linear_f32(self.gi, h)).view(B, T, self.M, self.G) * s2)
 
+    def _queries(self, z):
+        """The four query projections [qa_r | qa_i] (B,T,2M) and [qb_r | qb_i] (B,T,2dv) as
+        one product.  The separable query is normalised per (token, mode) and per (token,
+        channel), and the gradient of q / |q| scales with 1 / |q|: under autocast the product
+        keeps about 16 bits (ops.linear16: bf16 hi + lo operands, fp32 output), so a small q
+        keeps its relative precision; otherwise it is one fp32 product."""
+        B, T, _ = z.shape
+        w = torch.cat([self.qa_r.weight, self.qa_i.weight, self.qb_r.weight, self.qb_i.weight], 0)
+        if torch.is_autocast_enabled() and z.is_cuda:
+            qa, qb = ops.linear16(z, w, (2 * self.M, 2 * self.dv))
+            return qa.view(B, T, 2 * self.M), qb.view(B, T, 2 * self.dv)
+        with torch.autocast(device_type=z.device.type, enabled=False):
+            y = F.linear(z.float(), w.float())
+        return y[..., :2 * self.M], y[..., 2 * self.M:]
+
     def prefill(self, z, h, state=None):
         B, T, _ = z.shape
+        M = self.M
         st = state if state is not None else self.init_state(B, z.device)
         a_re, a_im = self._gate(h, B, T)
-        # the separable query is normalised per (token, mode) and per (token, channel), and the
-        # gradient of q / |q| scales with 1 / |q|: under autocast the query projections keep
-        # about 16 bits (bf16 hi + lo products), so a small q keeps its relative precision
-        if torch.is_autocast_enabled() and z.is_cuda:
-            ar, ai, br, bi = _linear_split((self.qa_r, self.qa_i, self.qb_r, self.qb_i), z)
-        else:
-            ar, ai = self.qa_r(z), self.qa_i(z)
-            br, bi = self.qb_r(z), self.qb_i(z)
+        qa, qb = self._queries(z)
+        ar, ai = qa[..., :M], qa[..., M:]
         an = torch.rsqrt(ar.square() + ai.square() + 1e-6)
-        bn = torch.rsqrt(br.square() + bi.square() + 1e-6)
         ab, (sr, si) = ops.dscan(a_re, a_im, self.V(z), ar * an, ai * an, (st["sr"], st["si"]), sep=True)
-        A, Bv = ab[:, :, 0], ab[:, :, 1]
-        br, bi = br * bn, bi * bn
-        u = torch.cat([br * A + bi * Bv, br * Bv - bi * A], -1)
-        return _gated_out(self, u, z).to(z.dtype), {"sr": sr, "si": si}
+        if getattr(self, "rms_read", True):  # channel-query normalisation, combine and RMS fused
+            u = ops.sepq_read(ab, qb)
+            if self.gated_read:
+                u = u * F.silu(self.rgate(z))
+        else:
+            br, bi = qb[..., :self.dv], qb[..., self.dv:]
+            bn = torch.rsqrt(br.square() + bi.square() + 1e-6)
+            A, Bv = ab[:, :, 0], ab[:, :, 1]
+            br, bi = br * bn, bi * bn
+            u = _gated_out(self, torch.cat([br * A + bi * Bv, br * Bv - bi * A], -1), z)
+        return u.to(z.dtype), {"sr": sr, "si": si}
 
     def forward(self, z, h):
         return self.prefill(z, h)[0]

@@ -6,6 +6,8 @@
     dscan(a_re, a_im, v, c_re, c_im, S0, sep)             D-head diagonal scan
     short_read(kh, kz, v, theta, omega, wr, wi, state)    short-head window read
     rms(x, eps)                                           per-row RMS read-out
+    sepq_read(ab, q)                                      separable D-head read-out + RMS
+    linear16(x, w, sizes)                                 x w^T to 16 bits on bf16 tensor cores
 
 Every op runs the CUDA kernels of libsca2b200.so on the current stream.  There is no
 CPU path: a CPU tensor or a missing library raises.  Device memory (outputs, saved
@@ -987,6 +989,145 @@ def rms(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     if x.dtype not in _DT:
         x = x.float()
     return torch.ops.sca2b200.rms_fwd(x.contiguous(), float(eps))
+
+
+# ======================================================================================
+#  separable D-head read-out (RMS fused) and the 16-bit projections
+# ======================================================================================
+def _rows(x: torch.Tensor, width: int) -> torch.Tensor:
+    """x as a (rows, width) matrix with unit column stride (a view where the strides allow)."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    try:
+        return x.view(-1, width)
+    except RuntimeError:
+        return x.contiguous().view(-1, width)
+
+
+@torch.library.custom_op("sca2b200::sepq_read_fwd", mutates_args=())
+def _sepq_read_fwd(ab: torch.Tensor, q: torch.Tensor, eps_q: float, eps: float) -> torch.Tensor:
+    """sca2_sepq_read_fwd: ab (..., 2, dv) and q (..., 2 dv) = [br | bi] -> (..., 2 dv) fp32."""
+    dv = ab.shape[-1]
+    q2 = _rows(q, 2 * dv)
+    rows = q2.shape[0]
+    out = torch.empty(*ab.shape[:-2], 2 * dv, device=ab.device, dtype=torch.float32)
+    _lib.check(_lib.load().sca2_sepq_read_fwd(ab.data_ptr(), q2.data_ptr(), q2.data_ptr() + 4 * dv, q2.stride(0),
+                                              out.data_ptr(), rows, dv, float(eps_q), float(eps), _stream()),
+               "sepq_read_fwd")
+    return out
+
+
+@_sepq_read_fwd.register_fake
+def _(ab, q, eps_q, eps):
+    return ab.new_empty(*ab.shape[:-2], 2 * ab.shape[-1], dtype=torch.float32)
+
+
+@torch.library.custom_op("sca2b200::sepq_read_bwd", mutates_args=())
+def _sepq_read_bwd(ab: torch.Tensor, q: torch.Tensor, dout: torch.Tensor, eps_q: float,
+                   eps: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """sca2_sepq_read_bwd: gradients of ab (..., 2, dv) and of q (..., 2 dv)."""
+    dv = ab.shape[-1]
+    q2 = _rows(q, 2 * dv)
+    rows = q2.shape[0]
+    dout = dout.float().contiguous()
+    dab = torch.empty(ab.shape, device=ab.device, dtype=torch.float32)
+    dq = torch.empty(rows, 2 * dv, device=ab.device, dtype=torch.float32)
+    _lib.check(_lib.load().sca2_sepq_read_bwd(ab.data_ptr(), q2.data_ptr(), q2.data_ptr() + 4 * dv, q2.stride(0),
+                                              dout.data_ptr(), dab.data_ptr(), dq.data_ptr(),
+                                              dq.data_ptr() + 4 * dv, 2 * dv, rows, dv, float(eps_q), float(eps),
+                                              _stream()), "sepq_read_bwd")
+    return dab, dq.view(q.shape)
+
+
+@_sepq_read_bwd.register_fake
+def _(ab, q, dout, eps_q, eps):
+    return ab.new_empty(ab.shape, dtype=torch.float32), q.new_empty(q.shape, dtype=torch.float32)
+
+
+def _sepq_setup(ctx, inputs, output):
+    ab, q, ctx.eps_q, ctx.eps = inputs
+    ctx.save_for_backward(ab, q)
+
+
+def _sepq_backward(ctx, dout):
+    ab, q = ctx.saved_tensors
+    dab, dq = torch.ops.sca2b200.sepq_read_bwd(ab, q, dout, ctx.eps_q, ctx.eps)
+    return dab, dq, None, None
+
+
+_sepq_read_fwd.register_autograd(_sepq_backward, setup_context=_sepq_setup)
+
+
+def sepq_read(ab: torch.Tensor, q: torch.Tensor, eps_q: float = 1e-6, eps: float = 1e-6) -> torch.Tensor:
+    """Separable D-head read-out with the RMS fused (sca2/arch_sepq.py:93-104, sca2/ref.py:29-30):
+    ab (..., 2, dv) = [A | Bv] from dscan(sep=True), q (..., 2 dv) = [br | bi] the raw channel
+    query (unit last stride; any single row stride) ->
+    rms([n (br A + bi Bv) | n (br Bv - bi A)]), n = rsqrt(br^2 + bi^2 + eps_q).  fp32."""
+    _need_cuda(ab, q)
+    if ab.dtype != torch.float32 or q.dtype != torch.float32:
+        raise TypeError("sepq_read takes fp32 ab and q")
+    return torch.ops.sca2b200.sepq_read_fwd(ab.contiguous(), q, float(eps_q), float(eps))
+
+
+def split_bf16(x: torch.Tensor, lo_blocks: Tuple[bool, ...]) -> torch.Tensor:
+    """sca2_split_bf16: x (rows, cols) fp32 -> (rows, len(lo_blocks) * cols) bf16 whose column
+    block b is bf16(x) (False) or bf16(x - bf16(x)) (True)."""
+    _need_cuda(x)
+    x2 = _rows(x.float(), x.shape[-1])
+    rows, cols = x2.shape
+    nb = len(lo_blocks)
+    out = torch.empty(rows, nb * cols, device=x.device, dtype=torch.bfloat16)
+    mask = sum(1 << b for b, lo in enumerate(lo_blocks) if lo)
+    _lib.check(_lib.load().sca2_split_bf16(x2.data_ptr(), rows, cols, x2.stride(0), out.data_ptr(), nb * cols, nb, mask,
+                                           _stream()), "split_bf16")
+    return out
+
+
+def _mm32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a @ b for bf16 operands with fp32 output (cuBLAS, fp32 accumulation, no output rounding)."""
+    return torch.mm(a, b, out_dtype=torch.float32)
+
+
+class _Linear16(torch.autograd.Function):
+    """y = x w^T with x and w each split into bf16 hi + lo: ONE bf16 GEMM over the stacked
+    contraction [xh | xh | xl] . [wh | wl | wh]^T = xh wh + xh wl + xl wh, fp32 output.  The
+    backward splits dy the same way: dx = [dyh | dyh | dyl] . [wh ; wl ; wh] (one GEMM) and
+    dw = dyh^T (xh + xl) + dyl^T xh (two GEMMs), all with fp32 outputs."""
+
+    @staticmethod
+    def forward(ctx, x2, w, sizes):
+        with torch.autocast(device_type="cuda", enabled=False):
+            X3 = split_bf16(x2, (False, False, True))
+            W3 = split_bf16(w, (False, True, False))
+            y = _mm32(X3, W3.t())
+        ctx.save_for_backward(X3, W3)
+        ctx.sizes = sizes
+        return tuple(y.split(list(sizes), 1))
+
+    @staticmethod
+    def backward(ctx, *dys):
+        X3, W3 = ctx.saved_tensors
+        R, d, N = X3.shape[0], X3.shape[1] // 3, W3.shape[0]
+        parts = [g.float() if g is not None else torch.zeros(R, n, device=X3.device) for g, n in zip(dys, ctx.sizes)]
+        with torch.autocast(device_type="cuda", enabled=False):
+            Y3 = split_bf16(torch.cat(parts, 1) if len(parts) > 1 else parts[0], (False, False, True))
+            dx = dw = None
+            if ctx.needs_input_grad[0]:
+                dx = _mm32(Y3, torch.cat([W3[:, :d], W3[:, d:2 * d], W3[:, :d]], 0))
+            if ctx.needs_input_grad[1]:
+                a = _mm32(Y3[:, :N].t(), X3[:, d:])
+                dw = a[:, :d] + a[:, d:] + _mm32(Y3[:, 2 * N:].t(), X3[:, :d])
+        return dx, dw, None
+
+
+def linear16(x: torch.Tensor, w: torch.Tensor, sizes: Tuple[int, ...]) -> Tuple[torch.Tensor, ...]:
+    """x (..., d) fp32 times w (N, d)^T to about 16 significant bits on bf16 tensor cores (see
+    _Linear16), returned as the column groups `sizes` (summing to N), each (rows, size) fp32
+    with rows = x.numel() / d.  Differentiable in x and w."""
+    _need_cuda(x, w)
+    if sum(sizes) != w.shape[0]:
+        raise ValueError("linear16: the column groups must cover the rows of w")
+    return _Linear16.apply(_rows(x.float(), x.shape[-1]), w.float(), tuple(sizes))
 
 
 # ======================================================================================
