@@ -191,6 +191,15 @@ SCA2_API int sca2_sepq_read_fwd(const float* ab, const float* br, const float* b
 SCA2_API int sca2_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_t ld_q,
                        const float* dout, float* dab, float* dbr, float* dbi, int64_t ld_dq,
                        int64_t rows, int32_t dv, float eps_q, float eps, void* stream);
+/* RMS read-out of a multi-head read (sca2/arch_gatedc.py:155-156 and _gated_out, :168;
+ * lapa/layer.py:384 with H = 1): x rows (rows, H, 2, dvh) contiguous in io_dtype, the heads'
+ * [re | im] reads; u rows (rows, 2, H, dvh) fp32 = [re of every head | im of every head] *
+ * rsqrt(mean(x^2) + eps).  dvh % 4 == 0; rows 16-byte (fp32) / 8-byte (bf16) aligned. */
+SCA2_API int sca2_rms_heads_fwd(const void* x, int32_t io_dtype, float* u, int64_t rows, int32_t H,
+                       int32_t dvh, float eps, void* stream);
+/* dx (rows, H, 2, dvh) in io_dtype from du (rows, 2, H, dvh) fp32. */
+SCA2_API int sca2_rms_heads_bwd(const void* x, int32_t io_dtype, const float* du, void* dx, int64_t rows,
+                       int32_t H, int32_t dvh, float eps, void* stream);
 /* bf16 hi / lo split of an fp32 matrix x (rows, cols), row stride ld_x: hi = bf16(x),
  * lo = bf16(x - hi).  out (rows, nblk * cols) bf16, row stride ld_out: column block b
  * (b < nblk <= 8) receives lo when bit b of lo_mask is set, else hi.  Operand preparation of

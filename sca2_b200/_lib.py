@@ -95,6 +95,10 @@ SIGNATURES = [
     ("sca2_sepq_read_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_float, C.c_float,
                                      C.c_void_p]),
+    ("sca2_rms_heads_fwd", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_float,
+                                     C.c_void_p]),
+    ("sca2_rms_heads_bwd", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_int32,
+                                     C.c_float, C.c_void_p]),
     ("sca2_split_bf16", C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int64, C.c_void_p, C.c_int64, C.c_int32,
                                   C.c_uint32, C.c_void_p]),
     ("sca2_rms_fwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_float,

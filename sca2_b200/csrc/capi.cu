@@ -38,6 +38,10 @@ cudaError_t launch_sepq_read_bwd(const float* ab, const float* br, const float* 
                                  float eps, cudaStream_t st);
 cudaError_t launch_split_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo, int nblk,
                               uint32_t lo_mask, cudaStream_t st);
+cudaError_t launch_rms_heads_fwd(const void* x, int dt, float* out, int64_t rows, int H, int dvh, float eps,
+                                 cudaStream_t st);
+cudaError_t launch_rms_heads_bwd(const void* x, int dt, const float* dout, void* dx, int64_t rows, int H, int dvh,
+                                 float eps, cudaStream_t st);
 // dscan.cu
 size_t dscan_work_floats(int B, int T, int M, int G, int V);
 cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
@@ -501,6 +505,36 @@ int sca2_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_
   cudaError_t e = sca2::launch_sepq_read_bwd(ab, br, bi, ld_q, dout, dab, dbr, dbi, ld_dq, rows, dv, eps_q, eps,
                                              reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "sca2_sepq_read_bwd");
+  return SCA2_OK;
+}
+
+static int check_rms_heads(const void* x, const void* y, int64_t rows, int32_t H, int32_t dvh, int32_t io_dtype) {
+  if (rows < 0 || H < 1 || dvh < 4 || dvh % 4) return fail(SCA2_ERR_ARG, "rms_heads: bad sizes (dvh % 4 != 0?)");
+  if (io_dtype != SCA2_F32 && io_dtype != SCA2_BF16) return fail(SCA2_ERR_ARG, "rms_heads: bad dtype");
+  if (rows > 0 && (!x || !y)) return fail(SCA2_ERR_ARG, "rms_heads: null pointer");
+  const uintptr_t a = io_dtype == SCA2_BF16 ? 8 : 16;
+  if (((uintptr_t)x % a) || ((uintptr_t)y % 16)) return fail(SCA2_ERR_ARG, "rms_heads: misaligned rows");
+  return SCA2_OK;
+}
+
+int sca2_rms_heads_fwd(const void* x, int32_t io_dtype, float* u, int64_t rows, int32_t H, int32_t dvh, float eps,
+                       void* stream) {
+  if (int r = check_rms_heads(x, u, rows, H, dvh, io_dtype)) return r;
+  if (rows == 0) return SCA2_OK;
+  cudaError_t e = sca2::launch_rms_heads_fwd(x, io_dtype, u, rows, H, dvh, eps, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_rms_heads_fwd");
+  return SCA2_OK;
+}
+
+int sca2_rms_heads_bwd(const void* x, int32_t io_dtype, const float* du, void* dx, int64_t rows, int32_t H,
+                       int32_t dvh, float eps, void* stream) {
+  if (int r = check_rms_heads(x, du, rows, H, dvh, io_dtype)) return r;
+  if (rows > 0 && (!dx || ((uintptr_t)dx % (io_dtype == SCA2_BF16 ? 8 : 16))))
+    return fail(SCA2_ERR_ARG, "rms_heads: null or misaligned dx");
+  if (rows == 0) return SCA2_OK;
+  cudaError_t e =
+      sca2::launch_rms_heads_bwd(x, io_dtype, du, dx, rows, H, dvh, eps, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_rms_heads_bwd");
   return SCA2_OK;
 }
 

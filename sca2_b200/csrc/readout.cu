@@ -177,6 +177,89 @@ __global__ void __launch_bounds__(NT) sepq_read_bwd_kernel(RowIO io, const float
   }
 }
 
+// ---- RMS read-out of a multi-head read (sca2/arch_gatedc.py:155-156, 168) ------------------
+// x rows hold H heads of [re | im] halves of dvh values, (H, 2, dvh); out rows are
+// [re of every head | im of every head], (2, H, dvh), times rsqrt(mean(x^2) + eps).  Four
+// consecutive values (one head, one half; dvh % 4 == 0) per lane and step.
+__device__ __forceinline__ void ld4_io(const void* p, int64_t i, int dt, float* x) {
+  if (dt == SCA2_BF16) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    x[0] = __low2float(h[0]), x[1] = __high2float(h[0]), x[2] = __low2float(h[1]), x[3] = __high2float(h[1]);
+  } else {
+    load4<true>(reinterpret_cast<const float*>(p), i, x);
+  }
+}
+__device__ __forceinline__ void st4_io(void* p, int64_t i, int dt, const float* x) {
+  if (dt == SCA2_BF16) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
+    uint2 raw;
+    raw.x = *reinterpret_cast<const uint32_t*>(&a);
+    raw.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p) + i) = raw;
+  } else {
+    store4<true>(reinterpret_cast<float*>(p), i, x);
+  }
+}
+// output position of input position i (a multiple of 4) of a row
+__device__ __forceinline__ int heads_out(int i, int H, int dvh) {
+  const int hr = i / dvh, j = i - hr * dvh;  // hr = 2 h + r
+  return ((hr & 1) * H + (hr >> 1)) * dvh + j;
+}
+
+__global__ void __launch_bounds__(NT) rms_heads_fwd_kernel(const void* x, int dt, float* out, int64_t rows, int H,
+                                                           int dvh, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * RPC + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int D = 2 * H * dvh;
+  const int64_t off = row * D;
+  float ss = 0.f;
+  for (int i = 4 * lane; i < D; i += 128) {
+    float v[4];
+    ld4_io(x, off + i, dt, v);
+    ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
+  }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / (float)D + eps);
+  for (int i = 4 * lane; i < D; i += 128) {
+    float v[4];
+    ld4_io(x, off + i, dt, v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] *= rs;
+    store4<true>(out, off + heads_out(i, H, dvh), v);
+  }
+}
+
+__global__ void __launch_bounds__(NT) rms_heads_bwd_kernel(const void* x, int dt, const float* dout, void* dx,
+                                                           int64_t rows, int H, int dvh, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * RPC + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int D = 2 * H * dvh;
+  const int64_t off = row * D;
+  float ss = 0.f, sd = 0.f;
+  for (int i = 4 * lane; i < D; i += 128) {
+    float v[4], g[4];
+    ld4_io(x, off + i, dt, v);
+    load4<true>(dout, off + heads_out(i, H, dvh), g);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ss = fmaf(v[k], v[k], ss), sd = fmaf(v[k], g[k], sd);
+  }
+  ss = warp_sum(ss);
+  sd = warp_sum(sd);
+  const float rs = rsqrtf(ss / (float)D + eps);
+  const float c = rs * rs * rs * sd / (float)D;
+  for (int i = 4 * lane; i < D; i += 128) {
+    float v[4], g[4], o[4];
+    ld4_io(x, off + i, dt, v);
+    load4<true>(dout, off + heads_out(i, H, dvh), g);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = fmaf(rs, g[k], -c * v[k]);
+    st4_io(dx, off + i, dt, o);
+  }
+}
+
 // ---- bf16 hi / lo split -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -243,6 +326,17 @@ cudaError_t launch_sepq_read_bwd(const float* ab, const float* br, const float* 
   else
     readout::sepq_read_bwd_kernel<false>
         <<<grid_rows(rows), readout::NT, 0, st>>>(io, dout, dab, dbr, dbi, lddq, rows, dv, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_heads_fwd(const void* x, int dt, float* out, int64_t rows, int H, int dvh, float eps,
+                                 cudaStream_t st) {
+  readout::rms_heads_fwd_kernel<<<grid_rows(rows), readout::NT, 0, st>>>(x, dt, out, rows, H, dvh, eps);
+  return cudaGetLastError();
+}
+cudaError_t launch_rms_heads_bwd(const void* x, int dt, const float* dout, void* dx, int64_t rows, int H, int dvh,
+                                 float eps, cudaStream_t st) {
+  readout::rms_heads_bwd_kernel<<<grid_rows(rows), readout::NT, 0, st>>>(x, dt, dout, dx, rows, H, dvh, eps);
   return cudaGetLastError();
 }
 

@@ -362,7 +362,6 @@ __global__ void __launch_bounds__(NT, 3) short_bwd_kernel(sca2_short_args p, con
         a2[k] = fmaf(r, s4[k], fmaf(-i, c4[k], a2[k]));
       }
     }
-#pragma unroll
     const int64_t t0i = ((int64_t)b * T + t) * L + l0;
     float kz[4], dk[4];
     if (vec) {

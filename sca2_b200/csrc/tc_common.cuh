@@ -445,7 +445,7 @@ __device__ void build_codes(const CodeRegs<FL, KD>& cr, const CodeOps<FL, KD, R>
     int i, m0;
     code_unit<KD / 16>(tid, i, m0);
     const bool live = i < Cl;
-    const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik, wv = g.w[i];
+    const float fi = (float)i, zb = g.beta[i] * g.a[i] * ik;
     float kc[8], ks[8], wc[8], ws[8], q0a[8], q0b[8], q1a[8], q1b[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {

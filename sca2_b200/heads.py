@@ -108,6 +108,18 @@ def _gated_out(head, u, z):
     return u * F.silu(head.rgate(z)) if getattr(head, "gated_read", False) else u
 
 
+def _read_heads(head, o, z):
+    """Read-out of a scan read o (..., H, 2, dvh) as u (..., 2 H dvh) = [re of every head | im
+    of every head] through _gated_out (sca2/arch_gatedc.py:155-156, 168).  With the RMS read
+    the head gathering and the RMS are one row kernel (ops.rms_heads), fp32 out."""
+    if getattr(head, "rms_read", True) and o.shape[-1] % 4 == 0:
+        u = ops.rms_heads(o)
+        return u * F.silu(head.rgate(z)) if getattr(head, "gated_read", False) else u
+    lead = o.shape[:-3]
+    u = torch.cat([o[..., 0, :].reshape(*lead, -1), o[..., 1, :].reshape(*lead, -1)], -1)
+    return _gated_out(head, u.float(), z)
+
+
 def _value_dtype(z: torch.Tensor) -> torch.dtype:
     """Dtype handed to the kernel for v / o: the autocast dtype on CUDA (the reference's
     gemm_dtype policy, lapa/layer.py:225-230), else float32."""
@@ -197,9 +209,9 @@ class LongHead(nn.Module):
         o, S = ops.phase_scan_proj(self.K(h)[:, :, None], self.K(z)[:, :, None], self.theta[None], self.omega[None],
                                    st["pos"], v, beta, None, self.lam()[None], self.wr.float()[None],
                                    self.wi.float()[None], S0)
-        u = _rms(o.reshape(B, T, 2 * self.dv)).to(z.dtype)
+        u = (ops.rms_heads(o) if self.dv % 4 == 0 else _rms(o.reshape(B, T, 2 * self.dv))).view(B, T, -1)
         M = self.M
-        return u, {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": st["pos"] + T}
+        return u.to(z.dtype), {"sr": S[:, 0, :M], "si": S[:, 0, M:], "pos": st["pos"] + T}
 
     def step(self, z_t, h_t, state: State):
         M = self.M
@@ -407,8 +419,7 @@ class CHeadGated(CHeadBase):
                                    self.omega.view(H, Mh), st["pos"],
                                    self.V(z).to(_value_dtype(z)).view(B, T, H, dvh), None, g, None,
                                    self.wr.float().view(H, Mh), self.wi.float().view(H, Mh), S0)
-        u = torch.cat([o[:, :, :, 0].reshape(B, T, self.dv), o[:, :, :, 1].reshape(B, T, self.dv)], -1)
-        u = _gated_out(self, u.float(), z).to(z.dtype)
+        u = _read_heads(self, o, z).to(z.dtype)
         return u, {"sr": S[:, :, :Mh], "si": S[:, :, Mh:], "pos": st["pos"] + T, "empty": False}
 
     def step(self, z_t, h_t, state):
@@ -421,8 +432,7 @@ class CHeadGated(CHeadBase):
         o, S = ops.phase_step(pw.view(B, H, Mh), pq.view(B, H, Mh), self.V(z_t).float().view(B, H, dvh),
                               None, g, None, self.wr.float().view(H, Mh), self.wi.float().view(H, Mh),
                               S, S_out=S)
-        u = torch.cat([o[:, :, 0].reshape(B, self.dv), o[:, :, 1].reshape(B, self.dv)], -1)
-        u = _gated_out(self, u, z_t).to(z_t.dtype)
+        u = _read_heads(self, o, z_t).to(z_t.dtype)
         return u, {"sr": S[:, :, :Mh], "si": S[:, :, Mh:], "pos": state["pos"] + 1, "empty": False}
 
 

@@ -7,6 +7,7 @@
     short_read(kh, kz, v, theta, omega, wr, wi, state)    short-head window read
     rms(x, eps)                                           per-row RMS read-out
     sepq_read(ab, q)                                      separable D-head read-out + RMS
+    rms_heads(o)                                          multi-head read gathered + RMS
     linear16(x, w, sizes)                                 x w^T to 16 bits on bf16 tensor cores
 
 Every op runs the CUDA kernels of libsca2b200.so on the current stream.  There is no
@@ -1067,6 +1068,64 @@ def sepq_read(ab: torch.Tensor, q: torch.Tensor, eps_q: float = 1e-6, eps: float
     if ab.dtype != torch.float32 or q.dtype != torch.float32:
         raise TypeError("sepq_read takes fp32 ab and q")
     return torch.ops.sca2b200.sepq_read_fwd(ab.contiguous(), q, float(eps_q), float(eps))
+
+
+@torch.library.custom_op("sca2b200::rms_heads_fwd", mutates_args=())
+def _rms_heads_fwd(o: torch.Tensor, eps: float) -> torch.Tensor:
+    """sca2_rms_heads_fwd: o (..., H, 2, dvh) contiguous fp32 / bf16 -> (..., 2 H dvh) fp32."""
+    H, dvh = o.shape[-3], o.shape[-1]
+    D = 2 * H * dvh
+    u = torch.empty(*o.shape[:-3], D, device=o.device, dtype=torch.float32)
+    _lib.check(_lib.load().sca2_rms_heads_fwd(o.data_ptr(), _DT[o.dtype], u.data_ptr(), o.numel() // D, H, dvh,
+                                              float(eps), _stream()), "rms_heads_fwd")
+    return u
+
+
+@_rms_heads_fwd.register_fake
+def _(o, eps):
+    return o.new_empty(*o.shape[:-3], 2 * o.shape[-3] * o.shape[-1], dtype=torch.float32)
+
+
+@torch.library.custom_op("sca2b200::rms_heads_bwd", mutates_args=())
+def _rms_heads_bwd(o: torch.Tensor, du: torch.Tensor, eps: float) -> torch.Tensor:
+    """sca2_rms_heads_bwd: the gradient of o (its shape and dtype) from du (..., 2 H dvh)."""
+    H, dvh = o.shape[-3], o.shape[-1]
+    D = 2 * H * dvh
+    du = du.float().contiguous()
+    do = torch.empty_like(o)
+    _lib.check(_lib.load().sca2_rms_heads_bwd(o.data_ptr(), _DT[o.dtype], du.data_ptr(), do.data_ptr(), o.numel() // D,
+                                              H, dvh, float(eps), _stream()), "rms_heads_bwd")
+    return do
+
+
+@_rms_heads_bwd.register_fake
+def _(o, du, eps):
+    return torch.empty_like(o)
+
+
+def _rms_heads_setup(ctx, inputs, output):
+    o, ctx.eps = inputs
+    ctx.save_for_backward(o)
+
+
+def _rms_heads_backward(ctx, du):
+    (o,) = ctx.saved_tensors
+    return torch.ops.sca2b200.rms_heads_bwd(o, du, ctx.eps), None
+
+
+_rms_heads_fwd.register_autograd(_rms_heads_backward, setup_context=_rms_heads_setup)
+
+
+def rms_heads(o: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """RMS read-out of a multi-head read (sca2/arch_gatedc.py:155-156 with _gated_out's RMS):
+    o (..., H, 2, dvh) -> rms([re of every head | im of every head]) (..., 2 H dvh) fp32, the
+    gathering fused into the row kernel.  dvh % 4 == 0."""
+    _need_cuda(o)
+    if o.dtype not in _DT:
+        o = o.float()
+    if o.shape[-2] != 2 or o.shape[-1] % 4:
+        raise ValueError("rms_heads takes (..., H, 2, dvh) reads with dvh % 4 == 0")
+    return torch.ops.sca2b200.rms_heads_fwd(o.contiguous(), float(eps))
 
 
 def split_bf16(x: torch.Tensor, lo_blocks: Tuple[bool, ...]) -> torch.Tensor:

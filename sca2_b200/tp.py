@@ -106,9 +106,7 @@ class ShardedCHeadGated(heads.CHeadGated):
 
     def _read_out(self, o, z):
         """o (B,T,H,2,dvh) of every head -> the head's read-out u (B,T,2dv), replicated."""
-        lead = o.shape[:-3]
-        u = torch.cat([o[..., 0, :].reshape(*lead, self.dv), o[..., 1, :].reshape(*lead, self.dv)], -1)
-        return heads._gated_out(self, u.float(), z).to(z.dtype)
+        return heads._read_heads(self, o, z).to(z.dtype)
 
     def prefill(self, z, h, state=None):
         B, T, _ = z.shape

@@ -74,3 +74,24 @@ def test_linear16_16_bits():
     (y64 * torch.cat([da, db], 1).double()).sum().backward()
     assert relerr(torch.cat([ya, yb], 1), y64) < 2e-4
     assert relerr(x.grad, x64.grad) < 2e-4 and relerr(w.grad, w64.grad) < 2e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("lead,H,dvh", [((2, 33), 4, 64), ((5,), 1, 12), ((1, 3), 16, 8)])
+def test_rms_heads_vs_torch(dtype, lead, H, dvh):
+    """Gathered multi-head RMS read-out (sca2/arch_gatedc.py:155-156 + sca2/ref.py:29-30):
+    fp32 output and the input gradient in the input's dtype (fp32 bar; bf16 inputs: the
+    gradient's own bf16 rounding, 1e-2 relative)."""
+    from sca2_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(H * dvh)
+    o = torch.randn(*lead, H, 2, dvh, device="cuda", generator=g).to(dtype).requires_grad_(True)
+    du = torch.randn(*lead, 2 * H * dvh, device="cuda", generator=g)
+    u = ops.rms_heads(o)
+    u.backward(du)
+    o64 = o.detach().double().requires_grad_(True)
+    cat = torch.cat([o64[..., 0, :].reshape(*lead, -1), o64[..., 1, :].reshape(*lead, -1)], -1)
+    ref = cat * torch.rsqrt(cat.square().mean(-1, keepdim=True) + 1e-6)
+    ref.backward(du.double())
+    assert u.dtype == torch.float32 and o.grad.dtype == dtype
+    assert relerr(u, ref) < TOL_F32
+    assert relerr(o.grad, o64.grad) < (TOL_F32 if dtype == torch.float32 else 1e-2)
