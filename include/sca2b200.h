@@ -191,6 +191,21 @@ SCA2_API int sca2_sepq_read_fwd(const float* ab, const float* br, const float* b
 SCA2_API int sca2_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_t ld_q,
                        const float* dout, float* dab, float* dbr, float* dbi, int64_t ld_dq,
                        int64_t rows, int32_t dv, float eps_q, float eps, void* stream);
+/* LayerNorm over rows of width d (torch.nn.LayerNorm: biased variance, eps inside the root,
+ * affine weight w and bias b), the layers' pre-norms n / fn (sca2/ref.py:345, 352;
+ * lapa/layer.py:563, 567) and the LM's final norm (lapa/model.py:37).  fp32 rows, 16-byte
+ * aligned; d = 128 ... 1024 in steps of 128 (sca2_layer_norm_supported).  The forward keeps
+ * each row's mean and rstd for the backward. */
+SCA2_API int sca2_layer_norm_supported(int32_t d);
+SCA2_API int sca2_layer_norm_fwd(const float* x, const float* w, const float* b, float* y,
+                        float* mean, float* rstd, int64_t rows, int32_t d, float eps,
+                        void* stream);
+/* Workspace of the backward (floats; the per-CTA partial sums of dw and db). */
+SCA2_API size_t sca2_layer_norm_work_floats(int64_t rows, int32_t d);
+/* dx (rows, d), and dw, db (d) overwritten (either may be NULL). */
+SCA2_API int sca2_layer_norm_bwd(const float* x, const float* w, const float* mean, const float* rstd,
+                        const float* dy, float* dx, float* dw, float* db, void* work,
+                        int64_t rows, int32_t d, void* stream);
 /* RMS read-out of a multi-head read (sca2/arch_gatedc.py:155-156 and _gated_out, :168;
  * lapa/layer.py:384 with H = 1): x rows (rows, H, 2, dvh) contiguous in io_dtype, the heads'
  * [re | im] reads; u rows (rows, 2, H, dvh) fp32 = [re of every head | im of every head] *

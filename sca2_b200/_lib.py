@@ -95,6 +95,12 @@ SIGNATURES = [
     ("sca2_sepq_read_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_float, C.c_float,
                                      C.c_void_p]),
+    ("sca2_layer_norm_supported", C.c_int, [C.c_int32]),
+    ("sca2_layer_norm_fwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_int64, C.c_int32, C.c_float, C.c_void_p]),
+    ("sca2_layer_norm_work_floats", C.c_size_t, [C.c_int64, C.c_int32]),
+    ("sca2_layer_norm_bwd", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p]),
     ("sca2_rms_heads_fwd", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_float,
                                      C.c_void_p]),
     ("sca2_rms_heads_bwd", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_int32,

@@ -42,6 +42,13 @@ cudaError_t launch_rms_heads_fwd(const void* x, int dt, float* out, int64_t rows
                                  cudaStream_t st);
 cudaError_t launch_rms_heads_bwd(const void* x, int dt, const float* dout, void* dx, int64_t rows, int H, int dvh,
                                  float eps, cudaStream_t st);
+// layernorm.cu
+bool ln_supported(int d);
+int ln_bwd_parts(int64_t rows);
+cudaError_t ln_fwd(const float* x, const float* w, const float* b, float* y, float* mean, float* rstd, int64_t rows,
+                   int d, float eps, cudaStream_t st);
+cudaError_t ln_bwd(const float* x, const float* w, const float* mean, const float* rstd, const float* dy, float* dx,
+                   float* dw, float* db, float* part, int64_t rows, int d, cudaStream_t st);
 // dscan.cu
 size_t dscan_work_floats(int B, int T, int M, int G, int V);
 cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
@@ -505,6 +512,43 @@ int sca2_sepq_read_bwd(const float* ab, const float* br, const float* bi, int64_
   cudaError_t e = sca2::launch_sepq_read_bwd(ab, br, bi, ld_q, dout, dab, dbr, dbi, ld_dq, rows, dv, eps_q, eps,
                                              reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "sca2_sepq_read_bwd");
+  return SCA2_OK;
+}
+
+int sca2_layer_norm_supported(int32_t d) { return sca2::ln_supported(d) ? 1 : 0; }
+
+size_t sca2_layer_norm_work_floats(int64_t rows, int32_t d) {
+  return rows > 0 && sca2::ln_supported(d) ? (size_t)sca2::ln_bwd_parts(rows) * 2 * (size_t)d : 0;
+}
+
+static int check_ln(const void* x, const void* w, int64_t rows, int32_t d) {
+  if (rows < 0) return fail(SCA2_ERR_ARG, "layer_norm: bad sizes");
+  if (!sca2::ln_supported(d)) return fail(SCA2_ERR_UNSUPPORTED, "layer_norm: width must be 128 ... 1024 in steps of 128");
+  if (rows > 0 && (!x || !w)) return fail(SCA2_ERR_ARG, "layer_norm: null pointer");
+  if (((uintptr_t)x | (uintptr_t)w) & 15u) return fail(SCA2_ERR_ARG, "layer_norm: rows must be 16-byte aligned");
+  return SCA2_OK;
+}
+
+int sca2_layer_norm_fwd(const float* x, const float* w, const float* b, float* y, float* mean, float* rstd,
+                        int64_t rows, int32_t d, float eps, void* stream) {
+  if (int r = check_ln(x, w, rows, d)) return r;
+  if (rows == 0) return SCA2_OK;
+  if (!b || !y || !mean || !rstd || (((uintptr_t)b | (uintptr_t)y) & 15u))
+    return fail(SCA2_ERR_ARG, "layer_norm: null or misaligned output");
+  cudaError_t e = sca2::ln_fwd(x, w, b, y, mean, rstd, rows, d, eps, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_layer_norm_fwd");
+  return SCA2_OK;
+}
+
+int sca2_layer_norm_bwd(const float* x, const float* w, const float* mean, const float* rstd, const float* dy,
+                        float* dx, float* dw, float* db, void* work, int64_t rows, int32_t d, void* stream) {
+  if (int r = check_ln(x, w, rows, d)) return r;
+  if (rows == 0) return SCA2_OK;
+  if (!mean || !rstd || !dy || !dx || !work || (((uintptr_t)dy | (uintptr_t)dx) & 15u))
+    return fail(SCA2_ERR_ARG, "layer_norm: null or misaligned argument");
+  cudaError_t e = sca2::ln_bwd(x, w, mean, rstd, dy, dx, dw, db, reinterpret_cast<float*>(work), rows, d,
+                               reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_layer_norm_bwd");
   return SCA2_OK;
 }
 

@@ -129,13 +129,21 @@ def _value_dtype(z: torch.Tensor) -> torch.dtype:
     return torch.bfloat16 if z.dtype == torch.bfloat16 else torch.float32
 
 
-def _linear_f32(lin: nn.Linear, x: torch.Tensor) -> torch.Tensor:
-    """lin(x) in float32 whatever the autocast state.  The decay and gate projections feed
-    exponentials whose products run over the whole sequence, so a bf16 rounding of their
-    outputs would compound along it; these projections are a few outputs wide, so float32
-    costs nothing measurable (the state, phases and solve are float32 for the same reason)."""
-    with torch.autocast(device_type=x.device.type, enabled=False):
-        return F.linear(x.float(), lin.weight.float(), None if lin.bias is None else lin.bias.float())
+def _gate_proj(lins, x: torch.Tensor):
+    """[lin(x) for lin in lins] as one product with fp32 outputs whatever the autocast state.
+    The decay and gate projections feed exponentials whose products run over the whole
+    sequence, so a bf16 rounding of their outputs would compound along it.  Under autocast on
+    CUDA the product is ops.linear16 (bf16 hi + lo operands, fp32 accumulation and output:
+    about 16 significant bits, 2^7 finer than a bf16 output); otherwise one fp32 product."""
+    w = torch.cat([lin.weight for lin in lins], 0) if len(lins) > 1 else lins[0].weight
+    sizes = [lin.out_features for lin in lins]
+    if torch.is_autocast_enabled() and x.is_cuda:
+        outs = ops.linear16(x, w, sizes)
+        outs = [o.view(*x.shape[:-1], o.shape[-1]) for o in outs]
+    else:
+        with torch.autocast(device_type=x.device.type, enabled=False):
+            outs = F.linear(x.float(), w.float()).split(sizes, -1)
+    return [o if lin.bias is None else o + lin.bias.float() for o, lin in zip(outs, lins)]
 
 
 def _positions(T: int, pos: torch.Tensor, device) -> torch.Tensor:
@@ -405,7 +413,7 @@ class CHeadGated(CHeadBase):
         return self.K(h).float() * th + p * om, kq.float() * th + p * om
 
     def _logdecay(self, z):
-        return -torch.exp(self.A_log.float()) * F.softplus(_linear_f32(self.a, z) + self.dt_bias.float())
+        return -torch.exp(self.A_log.float()) * F.softplus(_gate_proj((self.a,), z)[0] + self.dt_bias.float())
 
     def prefill(self, z, h, state=None):
         B, T, _ = z.shape
@@ -466,8 +474,8 @@ class DHeadRef(nn.Module):
 
     def _gate(self, h, B, T):
         s2 = 1.0 / math.sqrt(2.0)
-        return (torch.tanh(_linear_f32(self.gr, h)).view(B, T, self.M, self.G) * s2,
-                torch.tanh(_linear_f32(self.gi, h)).view(B, T, self.M, self.G) * s2)
+        sr, si = _gate_proj((self.gr, self.gi), h)
+        return (torch.tanh(sr).view(B, T, self.M, self.G) * s2, torch.tanh(si).view(B, T, self.M, self.G) * s2)
 
     def _scan(self, z, h, state):
         B, T, _ = z.shape
@@ -520,8 +528,8 @@ class DHeadSepQ(nn.Module):
 
     def _gate(self, h, B, T):
         s2 = 1.0 / math.sqrt(2.0)
-        return (torch.tanh(_linear_f32(self.gr, h)).view(B, T, self.M, self.G) * s2,
-                torch.tanh(_linear_f32(self.gi, h)).view(B, T, self.M, self.G) * s2)
+        sr, si = _gate_proj((self.gr, self.gi), h)
+        return (torch.tanh(sr).view(B, T, self.M, self.G) * s2, torch.tanh(si).view(B, T, self.M, self.G) * s2)
 
     def _queries(self, z):
         """The four query projections [qa_r | qa_i] (B,T,2M) and [qb_r | qb_i] (B,T,2dv) as
@@ -572,8 +580,9 @@ class DHeadSepQPolar(DHeadSepQ):
     a = exp(-softplus(gr(h))) e^{i gi(h)}."""
 
     def _gate(self, h, B, T):
-        mag = torch.exp(-F.softplus(_linear_f32(self.gr, h))).view(B, T, self.M, self.G)
-        ph = _linear_f32(self.gi, h).view(B, T, self.M, self.G)
+        sr, si = _gate_proj((self.gr, self.gi), h)
+        mag = torch.exp(-F.softplus(sr)).view(B, T, self.M, self.G)
+        ph = si.view(B, T, self.M, self.G)
         return mag * torch.cos(ph), mag * torch.sin(ph)
 
 

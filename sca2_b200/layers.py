@@ -38,7 +38,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import heads
+from . import heads, ops
 from .heads import LaplaceConfig
 
 
@@ -71,6 +71,19 @@ class LayerCfg:
     gdn_expand_v: float = 1.0
 
 
+class LayerNorm(nn.LayerNorm):
+    """nn.LayerNorm (same parameters and state-dict names) whose CUDA fp32 forward and backward
+    run on this package's row kernels (ops.layer_norm) for the widths they cover; autocast keeps
+    LayerNorm in fp32, as torch does."""
+
+    def forward(self, x):
+        d = self.normalized_shape[-1]
+        if (x.is_cuda and (x.dtype == torch.float32 or torch.is_autocast_enabled()) and self.elementwise_affine
+                and self.bias is not None and len(self.normalized_shape) == 1 and ops.layer_norm_supported(d)):
+            return ops.layer_norm(x, self.weight, self.bias, self.eps)
+        return super().forward(x)
+
+
 Slot = Tuple[str, str]  # (module attribute, state key)
 
 
@@ -80,12 +93,12 @@ class MixerLayer(nn.Module):
     def __init__(self, d: int, slots: Sequence[Tuple[str, str, nn.Module]], mix_in: int, ff: int, conv: int = 0):
         super().__init__()
         self.d = d
-        self.n = nn.LayerNorm(d)
+        self.n = LayerNorm(d)
         self.slots: Tuple[Slot, ...] = tuple((attr, key) for attr, key, _ in slots)
         for attr, _, module in slots:
             self.add_module(attr, module)
         self.mix = nn.Linear(mix_in, d)
-        self.fn = nn.LayerNorm(d)
+        self.fn = LayerNorm(d)
         self.ff = nn.Sequential(nn.Linear(d, ff), nn.GELU(), nn.Linear(ff, d))
         self.k = conv
         if conv:

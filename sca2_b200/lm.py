@@ -21,7 +21,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .heads import LaplaceConfig
-from .layers import GatedLayer, LaplaceAttention, LayerCfg
+from .layers import GatedLayer, LaplaceAttention, LayerCfg, LayerNorm
 
 
 class LM(nn.Module):
@@ -38,7 +38,7 @@ class LM(nn.Module):
         self.d, self.vocab = d, vocab
         self.embed = nn.Embedding(vocab, d)
         self.layers = nn.ModuleList(layer_factory(i) for i in range(n_layers))
-        self.norm = nn.LayerNorm(d)
+        self.norm = LayerNorm(d)
         self.head = nn.Linear(d, vocab, bias=False)
         if tie_embeddings:
             self.head.weight = self.embed.weight

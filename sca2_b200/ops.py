@@ -8,6 +8,7 @@
     rms(x, eps)                                           per-row RMS read-out
     sepq_read(ab, q)                                      separable D-head read-out + RMS
     rms_heads(o)                                          multi-head read gathered + RMS
+    layer_norm(x, w, b, eps)                              the layers' LayerNorm (fwd + bwd kernels)
     linear16(x, w, sizes)                                 x w^T to 16 bits on bf16 tensor cores
 
 Every op runs the CUDA kernels of libsca2b200.so on the current stream.  There is no
@@ -1068,6 +1069,77 @@ def sepq_read(ab: torch.Tensor, q: torch.Tensor, eps_q: float = 1e-6, eps: float
     if ab.dtype != torch.float32 or q.dtype != torch.float32:
         raise TypeError("sepq_read takes fp32 ab and q")
     return torch.ops.sca2b200.sepq_read_fwd(ab.contiguous(), q, float(eps_q), float(eps))
+
+
+@torch.library.custom_op("sca2b200::layer_norm_fwd", mutates_args=())
+def _layer_norm_fwd(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor,
+                    eps: float) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_layer_norm_fwd: x (..., d) fp32 contiguous -> y, and the rows' mean and rstd."""
+    d = x.shape[-1]
+    rows = x.numel() // d
+    y = torch.empty_like(x)
+    mean = torch.empty(rows, device=x.device, dtype=torch.float32)
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.load().sca2_layer_norm_fwd(x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), mean.data_ptr(),
+                                               rstd.data_ptr(), rows, d, float(eps), _stream()), "layer_norm_fwd")
+    return y, mean, rstd
+
+
+@_layer_norm_fwd.register_fake
+def _(x, w, b, eps):
+    rows = x.numel() // x.shape[-1]
+    return torch.empty_like(x), x.new_empty(rows), x.new_empty(rows)
+
+
+@torch.library.custom_op("sca2b200::layer_norm_bwd", mutates_args=())
+def _layer_norm_bwd(x: torch.Tensor, w: torch.Tensor, mean: torch.Tensor, rstd: torch.Tensor,
+                    dy: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """sca2_layer_norm_bwd: dx, dw, db."""
+    d = x.shape[-1]
+    rows = x.numel() // d
+    lib = _lib.load()
+    dy = dy.float().contiguous()
+    dx = torch.empty_like(x)
+    dw = torch.empty(d, device=x.device, dtype=torch.float32)
+    db = torch.empty(d, device=x.device, dtype=torch.float32)
+    work = torch.empty(max(1, lib.sca2_layer_norm_work_floats(rows, d)), device=x.device, dtype=torch.float32)
+    _lib.check(lib.sca2_layer_norm_bwd(x.data_ptr(), w.data_ptr(), mean.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
+                                       dx.data_ptr(), dw.data_ptr(), db.data_ptr(), work.data_ptr(), rows, d,
+                                       _stream()), "layer_norm_bwd")
+    return dx, dw, db
+
+
+@_layer_norm_bwd.register_fake
+def _(x, w, mean, rstd, dy):
+    return torch.empty_like(x), w.new_empty(w.shape), w.new_empty(w.shape)
+
+
+def _ln_setup(ctx, inputs, output):
+    x, w, _, _ = inputs
+    _, mean, rstd = output
+    ctx.save_for_backward(x, w, mean, rstd)
+
+
+def _ln_backward(ctx, dy, _dmean, _drstd):
+    x, w, mean, rstd = ctx.saved_tensors
+    dx, dw, db = torch.ops.sca2b200.layer_norm_bwd(x, w, mean, rstd, dy)
+    return dx, dw, db, None
+
+
+_layer_norm_fwd.register_autograd(_ln_backward, setup_context=_ln_setup)
+
+
+def layer_norm_supported(d: int) -> bool:
+    return bool(_lib.load().sca2_layer_norm_supported(int(d)))
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """torch.nn.functional.layer_norm over the last dimension on the fused row kernels (fp32;
+    d = 128 ... 1024 in steps of 128, layer_norm_supported)."""
+    _need_cuda(x, w, b)
+    y, _, _ = torch.ops.sca2b200.layer_norm_fwd(x.float().contiguous(), w.float().contiguous(),
+                                                b.float().contiguous(), float(eps))
+    return y
 
 
 @torch.library.custom_op("sca2b200::rms_heads_fwd", mutates_args=())

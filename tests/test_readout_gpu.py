@@ -95,3 +95,24 @@ def test_rms_heads_vs_torch(dtype, lead, H, dvh):
     assert u.dtype == torch.float32 and o.grad.dtype == dtype
     assert relerr(u, ref) < TOL_F32
     assert relerr(o.grad, o64.grad) < (TOL_F32 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("d,rows", [(1024, 300), (768, 33), (128, 5000), (384, 1)])
+def test_layer_norm_vs_torch(d, rows):
+    """The layers' LayerNorm kernels against torch.nn.functional.layer_norm in float64: output,
+    input, weight and bias gradients (fp32 bar), many rows per CTA in the backward's sums."""
+    from sca2_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(d + rows)
+    x = (3 * torch.randn(rows, d, device="cuda", generator=g) + 1).requires_grad_(True)
+    w = torch.randn(d, device="cuda", generator=g).requires_grad_(True)
+    b = torch.randn(d, device="cuda", generator=g).requires_grad_(True)
+    dy = torch.randn(rows, d, device="cuda", generator=g)
+    assert ops.layer_norm_supported(d)
+    y = ops.layer_norm(x, w, b, 1e-5)
+    y.backward(dy)
+    x64, w64, b64 = (t.detach().double().requires_grad_(True) for t in (x, w, b))
+    ref = torch.nn.functional.layer_norm(x64, (d,), w64, b64, 1e-5)
+    ref.backward(dy.double())
+    assert relerr(y, ref) < TOL_F32
+    for t, r in ((x, x64), (w, w64), (b, b64)):
+        assert relerr(t.grad, r.grad) < TOL_F32
