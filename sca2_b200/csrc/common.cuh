@@ -27,6 +27,23 @@ __device__ __forceinline__ int64_t out_off(const sca2_out& t, int b, int tt, int
   return (int64_t)b * t.sb + (int64_t)tt * t.st + (int64_t)h * t.sh + (int64_t)r * t.sr;
 }
 
+// ---- sine and cosine of large phases -----------------------------------------------------
+// Cody and Waite's additive reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
+// Functions", 1980): r = x - k 2pi with k = rint(x / 2pi) and 2pi split into three parts, the
+// first with only 9 significant bits so k * part1 is exact for |k| < 2^15 (|x| < 2e5), then the
+// SFU sine / cosine on r in [-pi, pi] (absolute error about 1e-6 for the phases of this scan).
+__device__ __forceinline__ void sincos_big(float x, float* s, float* c) {
+  constexpr float kInv2Pi = 0.15915494309189535f;
+  constexpr float kP1 = 6.28125f;                   // 2pi rounded to 9 bits
+  constexpr float kP2 = 1.9353071795864769e-3f;     // 2pi - kP1, rounded to fp32
+  constexpr float kP3 = 1.0253131677018246e-11f;    // 2pi - kP1 - kP2, rounded to fp32
+  const float k = rintf(x * kInv2Pi);
+  float r = fmaf(-k, kP1, x);
+  r = fmaf(-k, kP2, r);
+  r = fmaf(-k, kP3, r);
+  __sincosf(r, s, c);
+}
+
 // Slots of the saved-state buffer (B,H,slots,K,V) for T tokens: four per 64-token chunk.  The
 // fp32 path keeps the state entering its 32-token chunk c in slot c; the tensor-core path keeps
 // the state entering its 64-token chunk c in slot 2c, its saved T and E in slot 2c+1 and its

@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float s = 0.f, co = 0.f;
-      if (i < Cl) tc::sincos_big(cr.w[0][k], &s, &co);
+      if (i < Cl) sincos_big(cr.w[0][k], &s, &co);
       const float l = s_lam[m0 + k];
       const float ell = __expf(-l * fi), elli = __expf(l * fi);
       const float el1 = __expf(-l * (fi + 1.f)), ec = wv * __expf(-l * (float)(Cl - 1 - i));
@@ -547,8 +547,8 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     for (int k = 0; k < 8; ++k) {
       float s = 0.f, co = 0.f, sq = 0.f, cq = 0.f;
       if (ci < Cl) {
-        tc::sincos_big(cr.w[0][k], &s, &co);
-        tc::sincos_big(cr.q[0][k], &sq, &cq);
+        sincos_big(cr.w[0][k], &s, &co);
+        sincos_big(cr.q[0][k], &sq, &cq);
       }
       const float l = s_lam[cm0 + k];
       const float ell = __expf(-l * fi), elli = __expf(l * fi), el1 = __expf(-l * (fi + 1.f));

@@ -14,7 +14,8 @@
 // would turn that exact zero into a visible leak between lags.  The work is small (L (2L + 2dv)
 // multiply-adds per token) and independent across tokens, so each CTA takes TT consecutive
 // queries of one sequence and the L-1 keys before them; the codes (sin / cos of the phases,
-// computed here from K(h), K(z), theta, omega and the position), kappa and the values sit in
+// computed here from K(h), K(z), theta, omega and the position by the Cody-Waite reduction and
+// the SFU, absolute error about 1e-6, so the comb's leak stays near L * 1e-6), kappa and the values sit in
 // shared memory.  The inner products are register-blocked: a thread owns one token row and a
 // group of 4 lags, 4 modes or 8 value columns, lanes of a warp walk consecutive rows, and the
 // row strides (a multiple of 4 floats, = 4 mod 32 banks) make the 16-byte loads of 8
@@ -81,7 +82,7 @@ __device__ __forceinline__ void key_code(const sca2_short_args& p, const Geo& g,
     *sn = p.s0 ? p.s0[k] : 0.f;
   } else {
     const float ph = p.kh[((int64_t)b * g.T + s) * g.L + l] * p.theta[l] + ppos(g, s) * p.omega[l];
-    sincosf(ph, sn, c);
+    sincos_big(ph, sn, c);
   }
 }
 __device__ __forceinline__ float key_value(const sca2_short_args& p, const Geo& g, int b, int s, int j) {
@@ -110,7 +111,7 @@ __device__ __forceinline__ void load_queries(const sca2_short_args& p, const Geo
     float c = 0.f, s = 0.f, wr = 0.f, wi = 0.f;
     if (l < g.L) {
       const float ph = p.kz[((int64_t)b * g.T + t) * g.L + l] * p.theta[l] + ppos(g, t) * p.omega[l];
-      sincosf(ph, &s, &c);
+      sincos_big(ph, &s, &c);
       wr = p.wr[l];
       wi = p.wi[l];
     }

@@ -81,23 +81,6 @@ __device__ __forceinline__ void for_frag(uint32_t tbase, F f) {
   }
 }
 
-// ---- sine and cosine of large phases -----------------------------------------------------
-// Cody and Waite's additive reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
-// Functions", 1980): r = x - k 2pi with k = rint(x / 2pi) and 2pi split into three parts, the
-// first with only 9 significant bits so k * part1 is exact for |k| < 2^15 (|x| < 2e5), then the
-// SFU sine / cosine on r in [-pi, pi] (absolute error about 1e-6 for the phases of this scan).
-__device__ __forceinline__ void sincos_big(float x, float* s, float* c) {
-  constexpr float kInv2Pi = 0.15915494309189535f;
-  constexpr float kP1 = 6.28125f;                   // 2pi rounded to 9 bits
-  constexpr float kP2 = 1.9353071795864769e-3f;     // 2pi - kP1, rounded to fp32
-  constexpr float kP3 = 1.0253131677018246e-11f;    // 2pi - kP1 - kP2, rounded to fp32
-  const float k = rintf(x * kInv2Pi);
-  float r = fmaf(-k, kP1, x);
-  r = fmaf(-k, kP2, r);
-  r = fmaf(-k, kP3, r);
-  __sincosf(r, s, c);
-}
-
 // ---- asynchronous global -> shared copies (16 bytes; zero-filled when !valid) ----------------
 __device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(umma::smem_u32(dst)), "l"(src),
