@@ -584,6 +584,148 @@ inline bool use_blocks(const sca2_dscan_args& p, const float* work) {
   return work != nullptr && p.T > 4 * CK && (p.T + CK - 1) / CK <= 65535;
 }
 
+// ---- the folds over the blocks in three passes (long sequences) -------------------------
+// out[k] = s; s = A_k s + c_k over the blocks k in fold order (ascending: the forward's
+// checkpoints, A = P, c = e; descending: the adjoint entering each block from the right,
+// A = Q, c = q).  With NK blocks one thread per (b, m, j) would take NK dependent steps, so
+// the blocks are taken in groups of FG: (1) every group's composed map (A_g, c_g) in
+// parallel, (2) one fold over the groups giving the state entering each group and the final
+// state, (3) every group's blocks from its entering state in parallel.  Each pass loads its
+// group's inputs into registers before the dependent updates.
+constexpr int FG = 16;
+// floats of e + P + checkpoints (forward) or q + R + Q (backward)
+inline size_t dscan_base_floats(int B, int NK, int M, int G, int V) {
+  return (size_t)B * NK * 2 * (2 * (size_t)M * V + (size_t)M * G);
+}
+struct FoldIO {
+  const float* A;  // [(b NK + k) 2 + r][M][G]
+  const float* c;  // [(b NK + k) 2 + r][M][V]
+  float* Ag;       // [(b NG + g) 2 + r][M][G]  group maps (pass 1 -> 2)
+  float* cg;       // [(b NG + g) 2 + r][M][V]
+  float* Sg;       // [(b NG + g) 2 + r][M][V]  state entering each group (pass 2 -> 3)
+  int NK, NG;
+  bool rev;
+};
+// block of the i-th step of group gi in fold order, or -1 past the sequence
+__device__ __forceinline__ int fold_block(const FoldIO& f, int gi, int i) {
+  const int k0 = gi * FG + i;
+  if (k0 >= f.NK) return -1;
+  return f.rev ? f.NK - 1 - k0 : k0;
+}
+
+template <int M>
+__device__ __forceinline__ void fold_load(const sca2_dscan_args& p, const FoldIO& f, const Map& q, int gi, float* ar,
+                                          float* ai, float* cr, float* ci) {
+  const int V = p.V, G = p.G;
+#pragma unroll
+  for (int u = 0; u < FG; ++u) {
+    const int k = fold_block(f, gi, u);
+    const int64_t base = ((int64_t)q.b * f.NK + (k < 0 ? 0 : k)) * 2;
+    ar[u] = k < 0 ? 1.f : f.A[base * M * G + (int64_t)q.m * G + q.g];
+    ai[u] = k < 0 ? 0.f : f.A[(base + 1) * M * G + (int64_t)q.m * G + q.g];
+    cr[u] = k < 0 ? 0.f : f.c[base * M * V + (int64_t)q.m * V + q.j];
+    ci[u] = k < 0 ? 0.f : f.c[(base + 1) * M * V + (int64_t)q.m * V + q.j];
+  }
+}
+
+template <int M>
+__global__ void __launch_bounds__(NT) dscan_fold_groups(sca2_dscan_args p, FoldIO f) {
+  const Map q = chan_map<M>(p, blockIdx.z);
+  if (!q.live) return;
+  const int gi = blockIdx.y, V = p.V, G = p.G;
+  float ar[FG], ai[FG], cr[FG], ci[FG];
+  fold_load<M>(p, f, q, gi, ar, ai, cr, ci);
+  float Pr = 1.f, Pi = 0.f, xr = 0.f, xi = 0.f;  // the composed map s -> (Pr + i Pi) s + (xr + i xi)
+#pragma unroll
+  for (int u = 0; u < FG; ++u) {
+    const float nPr = ar[u] * Pr - ai[u] * Pi, nPi = ar[u] * Pi + ai[u] * Pr;
+    const float nxr = ar[u] * xr - ai[u] * xi + cr[u], nxi = ar[u] * xi + ai[u] * xr + ci[u];
+    Pr = nPr, Pi = nPi, xr = nxr, xi = nxi;
+  }
+  const int64_t gb = ((int64_t)q.b * f.NG + gi) * 2;
+  f.cg[gb * M * V + (int64_t)q.m * V + q.j] = xr;
+  f.cg[(gb + 1) * M * V + (int64_t)q.m * V + q.j] = xi;
+  if (q.j % (V / G) == 0) {
+    f.Ag[gb * M * G + (int64_t)q.m * G + q.g] = Pr;
+    f.Ag[(gb + 1) * M * G + (int64_t)q.m * G + q.g] = Pi;
+  }
+}
+
+template <int M>
+__global__ void __launch_bounds__(NT) dscan_fold_top(sca2_dscan_args p, FoldIO f, const float* s_re, const float* s_im,
+                                                     float* fin_re, float* fin_im) {
+  const Map q = chan_map<M>(p, blockIdx.y);
+  if (!q.live) return;
+  const int V = p.V, G = p.G;
+  const int64_t sidx = ((int64_t)q.b * M + q.m) * V + q.j;
+  float sr = s_re ? s_re[sidx] : 0.f, si = s_im ? s_im[sidx] : 0.f;
+  for (int g0 = 0; g0 < f.NG; g0 += FG) {
+    float ar[FG], ai[FG], cr[FG], ci[FG];
+#pragma unroll
+    for (int u = 0; u < FG; ++u) {
+      const int64_t gb = ((int64_t)q.b * f.NG + min(g0 + u, f.NG - 1)) * 2;
+      ar[u] = f.Ag[gb * M * G + (int64_t)q.m * G + q.g];
+      ai[u] = f.Ag[(gb + 1) * M * G + (int64_t)q.m * G + q.g];
+      cr[u] = f.cg[gb * M * V + (int64_t)q.m * V + q.j];
+      ci[u] = f.cg[(gb + 1) * M * V + (int64_t)q.m * V + q.j];
+    }
+#pragma unroll
+    for (int u = 0; u < FG; ++u) {
+      if (g0 + u >= f.NG) break;
+      const int64_t gb = ((int64_t)q.b * f.NG + g0 + u) * 2;
+      f.Sg[gb * M * V + (int64_t)q.m * V + q.j] = sr;
+      f.Sg[(gb + 1) * M * V + (int64_t)q.m * V + q.j] = si;
+      const float nr = ar[u] * sr - ai[u] * si + cr[u];
+      si = ar[u] * si + ai[u] * sr + ci[u];
+      sr = nr;
+    }
+  }
+  if (fin_re) fin_re[sidx] = sr;
+  if (fin_im) fin_im[sidx] = si;
+}
+
+template <int M>
+__global__ void __launch_bounds__(NT) dscan_fold_blocks(sca2_dscan_args p, FoldIO f, float* out) {
+  const Map q = chan_map<M>(p, blockIdx.z);
+  if (!q.live) return;
+  const int gi = blockIdx.y, V = p.V;
+  float ar[FG], ai[FG], cr[FG], ci[FG];
+  fold_load<M>(p, f, q, gi, ar, ai, cr, ci);
+  const int64_t gb = ((int64_t)q.b * f.NG + gi) * 2;
+  float sr = f.Sg[gb * M * V + (int64_t)q.m * V + q.j], si = f.Sg[(gb + 1) * M * V + (int64_t)q.m * V + q.j];
+#pragma unroll
+  for (int u = 0; u < FG; ++u) {
+    const int k = fold_block(f, gi, u);
+    if (k < 0) break;
+    const int64_t base = ((int64_t)q.b * f.NK + k) * 2;
+    out[base * M * V + (int64_t)q.m * V + q.j] = sr;
+    out[(base + 1) * M * V + (int64_t)q.m * V + q.j] = si;
+    const float nr = ar[u] * sr - ai[u] * si + cr[u];
+    si = ar[u] * si + ai[u] * sr + ci[u];
+    sr = nr;
+  }
+}
+
+// the three passes; `gw` holds Ag, cg, Sg (dscan_fold_floats)
+inline size_t fold_floats(int B, int NK, int M, int G, int V) {
+  const size_t NG = (size_t)((NK + FG - 1) / FG);
+  return (size_t)B * NG * 2 * (2 * (size_t)M * V + (size_t)M * G);
+}
+template <int M>
+cudaError_t launch_fold(const sca2_dscan_args& p, const float* A, const float* c, float* out, const float* s_re,
+                        const float* s_im, float* fin_re, float* fin_im, bool rev, float* gw, cudaStream_t st) {
+  const int NK = (p.T + CK - 1) / CK, NG = (NK + FG - 1) / FG, tiles = (M * p.V + NT - 1) / NT;
+  FoldIO f;
+  f.A = A, f.c = c, f.NK = NK, f.NG = NG, f.rev = rev;
+  f.cg = gw;
+  f.Sg = gw + (size_t)p.B * NG * 2 * M * p.V;
+  f.Ag = f.Sg + (size_t)p.B * NG * 2 * M * p.V;
+  dscan_fold_groups<M><<<dim3(p.B, NG, tiles), NT, 0, st>>>(p, f);
+  dscan_fold_top<M><<<dim3(p.B, tiles), NT, 0, st>>>(p, f, s_re, s_im, fin_re, fin_im);
+  dscan_fold_blocks<M><<<dim3(p.B, NG, tiles), NT, 0, st>>>(p, f, out);
+  return cudaGetLastError();
+}
+
 // dynamic shared memory of a staged block pass, and the opt-in for more than 48 KB
 template <int M>
 inline int stage_bytes(const sca2_dscan_args& p) {
@@ -614,7 +756,12 @@ cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float
   cudaError_t err = allow_smem(dscan_fwd_local<M>, sm);
   if (err != cudaSuccess) return err;
   dscan_fwd_local<M><<<gl, NT, sm, st>>>(p, e, P);
-  dscan_fwd_carry<M><<<gc, NT, 0, st>>>(p, e, P, ck, S_re, S_im);
+  if (NK > 2 * FG) {  // long sequences: the fold in three passes
+    float* gw = e + dscan_base_floats(p.B, NK, M, p.G, p.V);
+    if ((err = launch_fold<M>(p, P, e, ck, p.S0_re, p.S0_im, S_re, S_im, false, gw, st)) != cudaSuccess) return err;
+  } else {
+    dscan_fwd_carry<M><<<gc, NT, 0, st>>>(p, e, P, ck, S_re, S_im);
+  }
   if (p.sep) {
     if ((err = allow_smem(dscan_fwd_out<M, true>, sm)) != cudaSuccess) return err;
     dscan_fwd_out<M, true><<<gl, NT, sm, st>>>(p, ck, ab);
@@ -644,7 +791,12 @@ cudaError_t launch_bwd_m(const sca2_dscan_args& p, const float* dab, const float
   cudaError_t err = allow_smem(kl, sm);
   if (err != cudaSuccess) return err;
   kl<<<gl, NT, sm, st>>>(p, dab, qv, Qg);
-  dscan_bwd_carry<M><<<gc, NT, 0, st>>>(p, dS_re, dS_im, qv, Qg, R, g);
+  if (NK > 2 * FG) {  // long sequences: the reverse fold in three passes
+    float* gw = qv + dscan_base_floats(p.B, NK, M, p.G, p.V);
+    if ((err = launch_fold<M>(p, Qg, qv, R, dS_re, dS_im, g.dS0_re, g.dS0_im, true, gw, st)) != cudaSuccess) return err;
+  } else {
+    dscan_bwd_carry<M><<<gc, NT, 0, st>>>(p, dS_re, dS_im, qv, Qg, R, g);
+  }
   const int ngl = ngl_max(M, p.V / p.G);
   const int red = ((p.sep ? CK * M * 2 : 0) + CK * M * ngl * 2) * (int)sizeof(float) + (p.sep ? sm : 0);
   auto kb = p.sep ? dscan_bwd_block<M, true> : dscan_bwd_block<M, false>;
@@ -656,10 +808,10 @@ cudaError_t launch_bwd_m(const sca2_dscan_args& p, const float* dab, const float
 }  // namespace dscan
 
 // workspace of the chunk-parallel forms (floats): fwd e + P (+ checkpoints when the caller
-// keeps none), bwd q + R + Q
+// keeps none), bwd q + R + Q; then the three-pass fold's group maps and entering states
 size_t dscan_work_floats(int B, int T, int M, int G, int V) {
-  const size_t NK = (size_t)((T + dscan::CK - 1) / dscan::CK);
-  return (size_t)B * NK * 2 * (2 * (size_t)M * V + (size_t)M * G);
+  const int NK = (T + dscan::CK - 1) / dscan::CK;
+  return dscan::dscan_base_floats(B, NK, M, G, V) + dscan::fold_floats(B, NK, M, G, V);
 }
 
 cudaError_t dscan_fwd(const sca2_dscan_args& p, float* ab, float* S_re, float* S_im, float* ckpt, float* work,
