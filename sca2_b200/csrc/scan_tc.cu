@@ -72,8 +72,9 @@ struct FwdLayout {
   static constexpr int WS = TS + al(C * LDF * 4);               //   fp32 1024
   static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(1024 * 4));
   // scalars (floats): two sets of gates beta[C], Gc[C], a[C], w[C] (this chunk, next chunk),
-  // d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD], a of the previous chunk [C]
-  static constexpr int SC_FLOATS = 9 * C + 5 * KD;
+  // d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD], a of the previous chunk [C], the column factors
+  // of the decay mask [C]
+  static constexpr int SC_FLOATS = 10 * C + 5 * KD;
   // fp32 KD x VB staging of the state to save [m][v], where it fits the 227 KB opt-in limit
   static constexpr bool STAGE = A0_END + al(KD * VB * 4) + al(SC_FLOATS * 4) + 64 <= 227 * 1024;
   static constexpr int ST = A0_END;
@@ -102,7 +103,7 @@ __device__ __forceinline__ void copy_out(uint8_t* dst, const bf16* src, int nbyt
     *reinterpret_cast<uint4*>(dst + u) = *reinterpret_cast<const uint4*>(s + u);
 }
 
-template <int FL, int KD, int VB, int R>
+template <int FL, int KD, int VB, int R, bool HG>
 __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
                                                     float* cstates, int NCS, int flags, PhaseProj pp) {
   using L = FwdLayout<KD, VB, R>;
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   const int bh = blockIdx.x, b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int vb0 = blockIdx.y * VB;
   const int V = p.V;
-  const bool has_g = p.g.ptr != nullptr;
+  constexpr bool has_g = HG;  // a per-token scalar decay (p.g) is present
   const float kappa = FL == SCA2_FLAVOR_PHASE ? (float)(KD / 2) : 1.f;
   const float ik = 1.f / kappa;
   float* sc = reinterpret_cast<float*>(sm + L::SC);
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   float* s_wr = s_lam + KD;
   float* s_wi = s_wr + KD;
   float* s_aprev = s_wi + KD;
+  float* s_fdec = s_aprev + C;  // column factors of the decay mask (decay_block)
   float* LS = reinterpret_cast<float*>(sm + L::LS);
   float* TS = reinterpret_cast<float*>(sm + L::TS);
   float* WS = reinterpret_cast<float*>(sm + L::WS);
@@ -321,6 +323,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     const Gates gates = gset(c);
     cp_wait_all();
     for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * (float)(Cl - 1));
+    if (has_g) decay_factors(gates.Gc, s_fdec);
     kww_from_kw<FL, KD, R>(cops, gates);
     if (p.v_times_beta) {
       __syncthreads();  // every thread's value copies have landed
@@ -356,24 +359,24 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     if (!(ok = wait_mma())) break;
     // ---- L = beta Gr (fp32) and P (hi + lo), masked and decayed
     if (!prep) for_frag<64, 64>(tb + CO::G, [&](int i, int j0, int, const float* x) {
-      const float bi = gates.beta[i] * ik, gi = gates.Gc[i];
+      const float bi = gates.beta[i] * ik;
+      float dg[16];
+      if (has_g) decay_block(gates.Gc, s_fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
-        LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
+        LS[i * LDF + jj] = jj < i ? bi * x[j] * (has_g ? dg[j] : 1.f) : 0.f;
       }
     });
     {
       auto p_epi = [&](int row, int j0, int, const float* x) {
         const int i = row & 63;
-        const float gi = gates.Gc[i];
-        float y[16];
+        float y[16], dg[16];
+        if (has_g) decay_block(gates.Gc, s_fdec, i, j0, dg);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int jj = j0 + j;
-          const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
-          y[j] = jj <= i ? x[j] * ik * dg : 0.f;
+          y[j] = jj <= i ? x[j] * ik * (has_g ? dg[j] : 1.f) : 0.f;
         }
         st8_split(PB, PBL, umma::kmaj(row, j0, C), y);
         st8_split(PB, PBL, umma::kmaj(row, j0 + 8, C), y + 8);
@@ -506,7 +509,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
 template <int FL, int KD, int VB, int R>
 cudaError_t launch_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates,
                        int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
-  auto k = scan_fwd_tc<FL, KD, VB, R>;
+  auto k = p.g.ptr ? scan_fwd_tc<FL, KD, VB, R, true> : scan_fwd_tc<FL, KD, VB, R, false>;
   const int smem = FwdLayout<KD, VB, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

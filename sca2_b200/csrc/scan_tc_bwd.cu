@@ -342,11 +342,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   float* s_dwr = s_dlam + KD;
   float* s_dwi = s_dwr + KD;
   float* s_misc = s_dwi + KD;
-  // decay mask Dg(i, j) = exp(Gc_i - Gc_j), j <= i.  For a 16-column block left of row i (its
-  // last column jl < i) it factors as exp(Gc_i - Gc_jl) * s_fdec[j], s_fdec[j] = exp(Gc_jl - Gc_j):
-  // both factors <= 1 (Gc is non-increasing), so neither overflows; the row's own block takes
-  // the exponential of each difference
-  float* s_fdec = s_misc + 8 + 4 * C;
+  float* s_fdec = s_misc + 8 + 4 * C;  // column factors of the decay mask (decay_block)
   auto BF = [&](int off) { return reinterpret_cast<bf16*>(sm + off); };
   float* CST = reinterpret_cast<float*>(sm + L::CST);
   float* cache = reinterpret_cast<float*>(sm + L::CACHE);
@@ -420,35 +416,13 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     umma::fence_after_sync();
     return *s_err == 0;
   };
-  // Dg of row i over the 16 columns j0.. (zeros right of the row; 1 without a decay).  The
-  // row's own block is factored too when no 16-token block of the chunk decays by more than
-  // e^80 (fast, a CTA-uniform flag): exp(Gc_i - Gc_jl) <= e^80 stays finite, products clamped at 1
-  auto dg_block = [&](int i, int j0, bool fast, float* d) {
+  // Dg of row i over the 16 columns j0.. (zeros right of the row; 1 without a decay)
+  auto dg_block = [&](int i, int j0, float* d) {
     if (!has_g) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) d[j] = 1.f;
-    } else if (j0 + 15 < i) {
-      const float r = __expf(gates.Gc[i] - gates.Gc[j0 + 15]);
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(s_fdec + j0 + j);
-        d[j] = r * f.x, d[j + 1] = r * f.y, d[j + 2] = r * f.z, d[j + 3] = r * f.w;
-      }
-    } else if (j0 <= i && fast) {
-      const float r = __expf(gates.Gc[i] - gates.Gc[j0 + 15]);
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(s_fdec + j0 + j);
-        d[j] = fminf(r * f.x, 1.f), d[j + 1] = fminf(r * f.y, 1.f);
-        d[j + 2] = fminf(r * f.z, 1.f), d[j + 3] = fminf(r * f.w, 1.f);
-      }
-    } else if (j0 <= i) {
-      const float gi = gates.Gc[i];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) d[j] = __expf(fminf(gi - gates.Gc[j0 + j], 0.f));
     } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) d[j] = 0.f;
+      decay_block(gates.Gc, s_fdec, i, j0, d);
     }
   };
   const int64_t bhs = ((int64_t)b * p.H + h) * NCS;
@@ -494,11 +468,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       s_cols[tid] = 0.f;
     }
     if (tid == 0) s_misc[0] = 0.f;
-    if (has_g && tid < C) s_fdec[tid] = __expf(gates.Gc[tid | 15] - gates.Gc[tid]);
-    // staged copies, gates, dCm1 and the decay factors visible; whether every 16-token block
-    // decays by at most e^80 (the own-block factoring of the decay mask)
-    const bool dg_fast =
-        !__syncthreads_or(has_g && tid < C && (tid & 15) == 0 && gates.Gc[tid] - gates.Gc[tid | 15] > 80.f);
+    if (has_g) decay_factors(gates.Gc, s_fdec);
+    __syncthreads();  // staged copies, gates, dCm1 and the decay factors visible
     if (gstage) {  // this chunk's gradient rows, needed by the finish (first group of the chunk)
       pf_grad_rows<KH>(GRW, gr.dphw, b, h, t0, Cl);
       pf_grad_rows<KH>(GRQ, gr.dphq, b, h, t0, Cl);
@@ -636,7 +607,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         }
         float dkk[16], dkw[16], gcol[16], dgv[16];
         float sb = 0.f, srow_ = 0.f;
-        dg_block(i, j0, dg_fast, dgv);
+        dg_block(i, j0, dgv);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int jj = j0 + j;
@@ -684,7 +655,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         }
         float dqk[16], dqw[16], gcol[16], dgv[16];
         float srow_ = 0.f;
-        dg_block(i, j0, dg_fast, dgv);
+        dg_block(i, j0, dgv);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float pa[8];  // P of the row's 8 columns (one 16-byte load)

@@ -258,6 +258,41 @@ __device__ __forceinline__ void code_unit(int u, int& i, int& m0) {
 struct Gates {
   float *beta, *Gc, *a, *w;
 };
+
+// ---- the decay mask Dg(i, j) = exp(Gc_i - Gc_j), j <= i, of a chunk --------------------------
+// Gc is non-increasing along the chunk.  Per 16-column block (last column jl) the column
+// factors fdec[j] = exp(Gc_jl - Gc_j) <= 1 are formed once per chunk (threads 0..63); a block
+// left of row i (jl < i) is then exp(Gc_i - Gc_jl) * fdec[j], both factors <= 1, so one
+// exponential per row and block.  The row's own block is factored the same way (the row factor
+// >= 1, products clamped at 1) unless that block decays by more than e^80, where it takes one
+// exponential per element; blocks right of the row are zero.
+__device__ __forceinline__ void decay_factors(const float* Gc, float* fdec) {
+  const int t = threadIdx.x;
+  if (t < C) fdec[t] = __expf(Gc[t | 15] - Gc[t]);
+}
+__device__ __forceinline__ void decay_block(const float* Gc, const float* fdec, int i, int j0, float* d) {
+  const float gl = Gc[j0 + 15];
+  if (j0 > i) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) d[j] = 0.f;
+  } else if (j0 + 15 < i || Gc[j0] - gl <= 80.f) {
+    const float r = __expf(Gc[i] - gl);
+    const bool own = j0 + 15 >= i;
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float4 f = *reinterpret_cast<const float4*>(fdec + j0 + j);
+      d[j] = r * f.x, d[j + 1] = r * f.y, d[j + 2] = r * f.z, d[j + 3] = r * f.w;
+    }
+    if (own) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) d[j] = fminf(d[j], 1.f);
+    }
+  } else {
+    const float gi = Gc[i];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) d[j] = __expf(fminf(gi - Gc[j0 + j], 0.f));
+  }
+}
 // ---- per-thread register prefetch of a chunk's code inputs and gates ----------------------------
 // Codes: phase flavour, thread t holds (token t/4, modes 8(t%4)..+7) of phi and psi; key flavour,
 // units t and t+256 of (token u/8, dims 8(u%8)..+7) of k and q.  vec: 16-byte loads are aligned.
