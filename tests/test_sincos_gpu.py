@@ -1,6 +1,6 @@
 """sincos_big (Cody-Waite reduction + SFU sine/cosine, used to build the phase codes of the
-tensor-core kernels) against float64 and against CUDA's sincosf over the phase range of the
-benchmark workload (|phi| up to pi * 4096 plus noise)."""
+tensor-core kernels and of the short head) against float64 and against CUDA's sincosf over
+the phase range of the benchmark workload (|phi| up to pi * 4096 plus noise)."""
 import ctypes
 import os
 import subprocess
