@@ -144,11 +144,19 @@ __device__ __forceinline__ bool batch_wait(uint64_t* mbar, uint32_t parity) {
   return !bad;
 }
 
-__device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates& g, int b, int h, int t0, int Cl) {
+// (warp 0) and, with a decay, the column factors of the decay mask (tc::decay_factors) in fdec
+__device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates& g, int b, int h, int t0, int Cl,
+                                           float* fdec) {
   if ((threadIdx.x >> 5) == 0) {
     tc::GateRegs gr;
     tc::load_gate_regs(p, gr, b, h, t0, Cl);
     tc::gates_from_regs(gr, g, Cl);
+    if (p.g.ptr) {
+      __syncwarp();
+      const int l = threadIdx.x & 31;
+      fdec[l] = __expf(g.Gc[l | 15] - g.Gc[l]);
+      fdec[l + 32] = __expf(g.Gc[(l | 15) + 32] - g.Gc[l + 32]);
+    }
   }
 }
 
@@ -159,7 +167,7 @@ __device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates&
 // copies reuse the region of L (dead after the inversion); W and U take turns in TMEM.
 struct PrepL {
   static constexpr int KB = 0, VBUF = KB + al(C * KD * 2), LS = VBUF + al(C * VD * 2), TW = LS, TV = TW + C * C * 2,
-                       TS = LS + al(C * LDF * 4), WS = TS + al(C * LDF * 4), SC = WS + 4096, MBAR = SC + 4 * C * 4,
+                       TS = LS + al(C * LDF * 4), WS = TS + al(C * LDF * 4), SC = WS + 4096, MBAR = SC + 5 * C * 4,
                        TOTAL = MBAR + 16;
   static_assert(2 * C * C * 2 <= C * LDF * 4, "T's operand copies fit the region of L");
 };
@@ -179,11 +187,12 @@ __global__ void __launch_bounds__(NT, 3) cp_prep(sca2_scan_args p, float* cs, in
   float* WS = reinterpret_cast<float*>(sm + L::WS);
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   const Gates gt{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  float* fdec = sc + 4 * C;  // decay-mask column factors (tc::decay_block)
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   const bool has_g = p.g.ptr != nullptr;
 
-  load_gates(p, gt, b, h, t0, Cl);
+  load_gates(p, gt, b, h, t0, Cl, fdec);
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
@@ -202,12 +211,13 @@ __global__ void __launch_bounds__(NT, 3) cp_prep(sca2_scan_args p, float* cs, in
   bool ok = batch_wait(mbar, 0);
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {
-      const float bi = gt.beta[i], gi = gt.Gc[i];
+      const float bi = gt.beta[i];
+      float dg[16];
+      if (has_g) tc::decay_block(gt.Gc, fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gt.Gc[jj], 0.f)) : 1.f;
-        LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
+        LS[i * LDF + jj] = jj < i ? bi * x[j] * (has_g ? dg[j] : 1.f) : 0.f;
       }
     });
     umma::fence_before_sync();
@@ -506,7 +516,7 @@ __global__ void __launch_bounds__(NQF, 1) cp_state_fwd(sca2_scan_args p, float* 
 // accumulator.
 struct OutL {
   static constexpr int QB = 0, KB = QB + al(C * KD * 2), EB = KB, SB = KB + al(C * KD * 2),
-                       PB = SB + al(KD * VD * 2), SC = PB + al(C * C * 2), MBAR = SC + 4 * C * 4,
+                       PB = SB + al(KD * VD * 2), SC = PB + al(C * C * 2), MBAR = SC + 5 * C * 4,
                        TOTAL = MBAR + 16;
 };
 
@@ -525,12 +535,13 @@ __global__ void __launch_bounds__(NT, 3) cp_out(sca2_scan_args p, sca2_out o, co
   bf16* PB = reinterpret_cast<bf16*>(sm + L::PB);
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   const Gates gt{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  float* fdec = sc + 4 * C;  // decay-mask column factors (tc::decay_block)
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   const bool has_g = p.g.ptr != nullptr;
   const float qs = p.q_scale;
 
-  load_gates(p, gt, b, h, t0, Cl);
+  load_gates(p, gt, b, h, t0, Cl, fdec);
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
@@ -552,13 +563,12 @@ __global__ void __launch_bounds__(NT, 3) cp_out(sca2_scan_args p, sca2_out o, co
     flat_copy<NT>(EB, slot(cs, bh, NS, c, 1), C * VD * 2);  // over k (read by the product)
     tc::cp_commit();
     tc::for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {
-      const float gi = gt.Gc[i];
-      float y[16];
+      float y[16], dg[16];
+      if (has_g) tc::decay_block(gt.Gc, fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gt.Gc[jj], 0.f)) : 1.f;
-        y[j] = jj <= i ? x[j] * dg : 0.f;
+        y[j] = jj <= i ? x[j] * (has_g ? dg[j] : 1.f) : 0.f;
       }
       tc::st8(PB, umma::kmaj(i, j0, C), y);
       tc::st8(PB, umma::kmaj(i, j0 + 8, C), y + 8);
@@ -616,7 +626,7 @@ __global__ void __launch_bounds__(NT, 3) cp_out(sca2_scan_args p, sca2_out o, co
 struct BPrepL {
   static constexpr int QB = 0, KB = QB + al(C * KD * 2), DOB = KB + al(C * KD * 2), PB = DOB + al(C * VD * 2),
                        TB = PB + al(C * C * 2), TWB = TB + al(C * C * 2), Z1 = DOB,
-                       SC = TWB + al(C * C * 2), MBAR = SC + 4 * C * 4, TOTAL = MBAR + 16;
+                       SC = TWB + al(C * C * 2), MBAR = SC + 5 * C * 4, TOTAL = MBAR + 16;
 };
 
 __global__ void __launch_bounds__(NT, 3) cp_bprep(sca2_scan_args p, sca2_out dO, float* cs, int NS, int vec,
@@ -635,12 +645,13 @@ __global__ void __launch_bounds__(NT, 3) cp_bprep(sca2_scan_args p, sca2_out dO,
   bf16* Z1 = reinterpret_cast<bf16*>(sm + L::Z1);
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   const Gates gt{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  float* fdec = sc + 4 * C;  // decay-mask column factors (tc::decay_block)
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   const bool has_g = p.g.ptr != nullptr;
   const float qs = p.q_scale;
 
-  load_gates(p, gt, b, h, t0, Cl);
+  load_gates(p, gt, b, h, t0, Cl, fdec);
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
     umma::fence_mbar_init();
@@ -675,13 +686,12 @@ __global__ void __launch_bounds__(NT, 3) cp_bprep(sca2_scan_args p, sca2_out dO,
   bool ok = batch_wait(mbar, 0);
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {
-      const float gi = gt.Gc[i];
-      float y[16];
+      float y[16], dg[16];
+      if (has_g) tc::decay_block(gt.Gc, fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gt.Gc[jj], 0.f)) : 1.f;
-        y[j] = jj <= i ? qs * x[j] * dg : 0.f;
+        y[j] = jj <= i ? qs * x[j] * (has_g ? dg[j] : 1.f) : 0.f;
       }
       tc::st8(PB, umma::kmaj(i, j0, C), y);
       tc::st8(PB, umma::kmaj(i, j0 + 8, C), y + 8);
@@ -958,7 +968,7 @@ struct GradL {
   static constexpr int QB = 0, KB = QB + al(C * KD * 2), DOB = KB + al(C * KD * 2), DYB = DOB + al(C * VD * 2),
                        EB = DYB + al(C * VD * 2), SB = EB + al(C * VD * 2), DSB = SB + al(KD * VD * 2),
                        DKK = DSB + al(KD * VD * 2), DQK = DKK + al(C * C * 2), DYF = DQK + al(C * C * 2),
-                       DDG = DYF + C * YFP * 4, SC = DDG + C * DDP * 4, NSC = 4 * C + 12 * C + 16, MBAR = SC + NSC * 4,
+                       DDG = DYF + C * YFP * 4, SC = DDG + C * DDP * 4, NSC = 4 * C + 12 * C + 16 + C, MBAR = SC + NSC * 4,
                        TOTAL = MBAR + 16;
 };
 
@@ -983,6 +993,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   float* DYF = reinterpret_cast<float*>(sm + L::DYF);
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   const Gates gt{sc, sc + C, sc + 2 * C, sc + 3 * C};
+  float* fdec = sc + 16 * C + 16;  // decay-mask column factors (tc::decay_block)
   float* rsum = sc + 4 * C;          // [2 halves][6 sums][C]: dbeta1, rowDg, rY, rE, rO, (spare)
   float* red = rsum + 12 * C;        // block reduction scratch (16)
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
@@ -993,7 +1004,7 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
   enum { R_DB = 0, R_DG = 1, R_Y = 2, R_E = 3, R_O = 4 };
   auto rs = [&](int half, int which) { return rsum + (half * 6 + which) * C; };
 
-  load_gates(p, gt, b, h, t0, Cl);
+  load_gates(p, gt, b, h, t0, Cl, fdec);
   for (int u = tid; u < 12 * C; u += NT) rsum[u] = 0.f;
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
@@ -1046,13 +1057,14 @@ __global__ void __launch_bounds__(NT, 1) cp_grads(sca2_scan_args p, sca2_out dO,
     {
       const uint32_t bases[4] = {tb, tb + 64, tb + 128, tb + 192};
       frag_multi<64, 4>(bases, [&](int i, int j0, float (*v)[16]) {
-        const float gi = gt.Gc[i], bi = gt.beta[i];
-        float dkk[16], dqk[16], db1 = 0.f, rdg = 0.f;
+        const float bi = gt.beta[i];
+        float dkk[16], dqk[16], db1 = 0.f, rdg = 0.f, dgv[16];
+        if (has_g) tc::decay_block(gt.Gc, fdec, i, j0, dgv);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int jj = j0 + j;
           const bool incl = jj <= i, strict = jj < i;
-          const float dg = incl ? (has_g ? __expf(fminf(gi - gt.Gc[jj], 0.f)) : 1.f) : 0.f;
+          const float dg = incl ? (has_g ? dgv[j] : 1.f) : 0.f;
           const float qk = qs * v[0][j], gkk = v[1][j];
           const float dL = strict ? -v[2][j] : 0.f;
           const float dP = incl ? v[3][j] : 0.f;

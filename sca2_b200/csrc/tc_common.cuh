@@ -264,8 +264,9 @@ struct Gates {
 // factors fdec[j] = exp(Gc_jl - Gc_j) <= 1 are formed once per chunk (threads 0..63); a block
 // left of row i (jl < i) is then exp(Gc_i - Gc_jl) * fdec[j], both factors <= 1, so one
 // exponential per row and block.  The row's own block is factored the same way (the row factor
-// >= 1, products clamped at 1) unless that block decays by more than e^80, where it takes one
-// exponential per element; blocks right of the row are zero.
+// >= 1) unless that block decays by more than e^80, where it takes one exponential per element;
+// blocks right of the row are zero.  Products are clamped at 1: min(e^x, 1) = e^min(x, 0), the
+// mask's definition.
 __device__ __forceinline__ void decay_factors(const float* Gc, float* fdec) {
   const int t = threadIdx.x;
   if (t < C) fdec[t] = __expf(Gc[t | 15] - Gc[t]);
@@ -277,15 +278,11 @@ __device__ __forceinline__ void decay_block(const float* Gc, const float* fdec, 
     for (int j = 0; j < 16; ++j) d[j] = 0.f;
   } else if (j0 + 15 < i || Gc[j0] - gl <= 80.f) {
     const float r = __expf(Gc[i] - gl);
-    const bool own = j0 + 15 >= i;
 #pragma unroll
     for (int j = 0; j < 16; j += 4) {
       const float4 f = *reinterpret_cast<const float4*>(fdec + j0 + j);
-      d[j] = r * f.x, d[j + 1] = r * f.y, d[j + 2] = r * f.z, d[j + 3] = r * f.w;
-    }
-    if (own) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) d[j] = fminf(d[j], 1.f);
+      d[j] = fminf(r * f.x, 1.f), d[j + 1] = fminf(r * f.y, 1.f);
+      d[j + 2] = fminf(r * f.z, 1.f), d[j + 3] = fminf(r * f.w, 1.f);
     }
   } else {
     const float gi = Gc[i];
