@@ -151,12 +151,7 @@ __device__ __forceinline__ void load_gates(const sca2_scan_args& p, const Gates&
     tc::GateRegs gr;
     tc::load_gate_regs(p, gr, b, h, t0, Cl);
     tc::gates_from_regs(gr, g, Cl);
-    if (p.g.ptr) {
-      __syncwarp();
-      const int l = threadIdx.x & 31;
-      fdec[l] = __expf(g.Gc[l | 15] - g.Gc[l]);
-      fdec[l + 32] = __expf(g.Gc[(l | 15) + 32] - g.Gc[l + 32]);
-    }
+    if (p.g.ptr) tc::decay_factors_warp(g.Gc, fdec);
   }
 }
 

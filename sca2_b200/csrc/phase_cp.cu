@@ -125,8 +125,8 @@ struct PrepL {
   static constexpr int UBL = ZA, KCL = VA;         // after W', U: U lo over Z, Kc lo over the values
   static constexpr int TS = TB + C * C * 2;        // fp32 C x LDF
   static constexpr int WS = TS + C * LDF * 4;      // fp32 1024
-  static constexpr int SC = WS + 1024 * 4;         // beta, Gc, a, w [C], lam [KD]
-  static constexpr int MBAR = SC + (4 * C + KD) * 4;  // batch mbarrier, TMEM base, value-tile mbarrier
+  static constexpr int SC = WS + 1024 * 4;         // beta, Gc, a, w [C], lam [KD], decay factors [C]
+  static constexpr int MBAR = SC + (5 * C + KD) * 4;  // batch mbarrier, TMEM base, value-tile mbarrier
   static constexpr int TOTAL = MBAR + 32;
   static_assert(2 * C * KD * 2 <= A_BYTES, "KR and KW fit region A");
   static_assert(TOTAL <= 74 * 1024, "three CTAs per SM");
@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   const Gates gt{sc, sc + C, sc + 2 * C, sc + 3 * C};
   float* s_lam = sc + 4 * C;
+  float* s_fdec = s_lam + KD;  // column factors of the decay mask (tc::decay_block)
   bf16* KR = reinterpret_cast<bf16*>(sm + L::KR);
   bf16* KW = reinterpret_cast<bf16*>(sm + L::KW);
   bf16* ZA = reinterpret_cast<bf16*>(sm + L::ZA);
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
     tc::GateRegs gr;
     tc::load_gate_regs(p, gr, b, h, t0, Cl);
     tc::gates_from_regs(gr, gt, Cl);
+    if (has_g) tc::decay_factors_warp(gt.Gc, s_fdec);
   }
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
@@ -227,12 +229,13 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
   }
   if (ok) {
     tc::for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {  // L = beta G .* Dg, strict
-      const float bi = gt.beta[i] * ik, gi = gt.Gc[i];
+      const float bi = gt.beta[i] * ik;
+      float dg[16];
+      if (has_g) tc::decay_block(gt.Gc, s_fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gt.Gc[jj], 0.f)) : 1.f;
-        LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
+        LS[i * LDF + jj] = jj < i ? bi * x[j] * (has_g ? dg[j] : 1.f) : 0.f;
       }
     });
     __syncthreads();
@@ -455,8 +458,8 @@ struct OutL {
   static constexpr int TB = VA + C * VD * 2;       // T [i][j]                    -> Qa lo (with the next 8 KB)
   static constexpr int XR = TB + C * C * 2;        // (8 KB, second half of Qa lo)
   static constexpr int EB = ZA, EL = VA, PB = QR, PL = QRL, YB = KW, YL = KWL, QA = KW, QAL = TB;
-  static constexpr int SC = XR + C * KD * 2;       // beta, Gc, a, w [C], lam [KD], wr, wi [MH]
-  static constexpr int MBAR = SC + (4 * C + KD + 2 * MH) * 4;  // batch mbarrier, TMEM base, value-tile mbarrier
+  static constexpr int SC = XR + C * KD * 2;       // beta, Gc, a, w [C], lam [KD], wr, wi [MH], decay factors [C]
+  static constexpr int MBAR = SC + (5 * C + KD + 2 * MH) * 4;  // batch mbarrier, TMEM base, value-tile mbarrier
   static constexpr int TOTAL = MBAR + 32;
   static_assert(2 * C * KD * 2 == 2 * C * C * 2, "P hi / lo take the places of qr hi / lo");
   static_assert(TOTAL <= 113 * 1024, "two CTAs per SM");
@@ -477,6 +480,7 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
   float* s_lam = sc + 4 * C;
   float* s_wr = s_lam + KD;
   float* s_wi = s_wr + MH;
+  float* s_fdec = s_wi + MH;  // column factors of the decay mask (tc::decay_block)
   bf16* SH = reinterpret_cast<bf16*>(sm + L::SH);
   bf16* SL = reinterpret_cast<bf16*>(sm + L::SL);
   bf16* ZA = reinterpret_cast<bf16*>(sm + L::ZA);
@@ -504,6 +508,7 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     tc::GateRegs gr;
     tc::load_gate_regs(p, gr, b, h, t0, Cl);
     tc::gates_from_regs(gr, gt, Cl);
+    if (has_g) tc::decay_factors_warp(gt.Gc, s_fdec);
   }
   if (tid == 0) {
     umma::mbar_init(mbar, 1);
@@ -597,13 +602,12 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     });
     tc::for_frag<2 * 64, 64>(tb + 64, [&](int row, int j0, int, const float* x) {  // P masked, decayed
       const int i = row & 63;
-      const float gi = gt.Gc[i];
-      float y[16];
+      float y[16], dg[16];
+      if (has_g) tc::decay_block(gt.Gc, s_fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gt.Gc[jj], 0.f)) : 1.f;
-        y[j] = jj <= i ? x[j] * ik * dg : 0.f;
+        y[j] = jj <= i ? x[j] * ik * (has_g ? dg[j] : 1.f) : 0.f;
       }
       tc::st8_split(PB, PL, umma::kmaj(row, j0, C), y);
       tc::st8_split(PB, PL, umma::kmaj(row, j0 + 8, C), y + 8);

@@ -29,13 +29,13 @@ struct PrepLayout {
   static constexpr int WS = TB + al(C * C * 2);    // fp32 1024               (after G)
   static constexpr int LS = KW + al(C * KD * 2);   // fp32 C x LDF
   static constexpr int TS = LS + al(C * LDF * 4);  // fp32 C x LDF
-  static constexpr int SC = TS + al(C * LDF * 4);  // beta, Gc, a, w [C] + lam [KD]
-  static constexpr int MBAR = SC + ((4 * C + KD) * 4 + 15) / 16 * 16;
+  static constexpr int SC = TS + al(C * LDF * 4);  // beta, Gc, a, w [C] + lam [KD] + decay factors [C]
+  static constexpr int MBAR = SC + ((5 * C + KD) * 4 + 15) / 16 * 16;
   static constexpr int TOTAL = MBAR + 16;
   static_assert(WS + 1024 * 4 <= LS, "T and WS fit the code region");
 };
 
-template <int FL, int KD>
+template <int FL, int KD, bool HG>
 __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec,
                                                      PhaseProj pp) {
   using L = PrepLayout<KD>;
@@ -43,12 +43,13 @@ __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* c
   const int tid = threadIdx.x, warp = tid >> 5;
   const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int t0 = c * C, Cl = min(C, p.T - t0);
-  const bool has_g = p.g.ptr != nullptr;
+  constexpr bool has_g = HG;  // a per-token scalar decay (p.g) is present
   constexpr int KH = FL == SCA2_FLAVOR_PHASE ? KD / 2 : KD;
   const float ik = FL == SCA2_FLAVOR_PHASE ? 1.f / (float)(KD / 2) : 1.f;
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   Gates gates{sc, sc + C, sc + 2 * C, sc + 3 * C};
   float* s_lam = sc + 4 * C;
+  float* s_fdec = s_lam + KD;  // column factors of the decay mask (decay_block)
   bf16* KR = reinterpret_cast<bf16*>(sm + L::KR);
   bf16* KW = reinterpret_cast<bf16*>(sm + L::KW);
   bf16* TB = reinterpret_cast<bf16*>(sm + L::TB);
@@ -75,6 +76,7 @@ __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* c
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = *s_tmem;
+  if (has_g) decay_factors(gates.Gc, s_fdec);  // visible after the barrier past the Gram product
   // ---- codes kr, kw (bf16, [i][m])
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;
@@ -123,12 +125,13 @@ __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* c
   if (ok) {
     // L = beta Gr (fp32, strictly lower), then T
     for_frag<64, 64>(tb, [&](int i, int j0, int, const float* x) {
-      const float bi = gates.beta[i] * ik, gi = gates.Gc[i];
+      const float bi = gates.beta[i] * ik;
+      float dg[16];
+      if (has_g) decay_block(gates.Gc, s_fdec, i, j0, dg);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = j0 + j;
-        const float dg = has_g ? __expf(fminf(gi - gates.Gc[jj], 0.f)) : 1.f;
-        LS[i * LDF + jj] = jj < i ? bi * x[j] * dg : 0.f;
+        LS[i * LDF + jj] = jj < i ? bi * x[j] * (has_g ? dg[j] : 1.f) : 0.f;
       }
     });
     __syncthreads();
@@ -158,12 +161,12 @@ cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int v
   const int smem = tc::PrepLayout<64>::TOTAL;
   dim3 grid(NC, p.B * p.H);
   if (p.flavor == SCA2_FLAVOR_PHASE) {
-    auto k = tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64>;
+    auto k = p.g.ptr ? tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64, true> : tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64, false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec, pp);
   } else {
-    auto k = tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64>;
+    auto k = p.g.ptr ? tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64, true> : tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64, false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec, pp);

@@ -271,6 +271,13 @@ __device__ __forceinline__ void decay_factors(const float* Gc, float* fdec) {
   const int t = threadIdx.x;
   if (t < C) fdec[t] = __expf(Gc[t | 15] - Gc[t]);
 }
+// the same from the one warp that has just written Gc (two columns per lane)
+__device__ __forceinline__ void decay_factors_warp(const float* Gc, float* fdec) {
+  __syncwarp();
+  const int l = threadIdx.x & 31;
+  fdec[l] = __expf(Gc[l | 15] - Gc[l]);
+  fdec[l + 32] = __expf(Gc[(l | 15) + 32] - Gc[l + 32]);
+}
 __device__ __forceinline__ void decay_block(const float* Gc, const float* fdec, int i, int j0, float* d) {
   const float gl = Gc[j0 + 15];
   if (j0 > i) {
