@@ -119,6 +119,12 @@ class MixerLayer(nn.Module):
 
     # ---- the residual tail shared by prefill and step ---------------------------------
     def _tail(self, x: torch.Tensor, us) -> torch.Tensor:
+        if torch.is_autocast_enabled() and x.is_cuda:
+            # the mix product reads its input in the autocast dtype: cast each slot's read-out
+            # before joining them (the same elementwise rounding as casting the joined fp32
+            # tensor, without materialising it; the gradients come back per slot, contiguous)
+            dt = torch.get_autocast_dtype("cuda")
+            us = [u.to(dt) for u in us]
         y = x + self.mix(torch.cat(us, -1))
         return y + self.ff(self.fn(y))
 
