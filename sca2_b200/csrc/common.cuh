@@ -27,6 +27,13 @@ __device__ __forceinline__ int64_t out_off(const sca2_out& t, int b, int tt, int
   return (int64_t)b * t.sb + (int64_t)tt * t.st + (int64_t)h * t.sh + (int64_t)r * t.sr;
 }
 
+// ---- division by a runtime divisor ------------------------------------------------------
+// floor(u / d) by a multiply-high with m = magic(d) = ceil(2^32 / d): u m / 2^32 = u / d +
+// u e / (d 2^32) with e = m d - 2^32 < d, so the floor is exact while u e < 2^32 (u < 2^32 / d
+// suffices).  d = 1 would need m = 2^32: it is encoded as m = 0 and returns u.
+__host__ __device__ constexpr uint32_t magic(uint32_t d) { return d > 1 ? 0xFFFFFFFFu / d + 1u : 0u; }
+__device__ __forceinline__ int qdiv(int u, uint32_t m) { return m ? (int)__umulhi((uint32_t)u, m) : u; }
+
 // ---- sine and cosine of large phases -----------------------------------------------------
 // Cody and Waite's additive reduction (W. J. Cody, W. Waite, "Software Manual for the Elementary
 // Functions", 1980): r = x - k 2pi with k = rint(x / 2pi) and 2pi split into three parts, the

@@ -38,12 +38,8 @@ __device__ __forceinline__ int pmod(long long p, int L) {
   long long r = p % L;
   return (int)(r < 0 ? r + L : r);
 }
-// floor(u / d) by a multiply-high with m = magic(d) = ceil(2^32 / d): u m / 2^32 = u / d +
-// u e / (d 2^32) with e = m d - 2^32 < d, so the floor is exact while u e < 2^32 (every use
-// here: u < 2^16 with d < 2^16, or the phase position u < 2^27 with d = L <= 32)
-// (d = 1 would need m = 2^32: it is encoded as m = 0 and returns u)
-__host__ __device__ constexpr uint32_t magic(uint32_t d) { return d > 1 ? 0xFFFFFFFFu / d + 1u : 0u; }
-__device__ __forceinline__ int qdiv(int u, uint32_t m) { return m ? (int)__umulhi((uint32_t)u, m) : u; }
+// magic / qdiv (common.cuh): every use here has u < 2^16 with d < 2^16, or the phase position
+// u < 2^27 with d = L <= 32
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float dot4(float4 a, float4 b) {
   return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
