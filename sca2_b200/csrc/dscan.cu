@@ -475,8 +475,9 @@ __global__ void __launch_bounds__(NT) dscan_bwd_carry(sca2_dscan_args p, const f
 
 // gradient pass of one block from its incoming adjoint R(k).  The gradients summed over
 // channels (da per (t, m, g), and dc per (t, m) with the separable read) are reduced per warp by
-// shuffles, then across the CTA's warps with shared-memory atomics, and leave the CTA as one
-// global atomic per (t, m[, g]) instead of one per warp.
+// shuffles and stored per warp (plain stores: a warp's channels lie in one gate group); after
+// the block, one pass adds the warps' partials (those of each gate group for da) and the CTA
+// issues one global atomic per (t, m[, g]).
 template <int M, bool SEP>
 __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const float* dab, const float* ckpt,
                                                      const float* R, sca2_dscan_grads gr) {
@@ -489,11 +490,11 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
   const int64_t base = ((int64_t)q.b * NK + k) * 2;
   constexpr float iM = 1.f / M;
   const int gs = V / G, NGL = ngl_max(M, gs);
-  const int g0 = (blockIdx.z * (NT / M)) / gs;     // first gate group of this CTA's channels
-  float* sdc = sred;                              // [CK][M][2]            (separable read)
-  float* sda = sred + (SEP ? CK * M * 2 : 0);     // [CK][M][NGL][2]
-  const int nred = (SEP ? CK * M * 2 : 0) + CK * M * NGL * 2;
-  for (int u = threadIdx.x; u < nred; u += NT) sred[u] = 0.f;
+  constexpr int NW = NT / 32;
+  const int warp = threadIdx.x >> 5;
+  float* pdc = sred;                                  // [NW][CK][M][2] per-warp partials (separable read)
+  float* pda = sred + (SEP ? NW * CK * M * 2 : 0);    // [NW][CK][M][2]
+  const int nred = (SEP ? 2 : 1) * NW * CK * M * 2;  // every entry read is written (rows t < n)
   Stage<M> sg;
   if (SEP) sg.load(p, dab, q.b, t0, n, blockIdx.z * (NT / M), sred + nred, NGL);
   __syncthreads();
@@ -539,9 +540,10 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
     const float dcr = q.live ? gA * sr + gB * si : 0.f, dci = q.live ? gA * si - gB * sr : 0.f;
     if (SEP) {
       const float xr = sum_j<M>(dcr), xi = sum_j<M>(dci);
-      if (q.jj == 0 && q.live) {  // lane jj = 0 holds the warp's first channel
-        atomicAdd(sdc + (u * M + q.m) * 2, xr);
-        atomicAdd(sdc + (u * M + q.m) * 2 + 1, xi);
+      if (q.jj == 0) {  // lane jj = 0 holds the warp's sum (zeros past the value width)
+        float* d = pdc + ((warp * CK + u) * M + q.m) * 2;
+        d[0] = xr;
+        d[1] = xi;
       }
     } else if (q.live) {
       gr.dc_re[tm * V + q.j] = dcr;
@@ -551,30 +553,46 @@ __global__ void __launch_bounds__(NT) dscan_bwd_block(sca2_dscan_args p, const f
     if (q.m == 0 && q.live) gr.dv[(bT + t) * V + q.j] = dvt;
     const float dar = sum_j<M>(dsr * pr[u] + dsi * pi[u]);
     const float dai = sum_j<M>(-dsr * pi[u] + dsi * pr[u]);
-    if (q.jj == 0 && q.live) {
-      float* d = sda + ((u * M + q.m) * NGL + (q.g - g0)) * 2;
-      atomicAdd(d, dar);
-      atomicAdd(d + 1, dai);
+    if (q.jj == 0) {
+      float* d = pda + ((warp * CK + u) * M + q.m) * 2;
+      d[0] = dar;
+      d[1] = dai;
     }
     const float ndr = ar * dsr + ai * dsi;
     dsi = -ai * dsr + ar * dsi;
     dsr = ndr;
   }
   __syncthreads();
-  if (SEP)
-    for (int u = threadIdx.x; u < n * M; u += NT) {
-      const int64_t tm = (bT + t0 + u / M) * M + (u % M);
-      atomicAdd(gr.dc_re + tm, sdc[u * 2]);
-      atomicAdd(gr.dc_im + tm, sdc[u * 2 + 1]);
+  const int cj0 = blockIdx.z * (NT / M);  // the CTA's first channel; warp w's is cj0 + w (32 / M)
+  for (int u = threadIdx.x; u < n * M; u += NT) {  // u = t M + m
+    const int64_t tm = (bT + t0 + u / M) * M + (u % M);
+    if (SEP) {
+      float xr = 0.f, xi = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) xr += pdc[(w * CK * M + u) * 2], xi += pdc[(w * CK * M + u) * 2 + 1];
+      atomicAdd(gr.dc_re + tm, xr);
+      atomicAdd(gr.dc_im + tm, xi);
     }
-  for (int u = threadIdx.x; u < n * M * NGL; u += NT) {
-    const int gl = u % NGL, um = u / NGL, g = g0 + gl;
-    if (g >= G) continue;
-    const int64_t idx = ((bT + t0 + um / M) * M + (um % M)) * G + g;
-    const float xr = sda[u * 2], xi = sda[u * 2 + 1];
-    if (xr != 0.f || xi != 0.f) {  // groups outside this CTA's channels stay untouched
-      atomicAdd(gr.da_re + idx, xr);
-      atomicAdd(gr.da_im + idx, xi);
+    // da: the warps in channel order, one atomic per gate group they cover
+    int gc = -1;
+    float xr = 0.f, xi = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const int jw = cj0 + w * (32 / M);
+      if (jw >= V) break;
+      const int gw = jw / gs;
+      if (gw != gc) {
+        if (gc >= 0) {
+          atomicAdd(gr.da_re + tm * G + gc, xr);
+          atomicAdd(gr.da_im + tm * G + gc, xi);
+        }
+        gc = gw, xr = 0.f, xi = 0.f;
+      }
+      xr += pda[(w * CK * M + u) * 2];
+      xi += pda[(w * CK * M + u) * 2 + 1];
+    }
+    if (gc >= 0) {
+      atomicAdd(gr.da_re + tm * G + gc, xr);
+      atomicAdd(gr.da_im + tm * G + gc, xi);
     }
   }
 }
@@ -797,8 +815,7 @@ cudaError_t launch_bwd_m(const sca2_dscan_args& p, const float* dab, const float
   } else {
     dscan_bwd_carry<M><<<gc, NT, 0, st>>>(p, dS_re, dS_im, qv, Qg, R, g);
   }
-  const int ngl = ngl_max(M, p.V / p.G);
-  const int red = ((p.sep ? CK * M * 2 : 0) + CK * M * ngl * 2) * (int)sizeof(float) + (p.sep ? sm : 0);
+  const int red = (p.sep ? 2 : 1) * (NT / 32) * CK * M * 2 * (int)sizeof(float) + (p.sep ? sm : 0);
   auto kb = p.sep ? dscan_bwd_block<M, true> : dscan_bwd_block<M, false>;
   if ((err = allow_smem(kb, red)) != cudaSuccess) return err;
   kb<<<gl, NT, red, st>>>(p, dab, ckpt, R, g);
