@@ -24,6 +24,7 @@ namespace dscan {
 
 constexpr int NT = 256;
 constexpr int CK = 16;  // tokens per checkpoint block
+constexpr int OUT_TOK = 8;  // tokens per round of the output pass's row sums (16 KB of shared memory)
 
 struct Map {
   int b, m, j, g, jj;
@@ -357,39 +358,54 @@ __global__ void __launch_bounds__(NT) dscan_fwd_out(sca2_dscan_args p, const flo
   const int jc = q.live ? q.j : 0;
   const int64_t bT = (int64_t)q.b * T;
   const int64_t base = ((int64_t)q.b * NK + k) * 2;
+  constexpr int JC = NT / M, HT = OUT_TOK;
   Stage<M> sg;
+  float* pout = sst;  // [HT][re, im][JC][M]: the rows' terms of the read, summed over m after each round
   if (SEP) {  // separable read: the block's inputs staged once, coalesced
-    sg.load(p, nullptr, q.b, t0, n, blockIdx.z * (NT / M), sst, ngl_max(M, V / G));
+    sg.load(p, nullptr, q.b, t0, n, blockIdx.z * JC, sst, ngl_max(M, V / G));
+    pout = sst + Stage<M>::floats(sg.ngl);
     __syncthreads();
   }
-  const int jl = q.j - blockIdx.z * (NT / M);
+  const int cj0 = blockIdx.z * JC, jl = q.j - cj0;
   float sr = ckpt[base * M * V + (int64_t)q.m * V + jc], si = ckpt[(base + 1) * M * V + (int64_t)q.m * V + jc];
-#pragma unroll 4
-  for (int u = 0; u < n; ++u) {
-    const int t = t0 + u;
-    const int64_t tm = (bT + t) * M + q.m;
-    float ar, ai, vt, cr, ci;
-    if (SEP) {
-      const float2 a = sg.gate(u, q.m, q.live ? q.g : sg.g0);
-      ar = a.x, ai = a.y;
-      vt = sg.v[u * Stage<M>::JC + jl];
-      cr = sg.c[(u * M + q.m) * 2];
-      ci = sg.c[(u * M + q.m) * 2 + 1];
-    } else {
-      ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
-      vt = p.v[(bT + t) * V + jc];
-      cr = p.c_re[tm * V + jc];
-      ci = p.c_im[tm * V + jc];
+  for (int h0 = 0; h0 < n; h0 += HT) {
+#pragma unroll
+    for (int uu = 0; uu < HT; ++uu) {
+      const int u = h0 + uu;
+      if (u >= n) break;
+      const int t = t0 + u;
+      const int64_t tm = (bT + t) * M + q.m;
+      float ar, ai, vt, cr, ci;
+      if (SEP) {
+        const float2 a = sg.gate(u, q.m, q.live ? q.g : sg.g0);
+        ar = a.x, ai = a.y;
+        vt = sg.v[u * JC + jl];
+        cr = sg.c[(u * M + q.m) * 2];
+        ci = sg.c[(u * M + q.m) * 2 + 1];
+      } else {
+        ar = p.a_re[tm * G + q.g], ai = p.a_im[tm * G + q.g];
+        vt = p.v[(bT + t) * V + jc];
+        cr = p.c_re[tm * V + jc];
+        ci = p.c_im[tm * V + jc];
+      }
+      const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
+      si = fmaf(ar, si, ai * sr);
+      sr = nr;
+      // lane order (jl, m) is consecutive within a warp: conflict-free stores
+      pout[((uu * 2) * JC + jl) * M + q.m] = q.live ? sr * cr + si * ci : 0.f;
+      pout[((uu * 2 + 1) * JC + jl) * M + q.m] = q.live ? si * cr - sr * ci : 0.f;
     }
-    const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
-    si = fmaf(ar, si, ai * sr);
-    sr = nr;
-    const float pa = sum_m<M>(q.live ? sr * cr + si * ci : 0.f);
-    const float pb = sum_m<M>(q.live ? si * cr - sr * ci : 0.f);
-    if (q.m == 0 && q.live) {
-      ab[((bT + t) * 2) * V + q.j] = pa * (1.f / M);
-      ab[((bT + t) * 2 + 1) * V + q.j] = pb * (1.f / M);
+    __syncthreads();
+    const int nu = min(HT, n - h0);
+    for (int o = threadIdx.x; o < nu * 2 * JC; o += NT) {  // (token, re / im, channel): coalesced writes
+      const int c = o % JC, rr = (o / JC) & 1, uu = o / (2 * JC), j = cj0 + c;
+      const float* src = pout + ((uu * 2 + rr) * JC + c) * M;
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc += src[m];
+      if (j < V) ab[((bT + t0 + h0 + uu) * 2 + rr) * V + j] = acc * (1.f / M);
     }
+    __syncthreads();  // the buffer is rewritten by the next round
   }
 }
 
@@ -780,11 +796,13 @@ cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float
   } else {
     dscan_fwd_carry<M><<<gc, NT, 0, st>>>(p, e, P, ck, S_re, S_im);
   }
+  const int ob = OUT_TOK * 2 * NT * (int)sizeof(float);  // the output pass's row-sum buffer
   if (p.sep) {
-    if ((err = allow_smem(dscan_fwd_out<M, true>, sm)) != cudaSuccess) return err;
-    dscan_fwd_out<M, true><<<gl, NT, sm, st>>>(p, ck, ab);
+    if ((err = allow_smem(dscan_fwd_out<M, true>, sm + ob)) != cudaSuccess) return err;
+    dscan_fwd_out<M, true><<<gl, NT, sm + ob, st>>>(p, ck, ab);
   } else {
-    dscan_fwd_out<M, false><<<gl, NT, 0, st>>>(p, ck, ab);
+    if ((err = allow_smem(dscan_fwd_out<M, false>, ob)) != cudaSuccess) return err;
+    dscan_fwd_out<M, false><<<gl, NT, ob, st>>>(p, ck, ab);
   }
   return cudaGetLastError();
 }
