@@ -24,7 +24,8 @@ namespace dscan {
 
 constexpr int NT = 256;
 constexpr int CK = 16;  // tokens per checkpoint block
-constexpr int OUT_TOK = 8;  // tokens per round of the output pass's row sums (16 KB of shared memory)
+constexpr int OUT_TOK = 8;  // tokens per round of the output pass's row sums (16 to 17 KB of shared memory)
+__host__ __device__ constexpr int out_stride(int M) { return M >= 16 ? M + 1 : M; }
 
 struct Map {
   int b, m, j, g, jj;
@@ -358,9 +359,11 @@ __global__ void __launch_bounds__(NT) dscan_fwd_out(sca2_dscan_args p, const flo
   const int jc = q.live ? q.j : 0;
   const int64_t bT = (int64_t)q.b * T;
   const int64_t base = ((int64_t)q.b * NK + k) * 2;
-  constexpr int JC = NT / M, HT = OUT_TOK;
+  // rows of M >= 16 padded to an odd stride (the sums' loads conflict-free); narrower rows stay
+  // 16-byte aligned for vector loads
+  constexpr int JC = NT / M, HT = OUT_TOK, MP = out_stride(M);
   Stage<M> sg;
-  float* pout = sst;  // [HT][re, im][JC][M]: the rows' terms of the read, summed over m after each round
+  float* pout = sst;  // [HT][re, im][JC][MP]: the rows' terms of the read, summed over m after each round
   if (SEP) {  // separable read: the block's inputs staged once, coalesced
     sg.load(p, nullptr, q.b, t0, n, blockIdx.z * JC, sst, ngl_max(M, V / G));
     pout = sst + Stage<M>::floats(sg.ngl);
@@ -391,15 +394,15 @@ __global__ void __launch_bounds__(NT) dscan_fwd_out(sca2_dscan_args p, const flo
       const float nr = fmaf(ar, sr, fmaf(-ai, si, vt));
       si = fmaf(ar, si, ai * sr);
       sr = nr;
-      // lane order (jl, m) is consecutive within a warp: conflict-free stores
-      pout[((uu * 2) * JC + jl) * M + q.m] = q.live ? sr * cr + si * ci : 0.f;
-      pout[((uu * 2 + 1) * JC + jl) * M + q.m] = q.live ? si * cr - sr * ci : 0.f;
+      // lane order (jl, m) is consecutive within a warp: stores nearly conflict-free
+      pout[((uu * 2) * JC + jl) * MP + q.m] = q.live ? sr * cr + si * ci : 0.f;
+      pout[((uu * 2 + 1) * JC + jl) * MP + q.m] = q.live ? si * cr - sr * ci : 0.f;
     }
     __syncthreads();
     const int nu = min(HT, n - h0);
     for (int o = threadIdx.x; o < nu * 2 * JC; o += NT) {  // (token, re / im, channel): coalesced writes
       const int c = o % JC, rr = (o / JC) & 1, uu = o / (2 * JC), j = cj0 + c;
-      const float* src = pout + ((uu * 2 + rr) * JC + c) * M;
+      const float* src = pout + ((uu * 2 + rr) * JC + c) * MP;
       float acc = 0.f;
 #pragma unroll
       for (int m = 0; m < M; ++m) acc += src[m];
@@ -796,7 +799,7 @@ cudaError_t launch_fwd_m(const sca2_dscan_args& p, float* ab, float* S_re, float
   } else {
     dscan_fwd_carry<M><<<gc, NT, 0, st>>>(p, e, P, ck, S_re, S_im);
   }
-  const int ob = OUT_TOK * 2 * NT * (int)sizeof(float);  // the output pass's row-sum buffer
+  const int ob = OUT_TOK * 2 * (NT / M) * out_stride(M) * (int)sizeof(float);  // the output pass's row sums
   if (p.sep) {
     if ((err = allow_smem(dscan_fwd_out<M, true>, sm + ob)) != cudaSuccess) return err;
     dscan_fwd_out<M, true><<<gl, NT, sm + ob, st>>>(p, ck, ab);
