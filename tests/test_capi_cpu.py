@@ -90,3 +90,31 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(1, 4, 1, 2)
     with pytest.raises(_lib.Sca2Error):
         ops.phase_scan(x, x, torch.zeros(1, 4, 1, 3), wr=torch.ones(1, 2), wi=torch.zeros(1, 2))
+
+
+def test_row_ops_refuse_cpu_tensors():
+    """The read-out, split, 16-bit projection and LayerNorm ops have no CPU path either."""
+    import torch
+    from sca2_b200 import ops
+    with pytest.raises(_lib.Sca2Error):
+        ops.sepq_read(torch.zeros(2, 3, 2, 8), torch.zeros(2, 3, 16))
+    with pytest.raises(_lib.Sca2Error):
+        ops.rms_heads(torch.zeros(2, 3, 4, 2, 8))
+    with pytest.raises(_lib.Sca2Error):
+        ops.split_bf16(torch.zeros(4, 8), (False, True))
+    with pytest.raises(_lib.Sca2Error):
+        ops.linear16(torch.zeros(4, 8), torch.zeros(6, 8), (6,))
+    with pytest.raises(_lib.Sca2Error):
+        ops.layer_norm(torch.zeros(4, 128), torch.ones(128), torch.zeros(128))
+
+
+def test_row_ops_entry_points_refuse_bad_sizes():
+    """Argument checks of the new entry points run on the host before any launch (no device
+    pointer is dereferenced), so they can be exercised without a GPU."""
+    lib = _lib.load()
+    assert lib.sca2_sepq_read_fwd(None, None, None, 4, None, 3, 8, 1e-6, 1e-6, None) != 0  # ld_q < dv
+    assert lib.sca2_split_bf16(None, 2, 8, 8, None, 16, 9, 0, None) != 0                  # nblk > 8
+    assert lib.sca2_rms_heads_fwd(None, 0, None, 2, 2, 6, 1e-6, None) != 0                # dvh % 4
+    assert lib.sca2_layer_norm_supported(1024) == 1 and lib.sca2_layer_norm_supported(1000) == 0
+    assert lib.sca2_layer_norm_fwd(None, None, None, None, None, None, 2, 1000, 1e-5, None) != 0
+    assert lib.sca2_layer_norm_work_floats(0, 1024) == 0 and lib.sca2_layer_norm_work_floats(64, 1024) > 0
