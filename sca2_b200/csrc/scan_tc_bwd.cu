@@ -590,7 +590,56 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       cp_commit();
     }
     // ---- dL with G -> dKK (+ position-weighted), d(beta) row term, decay sums
-    {
+    if constexpr (!HG) {
+      // the 16 rows of each sub-partition over all 32 lanes (16x256b loads): lane t holds rows
+      // r0 = t/4 and r0 + 8, columns 2(t%4) and 2(t%4) + 1 of every 8-column group
+      const int i0 = 16 * sub + (lane >> 2), i1 = i0 + 8, cw = (warp >> 2) * 32, c2 = 2 * (lane & 3);
+      const float b0 = gates.beta[i0], b1 = gates.beta[i1];
+      uint32_t ud[4][4], ug[4][4];
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi) {
+        umma::ld4_rows16_issue(umma::taddr(tb + CO::DL, 32 * sub, cw + 8 * gi), ud[gi]);
+        umma::ld4_rows16_issue(umma::taddr(tb + CO::G, 32 * sub, cw + 8 * gi), ug[gi]);
+      }
+      umma::ld_wait();
+      float sb0 = 0.f, sb1 = 0.f;
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi) {
+        const int j = cw + 8 * gi + c2;  // columns j, j + 1
+        float dl[4], gg[4], kk[4], kw[4];
+        umma::take<4>(ud[gi], dl);
+        umma::take<4>(ug[gi], gg);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {  // (i0, j), (i0, j + 1), (i1, j), (i1, j + 1)
+          const int i = e < 2 ? i0 : i1, jj = j + (e & 1);
+          float val = 0.f;
+          if (jj < i) {
+            const float l = -dl[e];
+            if (e < 2)
+              sb0 = fmaf(l, gg[e] * ik, sb0);
+            else
+              sb1 = fmaf(l, gg[e] * ik, sb1);
+            val = (e < 2 ? b0 : b1) * l;
+          }
+          kk[e] = val;
+          kw[e] = val * (float)(jj - i);
+        }
+        *reinterpret_cast<__nv_bfloat162*>(DKKA + umma::kmaj(i0, j, C)) = __floats2bfloat162_rn(kk[0], kk[1]);
+        *reinterpret_cast<__nv_bfloat162*>(DKKA + umma::kmaj(i1, j, C)) = __floats2bfloat162_rn(kk[2], kk[3]);
+        *reinterpret_cast<__nv_bfloat162*>(DKKW + umma::kmaj(i0, j, C)) = __floats2bfloat162_rn(kw[0], kw[1]);
+        *reinterpret_cast<__nv_bfloat162*>(DKKW + umma::kmaj(i1, j, C)) = __floats2bfloat162_rn(kw[2], kw[3]);
+      }
+      // the row terms of d(beta): the four lanes of a row, then one atomic per row and warp
+#pragma unroll
+      for (int o = 1; o < 4; o <<= 1) {
+        sb0 += __shfl_xor_sync(0xffffffffu, sb0, o);
+        sb1 += __shfl_xor_sync(0xffffffffu, sb1, o);
+      }
+      if ((lane & 3) == 0) {
+        atomicAdd(&s_dbeta[i0], sb0);
+        atomicAdd(&s_dbeta[i1], sb1);
+      }
+    } else {
       const int i = frag_row<C>();
       const bool own = owns_rows<C>();
 #pragma unroll
