@@ -177,29 +177,52 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   uint32_t phase = 0, phase2 = 0;
   bool pending2 = false;  // a U^T / Wk batch was committed to mbar2 and not yet waited for
 
-  // ---- state S^T: fp32 registers in the layout of the Su^T accumulator (M = VB, N = KD)
-  constexpr int NS = KD / 2;
+  // ---- state S^T: fp32 registers in the layout of the Su^T accumulator (M = VB, N = KD).  With
+  // VB = 64 that is the all-lane layout of for_frag16 (element k at row s_v(k), column s_m(k));
+  // with VB = 128 the 32x32b one (lane row srow, columns frag_col0 + j).
+  constexpr bool W16 = VB == 64;
+  constexpr int NS = W16 ? KD / 4 : KD / 2;
   float Sreg[NS];
   const int srow = frag_row<VB>();
-  const bool sown = owns_rows<VB>();
+  const bool sown = W16 || owns_rows<VB>();
+  const int sv0 = 16 * (warp & 3) + (tid & 31) / 4, sm0 = (warp >> 2) * (KD / 2) + 2 * (tid & 3);
+  auto s_v = [&](int k) { return W16 ? sv0 + 8 * ((k >> 1) & 1) : srow; };
+  auto s_m = [&](int k) { return W16 ? sm0 + 8 * (k >> 2) + (k & 1) : frag_col0<VB, KD>(k / 16) + (k & 15); };
   const int64_t bhKV = ((int64_t)b * p.H + h) * KD * (int64_t)V;
-  const int64_t sbase = bhKV + vb0 + srow;
+  if constexpr (W16) {
 #pragma unroll
-  for (int q = 0; q < KD / 32; ++q) {
-    float x[16];
+    for (int g = 0; g < NS / 4; ++g) {
+      float x[4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int m = frag_col0<VB, KD>(q) + j;
-      const float s = (sown && p.S0) ? p.S0[sbase + (int64_t)m * V] : 0.f;
-      Sreg[16 * q + j] = s;
-      x[j] = s * s_d1[m];
+      for (int e = 0; e < 4; ++e) {
+        const int k = 4 * g + e, m = s_m(k);
+        const float s = p.S0 ? p.S0[bhKV + vb0 + s_v(k) + (int64_t)m * V] : 0.f;
+        Sreg[k] = s;
+        x[e] = s * s_d1[m];
+        if (L::STAGE && cstates && (flags & F_CS16)) ST[m * VB + s_v(k)] = s;
+      }
+      st2(SB, umma::kmaj(sv0, sm0 + 8 * g, KD), x[0], x[1]);
+      st2(SB, umma::kmaj(sv0 + 8, sm0 + 8 * g, KD), x[2], x[3]);
     }
-    if (sown) {
-      st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q), KD), x);
-      st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q) + 8, KD), x + 8);
-      if (L::STAGE && cstates && (flags & F_CS16))
+  } else {
+    const int64_t sbase = bhKV + vb0 + srow;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ST[(frag_col0<VB, KD>(q) + j) * VB + srow] = Sreg[16 * q + j];
+    for (int q = 0; q < KD / 32; ++q) {
+      float x[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int m = frag_col0<VB, KD>(q) + j;
+        const float s = (sown && p.S0) ? p.S0[sbase + (int64_t)m * V] : 0.f;
+        Sreg[16 * q + j] = s;
+        x[j] = s * s_d1[m];
+      }
+      if (sown) {
+        st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q), KD), x);
+        st8(SB, umma::kmaj(srow, frag_col0<VB, KD>(q) + 8, KD), x + 8);
+        if (L::STAGE && cstates && (flags & F_CS16))
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ST[(frag_col0<VB, KD>(q) + j) * VB + srow] = Sreg[16 * q + j];
+      }
     }
   }
   // The state entering each chunk goes to slot 2c.  Staged: in ST (fp32 [m][v]), written with
@@ -210,7 +233,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   const bool stage = L::STAGE && cstates && (flags & F_CS16);
   const bool st_issuer = stage && (st_one ? tid == 0 : tid < KD);
   publish_smem();
-  float Ureg[C / 2];
+  float Ureg[W16 ? C / 4 : C / 2];  // U^T in the Su^T / X^T accumulator layout
 
   auto wait_mma = [&]() -> bool {
     if (!umma::mbar_wait(mbar, phase)) *s_err = 1;
@@ -313,11 +336,9 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       bulk_commit();
     }
     if (!stage && cstates && sown) {
-      const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0 + srow;
+      const int64_t cb = (((int64_t)b * p.H + h) * NCS + 2 * c) * KD * (int64_t)V + vb0;
 #pragma unroll
-      for (int q = 0; q < KD / 32; ++q)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) cstates[cb + (int64_t)(frag_col0<VB, KD>(q) + j) * V] = Sreg[16 * q + j];
+      for (int k = 0; k < NS; ++k) cstates[cb + s_v(k) + (int64_t)s_m(k) * V] = Sreg[k];
     }
     // ---- operands of the chunk
     const Gates gates = gset(c);
@@ -409,13 +430,20 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
           cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(c + 1) + u, true);
       cp_commit();
     }
-    for_frag<VB, C>(tb + CO::UT, [&](int, int, int q, const float* x) {
+    if constexpr (W16) {
+      for_frag16<C>(tb + CO::UT, [&](int g, int, int, const float* x) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) Ureg[16 * q + j] = x[j];
-    });
-    for_frag<64, KD>(tb + CO::WK, [&](int i, int m0, int, const float* x) {
-      st8(WK, umma::kmaj(i, m0, KD), x);
-      st8(WK, umma::kmaj(i, m0 + 8, KD), x + 8);
+        for (int e = 0; e < 4; ++e) Ureg[4 * g + e] = x[e];
+      });
+    } else {
+      for_frag<VB, C>(tb + CO::UT, [&](int, int, int q, const float* x) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) Ureg[16 * q + j] = x[j];
+      });
+    }
+    for_frag16<KD>(tb + CO::WK, [&](int, int i0, int m, const float* x) {
+      st2(WK, umma::kmaj(i0, m, KD), x[0], x[1]);
+      st2(WK, umma::kmaj(i0 + 8, m, KD), x[2], x[3]);
     });
     publish_smem();
     if (p_save) {
@@ -439,13 +467,20 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     }
     if (warp == 0 && c + 1 < NC) gates_from_regs(greg, gset(c + 1), min(C, p.T - t0 - C));
     if (!(ok = wait_mma())) break;
-    for_frag<VB, C>(tb + CO::XT, [&](int v, int i0, int q, const float* x) {
-      float e[16];
+    if constexpr (W16) {
+      for_frag16<C>(tb + CO::XT, [&](int g, int v0, int i, const float* x) {
+        st2_split(EB, EBL, umma::kmaj(v0, i, C), Ureg[4 * g] - x[0], Ureg[4 * g + 1] - x[1]);
+        st2_split(EB, EBL, umma::kmaj(v0 + 8, i, C), Ureg[4 * g + 2] - x[2], Ureg[4 * g + 3] - x[3]);
+      });
+    } else {
+      for_frag<VB, C>(tb + CO::XT, [&](int v, int i0, int q, const float* x) {
+        float e[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) e[j] = Ureg[16 * q + j] - x[j];
-      st8_split(EB, EBL, umma::kmaj(v, i0, C), e);
-      st8_split(EB, EBL, umma::kmaj(v, i0 + 8, C), e + 8);
-    });
+        for (int j = 0; j < 16; ++j) e[j] = Ureg[16 * q + j] - x[j];
+        st8_split(EB, EBL, umma::kmaj(v, i0, C), e);
+        st8_split(EB, EBL, umma::kmaj(v, i0 + 8, C), e + 8);
+      });
+    }
     publish_smem();
     if (cstates) copy_out(saved + C * C * 2 + blockIdx.y * (VB * C * 2), EB, VB * C * 2);
     if (issuer) {
@@ -468,21 +503,48 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     // ---- state update
     if (CO::DEFER && tid < C) s_aprev[tid] = gates.a[tid];
     const float aC = gates.a[Cl - 1];
-    for_frag<VB, KD>(tb + CO::SUT, [&](int v, int m0, int q, const float* x) {
-      float y[16];
+    if constexpr (W16) {
+      // ST [m][v] rows are VB = 64 floats apart (bank = v % 32): each staging store takes row v0
+      // on lanes with (lane & 1) == 0 and row v0 + 8 on the others, 16 banks per instruction
+      const bool odd = tid & 1;
+      for_frag16<KD>(tb + CO::SUT, [&](int g, int v0, int m, const float* x) {
+        float y[4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = m0 + j;
-        const float s = s_dCm1[m] * (aC * s_d1[m] * Sreg[16 * q + j] + x[j]);
-        Sreg[16 * q + j] = s;
-        y[j] = s * s_d1[m];
-      }
-      st8(SB, umma::kmaj(v, m0, KD), y);
-      st8(SB, umma::kmaj(v, m0 + 8, KD), y + 8);
-      if (stage && c + 1 < NC)
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * g + e, mm = m + (e & 1);
+          const float s = s_dCm1[mm] * (aC * s_d1[mm] * Sreg[k] + x[e]);
+          Sreg[k] = s;
+          y[e] = s * s_d1[mm];
+        }
+        st2(SB, umma::kmaj(v0, m, KD), y[0], y[1]);
+        st2(SB, umma::kmaj(v0 + 8, m, KD), y[2], y[3]);
+        if (stage && c + 1 < NC) {
+          const int va = odd ? v0 + 8 : v0, vb = odd ? v0 : v0 + 8;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ST[(m0 + j) * VB + v] = Sreg[16 * q + j];
-    });
+          for (int cc = 0; cc < 2; ++cc) {
+            const float sa = Sreg[4 * g + cc], sb = Sreg[4 * g + 2 + cc];
+            ST[(m + cc) * VB + va] = odd ? sb : sa;
+            ST[(m + cc) * VB + vb] = odd ? sa : sb;
+          }
+        }
+      });
+    } else {
+      for_frag<VB, KD>(tb + CO::SUT, [&](int v, int m0, int q, const float* x) {
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + j;
+          const float s = s_dCm1[m] * (aC * s_d1[m] * Sreg[16 * q + j] + x[j]);
+          Sreg[16 * q + j] = s;
+          y[j] = s * s_d1[m];
+        }
+        st8(SB, umma::kmaj(v, m0, KD), y);
+        st8(SB, umma::kmaj(v, m0 + 8, KD), y + 8);
+        if (stage && c + 1 < NC)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ST[(m0 + j) * VB + v] = Sreg[16 * q + j];
+      });
+    }
     if (!CO::DEFER) emit_out(c, tb + CO::OS, gates.a);
     publish_smem();
   }
@@ -491,9 +553,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   if (st_issuer || p_issuer) bulk_wait_all();
   if (ok && S_final && sown) {
 #pragma unroll
-    for (int q = 0; q < KD / 32; ++q)
-#pragma unroll
-      for (int j = 0; j < 16; ++j) S_final[sbase + (int64_t)(frag_col0<VB, KD>(q) + j) * V] = Sreg[16 * q + j];
+    for (int k = 0; k < NS; ++k) S_final[bhKV + vb0 + s_v(k) + (int64_t)s_m(k) * V] = Sreg[k];
   }
   if (!ok) {
     if (tid == 0) atomicOr(&g_fault, 1u);

@@ -98,12 +98,16 @@ struct BCols {
 enum : int { B_PH_VEC = 1, B_DO_VEC = 2, B_DV_VEC = 4, B_G_VEC = 8, B_K_VEC = 16, B_OVERWRITE = 32 };
 
 // ---- asynchronous copies of the next chunk's saved data ------------------------------------
+// element (m, v) of the staged state: rows m of BVB floats, v XOR-swizzled in 8-float groups by
+// (m / 2) % 4, so the state-layout reads (8 rows v by 4 column pairs m per instruction) hit 32
+// distinct banks; 16-byte runs stay contiguous
+__device__ __forceinline__ int cst_idx(int m, int v) { return m * BVB + (v ^ (((m >> 1) & 3) << 3)); }
 template <int KD>
 __device__ __forceinline__ void pf_state(uint8_t* dst, const float* cstates, int64_t slot_base, int V, int vb0) {
   // 64 rows m of 64 fp32 columns -> [m][v] (16 copies per row)
   for (int u = threadIdx.x; u < KD * 16; u += NT) {
     const int m = u >> 4, v4 = (u & 15) * 4;
-    cp16(dst + (m * BVB + v4) * 4, cstates + slot_base + (int64_t)m * V + vb0 + v4, true);
+    cp16(dst + cst_idx(m, v4) * 4, cstates + slot_base + (int64_t)m * V + vb0 + v4, true);
   }
 }
 __device__ __forceinline__ void pf_bytes(uint8_t* dst, const uint8_t* src, int nbytes) {
@@ -394,20 +398,19 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     ELL[i * L::CS + m] = __expf(-s_lam[m] * (float)i);
   }
 
-  // state-layout registers (rows v of an M = 64 fragment, columns m): adjoint dS and Sp
-  constexpr int NS = KD / 2;
+  // state-layout registers: the M = VB (rows v) x N = KD (columns m) accumulator layout over all
+  // 32 lanes (for_frag16): element k at row s_v(k), column s_m(k); adjoint dS and Sp
+  constexpr int NS = KD / 4;
   float dSreg[NS], Spreg[NS], Lreg[NS];  // Lreg: state-side d(lam) terms summed over the chunks
-  const int srow = frag_row<VB>();
-  const bool sown = owns_rows<VB>();
+  const int sv0 = 16 * sub + (lane >> 2), sm0 = half * (KD / 2) + 2 * (lane & 3);
+  auto s_v = [&](int k) { return sv0 + 8 * ((k >> 1) & 1); };
+  auto s_m = [&](int k) { return sm0 + 8 * (k >> 2) + (k & 1); };
   const int64_t bhKV = ((int64_t)b * p.H + h) * KD * (int64_t)V;
 #pragma unroll
-  for (int q = 0; q < KD / 32; ++q)
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int m = frag_col0<VB, KD>(q) + j;
-      dSreg[16 * q + j] = (sown && dS_final) ? dS_final[bhKV + (int64_t)m * V + vb0 + srow] : 0.f;
-      Lreg[16 * q + j] = 0.f;
-    }
+  for (int k = 0; k < NS; ++k) {
+    dSreg[k] = dS_final ? dS_final[bhKV + (int64_t)s_m(k) * V + vb0 + s_v(k)] : 0.f;
+    Lreg[k] = 0.f;
+  }
 
   auto wait_mma = [&]() -> bool {
     if (!umma::mbar_wait(mbar, phase)) *s_err = 1;
@@ -476,23 +479,21 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     }
     cp_commit();
     // Sp = d1 .* S (state layout registers) and the bf16 operands Sp^T, dSc^T [v][m]
-    if (sown) {
 #pragma unroll
-      for (int q = 0; q < KD / 32; ++q) {
-        const int m0 = frag_col0<VB, KD>(q);
-        float xs[16], xd[16];
+    for (int g = 0; g < NS / 4; ++g) {
+      float xs[4], xd[4];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + j;
-          Spreg[16 * q + j] = CST[m * VB + srow] * s_d1[m];
-          xs[j] = Spreg[16 * q + j];
-          xd[j] = s_dCm1[m] * dSreg[16 * q + j];
-        }
-        st8(SB, umma::kmaj(srow, m0, KD), xs);
-        st8(SB, umma::kmaj(srow, m0 + 8, KD), xs + 8);
-        st8(DSB, umma::kmaj(srow, m0, KD), xd);
-        st8(DSB, umma::kmaj(srow, m0 + 8, KD), xd + 8);
+      for (int e = 0; e < 4; ++e) {
+        const int k = 4 * g + e, m = s_m(k);
+        Spreg[k] = CST[cst_idx(m, s_v(k))] * s_d1[m];
+        xs[e] = Spreg[k];
+        xd[e] = s_dCm1[m] * dSreg[k];
       }
+      const int m = sm0 + 8 * g;
+      st2(SB, umma::kmaj(sv0, m, KD), xs[0], xs[1]);
+      st2(SB, umma::kmaj(sv0 + 8, m, KD), xs[2], xs[3]);
+      st2(DSB, umma::kmaj(sv0, m, KD), xd[0], xd[1]);
+      st2(DSB, umma::kmaj(sv0 + 8, m, KD), xd[2], xd[3]);
     }
     build_codes2<FL, KD, R>(creg, sm, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
@@ -520,9 +521,9 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       if (warp == 0) load_gate_regs(p, greg, b, h, t1, C);
     }
     if (!(ok = wait_mma())) break;
-    for_frag<C, VB>(tb + CO::DE, [&](int j, int v0, int, const float* x) {
-      st8(DEA, umma::kmaj(j, v0, VB), x);
-      st8(DEA, umma::kmaj(j, v0 + 8, VB), x + 8);
+    for_frag16<VB>(tb + CO::DE, [&](int, int j0, int v, const float* x) {
+      st2(DEA, umma::kmaj(j0, v, VB), x[0], x[1]);
+      st2(DEA, umma::kmaj(j0 + 8, v, VB), x[2], x[3]);
     });
     publish_smem();
     // ================= batch 3: dY = T^T dE =================
@@ -743,29 +744,19 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       const float aC = gates.a[Cl - 1];
       const float fCl = (float)Cl;
       float daC = 0.f;
-      uint32_t ud0[KD / 32][16];
+      for_frag16<KD>(tb + CO::DS0, [&](int g, int, int, const float* d0) {
 #pragma unroll
-      for (int q = 0; q < KD / 32; ++q) umma::ld16_issue(umma::taddr(tb + CO::DS0, 32 * sub, frag_col0<VB, KD>(q)), ud0[q]);
-      umma::ld_wait();
-#pragma unroll
-      for (int q = 0; q < KD / 32; ++q) {
-        const int m0 = frag_col0<VB, KD>(q);
-        float d0[16];
-        umma::take<16>(ud0[q], d0);
-        if (sown) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + j;
-            const float sp = Spreg[16 * q + j], ds = dSreg[16 * q + j];
-            const float t = aC * s_dCm1[m] * sp * ds;
-            daC += t;
-            Lreg[16 * q + j] += -d0[j] * sp - fCl * t;
-            dSreg[16 * q + j] = aC * s_dCm1[m] * s_d1[m] * ds + s_d1[m] * d0[j];
-          }
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * g + e, m = s_m(k);
+          const float sp = Spreg[k], ds = dSreg[k];
+          const float t = aC * s_dCm1[m] * sp * ds;
+          daC += t;
+          Lreg[k] += -d0[e] * sp - fCl * t;
+          dSreg[k] = aC * s_dCm1[m] * s_d1[m] * ds + s_d1[m] * d0[e];
         }
-      }
+      });
       if (has_g) {
-        daC = warp_sum(sown ? daC : 0.f);
+        daC = warp_sum(daC);
         if (lane == 0) atomicAdd(&s_misc[0], daC);
       }
     }
@@ -1115,21 +1106,24 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   __syncthreads();
   // ---- incoming-state gradient and per-head gradients
   if (ok) {
-    if (gr.dS0 && sown) {
+    if (gr.dS0) {
 #pragma unroll
-      for (int q = 0; q < KD / 32; ++q)
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          gr.dS0[bhKV + (int64_t)(frag_col0<VB, KD>(q) + j) * V + vb0 + srow] = dSreg[16 * q + j];
+      for (int k = 0; k < NS; ++k) gr.dS0[bhKV + (int64_t)s_m(k) * V + vb0 + s_v(k)] = dSreg[k];
     }
-    if (p.lam) {  // state-side lambda terms: sum over the value rows (lanes of each warp)
+    if (p.lam) {  // state-side lambda terms: sum over the value rows (a lane's two rows, then the
+                  // eight lanes sharing its column pairs)
 #pragma unroll
-      for (int q = 0; q < KD / 32; ++q) {
-        float lv[16];
+      for (int g = 0; g < NS / 4; ++g) {
+        float l0 = Lreg[4 * g] + Lreg[4 * g + 2], l1 = Lreg[4 * g + 1] + Lreg[4 * g + 3];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) lv[j] = sown ? Lreg[16 * q + j] : 0.f;
-        const float x = warp_transpose_sum<16>(lv);
-        if ((lane & 1) == 0) atomicAdd(&s_dlam[frag_col0<VB, KD>(q) + red_index<16>(lane)], x);
+        for (int o = 4; o < 32; o <<= 1) {
+          l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        }
+        if (lane < 4) {
+          atomicAdd(&s_dlam[sm0 + 8 * g], l0);
+          atomicAdd(&s_dlam[sm0 + 8 * g + 1], l1);
+        }
       }
       __syncthreads();
     }

@@ -45,6 +45,17 @@ __device__ __forceinline__ void st8_split(bf16* hi, bf16* lo, int idx, const flo
   st8(lo, idx, l);
 }
 __device__ __forceinline__ void st1(bf16* base, int idx, float x) { base[idx] = __float2bfloat16_rn(x); }
+// 2 consecutive elements at element offset idx (even, so 4-byte aligned)
+__device__ __forceinline__ void st2(bf16* base, int idx, float a, float b) {
+  *reinterpret_cast<uint32_t*>(base + idx) = pack2(a, b);
+}
+// the same as a hi + lo pair (st8_split's rounding)
+__device__ __forceinline__ void st2_split(bf16* hi, bf16* lo, int idx, float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  *reinterpret_cast<__nv_bfloat162*>(hi + idx) = h;
+  *reinterpret_cast<uint32_t*>(lo + idx) = pack2(a - hf.x, b - hf.y);
+}
 
 // ---- accumulator fragments ----------------------------------------------------------------
 // Accumulator with M rows (64 or 128) and N columns: warp w reads TMEM sub-partition w%4 and the
@@ -78,6 +89,25 @@ __device__ __forceinline__ void for_frag(uint32_t tbase, F f) {
     float v[16];
     umma::take<16>(r[q], v);
     if (own) f(row, frag_col0<M, N>(q), q, v);
+  }
+}
+// 64-row accumulator over all 32 lanes (16x256b loads): warp w reads rows 16 (w%4) .. +15 and the
+// column half w/4 in groups of 8 columns; lane t holds rows r0 = 16 (w%4) + t/4 and r0 + 8 and
+// columns c = 2 (t%4), c + 1 of each group.  f(g, r0, col, v[4]) gets group g's values
+// (r0, col), (r0, col + 1), (r0 + 8, col), (r0 + 8, col + 1); every lane takes part.
+template <int N, class F>
+__device__ __forceinline__ void for_frag16(uint32_t tbase, F f) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = warp & 3;
+  const int r0 = 16 * sub + (lane >> 2), cb = (warp >> 2) * (N / 2);
+  uint32_t r[N / 16][4];
+#pragma unroll
+  for (int g = 0; g < N / 16; ++g) umma::ld4_rows16_issue(umma::taddr(tbase, 32 * sub, cb + 8 * g), r[g]);
+  umma::ld_wait();
+#pragma unroll
+  for (int g = 0; g < N / 16; ++g) {
+    float v[4];
+    umma::take<4>(r[g], v);
+    f(g, r0, cb + 8 * g + 2 * (lane & 3), v);
   }
 }
 
