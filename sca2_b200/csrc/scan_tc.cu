@@ -153,6 +153,8 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   // each mbar phase takes one arrival from each (a commit, or a plain arrive when it has none)
   constexpr int NISS = 2;
   const bool issuer = (tid & 31) == 0 && warp < NISS;
+  // the next chunk's gates: loaded and formed by the last warp, which issues no products
+  constexpr int GW = NT / 32 - 1;
 
   // ---- set-up: per-head constants, mbarrier, TMEM
   constexpr int KH = FL == SCA2_FLAVOR_PHASE ? KD / 2 : KD;
@@ -372,7 +374,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     if (c + 1 < NC) {  // next chunk's codes and gates into registers
       const int t1 = t0 + C, Cl1 = min(C, p.T - t1);
       load_code_regs<FL, KD>(p, creg, code_vec, b, h, t1, Cl1, pp);
-      if (warp == 0) load_gate_regs(p, greg, b, h, t1, Cl1);
+      if (warp == GW) load_gate_regs(p, greg, b, h, t1, Cl1);
     }
     // the previous chunk's outputs while this chunk's first batch runs
     if (CO::DEFER && c > 0) emit_out(c - 1, tb + CO::OS + ((c - 1) & 1) * VB, s_aprev);
@@ -465,7 +467,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
         umma::mbar_arrive(mbar);
       }
     }
-    if (warp == 0 && c + 1 < NC) gates_from_regs(greg, gset(c + 1), min(C, p.T - t0 - C));
+    if (warp == GW && c + 1 < NC) gates_from_regs(greg, gset(c + 1), min(C, p.T - t0 - C));
     if (!(ok = wait_mma())) break;
     if constexpr (W16) {
       for_frag16<C>(tb + CO::XT, [&](int g, int v0, int i, const float* x) {

@@ -320,6 +320,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   // commit (or arrive, when they have none in a batch) on the batch's mbarrier
   constexpr int NISS = 4;
   const bool issuer = lane == 0 && warp < NISS;
+  // the next chunk's gates: loaded and formed by the last warp, which issues no products
+  constexpr int GW = NT / 32 - 1;
   const int V = p.V;
   constexpr bool has_g = HG;  // a per-token scalar decay (p.g) is present: its gradient terms
   const bool excl = gridDim.y == 1;  // the only CTA writing this (b, h)'s key-side gradients
@@ -518,7 +520,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       pf_state<KD>(sm + L::CST, cstates, slot(2 * (c - 1)), V, vb0);
       cp_commit();
       load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t1, C, pp);
-      if (warp == 0) load_gate_regs(p, greg, b, h, t1, C);
+      if (warp == GW) load_gate_regs(p, greg, b, h, t1, C);
     }
     if (!(ok = wait_mma())) break;
     for_frag16<VB>(tb + CO::DE, [&](int, int j0, int v, const float* x) {
@@ -535,7 +537,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
         umma::mbar_arrive(mbar);
       }
     }
-    if (warp == 0 && c > 0) gates_from_regs(greg, gset(c - 1), C);  // the next chunk's gates
+    if (warp == GW && c > 0) gates_from_regs(greg, gset(c - 1), C);  // the next chunk's gates
     if (!(ok = wait_mma())) break;
     if (c > 0) {  // TB is free: the next chunk's T
       pf_bytes(sm + L::TB, saved(c - 1), C * C * 2);
