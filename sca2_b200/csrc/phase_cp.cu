@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
   int ui, um0;  // this thread's code unit: token ui, modes um0 .. um0 + 7
   tc::code_unit<KD / 16>(tid, ui, um0);
   float cc[8], cs8[8];  // its Kc values (cos, sin halves), kept for the lo part
+  tc::finish_code_regs<SCA2_FLAVOR_PHASE, KD>(cr, pp, h, t0, Cl);
   {  // codes
     const int i = ui, m0 = um0;
     const float fi = (float)i;
@@ -544,6 +545,7 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
   int ci, cm0;
   tc::code_unit<KD / 16>(tid, ci, cm0);
   float q1[8], q2[8];  // read columns c1, c2 of this thread's (token, 8 modes), kept for Qa
+  tc::finish_code_regs<SCA2_FLAVOR_PHASE, KD>(cr, pp, h, t0, Cl);
   {
     const float fi = (float)ci;
     const float zb = gt.beta[ci] * gt.a[ci] * ik;

@@ -73,8 +73,8 @@ struct FwdLayout {
   static constexpr int A0_END = mx(QRL + al(R * C * KD * 2), WS + al(1024 * 4));
   // scalars (floats): two sets of gates beta[C], Gc[C], a[C], w[C] (this chunk, next chunk),
   // d1[KD], dCm1[KD], lam[KD], wr[KD], wi[KD], a of the previous chunk [C], the column factors
-  // of the decay mask [C]
-  static constexpr int SC_FLOATS = 10 * C + 5 * KD;
+  // of the decay mask [C]; phase flavour (R = 2): the head's theta and omega [KD / 2 each]
+  static constexpr int SC_FLOATS = 10 * C + 5 * KD + (R == 2 ? KD : 0);
   // fp32 KD x VB staging of the state to save [m][v], where it fits the 227 KB opt-in limit
   static constexpr bool STAGE = A0_END + al(KD * VB * 4) + al(SC_FLOATS * 4) + 64 <= 227 * 1024;
   static constexpr int ST = A0_END;
@@ -103,9 +103,13 @@ __device__ __forceinline__ void copy_out(uint8_t* dst, const bf16* src, int nbyt
     *reinterpret_cast<uint4*>(dst + u) = *reinterpret_cast<const uint4*>(s + u);
 }
 
-template <int FL, int KD, int VB, int R, bool HG>
+// HG: a per-token scalar decay (p.g) is present; PJ: phases formed from projections (PhaseProj::on,
+// phase flavour).  Both are compile-time variants, so a kernel carries only the code its inputs use.
+template <int FL, int KD, int VB, int R, bool HG, bool PJ>
 __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
-                                                    float* cstates, int NCS, int flags, PhaseProj pp) {
+                                                    float* cstates, int NCS, int flags, PhaseProj pp_in) {
+  PhaseProj pp = pp_in;
+  pp.on = PJ;
   using L = FwdLayout<KD, VB, R>;
   using CO = Cols<KD, VB>;
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -129,6 +133,8 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   float* s_wi = s_wr + KD;
   float* s_aprev = s_wi + KD;
   float* s_fdec = s_aprev + C;  // column factors of the decay mask (decay_block)
+  float* s_th = R == 2 ? s_fdec + C : nullptr;  // theta, omega of the head (phases from projections)
+  float* s_om = R == 2 ? s_fdec + C + KD / 2 : nullptr;
   float* LS = reinterpret_cast<float*>(sm + L::LS);
   float* TS = reinterpret_cast<float*>(sm + L::TS);
   float* WS = reinterpret_cast<float*>(sm + L::WS);
@@ -164,6 +170,10 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     s_d1[m] = expf(-l);
     s_wr[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wr[h * KH + m] : 0.f;
     s_wi[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wi[h * KH + m] : 0.f;
+    if (R == 2 && pp.on && m < KD / 2) {
+      s_th[m] = pp.theta[h * (KD / 2) + m];
+      s_om[m] = pp.omega[h * (KD / 2) + m];
+    }
   }
   if (tid == 0) {
     umma::mbar_init(mbar, NISS);
@@ -319,6 +329,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       gates_from_regs(greg, gset(0), Cl0);
     }
     __syncthreads();
+    finish_code_regs<FL, KD>(creg, pp, h, 0, Cl0, s_th, s_om);
     build_codes<FL, KD, R>(creg, cops, gset(0), s_lam, s_wr, s_wi, p.q_scale, Cl0, ik, !prep);
   }
   // Per chunk c: the codes of chunk c (but KWW) and its gates were formed while chunk c - 1's
@@ -498,9 +509,11 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     }
     if (st_issuer) bulk_wait_read();  // ST is rewritten by the state update below
     // the next chunk's codes (their buffers are free: only KWW is read by this batch)
-    if (c + 1 < NC)
+    if (c + 1 < NC) {
+      finish_code_regs<FL, KD>(creg, pp, h, t0 + C, min(C, p.T - t0 - C), s_th, s_om);
       build_codes<FL, KD, R>(creg, cops, gset(c + 1), s_lam, s_wr, s_wi, p.q_scale, min(C, p.T - t0 - C), ik,
                              !prep);
+    }
     if (!(ok = wait_mma())) break;
     // ---- state update
     if (CO::DEFER && tid < C) s_aprev[tid] = gates.a[tid];
@@ -568,10 +581,19 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   if (tid < 32) umma::tmem_dealloc(tb, CO::ALLOC);
 }
 
+template <int FL, int KD, int VB, int R, bool HG>
+auto fwd_kernel(bool pj) {
+  if constexpr (FL == SCA2_FLAVOR_PHASE)
+    return pj ? scan_fwd_tc<FL, KD, VB, R, HG, true> : scan_fwd_tc<FL, KD, VB, R, HG, false>;
+  else
+    return scan_fwd_tc<FL, KD, VB, R, HG, false>;
+}
+
 template <int FL, int KD, int VB, int R>
 cudaError_t launch_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates,
                        int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
-  auto k = p.g.ptr ? scan_fwd_tc<FL, KD, VB, R, true> : scan_fwd_tc<FL, KD, VB, R, false>;
+  const bool pj = pp.on != 0;
+  auto k = p.g.ptr ? fwd_kernel<FL, KD, VB, R, true>(pj) : fwd_kernel<FL, KD, VB, R, false>(pj);
   const int smem = FwdLayout<KD, VB, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -72,8 +72,8 @@ struct BwdLayout {
   static constexpr int SC = ELL + C * CS * 4;
   // scalars (floats): beta, Gc, a, w, dbeta, da, dw, rows, cols [C]; d1, dCm1, lam, wr, wi,
   // dlam, dwr, dwi [KD]; misc[8]; a second set of beta, Gc, a, w [C] (the next chunk's); the
-  // column factors of the decay mask [C]
-  static constexpr int SC_FLOATS = 14 * C + 8 * KD + 8;
+  // column factors of the decay mask [C]; the head's theta and omega [Mh] (phases from projections)
+  static constexpr int SC_FLOATS = 14 * C + 8 * KD + 8 + 2 * Mh;
   static constexpr int MBAR = SC + ((SC_FLOATS * 4 + 1023) & ~1023);
   static constexpr int TOTAL = MBAR + 64;
   static_assert(TOTAL <= 227 * 1024, "shared memory");
@@ -304,10 +304,14 @@ __device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, b
   }
 }
 
-template <int FL, int R, bool HG>
+// HG: a per-token scalar decay (p.g) is present; PJ: phases formed from projections (PhaseProj::on,
+// phase flavour).  Both are compile-time variants, so a kernel carries only the code its inputs use.
+template <int FL, int R, bool HG, bool PJ>
 __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                     const float* cstates, sca2_scan_grads gr, int NCS,
-                                                    int flags, PhaseProj pp) {
+                                                    int flags, PhaseProj pp_in) {
+  PhaseProj pp = pp_in;
+  pp.on = PJ;
   using L = BwdLayout<FL, R>;
   using CO = BCols;
   constexpr int KD = 64, VB = BVB, RC = R * C, Mh = KD / 2;
@@ -349,6 +353,8 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   float* s_dwi = s_dwr + KD;
   float* s_misc = s_dwi + KD;
   float* s_fdec = s_misc + 8 + 4 * C;  // column factors of the decay mask (decay_block)
+  float* s_th = s_fdec + C;            // theta, omega of the head (phases from projections)
+  float* s_om = s_th + Mh;
   auto BF = [&](int off) { return reinterpret_cast<bf16*>(sm + off); };
   float* CST = reinterpret_cast<float*>(sm + L::CST);
   float* cache = reinterpret_cast<float*>(sm + L::CACHE);
@@ -378,6 +384,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     s_d1[m] = expf(-l);
     s_wr[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wr[h * KH + m] : 0.f;
     s_wi[m] = (FL == SCA2_FLAVOR_PHASE && m < KH) ? p.wi[h * KH + m] : 0.f;
+    if (FL == SCA2_FLAVOR_PHASE && pp.on && m < Mh) {
+      s_th[m] = pp.theta[h * Mh + m];
+      s_om[m] = pp.omega[h * Mh + m];
+    }
     s_dlam[m] = 0.f;
     s_dwr[m] = 0.f;
     s_dwi[m] = 0.f;
@@ -497,6 +507,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
       st2(DSB, umma::kmaj(sv0, m, KD), xd[0], xd[1]);
       st2(DSB, umma::kmaj(sv0 + 8, m, KD), xd[2], xd[3]);
     }
+    finish_code_regs<FL, KD>(creg, pp, h, t0, Cl, s_th, s_om);
     build_codes2<FL, KD, R>(creg, sm, gates, s_lam, s_wr, s_wi, p.q_scale, Cl, ik);
     publish_smem();
     // ================= batch 1 =================
@@ -1145,10 +1156,19 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   if (tid < 32) umma::tmem_dealloc(tb, CO::ALLOC);
 }
 
+template <int FL, int R, bool HG>
+auto bwd_kernel(bool pj) {
+  if constexpr (FL == SCA2_FLAVOR_PHASE)
+    return pj ? scan_bwd_tc<FL, R, HG, true> : scan_bwd_tc<FL, R, HG, false>;
+  else
+    return scan_bwd_tc<FL, R, HG, false>;
+}
+
 template <int FL, int R>
 cudaError_t launch_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
                        const sca2_scan_grads& gr, int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
-  auto k = p.g.ptr ? scan_bwd_tc<FL, R, true> : scan_bwd_tc<FL, R, false>;
+  const bool pj = pp.on != 0;
+  auto k = p.g.ptr ? bwd_kernel<FL, R, true>(pj) : bwd_kernel<FL, R, false>(pj);
   const int smem = BwdLayout<FL, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -77,6 +77,7 @@ __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* c
   umma::fence_after_sync();
   const uint32_t tb = *s_tmem;
   if (has_g) decay_factors(gates.Gc, s_fdec);  // visible after the barrier past the Gram product
+  finish_code_regs<FL, KD>(cr, pp, h, t0, Cl);
   // ---- codes kr, kw (bf16, [i][m])
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     constexpr int Mh = KD / 2;

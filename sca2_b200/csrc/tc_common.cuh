@@ -332,9 +332,13 @@ __device__ __forceinline__ void decay_block(const float* Gc, const float* fdec, 
 // units t and t+256 of (token u/8, dims 8(u%8)..+7) of k and q.  vec: 16-byte loads are aligned.
 template <int FL, int KD>
 struct CodeRegs {
-  // phase: one unit (phi, psi x 8 modes); key: NU units (k, q x 8 dims)
+  // phase: one unit (phi, psi x 8 modes); key: NU units (k, q x 8 dims).  Phases from the
+  // projections (PhaseProj::on): load_code_regs leaves the loaded K(h), K(z) bits in w, q (bf16:
+  // 4 words each; fp32: 8 values) and the position offset in pos; finish_code_regs forms the
+  // phases where the codes are built, so no thread waits for those loads in between.
   static constexpr int NU = FL == SCA2_FLAVOR_PHASE ? 1 : C * KD / 8 / NT;
   float w[NU][8], q[NU][8];
+  float pos;
 };
 
 // 8 projection values of one token row (bf16 or fp32, 16-byte loads when vec)
@@ -362,6 +366,34 @@ __device__ __forceinline__ void load8(const void* base, int64_t off, int dtype, 
   }
 }
 
+// 8 projection values of one token row as loaded: bf16 packed two per word in x[0..3], fp32 in
+// x[0..7] (16-byte loads when vec; the registers are not read here)
+__device__ __forceinline__ void raw8(const void* base, int64_t off, int dtype, bool vec, float* x) {
+  if (dtype == SCA2_BF16) {
+    const bf16* q = reinterpret_cast<const bf16*>(base) + off;
+    uint4 u;
+    if (vec) {
+      u = *reinterpret_cast<const uint4*>(q);
+    } else {
+      const uint16_t* q16 = reinterpret_cast<const uint16_t*>(q);
+      u.x = q16[0] | ((uint32_t)q16[1] << 16);
+      u.y = q16[2] | ((uint32_t)q16[3] << 16);
+      u.z = q16[4] | ((uint32_t)q16[5] << 16);
+      u.w = q16[6] | ((uint32_t)q16[7] << 16);
+    }
+    x[0] = __uint_as_float(u.x), x[1] = __uint_as_float(u.y), x[2] = __uint_as_float(u.z), x[3] = __uint_as_float(u.w);
+  } else {
+    const float* q = reinterpret_cast<const float*>(base) + off;
+    if (vec) {
+      const float4 a = reinterpret_cast<const float4*>(q)[0], c = reinterpret_cast<const float4*>(q)[1];
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = q[k];
+    }
+  }
+}
+
 template <int FL, int KD>
 __device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs<FL, KD>& r, bool vec, int b, int h,
                                                int t0, int Cl, const PhaseProj& pp = PhaseProj{}) {
@@ -369,24 +401,14 @@ __device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs
   if constexpr (FL == SCA2_FLAVOR_PHASE) {
     int i, m0;
     code_unit<KD / 16>(tid, i, m0);
-    if (pp.on) {  // phases from the projections: phi = K(h) theta + (pos + t) omega
+    if (pp.on) {  // projections K(h), K(z) as loaded (raw bits); the phases in finish_code_regs
+#pragma unroll
+      for (int k = 0; k < 8; ++k) { r.w[0][k] = 0.f; r.q[0][k] = 0.f; }
+      r.pos = 0.f;
       if (i < Cl) {
-        constexpr int Mh = KD / 2;
-        float kh[8], kz[8];
-        load8(p.phw.ptr, tok_off(p.phw, b, t0 + i, h) + m0, pp.dtype, vec, kh);
-        load8(p.phq.ptr, tok_off(p.phq, b, t0 + i, h) + m0, pp.dtype, vec, kz);
-        const float pt = __fadd_rn(pp.pos ? *pp.pos : 0.f, (float)(t0 + i));
-        const float* th = pp.theta + h * Mh + m0;
-        const float* om = pp.omega + h * Mh + m0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float po = __fmul_rn(pt, om[k]);
-          r.w[0][k] = __fadd_rn(__fmul_rn(kh[k], th[k]), po);
-          r.q[0][k] = __fadd_rn(__fmul_rn(kz[k], th[k]), po);
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { r.w[0][k] = 0.f; r.q[0][k] = 0.f; }
+        r.pos = pp.pos ? *pp.pos : 0.f;
+        raw8(p.phw.ptr, tok_off(p.phw, b, t0 + i, h) + m0, pp.dtype, vec, r.w[0]);
+        raw8(p.phq.ptr, tok_off(p.phq, b, t0 + i, h) + m0, pp.dtype, vec, r.q[0]);
       }
       return;
     }
@@ -438,6 +460,45 @@ __device__ __forceinline__ void load_code_regs(const sca2_scan_args& p, CodeRegs
 #pragma unroll
         for (int k = 0; k < 8; ++k) { r.w[u][k] = 0.f; r.q[u][k] = 0.f; }
       }
+    }
+  }
+}
+// The phases of the projections (PhaseProj::on) in place of the loaded bits, with the rounding
+// of each step as the reference forms them: phi = K(h) theta + (pos + t) omega and psi = K(z)
+// theta + (pos + t) omega (rows i >= Cl stay zero).  A no-op for every other input.  Called where
+// the codes are built, on the (t0, Cl) of the matching load_code_regs; s_th, s_om: the head's
+// theta and omega staged in shared memory (else read from global memory).
+template <int FL, int KD>
+__device__ __forceinline__ void finish_code_regs(CodeRegs<FL, KD>& r, const PhaseProj& pp, int h, int t0, int Cl,
+                                                 const float* s_th = nullptr, const float* s_om = nullptr) {
+  if constexpr (FL == SCA2_FLAVOR_PHASE) {
+    if (!pp.on) return;
+    int i, m0;
+    code_unit<KD / 16>(threadIdx.x, i, m0);
+    if (i >= Cl) return;
+    constexpr int Mh = KD / 2;
+    float kh[8], kz[8];
+    if (pp.dtype == SCA2_BF16) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t a = __float_as_uint(r.w[0][k]), c = __float_as_uint(r.q[0][k]);
+        const __nv_bfloat162 a2 = *reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162*>(&c);
+        kh[2 * k] = __low2float(a2), kh[2 * k + 1] = __high2float(a2);
+        kz[2 * k] = __low2float(c2), kz[2 * k + 1] = __high2float(c2);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) kh[k] = r.w[0][k], kz[k] = r.q[0][k];
+    }
+    const float pt = __fadd_rn(r.pos, (float)(t0 + i));
+    const float* th = (s_th ? s_th : pp.theta + h * Mh) + m0;
+    const float* om = (s_om ? s_om : pp.omega + h * Mh) + m0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float po = __fmul_rn(pt, om[k]);
+      r.w[0][k] = __fadd_rn(__fmul_rn(kh[k], th[k]), po);
+      r.q[0][k] = __fadd_rn(__fmul_rn(kz[k], th[k]), po);
     }
   }
 }
