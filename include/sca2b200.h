@@ -251,6 +251,22 @@ SCA2_API int sca2_scan_fwd_proj(const sca2_scan_args* a, const sca2_phase_proj* 
 /* Bytes of the workspace of sca2_scan_bwd_proj. */
 SCA2_API int64_t sca2_scan_proj_work_bytes(int32_t B, int32_t T, int32_t H, int32_t Mh);
 
+/* ---- inference forward with a work buffer ---------------------------------------------------
+ * Bytes of the work buffer of sca2_scan_fwd_work for these arguments: B*H*ceil(T/64)*8 KB where
+ * the tensor-core forward covers the call at K = 64 (bf16 values), else 0. */
+SCA2_API int64_t sca2_scan_fwd_work_bytes(const sca2_scan_args* a);
+
+/* Forward without saved chunk states (inference), with phases (pp NULL, as sca2_scan_fwd with
+ * chunk_states NULL) or projected phases (pp non-NULL, as sca2_scan_fwd_proj with chunk_states
+ * NULL).  Where sca2_scan_fwd_work_bytes(a) > 0 the delta-rule inverse of every 64-token chunk
+ * is first computed chunk-parallel into `work` (16-byte aligned, at least that many bytes), and
+ * the sequential chunk walk reads it instead of inverting inside its loop; otherwise `work` is
+ * not used.  Same outputs as the calls named (the inverse is formed by the same fp32 algorithm
+ * and rounded to bf16 in both).  Replaces the same reference prefill paths as sca2_scan_fwd
+ * (lapa/layer.py:298-366 with no autograd graph kept). */
+SCA2_API int sca2_scan_fwd_work(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out o,
+                   float* S_final, void* work, int64_t work_bytes, void* stream);
+
 /* Backward with projected phases: as sca2_scan_bwd, except that gr->dphw / gr->dphq receive
  * the gradients of K(h) / K(z) in pp->dtype (WRITTEN, not accumulated) and dtheta (H, Mh)
  * the gradient of theta (written). */

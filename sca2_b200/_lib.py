@@ -121,6 +121,9 @@ SIGNATURES = [
     ("sca2_scan_fwd_proj", C.c_int, [C.POINTER(ScanArgs), C.POINTER(PhaseProj), Out, C.c_void_p, C.c_void_p,
                                      C.c_void_p]),
     ("sca2_scan_proj_work_bytes", C.c_int64, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    ("sca2_scan_fwd_work_bytes", C.c_int64, [C.POINTER(ScanArgs)]),
+    ("sca2_scan_fwd_work", C.c_int, [C.POINTER(ScanArgs), C.POINTER(PhaseProj), Out, C.c_void_p, C.c_void_p,
+                                     C.c_int64, C.c_void_p]),
     ("sca2_scan_bwd_proj", C.c_int, [C.POINTER(ScanArgs), C.POINTER(PhaseProj), Out, C.c_void_p, C.c_void_p,
                                      C.POINTER(ScanGrads), C.c_void_p, C.c_void_p, C.c_void_p]),
     ("sca2_short_fwd", C.c_int, [C.POINTER(ShortArgs), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

@@ -27,7 +27,9 @@ cudaError_t launch_rms_bwd(const void* x, const void* du, void* dx, int64_t N, i
 // scan_tc.cu
 int tc_fwd_vb(int K, int V, int R, int max_smem);
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
-                        float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp = PhaseProj{});
+                        float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp = PhaseProj{},
+                        void* work = nullptr);
+int64_t tc_infer_work_bytes(const sca2_scan_args& p);
 cudaError_t tc_read_faults(unsigned int* out);
 cudaError_t tc_read_faults_bwd(unsigned int* out);
 // readout.cu
@@ -341,6 +343,42 @@ int sca2_scan_fwd_proj(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_
   cudaError_t e = sca2::tc_scan_fwd(*a, vb, o, S_final, chunk_states, sca2::state_slots(a->T),
                                     reinterpret_cast<cudaStream_t>(stream), to_pp(pp));
   if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd_proj");
+  return SCA2_OK;
+}
+
+// Inference forward with a caller work buffer: where the tensor-core forward covers the call at
+// K = 64, T of every chunk is computed chunk-parallel into the work buffer first, so the chunk walk
+// no longer inverts inside its sequential loop.  Needs sca2_scan_fwd_work_bytes(a) bytes; 0 bytes
+// (any other shape or dtype) runs exactly what sca2_scan_fwd / sca2_scan_fwd_proj run without
+// saved chunk states.
+int64_t sca2_scan_fwd_work_bytes(const sca2_scan_args* a) {
+  if (!a || check_scan(a, false) != SCA2_OK || a->T <= 0 || a->io_dtype != SCA2_BF16) return 0;
+  const int R = a->flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
+  if (sca2::tc_fwd_vb(a->K, a->V, R, max_optin_smem()) == 0) return 0;
+  return sca2::tc_infer_work_bytes(*a);
+}
+
+int sca2_scan_fwd_work(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out o, float* S_final, void* work,
+                       int64_t work_bytes, void* stream) {
+  int rc = check_scan(a, false);
+  if (rc) return rc;
+  if (a->T == 0) return sca2_scan_fwd(a, o, S_final, nullptr, stream);
+  if (!o.ptr) return fail(SCA2_ERR_ARG, "output o must be non-null");
+  if (pp && !proj_covered(a, pp, false))
+    return fail(SCA2_ERR_UNSUPPORTED, "projected phases need the tensor-core path (bf16 values, K = 64) and "
+                                      "16-byte aligned projection rows");
+  const int64_t need = sca2_scan_fwd_work_bytes(a);
+  if (need > 0 && (!work || work_bytes < need))
+    return fail(SCA2_ERR_ARG, "work buffer smaller than sca2_scan_fwd_work_bytes()");
+  if (need > 0 && ((uintptr_t)work & 15u) != 0) return fail(SCA2_ERR_ARG, "work buffer not 16-byte aligned");
+  if (need == 0) return pp ? sca2_scan_fwd_proj(a, pp, o, S_final, nullptr, stream)
+                           : sca2_scan_fwd(a, o, S_final, nullptr, stream);
+  const int R = a->flavor == SCA2_FLAVOR_PHASE ? 2 : 1;
+  const int vb = sca2::tc_fwd_vb(a->K, a->V, R, max_optin_smem());
+  cudaError_t e = sca2::tc_scan_fwd(*a, vb, o, S_final, nullptr, sca2::state_slots(a->T),
+                                    reinterpret_cast<cudaStream_t>(stream),
+                                    pp ? to_pp(pp) : sca2::PhaseProj{}, work);
+  if (e != cudaSuccess) return cuda_fail(e, "sca2_scan_fwd_work");
   return SCA2_OK;
 }
 

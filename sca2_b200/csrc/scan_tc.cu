@@ -107,7 +107,8 @@ __device__ __forceinline__ void copy_out(uint8_t* dst, const bf16* src, int nbyt
 // phase flavour).  Both are compile-time variants, so a kernel carries only the code its inputs use.
 template <int FL, int KD, int VB, int R, bool HG, bool PJ>
 __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
-                                                    float* cstates, int NCS, int flags, PhaseProj pp_in) {
+                                                    float* cstates, int NCS, int flags, PhaseProj pp_in,
+                                                    TSlots ts) {
   PhaseProj pp = pp_in;
   pp.on = PJ;
   using L = FwdLayout<KD, VB, R>;
@@ -309,19 +310,23 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   // the previous one runs
   CodeRegs<FL, KD> creg;
   GateRegs greg;
-  const bool prep = (flags & F_PREP) && cstates;
+  // prep: T of every chunk is read from ts (training: slot 2c + 1; inference: the work buffer)
+  const bool prep = (flags & F_PREP) && ts.base;
   // training: each chunk's P (hi part, operand layout) goes to slot 2 NC + c for the backward,
   // one bulk copy issued by thread 32 (plain 16-byte stores when the buffer is not aligned)
-  const bool p_save = prep && blockIdx.y == 0;
+  const bool p_save = prep && cstates && blockIdx.y == 0;
   const bool p_issuer = p_save && (flags & F_CS16) && tid == 32;
   auto saved_at = [&](int cc) -> uint8_t* {
     return reinterpret_cast<uint8_t*>(cstates + (((int64_t)b * p.H + h) * NCS + 2 * cc + 1) * KD * (int64_t)V);
+  };
+  auto t_at = [&](int cc) -> const uint8_t* {
+    return ts.base + ((int64_t)b * p.H + h) * ts.bh_stride + (int64_t)cc * ts.c_stride;
   };
   {
     const int Cl0 = min(C, p.T);
     pf_values<VB>(p, VA, flags & F_V_VEC, b, h, 0, Cl0, vb0);
     if (prep)
-      for (int u = tid * 16; u < C * C * 2; u += NT * 16) cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(0) + u, true);
+      for (int u = tid * 16; u < C * C * 2; u += NT * 16) cp16(reinterpret_cast<uint8_t*>(TB) + u, t_at(0) + u, true);
     cp_commit();
     load_code_regs<FL, KD>(p, creg, code_vec, b, h, 0, Cl0, pp);
     if (warp == 0) {
@@ -440,7 +445,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       pf_values<VB>(p, VA, flags & F_V_VEC, b, h, t1, min(C, p.T - t1), vb0);
       if (prep)
         for (int u = tid * 16; u < C * C * 2; u += NT * 16)
-          cp16(reinterpret_cast<uint8_t*>(TB) + u, saved_at(c + 1) + u, true);
+          cp16(reinterpret_cast<uint8_t*>(TB) + u, t_at(c + 1) + u, true);
       cp_commit();
     }
     if constexpr (W16) {
@@ -591,14 +596,14 @@ auto fwd_kernel(bool pj) {
 
 template <int FL, int KD, int VB, int R>
 cudaError_t launch_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates,
-                       int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
+                       int NCS, int flags, const PhaseProj& pp, const TSlots& ts, cudaStream_t st) {
   const bool pj = pp.on != 0;
   auto k = p.g.ptr ? fwd_kernel<FL, KD, VB, R, true>(pj) : fwd_kernel<FL, KD, VB, R, false>(pj);
   const int smem = FwdLayout<KD, VB, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, p.V / VB);
-  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags, pp);
+  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags, pp, ts);
   return cudaGetLastError();
 }
 
@@ -639,34 +644,52 @@ static int tc_flags(const sca2_scan_args& p, const sca2_out& o) {
   return f;
 }
 
-cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, const PhaseProj& pp,
+cudaError_t tc_scan_prep(const sca2_scan_args& p, const tc::TSlots& ts, int vec, const PhaseProj& pp,
                          cudaStream_t st);
+
+// Bytes of the inference work buffer (T of every chunk, bf16 C x C each) for a K = 64 forward on
+// the tensor cores; the preparation kernel covers K = 64 only.
+int64_t tc_infer_work_bytes(const sca2_scan_args& p) {
+  if (p.K != 64 || p.T <= 0) return 0;
+  return (int64_t)p.B * p.H * ((p.T + tc::C - 1) / tc::C) * (tc::C * tc::C * 2);
+}
 // phase_cp.cu: the chunk-parallel training forward of the phase flavour at K = V = 64
 bool pcp_covers(const sca2_scan_args& p, const float* cstates);
 cudaError_t pcp_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates, int NS,
                          int flags, const PhaseProj& pp, cudaStream_t st);
 
+// work: inference only (cstates == nullptr), nullptr or tc_infer_work_bytes(p) bytes, 16-byte
+// aligned: T of every chunk is computed chunk-parallel into it first and the walk reads it instead
+// of inverting inside its sequential loop (the training forward does the same through slot 2c + 1)
 cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, float* S_final,
-                        float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp) {
+                        float* cstates, int NCS, cudaStream_t st, const PhaseProj& pp, void* work) {
   const bool ph = p.flavor == SCA2_FLAVOR_PHASE;
   int fl = tc_flags(p, o);
   // training of the phase flavour at K = V = 64: chunk-parallel, its saved data in the layout the
   // tensor-core backward reads
   if (pcp_covers(p, cstates)) return pcp_scan_fwd(p, o, S_final, cstates, NCS, fl, pp, st);
   if (cstates && ((uintptr_t)cstates & 15u) == 0) fl |= tc::F_CS16;
-  if (cstates && p.K == 64) {  // training: T of every chunk from the chunk-parallel kernel
-    cudaError_t e = tc_scan_prep(p, cstates, NCS, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), pp, st);
+  tc::TSlots ts{nullptr, 0, 0};
+  if (cstates && p.K == 64) {  // training: T of every chunk in slot 2c + 1
+    const int64_t slot = (int64_t)p.K * p.V * 4;
+    ts = tc::TSlots{reinterpret_cast<uint8_t*>(cstates) + slot, NCS * slot, 2 * slot};
+  } else if (!cstates && work && tc_infer_work_bytes(p) > 0 && ((uintptr_t)work & 15u) == 0) {
+    const int64_t tb = tc::C * tc::C * 2;  // inference: compact, chunk after chunk
+    ts = tc::TSlots{static_cast<uint8_t*>(work), ((p.T + tc::C - 1) / tc::C) * tb, tb};
+  }
+  if (ts.base) {  // T of every chunk from the chunk-parallel kernel
+    cudaError_t e = tc_scan_prep(p, ts, fl & (ph ? tc::F_PH_VEC : tc::F_K_VEC), pp, st);
     if (e != cudaSuccess) return e;
     fl |= tc::F_PREP;
   }
-#define SCA2_TC_FWD(KD_, VB_)                                                                         \
-  if (p.K == KD_ && VB == VB_)                                                                        \
-    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, pp, st)   \
-              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, pp, st);
+#define SCA2_TC_FWD(KD_, VB_)                                                                             \
+  if (p.K == KD_ && VB == VB_)                                                                            \
+    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, pp, ts, st)   \
+              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, pp, ts, st);
   SCA2_TC_FWD(64, 64) SCA2_TC_FWD(64, 128)
 #undef SCA2_TC_FWD
   if (p.K == 128 && VB == 64 && !ph)
-    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, pp, st);
+    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, pp, ts, st);
   return cudaErrorInvalidValue;
 }
 

@@ -1,11 +1,12 @@
-// Chunk-parallel preparation for the tensor-core training scan (sm_100a): for every 64-token
-// chunk of every (b, h), the inverse
+// Chunk-parallel preparation for the tensor-core scan (sm_100a): for every 64-token chunk of
+// every (b, h), the inverse
 //
 //     T = (I + diag(beta) Gr)^{-1},   Gr = (kr kw^T / kappa) .* Dg, strictly lower
 //
 // (the delta-rule solve of the chunk, independent of the state) is computed once and written,
-// bf16 in the tcgen05 operand layout, to slot 2c+1 of the saved-state buffer.  The forward
-// and the backward copy it from there instead of inverting inside their sequential chunk walk.
+// bf16 in the tcgen05 operand layout: in training to slot 2c+1 of the saved-state buffer, where
+// the forward and the backward copy it from; in inference to a compact work buffer the forward
+// copies it from.  Neither walk then inverts inside its sequential chunk loop.
 //
 // One CTA (8 warps) per chunk and about 60 KB of shared memory, so several chunks run per SM:
 // codes from the phases (keys), G = KR KW^T on the tensor cores (bounded mbarrier wait), the
@@ -36,7 +37,7 @@ struct PrepLayout {
 };
 
 template <int FL, int KD, bool HG>
-__global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* cstates, int NCS, int vec,
+__global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, TSlots ts, int vec,
                                                      PhaseProj pp) {
   using L = PrepLayout<KD>;
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* c
     invert_unit_lower(LS, TS, WS);
     store_T<false>(TS, TB);
     __syncthreads();
-    uint8_t* dst = reinterpret_cast<uint8_t*>(cstates + (((int64_t)b * p.H + h) * NCS + 2 * c + 1) * KD * (int64_t)p.V);
+    uint8_t* dst = ts.base + (int64_t)bh * ts.bh_stride + (int64_t)c * ts.c_stride;
     const uint8_t* src = reinterpret_cast<const uint8_t*>(TB);
     for (int u = tid * 16; u < C * C * 2; u += NT * 16)
       *reinterpret_cast<uint4*>(dst + u) = *reinterpret_cast<const uint4*>(src + u);
@@ -154,8 +155,8 @@ __global__ void __launch_bounds__(NT, 4) scan_prep_tc(sca2_scan_args p, float* c
 
 }  // namespace tc
 
-// T of every chunk into slot 2c+1 of cstates (K = 64); vec: 16-byte loads of the phases / keys
-cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int vec, const PhaseProj& pp,
+// T of every chunk where ts says (K = 64); vec: 16-byte loads of the phases / keys
+cudaError_t tc_scan_prep(const sca2_scan_args& p, const tc::TSlots& ts, int vec, const PhaseProj& pp,
                          cudaStream_t st) {
   const int NC = (p.T + tc::C - 1) / tc::C;
   if (NC == 0) return cudaSuccess;
@@ -165,12 +166,12 @@ cudaError_t tc_scan_prep(const sca2_scan_args& p, float* cstates, int NCS, int v
     auto k = p.g.ptr ? tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64, true> : tc::scan_prep_tc<SCA2_FLAVOR_PHASE, 64, false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec, pp);
+    k<<<grid, tc::NT, smem, st>>>(p, ts, vec, pp);
   } else {
     auto k = p.g.ptr ? tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64, true> : tc::scan_prep_tc<SCA2_FLAVOR_KEY, 64, false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k<<<grid, tc::NT, smem, st>>>(p, cstates, NCS, vec, pp);
+    k<<<grid, tc::NT, smem, st>>>(p, ts, vec, pp);
   }
   return cudaGetLastError();
 }

@@ -15,9 +15,18 @@ constexpr int LDF = C + 4;  // fp32 row stride of the inversion scratch (rows 16
 using bf16 = __nv_bfloat16;
 
 // launch flags (host-computed, uniform)
-// F_PREP: T of every chunk was written to slot 2c+1 by the preparation kernel
+// F_PREP: T of every chunk was written by the preparation kernel (where TSlots says)
 // F_CS16: the chunk-state buffer is 16-byte aligned (bulk copies may write it)
 enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8, F_PREP = 16, F_CS16 = 32 };
+
+// Where the preparation kernel puts each chunk's inverse T (bf16 C x C in operand layout, 8 KB):
+// chunk c of sequence bh = b H + h at base + bh * bh_stride + c * c_stride (bytes, all multiples
+// of 16).  Training: slot 2c + 1 of the chunk-state buffer, which the backward reads again;
+// inference: a compact work buffer of the caller's (c_stride = 8 KB).
+struct TSlots {
+  uint8_t* base;
+  int64_t bh_stride, c_stride;
+};
 
 // ---- bf16 vector stores -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack2(float a, float b) {

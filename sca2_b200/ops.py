@@ -114,6 +114,17 @@ def _slots(T: int) -> int:
     return 4 * ((T + 63) // 64) if T > 0 else 0
 
 
+def _fwd_infer(a, pp, o: Out, S: torch.Tensor, dev: torch.device, what: str):
+    """Forward without saved chunk states (sca2_scan_fwd_work): where the tensor-core path covers
+    the call, every chunk's delta-rule inverse is formed chunk-parallel into a work buffer first
+    and the chunk walk reads it instead of inverting inside its sequential loop."""
+    lib = _lib.load()
+    n = int(lib.sca2_scan_fwd_work_bytes(C_ref(a)))
+    work = torch.empty(n, device=dev, dtype=torch.uint8) if n > 0 else None
+    _lib.check(lib.sca2_scan_fwd_work(C_ref(a), None if pp is None else C_ref(pp), o, _ptr(S), _ptr(work), n,
+                                      _stream()), what)
+
+
 @torch.library.custom_op("sca2b200::phase_scan_fwd", mutates_args=())
 def _phase_scan_fwd(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta: Optional[torch.Tensor],
                     g: Optional[torch.Tensor], lam: Optional[torch.Tensor], wr: torch.Tensor, wi: torch.Tensor,
@@ -134,8 +145,10 @@ def _phase_scan_fwd(phw: torch.Tensor, phq: torch.Tensor, v: torch.Tensor, beta:
     S = torch.empty(B, H, 2 * Mh, V, device=v.device, dtype=torch.float32)
     cs = (torch.empty(B, H, _slots(T), 2 * Mh, V, device=v.device, dtype=torch.float32) if save
           else torch.empty(0, device=v.device, dtype=torch.float32))
-    _lib.check(_lib.load().sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs) if save else None, _stream()),
-               "scan_fwd")
+    if save:
+        _lib.check(_lib.load().sca2_scan_fwd(C_ref(a), _out(o), _ptr(S), _ptr(cs), _stream()), "scan_fwd")
+    else:
+        _fwd_infer(a, None, _out(o), S, v.device, "scan_fwd")
     return o, S, cs
 
 
@@ -269,8 +282,12 @@ def _phase_scan_proj_fwd(kh: torch.Tensor, kz: torch.Tensor, v: torch.Tensor, be
     S = torch.empty(B, H, 2 * Mh, V, device=v.device, dtype=torch.float32)
     cs = (torch.empty(B, H, _slots(T), 2 * Mh, V, device=v.device, dtype=torch.float32) if save
           else torch.empty(0, device=v.device, dtype=torch.float32))
-    _lib.check(_lib.load().sca2_scan_fwd_proj(C_ref(a), C_ref(_pp(kh, theta, omega, pos)), _out(o), _ptr(S),
-                                              _ptr(cs) if save else None, _stream()), "scan_fwd_proj")
+    pp = _pp(kh, theta, omega, pos)
+    if save:
+        _lib.check(_lib.load().sca2_scan_fwd_proj(C_ref(a), C_ref(pp), _out(o), _ptr(S), _ptr(cs), _stream()),
+                   "scan_fwd_proj")
+    else:
+        _fwd_infer(a, pp, _out(o), S, v.device, "scan_fwd_proj")
     return o, S, cs
 
 
@@ -426,8 +443,11 @@ def _key_scan_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: Optional
     S = torch.empty(B, H, K, V, device=v.device, dtype=torch.float32)
     cs = (torch.empty(B, H, _slots(T), K, V, device=v.device, dtype=torch.float32) if save
           else torch.empty(0, device=v.device, dtype=torch.float32))
-    _lib.check(_lib.load().sca2_scan_fwd(C_ref(a), _out(o.unsqueeze(3)), _ptr(S), _ptr(cs) if save else None,
-                                         _stream()), "scan_fwd")
+    if save:
+        _lib.check(_lib.load().sca2_scan_fwd(C_ref(a), _out(o.unsqueeze(3)), _ptr(S), _ptr(cs), _stream()),
+                   "scan_fwd")
+    else:
+        _fwd_infer(a, None, _out(o.unsqueeze(3)), S, v.device, "scan_fwd")
     return o, S, cs
 
 
