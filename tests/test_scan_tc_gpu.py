@@ -39,7 +39,7 @@ TC_PHASE = [
     (1, 257, 1, 32, 32, False, False, False, True),  # additive, V = 32
     (3, 1, 2, 32, 64, True, True, True, True),
     (1, 100, 2, 32, 96, True, False, True, True),    # V = 96: not a multiple of 64 (fp32 path)
-    (2, 150, 2, 32, 128, True, True, True, True),    # value block 128
+    (2, 150, 2, 32, 128, True, True, True, True),    # two value blocks of 64
 ]
 
 
