@@ -75,23 +75,6 @@ __device__ __forceinline__ bool batch_wait(uint64_t* mbar, uint32_t parity) {
   return !bad;
 }
 
-// The value tile of a chunk (64 tokens x 64 bf16 values of one (b, h)) by one TMA load: the
-// 5-D tensor map (value % 8, token % 8, value / 8, row / 8, head), row = b T + t, with strides
-// (2 B, st, 16 B, 8 st, sh) traverses the tile in exactly the order of the K-major, no-swizzle
-// tcgen05 operand layout (8 x 8 core matrices of 128 B), so the copy lands in operand layout.
-// Used for full chunks when T % 8 == 0 and the rows of consecutive batches are contiguous
-// (b T + t addresses every row); the box never leaves the tensor.  No cluster multicast.
-__device__ __forceinline__ void tma_value_tile(void* dst, const CUtensorMap* map, int row0, int h, uint64_t* bar) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)),
-               "r"((uint32_t)(C * VD * 2))
-               : "memory");
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
-      ::"r"(umma::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(0), "r"(row0 >> 3), "r"(h),
-        "r"(umma::smem_u32(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void copy16(uint8_t* dst, const uint8_t* src, int nbytes, int nthr) {
   for (int u = threadIdx.x * 16; u < nbytes; u += nthr * 16)
     *reinterpret_cast<uint4*>(dst + u) = *reinterpret_cast<const uint4*>(src + u);
@@ -175,7 +158,7 @@ __global__ void __launch_bounds__(NT, 3) pcp_prep(sca2_scan_args p, float* cs, i
     umma::mbar_init(mbar, 1);
     umma::mbar_init(vbar, 1);
     umma::fence_mbar_init();
-    if (tma) tma_value_tile(VA, &vmap, b * p.T + t0, h, vbar);
+    if (tma) tc::tma_value_tile<VD>(VA, &vmap, b * p.T + t0, h, vbar);
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 128);
   if (!tma) tc::pf_values<VD>(p, VA, flags & tc::F_V_VEC, b, h, t0, Cl, 0);
@@ -515,7 +498,7 @@ __global__ void __launch_bounds__(NT, 2) pcp_out(sca2_scan_args p, sca2_out o, f
     umma::mbar_init(mbar, 1);
     umma::mbar_init(vbar, 1);
     umma::fence_mbar_init();
-    if (tma) tma_value_tile(VA, &vmap, b * p.T + t0, h, vbar);
+    if (tma) tc::tma_value_tile<VD>(VA, &vmap, b * p.T + t0, h, vbar);
   }
   if (warp == 0) umma::tmem_alloc(s_tmem, 128);
   if (!tma) tc::pf_values<VD>(p, VA, flags & tc::F_V_VEC, b, h, t0, Cl, 0);
@@ -718,11 +701,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Tensor map of the value tile (tma_value_tile): v bf16 with 16-byte aligned rows, T % 8 == 0 and
-// rows of consecutive batches contiguous (sb == T st), so row = b T + t addresses every token.
+// Tensor map of the value tile (tc::tma_value_tile): v bf16, V = 64, 16-byte aligned rows, T % 8 == 0
+// and rows of consecutive batches contiguous (sb == T st), so row = b T + t addresses every token.
+// Used by the chunk-parallel kernels here and by the tensor-core chunk walk (scan_tc.cu).
 // false (cp.async copies instead) where these do not hold or the encoder refuses the map.
-static bool value_tile_map(const sca2_scan_args& p, CUtensorMap* map) {
+bool value_tile_map(const sca2_scan_args& p, CUtensorMap* map) {
   const sca2_tok& v = p.v;
+  if (p.V != pcp::VD || p.io_dtype != SCA2_BF16) return false;
   if (p.T % 8 || v.sb != (int64_t)p.T * v.st || v.st % 8 || v.sh % 8 || ((uintptr_t)v.ptr & 15u)) return false;
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return false;

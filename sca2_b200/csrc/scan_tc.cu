@@ -22,9 +22,11 @@
 // contiguous run of the next operand, and operands are written with 16-byte stores.  Where a
 // bf16 operand alone would miss the bf16 parity bar (the intra-chunk read kernel P and the
 // corrected values E) it is carried as a hi + lo pair (three products hi*hi + hi*lo + lo*hi),
-// which keeps about 16 mantissa bits.  The next chunk's values are copied in with cp.async
-// (straight into the operand layout) and its phases (keys) and gates are loaded into registers
-// while the current chunk runs.  The MMAs of a batch are issued by two threads (warps 0 and
+// which keeps about 16 mantissa bits.  The next chunk's values are copied in while the current
+// chunk runs, straight into the operand layout: by one TMA tensor copy per full chunk (phase
+// flavour, V = 64, bf16 rows the tensor map can address; completion on an mbarrier whose wait is
+// bounded), else by 16-byte cp.async copies; its phases (keys) and gates are loaded into
+// registers meanwhile.  The MMAs of a batch are issued by two threads (warps 0 and
 // 1, independent accumulators: a thread issues one instruction in about 50 cycles, about what
 // an M = 128, N = 64 instruction takes on the tensor core) and complete on an mbarrier whose
 // wait is bounded: on a timeout the CTA records a fault bit, waits (bounded) once more for its
@@ -37,6 +39,8 @@
 // the chunk in slot 2c (fp32) and, in slot 2c+1, T (bf16 C x C, operand layout) followed by
 // E^T (bf16, 64 x C per block of 64 value columns, operand layout; the hi part of the split).
 // The backward reads them back instead of recomputing the inversion and the corrected values.
+#include <cstring>
+
 #include "tc_common.cuh"
 
 namespace sca2 {
@@ -80,7 +84,8 @@ struct FwdLayout {
   static constexpr int ST = A0_END;
   static constexpr int SC = ST + (STAGE ? al(KD * VB * 4) : 0);
   static constexpr int MBAR = SC + al(SC_FLOATS * 4);
-  static constexpr int TOTAL = MBAR + 64;  // mbarrier (8 B), TMEM base (4 B), error flag (4 B)
+  // mbarrier (8 B), TMEM base (4 B), error flag (4 B), U^T / Wk mbarrier (8 B), value-tile mbarrier (8 B)
+  static constexpr int TOTAL = MBAR + 64;
 };
 
 // TMEM columns: [0,64) Op ; [64,128) P ; [128,192) G, later U^T, later X^T ; [192, 192+KD) Wk,
@@ -108,7 +113,8 @@ __device__ __forceinline__ void copy_out(uint8_t* dst, const bf16* src, int nbyt
 template <int FL, int KD, int VB, int R, bool HG, bool PJ>
 __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out o, float* S_final,
                                                     float* cstates, int NCS, int flags, PhaseProj pp_in,
-                                                    TSlots ts) {
+                                                    TSlots ts, const __grid_constant__ CUtensorMap vmap,
+                                                    int use_tma) {
   PhaseProj pp = pp_in;
   pp.on = PJ;
   using L = FwdLayout<KD, VB, R>;
@@ -155,6 +161,11 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
   uint64_t* mbar2 = reinterpret_cast<uint64_t*>(sm + L::MBAR + 16);  // U^T / Wk batch (training)
+  // value tiles of full chunks by one TMA copy (issued by thread 0, completion on vbar, waited by
+  // every thread at the top of the chunk); the ragged last chunk takes 16-byte cp.async copies
+  uint64_t* vbar = reinterpret_cast<uint64_t*>(sm + L::MBAR + 24);
+  uint32_t vph = 0;
+  bool vpend = false;  // a value tile is in flight (uniform over the CTA)
   float* ST = reinterpret_cast<float*>(sm + L::ST);
   // MMA issuers: thread 0 and thread 32 (warps 0 and 1) issue independent products in parallel;
   // each mbar phase takes one arrival from each (a commit, or a plain arrive when it has none)
@@ -179,6 +190,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   if (tid == 0) {
     umma::mbar_init(mbar, NISS);
     umma::mbar_init(mbar2, 1);
+    umma::mbar_init(vbar, 1);
     umma::fence_mbar_init();
     *s_err = 0;
   }
@@ -324,7 +336,12 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
   };
   {
     const int Cl0 = min(C, p.T);
-    pf_values<VB>(p, VA, flags & F_V_VEC, b, h, 0, Cl0, vb0);
+    if (use_tma && Cl0 == C) {
+      if (tid == 0) tma_value_tile<VB>(VA, &vmap, b * p.T, h, vbar);
+      vpend = true;
+    } else {
+      pf_values<VB>(p, VA, flags & F_V_VEC, b, h, 0, Cl0, vb0);
+    }
     if (prep)
       for (int u = tid * 16; u < C * C * 2; u += NT * 16) cp16(reinterpret_cast<uint8_t*>(TB) + u, t_at(0) + u, true);
     cp_commit();
@@ -361,6 +378,11 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     // ---- operands of the chunk
     const Gates gates = gset(c);
     cp_wait_all();
+    if (vpend) {  // this chunk's value tile (TMA)
+      if (!umma::mbar_wait(vbar, vph)) *s_err = 1;
+      vph ^= 1u;
+      vpend = false;
+    }
     for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * (float)(Cl - 1));
     if (has_g) decay_factors(gates.Gc, s_fdec);
     kww_from_kw<FL, KD, R>(cops, gates);
@@ -441,8 +463,13 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
       if (!(ok = wait_mma2())) break;
     }
     if (c + 1 < NC) {  // VA and TB are free: next chunk's values (and T)
-      const int t1 = t0 + C;
-      pf_values<VB>(p, VA, flags & F_V_VEC, b, h, t1, min(C, p.T - t1), vb0);
+      const int t1 = t0 + C, Cl1 = min(C, p.T - t1);
+      if (use_tma && Cl1 == C) {
+        if (tid == 0) tma_value_tile<VB>(VA, &vmap, b * p.T + t1, h, vbar);
+        vpend = true;
+      } else {
+        pf_values<VB>(p, VA, flags & F_V_VEC, b, h, t1, Cl1, vb0);
+      }
       if (prep)
         for (int u = tid * 16; u < C * C * 2; u += NT * 16)
           cp16(reinterpret_cast<uint8_t*>(TB) + u, t_at(c + 1) + u, true);
@@ -581,6 +608,7 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_tc(sca2_scan_args p, sca2_out 
     umma::mbar_wait(mbar, phase ^ 1u);
     if (pending2) umma::mbar_wait(mbar2, phase2);
   }
+  if (vpend) umma::mbar_wait(vbar, vph);  // bounded: a value tile still in flight lands first
   umma::fence_before_sync();
   __syncthreads();
   if (tid < 32) umma::tmem_dealloc(tb, CO::ALLOC);
@@ -596,14 +624,15 @@ auto fwd_kernel(bool pj) {
 
 template <int FL, int KD, int VB, int R>
 cudaError_t launch_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates,
-                       int NCS, int flags, const PhaseProj& pp, const TSlots& ts, cudaStream_t st) {
+                       int NCS, int flags, const PhaseProj& pp, const TSlots& ts, const CUtensorMap& vmap,
+                       int use_tma, cudaStream_t st) {
   const bool pj = pp.on != 0;
   auto k = p.g.ptr ? fwd_kernel<FL, KD, VB, R, true>(pj) : fwd_kernel<FL, KD, VB, R, false>(pj);
   const int smem = FwdLayout<KD, VB, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, p.V / VB);
-  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags, pp, ts);
+  k<<<grid, NT, smem, st>>>(p, o, S_final, cstates, NCS, flags, pp, ts, vmap, use_tma);
   return cudaGetLastError();
 }
 
@@ -653,8 +682,10 @@ int64_t tc_infer_work_bytes(const sca2_scan_args& p) {
   if (p.K != 64 || p.T <= 0) return 0;
   return (int64_t)p.B * p.H * ((p.T + tc::C - 1) / tc::C) * (tc::C * tc::C * 2);
 }
-// phase_cp.cu: the chunk-parallel training forward of the phase flavour at K = V = 64
+// phase_cp.cu: the chunk-parallel training forward of the phase flavour at K = V = 64, and the
+// tensor map of a chunk's value tile (bf16, V = 64)
 bool pcp_covers(const sca2_scan_args& p, const float* cstates);
+bool value_tile_map(const sca2_scan_args& p, CUtensorMap* map);
 cudaError_t pcp_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_final, float* cstates, int NS,
                          int flags, const PhaseProj& pp, cudaStream_t st);
 
@@ -682,14 +713,19 @@ cudaError_t tc_scan_fwd(const sca2_scan_args& p, int VB, const sca2_out& o, floa
     if (e != cudaSuccess) return e;
     fl |= tc::F_PREP;
   }
+  // the phase flavour at K = V = 64 (one value block): value tiles of full chunks by TMA
+  alignas(64) CUtensorMap vmap;
+  memset(&vmap, 0, sizeof(vmap));
+  const int use_tma = (ph && p.K == 64 && VB == 64 && p.V == 64 && value_tile_map(p, &vmap)) ? 1 : 0;
 #define SCA2_TC_FWD(KD_, VB_)                                                                             \
   if (p.K == KD_ && VB == VB_)                                                                            \
-    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, pp, ts, st)   \
-              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, pp, ts, st);
+    return ph ? tc::launch_fwd<SCA2_FLAVOR_PHASE, KD_, VB_, 2>(p, o, S_final, cstates, NCS, fl, pp, ts, vmap,    \
+                                                              use_tma, st)                                     \
+              : tc::launch_fwd<SCA2_FLAVOR_KEY, KD_, VB_, 1>(p, o, S_final, cstates, NCS, fl, pp, ts, vmap, 0, st);
   SCA2_TC_FWD(64, 64) SCA2_TC_FWD(64, 128)
 #undef SCA2_TC_FWD
   if (p.K == 128 && VB == 64 && !ph)
-    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, pp, ts, st);
+    return tc::launch_fwd<SCA2_FLAVOR_KEY, 128, 64, 1>(p, o, S_final, cstates, NCS, fl, pp, ts, vmap, 0, st);
   return cudaErrorInvalidValue;
 }
 

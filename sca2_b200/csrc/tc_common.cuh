@@ -2,6 +2,8 @@
 // fragment iteration, the fp32 blocked inversion and the per-chunk operand prologue.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the type only; the library does not link the driver library)
+
 #include "common.cuh"
 #include "umma.cuh"
 
@@ -18,6 +20,24 @@ using bf16 = __nv_bfloat16;
 // F_PREP: T of every chunk was written by the preparation kernel (where TSlots says)
 // F_CS16: the chunk-state buffer is 16-byte aligned (bulk copies may write it)
 enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8, F_PREP = 16, F_CS16 = 32 };
+
+// The value tile of a full chunk (64 tokens x VW bf16 values of one (b, h)) by one TMA load: the
+// 5-D tensor map (value % 8, token % 8, value / 8, row / 8, head), row = b T + t, with strides
+// (2 B, st, 16 B, 8 st, sh) traverses the tile in exactly the order of the K-major, no-swizzle
+// tcgen05 operand layout (8 x 8 core matrices of 128 B), so the copy lands in operand layout.
+// The map covers the value tensor of this GPU only and the box never leaves it; no cluster
+// multicast.  Completion on `bar` (expect_tx of the tile's bytes, armed by the issuing thread).
+template <int VW>
+__device__ __forceinline__ void tma_value_tile(void* dst, const CUtensorMap* map, int row0, int h, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)),
+               "r"((uint32_t)(C * VW * 2))
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+      ::"r"(umma::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(0), "r"(row0 >> 3), "r"(h),
+        "r"(umma::smem_u32(bar))
+      : "memory");
+}
 
 // Where the preparation kernel puts each chunk's inverse T (bf16 C x C in operand layout, 8 KB):
 // chunk c of sequence bh = b H + h at base + bh * bh_stride + c * c_stride (bytes, all multiples
