@@ -740,6 +740,27 @@ cudaError_t pcp_scan_fwd(const sca2_scan_args& p, const sca2_out& o, float* S_fi
   return cudaGetLastError();
 }
 
+// Tensor map of the tensor-core backward's dO tiles (phase flavour, R = 2): dO (B, T, H, 2, V) bf16
+// with the read column r next to the head (sh == 2 sr), batches' rows contiguous, T % 8 == 0 and
+// 16-byte aligned rows; dims (value % 8, token % 8, value / 8, row / 8, 2 h + r), so the 64-token
+// x 64-value tile of one (b, h, r) at coordinates (0, 0, vb0 / 8, (b T + t0) / 8, 2 h + r) lands in
+// the K-major, no-swizzle operand layout, exactly as the value tiles above.  false (cp.async
+// copies instead) where these do not hold or the encoder refuses the map.
+bool dO_tile_map(const sca2_scan_args& p, const sca2_out& dO, CUtensorMap* map) {
+  if (p.flavor != SCA2_FLAVOR_PHASE || p.io_dtype != SCA2_BF16 || p.V % 64 || p.T % 8) return false;
+  if (dO.sb != (int64_t)p.T * dO.st || dO.sh != 2 * dO.sr || dO.st % 8 || dO.sr % 8 || ((uintptr_t)dO.ptr & 15u))
+    return false;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[5] = {8, 8, (cuuint64_t)p.V / 8, (cuuint64_t)p.B * p.T / 8, (cuuint64_t)p.H * 2};
+  const cuuint64_t strides[4] = {(cuuint64_t)dO.st * 2, 16, (cuuint64_t)dO.st * 16, (cuuint64_t)dO.sr * 2};
+  const cuuint32_t box[5] = {8, 8, 8, tc::C / 8, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, dO.ptr, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // whether a training forward of these arguments runs chunk-parallel with its value tiles by TMA
 bool pcp_value_tma(const sca2_scan_args& p, const float* cstates) {
   alignas(64) CUtensorMap map;

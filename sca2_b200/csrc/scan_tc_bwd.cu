@@ -27,9 +27,13 @@
 //
 // Every product is a bf16 MMA with fp32 accumulation in TMEM.  Operands used both ways are
 // stored once, K-major, and read through MN-major descriptors for the transposed use.  The
-// next chunk's state, T, E, P and dO are copied in with cp.async while the current chunk runs;
+// next chunk's state, T, E, P and dO are copied in while the current chunk runs: dO of a full
+// chunk by TMA (phase flavour, one 5-D tensor copy per read column into operand layout, completion
+// on an mbarrier whose wait is bounded) where the tensor map can address dO, the rest by cp.async;
 // its phases (keys) and gates are loaded into registers.  Every mbarrier wait is bounded: on a
 // timeout the CTA records a fault bit, frees its TMEM and returns.
+#include <cstring>
+
 #include "tc_common.cuh"
 
 namespace sca2 {
@@ -75,7 +79,7 @@ struct BwdLayout {
   // column factors of the decay mask [C]; the head's theta and omega [Mh] (phases from projections)
   static constexpr int SC_FLOATS = 14 * C + 8 * KD + 8 + 2 * Mh;
   static constexpr int MBAR = SC + ((SC_FLOATS * 4 + 1023) & ~1023);
-  static constexpr int TOTAL = MBAR + 64;
+  static constexpr int TOTAL = MBAR + 64;  // MMA mbarrier, TMEM base, error flag, dO-tile mbarrier
   static_assert(TOTAL <= 227 * 1024, "shared memory");
   static_assert(RC * 64 * 2 >= RC * KD * 2, "R1 holds QRA");
   static_assert(2 * VB * KD * 2 >= RC * C * 2, "R4 holds the weighted dQK");
@@ -309,7 +313,8 @@ __device__ __forceinline__ void acc_row8(float* dst, const float* x, bool vec, b
 template <int FL, int R, bool HG, bool PJ>
 __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out dO, const float* dS_final,
                                                     const float* cstates, sca2_scan_grads gr, int NCS,
-                                                    int flags, PhaseProj pp_in) {
+                                                    int flags, PhaseProj pp_in,
+                                                    const __grid_constant__ CUtensorMap omap, int use_tma) {
   PhaseProj pp = pp_in;
   pp.on = PJ;
   using L = BwdLayout<FL, R>;
@@ -376,6 +381,23 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L::MBAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + L::MBAR + 8);
   volatile int* s_err = reinterpret_cast<volatile int*>(sm + L::MBAR + 12);
+  // dO tiles of full chunks by TMA (phase flavour: one copy per read column r into its 64-row half
+  // of DOA), issued by thread 0, completion on obar, waited by every thread at the top of the
+  // chunk; the ragged chunk takes 16-byte cp.async copies
+  uint64_t* obar = reinterpret_cast<uint64_t*>(sm + L::MBAR + 16);
+  const CUtensorMap* omp = &omap;
+  uint32_t oph = 0;
+  bool opend = false;  // a dO tile is in flight (uniform over the CTA)
+  const bool otma = FL == SCA2_FLAVOR_PHASE && use_tma;  // compiled out of the key flavour
+  auto tma_dO = [&](int t0c) {
+    if (tid == 0) {
+      tma_expect(obar, (uint32_t)(RC * VB * 2));
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        tma_load5(sm + L::DOA + r * (C * VB * 2), omp, vb0 / 8, (b * p.T + t0c) / 8, R * h + r, obar);
+    }
+    opend = true;
+  };
 
   // ---- set-up
   for (int m = tid; m < KD; m += NT) {
@@ -394,6 +416,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
   }
   if (tid == 0) {
     umma::mbar_init(mbar, NISS);
+    umma::mbar_init(obar, 1);
     umma::fence_mbar_init();
     *s_err = 0;
   }
@@ -458,7 +481,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     pf_bytes(sm + L::TB, saved(c), C * C * 2);
     pf_bytes(sm + L::EB, saved(c) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
     pf_bytes(sm + L::PP, saved_P(c), RC * C * 2);
-    pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
+    if (otma && Cl == C)
+      tma_dO(t0);
+    else
+      pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0, Cl, vb0);
     cp_commit();
     load_code_regs<FL, KD>(p, creg, flags & (FL == SCA2_FLAVOR_PHASE ? B_PH_VEC : B_K_VEC), b, h, t0, Cl, pp);
     if (warp == 0) {
@@ -473,6 +499,11 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     const float fi_last = (float)(Cl - 1);
     // ================= prologue =================
     cp_wait_all();
+    if (opend) {  // this chunk's dO tile (TMA)
+      if (!umma::mbar_wait(obar, oph)) *s_err = 1;
+      oph ^= 1u;
+      opend = false;
+    }
     gates = gset(c);
     for (int m = tid; m < KD; m += NT) s_dCm1[m] = expf(-s_lam[m] * fi_last);
     if (tid < C) {
@@ -600,7 +631,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     if (!(ok = wait_mma())) break;
     if (c > 0) {  // EB and DOA are free: the next chunk's E and dO
       pf_bytes(sm + L::EB, saved(c - 1) + C * C * 2 + blockIdx.y * (VB * C * 2), VB * C * 2);
-      pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0 - C, C, vb0);
+      if (otma)
+        tma_dO(t0 - C);
+      else
+        pf_dO<R>(p, dO, BF(L::DOA), flags, b, h, t0 - C, C, vb0);
       cp_commit();
     }
     // ---- dL with G -> dKK (+ position-weighted), d(beta) row term, decay sums
@@ -1151,6 +1185,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_tc(sca2_scan_args p, sca2_out 
     if (tid == 0) atomicOr(&g_fault_bwd, 1u);
     umma::mbar_wait(mbar, phase ^ 1u);
   }
+  if (opend) umma::mbar_wait(obar, oph);  // bounded: a dO tile still in flight lands first
   umma::fence_before_sync();
   __syncthreads();
   if (tid < 32) umma::tmem_dealloc(tb, CO::ALLOC);
@@ -1166,14 +1201,15 @@ auto bwd_kernel(bool pj) {
 
 template <int FL, int R>
 cudaError_t launch_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
-                       const sca2_scan_grads& gr, int NCS, int flags, const PhaseProj& pp, cudaStream_t st) {
+                       const sca2_scan_grads& gr, int NCS, int flags, const PhaseProj& pp, const CUtensorMap& omap,
+                       int use_tma, cudaStream_t st) {
   const bool pj = pp.on != 0;
   auto k = p.g.ptr ? bwd_kernel<FL, R, true>(pj) : bwd_kernel<FL, R, false>(pj);
   const int smem = BwdLayout<FL, R>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B * p.H, p.V / BVB);
-  k<<<grid, NT, smem, st>>>(p, dO, dS_final, cstates, gr, NCS, flags, pp);
+  k<<<grid, NT, smem, st>>>(p, dO, dS_final, cstates, gr, NCS, flags, pp, omap, use_tma);
   return cudaGetLastError();
 }
 
@@ -1200,6 +1236,9 @@ bool tc_train_ok(const sca2_scan_args& p, int max_smem) {
   return p.io_dtype == SCA2_BF16 && p.K == 64 && p.V % 64 == 0 && tc_bwd_smem(64, R) <= max_smem;
 }
 
+// phase_cp.cu: the tensor map of the dO tiles (phase flavour)
+bool dO_tile_map(const sca2_scan_args& p, const sca2_out& dO, CUtensorMap* map);
+
 cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float* dS_final, const float* cstates,
                         const sca2_scan_grads& gr, int NCS, cudaStream_t st, const PhaseProj& pp) {
   auto a16 = [](const void* q) { return ((uintptr_t)q & 15u) == 0; };
@@ -1216,9 +1255,13 @@ cudaError_t tc_scan_bwd(const sca2_scan_args& p, const sca2_out& dO, const float
       gr.dphq.sb % 4 == 0 && gr.dphq.st % 4 == 0 && gr.dphq.sh % 4 == 0)
     f |= tc::B_G_VEC;
   if (gr.overwrite && p.V == tc::BVB && (f & tc::B_G_VEC)) f |= tc::B_OVERWRITE;
+  // phase flavour: the dO tile of every full chunk by TMA where the map can address dO
+  alignas(64) CUtensorMap omap;
+  memset(&omap, 0, sizeof(omap));
+  const int use_tma = (p.flavor == SCA2_FLAVOR_PHASE && dO_tile_map(p, dO, &omap)) ? 1 : 0;
   if (p.flavor == SCA2_FLAVOR_PHASE)
-    return tc::launch_bwd<SCA2_FLAVOR_PHASE, 2>(p, dO, dS_final, cstates, gr, NCS, f, pp, st);
-  return tc::launch_bwd<SCA2_FLAVOR_KEY, 1>(p, dO, dS_final, cstates, gr, NCS, f, pp, st);
+    return tc::launch_bwd<SCA2_FLAVOR_PHASE, 2>(p, dO, dS_final, cstates, gr, NCS, f, pp, omap, use_tma, st);
+  return tc::launch_bwd<SCA2_FLAVOR_KEY, 1>(p, dO, dS_final, cstates, gr, NCS, f, pp, omap, 0, st);
 }
 
 }  // namespace sca2

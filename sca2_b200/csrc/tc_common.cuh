@@ -27,16 +27,24 @@ enum : int { F_PH_VEC = 1, F_O_VEC = 2, F_K_VEC = 4, F_V_VEC = 8, F_PREP = 16, F
 // tcgen05 operand layout (8 x 8 core matrices of 128 B), so the copy lands in operand layout.
 // The map covers the value tensor of this GPU only and the box never leaves it; no cluster
 // multicast.  Completion on `bar` (expect_tx of the tile's bytes, armed by the issuing thread).
-template <int VW>
-__device__ __forceinline__ void tma_value_tile(void* dst, const CUtensorMap* map, int row0, int h, uint64_t* bar) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)),
-               "r"((uint32_t)(C * VW * 2))
+// Arm `bar` for `bytes` of TMA data: one arrival (the issuing thread's) plus the expected bytes.
+__device__ __forceinline__ void tma_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)), "r"(bytes)
                : "memory");
+}
+// One tile of a 5-D tensor map at coordinates (0, 0, x2, x3, x4) into shared memory, completing
+// on `bar`.  The innermost coordinate is 0, so the copy starts on a 16-byte boundary.
+__device__ __forceinline__ void tma_load5(void* dst, const CUtensorMap* map, int x2, int x3, int x4, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
-      ::"r"(umma::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(0), "r"(row0 >> 3), "r"(h),
+      ::"r"(umma::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(x2), "r"(x3), "r"(x4),
         "r"(umma::smem_u32(bar))
       : "memory");
+}
+template <int VW>
+__device__ __forceinline__ void tma_value_tile(void* dst, const CUtensorMap* map, int row0, int h, uint64_t* bar) {
+  tma_expect(bar, (uint32_t)(C * VW * 2));
+  tma_load5(dst, map, 0, row0 >> 3, h, bar);
 }
 
 // Where the preparation kernel puts each chunk's inverse T (bf16 C x C in operand layout, 8 KB):
