@@ -118,3 +118,11 @@ def test_row_ops_entry_points_refuse_bad_sizes():
     assert lib.sca2_layer_norm_supported(1024) == 1 and lib.sca2_layer_norm_supported(1000) == 0
     assert lib.sca2_layer_norm_fwd(None, None, None, None, None, None, 2, 1000, 1e-5, None) != 0
     assert lib.sca2_layer_norm_work_floats(0, 1024) == 0 and lib.sca2_layer_norm_work_floats(64, 1024) > 0
+
+
+def test_inference_work_entry_refuses_bad_arguments():
+    """The inference forward with a work buffer checks its arguments on the host before any
+    launch: no argument struct is an error, and its work-size query answers 0 for it."""
+    lib = _lib.load()
+    assert lib.sca2_scan_fwd_work_bytes(None) == 0
+    assert lib.sca2_scan_fwd_work(None, None, _lib.Out(None, 0, 0, 0, 0), None, None, 0, None) == _lib.SCA2_ERR_ARG
