@@ -261,8 +261,9 @@ SCA2_API int64_t sca2_scan_fwd_work_bytes(const sca2_scan_args* a);
  * NULL).  Where sca2_scan_fwd_work_bytes(a) > 0 the delta-rule inverse of every 64-token chunk
  * is first computed chunk-parallel into `work` (16-byte aligned, at least that many bytes), and
  * the sequential chunk walk reads it instead of inverting inside its loop; otherwise `work` is
- * not used.  Same outputs as the calls named (the inverse is formed by the same fp32 algorithm
- * and rounded to bf16 in both).  Replaces the same reference prefill paths as sca2_scan_fwd
+ * not used.  The outputs agree with the calls named within the bf16 parity bar (the inverse is
+ * formed by the same fp32 algorithm and rounded to bf16 in both; its inputs may round in the
+ * last bit differently).  Replaces the same reference prefill paths as sca2_scan_fwd
  * (lapa/layer.py:298-366 with no autograd graph kept). */
 SCA2_API int sca2_scan_fwd_work(const sca2_scan_args* a, const sca2_phase_proj* pp, sca2_out o,
                    float* S_final, void* work, int64_t work_bytes, void* stream);
